@@ -1,0 +1,421 @@
+"""Benchmark of the IQ3_S x MXFP8 linear path on B200 (driver contract: one JSON line on rank 0).
+
+Workload ("decode GEMV sweep"): Llama-3-8B projection
+shapes -- QKV 4096->6144, O 4096->4096, gate 4096->14336, up 4096->14336,
+down 14336->4096 -- at M in {1, 2, 4, 8}. Each M uses its own layer of
+seeded random IQ3_S weights, so one step streams 4 x 93.7 MB = 375 MB of
+weights (larger than the 126 MB L2: no flush needed). A step runs, for each
+M, the layer's 5 linears through the fused path (bf16 activations ->
+MXFP8 quantization -> IQ3_S x MXFP8 GEMV -> bf16 output), captured once in
+a CUDA graph and replayed.
+
+value  = algorithmic bytes per step (weights + bf16 activations in + bf16 out)
+         / device time per step, GB/s, summed over ranks (weak scaling: every
+         rank runs the full workload on its own weights; the path does not
+         shard at this size, so N > 1 runs independent replicas).
+e2e    = the same step through the public API with pinned host buffers:
+         host->device copy of the step's activations, the linears, and a
+         device->host copy of the outputs, all inside the timed region.
+roofline = the GEMV kernel alone: algorithmic bytes per launch / mean CUDA-event
+         duration of a launch, against MEASURED_PEAKS.json's HBM copy bandwidth.
+
+``--impl reference`` times the reference's CPU path (the C restatement of its
+IQ3_S decode + MXFP8 codec + float64 dot, oracle/iq3s_ref.c) on this host.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+PROJECTIONS = (  # name, N, K (Llama-3-8B)
+    ("qkv", 6144, 4096),
+    ("o", 4096, 4096),
+    ("gate", 14336, 4096),
+    ("up", 14336, 4096),
+    ("down", 4096, 14336),
+)
+M_SWEEP = (1, 2, 4, 8)
+METRIC = "IQ3_S x MXFP8 decode linear (Llama-3-8B shapes, M in {1,2,4,8}) algorithmic GB/s"
+HBM_FALLBACK_GBS = 6650.0
+
+
+def load_peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.is_file():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except (KeyError, ValueError):
+            pass
+    return HBM_FALLBACK_GBS, "fallback"
+
+
+def layer_bytes() -> int:
+    return sum(n * (k // 256) * 110 for _, n, k in PROJECTIONS)
+
+
+def step_bytes() -> tuple[int, int, int]:
+    """(weight bytes, activation-in bytes, output bytes) per step."""
+    w = layer_bytes() * len(M_SWEEP)
+    xin = sum(m * k * 2 for m in M_SWEEP for _, _, k in PROJECTIONS)
+    out = sum(m * n * 2 for m in M_SWEEP for _, n, _ in PROJECTIONS)
+    return w, xin, out
+
+
+# ---------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        if self.proc is None or self.path is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[5:9]))
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({names[i] for r in rows for i, v in enumerate(r[3]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "power_w_max": max(r[2] for r in rows), "samples": len(rows), "reasons": reasons}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline (the reference's CPU path, restated in C)
+# ---------------------------------------------------------------------------
+def cpu_baseline(budget_s: float = 15.0) -> dict:
+    import numpy as np
+
+    from oracle import c_oracle
+    from oracle import iq3s_oracle as O
+
+    threads = os.cpu_count() or 1
+    m, n, k = 8, 4096, 4096  # the O projection at M = 8
+    x = np.random.default_rng(20261017).standard_normal((m, k)).astype(np.float32)
+
+    def run(rows: int) -> float:
+        raw = O.make_synthetic_iq3s(rows, k, seed=0x1A3)
+        t0 = time.perf_counter()
+        q, s = c_oracle.quantize_mxfp8(x)
+        c_oracle.iq3s_linear_f64(q, s, raw, threads=threads)
+        return time.perf_counter() - t0
+
+    t_small = run(256)
+    rows = int(min(n, max(256, 256 * budget_s / max(t_small, 1e-6))))
+    rows = max(256, rows // 256 * 256)
+    t = run(rows)
+    weight_bytes = rows * (k // 256) * 110
+    alg = weight_bytes + m * k * 2 + m * rows * 2
+    return {"value": alg / t / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"O projection rows 0..{rows} of {n} x K={k}, M={m}: C oracle (IQ3_S decode + MXFP8 quant + "
+                      f"float64 dot), {threads} host threads, {t:.2f} s"}
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    budget = max(0.5, 60.0 / max(1, args.steps + args.warmup))
+    res = None
+    for _ in range(args.warmup):
+        cpu_baseline(budget)
+    t0 = time.perf_counter()
+    vals = [cpu_baseline(budget) for _ in range(args.steps)]
+    wall = time.perf_counter() - t0
+    res = vals[-1]
+    value = statistics.mean(v["value"] for v in vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": wall * 1000 / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic", "config": {"workload": "decode_gemv_sweep_llama3_8b (bounded CPU sample)",
+                                        "sample": res["sample"]},
+        "cpu_baseline": {**res, "value": value},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU
+# ---------------------------------------------------------------------------
+def build_workload(torch, dev):
+    from mambo_b200.utils.iq3_s_weight import prepare_iq3_s_fields
+
+    layers = {}
+    for li, m in enumerate(M_SWEEP):
+        projs = {}
+        for pi, (name, n, k) in enumerate(PROJECTIONS):
+            seed = 0x1A3 + 7919 * li + pi
+            gen = torch.Generator(device=dev).manual_seed(seed)
+            raw = torch.randint(0, 256, (n, k // 256, 110), dtype=torch.uint8, device=dev, generator=gen)
+            d = (torch.rand((n, k // 256), device=dev, generator=gen) * 9e-3 + 1e-3).half()
+            raw[..., :2] = d.view(torch.uint8).view(n, k // 256, 2)
+            projs[name] = prepare_iq3_s_fields(raw)
+            del raw
+        layers[m] = projs
+    gen = torch.Generator(device="cpu").manual_seed(20261017)
+    inputs = {m: {name: torch.randn((m, k), generator=gen).to(torch.bfloat16) for name, _, k in PROJECTIONS}
+              for m in M_SWEEP}
+    return layers, inputs
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("mambo", "reference"), default="mambo")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    from mambo_b200.kernels.iq3_s_fp8 import linear_into, select_config
+    from mambo_b200.kernels.quantize_fp8 import launch_quantize_fp8
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=__import__("datetime").timedelta(seconds=120))
+
+    layers, inputs = build_workload(torch, dev)
+    stream = torch.cuda.Stream(dev)
+
+    # device buffers
+    xs_dev = {m: {p: inputs[m][p].to(dev) for p in inputs[m]} for m in M_SWEEP}
+    q_buf = {m: {p: (torch.empty((m, k), dtype=torch.uint8, device=dev),
+                     torch.empty((m, k // 32), dtype=torch.uint8, device=dev)) for p, _, k in PROJECTIONS}
+             for m in M_SWEEP}
+    out_buf = {m: {p: torch.empty((m, n), dtype=torch.bfloat16, device=dev) for p, n, _ in PROJECTIONS}
+               for m in M_SWEEP}
+    configs = {m: {p: select_config(m, n, k, dev) for p, n, k in PROJECTIONS} for m in M_SWEEP}
+
+    def step_ops(x_src):
+        for m in M_SWEEP:
+            for p, n, k in PROJECTIONS:
+                xq, xsc = q_buf[m][p]
+                launch_quantize_fp8(x_src[m][p], out=(xq, xsc))
+                linear_into(xq, xsc, layers[m][p], out_buf[m][p], config=configs[m][p])
+
+    # warm up eagerly (allocates the workspace), then capture one step
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            step_ops(xs_dev)
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step_ops(xs_dev)
+    torch.cuda.synchronize(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- timed region: K graph replays of the step -------------------------
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize(dev)
+    barrier()
+    with ClockSampler(local) as clocks:
+        torch.cuda.synchronize(dev)
+        barrier()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        with torch.cuda.stream(stream):
+            for _ in range(args.steps):
+                graph.replay()
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+    ms_per_step = max_over_ranks(t0.elapsed_time(t1) / args.steps)
+    clock = clocks.summary()
+    w_bytes, in_bytes, out_bytes = step_bytes()
+    alg = w_bytes + in_bytes + out_bytes
+    value = alg * world / (ms_per_step * 1e-3) / 1e9
+
+    # ---- roofline of the GEMV kernel: per-launch CUDA-event durations ------
+    per_launch = []
+    for m in M_SWEEP:
+        for p, n, k in PROJECTIONS:
+            xq, xsc = q_buf[m][p]
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                linear_into(xq, xsc, layers[m][p], out_buf[m][p], config=configs[m][p])
+            reps = 20
+            with torch.cuda.stream(stream):
+                for _ in range(3):
+                    g.replay()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                for _ in range(reps):
+                    g.replay()
+                e1.record(stream)
+            torch.cuda.synchronize(dev)
+            us = e0.elapsed_time(e1) * 1000 / reps
+            b = n * (k // 256) * 110 + m * k + m * k // 32 + m * n * 2
+            per_launch.append({"m": m, "proj": p, "us": us, "bytes": b, "gbs": b / us / 1e3})
+            del g
+    peak, peak_kind = load_peaks()
+    tot_b = sum(r["bytes"] for r in per_launch)
+    tot_us = sum(r["us"] for r in per_launch)
+    achieved = tot_b / tot_us / 1e3
+    traffic = None
+    tpath = ROOT / "profiles" / "gemv_decode_traffic.json"
+    if tpath.is_file():
+        try:
+            traffic = json.loads(tpath.read_text()).get("dram_bytes_per_launch")
+        except ValueError:
+            traffic = None
+
+    # ---- e2e: public API with pinned host buffers, H2D + D2H in the region --
+    from mambo_b200.kernels.iq3_s_fp8 import iq3_s_fp8_linear
+
+    host_in = {m: {p: inputs[m][p].pin_memory() for p in inputs[m]} for m in M_SWEEP}
+    host_out = {m: {p: torch.empty((m, n), dtype=torch.bfloat16).pin_memory() for p, n, _ in PROJECTIONS}
+                for m in M_SWEEP}
+    dev_in = {m: {p: torch.empty_like(xs_dev[m][p]) for p in inputs[m]} for m in M_SWEEP}
+
+    def e2e_step():
+        for m in M_SWEEP:
+            for p, n, k in PROJECTIONS:
+                dev_in[m][p].copy_(host_in[m][p], non_blocking=True)
+                y = iq3_s_fp8_linear(dev_in[m][p], layers[m][p], config=configs[m][p])
+                host_out[m][p].copy_(y, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            e2e_step()
+    torch.cuda.synchronize(dev)
+    g_e2e = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_e2e, stream=stream):
+        e2e_step()
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            g_e2e.replay()
+    torch.cuda.synchronize(dev)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(args.steps):
+            g_e2e.replay()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    # eager (no graph) for reference
+    torch.cuda.synchronize(dev)
+    t_e = time.perf_counter()
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.steps // 5)):
+            e2e_step()
+    torch.cuda.synchronize(dev)
+    eager_ms = (time.perf_counter() - t_e) * 1000 / max(3, args.steps // 5)
+    # correctness spot check of the e2e output against the device path
+    ok = all(torch.equal(host_out[m][p], out_buf[m][p].cpu()) for m in M_SWEEP for p, _, _ in PROJECTIONS)
+
+    if world > 1:
+        del graph, g_e2e
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    cpu = None if args.no_cpu_baseline else cpu_baseline()
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_per_step,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "e4m3",
+        "data": "synthetic",
+        "config": {"workload": "decode_gemv_sweep_llama3_8b (BASELINE config 2)", "m_sweep": list(M_SWEEP),
+                   "projections": {p: [n, k] for p, n, k in PROJECTIONS},
+                   "bytes_per_step": {"weights": w_bytes, "act_in_bf16": in_bytes, "out_bf16": out_bytes},
+                   "l2": "inputs larger than L2 (375 MB of weights per step)", "execution": "cuda graph replay",
+                   "parallelism": f"replicas{world}"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": traffic, "peak_kind": peak_kind, "kernel": "iq3s_gemv_kernel",
+                     "per_launch": per_launch},
+        "e2e": {"value": alg * world / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
+                "h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": out_bytes,
+                "ms_per_step": e2e_ms, "execution": "cuda graph of public-API calls incl. H2D/D2H",
+                "eager_ms_per_step": eager_ms, "matches_device_path": ok},
+        "gpu_launches": args.steps * len(M_SWEEP) * len(PROJECTIONS) * 2,
+        "clocks": clock,
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

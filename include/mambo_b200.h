@@ -1,0 +1,161 @@
+/*
+ * mambo_b200 -- C ABI of the B200 (sm_100a) IQ3_S x MXFP8 quantized-linear path.
+ *
+ * Every entry point is asynchronous on the given CUDA stream, takes plain
+ * device pointers and sizes, returns an int status (MAMBO_OK on success) and
+ * never throws or aborts. On failure a message is kept per host thread and
+ * can be read with mambo_last_error().
+ *
+ * Each declaration cites the reference interface it replaces (paths relative
+ * to the Menooker/Mambo tree). The reference launches cuTile kernels from
+ * Python through CuPy; these functions are what its launch wrappers
+ * (src/python/mambo/kernels/*.py) bind to in this build.
+ */
+#ifndef MAMBO_B200_H
+#define MAMBO_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MAMBO_API __attribute__((visibility("default")))
+#else
+#define MAMBO_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* mambo_stream_t; /* a cudaStream_t; NULL = legacy default stream */
+
+/* Status codes. */
+enum {
+  MAMBO_OK = 0,
+  MAMBO_EINVAL = 1,         /* bad shape, dtype, stride or pointer (reference: ValueError / TypeError) */
+  MAMBO_ENOTSUPPORTED = 2,  /* device is not sm_100 (reference: RuntimeError "no tuned config") */
+  MAMBO_ECUDA = 3,          /* a CUDA runtime call failed */
+  MAMBO_ETIMEOUT = 4,       /* a bounded device-side wait gave up (see mambo_device_status) */
+  MAMBO_EWORKSPACE = 5      /* workspace missing or too small */
+};
+
+/* Element types of activations / outputs. */
+enum { MAMBO_F32 = 0, MAMBO_BF16 = 1 };
+
+/* Rounding of activation values to E4M3. */
+enum {
+  MAMBO_ROUND_NEAREST_EVEN = 0, /* cvt.rn (cuTile astype in quantize_fp8.py:37) */
+  MAMBO_ROUND_TIES_DOWN = 1     /* exact ties to the smaller magnitude (fp8_reference.py:81-83) */
+};
+
+/*
+ * Prepared IQ3_S weight: the byte-preserving structure-of-arrays split of
+ * GGUF blocks [N, B, 110] (B = K/256), fields laid out [B, N, ...] and
+ * C-contiguous. Mirrors IQ3SFields (src/python/mambo/utils/iq3_s_weight.py:10-22).
+ */
+typedef struct MamboIQ3SWeight {
+  const void* d;      /* float16 [B, N]       block base scale           */
+  const void* qs;     /* uint8   [B, N, 64]   low 8 bits of 9-bit codes  */
+  const void* qh;     /* uint8   [B, N, 8]    high code bits             */
+  const void* signs;  /* uint8   [B, N, 32]   one sign bit per weight    */
+  const void* scales; /* uint8   [B, N, 4]    8 packed 4-bit group scales */
+  int64_t n_rows;     /* N */
+  int64_t n_blocks;   /* B */
+} MamboIQ3SWeight;
+
+/* Launch configuration of the linear kernels (NULL = tuned default for the shape). */
+typedef struct MamboLinearConfig {
+  int kernel;        /* MAMBO_KERNEL_* */
+  int warps;         /* compute warps per CTA (GEMV: 16 weight rows each) */
+  int stages;        /* shared-memory pipeline depth */
+  int ctas_per_sm;   /* GEMV persistent grid = SMs * ctas_per_sm (0 = 1) */
+  int split;         /* GEMV: 0 = stream-K over all SMs, 1 = one CTA per row tile */
+  int loader;        /* GEMV weight staging: 0 = TMA when the layout allows it, 1 = plain loads */
+  int reserved[2];
+} MamboLinearConfig;
+
+enum { MAMBO_KERNEL_AUTO = 0, MAMBO_KERNEL_GEMV = 1, MAMBO_KERNEL_GEMM = 2 };
+
+/* Library version string. */
+MAMBO_API const char* mambo_version(void);
+
+/* Copies the calling thread's last error message into buf (NUL-terminated). Returns its status code. */
+MAMBO_API int mambo_last_error(char* buf, size_t len);
+
+/* MAMBO_OK when the current device is sm_100 and the library's kernels load on it. */
+MAMBO_API int mambo_device_check(void);
+
+/*
+ * Splits GGUF IQ3_S blocks into the SoA weight fields on the GPU.
+ * raw: byte tensor [N, B, 110] with arbitrary byte strides (element stride of
+ * the last dim may be > 1; any address alignment). Outputs must be
+ * C-contiguous buffers of the MamboIQ3SWeight field sizes.
+ * Replaces prepare_iq3_s_fields (src/python/mambo/utils/iq3_s_weight.py:25-54).
+ */
+MAMBO_API int mambo_iq3s_prepare(const uint8_t* raw, int64_t n_rows, int64_t n_blocks, int64_t stride_row, int64_t stride_block,
+                       int64_t stride_byte, void* d, void* qs, void* qh, void* signs, void* scales,
+                       mambo_stream_t stream);
+
+/*
+ * Standalone decoder: values u8 [N, B*256] signed E4M3 bytes, scales f32 [N, B*8] = d*(1+2*nibble).
+ * fp8_table: device uint32[512], the codebook with magnitudes as E4M3 bytes.
+ * Replaces decode_iq3_s_blocks / launch_dequant_iq3_s (src/python/mambo/kernels/iq3_s_fp8.py:202-222,341-351).
+ */
+MAMBO_API int mambo_iq3s_decode(const MamboIQ3SWeight* w, const uint32_t* fp8_table, uint8_t* values, float* scales,
+                      mambo_stream_t stream);
+
+/*
+ * MXFP8 activation quantization: x [M, K] (f32 or bf16, row stride ldx elements,
+ * K % 32 == 0) -> q u8 [M, K] E4M3 (row stride ldq) and s u8 [M, K/32] UE8M0
+ * (row stride lds). Scale exponent e = clamp(ceil(log2(amax/448)), -127, 127),
+ * amax == 0 -> e = 0; q = E4M3(x * 2^-e) with the given rounding.
+ * Replaces quantize_activation_fp8 / launch_quantize_fp8 (src/python/mambo/kernels/quantize_fp8.py:23-52,67-84).
+ */
+MAMBO_API int mambo_quantize_mxfp8(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, uint8_t* q, int64_t ldq,
+                         uint8_t* s, int64_t lds, int rounding, mambo_stream_t stream);
+
+/*
+ * IQ3_S x MXFP8 linear: out[M, N] = decode_mxfp8(xq, xs) @ dequant(w).T, FP32
+ * accumulation, each 32-weight group's partial product scaled by d*(1+2*nibble)
+ * in FP32. xq u8 [M, K] (row stride ldxq), xs u8 [M, K/32] (row stride ldxs),
+ * out f32 or bf16 [M, N] (row stride ldo). workspace: device scratch of
+ * mambo_iq3s_linear_workspace_bytes() bytes, zero-filled once when it is
+ * allocated (the kernels leave it zeroed again). Calls that share a workspace
+ * must not overlap on the GPU.
+ * Replaces iq3_s_fp8_matmul / iq3_s_fp8_matmul_medium / launch_iq3_s_fp8_matmul
+ * (src/python/mambo/kernels/iq3_s_fp8.py:225-333,364-399).
+ */
+MAMBO_API int mambo_iq3s_linear(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t ldxs, int64_t m,
+                      const MamboIQ3SWeight* w, const uint32_t* fp8_table, void* out, int out_dtype, int64_t ldo,
+                      const MamboLinearConfig* cfg, void* workspace, size_t workspace_bytes, mambo_stream_t stream);
+
+/* Workspace bytes mambo_iq3s_linear needs for this shape and configuration. */
+MAMBO_API size_t mambo_iq3s_linear_workspace_bytes(int64_t m, int64_t n_rows, int64_t n_blocks, const MamboLinearConfig* cfg);
+
+/* Number of tunable configurations of a kernel kind, and the i-th one (for the autotuner).
+ * Replaces the search spaces of make_benchmark_cases (src/python/mambo/kernels/iq3_s_fp8.py:402-465). */
+MAMBO_API int mambo_num_configs(int kernel);
+MAMBO_API int mambo_config_at(int kernel, int index, MamboLinearConfig* cfg);
+
+/* Tuned default configuration for a shape (what NULL cfg resolves to). */
+MAMBO_API int mambo_default_config(int64_t m, int64_t n_rows, int64_t n_blocks, MamboLinearConfig* cfg);
+
+/*
+ * Device-side failure channel (no counterpart in the reference, whose kernels
+ * have no waits). Every wait of the pipelined kernels is bounded: when one
+ * gives up it records MAMBO_ETIMEOUT with a site id and returns instead of
+ * hanging. mambo_device_status reads (and with reset != 0 clears) that record;
+ * it synchronizes with the device.
+ */
+MAMBO_API int mambo_device_status(int reset, int* code, int* where, int* block);
+/* Wall-clock limit of one bounded device wait (default 1 s). */
+MAMBO_API int mambo_set_wait_limit_ns(unsigned long long ns);
+/* Launches a kernel whose bounded wait on a barrier nothing completes gives up
+ * after limit_ns; afterwards mambo_device_status reports MAMBO_ETIMEOUT. */
+MAMBO_API int mambo_selftest_wait_timeout(unsigned long long limit_ns, mambo_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MAMBO_B200_H */

@@ -1,0 +1,374 @@
+// C ABI of libmambo_b200 (declared in include/mambo_b200.h).
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "kernels.cuh"
+
+namespace mambo {
+
+__device__ DeviceStatus g_device_status = {0, 0, 0, 0};
+__device__ unsigned long long g_wait_limit_ns = 1000000000ull;  // 1 s
+
+// Trivial kernel: its attributes tell whether this library's sm_100a image loads on the device.
+__global__ void probe_kernel() {}
+cudaError_t probe_kernel_image() {
+  cudaFuncAttributes attr;
+  return cudaFuncGetAttributes(&attr, probe_kernel);
+}
+
+// Waits on an mbarrier that nothing arrives at: the bounded wait must give up
+// after limit_ns, record MAMBO_ETIMEOUT in the device status and return.
+__global__ void wait_selftest_kernel(unsigned long long limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bar), 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint32_t addr = smem_u32(&bar);
+    const unsigned long long t0 = globaltimer_ns();
+    bool done = false;
+    for (uint32_t i = 1; !done; ++i) {
+      done = mbar_try_wait(addr, 0);
+      if (!done && (i & 63u) == 0 && globaltimer_ns() - t0 > limit_ns) {
+        record_timeout(kSiteSelfTest);
+        break;
+      }
+    }
+    // Complete the phase ourselves so the barrier is not left pending.
+    mbar_arrive(addr);
+  }
+}
+
+cudaError_t launch_wait_selftest(unsigned long long limit_ns, cudaStream_t stream) {
+  wait_selftest_kernel<<<1, 32, 0, stream>>>(limit_ns);
+  return cudaGetLastError();
+}
+
+}  // namespace mambo
+
+using namespace mambo;
+
+namespace {
+
+thread_local std::string g_last_error;
+thread_local int g_last_code = MAMBO_OK;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  g_last_code = code;
+  return code;
+}
+
+int ok() {
+  g_last_code = MAMBO_OK;
+  return MAMBO_OK;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  if (e == cudaErrorNoKernelImageForDevice || e == cudaErrorInvalidDeviceFunction)
+    return fail(MAMBO_ENOTSUPPORTED, "%s: %s (this library is built for sm_100a only)", what, cudaGetErrorString(e));
+  return fail(MAMBO_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+struct DeviceInfo {
+  int sms = 0;
+  int major = 0, minor = 0;
+  int max_smem_optin = 0;
+};
+
+DeviceInfo device_info(int* status) {
+  static std::mutex mu;
+  static DeviceInfo cache[64];
+  static bool have[64] = {false};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    *status = cuda_fail(e == cudaSuccess ? cudaErrorInvalidDevice : e, "cudaGetDevice");
+    return DeviceInfo{};
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!have[dev]) {
+    DeviceInfo d;
+    cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev);
+    cudaDeviceGetAttribute(&d.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cache[dev] = d;
+    have[dev] = true;
+  }
+  *status = MAMBO_OK;
+  return cache[dev];
+}
+
+int require_sm100(DeviceInfo* info) {
+  int st;
+  *info = device_info(&st);
+  if (st != MAMBO_OK) return st;
+  if (info->major != 10 || info->minor != 0)
+    return fail(MAMBO_ENOTSUPPORTED, "IQ3_S FP8 kernels have no build for sm%d%d (this library targets sm_100a)",
+                info->major, info->minor);
+  return MAMBO_OK;
+}
+
+// --- configurations ---------------------------------------------------------
+// GEMV search space: warps x stages (tokens per launch follow M).
+const int kGemvWarps[] = {4, 8};
+const int kGemvStages[] = {3, 4, 6, 8};
+constexpr int kNumGemvConfigs = 2 * 4 * 2;
+
+int gemv_nt_for(int64_t m) { return m <= 8 ? 1 : (m <= 16 ? 2 : 4); }
+
+void default_config(int64_t m, int64_t n, int64_t b, MamboLinearConfig* cfg) {
+  (void)n;
+  (void)b;
+  std::memset(cfg, 0, sizeof(*cfg));
+  cfg->kernel = MAMBO_KERNEL_GEMV;
+  cfg->warps = 8;
+  cfg->stages = gemv_nt_for(m) == 4 ? 5 : 6;
+  cfg->ctas_per_sm = 1;
+  cfg->split = 0;
+}
+
+int validate_config(const MamboLinearConfig* cfg, int64_t m, const DeviceInfo& info) {
+  if (cfg->kernel != MAMBO_KERNEL_GEMV && cfg->kernel != MAMBO_KERNEL_AUTO)
+    return fail(MAMBO_EINVAL, "unknown kernel kind %d", cfg->kernel);
+  if (cfg->warps != 4 && cfg->warps != 8) return fail(MAMBO_EINVAL, "warps must be 4 or 8");
+  if (cfg->stages < 2 || cfg->stages > 12) return fail(MAMBO_EINVAL, "stages must be in [2, 12]");
+  const uint32_t smem = gemv_smem_bytes_host(cfg->warps * 16, gemv_nt_for(m), cfg->stages);
+  if ((int)smem > info.max_smem_optin)
+    return fail(MAMBO_EINVAL, "configuration needs %u bytes of shared memory (device allows %d)", smem,
+                info.max_smem_optin);
+  return MAMBO_OK;
+}
+
+struct GemvPlan {
+  int nt, rows, row_tiles, units, grid;
+  size_t counters_bytes, partial_bytes;
+};
+
+GemvPlan plan_gemv(int64_t m_chunk, int64_t n, int64_t b, const MamboLinearConfig& cfg, int sms) {
+  GemvPlan P{};
+  P.nt = gemv_nt_for(m_chunk);
+  P.rows = cfg.warps * 16;
+  P.row_tiles = (int)((n + P.rows - 1) / P.rows);
+  P.units = (int)(P.row_tiles * b);
+  int ctas = sms * (cfg.ctas_per_sm > 0 ? cfg.ctas_per_sm : 1);
+  if (cfg.split == 1) ctas = P.row_tiles;  // one CTA per row tile, no split-K
+  P.grid = P.units < ctas ? P.units : ctas;
+  if (P.grid < 1) P.grid = 1;
+  P.counters_bytes = ((size_t)P.row_tiles * cfg.warps * sizeof(int) + 255) / 256 * 256;
+  P.partial_bytes = (size_t)P.grid * 2 * P.rows * 8 * P.nt * sizeof(float);
+  return P;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* mambo_version(void) { return "mambo_b200 0.1.0 (sm_100a)"; }
+
+int mambo_last_error(char* buf, size_t len) {
+  if (buf && len) {
+    std::strncpy(buf, g_last_error.c_str(), len - 1);
+    buf[len - 1] = '\0';
+  }
+  return g_last_code;
+}
+
+int mambo_device_check(void) {
+  DeviceInfo info;
+  int st = require_sm100(&info);
+  if (st != MAMBO_OK) return st;
+  cudaError_t e = probe_kernel_image();
+  if (e != cudaSuccess) return cuda_fail(e, "loading the sm_100a kernel image");
+  return ok();
+}
+
+int mambo_device_status(int reset, int* code, int* where, int* block) {
+  DeviceStatus st{};
+  cudaError_t e = cudaMemcpyFromSymbol(&st, g_device_status, sizeof(st));
+  if (e != cudaSuccess) return cuda_fail(e, "reading the device status");
+  if (code) *code = st.code;
+  if (where) *where = st.where;
+  if (block) *block = st.block;
+  if (reset) {
+    DeviceStatus zero{};
+    e = cudaMemcpyToSymbol(g_device_status, &zero, sizeof(zero));
+    if (e != cudaSuccess) return cuda_fail(e, "resetting the device status");
+  }
+  return ok();
+}
+
+int mambo_set_wait_limit_ns(unsigned long long ns) {
+  cudaError_t e = cudaMemcpyToSymbol(g_wait_limit_ns, &ns, sizeof(ns));
+  if (e != cudaSuccess) return cuda_fail(e, "setting the wait limit");
+  return ok();
+}
+
+int mambo_selftest_wait_timeout(unsigned long long limit_ns, mambo_stream_t stream) {
+  DeviceInfo info;
+  int st = require_sm100(&info);
+  if (st != MAMBO_OK) return st;
+  cudaError_t e = launch_wait_selftest(limit_ns, (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "launching the wait self-test");
+  return ok();
+}
+
+int mambo_iq3s_prepare(const uint8_t* raw, int64_t n_rows, int64_t n_blocks, int64_t stride_row,
+                       int64_t stride_block, int64_t stride_byte, void* d, void* qs, void* qh, void* signs,
+                       void* scales, mambo_stream_t stream) {
+  if (!raw || !d || !qs || !qh || !signs || !scales) return fail(MAMBO_EINVAL, "null pointer");
+  if (n_rows < 1 || n_blocks < 1) return fail(MAMBO_EINVAL, "IQ3_S weight must have positive N and K");
+  DeviceInfo info;
+  int st = require_sm100(&info);
+  if (st != MAMBO_OK) return st;
+  PrepareParams p{raw, n_rows, n_blocks, stride_row, stride_block, stride_byte,
+                  {(uint8_t*)d, (uint8_t*)qs, (uint8_t*)qh, (uint8_t*)signs, (uint8_t*)scales}};
+  cudaError_t e = launch_iq3s_prepare(p, info.sms, (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "iq3s_prepare");
+  return ok();
+}
+
+int mambo_iq3s_decode(const MamboIQ3SWeight* w, const uint32_t* fp8_table, uint8_t* values, float* scales,
+                      mambo_stream_t stream) {
+  if (!w || !fp8_table || !values || !scales) return fail(MAMBO_EINVAL, "null pointer");
+  if (w->n_rows < 1 || w->n_blocks < 1) return fail(MAMBO_EINVAL, "IQ3_S weight must have positive N and K");
+  if ((uintptr_t)values % 8) return fail(MAMBO_EINVAL, "values must be 8-byte aligned");
+  DeviceInfo info;
+  int st = require_sm100(&info);
+  if (st != MAMBO_OK) return st;
+  DecodeParams p{(const uint8_t*)w->d, (const uint8_t*)w->qs, (const uint8_t*)w->qh, (const uint8_t*)w->signs,
+                 (const uint8_t*)w->scales, w->n_rows, w->n_blocks, fp8_table, values, scales};
+  cudaError_t e = launch_iq3s_decode(p, info.sms, (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "iq3s_decode");
+  return ok();
+}
+
+int mambo_quantize_mxfp8(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, uint8_t* q, int64_t ldq,
+                         uint8_t* s, int64_t lds, int rounding, mambo_stream_t stream) {
+  if (!x || !q || !s) return fail(MAMBO_EINVAL, "null pointer");
+  if (x_dtype != MAMBO_F32 && x_dtype != MAMBO_BF16) return fail(MAMBO_EINVAL, "activation must be f32 or bf16");
+  if (m < 1 || k < 32 || k % 32) return fail(MAMBO_EINVAL, "activation must be [M,K] with K divisible by 32");
+  if (ldx < k || ldq < k || lds < k / 32) return fail(MAMBO_EINVAL, "row stride smaller than the row");
+  if (rounding != MAMBO_ROUND_NEAREST_EVEN && rounding != MAMBO_ROUND_TIES_DOWN)
+    return fail(MAMBO_EINVAL, "unknown rounding mode %d", rounding);
+  DeviceInfo info;
+  int st = require_sm100(&info);
+  if (st != MAMBO_OK) return st;
+  QuantParams p{x, m, k, ldx, q, ldq, s, lds};
+  cudaError_t e = launch_quantize_mxfp8(p, x_dtype, rounding, info.sms, (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "quantize_mxfp8");
+  return ok();
+}
+
+int mambo_default_config(int64_t m, int64_t n_rows, int64_t n_blocks, MamboLinearConfig* cfg) {
+  if (!cfg) return fail(MAMBO_EINVAL, "null config");
+  default_config(m, n_rows, n_blocks, cfg);
+  return ok();
+}
+
+int mambo_num_configs(int kernel) {
+  if (kernel == MAMBO_KERNEL_GEMV || kernel == MAMBO_KERNEL_AUTO) return kNumGemvConfigs;
+  return 0;
+}
+
+int mambo_config_at(int kernel, int index, MamboLinearConfig* cfg) {
+  if (!cfg) return fail(MAMBO_EINVAL, "null config");
+  if ((kernel != MAMBO_KERNEL_GEMV && kernel != MAMBO_KERNEL_AUTO) || index < 0 || index >= kNumGemvConfigs)
+    return fail(MAMBO_EINVAL, "no configuration %d for kernel %d", index, kernel);
+  std::memset(cfg, 0, sizeof(*cfg));
+  cfg->kernel = MAMBO_KERNEL_GEMV;
+  cfg->warps = kGemvWarps[index / 8];
+  cfg->stages = kGemvStages[(index / 2) % 4];
+  cfg->split = index % 2;
+  cfg->ctas_per_sm = 1;
+  return ok();
+}
+
+size_t mambo_iq3s_linear_workspace_bytes(int64_t m, int64_t n_rows, int64_t n_blocks, const MamboLinearConfig* cfg) {
+  MamboLinearConfig c;
+  if (cfg) c = *cfg; else default_config(m, n_rows, n_blocks, &c);
+  int st;
+  DeviceInfo info = device_info(&st);
+  const int sms = (st == MAMBO_OK && info.sms > 0) ? info.sms : 148;
+  const int64_t m_chunk = m < 32 ? m : 32;
+  GemvPlan P = plan_gemv(m_chunk, n_rows, n_blocks, c, sms);
+  return P.counters_bytes + P.partial_bytes;
+}
+
+int mambo_iq3s_linear(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t ldxs, int64_t m,
+                      const MamboIQ3SWeight* w, const uint32_t* fp8_table, void* out, int out_dtype, int64_t ldo,
+                      const MamboLinearConfig* cfg, void* workspace, size_t workspace_bytes, mambo_stream_t stream) {
+  if (!xq || !xs || !w || !fp8_table || !out) return fail(MAMBO_EINVAL, "null pointer");
+  if (!w->d || !w->qs || !w->qh || !w->signs || !w->scales) return fail(MAMBO_EINVAL, "null weight field");
+  if (w->n_rows < 1 || w->n_blocks < 1) return fail(MAMBO_EINVAL, "IQ3_S weight must have positive N and K");
+  if (w->n_rows > (1 << 30) || w->n_blocks > (1 << 20)) return fail(MAMBO_EINVAL, "weight too large");
+  const int64_t k = w->n_blocks * 256;
+  if (m < 1) return fail(MAMBO_EINVAL, "x_values must be uint8 [M,K] with M >= 1");
+  if (ldxq < k) return fail(MAMBO_EINVAL, "x_values row stride %lld is smaller than K=%lld", (long long)ldxq,
+                            (long long)k);
+  if (ldxs < k / 32) return fail(MAMBO_EINVAL, "x_scales row stride is smaller than K/32");
+  if (out_dtype != MAMBO_F32 && out_dtype != MAMBO_BF16) return fail(MAMBO_EINVAL, "out must be f32 or bf16");
+  if (ldo < w->n_rows) return fail(MAMBO_EINVAL, "out row stride is smaller than N");
+  DeviceInfo info;
+  int st = require_sm100(&info);
+  if (st != MAMBO_OK) return st;
+  MamboLinearConfig c;
+  if (cfg) c = *cfg; else default_config(m, w->n_rows, w->n_blocks, &c);
+  if (c.kernel == MAMBO_KERNEL_AUTO) c.kernel = MAMBO_KERNEL_GEMV;
+  st = validate_config(&c, m < 32 ? m : 32, info);
+  if (st != MAMBO_OK) return st;
+
+  const int64_t m_chunk_max = 32;
+  for (int64_t m0 = 0; m0 < m; m0 += m_chunk_max) {
+    const int64_t mc = (m - m0) < m_chunk_max ? (m - m0) : m_chunk_max;
+    GemvPlan P = plan_gemv(mc, w->n_rows, w->n_blocks, c, info.sms);
+    const size_t need = P.counters_bytes + P.partial_bytes;
+    if (!workspace || workspace_bytes < need)
+      return fail(MAMBO_EWORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+    GemvParams p{};
+    p.xq = xq + m0 * ldxq;
+    p.ldxq = ldxq;
+    p.xs = xs + m0 * ldxs;
+    p.ldxs = ldxs;
+    p.m = (int)mc;
+    p.n_rows = (int)w->n_rows;
+    p.n_blocks = (int)w->n_blocks;
+    p.d = (const uint8_t*)w->d;
+    p.qs = (const uint8_t*)w->qs;
+    p.qh = (const uint8_t*)w->qh;
+    p.signs = (const uint8_t*)w->signs;
+    p.scales = (const uint8_t*)w->scales;
+    p.table = fp8_table;
+    const size_t esz = out_dtype == MAMBO_BF16 ? 2 : 4;
+    p.out = (uint8_t*)out + m0 * ldo * esz;
+    p.out_bf16 = out_dtype == MAMBO_BF16;
+    p.ldo = ldo;
+    p.counters = (int*)workspace;
+    p.partials = (float*)((uint8_t*)workspace + P.counters_bytes);
+    p.warps = c.warps;
+    p.stages = c.stages;
+    p.row_tiles = P.row_tiles;
+    p.total_units = P.units;
+    p.x_vec = ((uintptr_t)p.xq % 16 == 0) && (ldxq % 16 == 0);
+    p.xs_vec = ((uintptr_t)p.xs % 8 == 0) && (ldxs % 8 == 0);
+    GemvMaps maps;
+    std::memset(&maps, 0, sizeof(maps));
+    const bool use_tma = (c.loader == 0) && make_gemv_maps(p, &maps);
+    cudaError_t e = launch_gemv(p, P.nt, use_tma, maps, P.grid, (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(e, "iq3s_gemv");
+  }
+  return ok();
+}
+
+}  // extern "C"

@@ -1,0 +1,78 @@
+// Parameter blocks and launchers shared between the kernel files and the C ABI.
+#pragma once
+
+#include "common.cuh"
+
+namespace mambo {
+
+struct QuantParams {
+  const void* x;
+  int64_t m, k, ldx;
+  uint8_t* q;
+  int64_t ldq;
+  uint8_t* s;
+  int64_t lds;
+};
+cudaError_t launch_quantize_mxfp8(const QuantParams& p, int x_dtype, int rounding, int num_sms, cudaStream_t stream);
+
+struct PrepareParams {
+  const uint8_t* raw;
+  int64_t n_rows, n_blocks, stride_row, stride_block, stride_byte;
+  uint8_t* dst[5];
+};
+cudaError_t launch_iq3s_prepare(const PrepareParams& p, int num_sms, cudaStream_t stream);
+
+struct DecodeParams {
+  const uint8_t* d;
+  const uint8_t* qs;
+  const uint8_t* qh;
+  const uint8_t* signs;
+  const uint8_t* scales;
+  int64_t n_rows, n_blocks;
+  const uint32_t* table;  // uint32[512], E4M3-encoded magnitudes
+  uint8_t* values;        // [N, B*256]
+  float* out_scales;      // [N, B*8]
+};
+cudaError_t launch_iq3s_decode(const DecodeParams& p, int num_sms, cudaStream_t stream);
+
+struct GemvParams {
+  const uint8_t* xq;
+  int64_t ldxq;
+  const uint8_t* xs;
+  int64_t ldxs;
+  int m;
+  int n_rows;
+  int n_blocks;
+  // SoA weight fields (the TMA loader reads them through the tensor maps)
+  const uint8_t* d;
+  const uint8_t* qs;
+  const uint8_t* qh;
+  const uint8_t* signs;
+  const uint8_t* scales;
+  const uint32_t* table;
+  void* out;
+  int out_bf16;
+  int64_t ldo;
+  float* partials;  // [grid][2][rows][8*NT]
+  int* counters;    // [row_tiles][warps], zero between launches
+  int warps;        // consumer warps (16 weight rows each)
+  int stages;
+  int row_tiles;
+  int total_units;
+  int x_vec;   // xq rows 16-byte aligned
+  int xs_vec;  // xs rows 8-byte aligned
+};
+
+struct GemvMaps {
+  CUtensorMap qs, signs, qh, d, scales;
+};
+
+bool make_gemv_maps(const GemvParams& p, GemvMaps* maps);
+cudaError_t launch_gemv(const GemvParams& p, int nt, bool use_tma, const GemvMaps& maps, int grid,
+                        cudaStream_t stream);
+uint32_t gemv_smem_bytes_host(int rows, int nt, int stages);
+
+cudaError_t launch_wait_selftest(unsigned long long limit_ns, cudaStream_t stream);
+cudaError_t probe_kernel_image();
+
+}  // namespace mambo

@@ -1,0 +1,83 @@
+// IQ3_S weight preparation (AoS GGUF blocks -> SoA fields) and the standalone
+// decoder used by the bit-exactness tests.
+#include "kernels.cuh"
+
+namespace mambo {
+
+// Field sizes and byte offsets inside one 110-byte block
+// (src/python/mambo/utils/iq3_s_weight.py:26-33): d 0..1, qs 2..65, qh 66..73,
+// signs 74..105, scales 106..109.
+__device__ __forceinline__ void field_of_byte(int byte, int& field, int& off, int& size) {
+  if (byte < 2) { field = 0; off = 0; size = 2; }
+  else if (byte < 66) { field = 1; off = 2; size = 64; }
+  else if (byte < 74) { field = 2; off = 66; size = 8; }
+  else if (byte < 106) { field = 3; off = 74; size = 32; }
+  else { field = 4; off = 106; size = 4; }
+}
+
+// One thread per source byte; raw may have any strides and alignment
+// (prepare_iq3_s_fields accepts odd-address and strided views, test_iq3_s_fp8.py:118-131).
+__global__ void iq3s_prepare_kernel(const PrepareParams p) {
+  const int64_t total = p.n_rows * p.n_blocks * 110;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int byte = (int)(i % 110);
+    const int64_t nb = i / 110;
+    const int64_t b = nb % p.n_blocks;
+    const int64_t n = nb / p.n_blocks;
+    const uint8_t v = p.raw[n * p.stride_row + b * p.stride_block + byte * p.stride_byte];
+    int field, off, size;
+    field_of_byte(byte, field, off, size);
+    p.dst[field][(b * p.n_rows + n) * size + (byte - off)] = v;
+  }
+}
+
+cudaError_t launch_iq3s_prepare(const PrepareParams& p, int num_sms, cudaStream_t stream) {
+  const int64_t total = p.n_rows * p.n_blocks * 110;
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > (int64_t)num_sms * 32) blocks = (int64_t)num_sms * 32;
+  if (blocks < 1) blocks = 1;
+  iq3s_prepare_kernel<<<(int)blocks, 256, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+// One warp per (row, block): lane l decodes codes 2l and 2l+1 (weights 8l..8l+7).
+// Mirrors decode_iq3_s_blocks (src/python/mambo/kernels/iq3_s_fp8.py:202-222).
+__global__ void iq3s_decode_kernel(const DecodeParams p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
+  for (int64_t wb = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; wb < p.n_rows * p.n_blocks;
+       wb += warps) {
+    const int64_t n = wb / p.n_blocks;
+    const int64_t b = wb % p.n_blocks;
+    const int64_t blk = b * p.n_rows + n;  // SoA index
+    const int g = lane >> 2;               // 32-weight group of this lane's codes
+    const uint32_t q0 = p.qs[blk * 64 + 2 * lane];
+    const uint32_t q1 = p.qs[blk * 64 + 2 * lane + 1];
+    const uint32_t hbyte = p.qh[blk * 8 + g];
+    const uint32_t c0 = 2 * (lane & 3), c1 = c0 + 1;  // code index inside the group
+    const uint32_t i0 = q0 | (((hbyte >> c0) & 1u) << 8);
+    const uint32_t i1 = q1 | (((hbyte >> c1) & 1u) << 8);
+    const uint32_t sbyte = p.signs[blk * 32 + lane];  // weights 8l..8l+7
+    const uint32_t w0 = __ldg(p.table + i0) | (((sbyte & 0xFu) * 0x10204080u) & 0x80808080u);
+    const uint32_t w1 = __ldg(p.table + i1) | (((sbyte >> 4) * 0x10204080u) & 0x80808080u);
+    uint2* dst = reinterpret_cast<uint2*>(p.values + n * (p.n_blocks * 256) + b * 256 + 8 * lane);
+    *dst = make_uint2(w0, w1);
+    if (lane < 8) {
+      const uint16_t dh = (uint16_t)(p.d[blk * 2] | (p.d[blk * 2 + 1] << 8));
+      const float dv = __half2float(__ushort_as_half(dh));
+      const uint32_t nib = (p.scales[blk * 4 + lane / 2] >> (4 * (lane & 1))) & 0xFu;
+      p.out_scales[n * (p.n_blocks * 8) + b * 8 + lane] = dv * (float)(1u + 2u * nib);
+    }
+  }
+}
+
+cudaError_t launch_iq3s_decode(const DecodeParams& p, int num_sms, cudaStream_t stream) {
+  const int64_t warps = p.n_rows * p.n_blocks;
+  int64_t blocks = (warps + 7) / 8;
+  if (blocks > (int64_t)num_sms * 16) blocks = (int64_t)num_sms * 16;
+  if (blocks < 1) blocks = 1;
+  iq3s_decode_kernel<<<(int)blocks, 256, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace mambo

@@ -1,0 +1,185 @@
+// MXFP8 activation quantization (sm_100a).
+//
+// Restates quantize_fp8_group / quantize_activation_fp8
+// (src/python/mambo/kernels/quantize_fp8.py:23-52): per 32 consecutive values
+// along K, amax -> e = clamp(ceil(log2(amax/448)), -127, 127) (amax == 0 -> 0),
+// q = E4M3(x * 2^-e), scale byte e + 127. The exponent is computed exactly
+// from the bits of amax (no log2 approximation).
+//
+// Layout: each warp quantizes 8 groups per step; 4 lanes own one group of 32
+// (8 values each, one 128-bit load for bf16 / two for f32), amax is reduced
+// with two quad shuffles, and each lane writes its 8 E4M3 bytes as one 64-bit
+// store (a warp writes 256 contiguous bytes).
+#include "kernels.cuh"
+
+namespace mambo {
+
+// Exact MXFP8 block exponent from the float bits of amax (amax >= 0).
+// Returns the UE8M0 scale code, 0xFF for a non-finite amax.
+__device__ __forceinline__ uint32_t mxfp8_scale_code(float amax) {
+  const uint32_t bits = __float_as_uint(amax);
+  const uint32_t biased = bits >> 23;  // sign is 0
+  if (bits == 0) return 127u;          // amax == 0 -> e = 0
+  if (biased == 0xFF) return 0xFFu;    // Inf / NaN
+  if (biased == 0) return 0u;          // subnormal amax -> e clamps to -127
+  // amax = 1.m * 2^(biased-127); 448 = 1.75 * 2^8.
+  int e = (int)biased - 127 - ((bits & 0x7FFFFFu) <= 0x600000u ? 8 : 7);
+  e = max(-127, min(127, e));
+  return (uint32_t)(e + 127);
+}
+
+// Two floats -> two E4M3 bytes (lo in bits 0..7), round-to-nearest-even, saturating.
+__device__ __forceinline__ uint32_t cvt_e4m3x2_rn(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+__device__ __forceinline__ float e4m3_to_float(uint32_t byte) {
+  uint32_t h2;
+  const uint16_t in = (uint16_t)(byte & 0xFFu);
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(in));
+  return __half2float(__ushort_as_half((unsigned short)(h2 & 0xFFFFu)));
+}
+
+// Round-to-nearest with exact ties resolved toward the smaller magnitude:
+// start from the RNE code and step the magnitude down by one code when y sat
+// exactly halfway and RNE rounded away from zero. All differences are exact.
+__device__ __forceinline__ uint32_t fix_tie_down(uint32_t code, float y) {
+  const uint32_t mag = code & 0x7Fu;
+  if (mag == 0) return code;
+  const float ay = fabsf(y);
+  const float up = e4m3_to_float(mag);
+  if (!(up > ay)) return code;
+  const float down = e4m3_to_float(mag - 1u);
+  return (up - ay == ay - down) ? ((code & 0x80u) | (mag - 1u)) : code;
+}
+
+template <typename T, bool kVec, int kRounding>
+__global__ void __launch_bounds__(256) quantize_mxfp8_kernel(const QuantParams p) {
+  const int lane = threadIdx.x & 31;
+  const int quad_lane = lane & 3;
+  const int64_t groups_per_row = p.k / 32;
+  const int64_t total_groups = p.m * groups_per_row;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
+  const int64_t warp_id = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const T* x = static_cast<const T*>(p.x);
+
+  for (int64_t base = warp_id * 8; base < total_groups; base += warps * 8) {
+    const int64_t grp = base + (lane >> 2);
+    const bool active = grp < total_groups;
+    const int64_t row = active ? grp / groups_per_row : 0;
+    const int64_t cg = active ? grp - row * groups_per_row : 0;
+    const T* src = x + row * p.ldx + cg * 32 + quad_lane * 8;
+
+    float v[8];
+    if (active) {
+      if constexpr (sizeof(T) == 2) {
+        if constexpr (kVec) {
+          const uint4 raw = __ldg(reinterpret_cast<const uint4*>(src));
+          const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            v[2 * i] = __uint_as_float(w[i] << 16);
+            v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+          }
+        } else {
+          const uint16_t* s16 = reinterpret_cast<const uint16_t*>(src);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[i] = __uint_as_float((uint32_t)__ldg(s16 + i) << 16);
+        }
+      } else {
+        if constexpr (kVec) {
+          const float4 a = __ldg(reinterpret_cast<const float4*>(src));
+          const float4 b = __ldg(reinterpret_cast<const float4*>(src) + 1);
+          v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+          v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+        } else {
+          const float* sf = reinterpret_cast<const float*>(src);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[i] = __ldg(sf + i);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = 0.f;
+    }
+
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    // fmaxf drops NaN; keep it visible so the group gets the NaN scale code.
+    bool any_nan = false;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) any_nan |= (v[i] != v[i]);
+    amax = any_nan ? __uint_as_float(0x7FC00000u) : amax;
+    float other = __shfl_xor_sync(0xFFFFFFFFu, amax, 1);
+    amax = (other != other) ? other : fmaxf(amax, other);
+    other = __shfl_xor_sync(0xFFFFFFFFu, amax, 2);
+    amax = (other != other) ? other : fmaxf(amax, other);
+
+    const uint32_t code = mxfp8_scale_code(amax);
+    // 2^-e with e = code - 127 (code 0xFF: scale by 2^-127, values become 0 / NaN / +-448).
+    const float inv = e8m0_to_float(code == 0xFFu ? 0u : 254u - code);
+
+    uint32_t packed[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      float y[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) y[i] = v[4 * h + i] * inv;
+      uint32_t lo = cvt_e4m3x2_rn(y[0], y[1]);
+      uint32_t hi = cvt_e4m3x2_rn(y[2], y[3]);
+      if constexpr (kRounding == MAMBO_ROUND_TIES_DOWN) {
+        uint32_t b0 = fix_tie_down(lo & 0xFFu, y[0]), b1 = fix_tie_down(lo >> 8, y[1]);
+        uint32_t b2 = fix_tie_down(hi & 0xFFu, y[2]), b3 = fix_tie_down(hi >> 8, y[3]);
+        lo = b0 | (b1 << 8);
+        hi = b2 | (b3 << 8);
+      }
+      packed[h] = lo | (hi << 16);
+    }
+
+    if (active) {
+      uint8_t* dst = p.q + row * p.ldq + cg * 32 + quad_lane * 8;
+      if constexpr (kVec) {
+        *reinterpret_cast<uint2*>(dst) = make_uint2(packed[0], packed[1]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) dst[i] = (uint8_t)(packed[i / 4] >> (8 * (i % 4)));
+      }
+      if (quad_lane == 0) p.s[row * p.lds + cg] = (uint8_t)code;
+    }
+  }
+}
+
+template <typename T, bool kVec>
+static cudaError_t launch_quant_t(const QuantParams& p, int rounding, int grid, cudaStream_t stream) {
+  if (rounding == MAMBO_ROUND_TIES_DOWN) {
+    quantize_mxfp8_kernel<T, kVec, MAMBO_ROUND_TIES_DOWN><<<grid, 256, 0, stream>>>(p);
+  } else {
+    quantize_mxfp8_kernel<T, kVec, MAMBO_ROUND_NEAREST_EVEN><<<grid, 256, 0, stream>>>(p);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_mxfp8(const QuantParams& p, int x_dtype, int rounding, int num_sms, cudaStream_t stream) {
+  const int64_t groups = p.m * (p.k / 32);
+  const int64_t warp_steps = (groups + 7) / 8;
+  int64_t blocks = (warp_steps + 7) / 8;  // 8 warps per block
+  const int64_t cap = (int64_t)num_sms * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  const uintptr_t xa = reinterpret_cast<uintptr_t>(p.x);
+  const uintptr_t qa = reinterpret_cast<uintptr_t>(p.q);
+  const bool q_vec = (qa % 8 == 0) && (p.ldq % 8 == 0);
+  if (x_dtype == MAMBO_BF16) {
+    const bool vec = q_vec && (xa % 16 == 0) && (p.ldx % 8 == 0);
+    return vec ? launch_quant_t<uint16_t, true>(p, rounding, (int)blocks, stream)
+               : launch_quant_t<uint16_t, false>(p, rounding, (int)blocks, stream);
+  }
+  const bool vec = q_vec && (xa % 16 == 0) && (p.ldx % 4 == 0);
+  return vec ? launch_quant_t<float, true>(p, rounding, (int)blocks, stream)
+             : launch_quant_t<float, false>(p, rounding, (int)blocks, stream);
+}
+
+}  // namespace mambo

@@ -1,0 +1,294 @@
+"""IQ3_S block decode and block-scaled FP8 projection on sm_100a (B200).
+
+Mirror of src/python/mambo/kernels/iq3_s_fp8.py (Menooker/Mambo): the same
+constants, codebook helpers, launch wrappers, errors and benchmark-case
+factory. The kernels are hand-written CUDA in libmambo_b200.so:
+
+* decode-sized M (< LARGE_TOKEN_THRESHOLD... and up to 32 tokens per launch):
+  a weight-streaming GEMV that stages IQ3_S fields with TMA, decodes each
+  IQ3_S code straight into an FP8 tensor-core fragment and splits K across all
+  SMs (stream-K, deterministic fixup);
+* the standalone decoder used by the bit-exactness tests.
+
+Arithmetic follows the reference exactly: every 32-weight group's E4M3 x E4M3
+product is accumulated in FP32 by the tensor core and scaled in FP32 by
+d*(1+2*nibble) and the activation's UE8M0 scale.
+
+One IQ3_S block along K (256 weights, 110 bytes):
+
+    byte  0..1   | d: FP16 base scale                 |  2 bytes
+    byte  2..65  | qs: 64 low 8-bit codebook indices  | 64 bytes
+    byte 66..73  | qh: 64 high index bits             |  8 bytes
+    byte 74..105 | signs: one bit per weight          | 32 bytes
+    byte 106..109| scales: 8 packed 4-bit values      |  4 bytes
+"""
+
+from __future__ import annotations
+
+import json
+import os
+import re
+import threading
+from functools import lru_cache
+from pathlib import Path
+
+import numpy as np
+import torch
+
+from .. import _lib, _runtime
+from ..utils.iq3_s_weight import (
+    IQ3SFields,
+    _weight_dimensions,
+    prepare_iq3_s_fields,
+    weight_struct,
+)
+
+IQ3_S_BLOCK_BYTES = 110
+IQ3_S_BLOCK_VALUES = 256
+IQ3_S_SCALE_VALUES = 32
+
+# Tuned on B200 for the Llama-3-8B projection shapes (decode M <= 8). Keys
+# follow the reference convention: GPU SM version, then medium/large by M.
+BEST_CONFIGS = {
+    "sm100": {
+        "medium": {"kernel": _lib.MAMBO_KERNEL_GEMV, "warps": 8, "stages": 6, "ctas_per_sm": 1, "split": 0},
+        "large": {"kernel": _lib.MAMBO_KERNEL_GEMV, "warps": 8, "stages": 5, "ctas_per_sm": 1, "split": 0},
+    },
+}
+LARGE_TOKEN_THRESHOLD = 32
+
+_IQ3_TABLES: dict[int, torch.Tensor] = {}
+_TABLE_LOCK = threading.Lock()
+_TUNED: dict[tuple[int, int, int], dict] = {}
+
+
+# ----------------------------------------------------------------------------
+# Codebook
+# ----------------------------------------------------------------------------
+@lru_cache(maxsize=1)
+def iq3_s_table() -> np.ndarray:
+    """The 512-entry IQ3_S codebook (uint32, four magnitude bytes each).
+
+    Like the reference (iq3_s_fp8.py:63-74) it is read from llama.cpp's
+    ``ggml-common.h`` when MAMBO_LLAMA_SOURCE_DIR points at a llama.cpp tree;
+    otherwise from the installed gguf-py, whose IQ3_S grid is the same table.
+    """
+    src = os.environ.get("MAMBO_LLAMA_SOURCE_DIR")
+    if src:
+        header = Path(src) / "ggml" / "src" / "ggml-common.h"
+        if header.is_file():
+            text = header.read_text(encoding="utf-8")
+            match = re.search(r"GGML_TABLE_BEGIN\(uint32_t, iq3s_grid, 512\)(.*?)GGML_TABLE_END\(\)", text, re.S)
+            if match is None:
+                raise ValueError(f"IQ3_S lookup table was not found in {header}")
+            values = np.asarray([int(s, 16) for s in re.findall(r"0x[0-9a-fA-F]+", match.group(1))], dtype=np.uint32)
+            if values.shape != (512,):
+                raise ValueError(f"expected 512 IQ3_S table entries, got {values.size}")
+            return values
+    from gguf.quants import IQ3_S  # the GGUF format's own Python package
+
+    IQ3_S.init_grid()
+    grid = np.asarray(IQ3_S.grid, dtype=np.float32).reshape(512, 4).astype(np.uint32)
+    return (grid[:, 0] | (grid[:, 1] << 8) | (grid[:, 2] << 16) | (grid[:, 3] << 24)).astype(np.uint32)
+
+
+@lru_cache(maxsize=1)
+def iq3_s_fp8_table() -> np.ndarray:
+    """Pack positive magnitudes as E4M3 bits (iq3_s_fp8.py:77-94)."""
+    magnitudes = np.array([1, 3, 5, 7, 9, 11, 13, 15], dtype=np.uint8)
+    fp8_bits = np.array([0x38, 0x44, 0x4A, 0x4E, 0x51, 0x53, 0x55, 0x57], dtype=np.uint8)
+    lookup = np.zeros(256, dtype=np.uint8)
+    valid = np.zeros(256, dtype=np.bool_)
+    lookup[magnitudes] = fp8_bits
+    valid[magnitudes] = True
+    raw_table = iq3_s_table()
+    encoded = np.zeros_like(raw_table)
+    for shift in (0, 8, 16, 24):
+        magnitude = (raw_table >> shift) & 0xFF
+        if not np.all(valid[magnitude]):
+            raise ValueError("IQ3_S codebook contains a magnitude without an E4M3 encoding")
+        encoded |= lookup[magnitude].astype(np.uint32) << shift
+    return encoded
+
+
+def _get_iq3_table(device: torch.device | None = None) -> torch.Tensor:
+    """Upload the FP8-encoded codebook once per CUDA device (iq3_s_fp8.py:97-102)."""
+    index = torch.cuda.current_device() if device is None or device.index is None else device.index
+    with _TABLE_LOCK:
+        table = _IQ3_TABLES.get(index)
+        if table is None:
+            host = torch.from_numpy(iq3_s_fp8_table().view(np.int32).copy())
+            table = host.to(torch.device("cuda", index)).view(torch.uint32)
+            _IQ3_TABLES[index] = table
+    return table
+
+
+def _power_of_two(value: int, name: str) -> None:
+    if value < 1 or value & (value - 1):
+        raise ValueError(f"{name} must be a positive power of two")
+
+
+# ----------------------------------------------------------------------------
+# Standalone decoder
+# ----------------------------------------------------------------------------
+def launch_dequant_iq3_s(iq3_weight: IQ3SFields, *, tile_n: int = 1, stream=None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Return [N,K] E4M3 bit patterns and [N,K/32] original F32 scales (iq3_s_fp8.py:341-351)."""
+    _power_of_two(tile_n, "tile_n")
+    n_rows, blocks = _weight_dimensions(iq3_weight)
+    w = weight_struct(iq3_weight)
+    dev = iq3_weight.d.device
+    _runtime.require_device(dev)
+    values = torch.empty((n_rows, blocks * 256), dtype=torch.uint8, device=dev)
+    scales = torch.empty((n_rows, blocks * 8), dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        st = _runtime.stream_handle(stream, dev)
+        _lib.check(_lib.load().mambo_iq3s_decode(w, _get_iq3_table(dev).data_ptr(), values.data_ptr(),
+                                                  scales.data_ptr(), st), "launch_dequant_iq3_s")
+    return values, scales
+
+
+# ----------------------------------------------------------------------------
+# Linear
+# ----------------------------------------------------------------------------
+def _sm_key(device: torch.device) -> str:
+    major, minor = torch.cuda.get_device_capability(device)
+    return f"sm{major}{minor}"
+
+
+def _m_bucket(m: int) -> int:
+    return 8 if m <= 8 else (16 if m <= 16 else 32)
+
+
+def register_tuned_config(m: int, n: int, k: int, config: dict) -> None:
+    """Record the autotuner's choice for a shape; launches consult it before BEST_CONFIGS."""
+    _TUNED[(_m_bucket(m), int(n), int(k))] = dict(config)
+
+
+def load_tuned_configs(path: str | os.PathLike) -> int:
+    """Load a JSON list of {"m","n","k","config"} records written by the autotuner."""
+    records = json.loads(Path(path).read_text())
+    for rec in records:
+        register_tuned_config(rec["m"], rec["n"], rec["k"], rec["config"])
+    return len(records)
+
+
+def select_config(m: int, n: int, k: int, device: torch.device) -> dict:
+    tuned = _TUNED.get((_m_bucket(m), n, k))
+    if tuned is not None:
+        return tuned
+    sm = _sm_key(device)
+    if sm not in BEST_CONFIGS:
+        raise RuntimeError(f"IQ3_S FP8 matmul has no tuned config for {sm}")
+    return BEST_CONFIGS[sm]["medium" if m < LARGE_TOKEN_THRESHOLD else "large"]
+
+
+def linear_into(x_values: torch.Tensor, x_scales: torch.Tensor, iq3_weight: IQ3SFields, out: torch.Tensor,
+                config: dict | None = None, stream=None) -> torch.Tensor:
+    """Launch the linear into a preallocated out [M,N] (f32 or bf16). No validation of x beyond the C ABI's."""
+    n_rows, blocks = _weight_dimensions(iq3_weight)
+    m = x_values.shape[0]
+    dev = x_values.device
+    cfg = _lib.MamboLinearConfig.from_dict(config if config is not None else select_config(m, n_rows, blocks * 256,
+                                                                                              dev))
+    w = weight_struct(iq3_weight)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        st = _runtime.stream_handle(stream, dev)
+        need = lib.mambo_iq3s_linear_workspace_bytes(m, n_rows, blocks, cfg)
+        ws = _runtime.workspace(dev, st, need)
+        out_dtype = _lib.MAMBO_BF16 if out.dtype == torch.bfloat16 else _lib.MAMBO_F32
+        _lib.check(
+            lib.mambo_iq3s_linear(
+                x_values.data_ptr(), x_values.stride(0), x_scales.data_ptr(), x_scales.stride(0), m, w,
+                _get_iq3_table(dev).data_ptr(), out.data_ptr(), out_dtype, out.stride(0), cfg,
+                ws.data_ptr(), ws.numel(), st,
+            ),
+            "launch_iq3_s_fp8_matmul",
+        )
+    return out
+
+
+def launch_iq3_s_fp8_matmul(x_values, x_scales, iq3_weight: IQ3SFields, *, stream=None,
+                            out_dtype: torch.dtype = torch.float32, config: dict | None = None) -> torch.Tensor:
+    """Multiply prepared SoA weights by prequantized MXFP8 activations (iq3_s_fp8.py:364-399).
+
+    Returns float32 [M,N] by default (``out_dtype=torch.bfloat16`` for the bf16
+    epilogue). Activation views with a non-unit column stride are copied to
+    contiguous memory first.
+    """
+    n_rows, k_blocks = _weight_dimensions(iq3_weight)
+    k = k_blocks * 256
+    x_values = _runtime.as_cuda_tensor(x_values)
+    x_scales = _runtime.as_cuda_tensor(x_scales)
+    if x_values.ndim != 2 or x_values.dtype != torch.uint8 or x_values.shape[0] < 1 or x_values.shape[1] != k:
+        raise ValueError("x_values must be uint8 [M,K]")
+    if tuple(x_scales.shape) != (x_values.shape[0], k // 32) or x_scales.dtype != torch.uint8:
+        raise ValueError("x_scales must be uint8 [M,K/32]")
+    if out_dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError("out_dtype must be torch.float32 or torch.bfloat16")
+    dev = x_values.device
+    if _sm_key(dev) not in BEST_CONFIGS:
+        raise RuntimeError(f"IQ3_S FP8 matmul has no tuned config for {_sm_key(dev)}")
+    _runtime.require_device(dev)
+    if x_values.stride(1) != 1:
+        x_values = x_values.contiguous()
+    if x_scales.stride(1) != 1:
+        x_scales = x_scales.contiguous()
+    out = torch.empty((x_values.shape[0], n_rows), dtype=out_dtype, device=dev)
+    return linear_into(x_values, x_scales, iq3_weight, out, config=config, stream=stream)
+
+
+def iq3_s_fp8_linear(x, iq3_weight: IQ3SFields, *, stream=None, out_dtype: torch.dtype = torch.bfloat16,
+                     rounding: str = "nearest_even", config: dict | None = None) -> torch.Tensor:
+    """bf16/f32 activations [M,K] -> MXFP8 -> IQ3_S linear -> out_dtype [M,N] (quantize + matmul)."""
+    from .quantize_fp8 import launch_quantize_fp8
+
+    xq, xs = launch_quantize_fp8(x, stream=stream, rounding=rounding)
+    return launch_iq3_s_fp8_matmul(xq, xs, iq3_weight, stream=stream, out_dtype=out_dtype, config=config)
+
+
+# ----------------------------------------------------------------------------
+# Autotuning cases (iq3_s_fp8.py:402-465)
+# ----------------------------------------------------------------------------
+def config_search_space(kernel: int = _lib.MAMBO_KERNEL_GEMV) -> list[dict]:
+    lib = _lib.load()
+    out = []
+    for i in range(lib.mambo_num_configs(kernel)):
+        c = _lib.MamboLinearConfig()
+        _lib.check(lib.mambo_config_at(kernel, i, c))
+        out.append(c.to_dict())
+    return out
+
+
+def make_benchmark_cases(iq3_weight, ms: tuple[int, ...] = (4, 128), seed: int = 0) -> list:
+    """Prepare SoA weights and FP8 inputs once; benchmark only the matmul."""
+    from ..utils.kernel_benchmark import BenchmarkCase
+    from .quantize_fp8 import launch_quantize_fp8
+
+    if not isinstance(iq3_weight, IQ3SFields):
+        iq3_weight = prepare_iq3_s_fields(iq3_weight)
+    n_rows, k_blocks = _weight_dimensions(iq3_weight)
+    k = k_blocks * IQ3_S_BLOCK_VALUES
+    dev = iq3_weight.d.device
+    stream = torch.cuda.current_stream(dev)
+    gen = torch.Generator(device=dev).manual_seed(seed)
+
+    def make_case(m: int) -> BenchmarkCase:
+        x = torch.randn((m, k), generator=gen, device=dev, dtype=torch.float32)
+        x_values, x_scales = launch_quantize_fp8(x, stream=stream)
+        out = torch.empty((m, n_rows), dtype=torch.float32, device=dev)
+
+        def run(config: dict) -> None:
+            linear_into(x_values, x_scales, iq3_weight, out, config=config, stream=stream)
+
+        return BenchmarkCase(
+            name=f"M={m} N={n_rows} K={k}", stream=stream, kernel=run,
+            search_space=config_search_space(),
+            grid_fn=lambda config: (config.get("ctas_per_sm", 1),),
+            args_fn=lambda config: (config,),
+            hints_fn=None,
+            summary_keys=("warps", "stages"),
+            shape=(m, n_rows, k),
+        )
+
+    return [make_case(m) for m in ms]

@@ -1,0 +1,121 @@
+"""Prepare persistent IQ3_S SoA weight fields for the sm_100a kernels.
+
+Mirror of src/python/mambo/utils/iq3_s_weight.py (Menooker/Mambo): same class,
+field names, dtypes, shapes and errors; the arrays are torch CUDA tensors and
+the AoS -> SoA split runs in libmambo_b200 (``mambo_iq3s_prepare``).
+
+One IQ3_S block along K (256 weights, 110 bytes):
+
+    byte  0..1   | d: FP16 base scale                 |  2 bytes
+    byte  2..65  | qs: 64 low 8-bit codebook indices  | 64 bytes
+    byte 66..73  | qh: 64 high index bits             |  8 bytes
+    byte 74..105 | signs: one bit per weight          | 32 bytes
+    byte 106..109| scales: 8 packed 4-bit values      |  4 bytes
+
+Each 9-bit (qs, qh) index selects four magnitudes from the codebook; each
+group of 32 weights uses scale d * (1 + 2 * scale_nibble).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from .. import _lib, _runtime
+
+
+@dataclass(frozen=True)
+class IQ3SFields:
+    """Byte-preserving SoA, K-block first and N rows second (iq3_s_weight.py:10-22).
+
+    d: float16 [B,N]; qs: uint32 [B,N,16]; qh: uint16 [B,N,4];
+    signs: int32 [B,N,8]; scales: uint32 [B,N]. Total: 110 bytes/block.
+    Prepare once on the launch stream, then reuse for all projections.
+    """
+
+    d: torch.Tensor
+    qs: torch.Tensor
+    qh: torch.Tensor
+    signs: torch.Tensor
+    scales: torch.Tensor
+
+
+def prepare_iq3_s_fields(iq3_weight, *, stream=None) -> IQ3SFields:
+    """Split GGUF uint8 [N,B,110] blocks into aligned SoA fields once (iq3_s_weight.py:25-54).
+
+    Accepts any strides and address alignment of the source view. The copy is
+    outside kernel timing.
+    """
+    raw = _runtime.as_cuda_tensor(iq3_weight)
+    if raw.ndim != 3 or raw.dtype != torch.uint8 or raw.shape[2] != 110:
+        raise ValueError("IQ3_S weight must be uint8 [N,K/256,110]")
+    n, blocks, _ = raw.shape
+    if n < 1 or blocks < 1:
+        raise ValueError("IQ3_S weight must have positive N and K")
+    dev = raw.device
+    _runtime.require_device(dev)
+    mk = lambda *shape: torch.empty(shape, dtype=torch.uint8, device=dev)  # noqa: E731
+    d, qs, qh, signs, scales = mk(blocks, n, 2), mk(blocks, n, 64), mk(blocks, n, 8), mk(blocks, n, 32), mk(blocks, n, 4)
+    with torch.cuda.device(dev):
+        st = _runtime.stream_handle(stream, dev)
+        _lib.check(
+            _lib.load().mambo_iq3s_prepare(
+                raw.data_ptr(), n, blocks, raw.stride(0), raw.stride(1), raw.stride(2),
+                d.data_ptr(), qs.data_ptr(), qh.data_ptr(), signs.data_ptr(), scales.data_ptr(), st,
+            ),
+            "prepare_iq3_s_fields",
+        )
+    return IQ3SFields(
+        d.view(torch.float16).reshape(blocks, n),
+        qs.view(torch.uint32),
+        qh.view(torch.uint16),
+        signs.view(torch.int32),
+        scales.view(torch.uint32).reshape(blocks, n),
+    )
+
+
+def _weight_dimensions(iq3_weight: IQ3SFields) -> tuple[int, int]:
+    """Return N and the number of K blocks in the prepared fields (iq3_s_weight.py:57-62)."""
+    if not isinstance(iq3_weight, IQ3SFields):
+        raise TypeError("prepare IQ3_S weights with prepare_iq3_s_fields before launch")
+    blocks, n_rows = iq3_weight.d.shape
+    return n_rows, blocks
+
+
+def _weight_kernel_args(iq3_weight: IQ3SFields) -> tuple[torch.Tensor, ...]:
+    return (iq3_weight.d, iq3_weight.qs, iq3_weight.qh, iq3_weight.signs, iq3_weight.scales)
+
+
+def _large_weight_kernel_args(iq3_weight: IQ3SFields) -> tuple[torch.Tensor, ...]:
+    """Zero-copy views: qh as uint32 [B,N,2], signs as int32 [B,N*8] (iq3_s_weight.py:69-77)."""
+    return (iq3_weight.d, iq3_weight.qs, iq3_weight.qh.view(torch.uint32),
+            iq3_weight.signs.reshape(iq3_weight.signs.shape[0], -1), iq3_weight.scales)
+
+
+def weight_struct(iq3_weight: IQ3SFields) -> _lib.MamboIQ3SWeight:
+    """The C-ABI view of prepared fields (validates contiguity and shapes)."""
+    n, b = _weight_dimensions(iq3_weight)
+    expect = {
+        "d": ((b, n), torch.float16),
+        "qs": ((b, n, 16), torch.uint32),
+        "qh": ((b, n, 4), torch.uint16),
+        "signs": ((b, n, 8), torch.int32),
+        "scales": ((b, n), torch.uint32),
+    }
+    for name, (shape, dtype) in expect.items():
+        t = getattr(iq3_weight, name)
+        if tuple(t.shape) != shape or t.dtype != dtype or not t.is_contiguous() or not t.is_cuda:
+            raise ValueError(f"IQ3SFields.{name} must be a contiguous CUDA {dtype} tensor of shape {shape}")
+    w = _lib.MamboIQ3SWeight()
+    w.d, w.qs, w.qh = iq3_weight.d.data_ptr(), iq3_weight.qs.data_ptr(), iq3_weight.qh.data_ptr()
+    w.signs, w.scales = iq3_weight.signs.data_ptr(), iq3_weight.scales.data_ptr()
+    w.n_rows, w.n_blocks = n, b
+    return w
+
+
+def fields_nbytes(iq3_weight: IQ3SFields) -> int:
+    return sum(t.numel() * t.element_size() for t in _weight_kernel_args(iq3_weight))
+
+
+__all__ = ["IQ3SFields", "prepare_iq3_s_fields", "weight_struct", "fields_nbytes"]
