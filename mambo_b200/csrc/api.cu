@@ -128,28 +128,38 @@ constexpr int kNumGemvConfigs = 2 * 4 * 2;
 
 int gemv_nt_for(int64_t m) { return m <= 8 ? 1 : (m <= 16 ? 2 : 4); }
 
-void default_config(int64_t m, int64_t n, int64_t b, MamboLinearConfig* cfg) {
+// Shared memory an SM offers one CTA (B200: 227 KB); used when no device is visible.
+constexpr int kSmemOptinDefault = 232448;
+
+void default_config(int64_t m, int64_t n, int64_t b, MamboLinearConfig* cfg, int smem_optin) {
   (void)n;
-  (void)b;
   std::memset(cfg, 0, sizeof(*cfg));
   cfg->kernel = MAMBO_KERNEL_GEMV;
   cfg->warps = 8;
-  cfg->stages = gemv_nt_for(m) == 4 ? 5 : 6;
   cfg->ctas_per_sm = 1;
   cfg->split = 0;
+  // Deepest pipeline (up to 8 stages) that fits next to the codebook and scales.
+  const int nt = gemv_nt_for(m < 32 ? m : 32);
+  int stages = 8;
+  while (stages > 2 && (int)gemv_smem_bytes_host(cfg->warps * 16, nt, stages, (int)b) > smem_optin) --stages;
+  cfg->stages = stages;
 }
 
-int validate_config(const MamboLinearConfig* cfg, int64_t m, const DeviceInfo& info) {
+int validate_config(const MamboLinearConfig* cfg, int64_t m, int64_t b, const DeviceInfo& info) {
   if (cfg->kernel != MAMBO_KERNEL_GEMV && cfg->kernel != MAMBO_KERNEL_AUTO)
     return fail(MAMBO_EINVAL, "unknown kernel kind %d", cfg->kernel);
   if (cfg->warps != 4 && cfg->warps != 8) return fail(MAMBO_EINVAL, "warps must be 4 or 8");
   if (cfg->stages < 2 || cfg->stages > 12) return fail(MAMBO_EINVAL, "stages must be in [2, 12]");
-  const uint32_t smem = gemv_smem_bytes_host(cfg->warps * 16, gemv_nt_for(m), cfg->stages);
+  const uint32_t smem = gemv_smem_bytes_host(cfg->warps * 16, gemv_nt_for(m), cfg->stages, (int)b);
   if ((int)smem > info.max_smem_optin)
     return fail(MAMBO_EINVAL, "configuration needs %u bytes of shared memory (device allows %d)", smem,
                 info.max_smem_optin);
   return MAMBO_OK;
 }
+
+// Split-K counters live at the start of every workspace: 64 Ki ints, zero
+// between calls. Shapes needing more (row_tiles * warps > 65536) are rejected.
+constexpr size_t kCounterBytes = 256 * 1024;
 
 struct GemvPlan {
   int nt, rows, row_tiles, units, grid;
@@ -166,7 +176,9 @@ GemvPlan plan_gemv(int64_t m_chunk, int64_t n, int64_t b, const MamboLinearConfi
   if (cfg.split == 1) ctas = P.row_tiles;  // one CTA per row tile, no split-K
   P.grid = P.units < ctas ? P.units : ctas;
   if (P.grid < 1) P.grid = 1;
-  P.counters_bytes = ((size_t)P.row_tiles * cfg.warps * sizeof(int) + 255) / 256 * 256;
+  // The counter region has a fixed size so that it never overlaps the
+  // partials of a call with another shape sharing the workspace.
+  P.counters_bytes = kCounterBytes;
   P.partial_bytes = (size_t)P.grid * 2 * P.rows * 8 * P.nt * sizeof(float);
   return P;
 }
@@ -273,7 +285,10 @@ int mambo_quantize_mxfp8(const void* x, int x_dtype, int64_t m, int64_t k, int64
 
 int mambo_default_config(int64_t m, int64_t n_rows, int64_t n_blocks, MamboLinearConfig* cfg) {
   if (!cfg) return fail(MAMBO_EINVAL, "null config");
-  default_config(m, n_rows, n_blocks, cfg);
+  int st;
+  DeviceInfo info = device_info(&st);
+  default_config(m, n_rows, n_blocks, cfg, (st == MAMBO_OK && info.max_smem_optin > 0) ? info.max_smem_optin
+                                                                                        : kSmemOptinDefault);
   return ok();
 }
 
@@ -296,10 +311,12 @@ int mambo_config_at(int kernel, int index, MamboLinearConfig* cfg) {
 }
 
 size_t mambo_iq3s_linear_workspace_bytes(int64_t m, int64_t n_rows, int64_t n_blocks, const MamboLinearConfig* cfg) {
-  MamboLinearConfig c;
-  if (cfg) c = *cfg; else default_config(m, n_rows, n_blocks, &c);
   int st;
   DeviceInfo info = device_info(&st);
+  MamboLinearConfig c;
+  if (cfg) c = *cfg;
+  else default_config(m, n_rows, n_blocks, &c, (st == MAMBO_OK && info.max_smem_optin > 0) ? info.max_smem_optin
+                                                                                          : kSmemOptinDefault);
   const int sms = (st == MAMBO_OK && info.sms > 0) ? info.sms : 148;
   const int64_t m_chunk = m < 32 ? m : 32;
   GemvPlan P = plan_gemv(m_chunk, n_rows, n_blocks, c, sms);
@@ -324,15 +341,17 @@ int mambo_iq3s_linear(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_
   int st = require_sm100(&info);
   if (st != MAMBO_OK) return st;
   MamboLinearConfig c;
-  if (cfg) c = *cfg; else default_config(m, w->n_rows, w->n_blocks, &c);
+  if (cfg) c = *cfg; else default_config(m, w->n_rows, w->n_blocks, &c, info.max_smem_optin);
   if (c.kernel == MAMBO_KERNEL_AUTO) c.kernel = MAMBO_KERNEL_GEMV;
-  st = validate_config(&c, m < 32 ? m : 32, info);
+  st = validate_config(&c, m < 32 ? m : 32, w->n_blocks, info);
   if (st != MAMBO_OK) return st;
 
   const int64_t m_chunk_max = 32;
   for (int64_t m0 = 0; m0 < m; m0 += m_chunk_max) {
     const int64_t mc = (m - m0) < m_chunk_max ? (m - m0) : m_chunk_max;
     GemvPlan P = plan_gemv(mc, w->n_rows, w->n_blocks, c, info.sms);
+    if ((size_t)P.row_tiles * c.warps * sizeof(int) > kCounterBytes)
+      return fail(MAMBO_EINVAL, "N=%lld needs more split-K counters than the workspace holds", (long long)w->n_rows);
     const size_t need = P.counters_bytes + P.partial_bytes;
     if (!workspace || workspace_bytes < need)
       return fail(MAMBO_EWORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
@@ -360,8 +379,7 @@ int mambo_iq3s_linear(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_
     p.stages = c.stages;
     p.row_tiles = P.row_tiles;
     p.total_units = P.units;
-    p.x_vec = ((uintptr_t)p.xq % 16 == 0) && (ldxq % 16 == 0);
-    p.xs_vec = ((uintptr_t)p.xs % 8 == 0) && (ldxs % 8 == 0);
+    p.x_bulk = ((uintptr_t)p.xq % 16 == 0) && (ldxq % 16 == 0);
     GemvMaps maps;
     std::memset(&maps, 0, sizeof(maps));
     const bool use_tma = (c.loader == 0) && make_gemv_maps(p, &maps);

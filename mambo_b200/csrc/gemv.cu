@@ -12,10 +12,11 @@
 //    Persistent CTAs (one per SM) walk a contiguous range of units
 //    (row-tile major, stream-K), so every SM streams the same number of
 //    weight bytes whatever the shape.
-//  * One producer warp stages units through a ring of shared-memory stages:
-//    lane 0 issues five TMA tensor copies per unit (qs/signs swizzled so the
-//    consumer reads are bank-conflict free); the lanes copy the unit's MXFP8
-//    activation slice and convert its scales to float.
+//  * One producer thread stages units through a ring of shared-memory stages
+//    with asynchronous copies completing on an mbarrier: five TMA tensor copies
+//    for the weight fields (qs/signs swizzled so consumer reads are bank-conflict
+//    free) and one bulk copy per token row of the MXFP8 activation slice.
+//  * The activation scales are converted to float once per CTA.
 //  * Consumer warps decode straight into mma.sync m16n8k32 A fragments: the
 //    fragment puts 4 consecutive K of one row in one register, which is exactly
 //    one IQ3_S code (4 weights sharing one codebook entry). The codebook lives
@@ -23,19 +24,20 @@
 //    512-entry gather is conflict free. Weights are the 16-row A operand
 //    (swap-AB); tokens are the n8 B operand.
 //  * Row tiles split between CTAs write FP32 partials to a workspace; per
-//    (row tile, warp) an atomic counter elects the last warp to finish, which
-//    sums the partials in CTA order (deterministic) and resets the counter.
+//    (row tile, warp) an acq_rel atomic counter elects the last warp to finish,
+//    which sums the partials in CTA order (deterministic) and resets the counter.
 #include "kernels.cuh"
 
 namespace mambo {
 
 constexpr int kTableBytes = 512 * 32 * 4;  // lane-private codebook
 constexpr int kMaxStages = 12;
+constexpr int kXRowBytes = 272;  // 256-byte activation rows padded to 272 (conflict-free B-fragment reads)
 
 __host__ __device__ constexpr uint32_t align_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
 struct StageLayout {
-  uint32_t qs, signs, qh, d, scales, x, xs, bytes;
+  uint32_t qs, signs, qh, d, scales, x, bytes;
 };
 
 __host__ __device__ inline StageLayout gemv_stage_layout(int rows, int nt) {
@@ -52,15 +54,18 @@ __host__ __device__ inline StageLayout gemv_stage_layout(int rows, int nt) {
   L.scales = off;
   off = align_up(off + rows * 4, 128);
   L.x = off;
-  off = align_up(off + 8 * nt * 256, 128);
-  L.xs = off;
-  off = align_up(off + 8 * 8 * nt * 4, 1024);
+  off = align_up(off + 8 * nt * kXRowBytes, 1024);
   L.bytes = off;
   return L;
 }
 
-__host__ __device__ inline uint32_t gemv_smem_bytes(int rows, int nt, int stages) {
-  return 1024 + kTableBytes + stages * gemv_stage_layout(rows, nt).bytes + 2 * kMaxStages * 8 + 64;
+__host__ __device__ inline uint32_t gemv_xs_bytes(int n_blocks, int nt) {
+  return align_up((uint32_t)n_blocks * 8u * 8u * nt * 4u, 128);
+}
+
+__host__ __device__ inline uint32_t gemv_smem_bytes(int rows, int nt, int stages, int n_blocks) {
+  return 1024 + kTableBytes + stages * gemv_stage_layout(rows, nt).bytes + gemv_xs_bytes(n_blocks, nt) +
+         2 * kMaxStages * 8;
 }
 
 __device__ __forceinline__ int unit_begin(int cta, int grid, int units) {
@@ -78,10 +83,6 @@ __device__ __forceinline__ uint32_t qs_off(uint32_t row, uint32_t byte) {
 __device__ __forceinline__ uint32_t signs_off(uint32_t row, uint32_t byte) {
   return row * 32 + ((((byte >> 4) ^ (row >> 2)) & 1) << 4) + (byte & 15);
 }
-// Activation tile: token rows of 256 bytes, 16-byte chunk c stored at c ^ (2*tok mod 16).
-__device__ __forceinline__ uint32_t x_off(uint32_t tok, uint32_t byte) {
-  return tok * 256 + ((((byte >> 4) ^ (2 * tok)) & 15) << 4) + (byte & 15);
-}
 
 __device__ __forceinline__ void mma_e4m3(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
@@ -98,6 +99,8 @@ __device__ void gemv_producer(const GemvParams& p, const GemvMaps* maps, uint8_t
   const int lane = threadIdx.x & 31;
   const int rows = p.warps * 16;
   const int tokens = 8 * NT;
+  const bool async_all = kTma && p.x_bulk;
+  if (async_all && lane != 0) return;  // one thread drives every copy
   uint64_t policy = 0;
   if constexpr (kTma) {
     if (lane == 0) {
@@ -120,12 +123,17 @@ __device__ void gemv_producer(const GemvParams& p, const GemvMaps* maps, uint8_t
     const int n0 = rt * rows;
     if constexpr (kTma) {
       if (lane == 0) {
-        mbar_expect_tx(full, (uint32_t)rows * 110u);
+        mbar_expect_tx(full, (uint32_t)rows * 110u + (p.x_bulk ? (uint32_t)p.m * 256u : 0u));
         tma_load_3d(smem_u32(st + L.qs), &maps->qs, 0, n0, kb, full, policy);
         tma_load_3d(smem_u32(st + L.signs), &maps->signs, 0, n0, kb, full, policy);
         tma_load_2d(smem_u32(st + L.qh), &maps->qh, n0, kb, full, policy);
         tma_load_2d(smem_u32(st + L.d), &maps->d, n0, kb, full, policy);
         tma_load_2d(smem_u32(st + L.scales), &maps->scales, n0, kb, full, policy);
+        if (p.x_bulk) {
+          for (int tok = 0; tok < p.m; ++tok)
+            bulk_load(smem_u32(st + L.x + tok * kXRowBytes), p.xq + (int64_t)tok * p.ldxq + (int64_t)kb * 256, 256,
+                      full);
+        }
       }
     } else {
       // Plain loads into the same swizzled layout (any N, any field alignment).
@@ -157,50 +165,25 @@ __device__ void gemv_producer(const GemvParams& p, const GemvMaps* maps, uint8_t
         *reinterpret_cast<uint32_t*>(st + L.scales + r * 4) = sc;
       }
     }
-    // Activation slice [tokens x 256] E4M3 (rows >= M are zero) and its scales as floats [8][tokens].
-    for (int i = lane; i < tokens * 16; i += 32) {
-      const int tok = i >> 4, c = i & 15;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (tok < p.m) {
-        const uint8_t* src = p.xq + (int64_t)tok * p.ldxq + (int64_t)kb * 256 + c * 16;
-        if (p.x_vec) {
-          v = __ldg(reinterpret_cast<const uint4*>(src));
-        } else {
-          uint32_t w[4];
+    if (!async_all) {
+      // Activation slice [tokens x 256] E4M3 with plain loads (rows >= M are zero).
+      for (int i = lane; i < tokens * 16; i += 32) {
+        const int tok = i >> 4, c = i & 15;
+        uint32_t w[4] = {0, 0, 0, 0};
+        if (tok < p.m) {
+          const uint8_t* src = p.xq + (int64_t)tok * p.ldxq + (int64_t)kb * 256 + c * 16;
 #pragma unroll
           for (int j = 0; j < 4; ++j)
             w[j] = (uint32_t)src[4 * j] | ((uint32_t)src[4 * j + 1] << 8) | ((uint32_t)src[4 * j + 2] << 16) |
                    ((uint32_t)src[4 * j + 3] << 24);
-          v = make_uint4(w[0], w[1], w[2], w[3]);
         }
-      }
-      *reinterpret_cast<uint4*>(st + L.x + x_off(tok, c * 16)) = v;
-    }
-    if (lane < tokens) {
-      uint32_t lo = 0x7F7F7F7Fu, hi = 0x7F7F7F7Fu;  // padding tokens: scale 1 (their x is 0)
-      if (lane < p.m) {
-        const uint8_t* src = p.xs + (int64_t)lane * p.ldxs + (int64_t)kb * 8;
-        if (p.xs_vec) {
-          const uint2 v = __ldg(reinterpret_cast<const uint2*>(src));
-          lo = v.x;
-          hi = v.y;
-        } else {
-          lo = (uint32_t)src[0] | ((uint32_t)src[1] << 8) | ((uint32_t)src[2] << 16) | ((uint32_t)src[3] << 24);
-          hi = (uint32_t)src[4] | ((uint32_t)src[5] << 8) | ((uint32_t)src[6] << 16) | ((uint32_t)src[7] << 24);
-        }
-      }
-      float* xsf = reinterpret_cast<float*>(st + L.xs);
-#pragma unroll
-      for (int g = 0; g < 8; ++g) {
-        const uint32_t code = ((g < 4 ? lo : hi) >> (8 * (g & 3))) & 0xFFu;
-        xsf[g * tokens + lane] = e8m0_to_float(code);
+        *reinterpret_cast<uint4*>(st + L.x + tok * kXRowBytes + c * 16) = make_uint4(w[0], w[1], w[2], w[3]);
       }
     }
     mbar_arrive(full);
   }
 }
 
-template <int NT>
 __device__ __forceinline__ void store_out(const GemvParams& p, int row, int tok, float v) {
   if (row < p.n_rows && tok < p.m) {
     if (p.out_bf16) {
@@ -212,8 +195,8 @@ __device__ __forceinline__ void store_out(const GemvParams& p, int row, int tok,
 }
 
 template <int NT>
-__device__ void gemv_consumer(const GemvParams& p, const uint8_t* table, uint8_t* stage0, const StageLayout& L,
-                              uint32_t full0, uint32_t empty0, int u0, int u1) {
+__device__ void gemv_consumer(const GemvParams& p, const uint8_t* table, const float* xsf, uint8_t* stage0,
+                              const StageLayout& L, uint32_t full0, uint32_t empty0, int u0, int u1) {
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int gid = lane >> 2, tig = lane & 3;
@@ -238,7 +221,7 @@ __device__ void gemv_consumer(const GemvParams& p, const uint8_t* table, uint8_t
     const int rt = u / p.n_blocks, kb = u % p.n_blocks;
 
     // Per-row metadata of this block for rows rl0 (h=0) and rl0+8 (h=1).
-    uint32_t e0[2][2], e1[2][2];  // [h][lo/hi 4 groups]: byte g = (high code bit << 7) | lane<<2
+    uint32_t e0[2][2], e1[2][2];  // [h][groups 0-3 / 4-7]: byte g = (high code bit << 7) | lane<<2
     uint32_t tb[2][2];            // [h][even/odd groups]: byte j = 2*nibble+1
     float dv[2], dneg[2];
 #pragma unroll
@@ -258,7 +241,8 @@ __device__ void gemv_consumer(const GemvParams& p, const uint8_t* table, uint8_t
       dv[h] = __half2float(__ushort_as_half(dh));
       dneg[h] = -8388608.0f * dv[h];
     }
-    const float* xsf = reinterpret_cast<const float*>(st + L.xs);
+    const float* xs_kb = xsf + (size_t)kb * 8 * tokens;
+    const uint8_t* xrow = st + L.x + gid * kXRowBytes + 8 * tig;
 
 #pragma unroll
     for (int g = 0; g < 8; ++g) {
@@ -283,10 +267,10 @@ __device__ void gemv_consumer(const GemvParams& p, const uint8_t* table, uint8_t
       }
 #pragma unroll
       for (int t = 0; t < NT; ++t) {
-        const uint2 b = *reinterpret_cast<const uint2*>(st + L.x + x_off(8 * t + gid, 32 * g + 8 * tig));
+        const uint2 b = *reinterpret_cast<const uint2*>(xrow + t * 8 * kXRowBytes + 32 * g);
         float c[4];
         mma_e4m3(c, a[0], a[1], a[2], a[3], b.x, b.y);
-        const float2 xsc = *reinterpret_cast<const float2*>(xsf + g * tokens + 8 * t + 2 * tig);
+        const float2 xsc = *reinterpret_cast<const float2*>(xs_kb + g * tokens + 8 * t + 2 * tig);
         acc[t][0] = fmaf(c[0] * xsc.x, w[0], acc[t][0]);
         acc[t][1] = fmaf(c[1] * xsc.y, w[0], acc[t][1]);
         acc[t][2] = fmaf(c[2] * xsc.x, w[1], acc[t][2]);
@@ -306,10 +290,10 @@ __device__ void gemv_consumer(const GemvParams& p, const uint8_t* table, uint8_t
 #pragma unroll
       for (int t = 0; t < NT; ++t) {
         const int tok = 8 * t + 2 * tig;
-        store_out<NT>(p, row0 + rl0, tok, acc[t][0]);
-        store_out<NT>(p, row0 + rl0, tok + 1, acc[t][1]);
-        store_out<NT>(p, row0 + rl0 + 8, tok, acc[t][2]);
-        store_out<NT>(p, row0 + rl0 + 8, tok + 1, acc[t][3]);
+        store_out(p, row0 + rl0, tok, acc[t][0]);
+        store_out(p, row0 + rl0, tok + 1, acc[t][1]);
+        store_out(p, row0 + rl0 + 8, tok, acc[t][2]);
+        store_out(p, row0 + rl0 + 8, tok + 1, acc[t][3]);
       }
     } else {
       // Partial: slot 0 = first row tile of this CTA, slot 1 = its last one.
@@ -325,47 +309,61 @@ __device__ void gemv_consumer(const GemvParams& p, const uint8_t* table, uint8_t
         __stcg(reinterpret_cast<float2*>(part + (size_t)rl0 * tokens + tok), make_float2(acc[t][0], acc[t][1]));
         __stcg(reinterpret_cast<float2*>(part + (size_t)(rl0 + 8) * tokens + tok), make_float2(acc[t][2], acc[t][3]));
       }
-      __threadfence();
       __syncwarp();
       const int c_first = cta_of_unit(rt * p.n_blocks, grid, p.total_units);
       const int c_last = cta_of_unit(rt * p.n_blocks + p.n_blocks - 1, grid, p.total_units);
       int last = 0;
       if (lane == 0) {
         int* counter = p.counters + (size_t)rt * p.warps + warp;
-        const int old = atomicAdd(counter, 1);
+        const int old = atomic_add_acq_rel_gpu(counter, 1);
         last = (old == c_last - c_first);
-        if (last) *counter = 0;  // leave the workspace zeroed for the next launch
+        if (last) *counter = 0;  // leave the counter zeroed for the next launch
       }
       last = __shfl_sync(0xFFFFFFFFu, last, 0);
       if (last) {
-        __threadfence();
         float sum[NT][4];
 #pragma unroll
         for (int t = 0; t < NT; ++t)
 #pragma unroll
           for (int i = 0; i < 4; ++i) sum[t][i] = 0.f;
-        for (int c = c_first; c <= c_last; ++c) {
-          const int c_rt0 = unit_begin(c, grid, p.total_units) / p.n_blocks;
-          const int c_slot = (rt == c_rt0) ? 0 : 1;
-          const float* src = p.partials + ((size_t)(c * 2 + c_slot) * rows) * tokens;
+        // Issue the loads of up to kBatch segments before summing them (in CTA order).
+        constexpr int kBatch = 8 / NT;
+        for (int c0 = c_first; c0 <= c_last; c0 += kBatch) {
+          float2 v[kBatch][NT][2];
 #pragma unroll
-          for (int t = 0; t < NT; ++t) {
-            const int tok = 8 * t + 2 * tig;
-            const float2 v0 = __ldcg(reinterpret_cast<const float2*>(src + (size_t)rl0 * tokens + tok));
-            const float2 v1 = __ldcg(reinterpret_cast<const float2*>(src + (size_t)(rl0 + 8) * tokens + tok));
-            sum[t][0] += v0.x;
-            sum[t][1] += v0.y;
-            sum[t][2] += v1.x;
-            sum[t][3] += v1.y;
+          for (int j = 0; j < kBatch; ++j) {
+            const int c = c0 + j;
+            if (c <= c_last) {
+              const int c_slot = (rt == unit_begin(c, grid, p.total_units) / p.n_blocks) ? 0 : 1;
+              const float* src = p.partials + ((size_t)(c * 2 + c_slot) * rows) * tokens;
+#pragma unroll
+              for (int t = 0; t < NT; ++t) {
+                const int tok = 8 * t + 2 * tig;
+                v[j][t][0] = __ldcg(reinterpret_cast<const float2*>(src + (size_t)rl0 * tokens + tok));
+                v[j][t][1] = __ldcg(reinterpret_cast<const float2*>(src + (size_t)(rl0 + 8) * tokens + tok));
+              }
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < kBatch; ++j) {
+            if (c0 + j <= c_last) {
+#pragma unroll
+              for (int t = 0; t < NT; ++t) {
+                sum[t][0] += v[j][t][0].x;
+                sum[t][1] += v[j][t][0].y;
+                sum[t][2] += v[j][t][1].x;
+                sum[t][3] += v[j][t][1].y;
+              }
+            }
           }
         }
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
           const int tok = 8 * t + 2 * tig;
-          store_out<NT>(p, row0 + rl0, tok, sum[t][0]);
-          store_out<NT>(p, row0 + rl0, tok + 1, sum[t][1]);
-          store_out<NT>(p, row0 + rl0 + 8, tok, sum[t][2]);
-          store_out<NT>(p, row0 + rl0 + 8, tok + 1, sum[t][3]);
+          store_out(p, row0 + rl0, tok, sum[t][0]);
+          store_out(p, row0 + rl0, tok + 1, sum[t][1]);
+          store_out(p, row0 + rl0 + 8, tok, sum[t][2]);
+          store_out(p, row0 + rl0 + 8, tok + 1, sum[t][3]);
         }
       }
     }
@@ -384,24 +382,21 @@ __global__ void __launch_bounds__(288, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* table = smem;
   const int rows = p.warps * 16;
+  const int tokens = 8 * NT;
   const StageLayout L = gemv_stage_layout(rows, NT);
   uint8_t* stage0 = smem + kTableBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(stage0 + (size_t)p.stages * L.bytes);
+  float* xsf = reinterpret_cast<float*>(stage0 + (size_t)p.stages * L.bytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(xsf) + gemv_xs_bytes(p.n_blocks, NT));
   const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + kMaxStages);
+  const bool async_all = kTma && p.x_bulk;
 
   const int u0 = unit_begin(blockIdx.x, gridDim.x, p.total_units);
   const int u1 = unit_begin(blockIdx.x + 1, gridDim.x, p.total_units);
 
-  // Lane-private codebook: entry (q | h<<8) of lane l at byte (q<<8)|(h<<7)|(l<<2).
-  for (int i = threadIdx.x; i < 512 * 32; i += blockDim.x) {
-    const uint32_t code = i >> 5, l = i & 31;
-    const uint32_t off = ((code & 0xFFu) << 8) | ((code >> 8) << 7) | (l << 2);
-    *reinterpret_cast<uint32_t*>(table + off) = __ldg(p.table + code);
-  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < p.stages; ++s) {
-      mbar_init(full0 + 8 * s, 32);        // 32 producer lanes (+ TMA bytes)
-      mbar_init(empty0 + 8 * s, p.warps);  // one arrival per consumer warp
+      mbar_init(full0 + 8 * s, async_all ? 1 : 32);  // producer arrivals (+ copy bytes)
+      mbar_init(empty0 + 8 * s, p.warps);            // one arrival per consumer warp
     }
     fence_barrier_init();
   }
@@ -410,9 +405,33 @@ __global__ void __launch_bounds__(288, 1)
   const int warp = threadIdx.x >> 5;
   if (warp == p.warps) {
     gemv_producer<NT, kTma>(p, &maps, stage0, L, full0, empty0, u0, u1);
-  } else {
-    gemv_consumer<NT>(p, table, stage0, L, full0, empty0, u0, u1);
+    return;
   }
+  // Consumers: codebook, activation scales and zero padding rows, then the main loop.
+  const int nthreads = p.warps * 32;
+  // Lane-private codebook: entry (q | h<<8) of lane l at byte (q<<8)|(h<<7)|(l<<2).
+  for (int i = threadIdx.x; i < 512 * 32; i += nthreads) {
+    const uint32_t code = i >> 5, l = i & 31;
+    const uint32_t off = ((code & 0xFFu) << 8) | ((code >> 8) << 7) | (l << 2);
+    *reinterpret_cast<uint32_t*>(table + off) = __ldg(p.table + code);
+  }
+  // Activation scales as floats, laid out [k group][token]; padding tokens get 1.
+  for (int i = threadIdx.x; i < p.n_blocks * 8 * tokens; i += nthreads) {
+    const int kg = i / tokens, tok = i - kg * tokens;
+    xsf[i] = tok < p.m ? e8m0_to_float(p.xs[(int64_t)tok * p.ldxs + kg]) : 1.0f;
+  }
+  if (async_all) {
+    // The bulk copies fill rows < M only: zero the padding rows of every stage once.
+    const int per_stage = (tokens - p.m) * (kXRowBytes / 16);
+    for (int i = threadIdx.x; i < p.stages * per_stage; i += nthreads) {
+      const int s = i / per_stage, j = i - s * per_stage;
+      const int tok = p.m + j / (kXRowBytes / 16), c = j % (kXRowBytes / 16);
+      *reinterpret_cast<uint4*>(stage0 + (size_t)s * L.bytes + L.x + tok * kXRowBytes + c * 16) =
+          make_uint4(0, 0, 0, 0);
+    }
+  }
+  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+  gemv_consumer<NT>(p, table, xsf, stage0, L, full0, empty0, u0, u1);
 }
 
 // ---------------------------------------------------------------------------
@@ -498,11 +517,13 @@ bool make_gemv_maps(const GemvParams& p, GemvMaps* maps) {
   return true;
 }
 
-uint32_t gemv_smem_bytes_host(int rows, int nt, int stages) { return gemv_smem_bytes(rows, nt, stages); }
+uint32_t gemv_smem_bytes_host(int rows, int nt, int stages, int n_blocks) {
+  return gemv_smem_bytes(rows, nt, stages, n_blocks);
+}
 
 template <int NT, bool kTma>
 static cudaError_t launch_gemv_t(const GemvParams& p, const GemvMaps& maps, int grid, cudaStream_t stream) {
-  const uint32_t smem = gemv_smem_bytes(p.warps * 16, NT, p.stages);
+  const uint32_t smem = gemv_smem_bytes(p.warps * 16, NT, p.stages, p.n_blocks);
   auto kern = iq3s_gemv_kernel<NT, kTma>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;

@@ -59,8 +59,7 @@ struct GemvParams {
   int stages;
   int row_tiles;
   int total_units;
-  int x_vec;   // xq rows 16-byte aligned
-  int xs_vec;  // xs rows 8-byte aligned
+  int x_bulk;  // xq base and row stride 16-byte aligned: activation rows arrive by bulk copies
 };
 
 struct GemvMaps {
@@ -70,7 +69,7 @@ struct GemvMaps {
 bool make_gemv_maps(const GemvParams& p, GemvMaps* maps);
 cudaError_t launch_gemv(const GemvParams& p, int nt, bool use_tma, const GemvMaps& maps, int grid,
                         cudaStream_t stream);
-uint32_t gemv_smem_bytes_host(int rows, int nt, int stages);
+uint32_t gemv_smem_bytes_host(int rows, int nt, int stages, int n_blocks);
 
 cudaError_t launch_wait_selftest(unsigned long long limit_ns, cudaStream_t stream);
 cudaError_t probe_kernel_image();
