@@ -122,9 +122,9 @@ int require_sm100(DeviceInfo* info) {
 
 // --- configurations ---------------------------------------------------------
 // GEMV search space: warps x stages (tokens per launch follow M).
-const int kGemvWarps[] = {4, 8};
+const int kGemvWarps[] = {4, 8, 12, 16};
 const int kGemvStages[] = {3, 4, 6, 8};
-constexpr int kNumGemvConfigs = 2 * 4 * 2;
+constexpr int kNumGemvConfigs = 4 * 4 * 2;
 
 int gemv_nt_for(int64_t m) { return m <= 8 ? 1 : (m <= 16 ? 2 : 4); }
 
@@ -148,7 +148,8 @@ void default_config(int64_t m, int64_t n, int64_t b, MamboLinearConfig* cfg, int
 int validate_config(const MamboLinearConfig* cfg, int64_t m, int64_t b, const DeviceInfo& info) {
   if (cfg->kernel != MAMBO_KERNEL_GEMV && cfg->kernel != MAMBO_KERNEL_AUTO)
     return fail(MAMBO_EINVAL, "unknown kernel kind %d", cfg->kernel);
-  if (cfg->warps != 4 && cfg->warps != 8) return fail(MAMBO_EINVAL, "warps must be 4 or 8");
+  if (cfg->warps != 4 && cfg->warps != 8 && cfg->warps != 12 && cfg->warps != 16)
+    return fail(MAMBO_EINVAL, "warps must be 4, 8, 12 or 16");
   if (cfg->stages < 2 || cfg->stages > 12) return fail(MAMBO_EINVAL, "stages must be in [2, 12]");
   const uint32_t smem = gemv_smem_bytes_host(cfg->warps * 16, gemv_nt_for(m), cfg->stages, (int)b);
   if ((int)smem > info.max_smem_optin)

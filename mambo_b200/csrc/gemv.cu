@@ -86,8 +86,8 @@ __device__ __forceinline__ uint32_t signs_off(uint32_t row, uint32_t byte) {
 
 __device__ __forceinline__ void mma_e4m3(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+  // Pure register-to-register: not volatile, so the compiler may overlap groups.
+  asm("mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%10,%10,%10,%10};\n"
       : "=f"(c[0]), "=f"(c[1]), "=f"(c[2]), "=f"(c[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.0f));
@@ -202,9 +202,19 @@ __device__ void gemv_consumer(const GemvParams& p, const uint8_t* table, const f
   const int gid = lane >> 2, tig = lane & 3;
   const int rows = p.warps * 16;
   const int tokens = 8 * NT;
-  const uint32_t table_base = smem_u32(table);  // the lane offset rides in the address bytes
   const uint32_t lane4x = (uint32_t)(lane << 2) * 0x01010101u;
   const int rl0 = warp * 16 + gid;  // local rows rl0 and rl0 + 8
+  // Swizzled in-stage offsets of this thread's qs halfwords and sign bytes,
+  // per row h and group g (the group's low bits ride in a constant).
+  uint32_t qs_o[2][4], sg_o[2][2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const uint32_t r = rl0 + 8 * h;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) qs_o[h][j] = L.qs + qs_off(r, 16 * j + 2 * tig);
+#pragma unroll
+    for (int j = 0; j < 2; ++j) sg_o[h][j] = L.signs + signs_off(r, 16 * j + tig);
+  }
 
   float acc[NT][4];
 #pragma unroll
@@ -250,15 +260,13 @@ __device__ void gemv_consumer(const GemvParams& p, const uint8_t* table, const f
       float w[2];
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        const int r = rl0 + 8 * h;
-        const uint32_t q = *reinterpret_cast<const uint16_t*>(st + L.qs + qs_off(r, 8 * g + 2 * tig));
-        const uint32_t sb = st[L.signs + signs_off(r, 4 * g + tig)];
+        const uint32_t q = *reinterpret_cast<const uint16_t*>(st + qs_o[h][g >> 1] + 8 * (g & 1));
+        const uint32_t sb = st[sg_o[h][g >> 2] + 4 * (g & 3)];
         const uint32_t sel = (uint32_t)(4 + (g & 3)) | 0x2200u;
         const uint32_t addr0 = prmt(q, e0[h][g >> 2], sel);
         const uint32_t addr1 = prmt(q, e1[h][g >> 2], sel | 0x10u);
-        uint32_t m0, m1;
-        asm volatile("ld.shared.u32 %0, [%1];" : "=r"(m0) : "r"(table_base + addr0));
-        asm volatile("ld.shared.u32 %0, [%1];" : "=r"(m1) : "r"(table_base + addr1));
+        const uint32_t m0 = *reinterpret_cast<const uint32_t*>(table + addr0);
+        const uint32_t m1 = *reinterpret_cast<const uint32_t*>(table + addr1);
         a[h] = lop3_and_or((sb & 0xFu) * 0x10204080u, 0x80808080u, m0);
         a[2 + h] = lop3_and_or((sb >> 4) * 0x10204080u, 0x80808080u, m1);
         // weight scale d*(2*nibble+1): float(2^23 + t) * d - 2^23 * d, exact
@@ -375,8 +383,8 @@ __device__ void gemv_consumer(const GemvParams& p, const uint8_t* table, const f
   }
 }
 
-template <int NT, bool kTma>
-__global__ void __launch_bounds__(288, 1)
+template <int NT, int kWarps, bool kTma>
+__global__ void __launch_bounds__((kWarps + 1) * 32, 1)
     iq3s_gemv_kernel(const __grid_constant__ GemvParams p, const __grid_constant__ GemvMaps maps) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -521,29 +529,39 @@ uint32_t gemv_smem_bytes_host(int rows, int nt, int stages, int n_blocks) {
   return gemv_smem_bytes(rows, nt, stages, n_blocks);
 }
 
-template <int NT, bool kTma>
+template <int NT, int kWarps, bool kTma>
 static cudaError_t launch_gemv_t(const GemvParams& p, const GemvMaps& maps, int grid, cudaStream_t stream) {
   const uint32_t smem = gemv_smem_bytes(p.warps * 16, NT, p.stages, p.n_blocks);
-  auto kern = iq3s_gemv_kernel<NT, kTma>;
+  auto kern = iq3s_gemv_kernel<NT, kWarps, kTma>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   kern<<<grid, (p.warps + 1) * 32, smem, stream>>>(p, maps);
   return cudaGetLastError();
 }
 
+template <int NT, bool kTma>
+static cudaError_t launch_gemv_w(const GemvParams& p, const GemvMaps& maps, int grid, cudaStream_t stream) {
+  switch (p.warps) {
+    case 4: return launch_gemv_t<NT, 4, kTma>(p, maps, grid, stream);
+    case 8: return launch_gemv_t<NT, 8, kTma>(p, maps, grid, stream);
+    case 12: return launch_gemv_t<NT, 12, kTma>(p, maps, grid, stream);
+    default: return launch_gemv_t<NT, 16, kTma>(p, maps, grid, stream);
+  }
+}
+
 cudaError_t launch_gemv(const GemvParams& p, int nt, bool use_tma, const GemvMaps& maps, int grid,
                         cudaStream_t stream) {
   if (use_tma) {
     switch (nt) {
-      case 1: return launch_gemv_t<1, true>(p, maps, grid, stream);
-      case 2: return launch_gemv_t<2, true>(p, maps, grid, stream);
-      default: return launch_gemv_t<4, true>(p, maps, grid, stream);
+      case 1: return launch_gemv_w<1, true>(p, maps, grid, stream);
+      case 2: return launch_gemv_w<2, true>(p, maps, grid, stream);
+      default: return launch_gemv_w<4, true>(p, maps, grid, stream);
     }
   }
   switch (nt) {
-    case 1: return launch_gemv_t<1, false>(p, maps, grid, stream);
-    case 2: return launch_gemv_t<2, false>(p, maps, grid, stream);
-    default: return launch_gemv_t<4, false>(p, maps, grid, stream);
+    case 1: return launch_gemv_w<1, false>(p, maps, grid, stream);
+    case 2: return launch_gemv_w<2, false>(p, maps, grid, stream);
+    default: return launch_gemv_w<4, false>(p, maps, grid, stream);
   }
 }
 
