@@ -64,7 +64,7 @@ __host__ __device__ inline uint32_t gemv_xs_bytes(int n_blocks, int nt) {
 }
 
 __host__ __device__ inline uint32_t gemv_smem_bytes(int rows, int nt, int stages, int n_blocks) {
-  return 1024 + kTableBytes + stages * gemv_stage_layout(rows, nt).bytes + gemv_xs_bytes(n_blocks, nt) +
+  return 1024 + kTableBytes + stages * gemv_stage_layout(rows, nt).bytes + gemv_xs_bytes(n_blocks, nt) + 2048 +
          2 * kMaxStages * 8;
 }
 
@@ -112,9 +112,37 @@ __device__ void gemv_producer(const GemvParams& p, const GemvMaps* maps, uint8_t
       tma_prefetch_desc(&maps->scales);
     }
   }
+  // Weights do not depend on the previous kernel: with the fully asynchronous
+  // path, issue the first stages' weight copies before waiting for it.
+  int issued_weights = 0;
+  if (async_all) {
+    issued_weights = min(p.stages, u1 - u0);
+    for (int it = 0; it < issued_weights; ++it) {
+      const int u = u0 + it;
+      const uint32_t full = full0 + 8 * it;
+      uint8_t* st = stage0 + (size_t)it * L.bytes;
+      const int rt = u / p.n_blocks, kb = u % p.n_blocks;
+      const int n0 = rt * rows;
+      mbar_expect_tx(full, (uint32_t)rows * 110u + (uint32_t)p.m * 256u);
+      tma_load_3d(smem_u32(st + L.qs), &maps->qs, 0, n0, kb, full, policy);
+      tma_load_3d(smem_u32(st + L.signs), &maps->signs, 0, n0, kb, full, policy);
+      tma_load_2d(smem_u32(st + L.qh), &maps->qh, n0, kb, full, policy);
+      tma_load_2d(smem_u32(st + L.d), &maps->d, n0, kb, full, policy);
+      tma_load_2d(smem_u32(st + L.scales), &maps->scales, n0, kb, full, policy);
+    }
+  }
+  pdl_wait();  // activations come from the previous kernel
   for (int u = u0, it = 0; u < u1; ++u, ++it) {
     const int s = it % p.stages;
     const uint32_t full = full0 + 8 * s, empty = empty0 + 8 * s;
+    if (it < issued_weights) {
+      uint8_t* st = stage0 + (size_t)s * L.bytes;
+      const int kb = u % p.n_blocks;
+      for (int tok = 0; tok < p.m; ++tok)
+        bulk_load(smem_u32(st + L.x + tok * kXRowBytes), p.xq + (int64_t)tok * p.ldxq + (int64_t)kb * 256, 256, full);
+      mbar_arrive(full);
+      continue;
+    }
     if (it >= p.stages) {
       if (!mbar_wait_bounded(empty, ((it / p.stages) & 1) ^ 1, kSiteGemvEmpty)) return;
     }
@@ -279,10 +307,11 @@ __device__ void gemv_consumer(const GemvParams& p, const uint8_t* table, const f
         float c[4];
         mma_e4m3(c, a[0], a[1], a[2], a[3], b.x, b.y);
         const float2 xsc = *reinterpret_cast<const float2*>(xs_kb + g * tokens + 8 * t + 2 * tig);
-        acc[t][0] = fmaf(c[0] * xsc.x, w[0], acc[t][0]);
-        acc[t][1] = fmaf(c[1] * xsc.y, w[0], acc[t][1]);
-        acc[t][2] = fmaf(c[2] * xsc.x, w[1], acc[t][2]);
-        acc[t][3] = fmaf(c[3] * xsc.y, w[1], acc[t][3]);
+        // acc += (c * activation scale) * weight scale; c * 2^e is exact.
+        mul2(c[0], c[1], c[0], c[1], xsc.x, xsc.y);
+        mul2(c[2], c[3], c[2], c[3], xsc.x, xsc.y);
+        fma2(acc[t][0], acc[t][1], c[0], c[1], w[0], w[0]);
+        fma2(acc[t][2], acc[t][3], c[2], c[3], w[1], w[1]);
       }
     }
     __syncwarp();
@@ -394,7 +423,8 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
   const StageLayout L = gemv_stage_layout(rows, NT);
   uint8_t* stage0 = smem + kTableBytes;
   float* xsf = reinterpret_cast<float*>(stage0 + (size_t)p.stages * L.bytes);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(xsf) + gemv_xs_bytes(p.n_blocks, NT));
+  uint32_t* tstage = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(xsf) + gemv_xs_bytes(p.n_blocks, NT));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(tstage) + 2048);
   const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + kMaxStages);
   const bool async_all = kTma && p.x_bulk;
 
@@ -417,16 +447,15 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
   }
   // Consumers: codebook, activation scales and zero padding rows, then the main loop.
   const int nthreads = p.warps * 32;
-  // Lane-private codebook: entry (q | h<<8) of lane l at byte (q<<8)|(h<<7)|(l<<2).
+  // Stage the 2 KB codebook (two independent loads per thread at most), then
+  // expand it to the lane-private copy: entry (q | h<<8) of lane l at byte
+  // (q<<8)|(h<<7)|(l<<2). Consecutive threads write consecutive banks.
+  for (int i = threadIdx.x; i < 512; i += nthreads) tstage[i] = __ldg(p.table + i);
+  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
   for (int i = threadIdx.x; i < 512 * 32; i += nthreads) {
     const uint32_t code = i >> 5, l = i & 31;
     const uint32_t off = ((code & 0xFFu) << 8) | ((code >> 8) << 7) | (l << 2);
-    *reinterpret_cast<uint32_t*>(table + off) = __ldg(p.table + code);
-  }
-  // Activation scales as floats, laid out [k group][token]; padding tokens get 1.
-  for (int i = threadIdx.x; i < p.n_blocks * 8 * tokens; i += nthreads) {
-    const int kg = i / tokens, tok = i - kg * tokens;
-    xsf[i] = tok < p.m ? e8m0_to_float(p.xs[(int64_t)tok * p.ldxs + kg]) : 1.0f;
+    *reinterpret_cast<uint32_t*>(table + off) = tstage[code];
   }
   if (async_all) {
     // The bulk copies fill rows < M only: zero the padding rows of every stage once.
@@ -438,7 +467,14 @@ __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
           make_uint4(0, 0, 0, 0);
     }
   }
+  pdl_wait();  // the activation scales come from the previous kernel
+  // Activation scales as floats, laid out [k group][token]; padding tokens get 1.
+  for (int i = threadIdx.x; i < p.n_blocks * 8 * tokens; i += nthreads) {
+    const int kg = i / tokens, tok = i - kg * tokens;
+    xsf[i] = tok < p.m ? e8m0_to_float(p.xs[(int64_t)tok * p.ldxs + kg]) : 1.0f;
+  }
   asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+  pdl_launch_dependents();
   gemv_consumer<NT>(p, table, xsf, stage0, L, full0, empty0, u0, u1);
 }
 
@@ -533,10 +569,9 @@ template <int NT, int kWarps, bool kTma>
 static cudaError_t launch_gemv_t(const GemvParams& p, const GemvMaps& maps, int grid, cudaStream_t stream) {
   const uint32_t smem = gemv_smem_bytes(p.warps * 16, NT, p.stages, p.n_blocks);
   auto kern = iq3s_gemv_kernel<NT, kWarps, kTma>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e = ensure_smem_attribute((const void*)kern, smem);
   if (e != cudaSuccess) return e;
-  kern<<<grid, (p.warps + 1) * 32, smem, stream>>>(p, maps);
-  return cudaGetLastError();
+  return launch_pdl((const void*)kern, dim3(grid), dim3((p.warps + 1) * 32), smem, stream, p, maps);
 }
 
 template <int NT, bool kTma>

@@ -5,6 +5,29 @@
 
 namespace mambo {
 
+// Sets a kernel's dynamic shared memory limit once per (kernel, device).
+cudaError_t ensure_smem_attribute(const void* kernel, size_t smem_bytes);
+
+// Launches with programmatic stream serialization: the kernel may begin while
+// the previous kernel in the stream finishes, and must call pdl_wait() before
+// touching memory that kernel produces or consumes.
+template <typename... Args>
+cudaError_t launch_pdl(const void* kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       const Args&... args) {
+  void* argv[] = {const_cast<void*>(static_cast<const void*>(&args))...};
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelExC(&cfg, kernel, argv);
+}
+
 struct QuantParams {
   const void* x;
   int64_t m, k, ldx;

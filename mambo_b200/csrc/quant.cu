@@ -64,6 +64,10 @@ __global__ void __launch_bounds__(256) quantize_mxfp8_kernel(const QuantParams p
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
   const int64_t warp_id = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const T* x = static_cast<const T*>(p.x);
+  // The activations may come from the previous kernel, and the outputs may
+  // still be read by it: wait for it, then let the next kernel start early.
+  pdl_wait();
+  pdl_launch_dependents();
 
   for (int64_t base = warp_id * 8; base < total_groups; base += warps * 8) {
     const int64_t grp = base + (lane >> 2);
@@ -154,12 +158,10 @@ __global__ void __launch_bounds__(256) quantize_mxfp8_kernel(const QuantParams p
 
 template <typename T, bool kVec>
 static cudaError_t launch_quant_t(const QuantParams& p, int rounding, int grid, cudaStream_t stream) {
-  if (rounding == MAMBO_ROUND_TIES_DOWN) {
-    quantize_mxfp8_kernel<T, kVec, MAMBO_ROUND_TIES_DOWN><<<grid, 256, 0, stream>>>(p);
-  } else {
-    quantize_mxfp8_kernel<T, kVec, MAMBO_ROUND_NEAREST_EVEN><<<grid, 256, 0, stream>>>(p);
-  }
-  return cudaGetLastError();
+  const void* kern = rounding == MAMBO_ROUND_TIES_DOWN
+                         ? (const void*)quantize_mxfp8_kernel<T, kVec, MAMBO_ROUND_TIES_DOWN>
+                         : (const void*)quantize_mxfp8_kernel<T, kVec, MAMBO_ROUND_NEAREST_EVEN>;
+  return launch_pdl(kern, dim3(grid), dim3(256), 0, stream, p);
 }
 
 cudaError_t launch_quantize_mxfp8(const QuantParams& p, int x_dtype, int rounding, int num_sms, cudaStream_t stream) {
