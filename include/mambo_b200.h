@@ -66,7 +66,7 @@ typedef struct MamboIQ3SWeight {
 /* Launch configuration of the linear kernels (NULL = tuned default for the shape). */
 typedef struct MamboLinearConfig {
   int kernel;        /* MAMBO_KERNEL_* */
-  int warps;         /* compute warps per CTA (GEMV: 16 weight rows each) */
+  int warps;         /* GEMV_SYNC: compute warps per CTA (16 weight rows each); GEMV: fixed 128-row tiles */
   int stages;        /* shared-memory pipeline depth */
   int ctas_per_sm;   /* GEMV persistent grid = SMs * ctas_per_sm (0 = 1) */
   int split;         /* GEMV: 0 = stream-K over all SMs, 1 = one CTA per row tile */
@@ -74,7 +74,11 @@ typedef struct MamboLinearConfig {
   int reserved[2];
 } MamboLinearConfig;
 
-enum { MAMBO_KERNEL_AUTO = 0, MAMBO_KERNEL_GEMV = 1, MAMBO_KERNEL_GEMM = 2 };
+/* Kernel kinds: GEMV = weight-streaming decode kernel on tcgen05 tensor cores
+ * (the default); GEMM = tcgen05 kernel for large M; GEMV_SYNC = the same
+ * weight-streaming kernel on legacy mma.sync FP8 instructions, kept as a
+ * measured baseline (on sm_100 its FP8 fragments go through conversions). */
+enum { MAMBO_KERNEL_AUTO = 0, MAMBO_KERNEL_GEMV = 1, MAMBO_KERNEL_GEMM = 2, MAMBO_KERNEL_GEMV_SYNC = 3 };
 
 /* Library version string. */
 MAMBO_API const char* mambo_version(void);

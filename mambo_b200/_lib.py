@@ -30,6 +30,7 @@ MAMBO_ROUND_TIES_DOWN = 1
 MAMBO_KERNEL_AUTO = 0
 MAMBO_KERNEL_GEMV = 1
 MAMBO_KERNEL_GEMM = 2
+MAMBO_KERNEL_GEMV_SYNC = 3
 
 # Every symbol include/mambo_b200.h declares.
 EXPORTED_SYMBOLS = (

@@ -137,38 +137,51 @@ int require_sm100(DeviceInfo* info) {
 }
 
 // --- configurations ---------------------------------------------------------
-// GEMV search space: warps x stages (tokens per launch follow M).
-const int kGemvWarps[] = {4, 8, 12, 16};
-const int kGemvStages[] = {3, 4, 6, 8};
-constexpr int kNumGemvConfigs = 4 * 4 * 2;
+// tcgen05 GEMV (MAMBO_KERNEL_GEMV): 128-row tiles; tuned over stages x split.
+const int kTcStages[] = {2, 3, 4, 5};
+constexpr int kNumTcConfigs = 4 * 2;
+// mma.sync GEMV (MAMBO_KERNEL_GEMV_SYNC): warps x stages x split.
+const int kSyncWarps[] = {4, 8, 12, 16};
+const int kSyncStages[] = {3, 4, 6, 8};
+constexpr int kNumSyncConfigs = 4 * 4 * 2;
 
 int gemv_nt_for(int64_t m) { return m <= 8 ? 1 : (m <= 16 ? 2 : 4); }
 
 // Shared memory an SM offers one CTA (B200: 227 KB); used when no device is visible.
 constexpr int kSmemOptinDefault = 232448;
 
+int kernel_of(const MamboLinearConfig& c) { return c.kernel == MAMBO_KERNEL_AUTO ? MAMBO_KERNEL_GEMV : c.kernel; }
+
+uint32_t config_smem(const MamboLinearConfig& c, int nt, int64_t b) {
+  if (kernel_of(c) == MAMBO_KERNEL_GEMV_SYNC) return gemv_smem_bytes_host(c.warps * 16, nt, c.stages, (int)b);
+  return gemv_tc_smem_bytes(nt, c.stages);
+}
+
 void default_config(int64_t m, int64_t n, int64_t b, MamboLinearConfig* cfg, int smem_optin) {
   (void)n;
   std::memset(cfg, 0, sizeof(*cfg));
   cfg->kernel = MAMBO_KERNEL_GEMV;
-  cfg->warps = 12;
+  cfg->warps = 8;
   cfg->ctas_per_sm = 1;
   cfg->split = 0;
-  // Measured best on B200 for the Llama-3-8B shapes: 12 consumer warps, 4 stages
-  // (fewer when the codebook, stages and scales do not fit).
+  // Deepest raw-stage ring (up to 4) that fits next to the codebook and the two operand slots.
   const int nt = gemv_nt_for(m < 32 ? m : 32);
-  int stages = 4;
-  while (stages > 2 && (int)gemv_smem_bytes_host(cfg->warps * 16, nt, stages, (int)b) > smem_optin) --stages;
-  cfg->stages = stages;
+  cfg->stages = 4;
+  while (cfg->stages > 2 && (int)config_smem(*cfg, nt, b) > smem_optin) --cfg->stages;
 }
 
 int validate_config(const MamboLinearConfig* cfg, int64_t m, int64_t b, const DeviceInfo& info) {
-  if (cfg->kernel != MAMBO_KERNEL_GEMV && cfg->kernel != MAMBO_KERNEL_AUTO)
+  const int kind = kernel_of(*cfg);
+  if (kind != MAMBO_KERNEL_GEMV && kind != MAMBO_KERNEL_GEMV_SYNC)
     return fail(MAMBO_EINVAL, "unknown kernel kind %d", cfg->kernel);
-  if (cfg->warps != 4 && cfg->warps != 8 && cfg->warps != 12 && cfg->warps != 16)
-    return fail(MAMBO_EINVAL, "warps must be 4, 8, 12 or 16");
-  if (cfg->stages < 2 || cfg->stages > 12) return fail(MAMBO_EINVAL, "stages must be in [2, 12]");
-  const uint32_t smem = gemv_smem_bytes_host(cfg->warps * 16, gemv_nt_for(m), cfg->stages, (int)b);
+  if (kind == MAMBO_KERNEL_GEMV_SYNC) {
+    if (cfg->warps != 4 && cfg->warps != 8 && cfg->warps != 12 && cfg->warps != 16)
+      return fail(MAMBO_EINVAL, "warps must be 4, 8, 12 or 16");
+    if (cfg->stages < 2 || cfg->stages > 12) return fail(MAMBO_EINVAL, "stages must be in [2, 12]");
+  } else if (cfg->stages < 2 || cfg->stages > gemv_tc_max_stages()) {
+    return fail(MAMBO_EINVAL, "stages must be in [2, %d]", gemv_tc_max_stages());
+  }
+  const uint32_t smem = config_smem(*cfg, gemv_nt_for(m), b);
   if ((int)smem > info.max_smem_optin)
     return fail(MAMBO_EINVAL, "configuration needs %u bytes of shared memory (device allows %d)", smem,
                 info.max_smem_optin);
@@ -176,28 +189,30 @@ int validate_config(const MamboLinearConfig* cfg, int64_t m, int64_t b, const De
 }
 
 // Split-K counters live at the start of every workspace: 64 Ki ints, zero
-// between calls. Shapes needing more (row_tiles * warps > 65536) are rejected.
+// between calls, a fixed region so that a call never finds another shape's
+// partials there. Shapes needing more are rejected.
 constexpr size_t kCounterBytes = 256 * 1024;
 
 struct GemvPlan {
-  int nt, rows, row_tiles, units, grid;
-  size_t counters_bytes, partial_bytes;
+  int nt, rows, row_tiles, units, grid, counter_slots;
+  size_t counters_bytes, partial_bytes, pack_bytes;
 };
 
 GemvPlan plan_gemv(int64_t m_chunk, int64_t n, int64_t b, const MamboLinearConfig& cfg, int sms) {
   GemvPlan P{};
+  const bool tc = kernel_of(cfg) == MAMBO_KERNEL_GEMV;
   P.nt = gemv_nt_for(m_chunk);
-  P.rows = cfg.warps * 16;
+  P.rows = tc ? 128 : cfg.warps * 16;
   P.row_tiles = (int)((n + P.rows - 1) / P.rows);
   P.units = (int)(P.row_tiles * b);
   int ctas = sms * (cfg.ctas_per_sm > 0 ? cfg.ctas_per_sm : 1);
   if (cfg.split == 1) ctas = P.row_tiles;  // one CTA per row tile, no split-K
   P.grid = P.units < ctas ? P.units : ctas;
   if (P.grid < 1) P.grid = 1;
-  // The counter region has a fixed size so that it never overlaps the
-  // partials of a call with another shape sharing the workspace.
+  P.counter_slots = P.row_tiles * (tc ? 4 : cfg.warps);
   P.counters_bytes = kCounterBytes;
   P.partial_bytes = (size_t)P.grid * 2 * P.rows * 8 * P.nt * sizeof(float);
+  P.pack_bytes = tc ? (size_t)b * gemv_tc_pack_bytes(P.nt) : 0;
   return P;
 }
 
@@ -311,20 +326,27 @@ int mambo_default_config(int64_t m, int64_t n_rows, int64_t n_blocks, MamboLinea
 }
 
 int mambo_num_configs(int kernel) {
-  if (kernel == MAMBO_KERNEL_GEMV || kernel == MAMBO_KERNEL_AUTO) return kNumGemvConfigs;
+  if (kernel == MAMBO_KERNEL_GEMV || kernel == MAMBO_KERNEL_AUTO) return kNumTcConfigs;
+  if (kernel == MAMBO_KERNEL_GEMV_SYNC) return kNumSyncConfigs;
   return 0;
 }
 
 int mambo_config_at(int kernel, int index, MamboLinearConfig* cfg) {
   if (!cfg) return fail(MAMBO_EINVAL, "null config");
-  if ((kernel != MAMBO_KERNEL_GEMV && kernel != MAMBO_KERNEL_AUTO) || index < 0 || index >= kNumGemvConfigs)
-    return fail(MAMBO_EINVAL, "no configuration %d for kernel %d", index, kernel);
+  if (kernel == MAMBO_KERNEL_AUTO) kernel = MAMBO_KERNEL_GEMV;
+  const int n = mambo_num_configs(kernel);
+  if (n == 0 || index < 0 || index >= n) return fail(MAMBO_EINVAL, "no configuration %d for kernel %d", index, kernel);
   std::memset(cfg, 0, sizeof(*cfg));
-  cfg->kernel = MAMBO_KERNEL_GEMV;
-  cfg->warps = kGemvWarps[index / 8];
-  cfg->stages = kGemvStages[(index / 2) % 4];
-  cfg->split = index % 2;
+  cfg->kernel = kernel;
   cfg->ctas_per_sm = 1;
+  cfg->split = index % 2;
+  if (kernel == MAMBO_KERNEL_GEMV) {
+    cfg->warps = 8;
+    cfg->stages = kTcStages[index / 2];
+  } else {
+    cfg->warps = kSyncWarps[index / 8];
+    cfg->stages = kSyncStages[(index / 2) % 4];
+  }
   return ok();
 }
 
@@ -338,7 +360,7 @@ size_t mambo_iq3s_linear_workspace_bytes(int64_t m, int64_t n_rows, int64_t n_bl
   const int sms = (st == MAMBO_OK && info.sms > 0) ? info.sms : 148;
   const int64_t m_chunk = m < 32 ? m : 32;
   GemvPlan P = plan_gemv(m_chunk, n_rows, n_blocks, c, sms);
-  return P.counters_bytes + P.partial_bytes;
+  return P.counters_bytes + P.partial_bytes + P.pack_bytes;
 }
 
 int mambo_iq3s_linear(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t ldxs, int64_t m,
@@ -361,48 +383,96 @@ int mambo_iq3s_linear(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_
   MamboLinearConfig c;
   if (cfg) c = *cfg; else default_config(m, w->n_rows, w->n_blocks, &c, info.max_smem_optin);
   if (c.kernel == MAMBO_KERNEL_AUTO) c.kernel = MAMBO_KERNEL_GEMV;
+  if (c.kernel == MAMBO_KERNEL_GEMV && (w->n_rows % 8 != 0 || c.loader != 0)) c.kernel = MAMBO_KERNEL_GEMV_SYNC;
+  if (c.kernel == MAMBO_KERNEL_GEMV_SYNC && c.warps == 0) c.warps = 8;
+  if (c.kernel == MAMBO_KERNEL_GEMV_SYNC && c.stages > 12) c.stages = 4;
   st = validate_config(&c, m < 32 ? m : 32, w->n_blocks, info);
   if (st != MAMBO_OK) return st;
 
   const int64_t m_chunk_max = 32;
+  const bool tc = kernel_of(c) == MAMBO_KERNEL_GEMV;
   for (int64_t m0 = 0; m0 < m; m0 += m_chunk_max) {
     const int64_t mc = (m - m0) < m_chunk_max ? (m - m0) : m_chunk_max;
     GemvPlan P = plan_gemv(mc, w->n_rows, w->n_blocks, c, info.sms);
-    if ((size_t)P.row_tiles * c.warps * sizeof(int) > kCounterBytes)
+    if ((size_t)P.counter_slots * sizeof(int) > kCounterBytes)
       return fail(MAMBO_EINVAL, "N=%lld needs more split-K counters than the workspace holds", (long long)w->n_rows);
-    const size_t need = P.counters_bytes + P.partial_bytes;
+    const size_t need = P.counters_bytes + P.partial_bytes + P.pack_bytes;
     if (!workspace || workspace_bytes < need)
       return fail(MAMBO_EWORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
-    GemvParams p{};
-    p.xq = xq + m0 * ldxq;
-    p.ldxq = ldxq;
-    p.xs = xs + m0 * ldxs;
-    p.ldxs = ldxs;
-    p.m = (int)mc;
-    p.n_rows = (int)w->n_rows;
-    p.n_blocks = (int)w->n_blocks;
-    p.d = (const uint8_t*)w->d;
-    p.qs = (const uint8_t*)w->qs;
-    p.qh = (const uint8_t*)w->qh;
-    p.signs = (const uint8_t*)w->signs;
-    p.scales = (const uint8_t*)w->scales;
-    p.table = fp8_table;
+    if ((uintptr_t)workspace % 256) return fail(MAMBO_EINVAL, "workspace must be 256-byte aligned");
     const size_t esz = out_dtype == MAMBO_BF16 ? 2 : 4;
-    p.out = (uint8_t*)out + m0 * ldo * esz;
-    p.out_bf16 = out_dtype == MAMBO_BF16;
-    p.ldo = ldo;
-    p.counters = (int*)workspace;
-    p.partials = (float*)((uint8_t*)workspace + P.counters_bytes);
-    p.warps = c.warps;
-    p.stages = c.stages;
-    p.row_tiles = P.row_tiles;
-    p.total_units = P.units;
-    p.x_bulk = ((uintptr_t)p.xq % 16 == 0) && (ldxq % 16 == 0);
+    int* counters = (int*)workspace;
+    float* partials = (float*)((uint8_t*)workspace + P.counters_bytes);
+    uint8_t* pack = (uint8_t*)workspace + P.counters_bytes + P.partial_bytes;
+
+    // Weight tensor maps (the tcgen05 kernel always uses 128-row boxes).
+    GemvParams mp{};
+    mp.n_rows = (int)w->n_rows;
+    mp.n_blocks = (int)w->n_blocks;
+    mp.d = (const uint8_t*)w->d;
+    mp.qs = (const uint8_t*)w->qs;
+    mp.qh = (const uint8_t*)w->qh;
+    mp.signs = (const uint8_t*)w->signs;
+    mp.scales = (const uint8_t*)w->scales;
+    mp.warps = tc ? 8 : c.warps;
     GemvMaps maps;
     std::memset(&maps, 0, sizeof(maps));
-    const bool use_tma = (c.loader == 0) && make_gemv_maps(p, &maps);
-    cudaError_t e = launch_gemv(p, P.nt, use_tma, maps, P.grid, (cudaStream_t)stream);
-    if (e != cudaSuccess) return cuda_fail(e, "iq3s_gemv");
+    const bool have_maps = (c.loader == 0) && make_gemv_maps(mp, &maps);
+
+    cudaError_t e;
+    if (tc) {
+      if (!have_maps)
+        return fail(MAMBO_EINVAL,
+                    "the tcgen05 GEMV needs N %% 8 == 0 and 16-byte aligned weight fields (use MAMBO_KERNEL_GEMV_SYNC)");
+      PackParams pk{};
+      pk.xq = xq + m0 * ldxq;
+      pk.ldxq = ldxq;
+      pk.xs = xs + m0 * ldxs;
+      pk.ldxs = ldxs;
+      pk.m = (int)mc;
+      pk.n_blocks = (int)w->n_blocks;
+      pk.nmma = P.nt == 4 ? 32 : 16;
+      pk.pack_bytes = (int)gemv_tc_pack_bytes(P.nt);
+      pk.x_vec = ((uintptr_t)pk.xq % 16 == 0) && (ldxq % 16 == 0);
+      pk.pack = pack;
+      e = launch_pack_activations(pk, info.sms, (cudaStream_t)stream);
+      if (e != cudaSuccess) return cuda_fail(e, "pack_activations");
+      GemvTcParams p{};
+      p.xpack = pack;
+      p.m = (int)mc;
+      p.n_rows = (int)w->n_rows;
+      p.n_blocks = (int)w->n_blocks;
+      p.table = fp8_table;
+      p.out = (uint8_t*)out + m0 * ldo * esz;
+      p.out_bf16 = out_dtype == MAMBO_BF16;
+      p.ldo = ldo;
+      p.partials = partials;
+      p.counters = counters;
+      p.stages = c.stages;
+      p.row_tiles = P.row_tiles;
+      p.total_units = P.units;
+      e = launch_gemv_tc(p, P.nt, maps, P.grid, (cudaStream_t)stream);
+      if (e != cudaSuccess) return cuda_fail(e, "iq3s_gemv_tc");
+    } else {
+      GemvParams p = mp;
+      p.xq = xq + m0 * ldxq;
+      p.ldxq = ldxq;
+      p.xs = xs + m0 * ldxs;
+      p.ldxs = ldxs;
+      p.m = (int)mc;
+      p.table = fp8_table;
+      p.out = (uint8_t*)out + m0 * ldo * esz;
+      p.out_bf16 = out_dtype == MAMBO_BF16;
+      p.ldo = ldo;
+      p.counters = counters;
+      p.partials = partials;
+      p.stages = c.stages;
+      p.row_tiles = P.row_tiles;
+      p.total_units = P.units;
+      p.x_bulk = ((uintptr_t)p.xq % 16 == 0) && (ldxq % 16 == 0);
+      e = launch_gemv(p, P.nt, have_maps, maps, P.grid, (cudaStream_t)stream);
+      if (e != cudaSuccess) return cuda_fail(e, "iq3s_gemv_sync");
+    }
   }
   return ok();
 }

@@ -184,14 +184,22 @@ def _linear_case(cuda_device, m, n, k, seed, outliers=False):
     return raw, x, xq, xs, ref
 
 
+KERNELS = {  # (kernel kind, weight loader)
+    "tcgen05": (_lib.MAMBO_KERNEL_GEMV, 0),
+    "sync_tma": (_lib.MAMBO_KERNEL_GEMV_SYNC, 0),
+    "sync_plain": (_lib.MAMBO_KERNEL_GEMV_SYNC, 1),
+}
+
+
 @pytest.mark.parametrize("m,n,k", [(1, 256, 512), (2, 384, 1024), (8, 1024, 2048), (13, 512, 768), (32, 640, 1536),
-                                   (40, 128, 256)])
-@pytest.mark.parametrize("loader", [0, 1])
+                                   (40, 128, 256), (17, 136, 512)])
+@pytest.mark.parametrize("kernel", sorted(KERNELS))
 @pytest.mark.parametrize("split", [0, 1])
-def test_linear_loaders_and_splits_match_oracle(cuda_device, m, n, k, loader, split):
+def test_linear_kernels_and_splits_match_oracle(cuda_device, m, n, k, kernel, split):
     raw, _, xq, xs, ref = _linear_case(cuda_device, m, n, k, seed=1000 + m + n)
     fields = gpu_weight(raw, cuda_device)
-    cfg = {"kernel": _lib.MAMBO_KERNEL_GEMV, "warps": 8, "stages": 4, "ctas_per_sm": 1, "split": split,
+    kind, loader = KERNELS[kernel]
+    cfg = {"kernel": kind, "warps": 8, "stages": 4 if m <= 16 else 3, "ctas_per_sm": 1, "split": split,
            "loader": loader}
     out = launch_iq3_s_fp8_matmul(torch.from_numpy(xq).to(cuda_device), torch.from_numpy(xs).to(cuda_device),
                                   fields, config=cfg)
@@ -200,11 +208,13 @@ def test_linear_loaders_and_splits_match_oracle(cuda_device, m, n, k, loader, sp
     np.testing.assert_allclose(got, ref, rtol=5e-4, atol=5e-4 * np.abs(ref).max())
 
 
-@pytest.mark.parametrize("warps,stages", [(4, 3), (4, 8), (8, 6)])
-def test_linear_all_warp_stage_configs(cuda_device, warps, stages):
+@pytest.mark.parametrize("kind,warps,stages", [(_lib.MAMBO_KERNEL_GEMV_SYNC, 4, 3), (_lib.MAMBO_KERNEL_GEMV_SYNC, 16, 8),
+                                               (_lib.MAMBO_KERNEL_GEMV_SYNC, 12, 6), (_lib.MAMBO_KERNEL_GEMV, 8, 2),
+                                               (_lib.MAMBO_KERNEL_GEMV, 8, 3), (_lib.MAMBO_KERNEL_GEMV, 8, 5)])
+def test_linear_all_warp_stage_configs(cuda_device, kind, warps, stages):
     raw, _, xq, xs, ref = _linear_case(cuda_device, 8, 1024, 4096, seed=77)
     fields = gpu_weight(raw, cuda_device)
-    cfg = {"kernel": _lib.MAMBO_KERNEL_GEMV, "warps": warps, "stages": stages, "ctas_per_sm": 1, "split": 0}
+    cfg = {"kernel": kind, "warps": warps, "stages": stages, "ctas_per_sm": 1, "split": 0}
     out = launch_iq3_s_fp8_matmul(torch.from_numpy(xq).to(cuda_device), torch.from_numpy(xs).to(cuda_device),
                                   fields, config=cfg)
     assert O.relative_frobenius(to_np(out), ref) < ORACLE_FROB_TOL
