@@ -138,8 +138,8 @@ int require_sm100(DeviceInfo* info) {
 
 // --- configurations ---------------------------------------------------------
 // tcgen05 GEMV (MAMBO_KERNEL_GEMV): 128-row tiles; tuned over stages x split.
-const int kTcStages[] = {2, 3, 4, 5};
-constexpr int kNumTcConfigs = 4 * 2;
+const int kTcStages[] = {2, 3, 4};
+constexpr int kNumTcConfigs = 3 * 2;
 // mma.sync GEMV (MAMBO_KERNEL_GEMV_SYNC): warps x stages x split.
 const int kSyncWarps[] = {4, 8, 12, 16};
 const int kSyncStages[] = {3, 4, 6, 8};
