@@ -66,7 +66,7 @@ typedef struct MamboIQ3SWeight {
 /* Launch configuration of the linear kernels (NULL = tuned default for the shape). */
 typedef struct MamboLinearConfig {
   int kernel;        /* MAMBO_KERNEL_* */
-  int warps;         /* GEMV_SYNC: compute warps per CTA (16 weight rows each); GEMV: fixed 128-row tiles */
+  int warps;         /* GEMV: decoder warps (8, 12, 16); GEMV_SYNC: compute warps (16 weight rows each) */
   int stages;        /* shared-memory pipeline depth */
   int ctas_per_sm;   /* GEMV persistent grid = SMs * ctas_per_sm (0 = 1) */
   int split;         /* GEMV: 0 = stream-K over all SMs, 1 = one CTA per row tile */

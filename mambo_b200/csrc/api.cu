@@ -139,7 +139,8 @@ int require_sm100(DeviceInfo* info) {
 // --- configurations ---------------------------------------------------------
 // tcgen05 GEMV (MAMBO_KERNEL_GEMV): 128-row tiles; tuned over stages x split.
 const int kTcStages[] = {2, 3, 4};
-constexpr int kNumTcConfigs = 3 * 2;
+const int kTcDecWarps[] = {8, 12, 16};
+constexpr int kNumTcConfigs = 3 * 3 * 2;
 // mma.sync GEMV (MAMBO_KERNEL_GEMV_SYNC): warps x stages x split.
 const int kSyncWarps[] = {4, 8, 12, 16};
 const int kSyncStages[] = {3, 4, 6, 8};
@@ -161,7 +162,7 @@ void default_config(int64_t m, int64_t n, int64_t b, MamboLinearConfig* cfg, int
   (void)n;
   std::memset(cfg, 0, sizeof(*cfg));
   cfg->kernel = MAMBO_KERNEL_GEMV;
-  cfg->warps = 8;
+  cfg->warps = 12;  // decoder warps
   cfg->ctas_per_sm = 1;
   cfg->split = 0;
   // Deepest raw-stage ring (up to 4) that fits next to the codebook and the two operand slots.
@@ -178,8 +179,11 @@ int validate_config(const MamboLinearConfig* cfg, int64_t m, int64_t b, const De
     if (cfg->warps != 4 && cfg->warps != 8 && cfg->warps != 12 && cfg->warps != 16)
       return fail(MAMBO_EINVAL, "warps must be 4, 8, 12 or 16");
     if (cfg->stages < 2 || cfg->stages > 12) return fail(MAMBO_EINVAL, "stages must be in [2, 12]");
-  } else if (cfg->stages < 2 || cfg->stages > gemv_tc_max_stages()) {
-    return fail(MAMBO_EINVAL, "stages must be in [2, %d]", gemv_tc_max_stages());
+  } else {
+    if (cfg->stages < 2 || cfg->stages > gemv_tc_max_stages())
+      return fail(MAMBO_EINVAL, "stages must be in [2, %d]", gemv_tc_max_stages());
+    if (cfg->warps != 8 && cfg->warps != 12 && cfg->warps != 16)
+      return fail(MAMBO_EINVAL, "decoder warps must be 8, 12 or 16");
   }
   const uint32_t smem = config_smem(*cfg, gemv_nt_for(m), b);
   if ((int)smem > info.max_smem_optin)
@@ -341,8 +345,8 @@ int mambo_config_at(int kernel, int index, MamboLinearConfig* cfg) {
   cfg->ctas_per_sm = 1;
   cfg->split = index % 2;
   if (kernel == MAMBO_KERNEL_GEMV) {
-    cfg->warps = 8;
-    cfg->stages = kTcStages[index / 2];
+    cfg->warps = kTcDecWarps[index / 6];
+    cfg->stages = kTcStages[(index / 2) % 3];
   } else {
     cfg->warps = kSyncWarps[index / 8];
     cfg->stages = kSyncStages[(index / 2) % 4];
@@ -451,7 +455,7 @@ int mambo_iq3s_linear(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_
       p.stages = c.stages;
       p.row_tiles = P.row_tiles;
       p.total_units = P.units;
-      e = launch_gemv_tc(p, P.nt, maps, P.grid, (cudaStream_t)stream);
+      e = launch_gemv_tc(p, P.nt, c.warps, maps, P.grid, (cudaStream_t)stream);
       if (e != cudaSuccess) return cuda_fail(e, "iq3s_gemv_tc");
     } else {
       GemvParams p = mp;

@@ -4,20 +4,20 @@
 // per 32-weight group g, P_g = sum_k E4M3(x) * E4M3(+-grid) is summed by the
 // tensor core in FP32, then out += P_g * 2^e(x, g) * d * (1 + 2*nibble_g) in FP32.
 //
-// Design (one persistent CTA per SM, 14 warps):
+// Design (one persistent CTA per SM, 22 warps):
 //  * warp 0, producer: per work unit (128 weight rows x one 256-wide K block,
 //    stream-K order) five TMA tensor copies of the IQ3_S fields plus one bulk
 //    copy of the packed activation slice, into a ring of stages.
-//  * warps 2-9, decoders: expand each 4-weight IQ3_S code through a lane-private
+//  * warps 2-17, decoders: expand each 4-weight IQ3_S code through a lane-private
 //    shared-memory codebook into E4M3 bytes, written as the K-major no-swizzle
 //    UMMA operand (8 x 16-byte core matrices); copy the activation tile and
-//    scales; compute the per-row group scales d * (1 + 2*nibble).
+//    scales and the rows' d and scale nibbles.
 //  * warp 1, MMA: one thread issues 8 tcgen05.mma (M=128 rows, N=16/32 tokens,
 //    K=32 each, one per group) into TMEM, double buffered, and commits them to
 //    an mbarrier; the warp owns the TMEM allocation.
-//  * warps 10-13, epilogue: each thread owns one weight row (its TMEM lane),
-//    loads the group partials with tcgen05.ld, scales and accumulates them in
-//    FP32 registers; finished rows go to the output, or to a split-K workspace
+//  * warps 18-21, epilogue: each thread owns one weight row (its TMEM lane),
+//    loads the group partials with tcgen05.ld, scales them by the activation
+//    scale and d * (1 + 2*nibble) and accumulates them in FP32 registers; finished rows go to the output, or to a split-K workspace
 //    whose last contributor (acq_rel counter) sums them in CTA order.
 #include "kernels.cuh"
 #include "tcgen05.cuh"
@@ -28,9 +28,8 @@ namespace {
 
 constexpr int kRows = 128;  // weight rows per unit = MMA M
 constexpr int kTableBytes = 512 * 32 * 4;
-constexpr int kDecWarps = 8;
 constexpr int kEpiWarps = 4;
-constexpr int kThreads = (2 + kDecWarps + kEpiWarps) * 32;
+__host__ __device__ constexpr int tc_threads(int dec_warps) { return (2 + dec_warps + kEpiWarps) * 32; }
 constexpr int kMaxStagesTc = 6;
 
 __host__ __device__ constexpr uint32_t align_up_tc(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
@@ -57,8 +56,8 @@ __host__ __device__ inline TcLayout tc_layout(int nt) {
   L.a = 0;
   L.bt = kRows * 256;               // 32 KB decoded E4M3 tile
   L.xs = L.bt + nm * 256;
-  L.w = L.xs + 8 * nm * 4;
-  L.slot_bytes = align_up_tc(L.w + 8 * kRows * 4, 1024);
+  L.w = L.xs + 8 * nm * 4;  // per row: d (fp16 bits) in the low half, scale nibbles word next: 2 x u32
+  L.slot_bytes = align_up_tc(L.w + 2 * kRows * 4, 1024);
   return L;
 }
 
@@ -150,8 +149,8 @@ cudaError_t launch_pack_activations(const PackParams& p, int num_sms, cudaStream
 // --------------------------------------------------------------------------
 // The linear kernel
 // --------------------------------------------------------------------------
-template <int NT>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int NT, int kDecWarps>
+__global__ void __launch_bounds__(tc_threads(kDecWarps), 1)
     iq3s_gemv_tc_kernel(const __grid_constant__ GemvTcParams p, const __grid_constant__ GemvMaps maps) {
   constexpr int NM = nmma_for(NT);       // MMA N (tokens, padded to 16)
   constexpr int TOK = 8 * NT;            // tokens the epilogue keeps
@@ -288,10 +287,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (it >= 2 && !mbar_wait_bounded(B.tfree + 8 * b, ((it >> 1) & 1) ^ 1, kSiteGemvEmpty)) return;
       const uint8_t* st = raw0 + (size_t)s * L.raw_bytes;
       uint8_t* slot = slot0 + (size_t)b * L.slot_bytes;
-      float* wbuf = reinterpret_cast<float*>(slot + L.w);
-#pragma unroll 2
-      for (int i = 0; i < 8; ++i) {
-        const int combo = dw + 8 * i;  // 8-row group x 4 K chunks per warp step
+#pragma unroll
+      for (int i = 0; i < (64 + kDecWarps - 1) / kDecWarps; ++i) {
+        const int combo = dw + kDecWarps * i;  // 8-row group x 4 K chunks per warp step
+        if (64 % kDecWarps != 0 && combo >= 64) break;
         const int rg = combo >> 2, kq = combo & 3;
         const int row = rg * 8 + (lane & 7);
         const int kc = kq * 4 + (lane >> 3);  // 16-weight chunk = 4 codes
@@ -310,13 +309,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         v.z = lop3_and_or(((sg >> 8) & 0xFu) * 0x10204080u, 0x80808080u, m2);
         v.w = lop3_and_or((sg >> 12) * 0x10204080u, 0x80808080u, m3);
         *reinterpret_cast<uint4*>(slot + L.a + rg * 2048 + kc * 128 + (lane & 7) * 16) = v;
-        if ((kc & 1) == 0) {  // group kc/2 scale of this row: d * (2*nibble + 1), exact
-          const int g = kc >> 1;
-          const float dv = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(st + L.d + row * 2)));
-          const uint32_t sc = *reinterpret_cast<const uint32_t*>(st + L.scales + row * 4);
-          const uint32_t t = ((sc >> (4 * g)) & 0xFu) * 2u + 1u;
-          wbuf[g * kRows + row] = dv * (__uint_as_float(0x4B000000u | t) - 8388608.0f);
-        }
+      }
+      // Rows' d and scale nibbles for the epilogue (it forms d * (1 + 2*nibble)).
+      for (int r = tid; r < kRows; r += nthreads) {
+        reinterpret_cast<uint2*>(slot + L.w)[r] =
+            make_uint2(*reinterpret_cast<const uint16_t*>(st + L.d + r * 2),
+                       *reinterpret_cast<const uint32_t*>(st + L.scales + r * 4));
       }
       // Activation tile and scales to the operand slot.
       for (int c = tid; c < (int)(L.pack_bytes / 16); c += nthreads)
@@ -349,7 +347,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::fence_after_sync();
       const uint8_t* slot = slot0 + (size_t)b * L.slot_bytes;
       const float* xs = reinterpret_cast<const float*>(slot + L.xs);
-      const float* wbuf = reinterpret_cast<const float*>(slot + L.w);
+      const uint2 dsc = reinterpret_cast<const uint2*>(slot + L.w)[rl];
+      const float dv = __half2float(__ushort_as_half((unsigned short)dsc.x));
+      const float dneg = -8388608.0f * dv;
+      // 2*nibble+1 of group g is byte g/2 of tb[g&1]; float(2^23 + t)*d - 2^23*d = t*d exactly.
+      const uint32_t tb0 = lop3_and_or(dsc.y << 1, 0x1E1E1E1Eu, 0x01010101u);
+      const uint32_t tb1 = lop3_and_or(dsc.y >> 3, 0x1E1E1E1Eu, 0x01010101u);
 #pragma unroll
       for (int g = 0; g < 8; g += 2) {
 #pragma unroll
@@ -357,7 +360,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           float c0[8], c1[8];
           tc::ld_x8_pair(tq + (uint32_t)(b * 8 * NM + g * NM + tb), tq + (uint32_t)(b * 8 * NM + (g + 1) * NM + tb),
                          c0, c1);
-          const float w0 = wbuf[g * kRows + rl], w1 = wbuf[(g + 1) * kRows + rl];
+          const float w0 = fmaf(__uint_as_float(prmt(tb0, 0x4B000000u, 0x7650u | (uint32_t)(g >> 1))), dv, dneg);
+          const float w1 = fmaf(__uint_as_float(prmt(tb1, 0x4B000000u, 0x7650u | (uint32_t)(g >> 1))), dv, dneg);
 #pragma unroll
           for (int t = 0; t < 8; t += 2) {
             float p0, p1;
@@ -447,20 +451,31 @@ uint32_t gemv_tc_smem_bytes(int nt, int stages) { return tc_smem_bytes(nt, stage
 uint32_t gemv_tc_pack_bytes(int nt) { return tc_layout(nt).pack_bytes; }
 int gemv_tc_max_stages() { return kMaxStagesTc; }
 
-template <int NT>
+template <int NT, int kDecWarps>
 static cudaError_t launch_gemv_tc_t(const GemvTcParams& p, const GemvMaps& maps, int grid, cudaStream_t stream) {
   const uint32_t smem = tc_smem_bytes(NT, p.stages);
-  const void* kern = (const void*)iq3s_gemv_tc_kernel<NT>;
+  const void* kern = (const void*)iq3s_gemv_tc_kernel<NT, kDecWarps>;
   cudaError_t e = ensure_smem_attribute(kern, smem);
   if (e != cudaSuccess) return e;
-  return launch_pdl(kern, dim3(grid), dim3(kThreads), smem, stream, p, maps);
+  return launch_pdl(kern, dim3(grid), dim3(tc_threads(kDecWarps)), smem, stream, p, maps);
 }
 
-cudaError_t launch_gemv_tc(const GemvTcParams& p, int nt, const GemvMaps& maps, int grid, cudaStream_t stream) {
+template <int NT>
+static cudaError_t launch_gemv_tc_n(const GemvTcParams& p, int dec_warps, const GemvMaps& maps, int grid,
+                                    cudaStream_t stream) {
+  switch (dec_warps) {
+    case 8: return launch_gemv_tc_t<NT, 8>(p, maps, grid, stream);
+    case 12: return launch_gemv_tc_t<NT, 12>(p, maps, grid, stream);
+    default: return launch_gemv_tc_t<NT, 16>(p, maps, grid, stream);
+  }
+}
+
+cudaError_t launch_gemv_tc(const GemvTcParams& p, int nt, int dec_warps, const GemvMaps& maps, int grid,
+                           cudaStream_t stream) {
   switch (nt) {
-    case 1: return launch_gemv_tc_t<1>(p, maps, grid, stream);
-    case 2: return launch_gemv_tc_t<2>(p, maps, grid, stream);
-    default: return launch_gemv_tc_t<4>(p, maps, grid, stream);
+    case 1: return launch_gemv_tc_n<1>(p, dec_warps, maps, grid, stream);
+    case 2: return launch_gemv_tc_n<2>(p, dec_warps, maps, grid, stream);
+    default: return launch_gemv_tc_n<4>(p, dec_warps, maps, grid, stream);
   }
 }
 

@@ -124,7 +124,8 @@ struct GemvTcParams {
   int row_tiles;
   int total_units;
 };
-cudaError_t launch_gemv_tc(const GemvTcParams& p, int nt, const GemvMaps& maps, int grid, cudaStream_t stream);
+cudaError_t launch_gemv_tc(const GemvTcParams& p, int nt, int dec_warps, const GemvMaps& maps, int grid,
+                           cudaStream_t stream);
 uint32_t gemv_tc_smem_bytes(int nt, int stages);
 uint32_t gemv_tc_pack_bytes(int nt);
 int gemv_tc_max_stages();

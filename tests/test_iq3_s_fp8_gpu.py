@@ -186,6 +186,7 @@ def _linear_case(cuda_device, m, n, k, seed, outliers=False):
 
 KERNELS = {  # (kernel kind, weight loader)
     "tcgen05": (_lib.MAMBO_KERNEL_GEMV, 0),
+    "tcgen05_w16": (_lib.MAMBO_KERNEL_GEMV, 0, 16),
     "sync_tma": (_lib.MAMBO_KERNEL_GEMV_SYNC, 0),
     "sync_plain": (_lib.MAMBO_KERNEL_GEMV_SYNC, 1),
 }
@@ -198,9 +199,9 @@ KERNELS = {  # (kernel kind, weight loader)
 def test_linear_kernels_and_splits_match_oracle(cuda_device, m, n, k, kernel, split):
     raw, _, xq, xs, ref = _linear_case(cuda_device, m, n, k, seed=1000 + m + n)
     fields = gpu_weight(raw, cuda_device)
-    kind, loader = KERNELS[kernel]
-    cfg = {"kernel": kind, "warps": 8, "stages": 4 if m <= 16 else 3, "ctas_per_sm": 1, "split": split,
-           "loader": loader}
+    kind, loader, *warps = KERNELS[kernel]
+    cfg = {"kernel": kind, "warps": warps[0] if warps else 8, "stages": 4 if m <= 16 else 3, "ctas_per_sm": 1,
+           "split": split, "loader": loader}
     out = launch_iq3_s_fp8_matmul(torch.from_numpy(xq).to(cuda_device), torch.from_numpy(xs).to(cuda_device),
                                   fields, config=cfg)
     got = to_np(out).astype(np.float64)
@@ -210,7 +211,7 @@ def test_linear_kernels_and_splits_match_oracle(cuda_device, m, n, k, kernel, sp
 
 @pytest.mark.parametrize("kind,warps,stages", [(_lib.MAMBO_KERNEL_GEMV_SYNC, 4, 3), (_lib.MAMBO_KERNEL_GEMV_SYNC, 16, 3),
                                                (_lib.MAMBO_KERNEL_GEMV_SYNC, 12, 6), (_lib.MAMBO_KERNEL_GEMV, 8, 2),
-                                               (_lib.MAMBO_KERNEL_GEMV, 8, 3), (_lib.MAMBO_KERNEL_GEMV, 8, 4)])
+                                               (_lib.MAMBO_KERNEL_GEMV, 12, 3), (_lib.MAMBO_KERNEL_GEMV, 16, 4)])
 def test_linear_all_warp_stage_configs(cuda_device, kind, warps, stages):
     raw, _, xq, xs, ref = _linear_case(cuda_device, 8, 1024, 4096, seed=77)
     fields = gpu_weight(raw, cuda_device)
