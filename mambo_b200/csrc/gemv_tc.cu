@@ -287,8 +287,12 @@ __global__ void __launch_bounds__(tc_threads(kDecWarps), 1)
       if (it >= 2 && !mbar_wait_bounded(B.tfree + 8 * b, ((it >> 1) & 1) ^ 1, kSiteGemvEmpty)) return;
       const uint8_t* st = raw0 + (size_t)s * L.raw_bytes;
       uint8_t* slot = slot0 + (size_t)b * L.slot_bytes;
+      // All gathers first, then all stores: a store may alias later loads as
+      // far as the compiler knows, so interleaving them would serialize the tasks.
+      constexpr int kTasks = (64 + kDecWarps - 1) / kDecWarps;
+      uint4 v[kTasks];
 #pragma unroll
-      for (int i = 0; i < (64 + kDecWarps - 1) / kDecWarps; ++i) {
+      for (int i = 0; i < kTasks; ++i) {
         const int combo = dw + kDecWarps * i;  // 8-row group x 4 K chunks per warp step
         if (64 % kDecWarps != 0 && combo >= 64) break;
         const int rg = combo >> 2, kq = combo & 3;
@@ -303,12 +307,17 @@ __global__ void __launch_bounds__(tc_threads(kDecWarps), 1)
         const uint32_t m1 = *reinterpret_cast<const uint32_t*>(table + prmt(q, e0, 0x6615u));
         const uint32_t m2 = *reinterpret_cast<const uint32_t*>(table + prmt(q, e1, 0x6624u));
         const uint32_t m3 = *reinterpret_cast<const uint32_t*>(table + prmt(q, e1, 0x6635u));
-        uint4 v;
-        v.x = lop3_and_or((sg & 0xFu) * 0x10204080u, 0x80808080u, m0);
-        v.y = lop3_and_or(((sg >> 4) & 0xFu) * 0x10204080u, 0x80808080u, m1);
-        v.z = lop3_and_or(((sg >> 8) & 0xFu) * 0x10204080u, 0x80808080u, m2);
-        v.w = lop3_and_or((sg >> 12) * 0x10204080u, 0x80808080u, m3);
-        *reinterpret_cast<uint4*>(slot + L.a + rg * 2048 + kc * 128 + (lane & 7) * 16) = v;
+        v[i].x = lop3_and_or((sg & 0xFu) * 0x10204080u, 0x80808080u, m0);
+        v[i].y = lop3_and_or(((sg >> 4) & 0xFu) * 0x10204080u, 0x80808080u, m1);
+        v[i].z = lop3_and_or(((sg >> 8) & 0xFu) * 0x10204080u, 0x80808080u, m2);
+        v[i].w = lop3_and_or((sg >> 12) * 0x10204080u, 0x80808080u, m3);
+      }
+#pragma unroll
+      for (int i = 0; i < kTasks; ++i) {
+        const int combo = dw + kDecWarps * i;
+        if (64 % kDecWarps != 0 && combo >= 64) break;
+        const int rg = combo >> 2, kc = (combo & 3) * 4 + (lane >> 3);
+        *reinterpret_cast<uint4*>(slot + L.a + rg * 2048 + kc * 128 + (lane & 7) * 16) = v[i];
       }
       // Rows' d and scale nibbles for the epilogue (it forms d * (1 + 2*nibble)).
       for (int r = tid; r < kRows; r += nthreads) {
