@@ -157,11 +157,14 @@ __global__ void __launch_bounds__(tc_threads(kDecWarps), 1)
   constexpr uint32_t kIdesc = tc::idesc_e4m3_f32(kRows, NM);
   constexpr uint32_t kTmemCols = 2 * 8 * NM;  // two buffers of 8 group partials
 
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
   const TcLayout L = tc_layout(NT);
-  uint8_t* table = smem;
-  uint8_t* raw0 = smem + kTableBytes;
+  // The codebook sits at the start of dynamic shared memory (a link-time
+  // constant address, so lookups need no base register); the TMA stages
+  // after it are aligned to 1024 bytes at run time.
+  uint8_t* table = smem_raw;
+  uint8_t* raw0 = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw + kTableBytes) + 1023) &
+                                             ~uintptr_t(1023));
   uint8_t* slot0 = raw0 + (size_t)p.stages * L.raw_bytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(slot0 + 2 * L.slot_bytes);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kMaxStagesTc + 7);
@@ -281,6 +284,19 @@ __global__ void __launch_bounds__(tc_threads(kDecWarps), 1)
     asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
 
     const uint32_t lane2x = (uint32_t)(lane << 2) * 0x0101u;
+    // Task i of this thread: weight row row0 + kRowStep*i, 16-weight chunk kc
+    // (kDecWarps is a multiple of 4, so the chunk and every swizzle term are
+    // the same for all i and each address is a base plus a constant).
+    constexpr int kTasks = (64 + kDecWarps - 1) / kDecWarps;
+    constexpr int kRowStep = 8 * (kDecWarps / 4);
+    static_assert(kDecWarps % 4 == 0, "decoder warps must be a multiple of 4");
+    const int row0 = (dw >> 2) * 8 + (lane & 7);
+    const int kc = (dw & 3) * 4 + (lane >> 3);
+    const uint32_t qs_base = L.qs + qs_off_tc(row0, 4 * kc);
+    const uint32_t qh_base = L.qh + row0 * 8 + (kc >> 1);
+    const uint32_t sg_base = L.signs + signs_off_tc(row0, 2 * kc);
+    const uint32_t a_base = L.a + (row0 >> 3) * 2048 + kc * 128 + (row0 & 7) * 16;
+    const uint32_t h_shift = (kc & 1) * 4;
     for (int it = 0, u = u0; u < u1; ++u, ++it) {
       const int s = it % p.stages, b = it & 1;
       if (!mbar_wait_bounded(B.full + 8 * s, (it / p.stages) & 1, kSiteGemvFull)) return;
@@ -289,18 +305,13 @@ __global__ void __launch_bounds__(tc_threads(kDecWarps), 1)
       uint8_t* slot = slot0 + (size_t)b * L.slot_bytes;
       // All gathers first, then all stores: a store may alias later loads as
       // far as the compiler knows, so interleaving them would serialize the tasks.
-      constexpr int kTasks = (64 + kDecWarps - 1) / kDecWarps;
       uint4 v[kTasks];
 #pragma unroll
       for (int i = 0; i < kTasks; ++i) {
-        const int combo = dw + kDecWarps * i;  // 8-row group x 4 K chunks per warp step
-        if (64 % kDecWarps != 0 && combo >= 64) break;
-        const int rg = combo >> 2, kq = combo & 3;
-        const int row = rg * 8 + (lane & 7);
-        const int kc = kq * 4 + (lane >> 3);  // 16-weight chunk = 4 codes
-        const uint32_t q = *reinterpret_cast<const uint32_t*>(st + L.qs + qs_off_tc(row, 4 * kc));
-        const uint32_t hn = (st[L.qh + row * 8 + (kc >> 1)] >> ((kc & 1) * 4)) & 0xFu;
-        const uint32_t sg = *reinterpret_cast<const uint16_t*>(st + L.signs + signs_off_tc(row, 2 * kc));
+        if (64 % kDecWarps != 0 && dw + kDecWarps * i >= 64) break;
+        const uint32_t q = *reinterpret_cast<const uint32_t*>(st + qs_base + i * (kRowStep * 64));
+        const uint32_t hn = (st[qh_base + i * (kRowStep * 8)] >> h_shift) & 0xFu;
+        const uint32_t sg = *reinterpret_cast<const uint16_t*>(st + sg_base + i * (kRowStep * 32));
         const uint32_t e0 = lop3_and_or((hn & 3u) * 0x4080u, 0x8080u, lane2x);
         const uint32_t e1 = lop3_and_or((hn >> 2) * 0x4080u, 0x8080u, lane2x);
         const uint32_t m0 = *reinterpret_cast<const uint32_t*>(table + prmt(q, e0, 0x6604u));
@@ -314,10 +325,8 @@ __global__ void __launch_bounds__(tc_threads(kDecWarps), 1)
       }
 #pragma unroll
       for (int i = 0; i < kTasks; ++i) {
-        const int combo = dw + kDecWarps * i;
-        if (64 % kDecWarps != 0 && combo >= 64) break;
-        const int rg = combo >> 2, kc = (combo & 3) * 4 + (lane >> 3);
-        *reinterpret_cast<uint4*>(slot + L.a + rg * 2048 + kc * 128 + (lane & 7) * 16) = v[i];
+        if (64 % kDecWarps != 0 && dw + kDecWarps * i >= 64) break;
+        *reinterpret_cast<uint4*>(slot + a_base + i * (kRowStep / 8) * 2048) = v[i];
       }
       // Rows' d and scale nibbles for the epilogue (it forms d * (1 + 2*nibble)).
       for (int r = tid; r < kRows; r += nthreads) {
