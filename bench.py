@@ -60,6 +60,20 @@ def load_peaks() -> tuple[float, str]:
     return HBM_FALLBACK_GBS, "fallback"
 
 
+def read_profiled_traffic():
+    """DRAM bytes per GEMV launch from the committed ncu summary (a line 'dram_bytes_per_launch: N')."""
+    path = ROOT / "profiles" / "iq3s_gemv_decode_llama3_8b.md"
+    if not path.is_file():
+        return None
+    for line in path.read_text().splitlines():
+        if line.strip().startswith("dram_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].split()[0])
+            except (ValueError, IndexError):
+                return None
+    return None
+
+
 def layer_bytes() -> int:
     return sum(n * (k // 256) * 110 for _, n, k in PROJECTIONS)
 
@@ -206,6 +220,32 @@ def build_workload(torch, dev):
     return layers, inputs
 
 
+def run_single(args) -> None:
+    """Four linear launches of one shape (for ncu captures of a single kernel)."""
+    import torch
+
+    from mambo_b200.kernels.iq3_s_fp8 import linear_into, select_config
+    from mambo_b200.kernels.quantize_fp8 import launch_quantize_fp8
+    from mambo_b200.utils.iq3_s_weight import prepare_iq3_s_fields
+
+    n, k, m = (int(v) for v in args.single.split(","))
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev).manual_seed(1)
+    raw = torch.randint(0, 256, (n, k // 256, 110), dtype=torch.uint8, device=dev, generator=gen)
+    d = (torch.rand((n, k // 256), device=dev, generator=gen) * 9e-3 + 1e-3).half()
+    raw[..., :2] = d.view(torch.uint8).view(n, k // 256, 2)
+    fields = prepare_iq3_s_fields(raw)
+    xq, xs = launch_quantize_fp8(torch.randn((m, k), device=dev, generator=gen).to(torch.bfloat16))
+    out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+    cfg = dict(select_config(m, n, k, dev))
+    if args.kernel is not None:
+        cfg["kernel"] = args.kernel
+    for _ in range(4):
+        linear_into(xq, xs, fields, out, config=cfg)
+    torch.cuda.synchronize()
+    print(f"single N={n} K={k} M={m} config={cfg}: ok")
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -213,8 +253,14 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("mambo", "reference"), default="mambo")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--single", metavar="N,K,M",
+                    help="profiling mode: run four linears of one shape (random IQ3_S weights) and exit")
+    ap.add_argument("--kernel", type=int, default=None, help="with --single: MAMBO_KERNEL_* to use")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
+    if args.single:
+        run_single(args)
+        return
 
     if args.impl == "reference":
         run_reference(args)
@@ -316,19 +362,13 @@ def main() -> None:
             torch.cuda.synchronize(dev)
             us = e0.elapsed_time(e1) * 1000 / reps
             b = n * (k // 256) * 110 + m * k + m * k // 32 + m * n * 2
-            per_launch.append({"m": m, "proj": p, "us": us, "bytes": b, "gbs": b / us / 1e3})
+            per_launch.append({"m": m, "proj": p, "us": round(us, 3), "bytes": b, "gbs": round(b / us / 1e3, 1)})
             del g
     peak, peak_kind = load_peaks()
     tot_b = sum(r["bytes"] for r in per_launch)
     tot_us = sum(r["us"] for r in per_launch)
     achieved = tot_b / tot_us / 1e3
-    traffic = None
-    tpath = ROOT / "profiles" / "gemv_decode_traffic.json"
-    if tpath.is_file():
-        try:
-            traffic = json.loads(tpath.read_text()).get("dram_bytes_per_launch")
-        except ValueError:
-            traffic = None
+    traffic = read_profiled_traffic()
 
     # ---- e2e: public API with pinned host buffers, H2D + D2H in the region --
     from mambo_b200.kernels.iq3_s_fp8 import iq3_s_fp8_linear
@@ -404,13 +444,15 @@ def main() -> None:
                    "l2": "inputs larger than L2 (375 MB of weights per step)", "execution": "cuda graph replay",
                    "parallelism": f"replicas{world}"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": traffic, "peak_kind": peak_kind, "kernel": "iq3s_gemv_kernel",
+                     "traffic": traffic, "peak_kind": peak_kind,
+                     "kernel": "iq3s_gemv_tc_kernel (per launch: activation pack + GEMV, CUDA-graph replay)",
                      "per_launch": per_launch},
         "e2e": {"value": alg * world / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
                 "h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": out_bytes,
                 "ms_per_step": e2e_ms, "execution": "cuda graph of public-API calls incl. H2D/D2H",
                 "eager_ms_per_step": eager_ms, "matches_device_path": ok},
-        "gpu_launches": args.steps * len(M_SWEEP) * len(PROJECTIONS) * 2,
+        # per linear: MXFP8 quantization, activation packing, IQ3_S GEMV
+        "gpu_launches": args.steps * len(M_SWEEP) * len(PROJECTIONS) * 3,
         "clocks": clock,
         "cpu_baseline": cpu,
     }
