@@ -136,6 +136,48 @@ MAMBO_API int mambo_iq3s_linear(const uint8_t* xq, int64_t ldxq, const uint8_t* 
 /* Workspace bytes mambo_iq3s_linear needs for this shape and configuration. */
 MAMBO_API size_t mambo_iq3s_linear_workspace_bytes(int64_t m, int64_t n_rows, int64_t n_blocks, const MamboLinearConfig* cfg);
 
+/* Size of the library-held scratch of mambo_iq3s_linear_noalloc (3 MiB per GPU). */
+#define MAMBO_STATIC_SCRATCH_BYTES (3u * 1024u * 1024u)
+
+/*
+ * mambo_iq3s_linear for callers that cannot allocate device memory. It has no
+ * counterpart in the reference, whose Python wrappers allocate freely.
+ *
+ * Who needs it: a plugin loaded into a host whose memory pool owns the device
+ * memory (a serving engine that reserves nearly all HBM up front for its KV
+ * cache, so a private cudaMalloc fails or eats into that reserve), and code that
+ * has no handle to the host's allocator. Such callers cannot provide the
+ * workspace that mambo_iq3s_linear takes.
+ *
+ * What it does instead: the split-K counters, FP32 partials and packed
+ * activations live in a file-scope static device array of
+ * MAMBO_STATIC_SCRATCH_BYTES. Every GPU on which the library's kernels are
+ * loaded holds that array until the process exits. Nothing is allocated:
+ * no cudaMalloc, no cudaFree, no allocating library routine.
+ *
+ * Arguments and results: the same as mambo_iq3s_linear without the workspace.
+ * It runs the tcgen05 GEMV only (cfg NULL or kernel MAMBO_KERNEL_GEMV or AUTO;
+ * N % 8 == 0; 16-byte aligned weight fields) and processes M in chunks of
+ * 8 tokens.
+ *
+ * Limits: N <= 524288 and K <= 98304 (K/256 <= 384). Larger shapes return
+ * MAMBO_EINVAL, and mambo_last_error names the limit.
+ *
+ * Set-up: the first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress, with that device current). Make that first call
+ * before any stream capture.
+ *
+ * Zeroing: each call clears the split-K counters it uses, with
+ * cudaMemsetAsync on `stream`, before launching its kernels.
+ *
+ * Concurrency: all calls on one device share the array. Calls that overlap on
+ * the GPU (different streams, or graphs replayed concurrently) race and give
+ * wrong results; order them on one stream.
+ */
+MAMBO_API int mambo_iq3s_linear_noalloc(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t ldxs, int64_t m,
+                              const MamboIQ3SWeight* w, const uint32_t* fp8_table, void* out, int out_dtype,
+                              int64_t ldo, const MamboLinearConfig* cfg, mambo_stream_t stream);
+
 /* Number of tunable configurations of a kernel kind, and the i-th one (for the autotuner).
  * Replaces the search spaces of make_benchmark_cases (src/python/mambo/kernels/iq3_s_fp8.py:402-465). */
 MAMBO_API int mambo_num_configs(int kernel);

@@ -42,6 +42,7 @@ EXPORTED_SYMBOLS = (
     "mambo_quantize_mxfp8",
     "mambo_iq3s_linear",
     "mambo_iq3s_linear_workspace_bytes",
+    "mambo_iq3s_linear_noalloc",
     "mambo_num_configs",
     "mambo_config_at",
     "mambo_default_config",
@@ -129,6 +130,11 @@ def load() -> ctypes.CDLL:
                 i32,
             ),
             "mambo_iq3s_linear_workspace_bytes": ([i64, i64, i64, ctypes.POINTER(MamboLinearConfig)], ctypes.c_size_t),
+            "mambo_iq3s_linear_noalloc": (
+                [vp, i64, vp, i64, i64, ctypes.POINTER(MamboIQ3SWeight), vp, vp, i32, i64,
+                 ctypes.POINTER(MamboLinearConfig), vp],
+                i32,
+            ),
             "mambo_num_configs": ([i32], i32),
             "mambo_config_at": ([i32, i32, ctypes.POINTER(MamboLinearConfig)], i32),
             "mambo_default_config": ([i64, i64, i64, ctypes.POINTER(MamboLinearConfig)], i32),

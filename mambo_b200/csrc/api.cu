@@ -482,3 +482,147 @@ int mambo_iq3s_linear(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_
 }
 
 }  // extern "C"
+
+// --------------------------------------------------------------------------
+// mambo_iq3s_linear_noalloc: the tcgen05 GEMV with library-held scratch, for
+// callers that cannot allocate device memory (see include/mambo_b200.h).
+// --------------------------------------------------------------------------
+
+// Every GPU on which this module is loaded holds this array until the process
+// exits. Layout: split-K counters | FP32 partials | packed activations.
+static __device__ __align__(256) uint8_t g_linear_scratch[MAMBO_STATIC_SCRATCH_BYTES];
+
+namespace {
+
+constexpr size_t kStaticCounterBytes = 64 * 1024;  // 4 counters per 128-row tile: N <= 524288
+constexpr int kStaticMaxCtas = 160;                // persistent grid cap (B200: 148 SMs)
+constexpr int64_t kStaticChunk = 8;                // tokens per launch (one 8-token tile)
+constexpr size_t kStaticPartialBytes = (size_t)kStaticMaxCtas * 2 * 128 * 8 * sizeof(float);
+constexpr size_t kStaticPackOffset = kStaticCounterBytes + kStaticPartialBytes;
+static_assert(kStaticPackOffset % 256 == 0, "scratch regions must stay 256-byte aligned");
+static_assert(kStaticPackOffset < MAMBO_STATIC_SCRATCH_BYTES, "static scratch too small");
+constexpr size_t kStaticPackBytes = MAMBO_STATIC_SCRATCH_BYTES - kStaticPackOffset;
+
+// Device address of g_linear_scratch on the current device, looked up once per
+// device (with that device current) and cached.
+int static_scratch_address(uint8_t** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(MAMBO_ENOTSUPPORTED, "device ordinal %d out of range", dev);
+  static std::mutex mu;
+  static void* addr[64] = {nullptr};
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_linear_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(static scratch)");
+    if (!p || (uintptr_t)p % 256) return fail(MAMBO_ECUDA, "static scratch is not 256-byte aligned");
+    addr[dev] = p;
+  }
+  *out = (uint8_t*)addr[dev];
+  return MAMBO_OK;
+}
+
+}  // namespace
+
+extern "C" int mambo_iq3s_linear_noalloc(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t ldxs, int64_t m,
+                                         const MamboIQ3SWeight* w, const uint32_t* fp8_table, void* out,
+                                         int out_dtype, int64_t ldo, const MamboLinearConfig* cfg,
+                                         mambo_stream_t stream) {
+  if (!xq || !xs || !w || !fp8_table || !out) return fail(MAMBO_EINVAL, "null pointer");
+  if (!w->d || !w->qs || !w->qh || !w->signs || !w->scales) return fail(MAMBO_EINVAL, "null weight field");
+  if (w->n_rows < 1 || w->n_blocks < 1) return fail(MAMBO_EINVAL, "IQ3_S weight must have positive N and K");
+  const int64_t k = w->n_blocks * 256;
+  if (m < 1) return fail(MAMBO_EINVAL, "x_values must be uint8 [M,K] with M >= 1");
+  if (ldxq < k) return fail(MAMBO_EINVAL, "x_values row stride %lld is smaller than K=%lld", (long long)ldxq,
+                            (long long)k);
+  if (ldxs < k / 32) return fail(MAMBO_EINVAL, "x_scales row stride is smaller than K/32");
+  if (out_dtype != MAMBO_F32 && out_dtype != MAMBO_BF16) return fail(MAMBO_EINVAL, "out must be f32 or bf16");
+  if (ldo < w->n_rows) return fail(MAMBO_EINVAL, "out row stride is smaller than N");
+  if (w->n_rows % 8 != 0) return fail(MAMBO_EINVAL, "mambo_iq3s_linear_noalloc needs N %% 8 == 0");
+  DeviceInfo info;
+  int st = require_sm100(&info);
+  if (st != MAMBO_OK) return st;
+  const int64_t m_chunk = m < kStaticChunk ? m : kStaticChunk;
+  MamboLinearConfig c;
+  if (cfg) c = *cfg; else default_config(m_chunk, w->n_rows, w->n_blocks, &c, info.max_smem_optin);
+  if (c.kernel == MAMBO_KERNEL_AUTO) c.kernel = MAMBO_KERNEL_GEMV;
+  if (c.kernel != MAMBO_KERNEL_GEMV || c.loader != 0)
+    return fail(MAMBO_EINVAL, "mambo_iq3s_linear_noalloc runs the tcgen05 GEMV (MAMBO_KERNEL_GEMV, loader 0) only");
+  st = validate_config(&c, m_chunk, w->n_blocks, info);
+  if (st != MAMBO_OK) return st;
+
+  const int sms = info.sms < kStaticMaxCtas ? info.sms : kStaticMaxCtas;
+  const GemvPlan P = plan_gemv(m_chunk, w->n_rows, w->n_blocks, c, sms);
+  const size_t counter_bytes = (size_t)P.counter_slots * sizeof(int);
+  if (counter_bytes > kStaticCounterBytes)
+    return fail(MAMBO_EINVAL, "N=%lld exceeds the static-scratch limit of mambo_iq3s_linear_noalloc (N <= %zu)",
+                (long long)w->n_rows, kStaticCounterBytes / sizeof(int) / 4 * 128);
+  if (P.pack_bytes > kStaticPackBytes)
+    return fail(MAMBO_EINVAL, "K=%lld exceeds the static-scratch limit of mambo_iq3s_linear_noalloc (K <= %zu)",
+                (long long)k, kStaticPackBytes / gemv_tc_pack_bytes(P.nt) * 256);
+  if (P.partial_bytes > kStaticPartialBytes)
+    return fail(MAMBO_EINVAL, "grid of %d CTAs exceeds the static scratch", P.grid);
+
+  uint8_t* scratch = nullptr;
+  st = static_scratch_address(&scratch);
+  if (st != MAMBO_OK) return st;
+  int* counters = (int*)scratch;
+  float* partials = (float*)(scratch + kStaticCounterBytes);
+  uint8_t* pack = scratch + kStaticPackOffset;
+
+  GemvParams mp{};
+  mp.n_rows = (int)w->n_rows;
+  mp.n_blocks = (int)w->n_blocks;
+  mp.d = (const uint8_t*)w->d;
+  mp.qs = (const uint8_t*)w->qs;
+  mp.qh = (const uint8_t*)w->qh;
+  mp.signs = (const uint8_t*)w->signs;
+  mp.scales = (const uint8_t*)w->scales;
+  mp.warps = 8;  // 128-row tensor-map boxes
+  GemvMaps maps;
+  std::memset(&maps, 0, sizeof(maps));
+  if (!make_gemv_maps(mp, &maps))
+    return fail(MAMBO_EINVAL, "the tcgen05 GEMV needs 16-byte aligned weight fields");
+
+  // The counters must start at zero; a call that gave up on a bounded wait may
+  // have left some behind, so every call clears the ones it uses.
+  cudaError_t e = cudaMemsetAsync(counters, 0, counter_bytes, (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(static scratch counters)");
+
+  const size_t esz = out_dtype == MAMBO_BF16 ? 2 : 4;
+  for (int64_t m0 = 0; m0 < m; m0 += kStaticChunk) {
+    const int64_t mc = (m - m0) < kStaticChunk ? (m - m0) : kStaticChunk;
+    PackParams pk{};
+    pk.xq = xq + m0 * ldxq;
+    pk.ldxq = ldxq;
+    pk.xs = xs + m0 * ldxs;
+    pk.ldxs = ldxs;
+    pk.m = (int)mc;
+    pk.n_blocks = (int)w->n_blocks;
+    pk.nmma = 16;
+    pk.pack_bytes = (int)gemv_tc_pack_bytes(P.nt);
+    pk.x_vec = ((uintptr_t)pk.xq % 16 == 0) && (ldxq % 16 == 0);
+    pk.pack = pack;
+    e = launch_pack_activations(pk, info.sms, (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(e, "pack_activations");
+    GemvTcParams p{};
+    p.xpack = pack;
+    p.m = (int)mc;
+    p.n_rows = (int)w->n_rows;
+    p.n_blocks = (int)w->n_blocks;
+    p.table = fp8_table;
+    p.out = (uint8_t*)out + m0 * ldo * esz;
+    p.out_bf16 = out_dtype == MAMBO_BF16;
+    p.ldo = ldo;
+    p.partials = partials;
+    p.counters = counters;
+    p.stages = c.stages;
+    p.row_tiles = P.row_tiles;
+    p.total_units = P.units;
+    e = launch_gemv_tc(p, P.nt, c.warps, maps, P.grid, (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(e, "iq3s_gemv_tc (static scratch)");
+  }
+  return ok();
+}
