@@ -445,14 +445,14 @@ def main() -> None:
                    "parallelism": f"replicas{world}"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": traffic, "peak_kind": peak_kind,
-                     "kernel": "iq3s_gemv_tc_kernel (per launch: activation pack + GEMV, CUDA-graph replay)",
+                     "kernel": "iq3s_gemv_tm_kernel (one launch per linear, CUDA-graph replay)",
                      "per_launch": per_launch},
         "e2e": {"value": alg * world / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
                 "h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": out_bytes,
                 "ms_per_step": e2e_ms, "execution": "cuda graph of public-API calls incl. H2D/D2H",
                 "eager_ms_per_step": eager_ms, "matches_device_path": ok},
-        # per linear: MXFP8 quantization, activation packing, IQ3_S GEMV
-        "gpu_launches": args.steps * len(M_SWEEP) * len(PROJECTIONS) * 3,
+        # per linear: MXFP8 quantization, IQ3_S GEMV
+        "gpu_launches": args.steps * len(M_SWEEP) * len(PROJECTIONS) * 2,
         "clocks": clock,
         "cpu_baseline": cpu,
     }

@@ -66,12 +66,13 @@ typedef struct MamboIQ3SWeight {
 /* Launch configuration of the linear kernels (NULL = tuned default for the shape). */
 typedef struct MamboLinearConfig {
   int kernel;        /* MAMBO_KERNEL_* */
-  int warps;         /* GEMV: decoder warps (8, 12, 16); GEMV_SYNC: compute warps (16 weight rows each) */
+  int warps;         /* GEMV: decoder warps (8, 16); GEMV_SYNC: compute warps (16 weight rows each) */
   int stages;        /* shared-memory pipeline depth */
-  int ctas_per_sm;   /* GEMV persistent grid = SMs * ctas_per_sm (0 = 1) */
-  int split;         /* GEMV: 0 = stream-K over all SMs, 1 = one CTA per row tile */
-  int loader;        /* GEMV weight staging: 0 = TMA when the layout allows it, 1 = plain loads */
-  int reserved[2];
+  int ctas_per_sm;   /* GEMV_SYNC: persistent grid = SMs * ctas_per_sm (0 = 1); GEMV: 0 or 1 */
+  int split;         /* 0 = stream-K over all SMs, 1 = one CTA per row tile */
+  int loader;        /* GEMV_SYNC weight staging: 0 = TMA when the layout allows it, 1 = plain loads */
+  int prefetch;      /* GEMV: work units whose weights are prefetched into L2 beyond the stage ring */
+  int reserved;
 } MamboLinearConfig;
 
 /* Kernel kinds: GEMV = weight-streaming decode kernel on tcgen05 tensor cores

@@ -72,10 +72,11 @@ class MamboLinearConfig(ctypes.Structure):
         ("ctas_per_sm", ctypes.c_int),
         ("split", ctypes.c_int),
         ("loader", ctypes.c_int),
-        ("reserved", ctypes.c_int * 2),
+        ("prefetch", ctypes.c_int),
+        ("reserved", ctypes.c_int),
     ]
 
-    FIELDS = ("kernel", "warps", "stages", "ctas_per_sm", "split", "loader")
+    FIELDS = ("kernel", "warps", "stages", "ctas_per_sm", "split", "loader", "prefetch")
 
     def to_dict(self) -> dict:
         return {name: int(getattr(self, name)) for name in self.FIELDS}

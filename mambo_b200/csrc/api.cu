@@ -100,6 +100,7 @@ struct DeviceInfo {
   int sms = 0;
   int major = 0, minor = 0;
   int max_smem_optin = 0;
+  int smem_per_sm = 0;
 };
 
 DeviceInfo device_info(int* status) {
@@ -119,6 +120,7 @@ DeviceInfo device_info(int* status) {
     cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev);
     cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev);
     cudaDeviceGetAttribute(&d.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaDeviceGetAttribute(&d.smem_per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
     cache[dev] = d;
     have[dev] = true;
   }
@@ -137,10 +139,15 @@ int require_sm100(DeviceInfo* info) {
 }
 
 // --- configurations ---------------------------------------------------------
-// tcgen05 GEMV (MAMBO_KERNEL_GEMV): 128-row tiles; tuned over stages x split.
-const int kTcStages[] = {2, 3, 4};
-const int kTcDecWarps[] = {8, 12, 16};
-constexpr int kNumTcConfigs = 3 * 3 * 2;
+// tcgen05 GEMV (MAMBO_KERNEL_GEMV): {decoder warps, stages, prefetch}, each with split 0 and 1.
+struct TcChoice {
+  int warps, stages, prefetch;
+};
+const TcChoice kTcChoices[] = {
+    {8, 3, 0}, {8, 4, 0}, {8, 4, 4}, {8, 6, 0}, {8, 6, 4}, {8, 8, 4},
+    {16, 3, 0}, {16, 4, 0}, {16, 4, 4}, {16, 6, 0}, {16, 6, 4}, {16, 8, 4},
+};
+constexpr int kNumTcConfigs = 2 * (int)(sizeof(kTcChoices) / sizeof(kTcChoices[0]));
 // mma.sync GEMV (MAMBO_KERNEL_GEMV_SYNC): warps x stages x split.
 const int kSyncWarps[] = {4, 8, 12, 16};
 const int kSyncStages[] = {3, 4, 6, 8};
@@ -155,19 +162,20 @@ int kernel_of(const MamboLinearConfig& c) { return c.kernel == MAMBO_KERNEL_AUTO
 
 uint32_t config_smem(const MamboLinearConfig& c, int nt, int64_t b) {
   if (kernel_of(c) == MAMBO_KERNEL_GEMV_SYNC) return gemv_smem_bytes_host(c.warps * 16, nt, c.stages, (int)b);
-  return gemv_tc_smem_bytes(nt, c.stages);
+  return gemv_tm_smem_bytes(nt, c.stages);
 }
 
 void default_config(int64_t m, int64_t n, int64_t b, MamboLinearConfig* cfg, int smem_optin) {
   (void)n;
   std::memset(cfg, 0, sizeof(*cfg));
   cfg->kernel = MAMBO_KERNEL_GEMV;
-  cfg->warps = 8;  // decoder warps (measured best for M <= 8)
+  cfg->warps = 8;
   cfg->ctas_per_sm = 1;
   cfg->split = 0;
-  // Deepest raw-stage ring (up to 4) that fits next to the codebook and the two operand slots.
+  cfg->prefetch = 4;
+  // Deepest stage ring (up to 6) that fits next to the codebook.
   const int nt = gemv_nt_for(m < 32 ? m : 32);
-  cfg->stages = 4;
+  cfg->stages = 6;
   while (cfg->stages > 2 && (int)config_smem(*cfg, nt, b) > smem_optin) --cfg->stages;
 }
 
@@ -180,10 +188,11 @@ int validate_config(const MamboLinearConfig* cfg, int64_t m, int64_t b, const De
       return fail(MAMBO_EINVAL, "warps must be 4, 8, 12 or 16");
     if (cfg->stages < 2 || cfg->stages > 12) return fail(MAMBO_EINVAL, "stages must be in [2, 12]");
   } else {
-    if (cfg->stages < 2 || cfg->stages > gemv_tc_max_stages())
-      return fail(MAMBO_EINVAL, "stages must be in [2, %d]", gemv_tc_max_stages());
-    if (cfg->warps != 8 && cfg->warps != 12 && cfg->warps != 16)
-      return fail(MAMBO_EINVAL, "decoder warps must be 8, 12 or 16");
+    if (cfg->stages < 2 || cfg->stages > gemv_tm_max_stages())
+      return fail(MAMBO_EINVAL, "stages must be in [2, %d]", gemv_tm_max_stages());
+    if (cfg->warps != 8 && cfg->warps != 16) return fail(MAMBO_EINVAL, "decoder warps must be 8 or 16");
+    if (cfg->ctas_per_sm < 0 || cfg->ctas_per_sm > 1) return fail(MAMBO_EINVAL, "ctas_per_sm must be 0 or 1");
+    if (cfg->prefetch < 0 || cfg->prefetch > 64) return fail(MAMBO_EINVAL, "prefetch must be in [0, 64]");
   }
   const uint32_t smem = config_smem(*cfg, gemv_nt_for(m), b);
   if ((int)smem > info.max_smem_optin)
@@ -199,8 +208,12 @@ constexpr size_t kCounterBytes = 256 * 1024;
 
 struct GemvPlan {
   int nt, rows, row_tiles, units, grid, counter_slots;
-  size_t counters_bytes, partial_bytes, pack_bytes;
+  size_t counters_bytes, partial_bytes, xcopy_bytes, xscopy_bytes;
 };
+
+size_t align256(size_t v) { return (v + 255) / 256 * 256; }
+// Row stride of activation scales copied for the TMA (a multiple of 16 bytes).
+int64_t xs_copy_stride(int64_t n_blocks) { return (n_blocks * 8 + 15) / 16 * 16; }
 
 GemvPlan plan_gemv(int64_t m_chunk, int64_t n, int64_t b, const MamboLinearConfig& cfg, int sms) {
   GemvPlan P{};
@@ -209,15 +222,73 @@ GemvPlan plan_gemv(int64_t m_chunk, int64_t n, int64_t b, const MamboLinearConfi
   P.rows = tc ? 128 : cfg.warps * 16;
   P.row_tiles = (int)((n + P.rows - 1) / P.rows);
   P.units = (int)(P.row_tiles * b);
-  int ctas = sms * (cfg.ctas_per_sm > 0 ? cfg.ctas_per_sm : 1);
+  int ctas = sms * (!tc && cfg.ctas_per_sm > 0 ? cfg.ctas_per_sm : 1);
   if (cfg.split == 1) ctas = P.row_tiles;  // one CTA per row tile, no split-K
   P.grid = P.units < ctas ? P.units : ctas;
   if (P.grid < 1) P.grid = 1;
   P.counter_slots = P.row_tiles * (tc ? 4 : cfg.warps);
   P.counters_bytes = kCounterBytes;
-  P.partial_bytes = (size_t)P.grid * 2 * P.rows * 8 * P.nt * sizeof(float);
-  P.pack_bytes = tc ? (size_t)b * gemv_tc_pack_bytes(P.nt) : 0;
+  P.partial_bytes = align256((size_t)P.grid * 2 * P.rows * 8 * P.nt * sizeof(float));
+  // Activations whose rows are not 16-byte aligned are copied here for the TMA.
+  P.xcopy_bytes = tc ? align256((size_t)m_chunk * b * 256) : 0;
+  P.xscopy_bytes = tc ? align256((size_t)m_chunk * xs_copy_stride(b)) : 0;
   return P;
+}
+
+// Launches the tcgen05 GEMV for tokens [0, mc) of xq/xs (already offset to the chunk).
+int launch_tc_chunk(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t ldxs, int64_t mc,
+                    const MamboIQ3SWeight* w, const uint32_t* fp8_table, void* out, int out_dtype, int64_t ldo,
+                    const MamboLinearConfig& c, const GemvPlan& P, const DeviceInfo& info, int* counters,
+                    float* partials, uint8_t* xcopy, uint8_t* xscopy, cudaStream_t stream) {
+  GemvTmMaps maps;
+  std::memset(&maps, 0, sizeof(maps));
+  const uintptr_t fields[5] = {(uintptr_t)w->d, (uintptr_t)w->qs, (uintptr_t)w->qh, (uintptr_t)w->signs,
+                               (uintptr_t)w->scales};
+  for (uintptr_t f : fields)
+    if (f % 16 != 0 || w->n_rows % 8 != 0)
+      return fail(MAMBO_EINVAL,
+                  "the tcgen05 GEMV needs N %% 8 == 0 and 16-byte aligned weight fields (use MAMBO_KERNEL_GEMV_SYNC)");
+  const int64_t k = w->n_blocks * 256;
+  const int box = 8 * P.nt;
+  if (!make_gemv_x_map(xq, ldxq, (int)mc, (int)w->n_blocks, box, &maps.x)) {
+    if (!xcopy) return fail(MAMBO_EINVAL, "x_values rows must be 16-byte aligned");
+    cudaError_t e = cudaMemcpy2DAsync(xcopy, (size_t)k, xq, (size_t)ldxq, (size_t)k, (size_t)mc,
+                                      cudaMemcpyDeviceToDevice, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "copy of unaligned x_values");
+    if (!make_gemv_x_map(xcopy, k, (int)mc, (int)w->n_blocks, box, &maps.x))
+      return fail(MAMBO_ECUDA, "activation tensor map could not be encoded");
+  }
+  if (!make_gemv_xs_map(xs, ldxs, (int)mc, (int)w->n_blocks, box, &maps.xs)) {
+    if (!xscopy) return fail(MAMBO_EINVAL, "x_scales rows must be 16-byte aligned");
+    const int64_t ld = xs_copy_stride(w->n_blocks);
+    cudaError_t e = cudaMemcpy2DAsync(xscopy, (size_t)ld, xs, (size_t)ldxs, (size_t)(w->n_blocks * 8), (size_t)mc,
+                                      cudaMemcpyDeviceToDevice, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "copy of unaligned x_scales");
+    if (!make_gemv_xs_map(xscopy, ld, (int)mc, (int)w->n_blocks, box, &maps.xs))
+      return fail(MAMBO_ECUDA, "activation-scale tensor map could not be encoded");
+  }
+  GemvTmParams p{};
+  p.m = (int)mc;
+  p.n_rows = (int)w->n_rows;
+  p.n_blocks = (int)w->n_blocks;
+  p.d = (const uint8_t*)w->d;
+  p.qs = (const uint8_t*)w->qs;
+  p.qh = (const uint8_t*)w->qh;
+  p.signs = (const uint8_t*)w->signs;
+  p.scales = (const uint8_t*)w->scales;
+  p.table = fp8_table;
+  p.out = out;
+  p.out_bf16 = out_dtype == MAMBO_BF16;
+  p.ldo = ldo;
+  p.partials = partials;
+  p.counters = counters;
+  p.stages = c.stages;
+  p.prefetch = c.prefetch;
+  p.row_tiles = P.row_tiles;
+  p.total_units = P.units;
+  cudaError_t e = launch_gemv_tm(p, P.nt, c.warps, maps, P.grid, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "iq3s_gemv_tm");
+  return MAMBO_OK;
 }
 
 }  // namespace
@@ -345,8 +416,10 @@ int mambo_config_at(int kernel, int index, MamboLinearConfig* cfg) {
   cfg->ctas_per_sm = 1;
   cfg->split = index % 2;
   if (kernel == MAMBO_KERNEL_GEMV) {
-    cfg->warps = kTcDecWarps[index / 6];
-    cfg->stages = kTcStages[(index / 2) % 3];
+    const TcChoice& t = kTcChoices[index / 2];
+    cfg->warps = t.warps;
+    cfg->stages = t.stages;
+    cfg->prefetch = t.prefetch;
   } else {
     cfg->warps = kSyncWarps[index / 8];
     cfg->stages = kSyncStages[(index / 2) % 4];
@@ -364,7 +437,7 @@ size_t mambo_iq3s_linear_workspace_bytes(int64_t m, int64_t n_rows, int64_t n_bl
   const int sms = (st == MAMBO_OK && info.sms > 0) ? info.sms : 148;
   const int64_t m_chunk = m < 32 ? m : 32;
   GemvPlan P = plan_gemv(m_chunk, n_rows, n_blocks, c, sms);
-  return P.counters_bytes + P.partial_bytes + P.pack_bytes;
+  return P.counters_bytes + P.partial_bytes + P.xcopy_bytes + P.xscopy_bytes;
 }
 
 int mambo_iq3s_linear(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t ldxs, int64_t m,
@@ -400,16 +473,23 @@ int mambo_iq3s_linear(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_
     GemvPlan P = plan_gemv(mc, w->n_rows, w->n_blocks, c, info.sms);
     if ((size_t)P.counter_slots * sizeof(int) > kCounterBytes)
       return fail(MAMBO_EINVAL, "N=%lld needs more split-K counters than the workspace holds", (long long)w->n_rows);
-    const size_t need = P.counters_bytes + P.partial_bytes + P.pack_bytes;
+    const size_t need = P.counters_bytes + P.partial_bytes + P.xcopy_bytes + P.xscopy_bytes;
     if (!workspace || workspace_bytes < need)
       return fail(MAMBO_EWORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
     if ((uintptr_t)workspace % 256) return fail(MAMBO_EINVAL, "workspace must be 256-byte aligned");
     const size_t esz = out_dtype == MAMBO_BF16 ? 2 : 4;
     int* counters = (int*)workspace;
     float* partials = (float*)((uint8_t*)workspace + P.counters_bytes);
-    uint8_t* pack = (uint8_t*)workspace + P.counters_bytes + P.partial_bytes;
+    uint8_t* xcopy = (uint8_t*)workspace + P.counters_bytes + P.partial_bytes;
+    uint8_t* xscopy = xcopy + P.xcopy_bytes;
 
-    // Weight tensor maps (the tcgen05 kernel always uses 128-row boxes).
+    if (tc) {
+      st = launch_tc_chunk(xq + m0 * ldxq, ldxq, xs + m0 * ldxs, ldxs, mc, w, fp8_table,
+                           (uint8_t*)out + m0 * ldo * esz, out_dtype, ldo, c, P, info, counters, partials, xcopy,
+                           xscopy, (cudaStream_t)stream);
+      if (st != MAMBO_OK) return st;
+      continue;
+    }
     GemvParams mp{};
     mp.n_rows = (int)w->n_rows;
     mp.n_blocks = (int)w->n_blocks;
@@ -418,46 +498,12 @@ int mambo_iq3s_linear(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_
     mp.qh = (const uint8_t*)w->qh;
     mp.signs = (const uint8_t*)w->signs;
     mp.scales = (const uint8_t*)w->scales;
-    mp.warps = tc ? 8 : c.warps;
+    mp.warps = c.warps;
     GemvMaps maps;
     std::memset(&maps, 0, sizeof(maps));
     const bool have_maps = (c.loader == 0) && make_gemv_maps(mp, &maps);
-
     cudaError_t e;
-    if (tc) {
-      if (!have_maps)
-        return fail(MAMBO_EINVAL,
-                    "the tcgen05 GEMV needs N %% 8 == 0 and 16-byte aligned weight fields (use MAMBO_KERNEL_GEMV_SYNC)");
-      PackParams pk{};
-      pk.xq = xq + m0 * ldxq;
-      pk.ldxq = ldxq;
-      pk.xs = xs + m0 * ldxs;
-      pk.ldxs = ldxs;
-      pk.m = (int)mc;
-      pk.n_blocks = (int)w->n_blocks;
-      pk.nmma = P.nt == 4 ? 32 : 16;
-      pk.pack_bytes = (int)gemv_tc_pack_bytes(P.nt);
-      pk.x_vec = ((uintptr_t)pk.xq % 16 == 0) && (ldxq % 16 == 0);
-      pk.pack = pack;
-      e = launch_pack_activations(pk, info.sms, (cudaStream_t)stream);
-      if (e != cudaSuccess) return cuda_fail(e, "pack_activations");
-      GemvTcParams p{};
-      p.xpack = pack;
-      p.m = (int)mc;
-      p.n_rows = (int)w->n_rows;
-      p.n_blocks = (int)w->n_blocks;
-      p.table = fp8_table;
-      p.out = (uint8_t*)out + m0 * ldo * esz;
-      p.out_bf16 = out_dtype == MAMBO_BF16;
-      p.ldo = ldo;
-      p.partials = partials;
-      p.counters = counters;
-      p.stages = c.stages;
-      p.row_tiles = P.row_tiles;
-      p.total_units = P.units;
-      e = launch_gemv_tc(p, P.nt, c.warps, maps, P.grid, (cudaStream_t)stream);
-      if (e != cudaSuccess) return cuda_fail(e, "iq3s_gemv_tc");
-    } else {
+    {
       GemvParams p = mp;
       p.xq = xq + m0 * ldxq;
       p.ldxq = ldxq;
@@ -489,7 +535,7 @@ int mambo_iq3s_linear(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_
 // --------------------------------------------------------------------------
 
 // Every GPU on which this module is loaded holds this array until the process
-// exits. Layout: split-K counters | FP32 partials | packed activations.
+// exits. Layout: split-K counters | FP32 partials | activation rows copied for alignment.
 static __device__ __align__(256) uint8_t g_linear_scratch[MAMBO_STATIC_SCRATCH_BYTES];
 
 namespace {
@@ -498,10 +544,11 @@ constexpr size_t kStaticCounterBytes = 64 * 1024;  // 4 counters per 128-row til
 constexpr int kStaticMaxCtas = 160;                // persistent grid cap (B200: 148 SMs)
 constexpr int64_t kStaticChunk = 8;                // tokens per launch (one 8-token tile)
 constexpr size_t kStaticPartialBytes = (size_t)kStaticMaxCtas * 2 * 128 * 8 * sizeof(float);
-constexpr size_t kStaticPackOffset = kStaticCounterBytes + kStaticPartialBytes;
-static_assert(kStaticPackOffset % 256 == 0, "scratch regions must stay 256-byte aligned");
-static_assert(kStaticPackOffset < MAMBO_STATIC_SCRATCH_BYTES, "static scratch too small");
-constexpr size_t kStaticPackBytes = MAMBO_STATIC_SCRATCH_BYTES - kStaticPackOffset;
+constexpr size_t kStaticXcopyOffset = kStaticCounterBytes + kStaticPartialBytes;
+constexpr int64_t kStaticMaxK = 98304;  // activation rows copied for alignment: kStaticChunk x K bytes
+static_assert(kStaticXcopyOffset % 256 == 0, "scratch regions must stay 256-byte aligned");
+static_assert(kStaticXcopyOffset + kStaticChunk * kStaticMaxK + kStaticChunk * (kStaticMaxK / 32) <= MAMBO_STATIC_SCRATCH_BYTES,
+              "static scratch too small");
 
 // Device address of g_linear_scratch on the current device, looked up once per
 // device (with that device current) and cached.
@@ -559,9 +606,9 @@ extern "C" int mambo_iq3s_linear_noalloc(const uint8_t* xq, int64_t ldxq, const 
   if (counter_bytes > kStaticCounterBytes)
     return fail(MAMBO_EINVAL, "N=%lld exceeds the static-scratch limit of mambo_iq3s_linear_noalloc (N <= %zu)",
                 (long long)w->n_rows, kStaticCounterBytes / sizeof(int) / 4 * 128);
-  if (P.pack_bytes > kStaticPackBytes)
-    return fail(MAMBO_EINVAL, "K=%lld exceeds the static-scratch limit of mambo_iq3s_linear_noalloc (K <= %zu)",
-                (long long)k, kStaticPackBytes / gemv_tc_pack_bytes(P.nt) * 256);
+  if (k > kStaticMaxK)
+    return fail(MAMBO_EINVAL, "K=%lld exceeds the static-scratch limit of mambo_iq3s_linear_noalloc (K <= %lld)",
+                (long long)k, (long long)kStaticMaxK);
   if (P.partial_bytes > kStaticPartialBytes)
     return fail(MAMBO_EINVAL, "grid of %d CTAs exceeds the static scratch", P.grid);
 
@@ -570,21 +617,7 @@ extern "C" int mambo_iq3s_linear_noalloc(const uint8_t* xq, int64_t ldxq, const 
   if (st != MAMBO_OK) return st;
   int* counters = (int*)scratch;
   float* partials = (float*)(scratch + kStaticCounterBytes);
-  uint8_t* pack = scratch + kStaticPackOffset;
-
-  GemvParams mp{};
-  mp.n_rows = (int)w->n_rows;
-  mp.n_blocks = (int)w->n_blocks;
-  mp.d = (const uint8_t*)w->d;
-  mp.qs = (const uint8_t*)w->qs;
-  mp.qh = (const uint8_t*)w->qh;
-  mp.signs = (const uint8_t*)w->signs;
-  mp.scales = (const uint8_t*)w->scales;
-  mp.warps = 8;  // 128-row tensor-map boxes
-  GemvMaps maps;
-  std::memset(&maps, 0, sizeof(maps));
-  if (!make_gemv_maps(mp, &maps))
-    return fail(MAMBO_EINVAL, "the tcgen05 GEMV needs 16-byte aligned weight fields");
+  uint8_t* xcopy = scratch + kStaticXcopyOffset;
 
   // The counters must start at zero; a call that gave up on a bounded wait may
   // have left some behind, so every call clears the ones it uses.
@@ -594,35 +627,10 @@ extern "C" int mambo_iq3s_linear_noalloc(const uint8_t* xq, int64_t ldxq, const 
   const size_t esz = out_dtype == MAMBO_BF16 ? 2 : 4;
   for (int64_t m0 = 0; m0 < m; m0 += kStaticChunk) {
     const int64_t mc = (m - m0) < kStaticChunk ? (m - m0) : kStaticChunk;
-    PackParams pk{};
-    pk.xq = xq + m0 * ldxq;
-    pk.ldxq = ldxq;
-    pk.xs = xs + m0 * ldxs;
-    pk.ldxs = ldxs;
-    pk.m = (int)mc;
-    pk.n_blocks = (int)w->n_blocks;
-    pk.nmma = 16;
-    pk.pack_bytes = (int)gemv_tc_pack_bytes(P.nt);
-    pk.x_vec = ((uintptr_t)pk.xq % 16 == 0) && (ldxq % 16 == 0);
-    pk.pack = pack;
-    e = launch_pack_activations(pk, info.sms, (cudaStream_t)stream);
-    if (e != cudaSuccess) return cuda_fail(e, "pack_activations");
-    GemvTcParams p{};
-    p.xpack = pack;
-    p.m = (int)mc;
-    p.n_rows = (int)w->n_rows;
-    p.n_blocks = (int)w->n_blocks;
-    p.table = fp8_table;
-    p.out = (uint8_t*)out + m0 * ldo * esz;
-    p.out_bf16 = out_dtype == MAMBO_BF16;
-    p.ldo = ldo;
-    p.partials = partials;
-    p.counters = counters;
-    p.stages = c.stages;
-    p.row_tiles = P.row_tiles;
-    p.total_units = P.units;
-    e = launch_gemv_tc(p, P.nt, c.warps, maps, P.grid, (cudaStream_t)stream);
-    if (e != cudaSuccess) return cuda_fail(e, "iq3s_gemv_tc (static scratch)");
+    st = launch_tc_chunk(xq + m0 * ldxq, ldxq, xs + m0 * ldxs, ldxs, mc, w, fp8_table,
+                         (uint8_t*)out + m0 * ldo * esz, out_dtype, ldo, c, P, info, counters, partials, xcopy,
+                         xcopy + kStaticChunk * kStaticMaxK, (cudaStream_t)stream);
+    if (st != MAMBO_OK) return st;
   }
   return ok();
 }

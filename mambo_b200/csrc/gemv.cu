@@ -416,7 +416,8 @@ template <int NT, int kWarps, bool kTma>
 __global__ void __launch_bounds__((kWarps + 1) * 32, 1)
     iq3s_gemv_kernel(const __grid_constant__ GemvParams p, const __grid_constant__ GemvMaps maps) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // An offset from smem_raw (not integer arithmetic) keeps the pointer in the shared address space.
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* table = smem;
   const int rows = p.warps * 16;
   const int tokens = 8 * NT;
@@ -559,6 +560,27 @@ bool make_gemv_maps(const GemvParams& p, GemvMaps* maps) {
       return false;
   }
   return true;
+}
+
+bool make_gemv_x_map(const uint8_t* xq, int64_t ldxq, int m, int n_blocks, int box_tokens, CUtensorMap* map) {
+  EncodeTiledFn fn = get_encode_fn();
+  if (!fn || (uintptr_t)xq % 16 || ldxq % 16 || m < 1 || box_tokens > 256) return false;
+  // [K/16 chunks][m tokens][16 bytes]: each box lands as 16-byte K chunks of
+  // box_tokens rows, the K-major no-swizzle layout of the MMA's B operand.
+  cuuint64_t dims[3] = {16, (cuuint64_t)m, (cuuint64_t)n_blocks * 16};
+  cuuint64_t str[2] = {(cuuint64_t)ldxq, 16};
+  cuuint32_t box[3] = {16, (cuuint32_t)box_tokens, 16};
+  return encode(fn, map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, xq, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+bool make_gemv_xs_map(const uint8_t* xs, int64_t ldxs, int m, int n_blocks, int box_tokens, CUtensorMap* map) {
+  EncodeTiledFn fn = get_encode_fn();
+  if (!fn || (uintptr_t)xs % 16 || ldxs % 16 || m < 1 || box_tokens > 256) return false;
+  // Boxes of 16 scale bytes (the groups of two K blocks) x box_tokens rows.
+  cuuint64_t dims[2] = {(cuuint64_t)n_blocks * 8, (cuuint64_t)m};
+  cuuint64_t str[1] = {(cuuint64_t)ldxs};
+  cuuint32_t box[2] = {16, (cuuint32_t)box_tokens};
+  return encode(fn, map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, xs, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
 uint32_t gemv_smem_bytes_host(int rows, int nt, int stages, int n_blocks) {

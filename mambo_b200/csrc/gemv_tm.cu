@@ -1,0 +1,579 @@
+// IQ3_S x MXFP8 weight-streaming linear on the 5th-generation tensor cores
+// (tcgen05, sm_100a), with the decoded weight operand kept in tensor memory.
+//
+// Same arithmetic as the reference (src/python/mambo/kernels/iq3_s_fp8.py:279-333):
+// per 32-weight group g, P_g = sum_k E4M3(w) * E4M3(x) is summed by the tensor
+// core in FP32, then out += P_g * 2^e(x, g) * d * (1 + 2*nibble_g) in FP32.
+//
+// One persistent CTA per SM walks a stream-K range of work units (128 weight
+// rows x one 256-wide K block). Roles:
+//  * warp 0, producer: five 1D bulk copies of the unit's IQ3_S fields (for one
+//    K block the fields of 128 consecutive rows are contiguous; evict-first),
+//    an L2 prefetch of the fields `prefetch` units further on, and, once the
+//    previous kernel has finished (programmatic dependent launch), one 3D TMA
+//    copy of the activation block straight into the UMMA B-operand layout
+//    (16-byte K chunks x tokens; rows past M read as zero).
+//  * decoder warps (8 or 16): a thread owns one weight row (its TMEM lane) and
+//    a quarter or half of the block; it reads its raw bytes with 128-bit loads,
+//    expands each 4-weight code through a lane-private
+//    codebook in shared memory, adds the sign bits and writes the E4M3 bytes to
+//    its TMEM lane with tcgen05.st (double-buffered A operand). Weight rows'
+//    d and scale nibbles go to a small shared buffer for the epilogue.
+//  * warp 1, MMA: the converged warp elects one lane that issues 8 tcgen05.mma
+//    (A from TMEM, B from shared memory, M=128, N=16/32, K=32: one per group)
+//    with descriptors formed once per unit, and commits them.
+//  * a scale warp turns the activation scales of each unit into floats.
+//  * 4 epilogue warps: each thread owns one weight row, reads the 8 group
+//    partials of its lane with tcgen05.ld, applies 2^e * d*(1+2*nibble) and
+//    accumulates in FP32 registers; finished rows go to the output or to the
+//    deterministic split-K reduction (acq_rel counter, CTA-ordered sum).
+#include "kernels.cuh"
+#include "tcgen05.cuh"
+
+namespace mambo {
+
+namespace {
+
+constexpr int kRows = 128;                 // weight rows per unit = MMA M = TMEM lanes
+constexpr int kTableBytes = 512 * 32 * 4;  // codebook, one copy per lane
+constexpr int kEpiWarps = 4;
+constexpr int kMaxStagesTm = 8;
+constexpr int kRing = 3;  // decoded units in flight: A operands in TMEM, epilogue data in shared memory
+constexpr uint32_t kBarBytes = 320;
+constexpr uint32_t kTableStageBytes = 512 * 4;  // the codebook as read from global memory
+
+// Warps: producer, MMA, decoders, 4 epilogue, scale.
+__host__ __device__ constexpr int tm_threads(int dec_warps) { return (2 + dec_warps + kEpiWarps + 1) * 32; }
+__host__ __device__ constexpr int tm_box_tokens(int nt) { return 8 * nt; }    // activation rows per B tile
+__host__ __device__ constexpr int tm_nmma(int nt) { return nt == 4 ? 32 : 16; }  // MMA N
+// TMEM columns: the A ring at [0, 64*kRing), then D (8 groups x N columns),
+// double-buffered unless that would not fit in 512 columns (N = 32).
+constexpr uint32_t kTmemD = 64u * kRing;
+__host__ __device__ constexpr int tm_d_buffers(int nt) { return nt != 4 ? 2 : 1; }
+__host__ __device__ constexpr uint32_t tm_tmem_cols(int nt) {
+  return kTmemD + tm_d_buffers(nt) * 8u * tm_nmma(nt) <= 256u ? 256u : 512u;
+}
+__host__ __device__ constexpr uint32_t align_up_tm(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
+
+// One stage: the IQ3_S fields of a unit at the offsets of their TMA boxes,
+// then the activation block. Stages are 512-byte aligned (64-byte swizzle).
+struct TmLayout {
+  uint32_t qs, signs, qh, d, scales, b, xs, stage;
+  uint32_t w, xsf, aux;  // one of two epilogue buffers: rows' (d, scale word), scales as floats
+};
+
+__host__ __device__ inline TmLayout tm_layout(int nt) {
+  TmLayout L{};
+  L.qs = 0;
+  L.signs = kRows * 64;         // 8192 (SWIZZLE_32B destination, 256-aligned)
+  L.qh = L.signs + kRows * 32;  // 12288
+  L.d = L.qh + kRows * 8;       // 13312
+  L.scales = L.d + kRows * 2;   // 13568
+  L.b = L.scales + kRows * 4;   // 14080
+  L.xs = L.b + 256u * tm_box_tokens(nt);  // activation scale bytes: [tokens][16] (two K blocks' groups)
+  L.stage = align_up_tm(L.xs + 16u * tm_box_tokens(nt), 512);
+  L.w = 0;
+  L.xsf = kRows * 8;
+  L.aux = L.xsf + 8u * 8u * nt * 4u;
+  return L;
+}
+
+__host__ __device__ inline uint32_t tm_smem_bytes(int nt, int stages) {
+  const TmLayout L = tm_layout(nt);
+  return kTableBytes + 1024 + stages * L.stage + kRing * L.aux + kTableStageBytes + kBarBytes;
+}
+
+__device__ __forceinline__ int unit_begin_tm(int cta, int grid, int units) {
+  return (int)(((int64_t)cta * units) / grid);
+}
+__device__ __forceinline__ int cta_of_unit_tm(int u, int grid, int units) {
+  return (int)((((int64_t)u + 1) * grid - 1) / units);
+}
+
+__device__ __forceinline__ void store_out_tm(const GemvTmParams& p, int row, int tok, float v) {
+  if (row < p.n_rows && tok < p.m) {
+    if (p.out_bf16) {
+      reinterpret_cast<__nv_bfloat16*>(p.out)[(int64_t)tok * p.ldo + row] = __float2bfloat16_rn(v);
+    } else {
+      reinterpret_cast<float*>(p.out)[(int64_t)tok * p.ldo + row] = v;
+    }
+  }
+}
+
+// Expands the 8 codes of one 32-weight group into E4M3 bytes (4 per register).
+//   q0, q1: the group's 8 qs bytes; hb: its qh byte (bit c = 9th index bit of
+//   code c); sg: its 32 sign bits (bit 4c+j = sign of weight j of code c);
+//   l4: (lane << 2) in every byte. Codebook entry e of lane l sits at byte
+//   (e & 0xFF) << 8 | (e >> 8) << 7 | l << 2, so lanes never share a bank.
+//   n * 0x10204080 (n < 16) puts bit j of n on bit 8j+7 (other partial
+//   products land elsewhere, without carries, and are masked off);
+//   n * 0x01020408 does the same for a nibble held in bits 4-7.
+__device__ __forceinline__ void decode_group(const uint8_t* table, uint32_t q0, uint32_t q1, uint32_t hb, uint32_t sg,
+                                             uint32_t l4, uint32_t* v) {
+  const uint32_t h0 = lop3_and_or((hb & 0xFu) * 0x10204080u, 0x80808080u, l4);   // byte j: h_j << 7 | lane << 2
+  const uint32_t h1 = lop3_and_or((hb & 0xF0u) * 0x01020408u, 0x80808080u, l4);  // codes 4..7
+  const uint32_t q0l = q0 & 0xFFFFu, q0h = q0 >> 16, q1l = q1 & 0xFFFFu, q1h = q1 >> 16;
+  const uint32_t m0 = *reinterpret_cast<const uint32_t*>(table + prmt(q0l, h0, 0x3204u));
+  const uint32_t m1 = *reinterpret_cast<const uint32_t*>(table + prmt(q0l, h0, 0x3215u));
+  const uint32_t m2 = *reinterpret_cast<const uint32_t*>(table + prmt(q0h, h0, 0x3206u));
+  const uint32_t m3 = *reinterpret_cast<const uint32_t*>(table + prmt(q0h, h0, 0x3217u));
+  const uint32_t m4 = *reinterpret_cast<const uint32_t*>(table + prmt(q1l, h1, 0x3204u));
+  const uint32_t m5 = *reinterpret_cast<const uint32_t*>(table + prmt(q1l, h1, 0x3215u));
+  const uint32_t m6 = *reinterpret_cast<const uint32_t*>(table + prmt(q1h, h1, 0x3206u));
+  const uint32_t m7 = *reinterpret_cast<const uint32_t*>(table + prmt(q1h, h1, 0x3217u));
+  const uint32_t s2 = sg >> 8, s4 = sg >> 16, s6 = sg >> 24;
+  v[0] = lop3_and_or((sg & 0xFu) * 0x10204080u, 0x80808080u, m0);
+  v[1] = lop3_and_or((sg & 0xF0u) * 0x01020408u, 0x80808080u, m1);
+  v[2] = lop3_and_or((s2 & 0xFu) * 0x10204080u, 0x80808080u, m2);
+  v[3] = lop3_and_or((s2 & 0xF0u) * 0x01020408u, 0x80808080u, m3);
+  v[4] = lop3_and_or((s4 & 0xFu) * 0x10204080u, 0x80808080u, m4);
+  v[5] = lop3_and_or((s4 & 0xF0u) * 0x01020408u, 0x80808080u, m5);
+  v[6] = lop3_and_or((s6 & 0xFu) * 0x10204080u, 0x80808080u, m6);
+  v[7] = lop3_and_or((sg >> 28) * 0x10204080u, 0x80808080u, m7);
+}
+
+}  // namespace
+
+// Elects one lane of a converged warp (tcgen05.mma reads its operands from
+// uniform registers: issuing from a converged warp keeps them there).
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\telect.sync _|p, 0xffffffff;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
+template <int NT, int kDecWarps>
+__global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
+    iq3s_gemv_tm_kernel(const __grid_constant__ GemvTmParams p, const __grid_constant__ GemvTmMaps maps) {
+  constexpr int TOK = 8 * NT;             // tokens the epilogue keeps
+  constexpr int NM = tm_nmma(NT);         // MMA N
+  constexpr int BOX = tm_box_tokens(NT);  // activation rows in a B tile
+  constexpr uint32_t kIdesc = tc::idesc_e4m3_f32(kRows, NM);
+  constexpr int kDBuf = tm_d_buffers(NT);
+  constexpr uint32_t kCols = tm_tmem_cols(NT);
+  constexpr int kParts = kDecWarps / 4;  // decoder threads per weight row
+  constexpr int kGroups = 8 / kParts;    // 32-weight groups per decoder thread and unit
+  constexpr uint32_t kBytesX = BOX * 256u + BOX * 16u;
+  // B tile [16-byte K chunk][BOX tokens][16 bytes]: K-direction core-matrix
+  // stride BOX*16, token-group stride 128. With 8 tokens the MMA's rows 8-15
+  // repeat rows 0-7 (stride 0) and their results are never read.
+  constexpr uint32_t kLbo = BOX * 16u;
+  constexpr uint32_t kSbo = NT == 1 ? 0u : 128u;
+  constexpr int kEpiWarp0 = 2 + kDecWarps, kScaleWarp = 2 + kDecWarps + kEpiWarps;
+  static_assert(kDecWarps == 8 || kDecWarps == 16, "8 or 16 decoder warps");
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  const TmLayout L = tm_layout(NT);
+  // The codebook sits at the start of dynamic shared memory (a link-time
+  // constant address); the stages follow, aligned to 1024 bytes at run time.
+  // (Offsets from smem_raw keep the pointers in the shared address space, so
+  // every access below compiles to a shared-memory instruction.)
+  uint8_t* table = smem_raw;
+  uint8_t* st0 = smem_raw + kTableBytes + ((1024u - ((smem_u32(smem_raw) + kTableBytes) & 1023u)) & 1023u);
+  uint8_t* aux0 = st0 + (size_t)p.stages * L.stage;
+  uint32_t* tstage = reinterpret_cast<uint32_t*>(aux0 + kRing * L.aux);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(aux0 + kRing * L.aux + kTableStageBytes);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * kMaxStagesTm + 3 * kRing + 3);
+  const uint32_t bar0 = smem_u32(bars);
+  // Barriers: per stage wfull (weights landed), xfull (activations landed),
+  // empty (stage consumed); per ring slot afull (A decoded, row data written),
+  // sfull (scales converted), efree (epilogue done with the slot); per D
+  // buffer mdone (MMAs complete); edone (epilogue finished).
+  const uint32_t kWfull = bar0, kXfull = bar0 + 8 * kMaxStagesTm, kEmpty = bar0 + 16 * kMaxStagesTm;
+  const uint32_t kAfull = bar0 + 24 * kMaxStagesTm, kSfull = kAfull + 8 * kRing, kEfree = kSfull + 8 * kRing;
+  const uint32_t kMdone = kEfree + 8 * kRing, kEdone = kMdone + 16;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int u0 = unit_begin_tm(blockIdx.x, gridDim.x, p.total_units);
+  const int u1 = unit_begin_tm(blockIdx.x + 1, gridDim.x, p.total_units);
+  const int n_units = u1 - u0;
+  const int S = p.stages;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(kWfull + 8 * s, 1);
+      mbar_init(kXfull + 8 * s, 1);
+      mbar_init(kEmpty + 8 * s, kDecWarps + 2);  // decoders, MMA commit, scale warp
+    }
+    for (int r = 0; r < kRing; ++r) {
+      mbar_init(kAfull + 8 * r, kDecWarps);
+      mbar_init(kSfull + 8 * r, 1);
+      mbar_init(kEfree + 8 * r, kEpiWarps);
+    }
+    for (int b = 0; b < 2; ++b) mbar_init(kMdone + 8 * b, 1);
+    mbar_init(kEdone, kEpiWarps);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tc::alloc(smem_u32(tmem_slot), kCols);
+    tc::relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+
+  // ------------------------------------------------------------------ producer
+  // The whole warp issues: lane f < 5 copies weight field f, so one warp
+  // instruction starts all five copies of a unit (a copy instruction costs
+  // its thread ~100 cycles or more to issue).
+  if (warp == 0) {
+    const uint64_t policy = l2_policy_evict_first();
+    const uint64_t keep = l2_policy_evict_last();  // activations: every CTA reads them
+    if (lane == 0) {
+      tma_prefetch_desc(&maps.x);
+      tma_prefetch_desc(&maps.xs);
+    }
+    const uint8_t* fptr = lane == 0 ? p.qs : lane == 1 ? p.signs : lane == 2 ? p.qh : lane == 3 ? p.d : p.scales;
+    const uint32_t fbpr = lane == 0 ? 64u : lane == 1 ? 32u : lane == 2 ? 8u : lane == 3 ? 2u : 4u;  // bytes per row
+    const uint32_t foff = lane == 0 ? L.qs : lane == 1 ? L.signs : lane == 2 ? L.qh : lane == 3 ? L.d : L.scales;
+    // Rows of the unit's tile (a multiple of 8) and their index in each field.
+    auto tile = [&](int u, uint32_t& rows, size_t& base) {
+      const int n0 = (u / p.n_blocks) * kRows;
+      rows = (uint32_t)min(kRows, p.n_rows - n0);
+      base = (size_t)(u % p.n_blocks) * p.n_rows + n0;
+    };
+    auto issue_weights = [&](int it) {
+      const int s = it % S;
+      const uint32_t full = kWfull + 8 * s;
+      uint32_t rows;
+      size_t base;
+      tile(u0 + it, rows, base);
+      if (lane == 0) mbar_arrive_expect_tx(full, rows * 110u);
+      __syncwarp();
+      if (lane < 5) bulk_load_hint(smem_u32(st0 + (size_t)s * L.stage) + foff, fptr + base * fbpr, rows * fbpr, full, policy);
+      __syncwarp();
+    };
+    auto issue_acts = [&](int it) {
+      const int s = it % S, kb = (u0 + it) % p.n_blocks;
+      const uint32_t full = kXfull + 8 * s;
+      if (lane == 0) mbar_arrive_expect_tx(full, kBytesX);
+      __syncwarp();
+      if (lane == 0) tma_load_3d(smem_u32(st0 + (size_t)s * L.stage + L.b), &maps.x, 0, 0, kb * 16, full, keep);
+      if (lane == 1) tma_load_2d(smem_u32(st0 + (size_t)s * L.stage + L.xs), &maps.xs, (kb >> 1) * 16, 0, full, keep);
+      __syncwarp();
+    };
+    auto prefetch = [&](int it) {
+      uint32_t rows;
+      size_t base;
+      tile(u0 + it, rows, base);
+      if (lane < 5) bulk_prefetch_l2(fptr + base * fbpr, rows * fbpr);
+      __syncwarp();
+    };
+    const int pre = min(S, n_units);
+    // Weights do not depend on the previous kernel: stream them first.
+    for (int it = 0; it < pre; ++it) issue_weights(it);
+    int pf = pre;
+    for (; pf < min(n_units, pre + p.prefetch); ++pf) prefetch(pf);
+    pdl_wait();
+    for (int it = 0; it < pre; ++it) issue_acts(it);
+    for (int it = pre; it < n_units; ++it) {
+      const bool ok = mbar_wait_bounded(kEmpty + 8 * (it % S), ((it / S) & 1) ^ 1, kSiteGemvEmpty);
+      if (!__all_sync(0xFFFFFFFFu, ok)) return;
+      issue_weights(it);
+      issue_acts(it);
+      for (; pf < min(n_units, it + 1 + p.prefetch); ++pf) prefetch(pf);
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------------ MMA
+  if (warp == 1) {
+    for (int it = 0; it < n_units; ++it) {
+      const int r = it % kRing, s = it % S, db = kDBuf == 2 ? (it & 1) : 0;
+      // The D buffer is free once the epilogue is done with the unit that used it last.
+      const int prev = it - kDBuf;
+      bool ok = mbar_try_wait(kAfull + 8 * r, (it / kRing) & 1);
+      bool ok2 = mbar_try_wait(kXfull + 8 * s, (it / S) & 1);
+      bool ok3 = prev < 0 || mbar_try_wait(kEfree + 8 * (prev % kRing), (prev / kRing) & 1);
+      if (!__all_sync(0xFFFFFFFFu, ok && ok2 && ok3)) {  // slow path, taken by the whole warp
+        ok = mbar_wait_bounded(kAfull + 8 * r, (it / kRing) & 1, kSiteGemvFull);
+        ok = ok && mbar_wait_bounded(kXfull + 8 * s, (it / S) & 1, kSiteGemvFull);
+        if (prev >= 0) ok = ok && mbar_wait_bounded(kEfree + 8 * (prev % kRing), (prev / kRing) & 1, kSiteGemvEmpty);
+        if (!__all_sync(0xFFFFFFFFu, ok)) break;
+      }
+      tc::fence_after_sync();
+      const uint64_t db0 = tc::smem_desc(smem_u32(st0 + (size_t)s * L.stage + L.b), kLbo, kSbo);
+      const uint32_t dcol = tmem + kTmemD + (uint32_t)(db * 8 * NM), acol = tmem + (uint32_t)(r * 64);
+      if (elect_one()) {
+#pragma unroll
+        for (int g = 0; g < 8; ++g)
+          tc::mma_e4m3_ts(dcol + (uint32_t)(g * NM), acol + (uint32_t)(g * 8), db0 + (uint64_t)((2u * kLbo * g) >> 4),
+                          kIdesc, 0);
+        tc::commit(kEmpty + 8 * s);
+        tc::commit(kMdone + 8 * db);
+      }
+      __syncwarp();
+    }
+    // Free the TMEM once every epilogue warp has read its last partials.
+    mbar_wait_bounded(kEdone, 0, kSiteGemvFull);
+    __syncwarp();
+    tc::fence_after_sync();
+    tc::dealloc(tmem, kCols);
+    return;
+  }
+
+  // ------------------------------------------------------------------ scales
+  if (warp == kScaleWarp) {
+    constexpr int VPL = TOK * 8 / 32;  // values per lane and unit
+    for (int it = 0; it < n_units; ++it) {
+      const int r = it % kRing, s = it % S;
+      bool ok = mbar_wait_bounded(kXfull + 8 * s, (it / S) & 1, kSiteGemvFull);
+      if (it >= kRing) ok = ok && mbar_wait_bounded(kEfree + 8 * r, ((it / kRing) & 1) ^ 1, kSiteGemvEmpty);
+      if (!__all_sync(0xFFFFFFFFu, ok)) return;
+      // Scale bytes of this K block ([token][16], groups at (kb & 1) * 8) -> floats [group][token].
+      const uint8_t* xsb = st0 + (size_t)s * L.stage + L.xs + (((u0 + it) % p.n_blocks) & 1) * 8;
+      float* xsf = reinterpret_cast<float*>(aux0 + (size_t)r * L.aux + L.xsf);
+#pragma unroll
+      for (int j = 0; j < VPL; ++j) {
+        const int v = j * 32 + lane, g = v / TOK, t = v % TOK;
+        xsf[v] = e8m0_to_float(xsb[t * 16 + g]);
+      }
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(kSfull + 8 * r);
+        mbar_arrive(kEmpty + 8 * s);
+      }
+      __syncwarp();
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------------ decoders
+  if (warp < kEpiWarp0) {
+    const int dw = warp - 2;
+    const int q = warp & 3;        // TMEM lane quadrant this warp may access
+    const int part = dw >> 2;      // which 1/kParts of the K block
+    const int rl = 32 * q + lane;  // weight row within the tile = TMEM lane
+    const int nthreads = kDecWarps * 32;
+    const int tid = threadIdx.x - 64;
+    // Codebook: stage the 2 KB read from global memory, then expand to the
+    // lane-private copy, four lanes' copies (16 contiguous bytes) per store.
+    for (int i = tid; i < 512; i += nthreads) tstage[i] = __ldg(p.table + i);
+    asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+    for (int i = tid; i < 512 * 8; i += nthreads) {
+      const uint32_t code = i >> 3, l0 = (i & 7) * 4, e = tstage[code];
+      *reinterpret_cast<uint4*>(table + (((code & 0xFFu) << 8) | ((code >> 8) << 7) | (l0 << 2))) =
+          make_uint4(e, e, e, e);
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+
+    const uint32_t l4 = (uint32_t)(lane << 2) * 0x01010101u;
+    const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(part * kGroups * 8);
+    for (int it = 0; it < n_units; ++it) {
+      const int s = it % S, r = it % kRing;
+      // A ring slot r is free once the epilogue is done with unit it - kRing.
+      const bool ok1 = mbar_try_wait(kWfull + 8 * s, (it / S) & 1);
+      const bool ok2 = it < kRing || mbar_try_wait(kEfree + 8 * r, ((it / kRing) & 1) ^ 1);
+      if (!__all_sync(0xFFFFFFFFu, ok1 && ok2)) {  // slow path, taken by the whole warp
+        bool ok = mbar_wait_bounded(kWfull + 8 * s, (it / S) & 1, kSiteGemvFull);
+        if (it >= kRing) ok = ok && mbar_wait_bounded(kEfree + 8 * r, ((it / kRing) & 1) ^ 1, kSiteGemvEmpty);
+        if (!__all_sync(0xFFFFFFFFu, ok)) return;
+      }
+      const uint8_t* st = st0 + (size_t)s * L.stage;
+      uint32_t qw[2 * kGroups], sw[kGroups], hw;
+      if constexpr (kParts == 2) {
+        const uint4 a = *reinterpret_cast<const uint4*>(st + L.qs + rl * 64 + 32 * part);
+        const uint4 c = *reinterpret_cast<const uint4*>(st + L.qs + rl * 64 + 32 * part + 16);
+        const uint4 g = *reinterpret_cast<const uint4*>(st + L.signs + rl * 32 + 16 * part);
+        qw[0] = a.x; qw[1] = a.y; qw[2] = a.z; qw[3] = a.w;
+        qw[4] = c.x; qw[5] = c.y; qw[6] = c.z; qw[7] = c.w;
+        sw[0] = g.x; sw[1] = g.y; sw[2] = g.z; sw[3] = g.w;
+        hw = *reinterpret_cast<const uint32_t*>(st + L.qh + rl * 8 + 4 * part);
+      } else {
+        const uint4 a = *reinterpret_cast<const uint4*>(st + L.qs + rl * 64 + 16 * part);
+        const uint2 g = *reinterpret_cast<const uint2*>(st + L.signs + rl * 32 + 8 * part);
+        qw[0] = a.x; qw[1] = a.y; qw[2] = a.z; qw[3] = a.w;
+        sw[0] = g.x; sw[1] = g.y;
+        hw = *reinterpret_cast<const uint16_t*>(st + L.qh + rl * 8 + 2 * part);
+      }
+      if (part == 0) {
+        // The row's d and scale nibbles for the epilogue (it forms d * (1 + 2*nibble)).
+        reinterpret_cast<uint2*>(aux0 + (size_t)r * L.aux + L.w)[rl] =
+            make_uint2(*reinterpret_cast<const uint16_t*>(st + L.d + rl * 2),
+                       *reinterpret_cast<const uint32_t*>(st + L.scales + rl * 4));
+      }
+      // All groups first, then one store: the codebook loads of every group can be in flight together.
+      uint32_t v[kGroups * 8];
+#pragma unroll
+      for (int g = 0; g < kGroups; ++g)
+        decode_group(table, qw[2 * g], qw[2 * g + 1], (hw >> (8 * g)) & 0xFFu, sw[g], l4, v + 8 * g);
+      tc::st_cols<kGroups * 8>(tq + (uint32_t)(r * 64), v);
+      tc::wait_st();
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(kAfull + 8 * r);
+        mbar_arrive(kEmpty + 8 * s);
+      }
+      __syncwarp();  // reconverge before the next waits
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------------ epilogue
+  {
+    const int q = warp & 3;        // TMEM lane quadrant of this warp
+    const int rl = 32 * q + lane;  // local weight row = TMEM lane
+    const uint32_t tq0 = tmem + ((uint32_t)(32 * q) << 16) + kTmemD;
+    float acc[TOK];
+#pragma unroll
+    for (int t = 0; t < TOK; ++t) acc[t] = 0.f;
+    pdl_wait();  // the workspace and output may still be in use by the previous kernel
+    pdl_launch_dependents();
+    int seg_begin = u0;
+    for (int it = 0, u = u0; u < u1; ++u, ++it) {
+      const int r = it % kRing, db = kDBuf == 2 ? (it & 1) : 0;
+      const uint32_t mpar = kDBuf == 2 ? ((it >> 1) & 1) : (it & 1);
+      bool ok = mbar_try_wait(kMdone + 8 * db, mpar);
+      bool ok2 = mbar_try_wait(kAfull + 8 * r, (it / kRing) & 1);
+      bool ok3 = mbar_try_wait(kSfull + 8 * r, (it / kRing) & 1);
+      if (!__all_sync(0xFFFFFFFFu, ok && ok2 && ok3)) {  // slow path, taken by the whole warp
+        ok = mbar_wait_bounded(kMdone + 8 * db, mpar, kSiteGemvFull);
+        ok = ok && mbar_wait_bounded(kAfull + 8 * r, (it / kRing) & 1, kSiteGemvFull);
+        ok = ok && mbar_wait_bounded(kSfull + 8 * r, (it / kRing) & 1, kSiteGemvFull);
+        if (!__all_sync(0xFFFFFFFFu, ok)) break;
+      }
+      tc::fence_after_sync();
+      const uint32_t tq = tq0 + (uint32_t)(db * 8 * NM);
+      const uint8_t* aux = aux0 + (size_t)r * L.aux;
+      const float* xs = reinterpret_cast<const float*>(aux + L.xsf);
+      const uint2 dsc = reinterpret_cast<const uint2*>(aux + L.w)[rl];
+      const float dv = __half2float(__ushort_as_half((unsigned short)dsc.x));
+      const float dneg = -8388608.0f * dv;
+      // 2*nibble+1 of group g is byte g/2 of tb[g&1]; float(2^23 + t)*d - 2^23*d = t*d exactly.
+      const uint32_t tb0 = lop3_and_or(dsc.y << 1, 0x1E1E1E1Eu, 0x01010101u);
+      const uint32_t tb1 = lop3_and_or(dsc.y >> 3, 0x1E1E1E1Eu, 0x01010101u);
+      // Groups per batch of TMEM loads (one wait per batch), within the register budget.
+      constexpr int GB = kDecWarps == 8 ? (TOK <= 16 ? 4 : 2) : 2;
+#pragma unroll
+      for (int t0 = 0; t0 < TOK; t0 += 8) {
+#pragma unroll
+        for (int g0 = 0; g0 < 8; g0 += GB) {
+          uint32_t off[GB];
+#pragma unroll
+          for (int j = 0; j < GB; ++j) off[j] = (uint32_t)((g0 + j) * NM + t0);
+          float c[GB][8];
+          tc::ld_x8_multi<GB>(tq, off, c);
+#pragma unroll
+          for (int j = 0; j < GB; ++j) {
+            const int g = g0 + j;
+            const float w = fmaf(__uint_as_float(prmt((g & 1) ? tb1 : tb0, 0x4B000000u, 0x7650u | (uint32_t)(g >> 1))),
+                                 dv, dneg);
+#pragma unroll
+            for (int t = 0; t < 8; t += 2) {
+              float p0, p1;
+              mul2(p0, p1, c[j][t], c[j][t + 1], xs[g * TOK + t0 + t], xs[g * TOK + t0 + t + 1]);
+              fma2(acc[t0 + t], acc[t0 + t + 1], p0, p1, w, w);
+            }
+          }
+        }
+      }
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(kEfree + 8 * r);
+      __syncwarp();  // reconverge before the next waits
+
+      const int kb = u % p.n_blocks, rt = u / p.n_blocks;
+      if (!(kb == p.n_blocks - 1 || u == u1 - 1)) continue;
+      const bool full_tile = (seg_begin % p.n_blocks == 0) && (kb == p.n_blocks - 1);
+      const int row = rt * kRows + rl;
+      if (full_tile) {
+#pragma unroll
+        for (int t = 0; t < TOK; ++t) store_out_tm(p, row, t, acc[t]);
+      } else {
+        const int cta = blockIdx.x, grid = gridDim.x;
+        const int slot_id = (rt == u0 / p.n_blocks) ? 0 : 1;
+        float* part = p.partials + ((size_t)(cta * 2 + slot_id) * kRows + rl) * TOK;
+#pragma unroll
+        for (int t = 0; t < TOK; t += 4)
+          __stcg(reinterpret_cast<float4*>(part + t), make_float4(acc[t], acc[t + 1], acc[t + 2], acc[t + 3]));
+        __syncwarp();
+        const int c_first = cta_of_unit_tm(rt * p.n_blocks, grid, p.total_units);
+        const int c_last = cta_of_unit_tm(rt * p.n_blocks + p.n_blocks - 1, grid, p.total_units);
+        int last = 0;
+        if (lane == 0) {
+          int* counter = p.counters + (size_t)rt * kEpiWarps + q;
+          last = (atomic_add_acq_rel_gpu(counter, 1) == c_last - c_first);
+          if (last) *counter = 0;  // leave the counter zeroed for the next launch
+        }
+        last = __shfl_sync(0xFFFFFFFFu, last, 0);
+        if (last) {
+          // Sum the contributors' partials in CTA order, 8 tokens at a time.
+          constexpr int kBatch = kDecWarps == 8 && TOK <= 8 ? 4 : 1;
+#pragma unroll 1
+          for (int t0 = 0; t0 < TOK; t0 += 8) {
+            float sum[8];
+#pragma unroll
+            for (int t = 0; t < 8; ++t) sum[t] = 0.f;
+#pragma unroll 1
+            for (int c0 = c_first; c0 <= c_last; c0 += kBatch) {
+              float4 v[kBatch][2];
+#pragma unroll
+              for (int j = 0; j < kBatch; ++j) {
+                const int c = c0 + j;
+                if (c <= c_last) {
+                  const int cs = (rt == unit_begin_tm(c, grid, p.total_units) / p.n_blocks) ? 0 : 1;
+                  const float4* src =
+                      reinterpret_cast<const float4*>(p.partials + ((size_t)(c * 2 + cs) * kRows + rl) * TOK + t0);
+                  v[j][0] = __ldcg(src);
+                  v[j][1] = __ldcg(src + 1);
+                }
+              }
+#pragma unroll
+              for (int j = 0; j < kBatch; ++j) {
+                if (c0 + j <= c_last) {
+                  sum[0] += v[j][0].x; sum[1] += v[j][0].y; sum[2] += v[j][0].z; sum[3] += v[j][0].w;
+                  sum[4] += v[j][1].x; sum[5] += v[j][1].y; sum[6] += v[j][1].z; sum[7] += v[j][1].w;
+                }
+              }
+            }
+#pragma unroll
+            for (int t = 0; t < 8; ++t) store_out_tm(p, row, t0 + t, sum[t]);
+          }
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < TOK; ++t) acc[t] = 0.f;
+      seg_begin = u + 1;
+    }
+    tc::fence_before_sync();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(kEdone);
+  }
+}
+
+// --------------------------------------------------------------------------
+// Host side
+// --------------------------------------------------------------------------
+uint32_t gemv_tm_smem_bytes(int nt, int stages) { return tm_smem_bytes(nt, stages); }
+int gemv_tm_max_stages() { return kMaxStagesTm; }
+
+template <int NT, int kDecWarps>
+static cudaError_t launch_gemv_tm_t(const GemvTmParams& p, const GemvTmMaps& maps, int grid, cudaStream_t stream) {
+  const uint32_t smem = tm_smem_bytes(NT, p.stages);
+  const void* kern = (const void*)iq3s_gemv_tm_kernel<NT, kDecWarps>;
+  cudaError_t e = ensure_smem_attribute(kern, smem);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(kern, dim3(grid), dim3(tm_threads(kDecWarps)), smem, stream, p, maps);
+}
+
+template <int NT>
+static cudaError_t launch_gemv_tm_n(const GemvTmParams& p, int dec_warps, const GemvTmMaps& maps, int grid,
+                                    cudaStream_t stream) {
+  if (dec_warps == 16) return launch_gemv_tm_t<NT, 16>(p, maps, grid, stream);
+  return launch_gemv_tm_t<NT, 8>(p, maps, grid, stream);
+}
+
+cudaError_t launch_gemv_tm(const GemvTmParams& p, int nt, int dec_warps, const GemvTmMaps& maps, int grid,
+                           cudaStream_t stream) {
+  switch (nt) {
+    case 1: return launch_gemv_tm_n<1>(p, dec_warps, maps, grid, stream);
+    case 2: return launch_gemv_tm_n<2>(p, dec_warps, maps, grid, stream);
+    default: return launch_gemv_tm_n<4>(p, dec_warps, maps, grid, stream);
+  }
+}
+
+}  // namespace mambo

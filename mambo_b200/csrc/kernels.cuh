@@ -94,41 +94,44 @@ cudaError_t launch_gemv(const GemvParams& p, int nt, bool use_tma, const GemvMap
                         cudaStream_t stream);
 uint32_t gemv_smem_bytes_host(int rows, int nt, int stages, int n_blocks);
 
-// Packed MXFP8 activations for the tcgen05 GEMV (one slice per 256-wide K block).
-struct PackParams {
-  const uint8_t* xq;
-  int64_t ldxq;
-  const uint8_t* xs;
-  int64_t ldxs;
-  int m;
-  int n_blocks;
-  int nmma;        // MMA N: tokens padded to 16 or 32
-  int pack_bytes;  // bytes per K block: nmma*256 (E4M3 tile) + 8*nmma*4 (float scales)
-  int x_vec;       // xq rows 16-byte aligned
-  uint8_t* pack;
-};
-cudaError_t launch_pack_activations(const PackParams& p, int num_sms, cudaStream_t stream);
-
-struct GemvTcParams {
-  const uint8_t* xpack;  // packed activations, n_blocks slices of pack_bytes
-  int m;
+// tcgen05 GEMV with the decoded weight operand in tensor memory.
+struct GemvTmParams {
+  int m;  // tokens of this launch (<= 8*NT)
   int n_rows;
   int n_blocks;
-  const uint32_t* table;
+  // SoA weight fields: for one K block, the fields of 128 consecutive rows are
+  // contiguous, so a work unit arrives as five 1D bulk copies.
+  const uint8_t* d;
+  const uint8_t* qs;
+  const uint8_t* qh;
+  const uint8_t* signs;
+  const uint8_t* scales;
+  const uint32_t* table;  // uint32[512], E4M3-encoded magnitudes
   void* out;
   int out_bf16;
   int64_t ldo;
   float* partials;  // [grid][2][128][8*NT]
   int* counters;    // [row_tiles][4], zero between launches
   int stages;
+  int prefetch;  // units prefetched into L2 beyond the stage ring
   int row_tiles;
   int total_units;
 };
-cudaError_t launch_gemv_tc(const GemvTcParams& p, int nt, int dec_warps, const GemvMaps& maps, int grid,
+
+struct GemvTmMaps {
+  CUtensorMap x;                         // activations [K/16 chunks][m tokens][16 bytes], box 16 x 8*NT x 16
+  CUtensorMap xs;                        // activation scales [m tokens][K/32 groups], box 16 x 8*NT
+};
+
+// Activation map for the tcgen05 GEMV; false when xq is not 16-byte aligned
+// with a row stride that is a multiple of 16.
+bool make_gemv_x_map(const uint8_t* xq, int64_t ldxq, int m, int n_blocks, int box_tokens, CUtensorMap* map);
+// Scale map for the tcgen05 GEMV; false unless xs is 16-byte aligned with a row stride that is a multiple of 16.
+bool make_gemv_xs_map(const uint8_t* xs, int64_t ldxs, int m, int n_blocks, int box_tokens, CUtensorMap* map);
+cudaError_t launch_gemv_tm(const GemvTmParams& p, int nt, int dec_warps, const GemvTmMaps& maps, int grid,
                            cudaStream_t stream);
-uint32_t gemv_tc_smem_bytes(int nt, int stages);
-uint32_t gemv_tc_pack_bytes(int nt);
-int gemv_tc_max_stages();
+uint32_t gemv_tm_smem_bytes(int nt, int stages);
+int gemv_tm_max_stages();
 
 cudaError_t launch_wait_selftest(unsigned long long limit_ns, cudaStream_t stream);
 cudaError_t probe_kernel_image();

@@ -34,6 +34,70 @@ __device__ __forceinline__ void mma_e4m3(uint32_t tmem_d, uint64_t desc_a, uint6
       "l"(desc_a), "l"(desc_b), "r"(idesc), "r"(accumulate));
 }
 
+// D[tmem] (+)= A[tmem] x B[smem]^T, issued by one thread. A occupies the TMEM
+// lanes of its rows, K packed four E4M3 values per 32-bit column.
+__device__ __forceinline__ void mma_e4m3_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t desc_b, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(desc_b), "r"(idesc), "r"(accumulate));
+}
+
+// Each lane writes 8 consecutive 32-bit columns of its TMEM lane (warp-wide).
+__device__ __forceinline__ void st_x8(uint32_t taddr, const uint32_t (&v)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(v[0]),
+               "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
+}
+// Each lane writes N (16 or 32) consecutive 32-bit columns of its TMEM lane.
+// No memory clobber: the store touches tensor memory only, so shared-memory
+// loads after it may be scheduled ahead of it (tcgen05.wait::st orders it).
+template <int N>
+__device__ __forceinline__ void st_cols(uint32_t taddr, const uint32_t (&v)[N]) {
+  static_assert(N == 16 || N == 32, "16 or 32 columns");
+  if constexpr (N == 16) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]));
+  } else {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+        "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+        "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31]));
+  }
+}
+
+// Loads 8 consecutive 32-bit columns of this lane's TMEM row for each of G
+// column offsets, then waits once for all of them.
+template <int G>
+__device__ __forceinline__ void ld_x8_multi(uint32_t taddr, const uint32_t (&off)[G], float (&v)[G][8]) {
+  uint32_t r[G][8];
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[g][0]), "=r"(r[g][1]), "=r"(r[g][2]), "=r"(r[g][3]), "=r"(r[g][4]), "=r"(r[g][5]),
+                   "=r"(r[g][6]), "=r"(r[g][7])
+                 : "r"(taddr + off[g]));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+  // Tie the registers to the wait: every use below depends on this empty asm.
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      asm volatile("" : "+r"(r[g][i]));
+      v[g][i] = __uint_as_float(r[g][i]);
+    }
+}
+
+// Waits until this thread's earlier tcgen05.st have completed.
+__device__ __forceinline__ void wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 // Arrives (once) on the mbarrier when all MMAs previously issued by this thread complete.
 __device__ __forceinline__ void commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)

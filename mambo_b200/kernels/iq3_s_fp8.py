@@ -51,8 +51,10 @@ IQ3_S_SCALE_VALUES = 32
 # follow the reference convention: GPU SM version, then medium/large by M.
 BEST_CONFIGS = {
     "sm100": {
-        "medium": {"kernel": _lib.MAMBO_KERNEL_GEMV, "warps": 8, "stages": 4, "ctas_per_sm": 1, "split": 0},
-        "large": {"kernel": _lib.MAMBO_KERNEL_GEMV, "warps": 8, "stages": 3, "ctas_per_sm": 1, "split": 0},
+        "medium": {"kernel": _lib.MAMBO_KERNEL_GEMV, "warps": 8, "stages": 6, "ctas_per_sm": 1, "split": 0,
+                   "prefetch": 4},
+        "large": {"kernel": _lib.MAMBO_KERNEL_GEMV, "warps": 8, "stages": 4, "ctas_per_sm": 1, "split": 0,
+                  "prefetch": 4},
     },
 }
 LARGE_TOKEN_THRESHOLD = 32

@@ -209,13 +209,15 @@ def test_linear_kernels_and_splits_match_oracle(cuda_device, m, n, k, kernel, sp
     np.testing.assert_allclose(got, ref, rtol=5e-4, atol=5e-4 * np.abs(ref).max())
 
 
-@pytest.mark.parametrize("kind,warps,stages", [(_lib.MAMBO_KERNEL_GEMV_SYNC, 4, 3), (_lib.MAMBO_KERNEL_GEMV_SYNC, 16, 3),
-                                               (_lib.MAMBO_KERNEL_GEMV_SYNC, 12, 6), (_lib.MAMBO_KERNEL_GEMV, 8, 2),
-                                               (_lib.MAMBO_KERNEL_GEMV, 12, 3), (_lib.MAMBO_KERNEL_GEMV, 16, 4)])
-def test_linear_all_warp_stage_configs(cuda_device, kind, warps, stages):
-    raw, _, xq, xs, ref = _linear_case(cuda_device, 8, 1024, 4096, seed=77)
+@pytest.mark.parametrize("kind,warps,stages,ctas,prefetch", [
+    (_lib.MAMBO_KERNEL_GEMV_SYNC, 4, 3, 1, 0), (_lib.MAMBO_KERNEL_GEMV_SYNC, 16, 3, 1, 0),
+    (_lib.MAMBO_KERNEL_GEMV_SYNC, 12, 6, 1, 0), (_lib.MAMBO_KERNEL_GEMV, 8, 2, 1, 0), (_lib.MAMBO_KERNEL_GEMV, 16, 3, 1, 8),
+    (_lib.MAMBO_KERNEL_GEMV, 8, 3, 1, 0), (_lib.MAMBO_KERNEL_GEMV, 16, 4, 1, 4), (_lib.MAMBO_KERNEL_GEMV, 8, 8, 1, 2)])
+@pytest.mark.parametrize("m", [8, 16])
+def test_linear_all_warp_stage_configs(cuda_device, kind, warps, stages, ctas, prefetch, m):
+    raw, _, xq, xs, ref = _linear_case(cuda_device, m, 1024, 4096, seed=77)
     fields = gpu_weight(raw, cuda_device)
-    cfg = {"kernel": kind, "warps": warps, "stages": stages, "ctas_per_sm": 1, "split": 0}
+    cfg = {"kernel": kind, "warps": warps, "stages": stages, "ctas_per_sm": ctas, "split": 0, "prefetch": prefetch}
     out = launch_iq3_s_fp8_matmul(torch.from_numpy(xq).to(cuda_device), torch.from_numpy(xs).to(cuda_device),
                                   fields, config=cfg)
     assert O.relative_frobenius(to_np(out), ref) < ORACLE_FROB_TOL
@@ -243,11 +245,30 @@ def test_deterministic_and_workspace_reusable(cuda_device):
 
 
 def test_config_that_does_not_fit_is_a_value_error(cuda_device):
-    raw, _, xq, xs, _ = _linear_case(cuda_device, 8, 256, 512, seed=3)
+    raw, _, xq, xs, _ = _linear_case(cuda_device, 32, 256, 512, seed=3)
     fields = gpu_weight(raw, cuda_device)
     with pytest.raises(ValueError):
         launch_iq3_s_fp8_matmul(torch.from_numpy(xq).to(cuda_device), torch.from_numpy(xs).to(cuda_device), fields,
-                                config={"kernel": _lib.MAMBO_KERNEL_GEMV, "warps": 8, "stages": 6})
+                                config={"kernel": _lib.MAMBO_KERNEL_GEMV, "warps": 8, "stages": 8})
+
+
+@pytest.mark.parametrize("m", [5, 13])
+@pytest.mark.parametrize("which", ["values", "scales", "both"])
+def test_unaligned_activation_rows_match_oracle(cuda_device, m, which):
+    """Activations at odd addresses: the tcgen05 path copies them to 16-byte aligned rows first."""
+    raw, _, xq, xs, ref = _linear_case(cuda_device, m, 512, 1024, seed=31 + m)
+    fields = gpu_weight(raw, cuda_device)
+
+    def odd(a):
+        buf = torch.empty(a.size + 1, dtype=torch.uint8, device=cuda_device)
+        view = buf[1:].view(a.shape)
+        view.copy_(torch.from_numpy(a).to(cuda_device))
+        return view
+
+    q = odd(xq) if which in ("values", "both") else torch.from_numpy(xq).to(cuda_device)
+    sc = odd(xs) if which in ("scales", "both") else torch.from_numpy(xs).to(cuda_device)
+    out = launch_iq3_s_fp8_matmul(q, sc, fields)
+    assert O.relative_frobenius(to_np(out), ref) < ORACLE_FROB_TOL
 
 
 def test_errors_match_reference(cuda_device):
