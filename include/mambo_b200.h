@@ -61,7 +61,13 @@ typedef struct MamboIQ3SWeight {
   const void* scales; /* uint8   [B, N, 4]    8 packed 4-bit group scales */
   int64_t n_rows;     /* N */
   int64_t n_blocks;   /* B */
+  const void* packed; /* optional tile-major copy made by mambo_iq3s_pack (NULL = none): the
+                         tcgen05 GEMV then fetches a work unit with one copy instead of five */
 } MamboIQ3SWeight;
+
+/* Rows per tile of the packed layout and bytes per (tile, K block) record. */
+#define MAMBO_IQ3S_TILE_ROWS 128
+#define MAMBO_IQ3S_RECORD_BYTES 14080
 
 /* Launch configuration of the linear kernels (NULL = tuned default for the shape). */
 typedef struct MamboLinearConfig {
@@ -100,6 +106,21 @@ MAMBO_API int mambo_device_check(void);
 MAMBO_API int mambo_iq3s_prepare(const uint8_t* raw, int64_t n_rows, int64_t n_blocks, int64_t stride_row, int64_t stride_block,
                        int64_t stride_byte, void* d, void* qs, void* qh, void* signs, void* scales,
                        mambo_stream_t stream);
+
+/*
+ * Packed weight layout (no counterpart in the reference; an addition for the
+ * tcgen05 GEMV). Records of MAMBO_IQ3S_RECORD_BYTES, one per (128-row tile t,
+ * K block b), at ((t * B) + b) * MAMBO_IQ3S_RECORD_BYTES, each holding the
+ * tile's fields back to back, chunk-major so that consecutive rows' bytes are
+ * adjacent: qs [4][128][16 B] (16-byte chunk, row), signs [2][128][16 B],
+ * qh [2][128][4 B], d [128] fp16, scales [128][4 B]; rows at or past N are zero. A run of work
+ * units (consecutive K blocks of one tile, then the next tile) is one
+ * contiguous range. mambo_iq3s_packed_bytes gives the size of the buffer and
+ * mambo_iq3s_pack fills it from prepared SoA fields (N % 8 == 0; 16-byte
+ * aligned fields and buffer). The SoA fields stay valid and unchanged.
+ */
+MAMBO_API size_t mambo_iq3s_packed_bytes(int64_t n_rows, int64_t n_blocks);
+MAMBO_API int mambo_iq3s_pack(const MamboIQ3SWeight* w, void* packed, mambo_stream_t stream);
 
 /*
  * Standalone decoder: values u8 [N, B*256] signed E4M3 bytes, scales f32 [N, B*8] = d*(1+2*nibble).

@@ -38,6 +38,8 @@ EXPORTED_SYMBOLS = (
     "mambo_last_error",
     "mambo_device_check",
     "mambo_iq3s_prepare",
+    "mambo_iq3s_packed_bytes",
+    "mambo_iq3s_pack",
     "mambo_iq3s_decode",
     "mambo_quantize_mxfp8",
     "mambo_iq3s_linear",
@@ -61,6 +63,7 @@ class MamboIQ3SWeight(ctypes.Structure):
         ("scales", ctypes.c_void_p),
         ("n_rows", ctypes.c_int64),
         ("n_blocks", ctypes.c_int64),
+        ("packed", ctypes.c_void_p),
     ]
 
 
@@ -123,6 +126,8 @@ def load() -> ctypes.CDLL:
             "mambo_last_error": ([ctypes.c_char_p, ctypes.c_size_t], i32),
             "mambo_device_check": ([], i32),
             "mambo_iq3s_prepare": ([vp, i64, i64, i64, i64, i64, vp, vp, vp, vp, vp, vp], i32),
+            "mambo_iq3s_packed_bytes": ([i64, i64], ctypes.c_size_t),
+            "mambo_iq3s_pack": ([ctypes.POINTER(MamboIQ3SWeight), vp, vp], i32),
             "mambo_iq3s_decode": ([ctypes.POINTER(MamboIQ3SWeight), vp, vp, vp, vp], i32),
             "mambo_quantize_mxfp8": ([vp, i32, i64, i64, i64, vp, i64, vp, i64, i32, vp], i32),
             "mambo_iq3s_linear": (

@@ -160,18 +160,20 @@ constexpr int kSmemOptinDefault = 232448;
 
 int kernel_of(const MamboLinearConfig& c) { return c.kernel == MAMBO_KERNEL_AUTO ? MAMBO_KERNEL_GEMV : c.kernel; }
 
+// Shared memory of a configuration (for MAMBO_KERNEL_GEMV without the cluster
+// partials, which the plan sizes to what is left).
 uint32_t config_smem(const MamboLinearConfig& c, int nt, int64_t b) {
   if (kernel_of(c) == MAMBO_KERNEL_GEMV_SYNC) return gemv_smem_bytes_host(c.warps * 16, nt, c.stages, (int)b);
-  return gemv_tm_smem_bytes(nt, c.stages);
+  return gemv_tm_smem_bytes(nt, c.stages, 1);
 }
 
-void default_config(int64_t m, int64_t n, int64_t b, MamboLinearConfig* cfg, int smem_optin) {
-  (void)n;
+void default_config(int64_t m, int64_t n, int64_t b, MamboLinearConfig* cfg, int smem_optin, int sms) {
   std::memset(cfg, 0, sizeof(*cfg));
   cfg->kernel = MAMBO_KERNEL_GEMV;
   cfg->warps = 8;
   cfg->ctas_per_sm = 1;
-  cfg->split = 0;
+  // Cluster K-split while every row tile gets its own CTAs; stream-K beyond that.
+  cfg->split = (n + 127) / 128 <= (sms > 0 ? sms : 148) ? 2 : 0;
   cfg->prefetch = 4;
   // Deepest stage ring (up to 6) that fits next to the codebook.
   const int nt = gemv_nt_for(m < 32 ? m : 32);
@@ -193,6 +195,7 @@ int validate_config(const MamboLinearConfig* cfg, int64_t m, int64_t b, const De
     if (cfg->warps != 8 && cfg->warps != 16) return fail(MAMBO_EINVAL, "decoder warps must be 8 or 16");
     if (cfg->ctas_per_sm < 0 || cfg->ctas_per_sm > 1) return fail(MAMBO_EINVAL, "ctas_per_sm must be 0 or 1");
     if (cfg->prefetch < 0 || cfg->prefetch > 64) return fail(MAMBO_EINVAL, "prefetch must be in [0, 64]");
+    if (cfg->split < 0 || cfg->split > 2) return fail(MAMBO_EINVAL, "split must be 0 (stream-K), 1 (row tile per CTA) or 2 (cluster K-split)");
   }
   const uint32_t smem = config_smem(*cfg, gemv_nt_for(m), b);
   if ((int)smem > info.max_smem_optin)
@@ -207,7 +210,7 @@ int validate_config(const MamboLinearConfig* cfg, int64_t m, int64_t b, const De
 constexpr size_t kCounterBytes = 256 * 1024;
 
 struct GemvPlan {
-  int nt, rows, row_tiles, units, grid, counter_slots;
+  int nt, rows, row_tiles, units, grid, counter_slots, kparts;
   size_t counters_bytes, partial_bytes, xcopy_bytes, xscopy_bytes;
 };
 
@@ -215,20 +218,39 @@ size_t align256(size_t v) { return (v + 255) / 256 * 256; }
 // Row stride of activation scales copied for the TMA (a multiple of 16 bytes).
 int64_t xs_copy_stride(int64_t n_blocks) { return (n_blocks * 8 + 15) / 16 * 16; }
 
-GemvPlan plan_gemv(int64_t m_chunk, int64_t n, int64_t b, const MamboLinearConfig& cfg, int sms) {
+// K parts per row tile for the cluster K-split: as many as leave every row
+// tile its own cluster on the SMs (at most 8, the portable cluster size, and
+// one K block each), within shared memory, and with every cluster resident at
+// once.
+int cluster_kparts(int row_tiles, int64_t b, const MamboLinearConfig& cfg, int nt, int sms, int smem_optin) {
+  int kp = row_tiles > 0 ? sms / row_tiles : 1;
+  kp = kp < 1 ? 1 : kp > 8 ? 8 : kp;
+  if (kp > b) kp = (int)b;
+  while (kp > 1 && (int)gemv_tm_smem_bytes(nt, cfg.stages, kp) > smem_optin) --kp;
+  while (kp > 1 && gemv_tm_max_clusters(nt, cfg.warps, cfg.stages, kp) < row_tiles) --kp;
+  return kp;
+}
+
+GemvPlan plan_gemv(int64_t m_chunk, int64_t n, int64_t b, const MamboLinearConfig& cfg, int sms, int smem_optin) {
   GemvPlan P{};
   const bool tc = kernel_of(cfg) == MAMBO_KERNEL_GEMV;
   P.nt = gemv_nt_for(m_chunk);
   P.rows = tc ? 128 : cfg.warps * 16;
   P.row_tiles = (int)((n + P.rows - 1) / P.rows);
   P.units = (int)(P.row_tiles * b);
-  int ctas = sms * (!tc && cfg.ctas_per_sm > 0 ? cfg.ctas_per_sm : 1);
-  if (cfg.split == 1) ctas = P.row_tiles;  // one CTA per row tile, no split-K
-  P.grid = P.units < ctas ? P.units : ctas;
-  if (P.grid < 1) P.grid = 1;
   P.counter_slots = P.row_tiles * (tc ? 4 : cfg.warps);
   P.counters_bytes = kCounterBytes;
-  P.partial_bytes = align256((size_t)P.grid * 2 * P.rows * 8 * P.nt * sizeof(float));
+  if (tc && cfg.split != 0) {
+    // Whole row tiles (split 1) or row tiles split over the CTAs of a cluster (split 2).
+    P.kparts = cfg.split == 2 ? cluster_kparts(P.row_tiles, b, cfg, P.nt, sms, smem_optin) : 1;
+    P.grid = P.row_tiles * P.kparts;
+  } else {
+    int ctas = sms * (!tc && cfg.ctas_per_sm > 0 ? cfg.ctas_per_sm : 1);
+    if (cfg.split == 1) ctas = P.row_tiles;  // one CTA per row tile, no split-K
+    P.grid = P.units < ctas ? P.units : ctas;
+    if (P.grid < 1) P.grid = 1;
+    P.partial_bytes = align256((size_t)P.grid * 2 * P.rows * 8 * P.nt * sizeof(float));
+  }
   // Activations whose rows are not 16-byte aligned are copied here for the TMA.
   P.xcopy_bytes = tc ? align256((size_t)m_chunk * b * 256) : 0;
   P.xscopy_bytes = tc ? align256((size_t)m_chunk * xs_copy_stride(b)) : 0;
@@ -276,6 +298,8 @@ int launch_tc_chunk(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t 
   p.qh = (const uint8_t*)w->qh;
   p.signs = (const uint8_t*)w->signs;
   p.scales = (const uint8_t*)w->scales;
+  p.packed = (const uint8_t*)w->packed;
+  if ((uintptr_t)w->packed % 16) return fail(MAMBO_EINVAL, "the packed weight buffer must be 16-byte aligned");
   p.table = fp8_table;
   p.out = out;
   p.out_bf16 = out_dtype == MAMBO_BF16;
@@ -284,6 +308,7 @@ int launch_tc_chunk(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t 
   p.counters = counters;
   p.stages = c.stages;
   p.prefetch = c.prefetch;
+  p.kparts = P.kparts;
   p.row_tiles = P.row_tiles;
   p.total_units = P.units;
   cudaError_t e = launch_gemv_tm(p, P.nt, c.warps, maps, P.grid, stream);
@@ -359,6 +384,31 @@ int mambo_iq3s_prepare(const uint8_t* raw, int64_t n_rows, int64_t n_blocks, int
   return ok();
 }
 
+size_t mambo_iq3s_packed_bytes(int64_t n_rows, int64_t n_blocks) {
+  if (n_rows < 1 || n_blocks < 1) return 0;
+  return (size_t)((n_rows + MAMBO_IQ3S_TILE_ROWS - 1) / MAMBO_IQ3S_TILE_ROWS) * (size_t)n_blocks *
+         MAMBO_IQ3S_RECORD_BYTES;
+}
+
+int mambo_iq3s_pack(const MamboIQ3SWeight* w, void* packed, mambo_stream_t stream) {
+  if (!w || !packed) return fail(MAMBO_EINVAL, "null pointer");
+  if (!w->d || !w->qs || !w->qh || !w->signs || !w->scales) return fail(MAMBO_EINVAL, "null weight field");
+  if (w->n_rows < 1 || w->n_blocks < 1) return fail(MAMBO_EINVAL, "IQ3_S weight must have positive N and K");
+  if (w->n_rows % 8 != 0) return fail(MAMBO_EINVAL, "the packed layout needs N %% 8 == 0");
+  const uintptr_t ptrs[6] = {(uintptr_t)w->d, (uintptr_t)w->qs, (uintptr_t)w->qh, (uintptr_t)w->signs,
+                             (uintptr_t)w->scales, (uintptr_t)packed};
+  for (uintptr_t a : ptrs)
+    if (a % 16) return fail(MAMBO_EINVAL, "weight fields and the packed buffer must be 16-byte aligned");
+  DeviceInfo info;
+  int st = require_sm100(&info);
+  if (st != MAMBO_OK) return st;
+  PackWeightParams p{(const uint8_t*)w->d, (const uint8_t*)w->qs, (const uint8_t*)w->qh, (const uint8_t*)w->signs,
+                     (const uint8_t*)w->scales, w->n_rows, w->n_blocks, (uint8_t*)packed};
+  cudaError_t e = launch_iq3s_pack(p, info.sms, (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "iq3s_pack");
+  return ok();
+}
+
 int mambo_iq3s_decode(const MamboIQ3SWeight* w, const uint32_t* fp8_table, uint8_t* values, float* scales,
                       mambo_stream_t stream) {
   if (!w || !fp8_table || !values || !scales) return fail(MAMBO_EINVAL, "null pointer");
@@ -396,7 +446,8 @@ int mambo_default_config(int64_t m, int64_t n_rows, int64_t n_blocks, MamboLinea
   int st;
   DeviceInfo info = device_info(&st);
   default_config(m, n_rows, n_blocks, cfg, (st == MAMBO_OK && info.max_smem_optin > 0) ? info.max_smem_optin
-                                                                                        : kSmemOptinDefault);
+                                                                                        : kSmemOptinDefault,
+                 st == MAMBO_OK ? info.sms : 148);
   return ok();
 }
 
@@ -433,10 +484,12 @@ size_t mambo_iq3s_linear_workspace_bytes(int64_t m, int64_t n_rows, int64_t n_bl
   MamboLinearConfig c;
   if (cfg) c = *cfg;
   else default_config(m, n_rows, n_blocks, &c, (st == MAMBO_OK && info.max_smem_optin > 0) ? info.max_smem_optin
-                                                                                          : kSmemOptinDefault);
+                                                                                          : kSmemOptinDefault,
+                      st == MAMBO_OK ? info.sms : 148);
   const int sms = (st == MAMBO_OK && info.sms > 0) ? info.sms : 148;
   const int64_t m_chunk = m < 32 ? m : 32;
-  GemvPlan P = plan_gemv(m_chunk, n_rows, n_blocks, c, sms);
+  GemvPlan P = plan_gemv(m_chunk, n_rows, n_blocks, c, sms,
+                         (st == MAMBO_OK && info.max_smem_optin > 0) ? info.max_smem_optin : kSmemOptinDefault);
   return P.counters_bytes + P.partial_bytes + P.xcopy_bytes + P.xscopy_bytes;
 }
 
@@ -458,7 +511,7 @@ int mambo_iq3s_linear(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_
   int st = require_sm100(&info);
   if (st != MAMBO_OK) return st;
   MamboLinearConfig c;
-  if (cfg) c = *cfg; else default_config(m, w->n_rows, w->n_blocks, &c, info.max_smem_optin);
+  if (cfg) c = *cfg; else default_config(m, w->n_rows, w->n_blocks, &c, info.max_smem_optin, info.sms);
   if (c.kernel == MAMBO_KERNEL_AUTO) c.kernel = MAMBO_KERNEL_GEMV;
   if (c.kernel == MAMBO_KERNEL_GEMV && (w->n_rows % 8 != 0 || c.loader != 0)) c.kernel = MAMBO_KERNEL_GEMV_SYNC;
   if (c.kernel == MAMBO_KERNEL_GEMV_SYNC && c.warps == 0) c.warps = 8;
@@ -470,7 +523,7 @@ int mambo_iq3s_linear(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_
   const bool tc = kernel_of(c) == MAMBO_KERNEL_GEMV;
   for (int64_t m0 = 0; m0 < m; m0 += m_chunk_max) {
     const int64_t mc = (m - m0) < m_chunk_max ? (m - m0) : m_chunk_max;
-    GemvPlan P = plan_gemv(mc, w->n_rows, w->n_blocks, c, info.sms);
+    GemvPlan P = plan_gemv(mc, w->n_rows, w->n_blocks, c, info.sms, info.max_smem_optin);
     if ((size_t)P.counter_slots * sizeof(int) > kCounterBytes)
       return fail(MAMBO_EINVAL, "N=%lld needs more split-K counters than the workspace holds", (long long)w->n_rows);
     const size_t need = P.counters_bytes + P.partial_bytes + P.xcopy_bytes + P.xscopy_bytes;
@@ -593,7 +646,7 @@ extern "C" int mambo_iq3s_linear_noalloc(const uint8_t* xq, int64_t ldxq, const 
   if (st != MAMBO_OK) return st;
   const int64_t m_chunk = m < kStaticChunk ? m : kStaticChunk;
   MamboLinearConfig c;
-  if (cfg) c = *cfg; else default_config(m_chunk, w->n_rows, w->n_blocks, &c, info.max_smem_optin);
+  if (cfg) c = *cfg; else default_config(m_chunk, w->n_rows, w->n_blocks, &c, info.max_smem_optin, info.sms);
   if (c.kernel == MAMBO_KERNEL_AUTO) c.kernel = MAMBO_KERNEL_GEMV;
   if (c.kernel != MAMBO_KERNEL_GEMV || c.loader != 0)
     return fail(MAMBO_EINVAL, "mambo_iq3s_linear_noalloc runs the tcgen05 GEMV (MAMBO_KERNEL_GEMV, loader 0) only");
@@ -601,7 +654,7 @@ extern "C" int mambo_iq3s_linear_noalloc(const uint8_t* xq, int64_t ldxq, const 
   if (st != MAMBO_OK) return st;
 
   const int sms = info.sms < kStaticMaxCtas ? info.sms : kStaticMaxCtas;
-  const GemvPlan P = plan_gemv(m_chunk, w->n_rows, w->n_blocks, c, sms);
+  const GemvPlan P = plan_gemv(m_chunk, w->n_rows, w->n_blocks, c, sms, info.max_smem_optin);
   const size_t counter_bytes = (size_t)P.counter_slots * sizeof(int);
   if (counter_bytes > kStaticCounterBytes)
     return fail(MAMBO_EINVAL, "N=%lld exceeds the static-scratch limit of mambo_iq3s_linear_noalloc (N <= %zu)",

@@ -97,6 +97,18 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parit
   return ok != 0;
 }
 
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Waits for the phase with the given parity to complete. Gives up after
 // g_wait_limit_ns (or at once when another wait of this launch already gave
 // up), records the timeout and returns false.
@@ -104,13 +116,59 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long limit = g_wait_limit_ns;
   const unsigned long long t0 = globaltimer_ns();
-  for (;;) {
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+    // Back off between polls: a waiting warp should not take issue slots
+    // from the warps doing the work.
+    __nanosleep(64);
+    if ((i & 15u) == 0 && (*(volatile int*)&g_device_status.code != 0 || globaltimer_ns() - t0 > limit)) {
+      record_timeout(site);
+      return false;
+    }
+  }
+}
+
+// As mbar_wait_bounded, for a barrier that other CTAs of the cluster arrive on
+// (acquire at cluster scope).
+__device__ __forceinline__ bool mbar_wait_cluster_bounded(uint32_t bar, uint32_t parity, int site) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const unsigned long long limit = g_wait_limit_ns;
+  const unsigned long long t0 = globaltimer_ns();
+  for (;;) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    __nanosleep(200);
     if (*(volatile int*)&g_device_status.code != 0 || globaltimer_ns() - t0 > limit) {
       record_timeout(site);
       return false;
     }
   }
+}
+
+// ---------------------------------------------------------------------------
+// Thread-block clusters: rank, shared-memory addresses of another CTA of the
+// cluster, stores and mbarrier arrivals there, cluster-wide barrier.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, float a, float b, float c, float d) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+// Arrival (release at cluster scope) on an mbarrier of another CTA of the cluster.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t remote_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar) : "memory");
+}
+// All threads of all CTAs of the cluster (none may have exited).
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ void fence_barrier_init() {
@@ -195,6 +253,12 @@ __device__ __forceinline__ void tma_prefetch_l2_3d(const CUtensorMap* map, int32
                    reinterpret_cast<uint64_t>(map)),
                "r"(c0), "r"(c1), "r"(c2)
                : "memory");
+}
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* addr) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+  return v;
 }
 
 // Release/acquire counter increment at GPU scope (orders this warp's earlier

@@ -27,6 +27,10 @@
 //    partials of its lane with tcgen05.ld, applies 2^e * d*(1+2*nibble) and
 //    accumulates in FP32 registers; finished rows go to the output or to the
 //    deterministic split-K reduction (acq_rel counter, CTA-ordered sum).
+#include <map>
+#include <mutex>
+#include <tuple>
+
 #include "kernels.cuh"
 #include "tcgen05.cuh"
 
@@ -41,6 +45,7 @@ constexpr int kMaxStagesTm = 8;
 constexpr int kRing = 3;  // decoded units in flight: A operands in TMEM, epilogue data in shared memory
 constexpr uint32_t kBarBytes = 320;
 constexpr uint32_t kTableStageBytes = 512 * 4;  // the codebook as read from global memory
+constexpr uint32_t kRecordBytes = 14080;         // one (128-row tile, K block) of every field
 
 // Warps: producer, MMA, decoders, 4 epilogue, scale.
 __host__ __device__ constexpr int tm_threads(int dec_warps) { return (2 + dec_warps + kEpiWarps + 1) * 32; }
@@ -78,9 +83,11 @@ __host__ __device__ inline TmLayout tm_layout(int nt) {
   return L;
 }
 
-__host__ __device__ inline uint32_t tm_smem_bytes(int nt, int stages) {
+// kparts > 1: rank 0 of each cluster also holds the other ranks' partials.
+__host__ __device__ inline uint32_t tm_smem_bytes(int nt, int stages, int kparts) {
   const TmLayout L = tm_layout(nt);
-  return kTableBytes + 1024 + stages * L.stage + kRing * L.aux + kTableStageBytes + kBarBytes;
+  const uint32_t cpart = kparts > 1 ? (uint32_t)(kparts - 1) * kRows * 8u * nt * 4u : 0u;
+  return kTableBytes + 1024 + stages * L.stage + kRing * L.aux + kTableStageBytes + kBarBytes + cpart;
 }
 
 __device__ __forceinline__ int unit_begin_tm(int cta, int grid, int units) {
@@ -97,6 +104,56 @@ __device__ __forceinline__ void store_out_tm(const GemvTmParams& p, int row, int
     } else {
       reinterpret_cast<float*>(p.out)[(int64_t)tok * p.ldo + row] = v;
     }
+  }
+}
+
+// Sums the partials of one weight row (local row rl of tile rt) over the
+// contributing CTAs in CTA order and stores it; the partials of CTA `self`
+// come from `acc` (its registers) instead of memory. Loads for several
+// contributors are in flight together.
+template <int TOK>
+__device__ __forceinline__ void sum_partials(const GemvTmParams& p, int rt, int rl, int row, int self, int c_first,
+                                             int c_last, const float (&acc)[TOK]) {
+  const int grid = gridDim.x;
+#pragma unroll
+  for (int t0 = 0; t0 < TOK; t0 += 8) {
+    float sum[8];
+#pragma unroll
+    for (int t = 0; t < 8; ++t) sum[t] = 0.f;
+    constexpr int kB = TOK <= 8 ? 4 : 2;  // contributors whose loads are in flight together
+#pragma unroll 1
+    for (int c0 = c_first; c0 <= c_last; c0 += kB) {
+      float4 v[kB][2];
+#pragma unroll
+      for (int j = 0; j < kB; ++j) {
+        const int c = c0 + j;
+        if (c <= c_last && c != self) {
+          const int cs = (rt == unit_begin_tm(c, grid, p.total_units) / p.n_blocks) ? 0 : 1;
+          const float4* src = reinterpret_cast<const float4*>(p.partials + ((size_t)(c * 2 + cs) * 128 + rl) * TOK + t0);
+          v[j][0] = __ldcg(src);
+          v[j][1] = __ldcg(src + 1);
+        } else {
+          float x[8];
+#pragma unroll
+          for (int t = 0; t < 8; ++t) x[t] = 0.f;
+          if (c == self) {
+#pragma unroll
+            for (int t = 0; t < 8; ++t) x[t] = acc[t0 + t];
+          }
+          v[j][0] = make_float4(x[0], x[1], x[2], x[3]);
+          v[j][1] = make_float4(x[4], x[5], x[6], x[7]);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kB; ++j) {
+        if (c0 + j <= c_last) {
+          sum[0] += v[j][0].x; sum[1] += v[j][0].y; sum[2] += v[j][0].z; sum[3] += v[j][0].w;
+          sum[4] += v[j][1].x; sum[5] += v[j][1].y; sum[6] += v[j][1].z; sum[7] += v[j][1].w;
+        }
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < 8; ++t) store_out_tm(p, row, t0 + t, sum[t]);
   }
 }
 
@@ -175,22 +232,41 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
   uint8_t* aux0 = st0 + (size_t)p.stages * L.stage;
   uint32_t* tstage = reinterpret_cast<uint32_t*>(aux0 + kRing * L.aux);
   uint64_t* bars = reinterpret_cast<uint64_t*>(aux0 + kRing * L.aux + kTableStageBytes);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * kMaxStagesTm + 3 * kRing + 3);
+  float* cpart = reinterpret_cast<float*>(aux0 + kRing * L.aux + kTableStageBytes + kBarBytes);  // cluster partials
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * kMaxStagesTm + 2 * kRing + 4);  // after cred
   const uint32_t bar0 = smem_u32(bars);
   // Barriers: per stage wfull (weights landed), xfull (activations landed),
-  // empty (stage consumed); per ring slot afull (A decoded, row data written),
-  // sfull (scales converted), efree (epilogue done with the slot); per D
-  // buffer mdone (MMAs complete); edone (epilogue finished).
+  // empty (stage consumed); per ring slot afull (A decoded and the epilogue's
+  // row data and scales written: decoders + scale warp), efree (epilogue done
+  // with the slot); per D buffer mdone (MMAs complete); edone (epilogue finished);
+  // cred (cluster K-split: the other CTAs of the cluster have written their
+  // partials into this CTA's shared memory; used in the cluster's rank 0).
   const uint32_t kWfull = bar0, kXfull = bar0 + 8 * kMaxStagesTm, kEmpty = bar0 + 16 * kMaxStagesTm;
-  const uint32_t kAfull = bar0 + 24 * kMaxStagesTm, kSfull = kAfull + 8 * kRing, kEfree = kSfull + 8 * kRing;
-  const uint32_t kMdone = kEfree + 8 * kRing, kEdone = kMdone + 16;
+  const uint32_t kAfull = bar0 + 24 * kMaxStagesTm, kEfree = kAfull + 8 * kRing;
+  const uint32_t kMdone = kEfree + 8 * kRing, kEdone = kMdone + 16, kCred = kEdone + 8;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int u0 = unit_begin_tm(blockIdx.x, gridDim.x, p.total_units);
-  const int u1 = unit_begin_tm(blockIdx.x + 1, gridDim.x, p.total_units);
+  // Work range: with kparts > 0 each row tile is split into kparts K ranges,
+  // one per CTA of a cluster (rank = K part); otherwise a stream-K range.
+  int u0, u1;
+  if (p.kparts > 0) {
+    const int t = blockIdx.x / p.kparts, k = blockIdx.x % p.kparts;
+    u0 = t * p.n_blocks + (int)((int64_t)k * p.n_blocks / p.kparts);
+    u1 = t * p.n_blocks + (int)((int64_t)(k + 1) * p.n_blocks / p.kparts);
+  } else {
+    u0 = unit_begin_tm(blockIdx.x, gridDim.x, p.total_units);
+    u1 = unit_begin_tm(blockIdx.x + 1, gridDim.x, p.total_units);
+  }
   const int n_units = u1 - u0;
   const int S = p.stages;
 
+  // Decoder threads fetch the 2 KB codebook now, so that its global-memory
+  // latency overlaps the barrier and TMEM set-up below.
+  uint32_t tw[512 / (kDecWarps * 32)];
+  if (warp >= 2 && warp < kEpiWarp0) {
+#pragma unroll
+    for (int j = 0; j < 512 / (kDecWarps * 32); ++j) tw[j] = __ldg(p.table + (threadIdx.x - 64) + j * kDecWarps * 32);
+  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(kWfull + 8 * s, 1);
@@ -198,12 +274,12 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
       mbar_init(kEmpty + 8 * s, kDecWarps + 2);  // decoders, MMA commit, scale warp
     }
     for (int r = 0; r < kRing; ++r) {
-      mbar_init(kAfull + 8 * r, kDecWarps);
-      mbar_init(kSfull + 8 * r, 1);
+      mbar_init(kAfull + 8 * r, kDecWarps + 1);
       mbar_init(kEfree + 8 * r, kEpiWarps);
     }
     for (int b = 0; b < 2; ++b) mbar_init(kMdone + 8 * b, 1);
     mbar_init(kEdone, kEpiWarps);
+    mbar_init(kCred, p.kparts > 1 ? (p.kparts - 1) * kEpiWarps : 1);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -212,6 +288,7 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
   }
   tc::fence_before_sync();
   __syncthreads();
+  if (p.kparts > 1) cluster_sync_all();  // every CTA's barriers initialized before any remote arrival
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
 
@@ -238,12 +315,21 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
     auto issue_weights = [&](int it) {
       const int s = it % S;
       const uint32_t full = kWfull + 8 * s;
-      uint32_t rows;
-      size_t base;
-      tile(u0 + it, rows, base);
-      if (lane == 0) mbar_arrive_expect_tx(full, rows * 110u);
-      __syncwarp();
-      if (lane < 5) bulk_load_hint(smem_u32(st0 + (size_t)s * L.stage) + foff, fptr + base * fbpr, rows * fbpr, full, policy);
+      const uint32_t st = smem_u32(st0 + (size_t)s * L.stage);
+      if (p.packed) {
+        // Tile-major records have the stage's layout: one copy per unit.
+        if (lane == 0) {
+          mbar_arrive_expect_tx(full, (uint32_t)kRecordBytes);
+          bulk_load_hint(st, p.packed + (size_t)(u0 + it) * kRecordBytes, kRecordBytes, full, policy);
+        }
+      } else {
+        uint32_t rows;
+        size_t base;
+        tile(u0 + it, rows, base);
+        if (lane == 0) mbar_arrive_expect_tx(full, rows * 110u);
+        __syncwarp();
+        if (lane < 5) bulk_load_hint(st + foff, fptr + base * fbpr, rows * fbpr, full, policy);
+      }
       __syncwarp();
     };
     auto issue_acts = [&](int it) {
@@ -256,10 +342,14 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
       __syncwarp();
     };
     auto prefetch = [&](int it) {
-      uint32_t rows;
-      size_t base;
-      tile(u0 + it, rows, base);
-      if (lane < 5) bulk_prefetch_l2(fptr + base * fbpr, rows * fbpr);
+      if (p.packed) {
+        if (lane == 0) bulk_prefetch_l2(p.packed + (size_t)(u0 + it) * kRecordBytes, kRecordBytes);
+      } else {
+        uint32_t rows;
+        size_t base;
+        tile(u0 + it, rows, base);
+        if (lane < 5) bulk_prefetch_l2(fptr + base * fbpr, rows * fbpr);
+      }
       __syncwarp();
     };
     const int pre = min(S, n_units);
@@ -333,7 +423,7 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
       }
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(kSfull + 8 * r);
+        mbar_arrive(kAfull + 8 * r);
         mbar_arrive(kEmpty + 8 * s);
       }
       __syncwarp();
@@ -349,9 +439,10 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
     const int rl = 32 * q + lane;  // weight row within the tile = TMEM lane
     const int nthreads = kDecWarps * 32;
     const int tid = threadIdx.x - 64;
-    // Codebook: stage the 2 KB read from global memory, then expand to the
+    // Codebook: stage the 2 KB read at kernel entry, then expand to the
     // lane-private copy, four lanes' copies (16 contiguous bytes) per store.
-    for (int i = tid; i < 512; i += nthreads) tstage[i] = __ldg(p.table + i);
+#pragma unroll
+    for (int j = 0; j < 512 / (kDecWarps * 32); ++j) tstage[tid + j * nthreads] = tw[j];
     asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
     for (int i = tid; i < 512 * 8; i += nthreads) {
       const uint32_t code = i >> 3, l0 = (i & 7) * 4, e = tstage[code];
@@ -362,6 +453,23 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
 
     const uint32_t l4 = (uint32_t)(lane << 2) * 0x01010101u;
     const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(part * kGroups * 8);
+    // Offsets of this thread's raw bytes in a stage. Packed records are
+    // chunk-major ([16-byte chunk][row][16 bytes] for qs and signs, [4-byte
+    // column][row][4 bytes] for qh), so the 8 rows of a load phase read
+    // consecutive bytes; bulk-copied SoA fields land row-major.
+    const bool cm = p.packed != nullptr;
+    uint32_t off_q0, off_q1, off_sg, off_qh;
+    if constexpr (kParts == 2) {
+      off_q0 = L.qs + (cm ? (2 * part) * 2048 + rl * 16 : rl * 64 + 32 * part);
+      off_q1 = off_q0 + (cm ? 2048 : 16);
+      off_sg = L.signs + (cm ? part * 2048 + rl * 16 : rl * 32 + 16 * part);
+      off_qh = L.qh + (cm ? part * 512 + rl * 4 : rl * 8 + 4 * part);
+    } else {
+      off_q0 = L.qs + (cm ? part * 2048 + rl * 16 : rl * 64 + 16 * part);
+      off_q1 = off_q0;
+      off_sg = L.signs + (cm ? (part >> 1) * 2048 + rl * 16 + (part & 1) * 8 : rl * 32 + 8 * part);
+      off_qh = L.qh + (cm ? (part >> 1) * 512 + rl * 4 + (part & 1) * 2 : rl * 8 + 2 * part);
+    }
     for (int it = 0; it < n_units; ++it) {
       const int s = it % S, r = it % kRing;
       // A ring slot r is free once the epilogue is done with unit it - kRing.
@@ -375,19 +483,19 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
       const uint8_t* st = st0 + (size_t)s * L.stage;
       uint32_t qw[2 * kGroups], sw[kGroups], hw;
       if constexpr (kParts == 2) {
-        const uint4 a = *reinterpret_cast<const uint4*>(st + L.qs + rl * 64 + 32 * part);
-        const uint4 c = *reinterpret_cast<const uint4*>(st + L.qs + rl * 64 + 32 * part + 16);
-        const uint4 g = *reinterpret_cast<const uint4*>(st + L.signs + rl * 32 + 16 * part);
+        const uint4 a = *reinterpret_cast<const uint4*>(st + off_q0);
+        const uint4 c = *reinterpret_cast<const uint4*>(st + off_q1);
+        const uint4 g = *reinterpret_cast<const uint4*>(st + off_sg);
         qw[0] = a.x; qw[1] = a.y; qw[2] = a.z; qw[3] = a.w;
         qw[4] = c.x; qw[5] = c.y; qw[6] = c.z; qw[7] = c.w;
         sw[0] = g.x; sw[1] = g.y; sw[2] = g.z; sw[3] = g.w;
-        hw = *reinterpret_cast<const uint32_t*>(st + L.qh + rl * 8 + 4 * part);
+        hw = *reinterpret_cast<const uint32_t*>(st + off_qh);
       } else {
-        const uint4 a = *reinterpret_cast<const uint4*>(st + L.qs + rl * 64 + 16 * part);
-        const uint2 g = *reinterpret_cast<const uint2*>(st + L.signs + rl * 32 + 8 * part);
+        const uint4 a = *reinterpret_cast<const uint4*>(st + off_q0);
+        const uint2 g = *reinterpret_cast<const uint2*>(st + off_sg);
         qw[0] = a.x; qw[1] = a.y; qw[2] = a.z; qw[3] = a.w;
         sw[0] = g.x; sw[1] = g.y;
-        hw = *reinterpret_cast<const uint16_t*>(st + L.qh + rl * 8 + 2 * part);
+        hw = *reinterpret_cast<const uint16_t*>(st + off_qh);
       }
       if (part == 0) {
         // The row's d and scale nibbles for the epilogue (it forms d * (1 + 2*nibble)).
@@ -429,11 +537,9 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
       const uint32_t mpar = kDBuf == 2 ? ((it >> 1) & 1) : (it & 1);
       bool ok = mbar_try_wait(kMdone + 8 * db, mpar);
       bool ok2 = mbar_try_wait(kAfull + 8 * r, (it / kRing) & 1);
-      bool ok3 = mbar_try_wait(kSfull + 8 * r, (it / kRing) & 1);
-      if (!__all_sync(0xFFFFFFFFu, ok && ok2 && ok3)) {  // slow path, taken by the whole warp
+      if (!__all_sync(0xFFFFFFFFu, ok && ok2)) {  // slow path, taken by the whole warp
         ok = mbar_wait_bounded(kMdone + 8 * db, mpar, kSiteGemvFull);
         ok = ok && mbar_wait_bounded(kAfull + 8 * r, (it / kRing) & 1, kSiteGemvFull);
-        ok = ok && mbar_wait_bounded(kSfull + 8 * r, (it / kRing) & 1, kSiteGemvFull);
         if (!__all_sync(0xFFFFFFFFu, ok)) break;
       }
       tc::fence_after_sync();
@@ -464,9 +570,11 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
                                  dv, dneg);
 #pragma unroll
             for (int t = 0; t < 8; t += 2) {
-              float p0, p1;
-              mul2(p0, p1, c[j][t], c[j][t + 1], xs[g * TOK + t0 + t], xs[g * TOK + t0 + t + 1]);
-              fma2(acc[t0 + t], acc[t0 + t + 1], p0, p1, w, w);
+              if (t0 + t < p.m) {  // tokens past M are padding (warp-uniform branch)
+                float p0, p1;
+                mul2(p0, p1, c[j][t], c[j][t + 1], xs[g * TOK + t0 + t], xs[g * TOK + t0 + t + 1]);
+                fma2(acc[t0 + t], acc[t0 + t + 1], p0, p1, w, w);
+              }
             }
           }
         }
@@ -480,59 +588,58 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
       if (!(kb == p.n_blocks - 1 || u == u1 - 1)) continue;
       const bool full_tile = (seg_begin % p.n_blocks == 0) && (kb == p.n_blocks - 1);
       const int row = rt * kRows + rl;
-      if (full_tile) {
+      if (p.kparts > 1) {
+        // Cluster K-split: ranks 1.. write their partials into rank 0's shared
+        // memory and arrive on its barrier; rank 0 sums in rank order.
+        const uint32_t rank = cluster_ctarank();
+        if (rank != 0) {
+          const uint32_t remote = mapa_shared(smem_u32(cpart) + (((rank - 1) * kRows + rl) * TOK) * 4u, 0);
+#pragma unroll
+          for (int t = 0; t < TOK; t += 4) st_cluster_v4(remote + 4u * t, acc[t], acc[t + 1], acc[t + 2], acc[t + 3]);
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(mapa_shared(kCred, 0));
+          __syncwarp();
+        } else {
+          if (__all_sync(0xFFFFFFFFu, mbar_wait_cluster_bounded(kCred, 0, kSiteGemvFull))) {
+            for (int r = 1; r < p.kparts; ++r) {
+              const float* src = cpart + ((r - 1) * kRows + rl) * TOK;
+#pragma unroll
+              for (int t = 0; t < TOK; ++t) acc[t] += src[t];
+            }
+#pragma unroll
+            for (int t = 0; t < TOK; ++t) store_out_tm(p, row, t, acc[t]);
+          }
+        }
+      } else if (full_tile) {
 #pragma unroll
         for (int t = 0; t < TOK; ++t) store_out_tm(p, row, t, acc[t]);
       } else {
+        // Stream-K: a row tile shared with other CTAs. The segment a CTA
+        // finishes last is usually the last contribution: if every other
+        // contributor has already published, sum at once; otherwise publish,
+        // and the last to arrive sums (in CTA order either way).
         const int cta = blockIdx.x, grid = gridDim.x;
-        const int slot_id = (rt == u0 / p.n_blocks) ? 0 : 1;
-        float* part = p.partials + ((size_t)(cta * 2 + slot_id) * kRows + rl) * TOK;
-#pragma unroll
-        for (int t = 0; t < TOK; t += 4)
-          __stcg(reinterpret_cast<float4*>(part + t), make_float4(acc[t], acc[t + 1], acc[t + 2], acc[t + 3]));
-        __syncwarp();
         const int c_first = cta_of_unit_tm(rt * p.n_blocks, grid, p.total_units);
         const int c_last = cta_of_unit_tm(rt * p.n_blocks + p.n_blocks - 1, grid, p.total_units);
+        const int slot_id = (rt == u0 / p.n_blocks) ? 0 : 1;
+        int* counter = p.counters + (size_t)rt * kEpiWarps + q;
         int last = 0;
-        if (lane == 0) {
-          int* counter = p.counters + (size_t)rt * kEpiWarps + q;
-          last = (atomic_add_acq_rel_gpu(counter, 1) == c_last - c_first);
-          if (last) *counter = 0;  // leave the counter zeroed for the next launch
+        if (u == u1 - 1) {
+          if (lane == 0) last = ld_acquire_gpu(counter) == c_last - c_first;
+          last = __shfl_sync(0xFFFFFFFFu, last, 0);
         }
-        last = __shfl_sync(0xFFFFFFFFu, last, 0);
+        if (!last) {
+          float* part = p.partials + ((size_t)(cta * 2 + slot_id) * kRows + rl) * TOK;
+#pragma unroll
+          for (int t = 0; t < TOK; t += 4)
+            __stcg(reinterpret_cast<float4*>(part + t), make_float4(acc[t], acc[t + 1], acc[t + 2], acc[t + 3]));
+          __syncwarp();
+          if (lane == 0) last = atomic_add_acq_rel_gpu(counter, 1) == c_last - c_first;
+          last = __shfl_sync(0xFFFFFFFFu, last, 0);
+        }
         if (last) {
-          // Sum the contributors' partials in CTA order, 8 tokens at a time.
-          constexpr int kBatch = kDecWarps == 8 && TOK <= 8 ? 4 : 1;
-#pragma unroll 1
-          for (int t0 = 0; t0 < TOK; t0 += 8) {
-            float sum[8];
-#pragma unroll
-            for (int t = 0; t < 8; ++t) sum[t] = 0.f;
-#pragma unroll 1
-            for (int c0 = c_first; c0 <= c_last; c0 += kBatch) {
-              float4 v[kBatch][2];
-#pragma unroll
-              for (int j = 0; j < kBatch; ++j) {
-                const int c = c0 + j;
-                if (c <= c_last) {
-                  const int cs = (rt == unit_begin_tm(c, grid, p.total_units) / p.n_blocks) ? 0 : 1;
-                  const float4* src =
-                      reinterpret_cast<const float4*>(p.partials + ((size_t)(c * 2 + cs) * kRows + rl) * TOK + t0);
-                  v[j][0] = __ldcg(src);
-                  v[j][1] = __ldcg(src + 1);
-                }
-              }
-#pragma unroll
-              for (int j = 0; j < kBatch; ++j) {
-                if (c0 + j <= c_last) {
-                  sum[0] += v[j][0].x; sum[1] += v[j][0].y; sum[2] += v[j][0].z; sum[3] += v[j][0].w;
-                  sum[4] += v[j][1].x; sum[5] += v[j][1].y; sum[6] += v[j][1].z; sum[7] += v[j][1].w;
-                }
-              }
-            }
-#pragma unroll
-            for (int t = 0; t < 8; ++t) store_out_tm(p, row, t0 + t, sum[t]);
-          }
+          if (lane == 0) *counter = 0;  // every contributor has arrived: leave it zeroed for the next launch
+          sum_partials<TOK>(p, rt, rl, row, cta, c_first, c_last, acc);
         }
       }
 #pragma unroll
@@ -548,16 +655,70 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
 // --------------------------------------------------------------------------
 // Host side
 // --------------------------------------------------------------------------
-uint32_t gemv_tm_smem_bytes(int nt, int stages) { return tm_smem_bytes(nt, stages); }
+uint32_t gemv_tm_smem_bytes(int nt, int stages, int kparts) { return tm_smem_bytes(nt, stages, kparts); }
 int gemv_tm_max_stages() { return kMaxStagesTm; }
 
 template <int NT, int kDecWarps>
+static const void* tm_kernel() {
+  return (const void*)iq3s_gemv_tm_kernel<NT, kDecWarps>;
+}
+
+static int query_max_clusters(int nt, int dec_warps, int stages, int kparts);
+
+static const void* tm_kernel_for(int nt, int dec_warps) {
+  if (dec_warps == 16) return nt == 1 ? tm_kernel<1, 16>() : nt == 2 ? tm_kernel<2, 16>() : tm_kernel<4, 16>();
+  return nt == 1 ? tm_kernel<1, 8>() : nt == 2 ? tm_kernel<2, 8>() : tm_kernel<4, 8>();
+}
+
+int gemv_tm_max_clusters(int nt, int dec_warps, int stages, int kparts) {
+  // Cached per (device, configuration): the query runs once.
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int, int, int>, int> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  const auto key = std::make_tuple(dev, nt, dec_warps, stages, kparts);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  const int n = query_max_clusters(nt, dec_warps, stages, kparts);
+  std::lock_guard<std::mutex> lock(mu);
+  cache[key] = n;
+  return n;
+}
+
+static int query_max_clusters(int nt, int dec_warps, int stages, int kparts) {
+  const void* kern = tm_kernel_for(nt, dec_warps);
+  const uint32_t smem = tm_smem_bytes(nt, stages, kparts);
+  if (ensure_smem_attribute(kern, smem) != cudaSuccess) return 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(kparts * 16);
+  cfg.blockDim = dim3(tm_threads(dec_warps));
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)kparts;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+template <int NT, int kDecWarps>
 static cudaError_t launch_gemv_tm_t(const GemvTmParams& p, const GemvTmMaps& maps, int grid, cudaStream_t stream) {
-  const uint32_t smem = tm_smem_bytes(NT, p.stages);
-  const void* kern = (const void*)iq3s_gemv_tm_kernel<NT, kDecWarps>;
+  const uint32_t smem = tm_smem_bytes(NT, p.stages, p.kparts);
+  const void* kern = tm_kernel<NT, kDecWarps>();
   cudaError_t e = ensure_smem_attribute(kern, smem);
   if (e != cudaSuccess) return e;
-  return launch_pdl(kern, dim3(grid), dim3(tm_threads(kDecWarps)), smem, stream, p, maps);
+  return launch_pdl_cluster(kern, dim3(grid), dim3(tm_threads(kDecWarps)), smem, stream, p.kparts > 1 ? p.kparts : 1,
+                            p, maps);
 }
 
 template <int NT>

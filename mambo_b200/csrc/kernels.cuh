@@ -8,24 +8,40 @@ namespace mambo {
 // Sets a kernel's dynamic shared memory limit once per (kernel, device).
 cudaError_t ensure_smem_attribute(const void* kernel, size_t smem_bytes);
 
-// Launches with programmatic stream serialization: the kernel may begin while
-// the previous kernel in the stream finishes, and must call pdl_wait() before
-// touching memory that kernel produces or consumes.
+// Launches with programmatic stream serialization (and, for cluster > 1, in
+// thread-block clusters of `cluster` CTAs along x).
 template <typename... Args>
-cudaError_t launch_pdl(const void* kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
-                       const Args&... args) {
+cudaError_t launch_pdl_cluster(const void* kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, int cluster,
+                               const Args&... args) {
   void* argv[] = {const_cast<void*>(static_cast<const void*>(&args))...};
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  int n = 1;
+  if (cluster > 1) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = (unsigned)cluster;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    n = 2;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = n;
   return cudaLaunchKernelExC(&cfg, kernel, argv);
+}
+
+// Launches with programmatic stream serialization: the kernel may begin while
+// the previous kernel in the stream finishes, and must call pdl_wait() before
+// touching memory that kernel produces or consumes.
+template <typename... Args>
+cudaError_t launch_pdl(const void* kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       const Args&... args) {
+  return launch_pdl_cluster(kernel, grid, block, smem, stream, 1, args...);
 }
 
 struct QuantParams {
@@ -57,6 +73,18 @@ struct DecodeParams {
   float* out_scales;      // [N, B*8]
 };
 cudaError_t launch_iq3s_decode(const DecodeParams& p, int num_sms, cudaStream_t stream);
+
+// SoA fields -> tile-major packed records (see mambo_iq3s_pack).
+struct PackWeightParams {
+  const uint8_t* d;
+  const uint8_t* qs;
+  const uint8_t* qh;
+  const uint8_t* signs;
+  const uint8_t* scales;
+  int64_t n_rows, n_blocks;
+  uint8_t* packed;
+};
+cudaError_t launch_iq3s_pack(const PackWeightParams& p, int num_sms, cudaStream_t stream);
 
 struct GemvParams {
   const uint8_t* xq;
@@ -106,6 +134,7 @@ struct GemvTmParams {
   const uint8_t* qh;
   const uint8_t* signs;
   const uint8_t* scales;
+  const uint8_t* packed;  // tile-major records (one copy per unit), or null: five copies from the fields
   const uint32_t* table;  // uint32[512], E4M3-encoded magnitudes
   void* out;
   int out_bf16;
@@ -114,6 +143,7 @@ struct GemvTmParams {
   int* counters;    // [row_tiles][4], zero between launches
   int stages;
   int prefetch;  // units prefetched into L2 beyond the stage ring
+  int kparts;    // > 0: row tile t is split into kparts K ranges, CTA t*kparts+k in a cluster of kparts; 0: stream-K
   int row_tiles;
   int total_units;
 };
@@ -130,7 +160,9 @@ bool make_gemv_x_map(const uint8_t* xq, int64_t ldxq, int m, int n_blocks, int b
 bool make_gemv_xs_map(const uint8_t* xs, int64_t ldxs, int m, int n_blocks, int box_tokens, CUtensorMap* map);
 cudaError_t launch_gemv_tm(const GemvTmParams& p, int nt, int dec_warps, const GemvTmMaps& maps, int grid,
                            cudaStream_t stream);
-uint32_t gemv_tm_smem_bytes(int nt, int stages);
+uint32_t gemv_tm_smem_bytes(int nt, int stages, int kparts);
+// Clusters of `kparts` CTAs of this configuration that can be resident at once (0 if none / on error).
+int gemv_tm_max_clusters(int nt, int dec_warps, int stages, int kparts);
 int gemv_tm_max_stages();
 
 cudaError_t launch_wait_selftest(unsigned long long limit_ns, cudaStream_t stream);

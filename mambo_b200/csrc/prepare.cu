@@ -40,6 +40,52 @@ cudaError_t launch_iq3s_prepare(const PrepareParams& p, int num_sms, cudaStream_
   return cudaGetLastError();
 }
 
+// One thread per 16-byte chunk of the packed buffer. Record layout (one
+// 128-row tile t, one K block b): qs [4 chunks][128 rows][16 B], signs
+// [2 chunks][128 rows][16 B], qh [2 columns][128 rows][4 B], d [128] fp16,
+// scales [128][4 B]; rows past N are zero (N % 8 == 0, so a chunk never mixes
+// valid and padding rows).
+__global__ void iq3s_pack_kernel(const PackWeightParams p) {
+  constexpr int kChunks = 14080 / 16;
+  const int64_t tiles = (p.n_rows + 127) / 128;
+  const int64_t total = tiles * p.n_blocks * kChunks;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t rec = i / kChunks;
+    const int off = (int)(i - rec * kChunks) * 16;
+    const int64_t t = rec / p.n_blocks, b = rec - t * p.n_blocks;
+    const int64_t row0 = b * p.n_rows + t * 128;  // SoA index of the tile's first row
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (off < 12288) {  // qs or signs: 16 bytes of one row
+      const bool is_qs = off < 8192;
+      const int o = is_qs ? off : off - 8192, c = o / 2048, r = (o % 2048) / 16;
+      if (t * 128 + r < p.n_rows)
+        v = __ldg(reinterpret_cast<const uint4*>((is_qs ? p.qs : p.signs) + (row0 + r) * (is_qs ? 64 : 32) + c * 16));
+    } else if (off < 13312) {  // qh: 4 bytes of 4 consecutive rows
+      const int o = off - 12288, c = o / 512, r = (o % 512) / 4;
+      if (t * 128 + r < p.n_rows) {
+        const uint8_t* src = p.qh + (row0 + r) * 8 + c * 4;
+        v = make_uint4(__ldg(reinterpret_cast<const uint32_t*>(src)), __ldg(reinterpret_cast<const uint32_t*>(src + 8)),
+                       __ldg(reinterpret_cast<const uint32_t*>(src + 16)),
+                       __ldg(reinterpret_cast<const uint32_t*>(src + 24)));
+      }
+    } else {  // d and scales: rows contiguous
+      const bool is_d = off < 13568;
+      const int o = is_d ? off - 13312 : off - 13568, bpr = is_d ? 2 : 4, r = o / bpr;
+      if (t * 128 + r < p.n_rows) v = __ldg(reinterpret_cast<const uint4*>((is_d ? p.d : p.scales) + row0 * bpr + o));
+    }
+    reinterpret_cast<uint4*>(p.packed)[i] = v;
+  }
+}
+
+cudaError_t launch_iq3s_pack(const PackWeightParams& p, int num_sms, cudaStream_t stream) {
+  const int64_t total = (p.n_rows + 127) / 128 * p.n_blocks * (14080 / 16);
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > (int64_t)num_sms * 32) blocks = (int64_t)num_sms * 32;
+  if (blocks < 1) blocks = 1;
+  iq3s_pack_kernel<<<(int)blocks, 256, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
 // One warp per (row, block): lane l decodes codes 2l and 2l+1 (weights 8l..8l+7).
 // Mirrors decode_iq3_s_blocks (src/python/mambo/kernels/iq3_s_fp8.py:202-222).
 __global__ void iq3s_decode_kernel(const DecodeParams p) {

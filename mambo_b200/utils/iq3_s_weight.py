@@ -18,6 +18,7 @@ group of 32 weights uses scale d * (1 + 2 * scale_nibble).
 
 from __future__ import annotations
 
+import dataclasses
 from dataclasses import dataclass
 
 import torch
@@ -39,13 +40,18 @@ class IQ3SFields:
     qh: torch.Tensor
     signs: torch.Tensor
     scales: torch.Tensor
+    # Addition of this build: the same bytes in tile-major records (one copy per
+    # GEMV work unit), made by prepare_iq3_s_fields; None when not built.
+    packed: torch.Tensor | None = None
 
 
-def prepare_iq3_s_fields(iq3_weight, *, stream=None) -> IQ3SFields:
+def prepare_iq3_s_fields(iq3_weight, *, stream=None, packed: bool = True) -> IQ3SFields:
     """Split GGUF uint8 [N,B,110] blocks into aligned SoA fields once (iq3_s_weight.py:25-54).
 
     Accepts any strides and address alignment of the source view. The copy is
-    outside kernel timing.
+    outside kernel timing. With ``packed`` (and N % 8 == 0) it also builds the
+    tile-major copy the tcgen05 GEMV streams with one copy per work unit; that
+    doubles the weight memory.
     """
     raw = _runtime.as_cuda_tensor(iq3_weight)
     if raw.ndim != 3 or raw.dtype != torch.uint8 or raw.shape[2] != 110:
@@ -66,13 +72,28 @@ def prepare_iq3_s_fields(iq3_weight, *, stream=None) -> IQ3SFields:
             ),
             "prepare_iq3_s_fields",
         )
-    return IQ3SFields(
+    fields = IQ3SFields(
         d.view(torch.float16).reshape(blocks, n),
         qs.view(torch.uint32),
         qh.view(torch.uint16),
         signs.view(torch.int32),
         scales.view(torch.uint32).reshape(blocks, n),
     )
+    if packed and n % 8 == 0:
+        fields = pack_iq3_s_fields(fields, stream=stream)
+    return fields
+
+
+def pack_iq3_s_fields(fields: IQ3SFields, *, stream=None) -> IQ3SFields:
+    """Return ``fields`` with the tile-major packed copy built (mambo_iq3s_pack)."""
+    n, blocks = _weight_dimensions(fields)
+    lib = _lib.load()
+    dev = fields.d.device
+    buf = torch.empty(lib.mambo_iq3s_packed_bytes(n, blocks), dtype=torch.uint8, device=dev)
+    w = weight_struct(fields)
+    with torch.cuda.device(dev):
+        _lib.check(lib.mambo_iq3s_pack(w, buf.data_ptr(), _runtime.stream_handle(stream, dev)), "pack_iq3_s_fields")
+    return dataclasses.replace(fields, packed=buf)
 
 
 def _weight_dimensions(iq3_weight: IQ3SFields) -> tuple[int, int]:
@@ -111,6 +132,8 @@ def weight_struct(iq3_weight: IQ3SFields) -> _lib.MamboIQ3SWeight:
     w.d, w.qs, w.qh = iq3_weight.d.data_ptr(), iq3_weight.qs.data_ptr(), iq3_weight.qh.data_ptr()
     w.signs, w.scales = iq3_weight.signs.data_ptr(), iq3_weight.scales.data_ptr()
     w.n_rows, w.n_blocks = n, b
+    packed = getattr(iq3_weight, "packed", None)
+    w.packed = packed.data_ptr() if packed is not None else None
     return w
 
 

@@ -195,8 +195,10 @@ KERNELS = {  # (kernel kind, weight loader)
 @pytest.mark.parametrize("m,n,k", [(1, 256, 512), (2, 384, 1024), (8, 1024, 2048), (13, 512, 768), (32, 640, 1536),
                                    (40, 128, 256), (17, 136, 512)])
 @pytest.mark.parametrize("kernel", sorted(KERNELS))
-@pytest.mark.parametrize("split", [0, 1])
+@pytest.mark.parametrize("split", [0, 1, 2])
 def test_linear_kernels_and_splits_match_oracle(cuda_device, m, n, k, kernel, split):
+    if split == 2 and not KERNELS[kernel][0] == _lib.MAMBO_KERNEL_GEMV:
+        pytest.skip("cluster K-split is a tcgen05 GEMV mode")
     raw, _, xq, xs, ref = _linear_case(cuda_device, m, n, k, seed=1000 + m + n)
     fields = gpu_weight(raw, cuda_device)
     kind, loader, *warps = KERNELS[kernel]
@@ -269,6 +271,31 @@ def test_unaligned_activation_rows_match_oracle(cuda_device, m, which):
     sc = odd(xs) if which in ("scales", "both") else torch.from_numpy(xs).to(cuda_device)
     out = launch_iq3_s_fp8_matmul(q, sc, fields)
     assert O.relative_frobenius(to_np(out), ref) < ORACLE_FROB_TOL
+
+
+@pytest.mark.parametrize("m,n,k", [(8, 520, 768), (3, 1024, 2048), (13, 136, 512)])
+def test_packed_layout_and_results_match_soa(cuda_device, m, n, k):
+    """Tile-major packed records hold the raw block bytes; both weight paths give identical outputs."""
+    raw, _, xq, xs, ref = _linear_case(cuda_device, m, n, k, seed=55 + n)
+    soa = prepare_iq3_s_fields(torch.from_numpy(raw).to(cuda_device), packed=False)
+    packed = prepare_iq3_s_fields(torch.from_numpy(raw).to(cuda_device))
+    assert soa.packed is None and packed.packed is not None
+    blocks, tiles = k // 256, (n + 127) // 128
+    rec = to_np(packed.packed).reshape(tiles, blocks, 14080)
+    pad = np.zeros((tiles * 128, blocks, 110), dtype=np.uint8)
+    pad[:n] = raw
+    for t in range(tiles):
+        rows = pad[t * 128:(t + 1) * 128].transpose(1, 0, 2)  # [B, 128, 110]
+        chunk_major = lambda f, w: f.reshape(blocks, 128, -1, w).transpose(0, 2, 1, 3).reshape(blocks, -1)  # noqa: E731
+        expect = np.concatenate([chunk_major(rows[:, :, 2:66], 16), chunk_major(rows[:, :, 74:106], 16),
+                                 chunk_major(rows[:, :, 66:74], 4), rows[:, :, 0:2].reshape(blocks, -1),
+                                 rows[:, :, 106:110].reshape(blocks, -1)], axis=1)
+        np.testing.assert_array_equal(rec[t], expect, err_msg=f"tile {t}")
+    xq_t, xs_t = torch.from_numpy(xq).to(cuda_device), torch.from_numpy(xs).to(cuda_device)
+    a = launch_iq3_s_fp8_matmul(xq_t, xs_t, soa)
+    b = launch_iq3_s_fp8_matmul(xq_t, xs_t, packed)
+    assert torch.equal(a, b)
+    assert O.relative_frobenius(to_np(b), ref) < ORACLE_FROB_TOL
 
 
 def test_errors_match_reference(cuda_device):
