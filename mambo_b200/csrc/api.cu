@@ -175,9 +175,9 @@ void default_config(int64_t m, int64_t n, int64_t b, MamboLinearConfig* cfg, int
   // Cluster K-split while every row tile gets its own CTAs; stream-K beyond that.
   cfg->split = (n + 127) / 128 <= (sms > 0 ? sms : 148) ? 2 : 0;
   cfg->prefetch = 4;
-  // Deepest stage ring (up to 6) that fits next to the codebook.
+  // Deepest weight-stage ring (up to 8) that fits next to the codebook.
   const int nt = gemv_nt_for(m < 32 ? m : 32);
-  cfg->stages = 6;
+  cfg->stages = 8;
   while (cfg->stages > 2 && (int)config_smem(*cfg, nt, b) > smem_optin) --cfg->stages;
 }
 

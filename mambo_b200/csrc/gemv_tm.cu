@@ -2,31 +2,40 @@
 // (tcgen05, sm_100a), with the decoded weight operand kept in tensor memory.
 //
 // Same arithmetic as the reference (src/python/mambo/kernels/iq3_s_fp8.py:279-333):
-// per 32-weight group g, P_g = sum_k E4M3(w) * E4M3(x) is summed by the tensor
-// core in FP32, then out += P_g * 2^e(x, g) * d * (1 + 2*nibble_g) in FP32.
+// per 32-weight group g, P_g = sum_k E4M3(w) * E4M3(x) * 2^e(x, g) is summed by
+// the tensor core in FP32 (block-scaled MMA: the activation's UE8M0 scale is
+// applied in the MMA, an exact power of two), then out += P_g * d * (1 + 2*nibble_g)
+// in FP32.
 //
-// One persistent CTA per SM walks a stream-K range of work units (128 weight
-// rows x one 256-wide K block). Roles:
-//  * warp 0, producer: five 1D bulk copies of the unit's IQ3_S fields (for one
-//    K block the fields of 128 consecutive rows are contiguous; evict-first),
-//    an L2 prefetch of the fields `prefetch` units further on, and, once the
-//    previous kernel has finished (programmatic dependent launch), one 3D TMA
-//    copy of the activation block straight into the UMMA B-operand layout
-//    (16-byte K chunks x tokens; rows past M read as zero).
+// One persistent CTA per SM walks a range of work units (128 weight rows x one
+// 256-wide K block): a stream-K range, one row tile, or one K part of a row
+// tile within a thread-block cluster. Roles:
+//  * warp 0, weight producer: one bulk copy of the unit's tile-major record
+//    (or five, one per IQ3_S field; evict-first) into a ring of weight stages,
+//    and an L2 prefetch of the records `prefetch` units further on. A stage is
+//    refilled as soon as the decoders have read it.
+//  * activation producer warp: once the previous kernel has finished
+//    (programmatic dependent launch), one 3D TMA copy of the unit's activation
+//    block straight into the UMMA B-operand layout (16-byte K chunks x tokens;
+//    rows past M read as zero) and one of its scale bytes, into a separate ring
+//    that runs up to 8 units ahead of the MMAs.
 //  * decoder warps (8 or 16): a thread owns one weight row (its TMEM lane) and
 //    a quarter or half of the block; it reads its raw bytes with 128-bit loads,
-//    expands each 4-weight code through a lane-private
-//    codebook in shared memory, adds the sign bits and writes the E4M3 bytes to
-//    its TMEM lane with tcgen05.st (double-buffered A operand). Weight rows'
-//    d and scale nibbles go to a small shared buffer for the epilogue.
-//  * warp 1, MMA: the converged warp elects one lane that issues 8 tcgen05.mma
-//    (A from TMEM, B from shared memory, M=128, N=16/32, K=32: one per group)
-//    with descriptors formed once per unit, and commits them.
-//  * a scale warp turns the activation scales of each unit into floats.
-//  * 4 epilogue warps: each thread owns one weight row, reads the 8 group
-//    partials of its lane with tcgen05.ld, applies 2^e * d*(1+2*nibble) and
-//    accumulates in FP32 registers; finished rows go to the output or to the
-//    deterministic split-K reduction (acq_rel counter, CTA-ordered sum).
+//    expands each 4-weight code through a lane-private codebook in shared
+//    memory, adds the sign bits and writes the E4M3 bytes to its TMEM lane with
+//    tcgen05.st (a ring of 3 A operands). Weight rows' d and scale nibbles go
+//    to a small shared buffer for the epilogue.
+//  * warp 1, MMA: the converged warp elects one lane that issues 8 block-scaled
+//    tcgen05.mma (A from TMEM, B from shared memory, M=128, N=16/32, K=32: one
+//    per group) with descriptors formed once per unit, and commits them.
+//  * 4 epilogue warps (one per TMEM lane quadrant): each thread owns one weight
+//    row, reads the 8 group partials of its lane with tcgen05.ld, applies
+//    d*(1+2*nibble) and accumulates in FP32 registers; finished rows go to the
+//    output or to the deterministic split-K reduction (acq_rel counter,
+//    CTA-ordered sum, or the cluster's rank 0). Before releasing a D buffer
+//    they write the activation scales of the unit whose MMAs wait for that
+//    buffer into TMEM (tcgen05.st, all four quadrants), so the MMA warp only
+//    issues MMAs.
 #include <map>
 #include <mutex>
 #include <tuple>
@@ -41,45 +50,60 @@ namespace {
 constexpr int kRows = 128;                 // weight rows per unit = MMA M = TMEM lanes
 constexpr int kTableBytes = 512 * 32 * 4;  // codebook, one copy per lane
 constexpr int kEpiWarps = 4;
-constexpr int kMaxStagesTm = 8;
+constexpr int kMaxStagesTm = 12;
 constexpr int kRing = 3;  // decoded units in flight: A operands in TMEM, epilogue data in shared memory
-constexpr uint32_t kBarBytes = 320;
+constexpr uint32_t kBarBytes = 512;
 constexpr uint32_t kTableStageBytes = 512 * 4;  // the codebook as read from global memory
 constexpr uint32_t kRecordBytes = 14080;         // one (128-row tile, K block) of every field
 
-// Warps: producer, MMA, decoders, 4 epilogue, scale.
-__host__ __device__ constexpr int tm_threads(int dec_warps) { return (2 + dec_warps + kEpiWarps + 1) * 32; }
+// Warps: weight producer, MMA, decoders, 4 epilogue, activation producer.
+__host__ __device__ constexpr int tm_threads(int dec_warps) { return (3 + dec_warps + kEpiWarps) * 32; }
 __host__ __device__ constexpr int tm_box_tokens(int nt) { return 8 * nt; }    // activation rows per B tile
+// Activation tiles in flight (their own ring, filled ahead of the weights).
+constexpr int kMaxXStages = 8;
+__host__ __device__ constexpr int tm_xstages(int nt) { return nt == 1 ? 8 : nt == 2 ? 6 : 4; }
 __host__ __device__ constexpr int tm_nmma(int nt) { return nt == 4 ? 32 : 16; }  // MMA N
 // TMEM columns: the A ring at [0, 64*kRing), then D (8 groups x N columns),
-// double-buffered unless that would not fit in 512 columns (N = 32).
+// double-buffered unless that would not fit in 512 columns (N = 32), then the
+// scale factors: A's (all 2^0) and a ring of B's (8 columns a unit: K blocks
+// 0-3 and 4-7 of the unit in byte 0-3 of columns +0 and +4).
+// The MMA reads a scale-factor matrix from 4 columns starting at the address
+// it is given (column + row / 32), so every such address is a multiple of 4.
 constexpr uint32_t kTmemD = 64u * kRing;
 __host__ __device__ constexpr int tm_d_buffers(int nt) { return nt != 4 ? 2 : 1; }
-__host__ __device__ constexpr uint32_t tm_tmem_cols(int nt) {
-  return kTmemD + tm_d_buffers(nt) * 8u * tm_nmma(nt) <= 256u ? 256u : 512u;
-}
+__host__ __device__ constexpr uint32_t tm_sfa_col(int nt) { return kTmemD + tm_d_buffers(nt) * 8u * tm_nmma(nt); }
+__host__ __device__ constexpr uint32_t tm_sfb_col(int nt) { return tm_sfa_col(nt) + 16u; }
+__host__ __device__ constexpr uint32_t tm_tmem_cols(int nt) { return tm_sfb_col(nt) + 8u * kRing <= 256u ? 256u : 512u; }
+static_assert(tm_sfb_col(1) + 8u * kRing <= 512u && tm_sfb_col(2) + 8u * kRing <= 512u &&
+                  tm_sfb_col(4) + 8u * kRing <= 512u,
+              "TMEM plan exceeds 512 columns");
+static_assert(tm_sfa_col(1) % 16u == 0 && tm_sfa_col(2) % 16u == 0 && tm_sfa_col(4) % 16u == 0,
+              "scale-factor columns must stay aligned");
 __host__ __device__ constexpr uint32_t align_up_tm(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
-// One stage: the IQ3_S fields of a unit at the offsets of their TMA boxes,
-// then the activation block. Stages are 512-byte aligned (64-byte swizzle).
+// A weight stage: the IQ3_S fields of a unit (one tile-major record, or the
+// five fields copied separately to the same offsets). An activation slot: the
+// B tile, then the scale bytes. Weight stages are 128-byte aligned, the
+// activation slots (after the stages) 1024-byte aligned.
 struct TmLayout {
-  uint32_t qs, signs, qh, d, scales, b, xs, stage;
-  uint32_t w, xsf, aux;  // one of two epilogue buffers: rows' (d, scale word), scales as floats
+  uint32_t qs, signs, qh, d, scales, stage;
+  uint32_t b, xs, xslot;
+  uint32_t w, aux;  // one of kRing epilogue buffers: rows' (d, scale word)
 };
 
 __host__ __device__ inline TmLayout tm_layout(int nt) {
   TmLayout L{};
   L.qs = 0;
-  L.signs = kRows * 64;         // 8192 (SWIZZLE_32B destination, 256-aligned)
+  L.signs = kRows * 64;         // 8192
   L.qh = L.signs + kRows * 32;  // 12288
   L.d = L.qh + kRows * 8;       // 13312
   L.scales = L.d + kRows * 2;   // 13568
-  L.b = L.scales + kRows * 4;   // 14080
-  L.xs = L.b + 256u * tm_box_tokens(nt);  // activation scale bytes: [tokens][16] (two K blocks' groups)
-  L.stage = align_up_tm(L.xs + 16u * tm_box_tokens(nt), 512);
+  L.stage = L.scales + kRows * 4;  // 14080 = kRecordBytes
+  L.b = 0;
+  L.xs = 256u * tm_box_tokens(nt);  // activation scale bytes: [tokens][16] (two K blocks' groups)
+  L.xslot = align_up_tm(L.xs + 16u * tm_box_tokens(nt), 1024);
   L.w = 0;
-  L.xsf = kRows * 8;
-  L.aux = L.xsf + 8u * 8u * nt * 4u;
+  L.aux = kRows * 8;
   return L;
 }
 
@@ -87,7 +111,8 @@ __host__ __device__ inline TmLayout tm_layout(int nt) {
 __host__ __device__ inline uint32_t tm_smem_bytes(int nt, int stages, int kparts) {
   const TmLayout L = tm_layout(nt);
   const uint32_t cpart = kparts > 1 ? (uint32_t)(kparts - 1) * kRows * 8u * nt * 4u : 0u;
-  return kTableBytes + 1024 + stages * L.stage + kRing * L.aux + kTableStageBytes + kBarBytes + cpart;
+  return kTableBytes + 1024 + align_up_tm(stages * L.stage, 1024) + tm_xstages(nt) * L.xslot + kRing * L.aux +
+         kTableStageBytes + kBarBytes + cpart;
 }
 
 __device__ __forceinline__ int unit_begin_tm(int cta, int grid, int units) {
@@ -207,7 +232,7 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
   constexpr int TOK = 8 * NT;             // tokens the epilogue keeps
   constexpr int NM = tm_nmma(NT);         // MMA N
   constexpr int BOX = tm_box_tokens(NT);  // activation rows in a B tile
-  constexpr uint32_t kIdesc = tc::idesc_e4m3_f32(kRows, NM);
+  constexpr uint32_t kIdesc = tc::idesc_mx_e4m3(kRows, NM, 0, 0);
   constexpr int kDBuf = tm_d_buffers(NT);
   constexpr uint32_t kCols = tm_tmem_cols(NT);
   constexpr int kParts = kDecWarps / 4;  // decoder threads per weight row
@@ -218,7 +243,8 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
   // repeat rows 0-7 (stride 0) and their results are never read.
   constexpr uint32_t kLbo = BOX * 16u;
   constexpr uint32_t kSbo = NT == 1 ? 0u : 128u;
-  constexpr int kEpiWarp0 = 2 + kDecWarps, kScaleWarp = 2 + kDecWarps + kEpiWarps;
+  constexpr int kEpiWarp0 = 2 + kDecWarps, kXWarp = kEpiWarp0 + kEpiWarps;
+  constexpr int AS = tm_xstages(NT);
   static_assert(kDecWarps == 8 || kDecWarps == 16, "8 or 16 decoder warps");
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -229,21 +255,24 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
   // every access below compiles to a shared-memory instruction.)
   uint8_t* table = smem_raw;
   uint8_t* st0 = smem_raw + kTableBytes + ((1024u - ((smem_u32(smem_raw) + kTableBytes) & 1023u)) & 1023u);
-  uint8_t* aux0 = st0 + (size_t)p.stages * L.stage;
+  uint8_t* x0 = st0 + align_up_tm((uint32_t)p.stages * L.stage, 1024);  // activation slots
+  uint8_t* aux0 = x0 + (size_t)AS * L.xslot;
   uint32_t* tstage = reinterpret_cast<uint32_t*>(aux0 + kRing * L.aux);
   uint64_t* bars = reinterpret_cast<uint64_t*>(aux0 + kRing * L.aux + kTableStageBytes);
   float* cpart = reinterpret_cast<float*>(aux0 + kRing * L.aux + kTableStageBytes + kBarBytes);  // cluster partials
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * kMaxStagesTm + 2 * kRing + 4);  // after cred
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kMaxStagesTm + 2 * kMaxXStages + 2 * kRing + 5);
   const uint32_t bar0 = smem_u32(bars);
-  // Barriers: per stage wfull (weights landed), xfull (activations landed),
-  // empty (stage consumed); per ring slot afull (A decoded and the epilogue's
-  // row data and scales written: decoders + scale warp), efree (epilogue done
-  // with the slot); per D buffer mdone (MMAs complete); edone (epilogue finished);
-  // cred (cluster K-split: the other CTAs of the cluster have written their
-  // partials into this CTA's shared memory; used in the cluster's rank 0).
-  const uint32_t kWfull = bar0, kXfull = bar0 + 8 * kMaxStagesTm, kEmpty = bar0 + 16 * kMaxStagesTm;
-  const uint32_t kAfull = bar0 + 24 * kMaxStagesTm, kEfree = kAfull + 8 * kRing;
-  const uint32_t kMdone = kEfree + 8 * kRing, kEdone = kMdone + 16, kCred = kEdone + 8;
+  // Barriers: per weight stage wfull (landed) and empty (decoded); per
+  // activation slot xfull (landed) and xempty (its MMAs complete); per ring
+  // slot afull (A decoded and the epilogue's row data written), efree
+  // (epilogue done with the slot); per D buffer mdone (MMAs complete); edone
+  // (epilogue finished); cred (cluster K-split: the other CTAs of the cluster
+  // have written their partials into this CTA's shared memory; used in the
+  // cluster's rank 0); sfinit (scales of the first units written).
+  const uint32_t kWfull = bar0, kEmpty = bar0 + 8 * kMaxStagesTm;
+  const uint32_t kXfull = bar0 + 16 * kMaxStagesTm, kXempty = kXfull + 8 * kMaxXStages;
+  const uint32_t kAfull = kXempty + 8 * kMaxXStages, kEfree = kAfull + 8 * kRing;
+  const uint32_t kMdone = kEfree + 8 * kRing, kEdone = kMdone + 16, kCred = kEdone + 8, kSfInit = kCred + 8;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // Work range: with kparts > 0 each row tile is split into kparts K ranges,
@@ -270,16 +299,20 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(kWfull + 8 * s, 1);
-      mbar_init(kXfull + 8 * s, 1);
-      mbar_init(kEmpty + 8 * s, kDecWarps + 2);  // decoders, MMA commit, scale warp
+      mbar_init(kEmpty + 8 * s, kDecWarps);
+    }
+    for (int x = 0; x < AS; ++x) {
+      mbar_init(kXfull + 8 * x, 1);
+      mbar_init(kXempty + 8 * x, 1);  // MMA commit
     }
     for (int r = 0; r < kRing; ++r) {
-      mbar_init(kAfull + 8 * r, kDecWarps + 1);
+      mbar_init(kAfull + 8 * r, kDecWarps);
       mbar_init(kEfree + 8 * r, kEpiWarps);
     }
     for (int b = 0; b < 2; ++b) mbar_init(kMdone + 8 * b, 1);
     mbar_init(kEdone, kEpiWarps);
     mbar_init(kCred, p.kparts > 1 ? (p.kparts - 1) * kEpiWarps : 1);
+    mbar_init(kSfInit, kEpiWarps);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -292,17 +325,13 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
 
-  // ------------------------------------------------------------------ producer
+  // ------------------------------------------------------------------ weight producer
   // The whole warp issues: lane f < 5 copies weight field f, so one warp
   // instruction starts all five copies of a unit (a copy instruction costs
-  // its thread ~100 cycles or more to issue).
+  // its thread ~100 cycles or more to issue). Weights do not depend on the
+  // previous kernel: no wait for it.
   if (warp == 0) {
     const uint64_t policy = l2_policy_evict_first();
-    const uint64_t keep = l2_policy_evict_last();  // activations: every CTA reads them
-    if (lane == 0) {
-      tma_prefetch_desc(&maps.x);
-      tma_prefetch_desc(&maps.xs);
-    }
     const uint8_t* fptr = lane == 0 ? p.qs : lane == 1 ? p.signs : lane == 2 ? p.qh : lane == 3 ? p.d : p.scales;
     const uint32_t fbpr = lane == 0 ? 64u : lane == 1 ? 32u : lane == 2 ? 8u : lane == 3 ? 2u : 4u;  // bytes per row
     const uint32_t foff = lane == 0 ? L.qs : lane == 1 ? L.signs : lane == 2 ? L.qh : lane == 3 ? L.d : L.scales;
@@ -332,15 +361,6 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
       }
       __syncwarp();
     };
-    auto issue_acts = [&](int it) {
-      const int s = it % S, kb = (u0 + it) % p.n_blocks;
-      const uint32_t full = kXfull + 8 * s;
-      if (lane == 0) mbar_arrive_expect_tx(full, kBytesX);
-      __syncwarp();
-      if (lane == 0) tma_load_3d(smem_u32(st0 + (size_t)s * L.stage + L.b), &maps.x, 0, 0, kb * 16, full, keep);
-      if (lane == 1) tma_load_2d(smem_u32(st0 + (size_t)s * L.stage + L.xs), &maps.xs, (kb >> 1) * 16, 0, full, keep);
-      __syncwarp();
-    };
     auto prefetch = [&](int it) {
       if (p.packed) {
         if (lane == 0) bulk_prefetch_l2(p.packed + (size_t)(u0 + it) * kRecordBytes, kRecordBytes);
@@ -353,18 +373,43 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
       __syncwarp();
     };
     const int pre = min(S, n_units);
-    // Weights do not depend on the previous kernel: stream them first.
     for (int it = 0; it < pre; ++it) issue_weights(it);
     int pf = pre;
     for (; pf < min(n_units, pre + p.prefetch); ++pf) prefetch(pf);
-    pdl_wait();
-    for (int it = 0; it < pre; ++it) issue_acts(it);
     for (int it = pre; it < n_units; ++it) {
       const bool ok = mbar_wait_bounded(kEmpty + 8 * (it % S), ((it / S) & 1) ^ 1, kSiteGemvEmpty);
       if (!__all_sync(0xFFFFFFFFu, ok)) return;
       issue_weights(it);
-      issue_acts(it);
       for (; pf < min(n_units, it + 1 + p.prefetch); ++pf) prefetch(pf);
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------------ activation producer
+  // Activation tiles (B operand and scale bytes of a K block) once the previous
+  // kernel has finished (programmatic dependent launch), AS units ahead: slot
+  // j % AS is refilled when the MMAs of unit j - AS have completed.
+  if (warp == kXWarp) {
+    const uint64_t keep = l2_policy_evict_last();  // every CTA reads them
+    if (lane == 0) {
+      tma_prefetch_desc(&maps.x);
+      tma_prefetch_desc(&maps.xs);
+    }
+    pdl_wait();
+    for (int j = 0; j < n_units; ++j) {
+      const int x = j % AS;
+      if (j >= AS) {
+        const bool ok = mbar_wait_bounded(kXempty + 8 * x, ((j / AS) & 1) ^ 1, kSiteGemvEmpty);
+        if (!__all_sync(0xFFFFFFFFu, ok)) return;
+      }
+      const int kb = (u0 + j) % p.n_blocks;
+      const uint32_t full = kXfull + 8 * x, slot = smem_u32(x0 + (size_t)x * L.xslot);
+      if (lane == 0) {
+        mbar_arrive_expect_tx(full, kBytesX);
+        tma_load_3d(slot + L.b, &maps.x, 0, 0, kb * 16, full, keep);
+        tma_load_2d(slot + L.xs, &maps.xs, (kb >> 1) * 16, 0, full, keep);
+      }
+      __syncwarp();
     }
     return;
   }
@@ -372,27 +417,32 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
   // ------------------------------------------------------------------ MMA
   if (warp == 1) {
     for (int it = 0; it < n_units; ++it) {
-      const int r = it % kRing, s = it % S, db = kDBuf == 2 ? (it & 1) : 0;
+      const int r = it % kRing, x = it % AS, db = kDBuf == 2 ? (it & 1) : 0;
       // The D buffer is free once the epilogue is done with the unit that used it last.
       const int prev = it - kDBuf;
       bool ok = mbar_try_wait(kAfull + 8 * r, (it / kRing) & 1);
-      bool ok2 = mbar_try_wait(kXfull + 8 * s, (it / S) & 1);
-      bool ok3 = prev < 0 || mbar_try_wait(kEfree + 8 * (prev % kRing), (prev / kRing) & 1);
+      bool ok2 = mbar_try_wait(kXfull + 8 * x, (it / AS) & 1);
+      // The activation scales of units 0 .. kDBuf-1 are written before the
+      // epilogue's first unit; later ones before it frees the D buffer.
+      bool ok3 = prev < 0 ? (it > 0 || mbar_try_wait(kSfInit, 0))
+                          : mbar_try_wait(kEfree + 8 * (prev % kRing), (prev / kRing) & 1);
       if (!__all_sync(0xFFFFFFFFu, ok && ok2 && ok3)) {  // slow path, taken by the whole warp
         ok = mbar_wait_bounded(kAfull + 8 * r, (it / kRing) & 1, kSiteGemvFull);
-        ok = ok && mbar_wait_bounded(kXfull + 8 * s, (it / S) & 1, kSiteGemvFull);
+        ok = ok && mbar_wait_bounded(kXfull + 8 * x, (it / AS) & 1, kSiteGemvFull);
         if (prev >= 0) ok = ok && mbar_wait_bounded(kEfree + 8 * (prev % kRing), (prev / kRing) & 1, kSiteGemvEmpty);
+        else if (it == 0) ok = ok && mbar_wait_bounded(kSfInit, 0, kSiteGemvFull);
         if (!__all_sync(0xFFFFFFFFu, ok)) break;
       }
       tc::fence_after_sync();
-      const uint64_t db0 = tc::smem_desc(smem_u32(st0 + (size_t)s * L.stage + L.b), kLbo, kSbo);
+      const uint64_t db0 = tc::smem_desc(smem_u32(x0 + (size_t)x * L.xslot + L.b), kLbo, kSbo);
       const uint32_t dcol = tmem + kTmemD + (uint32_t)(db * 8 * NM), acol = tmem + (uint32_t)(r * 64);
+      const uint32_t sfb = tmem + tm_sfb_col(NT) + 8u * r;  // written by the epilogue
       if (elect_one()) {
 #pragma unroll
         for (int g = 0; g < 8; ++g)
-          tc::mma_e4m3_ts(dcol + (uint32_t)(g * NM), acol + (uint32_t)(g * 8), db0 + (uint64_t)((2u * kLbo * g) >> 4),
-                          kIdesc, 0);
-        tc::commit(kEmpty + 8 * s);
+          tc::mma_mx_e4m3_ts(dcol + (uint32_t)(g * NM), acol + (uint32_t)(g * 8), db0 + (uint64_t)((2u * kLbo * g) >> 4),
+                             kIdesc | ((uint32_t)(g & 3) << 4), tmem + tm_sfa_col(NT), sfb + 4u * (uint32_t)(g >> 2), 0);
+        tc::commit(kXempty + 8 * x);
         tc::commit(kMdone + 8 * db);
       }
       __syncwarp();
@@ -402,32 +452,6 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
     __syncwarp();
     tc::fence_after_sync();
     tc::dealloc(tmem, kCols);
-    return;
-  }
-
-  // ------------------------------------------------------------------ scales
-  if (warp == kScaleWarp) {
-    constexpr int VPL = TOK * 8 / 32;  // values per lane and unit
-    for (int it = 0; it < n_units; ++it) {
-      const int r = it % kRing, s = it % S;
-      bool ok = mbar_wait_bounded(kXfull + 8 * s, (it / S) & 1, kSiteGemvFull);
-      if (it >= kRing) ok = ok && mbar_wait_bounded(kEfree + 8 * r, ((it / kRing) & 1) ^ 1, kSiteGemvEmpty);
-      if (!__all_sync(0xFFFFFFFFu, ok)) return;
-      // Scale bytes of this K block ([token][16], groups at (kb & 1) * 8) -> floats [group][token].
-      const uint8_t* xsb = st0 + (size_t)s * L.stage + L.xs + (((u0 + it) % p.n_blocks) & 1) * 8;
-      float* xsf = reinterpret_cast<float*>(aux0 + (size_t)r * L.aux + L.xsf);
-#pragma unroll
-      for (int j = 0; j < VPL; ++j) {
-        const int v = j * 32 + lane, g = v / TOK, t = v % TOK;
-        xsf[v] = e8m0_to_float(xsb[t * 16 + g]);
-      }
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(kAfull + 8 * r);
-        mbar_arrive(kEmpty + 8 * s);
-      }
-      __syncwarp();
-    }
     return;
   }
 
@@ -453,6 +477,9 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
 
     const uint32_t l4 = (uint32_t)(lane << 2) * 0x01010101u;
     const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(part * kGroups * 8);
+    // The weights' MMA scale factors are all 2^0 (UE8M0 127); the first afull
+    // arrival orders these stores before the first MMA.
+    if (part == 0) tc::st_x4(tmem + ((uint32_t)(32 * q) << 16) + tm_sfa_col(NT), 0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu);
     // Offsets of this thread's raw bytes in a stage. Packed records are
     // chunk-major ([16-byte chunk][row][16 bytes] for qs and signs, [4-byte
     // column][row][4 bytes] for qh), so the 8 rows of a load phase read
@@ -531,8 +558,35 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
     for (int t = 0; t < TOK; ++t) acc[t] = 0.f;
     pdl_wait();  // the workspace and output may still be in use by the previous kernel
     pdl_launch_dependents();
+    // Unit j's activation scales (UE8M0, one per token and 32-wide group) go
+    // to TMEM scale-factor slot j % kRing of this warp's quadrant, token t in
+    // lane t: groups 0-3 in bytes 0-3 of column +0, groups 4-7 in column +4
+    // (the MMA's scale addresses must be 4-column aligned). Lanes past the
+    // activation tile's rows read other bytes of shared memory; their columns
+    // of D are never read.
+    const uint32_t tsf = tmem + ((uint32_t)(32 * q) << 16) + tm_sfb_col(NT);
+    auto write_sf = [&](int j) -> bool {
+      const int xj = j % AS;
+      bool ok = mbar_try_wait(kXfull + 8 * xj, (j / AS) & 1);
+      if (!__all_sync(0xFFFFFFFFu, ok)) {
+        ok = mbar_wait_bounded(kXfull + 8 * xj, (j / AS) & 1, kSiteGemvFull);
+        if (!__all_sync(0xFFFFFFFFu, ok)) return false;
+      }
+      const uint2 v = *reinterpret_cast<const uint2*>(x0 + (size_t)xj * L.xslot + L.xs + lane * 16 +
+                                                      (((u0 + j) % p.n_blocks) & 1) * 8);
+      const uint32_t vv[8] = {v.x, v.x, v.x, v.x, v.y, v.y, v.y, v.y};
+      tc::st_x8(tsf + 8u * (uint32_t)(j % kRing), vv);
+      return true;
+    };
+    bool sf_ok = true;
+    for (int j = 0; j < kDBuf && j < n_units; ++j) sf_ok = sf_ok && write_sf(j);
+    tc::wait_st();
+    tc::fence_before_sync();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(kSfInit);
+    __syncwarp();
     int seg_begin = u0;
-    for (int it = 0, u = u0; u < u1; ++u, ++it) {
+    for (int it = 0, u = u0; sf_ok && u < u1; ++u, ++it) {
       const int r = it % kRing, db = kDBuf == 2 ? (it & 1) : 0;
       const uint32_t mpar = kDBuf == 2 ? ((it >> 1) & 1) : (it & 1);
       bool ok = mbar_try_wait(kMdone + 8 * db, mpar);
@@ -545,7 +599,6 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
       tc::fence_after_sync();
       const uint32_t tq = tq0 + (uint32_t)(db * 8 * NM);
       const uint8_t* aux = aux0 + (size_t)r * L.aux;
-      const float* xs = reinterpret_cast<const float*>(aux + L.xsf);
       const uint2 dsc = reinterpret_cast<const uint2*>(aux + L.w)[rl];
       const float dv = __half2float(__ushort_as_half((unsigned short)dsc.x));
       const float dneg = -8388608.0f * dv;
@@ -570,15 +623,15 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
                                  dv, dneg);
 #pragma unroll
             for (int t = 0; t < 8; t += 2) {
-              if (t0 + t < p.m) {  // tokens past M are padding (warp-uniform branch)
-                float p0, p1;
-                mul2(p0, p1, c[j][t], c[j][t + 1], xs[g * TOK + t0 + t], xs[g * TOK + t0 + t + 1]);
-                fma2(acc[t0 + t], acc[t0 + t + 1], p0, p1, w, w);
-              }
+              if (t0 + t < p.m)  // tokens past M are padding (warp-uniform branch)
+                fma2(acc[t0 + t], acc[t0 + t + 1], c[j][t], c[j][t + 1], w, w);
             }
           }
         }
       }
+      // The MMAs of unit it + kDBuf wait for this D buffer: their scales first.
+      if (it + kDBuf < n_units && !write_sf(it + kDBuf)) break;
+      tc::wait_st();
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(kEfree + 8 * r);

@@ -44,6 +44,39 @@ __device__ __forceinline__ void mma_e4m3_ts(uint32_t tmem_d, uint32_t tmem_a, ui
       "r"(tmem_a), "l"(desc_b), "r"(idesc), "r"(accumulate));
 }
 
+// Instruction descriptor of kind::mxf8f6f4 (block-scaled, UE8M0 scales, one
+// per 32 K elements): A = B = E4M3, both K-major, D = F32. b_id / a_id pick
+// the byte of the 32-bit scale-factor element of TMEM the MMA uses.
+__host__ __device__ constexpr uint32_t idesc_mx_e4m3(int m, int n, uint32_t b_id, uint32_t a_id) {
+  return (b_id << 4) | ((uint32_t)(n >> 3) << 17) | (1u << 23) | ((uint32_t)(m >> 4) << 24) | (a_id << 29);
+}
+
+// D[tmem] (+)= (A[tmem] * 2^sfa) x (B[smem] * 2^sfb)^T, issued by one thread;
+// the scale factors of A's rows and B's columns are read from TMEM.
+__device__ __forceinline__ void mma_mx_e4m3_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t desc_b, uint32_t idesc,
+                                               uint32_t tmem_sfa, uint32_t tmem_sfb, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale.scale_vec::1X [%0], [%1], %2, %3, [%5], [%6], p;\n\t}" ::"r"(
+          tmem_d),
+      "r"(tmem_a), "l"(desc_b), "r"(idesc), "r"(accumulate), "r"(tmem_sfa), "r"(tmem_sfb));
+}
+
+// Copies a 32-row x 16-byte matrix from shared memory (descriptor `sdesc`)
+// to 4 consecutive 32-bit columns of TMEM lanes 0-31, repeated in each of the
+// four 32-lane quadrants (the layout of MMA scale factors). Ordered before
+// later tcgen05.mma of the issuing thread.
+__device__ __forceinline__ void cp_32x128b_warpx4(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+// Each lane writes 4 consecutive 32-bit columns of its TMEM lane (warp-wide).
+__device__ __forceinline__ void st_x4(uint32_t taddr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};" ::"r"(taddr), "r"(a), "r"(b), "r"(c),
+               "r"(d)
+               : "memory");
+}
+
 // Each lane writes 8 consecutive 32-bit columns of its TMEM lane (warp-wide).
 __device__ __forceinline__ void st_x8(uint32_t taddr, const uint32_t (&v)[8]) {
   asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(v[0]),

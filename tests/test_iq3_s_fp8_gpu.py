@@ -251,7 +251,7 @@ def test_config_that_does_not_fit_is_a_value_error(cuda_device):
     fields = gpu_weight(raw, cuda_device)
     with pytest.raises(ValueError):
         launch_iq3_s_fp8_matmul(torch.from_numpy(xq).to(cuda_device), torch.from_numpy(xs).to(cuda_device), fields,
-                                config={"kernel": _lib.MAMBO_KERNEL_GEMV, "warps": 8, "stages": 8})
+                                config={"kernel": _lib.MAMBO_KERNEL_GEMV, "warps": 8, "stages": 12})
 
 
 @pytest.mark.parametrize("m", [5, 13])
