@@ -164,11 +164,27 @@ int kernel_of(const MamboLinearConfig& c) { return c.kernel == MAMBO_KERNEL_AUTO
 // partials, which the plan sizes to what is left).
 uint32_t config_smem(const MamboLinearConfig& c, int nt, int64_t b) {
   if (kernel_of(c) == MAMBO_KERNEL_GEMV_SYNC) return gemv_smem_bytes_host(c.warps * 16, nt, c.stages, (int)b);
+  if (kernel_of(c) == MAMBO_KERNEL_GEMM) return gemm_tm_smem_bytes(c.stages);
   return gemv_tm_smem_bytes(nt, c.stages, 1);
 }
 
+// Prefill-sized M (the reference's large-token path, LARGE_TOKEN_THRESHOLD):
+// the tcgen05 GEMM over 128 x 128 tiles.
+constexpr int64_t kGemmMinTokens = 32;
+// Weight stages of the GEMM configurations (the other fields are fixed).
+const int kGemmStages[] = {2, 3, 4};
+constexpr int kNumGemmConfigs = (int)(sizeof(kGemmStages) / sizeof(kGemmStages[0]));
+
 void default_config(int64_t m, int64_t n, int64_t b, MamboLinearConfig* cfg, int smem_optin, int sms) {
   std::memset(cfg, 0, sizeof(*cfg));
+  if (m >= kGemmMinTokens) {
+    cfg->kernel = MAMBO_KERNEL_GEMM;
+    cfg->warps = 8;
+    cfg->ctas_per_sm = 1;
+    cfg->stages = 4;
+    while (cfg->stages > 2 && (int)config_smem(*cfg, 4, b) > smem_optin) --cfg->stages;
+    return;
+  }
   cfg->kernel = MAMBO_KERNEL_GEMV;
   cfg->warps = 8;
   cfg->ctas_per_sm = 1;
@@ -183,9 +199,12 @@ void default_config(int64_t m, int64_t n, int64_t b, MamboLinearConfig* cfg, int
 
 int validate_config(const MamboLinearConfig* cfg, int64_t m, int64_t b, const DeviceInfo& info) {
   const int kind = kernel_of(*cfg);
-  if (kind != MAMBO_KERNEL_GEMV && kind != MAMBO_KERNEL_GEMV_SYNC)
+  if (kind != MAMBO_KERNEL_GEMV && kind != MAMBO_KERNEL_GEMV_SYNC && kind != MAMBO_KERNEL_GEMM)
     return fail(MAMBO_EINVAL, "unknown kernel kind %d", cfg->kernel);
-  if (kind == MAMBO_KERNEL_GEMV_SYNC) {
+  if (kind == MAMBO_KERNEL_GEMM) {
+    if (cfg->stages < 2 || cfg->stages > gemm_tm_max_wstages())
+      return fail(MAMBO_EINVAL, "stages must be in [2, %d]", gemm_tm_max_wstages());
+  } else if (kind == MAMBO_KERNEL_GEMV_SYNC) {
     if (cfg->warps != 4 && cfg->warps != 8 && cfg->warps != 12 && cfg->warps != 16)
       return fail(MAMBO_EINVAL, "warps must be 4, 8, 12 or 16");
     if (cfg->stages < 2 || cfg->stages > 12) return fail(MAMBO_EINVAL, "stages must be in [2, 12]");
@@ -231,6 +250,19 @@ int cluster_kparts(int row_tiles, int64_t b, const MamboLinearConfig& cfg, int n
   return kp;
 }
 
+// The GEMM's activation scales in scale-factor atom layout: 1 KB per (128-token tile, K block).
+size_t gemm_workspace_bytes(int64_t m, int64_t b) {
+  const int64_t tok = gemm_tm_tile_tokens();
+  return align256((size_t)((m + tok - 1) / tok) * (size_t)b * 1024);
+}
+
+// The GEMM reads activations through a TMA map (16-byte aligned rows) and
+// weights from the tile-major packed copy.
+bool gemm_usable(const MamboIQ3SWeight* w, const uint8_t* xq, int64_t ldxq, int64_t m) {
+  return w->packed != nullptr && w->n_rows % 8 == 0 && (uintptr_t)xq % 16 == 0 && ldxq % 16 == 0 &&
+         m <= (int64_t)1 << 30;
+}
+
 GemvPlan plan_gemv(int64_t m_chunk, int64_t n, int64_t b, const MamboLinearConfig& cfg, int sms, int smem_optin) {
   GemvPlan P{};
   const bool tc = kernel_of(cfg) == MAMBO_KERNEL_GEMV;
@@ -255,6 +287,45 @@ GemvPlan plan_gemv(int64_t m_chunk, int64_t n, int64_t b, const MamboLinearConfi
   P.xcopy_bytes = tc ? align256((size_t)m_chunk * b * 256) : 0;
   P.xscopy_bytes = tc ? align256((size_t)m_chunk * xs_copy_stride(b)) : 0;
   return P;
+}
+
+// The tcgen05 GEMM: activation scales to scale-factor atoms (workspace), then
+// one persistent launch over all (128-row, 128-token) tiles.
+int launch_gemm(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t ldxs, int64_t m, const MamboIQ3SWeight* w,
+                const uint32_t* fp8_table, void* out, int out_dtype, int64_t ldo, const MamboLinearConfig& c,
+                const DeviceInfo& info, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  const size_t need = gemm_workspace_bytes(m, w->n_blocks);
+  if (!workspace || workspace_bytes < need)
+    return fail(MAMBO_EWORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+  if ((uintptr_t)workspace % 256) return fail(MAMBO_EINVAL, "workspace must be 256-byte aligned");
+  if ((int)gemm_tm_smem_bytes(c.stages) > info.max_smem_optin)
+    return fail(MAMBO_EINVAL, "configuration needs %u bytes of shared memory (device allows %d)",
+                gemm_tm_smem_bytes(c.stages), info.max_smem_optin);
+  uint8_t* atoms = (uint8_t*)workspace;
+  cudaError_t e = launch_xs_atoms(xs, ldxs, (int)m, (int)w->n_blocks, atoms, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "iq3s_xs_atoms");
+  GemmTmMaps maps;
+  std::memset(&maps, 0, sizeof(maps));
+  if (!make_gemv_x_map(xq, ldxq, (int)m, (int)w->n_blocks, gemm_tm_tile_tokens(), &maps.x))
+    return fail(MAMBO_ECUDA, "could not encode the activation tensor map");
+  GemmTmParams p{};
+  p.m = (int)m;
+  p.n_rows = (int)w->n_rows;
+  p.n_blocks = (int)w->n_blocks;
+  p.packed = (const uint8_t*)w->packed;
+  p.xs_atoms = atoms;
+  p.table = fp8_table;
+  p.out = out;
+  p.out_bf16 = out_dtype == MAMBO_BF16;
+  p.ldo = ldo;
+  p.wstages = c.stages;
+  p.row_tiles = (int)((w->n_rows + 127) / 128);
+  p.tok_tiles = (int)((m + gemm_tm_tile_tokens() - 1) / gemm_tm_tile_tokens());
+  const int64_t tiles = (int64_t)p.row_tiles * p.tok_tiles;
+  const int grid = (int)(tiles < info.sms ? tiles : info.sms);
+  e = launch_gemm_tm(p, maps, grid, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "iq3s_gemm_tm");
+  return ok();
 }
 
 // Launches the tcgen05 GEMV for tokens [0, mc) of xq/xs (already offset to the chunk).
@@ -453,6 +524,7 @@ int mambo_default_config(int64_t m, int64_t n_rows, int64_t n_blocks, MamboLinea
 
 int mambo_num_configs(int kernel) {
   if (kernel == MAMBO_KERNEL_GEMV || kernel == MAMBO_KERNEL_AUTO) return kNumTcConfigs;
+  if (kernel == MAMBO_KERNEL_GEMM) return kNumGemmConfigs;
   if (kernel == MAMBO_KERNEL_GEMV_SYNC) return kNumSyncConfigs;
   return 0;
 }
@@ -466,7 +538,11 @@ int mambo_config_at(int kernel, int index, MamboLinearConfig* cfg) {
   cfg->kernel = kernel;
   cfg->ctas_per_sm = 1;
   cfg->split = index % 2;
-  if (kernel == MAMBO_KERNEL_GEMV) {
+  if (kernel == MAMBO_KERNEL_GEMM) {
+    cfg->split = 0;
+    cfg->warps = 8;
+    cfg->stages = kGemmStages[index];
+  } else if (kernel == MAMBO_KERNEL_GEMV) {
     const TcChoice& t = kTcChoices[index / 2];
     cfg->warps = t.warps;
     cfg->stages = t.stages;
@@ -487,10 +563,16 @@ size_t mambo_iq3s_linear_workspace_bytes(int64_t m, int64_t n_rows, int64_t n_bl
                                                                                           : kSmemOptinDefault,
                       st == MAMBO_OK ? info.sms : 148);
   const int sms = (st == MAMBO_OK && info.sms > 0) ? info.sms : 148;
+  const int smem_optin = (st == MAMBO_OK && info.max_smem_optin > 0) ? info.max_smem_optin : kSmemOptinDefault;
+  // A GEMM call may fall back to the GEMV (unaligned activations, no packed
+  // weight copy): room for both.
+  MamboLinearConfig cv = c;
+  if (kernel_of(c) == MAMBO_KERNEL_GEMM) default_config(m < 32 ? m : 31, n_rows, n_blocks, &cv, smem_optin, sms);
   const int64_t m_chunk = m < 32 ? m : 32;
-  GemvPlan P = plan_gemv(m_chunk, n_rows, n_blocks, c, sms,
-                         (st == MAMBO_OK && info.max_smem_optin > 0) ? info.max_smem_optin : kSmemOptinDefault);
-  return P.counters_bytes + P.partial_bytes + P.xcopy_bytes + P.xscopy_bytes;
+  GemvPlan P = plan_gemv(m_chunk, n_rows, n_blocks, cv, sms, smem_optin);
+  const size_t gemv = P.counters_bytes + P.partial_bytes + P.xcopy_bytes + P.xscopy_bytes;
+  const size_t gemm = kernel_of(c) == MAMBO_KERNEL_GEMM ? gemm_workspace_bytes(m, n_blocks) : 0;
+  return gemv > gemm ? gemv : gemm;
 }
 
 int mambo_iq3s_linear(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t ldxs, int64_t m,
@@ -512,8 +594,33 @@ int mambo_iq3s_linear(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_
   if (st != MAMBO_OK) return st;
   MamboLinearConfig c;
   if (cfg) c = *cfg; else default_config(m, w->n_rows, w->n_blocks, &c, info.max_smem_optin, info.sms);
-  if (c.kernel == MAMBO_KERNEL_AUTO) c.kernel = MAMBO_KERNEL_GEMV;
-  if (c.kernel == MAMBO_KERNEL_GEMV && (w->n_rows % 8 != 0 || c.loader != 0)) c.kernel = MAMBO_KERNEL_GEMV_SYNC;
+  if (c.kernel == MAMBO_KERNEL_AUTO) {
+    MamboLinearConfig a;
+    default_config(m, w->n_rows, w->n_blocks, &a, info.max_smem_optin, info.sms);
+    c.kernel = a.kernel;
+    if (c.stages == 0) c.stages = a.stages;
+  }
+  if (c.kernel == MAMBO_KERNEL_GEMM) {
+    if (gemm_usable(w, xq, ldxq, m)) {
+      st = validate_config(&c, 32, w->n_blocks, info);
+      if (st != MAMBO_OK) return st;
+      return launch_gemm(xq, ldxq, xs, ldxs, m, w, fp8_table, out, out_dtype, ldo, c, info, workspace,
+                         workspace_bytes, (cudaStream_t)stream);
+    }
+    if (cfg && cfg->kernel == MAMBO_KERNEL_GEMM)
+      return fail(MAMBO_EINVAL,
+                  "the GEMM needs the tile-major packed weight copy (N %% 8 == 0) and 16-byte aligned activation rows");
+    // Otherwise the GEMV in 32-token chunks.
+    default_config(31, w->n_rows, w->n_blocks, &c, info.max_smem_optin, info.sms);
+  }
+  if (c.kernel == MAMBO_KERNEL_GEMV && (w->n_rows % 8 != 0 || c.loader != 0)) {
+    // The legacy mma.sync GEMV: the deepest of the given stages that fits.
+    c.kernel = MAMBO_KERNEL_GEMV_SYNC;
+    if (c.stages > 12) c.stages = 12;
+    while (c.stages > 2 &&
+           (int)config_smem(c, gemv_nt_for(m < 32 ? m : 32), w->n_blocks) > info.max_smem_optin)
+      --c.stages;
+  }
   if (c.kernel == MAMBO_KERNEL_GEMV_SYNC && c.warps == 0) c.warps = 8;
   if (c.kernel == MAMBO_KERNEL_GEMV_SYNC && c.stages > 12) c.stages = 4;
   st = validate_config(&c, m < 32 ? m : 32, w->n_blocks, info);

@@ -42,19 +42,20 @@
 
 #include "kernels.cuh"
 #include "tcgen05.cuh"
+#include "iq3s_tm.cuh"
 
 namespace mambo {
 
 namespace {
 
 constexpr int kRows = 128;                 // weight rows per unit = MMA M = TMEM lanes
-constexpr int kTableBytes = 512 * 32 * 4;  // codebook, one copy per lane
+using tm::kTableBytes;
 constexpr int kEpiWarps = 4;
 constexpr int kMaxStagesTm = 12;
 constexpr int kRing = 3;  // decoded units in flight: A operands in TMEM, epilogue data in shared memory
 constexpr uint32_t kBarBytes = 512;
-constexpr uint32_t kTableStageBytes = 512 * 4;  // the codebook as read from global memory
-constexpr uint32_t kRecordBytes = 14080;         // one (128-row tile, K block) of every field
+using tm::kTableStageBytes;
+using tm::kRecordBytes;
 
 // Warps: weight producer, MMA, decoders, 4 epilogue, activation producer.
 __host__ __device__ constexpr int tm_threads(int dec_warps) { return (3 + dec_warps + kEpiWarps) * 32; }
@@ -182,49 +183,7 @@ __device__ __forceinline__ void sum_partials(const GemvTmParams& p, int rt, int 
   }
 }
 
-// Expands the 8 codes of one 32-weight group into E4M3 bytes (4 per register).
-//   q0, q1: the group's 8 qs bytes; hb: its qh byte (bit c = 9th index bit of
-//   code c); sg: its 32 sign bits (bit 4c+j = sign of weight j of code c);
-//   l4: (lane << 2) in every byte. Codebook entry e of lane l sits at byte
-//   (e & 0xFF) << 8 | (e >> 8) << 7 | l << 2, so lanes never share a bank.
-//   n * 0x10204080 (n < 16) puts bit j of n on bit 8j+7 (other partial
-//   products land elsewhere, without carries, and are masked off);
-//   n * 0x01020408 does the same for a nibble held in bits 4-7.
-__device__ __forceinline__ void decode_group(const uint8_t* table, uint32_t q0, uint32_t q1, uint32_t hb, uint32_t sg,
-                                             uint32_t l4, uint32_t* v) {
-  const uint32_t h0 = lop3_and_or((hb & 0xFu) * 0x10204080u, 0x80808080u, l4);   // byte j: h_j << 7 | lane << 2
-  const uint32_t h1 = lop3_and_or((hb & 0xF0u) * 0x01020408u, 0x80808080u, l4);  // codes 4..7
-  const uint32_t q0l = q0 & 0xFFFFu, q0h = q0 >> 16, q1l = q1 & 0xFFFFu, q1h = q1 >> 16;
-  const uint32_t m0 = *reinterpret_cast<const uint32_t*>(table + prmt(q0l, h0, 0x3204u));
-  const uint32_t m1 = *reinterpret_cast<const uint32_t*>(table + prmt(q0l, h0, 0x3215u));
-  const uint32_t m2 = *reinterpret_cast<const uint32_t*>(table + prmt(q0h, h0, 0x3206u));
-  const uint32_t m3 = *reinterpret_cast<const uint32_t*>(table + prmt(q0h, h0, 0x3217u));
-  const uint32_t m4 = *reinterpret_cast<const uint32_t*>(table + prmt(q1l, h1, 0x3204u));
-  const uint32_t m5 = *reinterpret_cast<const uint32_t*>(table + prmt(q1l, h1, 0x3215u));
-  const uint32_t m6 = *reinterpret_cast<const uint32_t*>(table + prmt(q1h, h1, 0x3206u));
-  const uint32_t m7 = *reinterpret_cast<const uint32_t*>(table + prmt(q1h, h1, 0x3217u));
-  const uint32_t s2 = sg >> 8, s4 = sg >> 16, s6 = sg >> 24;
-  v[0] = lop3_and_or((sg & 0xFu) * 0x10204080u, 0x80808080u, m0);
-  v[1] = lop3_and_or((sg & 0xF0u) * 0x01020408u, 0x80808080u, m1);
-  v[2] = lop3_and_or((s2 & 0xFu) * 0x10204080u, 0x80808080u, m2);
-  v[3] = lop3_and_or((s2 & 0xF0u) * 0x01020408u, 0x80808080u, m3);
-  v[4] = lop3_and_or((s4 & 0xFu) * 0x10204080u, 0x80808080u, m4);
-  v[5] = lop3_and_or((s4 & 0xF0u) * 0x01020408u, 0x80808080u, m5);
-  v[6] = lop3_and_or((s6 & 0xFu) * 0x10204080u, 0x80808080u, m6);
-  v[7] = lop3_and_or((sg >> 28) * 0x10204080u, 0x80808080u, m7);
-}
-
 }  // namespace
-
-// Elects one lane of a converged warp (tcgen05.mma reads its operands from
-// uniform registers: issuing from a converged warp keeps them there).
-__device__ __forceinline__ bool elect_one() {
-  uint32_t pred;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\telect.sync _|p, 0xffffffff;\n\tselp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(pred));
-  return pred != 0;
-}
 
 template <int NT, int kDecWarps>
 __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
@@ -437,7 +396,7 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
       const uint64_t db0 = tc::smem_desc(smem_u32(x0 + (size_t)x * L.xslot + L.b), kLbo, kSbo);
       const uint32_t dcol = tmem + kTmemD + (uint32_t)(db * 8 * NM), acol = tmem + (uint32_t)(r * 64);
       const uint32_t sfb = tmem + tm_sfb_col(NT) + 8u * r;  // written by the epilogue
-      if (elect_one()) {
+      if (tm::elect_one()) {
 #pragma unroll
         for (int g = 0; g < 8; ++g)
           tc::mma_mx_e4m3_ts(dcol + (uint32_t)(g * NM), acol + (uint32_t)(g * 8), db0 + (uint64_t)((2u * kLbo * g) >> 4),
@@ -465,15 +424,7 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
     const int tid = threadIdx.x - 64;
     // Codebook: stage the 2 KB read at kernel entry, then expand to the
     // lane-private copy, four lanes' copies (16 contiguous bytes) per store.
-#pragma unroll
-    for (int j = 0; j < 512 / (kDecWarps * 32); ++j) tstage[tid + j * nthreads] = tw[j];
-    asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
-    for (int i = tid; i < 512 * 8; i += nthreads) {
-      const uint32_t code = i >> 3, l0 = (i & 7) * 4, e = tstage[code];
-      *reinterpret_cast<uint4*>(table + (((code & 0xFFu) << 8) | ((code >> 8) << 7) | (l0 << 2))) =
-          make_uint4(e, e, e, e);
-    }
-    asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+    tm::build_table(table, tstage, tw, tid, nthreads);
 
     const uint32_t l4 = (uint32_t)(lane << 2) * 0x01010101u;
     const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(part * kGroups * 8);
@@ -534,7 +485,7 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
       uint32_t v[kGroups * 8];
 #pragma unroll
       for (int g = 0; g < kGroups; ++g)
-        decode_group(table, qw[2 * g], qw[2 * g + 1], (hw >> (8 * g)) & 0xFFu, sw[g], l4, v + 8 * g);
+        tm::decode_group(table, qw[2 * g], qw[2 * g + 1], (hw >> (8 * g)) & 0xFFu, sw[g], l4, v + 8 * g);
       tc::st_cols<kGroups * 8>(tq + (uint32_t)(r * 64), v);
       tc::wait_st();
       tc::fence_before_sync();

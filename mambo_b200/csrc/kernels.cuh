@@ -165,6 +165,31 @@ uint32_t gemv_tm_smem_bytes(int nt, int stages, int kparts);
 int gemv_tm_max_clusters(int nt, int dec_warps, int stages, int kparts);
 int gemv_tm_max_stages();
 
+// tcgen05 GEMM for prefill-sized M (128 weight rows x 128 tokens per tile).
+struct GemmTmParams {
+  int m;  // tokens
+  int n_rows;
+  int n_blocks;
+  const uint8_t* packed;    // tile-major weight records (iq3s_pack_kernel)
+  const uint8_t* xs_atoms;  // activation scales as scale-factor atoms (launch_xs_atoms)
+  const uint32_t* table;    // uint32[512], E4M3-encoded magnitudes
+  void* out;
+  int out_bf16;
+  int64_t ldo;
+  int wstages;  // weight stages
+  int row_tiles;
+  int tok_tiles;
+};
+struct GemmTmMaps {
+  CUtensorMap x;  // activations [K/16 chunks][m tokens][16 bytes], box 16 x 128 x 16
+};
+cudaError_t launch_gemm_tm(const GemmTmParams& p, const GemmTmMaps& maps, int grid, cudaStream_t stream);
+uint32_t gemm_tm_smem_bytes(int wstages);
+int gemm_tm_max_wstages();
+int gemm_tm_tile_tokens();
+// Activation scales [m][K/32] -> atoms [ceil(m/128)][K/128][32][16] (bytes: m_pad * K / 32).
+cudaError_t launch_xs_atoms(const uint8_t* xs, int64_t ldxs, int m, int n_blocks, uint8_t* atoms, cudaStream_t stream);
+
 cudaError_t launch_wait_selftest(unsigned long long limit_ns, cudaStream_t stream);
 cudaError_t probe_kernel_image();
 

@@ -4,10 +4,13 @@ Mirror of src/python/mambo/kernels/iq3_s_fp8.py (Menooker/Mambo): the same
 constants, codebook helpers, launch wrappers, errors and benchmark-case
 factory. The kernels are hand-written CUDA in libmambo_b200.so:
 
-* decode-sized M (< LARGE_TOKEN_THRESHOLD... and up to 32 tokens per launch):
-  a weight-streaming GEMV that stages IQ3_S fields with TMA, decodes each
-  IQ3_S code straight into an FP8 tensor-core fragment and splits K across all
-  SMs (stream-K, deterministic fixup);
+* decode-sized M (< LARGE_TOKEN_THRESHOLD): a weight-streaming tcgen05 GEMV
+  that bulk-copies tile-major IQ3_S records, decodes them into E4M3 bytes in
+  tensor memory and splits K across all SMs (stream-K with a deterministic
+  fixup, or a thread-block-cluster K split);
+* prefill-sized M (>= LARGE_TOKEN_THRESHOLD): a tcgen05 GEMM over 128-row x
+  128-token tiles with the same decoder, one block-scaled MMA per 32-weight
+  group and the per-group FP32 rescale in the epilogue;
 * the standalone decoder used by the bit-exactness tests.
 
 Arithmetic follows the reference exactly: every 32-weight group's E4M3 x E4M3
@@ -53,8 +56,9 @@ BEST_CONFIGS = {
     "sm100": {
         "medium": {"kernel": _lib.MAMBO_KERNEL_GEMV, "warps": 8, "stages": 6, "ctas_per_sm": 1, "split": 0,
                    "prefetch": 4},
-        "large": {"kernel": _lib.MAMBO_KERNEL_GEMV, "warps": 8, "stages": 4, "ctas_per_sm": 1, "split": 0,
-                  "prefetch": 4},
+        # AUTO: the GEMM where it applies (packed weights, 16-byte aligned
+        # activation rows), else the GEMV in 32-token chunks.
+        "large": {"kernel": _lib.MAMBO_KERNEL_AUTO, "warps": 8, "stages": 4, "ctas_per_sm": 1, "split": 0},
     },
 }
 LARGE_TOKEN_THRESHOLD = 32
@@ -285,7 +289,8 @@ def make_benchmark_cases(iq3_weight, ms: tuple[int, ...] = (4, 128), seed: int =
 
         return BenchmarkCase(
             name=f"M={m} N={n_rows} K={k}", stream=stream, kernel=run,
-            search_space=config_search_space(),
+            search_space=config_search_space(_lib.MAMBO_KERNEL_GEMM if m >= LARGE_TOKEN_THRESHOLD
+                                             else _lib.MAMBO_KERNEL_GEMV),
             grid_fn=lambda config: (config.get("ctas_per_sm", 1),),
             args_fn=lambda config: (config,),
             hints_fn=None,

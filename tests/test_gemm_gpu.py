@@ -1,0 +1,139 @@
+"""GPU parity of the tcgen05 prefill GEMM (M >= LARGE_TOKEN_THRESHOLD) against the oracle.
+
+The reference's large-token kernel (iq3_s_fp8.py:225-276) forms every
+32-weight group's block-scaled E4M3 product in FP32 and accumulates it scaled
+by d*(1+2*nibble); the cases below follow test_iq3_s_fp8.py's matmul tests
+(ragged M and N, f32 output) and add the prefill shapes of the north star with
+the outlier activations it names.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import iq3s_oracle as O
+from mambo_b200 import _lib
+from mambo_b200.kernels.iq3_s_fp8 import launch_dequant_iq3_s, launch_iq3_s_fp8_matmul
+from mambo_b200.kernels.quantize_fp8 import launch_quantize_fp8
+from mambo_b200.utils.iq3_s_weight import prepare_iq3_s_fields
+
+pytestmark = pytest.mark.gpu
+
+REL_FROB_TOL = 1e-3    # north star: vs fp32/f64 matmul of the dequantized operands
+ORACLE_FROB_TOL = 1e-4  # vs the float64 oracle on the same MXFP8 inputs (FP32 accumulation only)
+GEMM = {"kernel": _lib.MAMBO_KERNEL_GEMM, "warps": 8, "stages": 4}
+
+
+def to_np(t: torch.Tensor) -> np.ndarray:
+    return t.detach().cpu().numpy()
+
+
+def _case(dev, m, n, k, seed, outliers=False):
+    raw = O.make_synthetic_iq3s(n, k, seed)
+    rng = np.random.default_rng(seed + 1)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    if outliers:
+        cols = rng.permutation(k)[: max(1, round(0.01 * k))]
+        x[:, cols] *= 50.0
+    xq, xs = O.quantize_mxfp8(x)
+    ref = O.iq3s_linear_f64(xq, xs, raw)
+    fields = prepare_iq3_s_fields(torch.from_numpy(raw).to(dev))
+    return fields, torch.from_numpy(xq).to(dev), torch.from_numpy(xs).to(dev), ref
+
+
+@pytest.mark.parametrize("m,n,k,outliers", [(32, 256, 512, False), (128, 128, 256, False), (130, 384, 1024, True),
+                                            (257, 136, 512, False), (64, 640, 1536, True), (300, 256, 2048, True)])
+@pytest.mark.parametrize("stages", [2, 3, 4])
+def test_gemm_matches_oracle(cuda_device, m, n, k, outliers, stages):
+    fields, xq, xs, ref = _case(cuda_device, m, n, k, seed=900 + m + n + stages, outliers=outliers)
+    out = launch_iq3_s_fp8_matmul(xq, xs, fields, config=dict(GEMM, stages=stages))
+    got = to_np(out).astype(np.float64)
+    assert O.relative_frobenius(got, ref) < ORACLE_FROB_TOL
+    np.testing.assert_allclose(got, ref, rtol=5e-4, atol=5e-4 * np.abs(ref).max())
+
+
+def test_gemm_bf16_output(cuda_device):
+    fields, xq, xs, ref = _case(cuda_device, 160, 512, 1024, seed=7)
+    out = launch_iq3_s_fp8_matmul(xq, xs, fields, out_dtype=torch.bfloat16, config=GEMM)
+    assert out.dtype == torch.bfloat16
+    assert O.relative_frobenius(to_np(out.float()), ref) < 4e-3  # bf16 output rounding
+
+
+def test_default_config_picks_the_gemm_at_large_m(cuda_device):
+    lib = _lib.load()
+    for m, kind in ((8, _lib.MAMBO_KERNEL_GEMV), (31, _lib.MAMBO_KERNEL_GEMV), (32, _lib.MAMBO_KERNEL_GEMM),
+                    (4096, _lib.MAMBO_KERNEL_GEMM)):
+        c = _lib.MamboLinearConfig()
+        _lib.check(lib.mambo_default_config(m, 4096, 16, c))
+        assert c.kernel == kind, (m, c.kernel)
+    # and the default path gives the oracle's result
+    fields, xq, xs, ref = _case(cuda_device, 96, 256, 768, seed=21)
+    out = launch_iq3_s_fp8_matmul(xq, xs, fields)
+    assert O.relative_frobenius(to_np(out), ref) < ORACLE_FROB_TOL
+
+
+def test_gemm_agrees_with_chunked_gemv(cuda_device):
+    """Two independent kernels, same arithmetic: only FP32 summation order differs."""
+    fields, xq, xs, ref = _case(cuda_device, 96, 1024, 2048, seed=33, outliers=True)
+    a = launch_iq3_s_fp8_matmul(xq, xs, fields, config=GEMM)
+    b = launch_iq3_s_fp8_matmul(xq, xs, fields, config={"kernel": _lib.MAMBO_KERNEL_GEMV, "warps": 8, "stages": 4})
+    assert O.relative_frobenius(to_np(a), to_np(b).astype(np.float64)) < 1e-5
+
+
+def test_gemm_is_deterministic(cuda_device):
+    fields, xq, xs, _ = _case(cuda_device, 200, 384, 1024, seed=44)
+    a = launch_iq3_s_fp8_matmul(xq, xs, fields, config=GEMM)
+    b = launch_iq3_s_fp8_matmul(xq, xs, fields, config=GEMM)
+    assert torch.equal(a, b)
+
+
+def test_unaligned_activations_fall_back_or_raise(cuda_device):
+    """The GEMM's TMA needs 16-byte aligned rows: the default path falls back to the GEMV; an explicit GEMM raises."""
+    fields, xq, xs, ref = _case(cuda_device, 48, 256, 512, seed=55)
+    buf = torch.empty(xq.numel() + 1, dtype=torch.uint8, device=cuda_device)
+    odd = buf[1:].view(xq.shape)
+    odd.copy_(xq)
+    out = launch_iq3_s_fp8_matmul(odd, xs, fields)
+    assert O.relative_frobenius(to_np(out), ref) < ORACLE_FROB_TOL
+    with pytest.raises(ValueError):
+        launch_iq3_s_fp8_matmul(odd, xs, fields, config=GEMM)
+
+
+def test_gemm_without_packed_weights_falls_back(cuda_device):
+    raw = O.make_synthetic_iq3s(256, 512, 66)
+    soa = prepare_iq3_s_fields(torch.from_numpy(raw).to(cuda_device), packed=False)
+    rng = np.random.default_rng(67)
+    xq, xs = O.quantize_mxfp8(rng.standard_normal((40, 512)).astype(np.float32))
+    ref = O.iq3s_linear_f64(xq, xs, raw)
+    out = launch_iq3_s_fp8_matmul(torch.from_numpy(xq).to(cuda_device), torch.from_numpy(xs).to(cuda_device), soa)
+    assert O.relative_frobenius(to_np(out), ref) < ORACLE_FROB_TOL
+
+
+LLAMA3_8B = {"qkv": (6144, 4096), "o": (4096, 4096), "gate_up": (14336, 4096), "down": (4096, 14336)}
+
+
+@pytest.mark.parametrize("proj", sorted(LLAMA3_8B))
+@pytest.mark.parametrize("m", [512, 2048])
+def test_full_size_prefill_frobenius(cuda_device, proj, m):
+    """Prefill shapes with 1% outlier columns (x50): GPU float64 reference of the dequantized operands."""
+    n, k = LLAMA3_8B[proj]
+    gen = torch.Generator(device=cuda_device).manual_seed(101 + m)
+    raw = torch.randint(0, 256, (n, k // 256, 110), dtype=torch.uint8, device=cuda_device, generator=gen)
+    d = (torch.rand((n, k // 256), device=cuda_device, generator=gen) * 9e-3 + 1e-3).half()
+    raw[..., :2] = d.view(torch.uint8).view(n, k // 256, 2)
+    fields = prepare_iq3_s_fields(raw)
+    x = torch.randn((m, k), device=cuda_device, generator=gen)
+    cols = torch.randperm(k, device=cuda_device, generator=gen)[: round(0.01 * k)]
+    x[:, cols] *= 50.0
+    xq, xs = launch_quantize_fp8(x.to(torch.bfloat16))
+    out = launch_iq3_s_fp8_matmul(xq, xs, fields)
+    bits, scales = launch_dequant_iq3_s(fields)
+    lut = torch.from_numpy(O.decode_e4m3(np.arange(256, dtype=np.uint8))).to(cuda_device)
+    w = (lut[bits.long()] * scales.repeat_interleave(32, dim=1)).double()
+    del bits, scales
+    xe = lut[xq.long()].double() * torch.exp2(xs.double() - 127).repeat_interleave(32, dim=1)
+    ref = xe @ w.t()
+    err = (torch.linalg.norm(out.double() - ref) / torch.linalg.norm(ref)).item()
+    assert err < REL_FROB_TOL, err
