@@ -1,0 +1,177 @@
+"""Tensor-parallel IQ3_S x MXFP8 linears: one process per GPU, NCCL collectives.
+
+The projection shards without splitting a quantization block:
+
+* column split (QKV, gate, up): rank r holds weight rows [n0, n1) -- a slice
+  of every IQ3_S block row, no exchange inside the linear -- and produces
+  out[:, n0:n1]; an all-gather along N gives the full output when asked.
+* row split (O, down): rank r holds K blocks [b0, b1) of every row (super-
+  blocks of 256 weights, so an MXFP8 group of 32 never straddles ranks) and
+  the matching K slice of the activations, and produces an FP32 partial of
+  the full output; an all-reduce (sum) combines the partials.
+
+Shard sizes: N is split into multiples of 8 rows (the packed weight records),
+K into whole 256-weight blocks; ``K % (256 * world) == 0`` and
+``N % (8 * world) == 0`` are required, as for every Llama-3 shape.
+
+The collectives go through ``torch.distributed`` (NCCL on GPUs, gloo in the
+CPU tests). The per-rank compute is the single-GPU path of this package;
+``linear``/``quantize`` can be replaced (the CPU tests plug in a restatement).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable
+
+import torch
+import torch.distributed as dist
+
+COLUMN = "column"
+ROW = "row"
+
+
+def shard_range(total: int, rank: int, world: int, unit: int) -> tuple[int, int]:
+    """[start, end) of rank's equal share of `total` items, in whole `unit`s."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} is not in a world of {world}")
+    if total % (unit * world):
+        raise ValueError(f"{total} does not split into {world} shards of whole {unit}-item units")
+    per = total // world
+    return rank * per, (rank + 1) * per
+
+
+def shard_iq3_s_blocks(raw: torch.Tensor, mode: str, rank: int, world: int) -> torch.Tensor:
+    """This rank's slice of GGUF IQ3_S blocks uint8 [N, K/256, 110] (a view; prepare it afterwards)."""
+    if raw.ndim != 3 or raw.shape[2] != 110:
+        raise ValueError("IQ3_S weight must be uint8 [N,K/256,110]")
+    if mode == COLUMN:
+        n0, n1 = shard_range(raw.shape[0], rank, world, 8)
+        return raw[n0:n1]
+    if mode == ROW:
+        b0, b1 = shard_range(raw.shape[1], rank, world, 1)
+        return raw[:, b0:b1]
+    raise ValueError(f"mode must be {COLUMN!r} or {ROW!r}")
+
+
+def _default_quantize(x: torch.Tensor):
+    from .kernels.quantize_fp8 import launch_quantize_fp8
+
+    return launch_quantize_fp8(x)
+
+
+def _default_linear(xq: torch.Tensor, xs: torch.Tensor, fields, out_dtype: torch.dtype) -> torch.Tensor:
+    from .kernels.iq3_s_fp8 import launch_iq3_s_fp8_matmul
+
+    return launch_iq3_s_fp8_matmul(xq, xs, fields, out_dtype=out_dtype)
+
+
+def _default_prepare(raw: torch.Tensor):
+    from .utils.iq3_s_weight import prepare_iq3_s_fields
+
+    return prepare_iq3_s_fields(raw)
+
+
+@dataclass
+class CollectiveTimes:
+    """Device time of the last forward's collective (ms), when timing was asked for."""
+
+    collective_ms: float = 0.0
+
+
+class TensorParallelIQ3SLinear:
+    """One rank's shard of an IQ3_S x MXFP8 linear y = x @ W^T.
+
+    ``raw``: the FULL uint8 [N, K/256, 110] weight (each rank keeps only its
+    slice) or, with ``raw_is_shard``, this rank's slice already.
+    ``mode``: COLUMN or ROW. ``gather_output`` (COLUMN): all-gather the
+    [M, N/P] shards into [M, N]. ``input_is_sharded`` (ROW): the activation
+    passed to forward is this rank's K slice [M, K/P] instead of [M, K].
+    """
+
+    def __init__(self, raw: torch.Tensor, mode: str, *, group=None, raw_is_shard: bool = False,
+                 gather_output: bool = True, input_is_sharded: bool = False,
+                 out_dtype: torch.dtype = torch.bfloat16,
+                 prepare: Callable | None = None, quantize: Callable | None = None, linear: Callable | None = None):
+        if mode not in (COLUMN, ROW):
+            raise ValueError(f"mode must be {COLUMN!r} or {ROW!r}")
+        if out_dtype not in (torch.float32, torch.bfloat16):
+            raise ValueError("out_dtype must be torch.float32 or torch.bfloat16")
+        self.mode = mode
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.gather_output = gather_output
+        self.input_is_sharded = input_is_sharded
+        self.out_dtype = out_dtype
+        self._quantize = quantize or _default_quantize
+        self._linear = linear or _default_linear
+        if raw_is_shard:
+            local = raw
+            full_n = raw.shape[0] * (self.world if mode == COLUMN else 1)
+            full_b = raw.shape[1] * (self.world if mode == ROW else 1)
+        else:
+            local = shard_iq3_s_blocks(raw, mode, self.rank, self.world)
+            full_n, full_b = raw.shape[0], raw.shape[1]
+        self.n, self.k = full_n, full_b * 256
+        self.local_n, self.local_k = local.shape[0], local.shape[1] * 256
+        if mode == COLUMN:
+            self.n0 = self.rank * self.local_n
+            self.k0 = 0
+        else:
+            self.n0 = 0
+            self.k0 = self.rank * self.local_k
+        self.fields = (prepare or _default_prepare)(local)
+        self.times = CollectiveTimes()
+
+    def forward(self, x: torch.Tensor, *, time_collective: bool = False) -> torch.Tensor:
+        """x: [M, K] (or [M, K/P] for a row split with sharded input) -> [M, N] (or [M, N/P])."""
+        if x.ndim != 2:
+            raise ValueError("activation must be [M,K]")
+        if self.mode == COLUMN:
+            if x.shape[1] != self.k:
+                raise ValueError(f"column-split activation must be [M,{self.k}]")
+            xq, xs = self._quantize(x)
+            y = self._linear(xq, xs, self.fields, self.out_dtype)
+            if not self.gather_output or self.world == 1:
+                return y
+            return self._timed(time_collective, lambda: self._gather_columns(y))
+        # Row split: this rank's K slice (whole 256-weight blocks: MXFP8 groups stay intact).
+        if self.input_is_sharded:
+            if x.shape[1] != self.local_k:
+                raise ValueError(f"sharded row-split activation must be [M,{self.local_k}]")
+            xq, xs = self._quantize(x)
+        else:
+            if x.shape[1] != self.k:
+                raise ValueError(f"row-split activation must be [M,{self.k}]")
+            xq, xs = self._quantize(x[:, self.k0:self.k0 + self.local_k])
+        partial = self._linear(xq, xs, self.fields, torch.float32)
+        if self.world > 1:
+            self._timed(time_collective, lambda: dist.all_reduce(partial, op=dist.ReduceOp.SUM, group=self.group))
+        return partial if self.out_dtype == torch.float32 else partial.to(self.out_dtype)
+
+    __call__ = forward
+
+    def _gather_columns(self, y: torch.Tensor) -> torch.Tensor:
+        if dist.get_backend(self.group) == "nccl":
+            # One buffer: gather the [N/P, M] shards along dim 0, then transpose back.
+            yt = y.t().contiguous()
+            full = torch.empty((self.world * yt.shape[0], yt.shape[1]), dtype=y.dtype, device=y.device)
+            dist.all_gather_into_tensor(full, yt, group=self.group)
+            return full.t().contiguous()
+        parts = [torch.empty_like(y) for _ in range(self.world)]
+        dist.all_gather(parts, y.contiguous(), group=self.group)
+        return torch.cat(parts, dim=1)
+
+    def _timed(self, on: bool, fn):
+        if not on or not torch.cuda.is_available():
+            return fn()
+        dev = torch.cuda.current_device()
+        s = torch.cuda.current_stream(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        out = fn()
+        e1.record(s)
+        e1.synchronize()
+        self.times.collective_ms = e0.elapsed_time(e1)
+        return out
