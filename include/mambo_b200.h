@@ -72,19 +72,22 @@ typedef struct MamboIQ3SWeight {
 /* Launch configuration of the linear kernels (NULL = tuned default for the shape). */
 typedef struct MamboLinearConfig {
   int kernel;        /* MAMBO_KERNEL_* */
-  int warps;         /* GEMV: decoder warps (8, 16); GEMV_SYNC: compute warps (16 weight rows each) */
-  int stages;        /* shared-memory pipeline depth */
+  int warps;         /* GEMV: decoder warps (8, 16); GEMV_SYNC: compute warps (16 weight rows each); GEMM: 8 */
+  int stages;        /* shared-memory pipeline depth (GEMV, GEMM: weight stages) */
   int ctas_per_sm;   /* GEMV_SYNC: persistent grid = SMs * ctas_per_sm (0 = 1); GEMV: 0 or 1 */
-  int split;         /* 0 = stream-K over all SMs, 1 = one CTA per row tile */
+  int split;         /* GEMV: 0 = stream-K over all SMs, 1 = one CTA per row tile, 2 = K split in clusters */
   int loader;        /* GEMV_SYNC weight staging: 0 = TMA when the layout allows it, 1 = plain loads */
   int prefetch;      /* GEMV: work units whose weights are prefetched into L2 beyond the stage ring */
   int reserved;
 } MamboLinearConfig;
 
 /* Kernel kinds: GEMV = weight-streaming decode kernel on tcgen05 tensor cores
- * (the default); GEMM = tcgen05 kernel for large M; GEMV_SYNC = the same
- * weight-streaming kernel on legacy mma.sync FP8 instructions, kept as a
- * measured baseline (on sm_100 its FP8 fragments go through conversions). */
+ * (the default below 32 tokens); GEMM = tcgen05 kernel over 128-row x
+ * 128-token tiles (the default from 32 tokens; needs the packed weight copy
+ * and 16-byte aligned activation rows); GEMV_SYNC = the weight-streaming
+ * kernel on legacy mma.sync FP8 instructions, kept as a measured baseline (on
+ * sm_100 its FP8 fragments go through conversions). AUTO = pick by M as the
+ * reference does with LARGE_TOKEN_THRESHOLD (iq3_s_fp8.py:384-399). */
 enum { MAMBO_KERNEL_AUTO = 0, MAMBO_KERNEL_GEMV = 1, MAMBO_KERNEL_GEMM = 2, MAMBO_KERNEL_GEMV_SYNC = 3 };
 
 /* Library version string. */
