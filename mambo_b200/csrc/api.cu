@@ -250,10 +250,12 @@ int cluster_kparts(int row_tiles, int64_t b, const MamboLinearConfig& cfg, int n
   return kp;
 }
 
-// The GEMM's activation scales in scale-factor atom layout: 1 KB per (128-token tile, K block).
+// The GEMM's activation scales in scale-factor atom layout, 1 KB per
+// (128-token tile, K block), after the split-K counters: those must stay zero
+// for the GEMV calls that share the workspace.
 size_t gemm_workspace_bytes(int64_t m, int64_t b) {
   const int64_t tok = gemm_tm_tile_tokens();
-  return align256((size_t)((m + tok - 1) / tok) * (size_t)b * 1024);
+  return kCounterBytes + align256((size_t)((m + tok - 1) / tok) * (size_t)b * 1024);
 }
 
 // The GEMM reads activations through a TMA map (16-byte aligned rows) and
@@ -301,7 +303,7 @@ int launch_gemm(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t ldxs
   if ((int)gemm_tm_smem_bytes(c.stages) > info.max_smem_optin)
     return fail(MAMBO_EINVAL, "configuration needs %u bytes of shared memory (device allows %d)",
                 gemm_tm_smem_bytes(c.stages), info.max_smem_optin);
-  uint8_t* atoms = (uint8_t*)workspace;
+  uint8_t* atoms = (uint8_t*)workspace + kCounterBytes;
   cudaError_t e = launch_xs_atoms(xs, ldxs, (int)m, (int)w->n_blocks, atoms, stream);
   if (e != cudaSuccess) return cuda_fail(e, "iq3s_xs_atoms");
   GemmTmMaps maps;

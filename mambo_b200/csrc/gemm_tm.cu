@@ -297,7 +297,7 @@ __global__ void __launch_bounds__(kThreadsG, 1)
         uint32_t v[32];
 #pragma unroll
         for (int g = 0; g < 4; ++g)
-          tm::decode_group(table, qw[2 * g], qw[2 * g + 1], (hw >> (8 * g)) & 0xFFu, sw[g], l4, v + 8 * g);
+          tm::decode_group_packed(table, qw[2 * g], qw[2 * g + 1], hw, 2u * (uint32_t)g, sw[g], l4, v + 8 * g);
         tc::st_cols<32>(tq + (uint32_t)(r * 64), v);
         tc::wait_st();
         tc::fence_before_sync();

@@ -300,8 +300,7 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
       rows = (uint32_t)min(kRows, p.n_rows - n0);
       base = (size_t)(u % p.n_blocks) * p.n_rows + n0;
     };
-    auto issue_weights = [&](int it) {
-      const int s = it % S;
+    auto issue_weights = [&](int it, int s) {
       const uint32_t full = kWfull + 8 * s;
       const uint32_t st = smem_u32(st0 + (size_t)s * L.stage);
       if (p.packed) {
@@ -332,13 +331,20 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
       __syncwarp();
     };
     const int pre = min(S, n_units);
-    for (int it = 0; it < pre; ++it) issue_weights(it);
+    for (int it = 0; it < pre; ++it) issue_weights(it, it);
     int pf = pre;
     for (; pf < min(n_units, pre + p.prefetch); ++pf) prefetch(pf);
+    int es = pre % S;
+    uint32_t eph = (uint32_t)(pre / S) & 1u;  // stage and phase of unit `it`
     for (int it = pre; it < n_units; ++it) {
-      const bool ok = mbar_wait_bounded(kEmpty + 8 * (it % S), ((it / S) & 1) ^ 1, kSiteGemvEmpty);
+      const bool ok = mbar_wait_bounded(kEmpty + 8 * es, eph ^ 1, kSiteGemvEmpty);
+      const int s = es;
+      if (++es == S) {
+        es = 0;
+        eph ^= 1;
+      }
       if (!__all_sync(0xFFFFFFFFu, ok)) return;
-      issue_weights(it);
+      issue_weights(it, s);
       for (; pf < min(n_units, it + 1 + p.prefetch); ++pf) prefetch(pf);
     }
     return;
@@ -355,13 +361,13 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
       tma_prefetch_desc(&maps.xs);
     }
     pdl_wait();
-    for (int j = 0; j < n_units; ++j) {
+    int kb = u0 % p.n_blocks;
+    for (int j = 0; j < n_units; ++j, kb = (kb + 1 == p.n_blocks) ? 0 : kb + 1) {
       const int x = j % AS;
       if (j >= AS) {
         const bool ok = mbar_wait_bounded(kXempty + 8 * x, ((j / AS) & 1) ^ 1, kSiteGemvEmpty);
         if (!__all_sync(0xFFFFFFFFu, ok)) return;
       }
-      const int kb = (u0 + j) % p.n_blocks;
       const uint32_t full = kXfull + 8 * x, slot = smem_u32(x0 + (size_t)x * L.xslot);
       if (lane == 0) {
         mbar_arrive_expect_tx(full, kBytesX);
@@ -446,16 +452,20 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
       off_q0 = L.qs + (cm ? part * 2048 + rl * 16 : rl * 64 + 16 * part);
       off_q1 = off_q0;
       off_sg = L.signs + (cm ? (part >> 1) * 2048 + rl * 16 + (part & 1) * 8 : rl * 32 + 8 * part);
-      off_qh = L.qh + (cm ? (part >> 1) * 512 + rl * 4 + (part & 1) * 2 : rl * 8 + 2 * part);
+      // Packed records: the whole 4-group qh word (its bits are permuted per group pair).
+      off_qh = L.qh + (cm ? (part >> 1) * 512 + rl * 4 : rl * 8 + 2 * part);
     }
+    // First group of this thread within its packed qh word (the word's shift base).
+    const uint32_t gl0 = kParts == 4 ? 2u * (uint32_t)(part & 1) : 0u;
+    int s = 0, r = 0;
+    uint32_t sph = 0, rph = 0;  // phases of stage s and ring slot r
     for (int it = 0; it < n_units; ++it) {
-      const int s = it % S, r = it % kRing;
       // A ring slot r is free once the epilogue is done with unit it - kRing.
-      const bool ok1 = mbar_try_wait(kWfull + 8 * s, (it / S) & 1);
-      const bool ok2 = it < kRing || mbar_try_wait(kEfree + 8 * r, ((it / kRing) & 1) ^ 1);
+      const bool ok1 = mbar_try_wait(kWfull + 8 * s, sph);
+      const bool ok2 = it < kRing || mbar_try_wait(kEfree + 8 * r, rph ^ 1);
       if (!__all_sync(0xFFFFFFFFu, ok1 && ok2)) {  // slow path, taken by the whole warp
-        bool ok = mbar_wait_bounded(kWfull + 8 * s, (it / S) & 1, kSiteGemvFull);
-        if (it >= kRing) ok = ok && mbar_wait_bounded(kEfree + 8 * r, ((it / kRing) & 1) ^ 1, kSiteGemvEmpty);
+        bool ok = mbar_wait_bounded(kWfull + 8 * s, sph, kSiteGemvFull);
+        if (it >= kRing) ok = ok && mbar_wait_bounded(kEfree + 8 * r, rph ^ 1, kSiteGemvEmpty);
         if (!__all_sync(0xFFFFFFFFu, ok)) return;
       }
       const uint8_t* st = st0 + (size_t)s * L.stage;
@@ -473,7 +483,7 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
         const uint2 g = *reinterpret_cast<const uint2*>(st + off_sg);
         qw[0] = a.x; qw[1] = a.y; qw[2] = a.z; qw[3] = a.w;
         sw[0] = g.x; sw[1] = g.y;
-        hw = *reinterpret_cast<const uint16_t*>(st + off_qh);
+        hw = cm ? *reinterpret_cast<const uint32_t*>(st + off_qh) : *reinterpret_cast<const uint16_t*>(st + off_qh);
       }
       if (part == 0) {
         // The row's d and scale nibbles for the epilogue (it forms d * (1 + 2*nibble)).
@@ -483,9 +493,15 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
       }
       // All groups first, then one store: the codebook loads of every group can be in flight together.
       uint32_t v[kGroups * 8];
+      if (cm) {
 #pragma unroll
-      for (int g = 0; g < kGroups; ++g)
-        tm::decode_group(table, qw[2 * g], qw[2 * g + 1], (hw >> (8 * g)) & 0xFFu, sw[g], l4, v + 8 * g);
+        for (int g = 0; g < kGroups; ++g)
+          tm::decode_group_packed(table, qw[2 * g], qw[2 * g + 1], hw, 2u * (gl0 + (uint32_t)g), sw[g], l4, v + 8 * g);
+      } else {
+#pragma unroll
+        for (int g = 0; g < kGroups; ++g)
+          tm::decode_group(table, qw[2 * g], qw[2 * g + 1], (hw >> (8 * g)) & 0xFFu, sw[g], l4, v + 8 * g);
+      }
       tc::st_cols<kGroups * 8>(tq + (uint32_t)(r * 64), v);
       tc::wait_st();
       tc::fence_before_sync();
@@ -495,6 +511,14 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
         mbar_arrive(kEmpty + 8 * s);
       }
       __syncwarp();  // reconverge before the next waits
+      if (++s == S) {
+        s = 0;
+        sph ^= 1;
+      }
+      if (++r == kRing) {
+        r = 0;
+        rph ^= 1;
+      }
     }
     return;
   }
@@ -516,7 +540,8 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
     // activation tile's rows read other bytes of shared memory; their columns
     // of D are never read.
     const uint32_t tsf = tmem + ((uint32_t)(32 * q) << 16) + tm_sfb_col(NT);
-    auto write_sf = [&](int j) -> bool {
+    // kbj: the K block of unit j (for the half of the scale row it uses).
+    auto write_sf = [&](int j, int kbj) -> bool {
       const int xj = j % AS;
       bool ok = mbar_try_wait(kXfull + 8 * xj, (j / AS) & 1);
       if (!__all_sync(0xFFFFFFFFu, ok)) {
@@ -524,20 +549,25 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
         if (!__all_sync(0xFFFFFFFFu, ok)) return false;
       }
       const uint2 v = *reinterpret_cast<const uint2*>(x0 + (size_t)xj * L.xslot + L.xs + lane * 16 +
-                                                      (((u0 + j) % p.n_blocks) & 1) * 8);
+                                                      (kbj & 1) * 8);
       const uint32_t vv[8] = {v.x, v.x, v.x, v.x, v.y, v.y, v.y, v.y};
       tc::st_x8(tsf + 8u * (uint32_t)(j % kRing), vv);
       return true;
     };
+    // K block of unit `it` and of unit it + kDBuf, advanced incrementally.
+    const int kb_first = u0 % p.n_blocks;
+    auto kb_step = [&](int kb) { return kb + 1 == p.n_blocks ? 0 : kb + 1; };
+    int kb_ahead = kb_first;
     bool sf_ok = true;
-    for (int j = 0; j < kDBuf && j < n_units; ++j) sf_ok = sf_ok && write_sf(j);
+    for (int j = 0; j < kDBuf && j < n_units; ++j, kb_ahead = kb_step(kb_ahead)) sf_ok = sf_ok && write_sf(j, kb_ahead);
     tc::wait_st();
     tc::fence_before_sync();
     __syncwarp();
     if (lane == 0) mbar_arrive(kSfInit);
     __syncwarp();
     int seg_begin = u0;
-    for (int it = 0, u = u0; sf_ok && u < u1; ++u, ++it) {
+    int kb_next = kb_first, rt_next = u0 / p.n_blocks;  // K block and row tile of unit `it`
+    for (int it = 0, u = u0; sf_ok && u < u1; ++u, ++it, kb_ahead = kb_step(kb_ahead)) {
       const int r = it % kRing, db = kDBuf == 2 ? (it & 1) : 0;
       const uint32_t mpar = kDBuf == 2 ? ((it >> 1) & 1) : (it & 1);
       bool ok = mbar_try_wait(kMdone + 8 * db, mpar);
@@ -581,14 +611,18 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
         }
       }
       // The MMAs of unit it + kDBuf wait for this D buffer: their scales first.
-      if (it + kDBuf < n_units && !write_sf(it + kDBuf)) break;
+      if (it + kDBuf < n_units && !write_sf(it + kDBuf, kb_ahead)) break;
       tc::wait_st();
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(kEfree + 8 * r);
       __syncwarp();  // reconverge before the next waits
 
-      const int kb = u % p.n_blocks, rt = u / p.n_blocks;
+      const int kb = kb_next, rt = rt_next;
+      if (++kb_next == p.n_blocks) {
+        kb_next = 0;
+        ++rt_next;
+      }
       if (!(kb == p.n_blocks - 1 || u == u1 - 1)) continue;
       const bool full_tile = (seg_begin % p.n_blocks == 0) && (kb == p.n_blocks - 1);
       const int row = rt * kRows + rl;

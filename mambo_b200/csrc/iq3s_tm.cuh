@@ -16,6 +16,7 @@ constexpr uint32_t kTableStageBytes = 512 * 4;
 // One tile-major record: the fields of a (128-row tile, K block) unit, written
 // by iq3s_pack_kernel. qs and signs are chunk-major ([16-byte chunk][row][16
 // bytes]), qh [4-byte column][row][4 bytes]; then d [row] and scales [row].
+// Sign and qh words are bit-permuted (see decode_group_packed).
 constexpr int kRecordRows = 128;
 constexpr uint32_t kRecQs = 0, kRecSigns = 8192, kRecQh = 12288, kRecD = 13312, kRecScales = 13568;
 constexpr uint32_t kRecordBytes = 14080;
@@ -50,6 +51,34 @@ static __device__ __forceinline__ void decode_group(const uint8_t* table, uint32
   v[5] = lop3_and_or((s4 & 0xF0u) * 0x01020408u, 0x80808080u, m5);
   v[6] = lop3_and_or((s6 & 0xFu) * 0x10204080u, 0x80808080u, m6);
   v[7] = lop3_and_or((sg >> 28) * 0x10204080u, 0x80808080u, m7);
+}
+
+// As decode_group, for the bit-permuted words of a packed record: hw is the
+// thread's 4-group qh word with code c's high bit of group g at bit 8j+7-(2g+h)
+// (c = 4h+j), hs = 2g for this group; sg is the group's sign word with weight
+// j of code c at bit 8j+7-c. Both expand with a shift and one LOP3.
+static __device__ __forceinline__ void decode_group_packed(const uint8_t* table, uint32_t q0, uint32_t q1,
+                                                           uint32_t hw, uint32_t hs, uint32_t sg, uint32_t l4,
+                                                           uint32_t* v) {
+  const uint32_t h0 = lop3_and_or(hw << hs, 0x80808080u, l4);         // byte j: h_j << 7 | lane << 2
+  const uint32_t h1 = lop3_and_or(hw << (hs + 1u), 0x80808080u, l4);  // codes 4..7
+  const uint32_t q0l = q0 & 0xFFFFu, q0h = q0 >> 16, q1l = q1 & 0xFFFFu, q1h = q1 >> 16;
+  const uint32_t m0 = *reinterpret_cast<const uint32_t*>(table + prmt(q0l, h0, 0x3204u));
+  const uint32_t m1 = *reinterpret_cast<const uint32_t*>(table + prmt(q0l, h0, 0x3215u));
+  const uint32_t m2 = *reinterpret_cast<const uint32_t*>(table + prmt(q0h, h0, 0x3206u));
+  const uint32_t m3 = *reinterpret_cast<const uint32_t*>(table + prmt(q0h, h0, 0x3217u));
+  const uint32_t m4 = *reinterpret_cast<const uint32_t*>(table + prmt(q1l, h1, 0x3204u));
+  const uint32_t m5 = *reinterpret_cast<const uint32_t*>(table + prmt(q1l, h1, 0x3215u));
+  const uint32_t m6 = *reinterpret_cast<const uint32_t*>(table + prmt(q1h, h1, 0x3206u));
+  const uint32_t m7 = *reinterpret_cast<const uint32_t*>(table + prmt(q1h, h1, 0x3217u));
+  v[0] = lop3_and_or(sg, 0x80808080u, m0);
+  v[1] = lop3_and_or(sg << 1, 0x80808080u, m1);
+  v[2] = lop3_and_or(sg << 2, 0x80808080u, m2);
+  v[3] = lop3_and_or(sg << 3, 0x80808080u, m3);
+  v[4] = lop3_and_or(sg << 4, 0x80808080u, m4);
+  v[5] = lop3_and_or(sg << 5, 0x80808080u, m5);
+  v[6] = lop3_and_or(sg << 6, 0x80808080u, m6);
+  v[7] = lop3_and_or(sg << 7, 0x80808080u, m7);
 }
 
 // Builds the lane-private codebook: `tw` holds this thread's share of the

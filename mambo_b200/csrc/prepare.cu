@@ -45,6 +45,30 @@ cudaError_t launch_iq3s_prepare(const PrepareParams& p, int num_sms, cudaStream_
 // [2 chunks][128 rows][16 B], qh [2 columns][128 rows][4 B], d [128] fp16,
 // scales [128][4 B]; rows past N are zero (N % 8 == 0, so a chunk never mixes
 // valid and padding rows).
+// Bit permutations of the packed record (the decoder's shift-and-mask forms):
+// a group's sign word, bit 4c+j (weight j of code c) -> bit 8j+7-c, so that
+// (w << c) & 0x80808080 puts code c's four signs on bit 7 of each byte;
+// a 4-group qh word, bit 8g+4h+j (code 4h+j of group g) -> bit 8j+7-(2g+h),
+// so that (w << (2g+h)) & 0x80808080 puts those codes' high index bits there.
+__device__ __forceinline__ uint32_t permute_sign_word(uint32_t w) {
+  uint32_t o = 0;
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o |= ((w >> (4 * c + j)) & 1u) << (8 * j + 7 - c);
+  return o;
+}
+__device__ __forceinline__ uint32_t permute_qh_word(uint32_t w) {
+  uint32_t o = 0;
+#pragma unroll
+  for (int g = 0; g < 4; ++g)
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) o |= ((w >> (8 * g + 4 * h + j)) & 1u) << (8 * j + 7 - (2 * g + h));
+  return o;
+}
+
 __global__ void iq3s_pack_kernel(const PackWeightParams p) {
   constexpr int kChunks = 14080 / 16;
   const int64_t tiles = (p.n_rows + 127) / 128;
@@ -58,15 +82,23 @@ __global__ void iq3s_pack_kernel(const PackWeightParams p) {
     if (off < 12288) {  // qs or signs: 16 bytes of one row
       const bool is_qs = off < 8192;
       const int o = is_qs ? off : off - 8192, c = o / 2048, r = (o % 2048) / 16;
-      if (t * 128 + r < p.n_rows)
+      if (t * 128 + r < p.n_rows) {
         v = __ldg(reinterpret_cast<const uint4*>((is_qs ? p.qs : p.signs) + (row0 + r) * (is_qs ? 64 : 32) + c * 16));
+        if (!is_qs) {
+          v.x = permute_sign_word(v.x);
+          v.y = permute_sign_word(v.y);
+          v.z = permute_sign_word(v.z);
+          v.w = permute_sign_word(v.w);
+        }
+      }
     } else if (off < 13312) {  // qh: 4 bytes of 4 consecutive rows
       const int o = off - 12288, c = o / 512, r = (o % 512) / 4;
       if (t * 128 + r < p.n_rows) {
         const uint8_t* src = p.qh + (row0 + r) * 8 + c * 4;
-        v = make_uint4(__ldg(reinterpret_cast<const uint32_t*>(src)), __ldg(reinterpret_cast<const uint32_t*>(src + 8)),
-                       __ldg(reinterpret_cast<const uint32_t*>(src + 16)),
-                       __ldg(reinterpret_cast<const uint32_t*>(src + 24)));
+        v = make_uint4(permute_qh_word(__ldg(reinterpret_cast<const uint32_t*>(src))),
+                       permute_qh_word(__ldg(reinterpret_cast<const uint32_t*>(src + 8))),
+                       permute_qh_word(__ldg(reinterpret_cast<const uint32_t*>(src + 16))),
+                       permute_qh_word(__ldg(reinterpret_cast<const uint32_t*>(src + 24))));
       }
     } else {  // d and scales: rows contiguous
       const bool is_d = off < 13568;

@@ -54,8 +54,10 @@ IQ3_S_SCALE_VALUES = 32
 # follow the reference convention: GPU SM version, then medium/large by M.
 BEST_CONFIGS = {
     "sm100": {
-        "medium": {"kernel": _lib.MAMBO_KERNEL_GEMV, "warps": 8, "stages": 6, "ctas_per_sm": 1, "split": 0,
-                   "prefetch": 4},
+        # split: the thread-block-cluster K split while every 128-row tile gets
+        # its own CTAs (select_config), stream-K beyond that.
+        "medium": {"kernel": _lib.MAMBO_KERNEL_GEMV, "warps": 8, "stages": 8, "ctas_per_sm": 1, "split": 2,
+                   "prefetch": 0},
         # AUTO: the GEMM where it applies (packed weights, 16-byte aligned
         # activation rows), else the GEMV in 32-token chunks.
         "large": {"kernel": _lib.MAMBO_KERNEL_AUTO, "warps": 8, "stages": 4, "ctas_per_sm": 1, "split": 0},
@@ -185,7 +187,15 @@ def select_config(m: int, n: int, k: int, device: torch.device) -> dict:
     sm = _sm_key(device)
     if sm not in BEST_CONFIGS:
         raise RuntimeError(f"IQ3_S FP8 matmul has no tuned config for {sm}")
-    return BEST_CONFIGS[sm]["medium" if m < LARGE_TOKEN_THRESHOLD else "large"]
+    cfg = BEST_CONFIGS[sm]["medium" if m < LARGE_TOKEN_THRESHOLD else "large"]
+    if cfg.get("split") == 2 and (n + 127) // 128 > _sm_count(device):
+        cfg = dict(cfg, split=0)
+    return cfg
+
+
+@lru_cache(maxsize=None)
+def _sm_count(device: torch.device) -> int:
+    return torch.cuda.get_device_properties(device).multi_processor_count
 
 
 def linear_into(x_values: torch.Tensor, x_scales: torch.Tensor, iq3_weight: IQ3SFields, out: torch.Tensor,

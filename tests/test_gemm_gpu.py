@@ -137,3 +137,17 @@ def test_full_size_prefill_frobenius(cuda_device, proj, m):
     ref = xe @ w.t()
     err = (torch.linalg.norm(out.double() - ref) / torch.linalg.norm(ref)).item()
     assert err < REL_FROB_TOL, err
+
+
+def test_gemv_after_gemm_on_one_stream(cuda_device):
+    """The GEMM and the GEMV share the per-stream workspace; the GEMV's split-K counters must stay zero."""
+    fields, xq, xs, _ = _case(cuda_device, 256, 1024, 2048, seed=77)
+    raw = O.make_synthetic_iq3s(1024, 2048, 77)
+    rng = np.random.default_rng(78)
+    for _ in range(2):
+        launch_iq3_s_fp8_matmul(xq, xs, fields, config=GEMM)
+        x8q, x8s = O.quantize_mxfp8(rng.standard_normal((8, 2048)).astype(np.float32))
+        ref = O.iq3s_linear_f64(x8q, x8s, raw)
+        out = launch_iq3_s_fp8_matmul(torch.from_numpy(x8q).to(cuda_device), torch.from_numpy(x8s).to(cuda_device),
+                                      fields)
+        assert O.relative_frobenius(to_np(out), ref) < ORACLE_FROB_TOL

@@ -273,9 +273,29 @@ def test_unaligned_activation_rows_match_oracle(cuda_device, m, which):
     assert O.relative_frobenius(to_np(out), ref) < ORACLE_FROB_TOL
 
 
+def _permute_sign_words(w: np.ndarray) -> np.ndarray:
+    """Packed-record sign words: bit 4c+j (weight j of code c) moves to bit 8j+7-c."""
+    o = np.zeros_like(w)
+    for c in range(8):
+        for j in range(4):
+            o |= ((w >> np.uint32(4 * c + j)) & np.uint32(1)) << np.uint32(8 * j + 7 - c)
+    return o
+
+
+def _permute_qh_words(w: np.ndarray) -> np.ndarray:
+    """Packed-record qh words (4 groups): bit 8g+4h+j moves to bit 8j+7-(2g+h)."""
+    o = np.zeros_like(w)
+    for g in range(4):
+        for h in range(2):
+            for j in range(4):
+                o |= ((w >> np.uint32(8 * g + 4 * h + j)) & np.uint32(1)) << np.uint32(8 * j + 7 - (2 * g + h))
+    return o
+
+
 @pytest.mark.parametrize("m,n,k", [(8, 520, 768), (3, 1024, 2048), (13, 136, 512)])
 def test_packed_layout_and_results_match_soa(cuda_device, m, n, k):
-    """Tile-major packed records hold the raw block bytes; both weight paths give identical outputs."""
+    """Tile-major packed records hold the block bytes (sign and qh words bit-permuted); both weight paths
+    give identical outputs."""
     raw, _, xq, xs, ref = _linear_case(cuda_device, m, n, k, seed=55 + n)
     soa = prepare_iq3_s_fields(torch.from_numpy(raw).to(cuda_device), packed=False)
     packed = prepare_iq3_s_fields(torch.from_numpy(raw).to(cuda_device))
@@ -287,8 +307,10 @@ def test_packed_layout_and_results_match_soa(cuda_device, m, n, k):
     for t in range(tiles):
         rows = pad[t * 128:(t + 1) * 128].transpose(1, 0, 2)  # [B, 128, 110]
         chunk_major = lambda f, w: f.reshape(blocks, 128, -1, w).transpose(0, 2, 1, 3).reshape(blocks, -1)  # noqa: E731
-        expect = np.concatenate([chunk_major(rows[:, :, 2:66], 16), chunk_major(rows[:, :, 74:106], 16),
-                                 chunk_major(rows[:, :, 66:74], 4), rows[:, :, 0:2].reshape(blocks, -1),
+        signs = _permute_sign_words(np.ascontiguousarray(rows[:, :, 74:106]).view("<u4")).view(np.uint8)
+        qh = _permute_qh_words(np.ascontiguousarray(rows[:, :, 66:74]).view("<u4")).view(np.uint8)
+        expect = np.concatenate([chunk_major(rows[:, :, 2:66], 16), chunk_major(signs, 16),
+                                 chunk_major(qh, 4), rows[:, :, 0:2].reshape(blocks, -1),
                                  rows[:, :, 106:110].reshape(blocks, -1)], axis=1)
         np.testing.assert_array_equal(rec[t], expect, err_msg=f"tile {t}")
     xq_t, xs_t = torch.from_numpy(xq).to(cuda_device), torch.from_numpy(xs).to(cuda_device)
