@@ -87,8 +87,18 @@ typedef struct MamboLinearConfig {
  * and 16-byte aligned activation rows); GEMV_SYNC = the weight-streaming
  * kernel on legacy mma.sync FP8 instructions, kept as a measured baseline (on
  * sm_100 its FP8 fragments go through conversions). AUTO = pick by M as the
- * reference does with LARGE_TOKEN_THRESHOLD (iq3_s_fp8.py:384-399). */
-enum { MAMBO_KERNEL_AUTO = 0, MAMBO_KERNEL_GEMV = 1, MAMBO_KERNEL_GEMM = 2, MAMBO_KERNEL_GEMV_SYNC = 3 };
+ * reference does with LARGE_TOKEN_THRESHOLD (iq3_s_fp8.py:384-399).
+ * GEMM_F16 = the large-M tcgen05 kernel with FP16 operands: the group scale
+ * (1+2*nibble) folded exactly into the weight operand and one FP32 accumulator
+ * per 256-wide K block; activations enter as FP16 relative to each token's
+ * largest scale (exact unless a group's scale is more than 2^12 below it). */
+enum {
+  MAMBO_KERNEL_AUTO = 0,
+  MAMBO_KERNEL_GEMV = 1,
+  MAMBO_KERNEL_GEMM = 2,
+  MAMBO_KERNEL_GEMV_SYNC = 3,
+  MAMBO_KERNEL_GEMM_F16 = 4
+};
 
 /* Library version string. */
 MAMBO_API const char* mambo_version(void);

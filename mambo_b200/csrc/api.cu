@@ -165,6 +165,7 @@ int kernel_of(const MamboLinearConfig& c) { return c.kernel == MAMBO_KERNEL_AUTO
 uint32_t config_smem(const MamboLinearConfig& c, int nt, int64_t b) {
   if (kernel_of(c) == MAMBO_KERNEL_GEMV_SYNC) return gemv_smem_bytes_host(c.warps * 16, nt, c.stages, (int)b);
   if (kernel_of(c) == MAMBO_KERNEL_GEMM) return gemm_tm_smem_bytes(c.stages);
+  if (kernel_of(c) == MAMBO_KERNEL_GEMM_F16) return gemm_f16_smem_bytes(c.stages);
   return gemv_tm_smem_bytes(nt, c.stages, 1);
 }
 
@@ -178,7 +179,7 @@ constexpr int kNumGemmConfigs = (int)(sizeof(kGemmStages) / sizeof(kGemmStages[0
 void default_config(int64_t m, int64_t n, int64_t b, MamboLinearConfig* cfg, int smem_optin, int sms) {
   std::memset(cfg, 0, sizeof(*cfg));
   if (m >= kGemmMinTokens) {
-    cfg->kernel = MAMBO_KERNEL_GEMM;
+    cfg->kernel = MAMBO_KERNEL_GEMM_F16;
     cfg->warps = 8;
     cfg->ctas_per_sm = 1;
     cfg->stages = 4;
@@ -199,11 +200,12 @@ void default_config(int64_t m, int64_t n, int64_t b, MamboLinearConfig* cfg, int
 
 int validate_config(const MamboLinearConfig* cfg, int64_t m, int64_t b, const DeviceInfo& info) {
   const int kind = kernel_of(*cfg);
-  if (kind != MAMBO_KERNEL_GEMV && kind != MAMBO_KERNEL_GEMV_SYNC && kind != MAMBO_KERNEL_GEMM)
+  if (kind != MAMBO_KERNEL_GEMV && kind != MAMBO_KERNEL_GEMV_SYNC && kind != MAMBO_KERNEL_GEMM &&
+      kind != MAMBO_KERNEL_GEMM_F16)
     return fail(MAMBO_EINVAL, "unknown kernel kind %d", cfg->kernel);
-  if (kind == MAMBO_KERNEL_GEMM) {
-    if (cfg->stages < 2 || cfg->stages > gemm_tm_max_wstages())
-      return fail(MAMBO_EINVAL, "stages must be in [2, %d]", gemm_tm_max_wstages());
+  if (kind == MAMBO_KERNEL_GEMM || kind == MAMBO_KERNEL_GEMM_F16) {
+    const int smax = kind == MAMBO_KERNEL_GEMM ? gemm_tm_max_wstages() : gemm_f16_max_wstages();
+    if (cfg->stages < 2 || cfg->stages > smax) return fail(MAMBO_EINVAL, "stages must be in [2, %d]", smax);
   } else if (kind == MAMBO_KERNEL_GEMV_SYNC) {
     if (cfg->warps != 4 && cfg->warps != 8 && cfg->warps != 12 && cfg->warps != 16)
       return fail(MAMBO_EINVAL, "warps must be 4, 8, 12 or 16");
@@ -256,6 +258,12 @@ int cluster_kparts(int row_tiles, int64_t b, const MamboLinearConfig& cfg, int n
 size_t gemm_workspace_bytes(int64_t m, int64_t b) {
   const int64_t tok = gemm_tm_tile_tokens();
   return kCounterBytes + align256((size_t)((m + tok - 1) / tok) * (size_t)b * 1024);
+}
+
+// The FP16 GEMM's workspace: the split-K counters (left zero for the GEMV),
+// the FP16 activations [m][K] and the per-token scales.
+size_t gemm_f16_workspace_bytes(int64_t m, int64_t b) {
+  return kCounterBytes + align256((size_t)m * (size_t)b * 256 * 2) + align256((size_t)m * 4);
 }
 
 // The GEMM reads activations through a TMA map (16-byte aligned rows) and
@@ -327,6 +335,48 @@ int launch_gemm(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t ldxs
   const int grid = (int)(tiles < info.sms ? tiles : info.sms);
   e = launch_gemm_tm(p, maps, grid, stream);
   if (e != cudaSuccess) return cuda_fail(e, "iq3s_gemm_tm");
+  return ok();
+}
+
+// The FP16-operand GEMM: activations to FP16 with per-token scales
+// (workspace), then one persistent launch over all tiles.
+int launch_gemm_f16_path(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t ldxs, int64_t m,
+                         const MamboIQ3SWeight* w, const uint32_t* fp8_table, void* out, int out_dtype, int64_t ldo,
+                         const MamboLinearConfig& c, const DeviceInfo& info, void* workspace, size_t workspace_bytes,
+                         cudaStream_t stream) {
+  const size_t need = gemm_f16_workspace_bytes(m, w->n_blocks);
+  if (!workspace || workspace_bytes < need)
+    return fail(MAMBO_EWORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+  if ((uintptr_t)workspace % 256) return fail(MAMBO_EINVAL, "workspace must be 256-byte aligned");
+  if ((int)gemm_f16_smem_bytes(c.stages) > info.max_smem_optin)
+    return fail(MAMBO_EINVAL, "configuration needs %u bytes of shared memory (device allows %d)",
+                gemm_f16_smem_bytes(c.stages), info.max_smem_optin);
+  const int64_t k = w->n_blocks * 256;
+  uint16_t* x16 = (uint16_t*)((uint8_t*)workspace + kCounterBytes);
+  float* tok_scale = (float*)((uint8_t*)x16 + align256((size_t)m * k * 2));
+  cudaError_t e = launch_x16(xq, ldxq, xs, ldxs, (int)m, k, x16, k, tok_scale, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "iq3s_x16");
+  GemmF16Maps maps;
+  std::memset(&maps, 0, sizeof(maps));
+  if (!make_gemm_x16_map(x16, k, (int)m, k, &maps.x16))
+    return fail(MAMBO_ECUDA, "could not encode the FP16 activation tensor map");
+  GemmF16Params p{};
+  p.m = (int)m;
+  p.n_rows = (int)w->n_rows;
+  p.n_blocks = (int)w->n_blocks;
+  p.packed = (const uint8_t*)w->packed;
+  p.tok_scale = tok_scale;
+  p.table = fp8_table;
+  p.out = out;
+  p.out_bf16 = out_dtype == MAMBO_BF16;
+  p.ldo = ldo;
+  p.wstages = c.stages;
+  p.row_tiles = (int)((w->n_rows + 127) / 128);
+  p.tok_tiles = (int)((m + 127) / 128);
+  const int64_t tiles = (int64_t)p.row_tiles * p.tok_tiles;
+  const int grid = (int)(tiles < info.sms ? tiles : info.sms);
+  e = launch_gemm_f16(p, maps, grid, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "iq3s_gemm_f16");
   return ok();
 }
 
@@ -526,7 +576,7 @@ int mambo_default_config(int64_t m, int64_t n_rows, int64_t n_blocks, MamboLinea
 
 int mambo_num_configs(int kernel) {
   if (kernel == MAMBO_KERNEL_GEMV || kernel == MAMBO_KERNEL_AUTO) return kNumTcConfigs;
-  if (kernel == MAMBO_KERNEL_GEMM) return kNumGemmConfigs;
+  if (kernel == MAMBO_KERNEL_GEMM || kernel == MAMBO_KERNEL_GEMM_F16) return kNumGemmConfigs;
   if (kernel == MAMBO_KERNEL_GEMV_SYNC) return kNumSyncConfigs;
   return 0;
 }
@@ -540,7 +590,7 @@ int mambo_config_at(int kernel, int index, MamboLinearConfig* cfg) {
   cfg->kernel = kernel;
   cfg->ctas_per_sm = 1;
   cfg->split = index % 2;
-  if (kernel == MAMBO_KERNEL_GEMM) {
+  if (kernel == MAMBO_KERNEL_GEMM || kernel == MAMBO_KERNEL_GEMM_F16) {
     cfg->split = 0;
     cfg->warps = 8;
     cfg->stages = kGemmStages[index];
@@ -569,11 +619,14 @@ size_t mambo_iq3s_linear_workspace_bytes(int64_t m, int64_t n_rows, int64_t n_bl
   // A GEMM call may fall back to the GEMV (unaligned activations, no packed
   // weight copy): room for both.
   MamboLinearConfig cv = c;
-  if (kernel_of(c) == MAMBO_KERNEL_GEMM) default_config(m < 32 ? m : 31, n_rows, n_blocks, &cv, smem_optin, sms);
+  if (kernel_of(c) == MAMBO_KERNEL_GEMM || kernel_of(c) == MAMBO_KERNEL_GEMM_F16)
+    default_config(m < 32 ? m : 31, n_rows, n_blocks, &cv, smem_optin, sms);
   const int64_t m_chunk = m < 32 ? m : 32;
   GemvPlan P = plan_gemv(m_chunk, n_rows, n_blocks, cv, sms, smem_optin);
   const size_t gemv = P.counters_bytes + P.partial_bytes + P.xcopy_bytes + P.xscopy_bytes;
-  const size_t gemm = kernel_of(c) == MAMBO_KERNEL_GEMM ? gemm_workspace_bytes(m, n_blocks) : 0;
+  const size_t gemm = kernel_of(c) == MAMBO_KERNEL_GEMM       ? gemm_workspace_bytes(m, n_blocks)
+                     : kernel_of(c) == MAMBO_KERNEL_GEMM_F16 ? gemm_f16_workspace_bytes(m, n_blocks)
+                                                             : 0;
   return gemv > gemm ? gemv : gemm;
 }
 
@@ -602,14 +655,17 @@ int mambo_iq3s_linear(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_
     c.kernel = a.kernel;
     if (c.stages == 0) c.stages = a.stages;
   }
-  if (c.kernel == MAMBO_KERNEL_GEMM) {
+  if (c.kernel == MAMBO_KERNEL_GEMM || c.kernel == MAMBO_KERNEL_GEMM_F16) {
     if (gemm_usable(w, xq, ldxq, m)) {
       st = validate_config(&c, 32, w->n_blocks, info);
       if (st != MAMBO_OK) return st;
+      if (c.kernel == MAMBO_KERNEL_GEMM_F16)
+        return launch_gemm_f16_path(xq, ldxq, xs, ldxs, m, w, fp8_table, out, out_dtype, ldo, c, info, workspace,
+                                    workspace_bytes, (cudaStream_t)stream);
       return launch_gemm(xq, ldxq, xs, ldxs, m, w, fp8_table, out, out_dtype, ldo, c, info, workspace,
                          workspace_bytes, (cudaStream_t)stream);
     }
-    if (cfg && cfg->kernel == MAMBO_KERNEL_GEMM)
+    if (cfg && (cfg->kernel == MAMBO_KERNEL_GEMM || cfg->kernel == MAMBO_KERNEL_GEMM_F16))
       return fail(MAMBO_EINVAL,
                   "the GEMM needs the tile-major packed weight copy (N %% 8 == 0) and 16-byte aligned activation rows");
     // Otherwise the GEMV in 32-token chunks.

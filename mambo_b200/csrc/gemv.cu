@@ -573,6 +573,17 @@ bool make_gemv_x_map(const uint8_t* xq, int64_t ldxq, int m, int n_blocks, int b
   return encode(fn, map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, xq, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
+bool make_gemm_x16_map(const uint16_t* x16, int64_t ld, int m, int64_t k, CUtensorMap* map) {
+  EncodeTiledFn fn = get_encode_fn();
+  if (!fn || (uintptr_t)x16 % 16 || (ld * 2) % 16 || m < 1 || k % 128) return false;
+  // [m tokens][K halves]: a box of 128 tokens x 64 halves (128 bytes) lands as
+  // eight 1024-byte atoms of the K-major 128-byte-swizzled UMMA layout.
+  cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)m};
+  cuuint64_t str[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {64, 128};
+  return encode(fn, map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, x16, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
 bool make_gemv_xs_map(const uint8_t* xs, int64_t ldxs, int m, int n_blocks, int box_tokens, CUtensorMap* map) {
   EncodeTiledFn fn = get_encode_fn();
   if (!fn || (uintptr_t)xs % 16 || ldxs % 16 || m < 1 || box_tokens > 256) return false;

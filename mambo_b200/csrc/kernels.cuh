@@ -187,6 +187,34 @@ cudaError_t launch_gemm_tm(const GemmTmParams& p, const GemmTmMaps& maps, int gr
 uint32_t gemm_tm_smem_bytes(int wstages);
 int gemm_tm_max_wstages();
 int gemm_tm_tile_tokens();
+// FP16-operand GEMM (A = sign*grid*(1+2*nibble) exact in FP16, one accumulator
+// per K block): activations converted to FP16 relative to a per-token power of two.
+struct GemmF16Params {
+  int m;
+  int n_rows;
+  int n_blocks;
+  const uint8_t* packed;       // tile-major weight records
+  const float* tok_scale;      // [m]: 2^(largest scale exponent of the token)
+  const uint32_t* table;       // uint32[512], E4M3-encoded magnitudes
+  void* out;
+  int out_bf16;
+  int64_t ldo;
+  int wstages;
+  int row_tiles;
+  int tok_tiles;
+};
+struct GemmF16Maps {
+  CUtensorMap x16;  // FP16 activations [m tokens][K], box 64 halves x 128 tokens, 128-byte swizzle
+};
+cudaError_t launch_gemm_f16(const GemmF16Params& p, const GemmF16Maps& maps, int grid, cudaStream_t stream);
+uint32_t gemm_f16_smem_bytes(int wstages);
+int gemm_f16_max_wstages();
+// MXFP8 activations -> FP16 x16[m][k] (row stride ld halves) = E4M3 * 2^(e_group - e_max(token)),
+// tok_scale[m] = 2^(e_max - 127). Exact while a group's exponent is within 12 of the token's largest.
+cudaError_t launch_x16(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t ldxs, int m, int64_t k,
+                       uint16_t* x16, int64_t ld, float* tok_scale, cudaStream_t stream);
+bool make_gemm_x16_map(const uint16_t* x16, int64_t ld, int m, int64_t k, CUtensorMap* map);
+
 // Activation scales [m][K/32] -> atoms [ceil(m/128)][K/128][32][16] (bytes: m_pad * K / 32).
 cudaError_t launch_xs_atoms(const uint8_t* xs, int64_t ldxs, int m, int n_blocks, uint8_t* atoms, cudaStream_t stream);
 

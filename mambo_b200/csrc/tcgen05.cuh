@@ -20,6 +20,19 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint
   return d;
 }
 
+// Shared-memory matrix descriptor, K-major with the 128-byte swizzle: 8-row x
+// 128-byte atoms (1024-byte aligned), `sbo` = distance between 8-row groups.
+// Layout type 2 (SWIZZLE_128B) at bits 61-63. A K step inside the 128-byte
+// row advances the start address by its byte offset.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t sbo) {
+  uint64_t d = (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)1 << 16;  // leading byte offset: unused for swizzled K-major
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
 // Instruction descriptor of kind::f8f6f4: D = F32, A = B = E4M3, both K-major.
 __host__ __device__ constexpr uint32_t idesc_e4m3_f32(int m, int n) {
   return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
@@ -32,6 +45,21 @@ __device__ __forceinline__ void mma_e4m3(uint32_t tmem_d, uint64_t desc_a, uint6
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
       "l"(desc_a), "l"(desc_b), "r"(idesc), "r"(accumulate));
+}
+
+// Instruction descriptor of kind::f16: D = F32, A = B = F16, both K-major.
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n) {
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+// D[tmem] (+)= A[tmem] x B[smem]^T with FP16 operands (K = 16), issued by one
+// thread. A occupies the TMEM lanes of its rows, two FP16 values per column.
+__device__ __forceinline__ void mma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t desc_b, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(desc_b), "r"(idesc), "r"(accumulate));
 }
 
 // D[tmem] (+)= A[tmem] x B[smem]^T, issued by one thread. A occupies the TMEM

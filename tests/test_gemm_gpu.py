@@ -24,6 +24,10 @@ pytestmark = pytest.mark.gpu
 REL_FROB_TOL = 1e-3    # north star: vs fp32/f64 matmul of the dequantized operands
 ORACLE_FROB_TOL = 1e-4  # vs the float64 oracle on the same MXFP8 inputs (FP32 accumulation only)
 GEMM = {"kernel": _lib.MAMBO_KERNEL_GEMM, "warps": 8, "stages": 4}
+GEMM_F16 = {"kernel": _lib.MAMBO_KERNEL_GEMM_F16, "warps": 8, "stages": 4}
+# The per-group FP8 kernel (the reference's decomposition) and the FP16-operand kernel (group scale folded
+# into the weight operand, one accumulator per K block).
+KINDS = {"fp8_groups": GEMM, "f16": GEMM_F16}
 
 
 def to_np(t: torch.Tensor) -> np.ndarray:
@@ -46,25 +50,27 @@ def _case(dev, m, n, k, seed, outliers=False):
 @pytest.mark.parametrize("m,n,k,outliers", [(32, 256, 512, False), (128, 128, 256, False), (130, 384, 1024, True),
                                             (257, 136, 512, False), (64, 640, 1536, True), (300, 256, 2048, True)])
 @pytest.mark.parametrize("stages", [2, 3, 4])
-def test_gemm_matches_oracle(cuda_device, m, n, k, outliers, stages):
+@pytest.mark.parametrize("kind", sorted(KINDS))
+def test_gemm_matches_oracle(cuda_device, m, n, k, outliers, stages, kind):
     fields, xq, xs, ref = _case(cuda_device, m, n, k, seed=900 + m + n + stages, outliers=outliers)
-    out = launch_iq3_s_fp8_matmul(xq, xs, fields, config=dict(GEMM, stages=stages))
+    out = launch_iq3_s_fp8_matmul(xq, xs, fields, config=dict(KINDS[kind], stages=stages))
     got = to_np(out).astype(np.float64)
     assert O.relative_frobenius(got, ref) < ORACLE_FROB_TOL
     np.testing.assert_allclose(got, ref, rtol=5e-4, atol=5e-4 * np.abs(ref).max())
 
 
-def test_gemm_bf16_output(cuda_device):
+@pytest.mark.parametrize("kind", sorted(KINDS))
+def test_gemm_bf16_output(cuda_device, kind):
     fields, xq, xs, ref = _case(cuda_device, 160, 512, 1024, seed=7)
-    out = launch_iq3_s_fp8_matmul(xq, xs, fields, out_dtype=torch.bfloat16, config=GEMM)
+    out = launch_iq3_s_fp8_matmul(xq, xs, fields, out_dtype=torch.bfloat16, config=KINDS[kind])
     assert out.dtype == torch.bfloat16
     assert O.relative_frobenius(to_np(out.float()), ref) < 4e-3  # bf16 output rounding
 
 
 def test_default_config_picks_the_gemm_at_large_m(cuda_device):
     lib = _lib.load()
-    for m, kind in ((8, _lib.MAMBO_KERNEL_GEMV), (31, _lib.MAMBO_KERNEL_GEMV), (32, _lib.MAMBO_KERNEL_GEMM),
-                    (4096, _lib.MAMBO_KERNEL_GEMM)):
+    for m, kind in ((8, _lib.MAMBO_KERNEL_GEMV), (31, _lib.MAMBO_KERNEL_GEMV), (32, _lib.MAMBO_KERNEL_GEMM_F16),
+                    (4096, _lib.MAMBO_KERNEL_GEMM_F16)):
         c = _lib.MamboLinearConfig()
         _lib.check(lib.mambo_default_config(m, 4096, 16, c))
         assert c.kernel == kind, (m, c.kernel)
@@ -74,18 +80,20 @@ def test_default_config_picks_the_gemm_at_large_m(cuda_device):
     assert O.relative_frobenius(to_np(out), ref) < ORACLE_FROB_TOL
 
 
-def test_gemm_agrees_with_chunked_gemv(cuda_device):
-    """Two independent kernels, same arithmetic: only FP32 summation order differs."""
+@pytest.mark.parametrize("kind", sorted(KINDS))
+def test_gemm_agrees_with_chunked_gemv(cuda_device, kind):
+    """Independent kernels, exact products: only the FP32 summation order differs."""
     fields, xq, xs, ref = _case(cuda_device, 96, 1024, 2048, seed=33, outliers=True)
-    a = launch_iq3_s_fp8_matmul(xq, xs, fields, config=GEMM)
+    a = launch_iq3_s_fp8_matmul(xq, xs, fields, config=KINDS[kind])
     b = launch_iq3_s_fp8_matmul(xq, xs, fields, config={"kernel": _lib.MAMBO_KERNEL_GEMV, "warps": 8, "stages": 4})
     assert O.relative_frobenius(to_np(a), to_np(b).astype(np.float64)) < 1e-5
 
 
-def test_gemm_is_deterministic(cuda_device):
+@pytest.mark.parametrize("kind", sorted(KINDS))
+def test_gemm_is_deterministic(cuda_device, kind):
     fields, xq, xs, _ = _case(cuda_device, 200, 384, 1024, seed=44)
-    a = launch_iq3_s_fp8_matmul(xq, xs, fields, config=GEMM)
-    b = launch_iq3_s_fp8_matmul(xq, xs, fields, config=GEMM)
+    a = launch_iq3_s_fp8_matmul(xq, xs, fields, config=KINDS[kind])
+    b = launch_iq3_s_fp8_matmul(xq, xs, fields, config=KINDS[kind])
     assert torch.equal(a, b)
 
 
@@ -97,8 +105,9 @@ def test_unaligned_activations_fall_back_or_raise(cuda_device):
     odd.copy_(xq)
     out = launch_iq3_s_fp8_matmul(odd, xs, fields)
     assert O.relative_frobenius(to_np(out), ref) < ORACLE_FROB_TOL
-    with pytest.raises(ValueError):
-        launch_iq3_s_fp8_matmul(odd, xs, fields, config=GEMM)
+    for cfg in KINDS.values():
+        with pytest.raises(ValueError):
+            launch_iq3_s_fp8_matmul(odd, xs, fields, config=cfg)
 
 
 def test_gemm_without_packed_weights_falls_back(cuda_device):
@@ -116,7 +125,8 @@ LLAMA3_8B = {"qkv": (6144, 4096), "o": (4096, 4096), "gate_up": (14336, 4096), "
 
 @pytest.mark.parametrize("proj", sorted(LLAMA3_8B))
 @pytest.mark.parametrize("m", [512, 2048])
-def test_full_size_prefill_frobenius(cuda_device, proj, m):
+@pytest.mark.parametrize("kind", sorted(KINDS))
+def test_full_size_prefill_frobenius(cuda_device, proj, m, kind):
     """Prefill shapes with 1% outlier columns (x50): GPU float64 reference of the dequantized operands."""
     n, k = LLAMA3_8B[proj]
     gen = torch.Generator(device=cuda_device).manual_seed(101 + m)
@@ -128,7 +138,7 @@ def test_full_size_prefill_frobenius(cuda_device, proj, m):
     cols = torch.randperm(k, device=cuda_device, generator=gen)[: round(0.01 * k)]
     x[:, cols] *= 50.0
     xq, xs = launch_quantize_fp8(x.to(torch.bfloat16))
-    out = launch_iq3_s_fp8_matmul(xq, xs, fields)
+    out = launch_iq3_s_fp8_matmul(xq, xs, fields, config=KINDS[kind])
     bits, scales = launch_dequant_iq3_s(fields)
     lut = torch.from_numpy(O.decode_e4m3(np.arange(256, dtype=np.uint8))).to(cuda_device)
     w = (lut[bits.long()] * scales.repeat_interleave(32, dim=1)).double()
@@ -146,8 +156,23 @@ def test_gemv_after_gemm_on_one_stream(cuda_device):
     rng = np.random.default_rng(78)
     for _ in range(2):
         launch_iq3_s_fp8_matmul(xq, xs, fields, config=GEMM)
+        launch_iq3_s_fp8_matmul(xq, xs, fields, config=GEMM_F16)
         x8q, x8s = O.quantize_mxfp8(rng.standard_normal((8, 2048)).astype(np.float32))
         ref = O.iq3s_linear_f64(x8q, x8s, raw)
         out = launch_iq3_s_fp8_matmul(torch.from_numpy(x8q).to(cuda_device), torch.from_numpy(x8s).to(cuda_device),
                                       fields)
         assert O.relative_frobenius(to_np(out), ref) < ORACLE_FROB_TOL
+
+
+def test_f16_operands_exact_across_wide_scale_ranges(cuda_device):
+    """Groups up to 2^12 below the token's largest scale stay exact in the FP16 activation operand."""
+    raw = O.make_synthetic_iq3s(256, 2048, 88)
+    rng = np.random.default_rng(89)
+    x = rng.standard_normal((64, 2048)).astype(np.float32)
+    x *= np.exp2(rng.integers(-12, 1, size=(64, 2048 // 32)).repeat(32, axis=1)).astype(np.float32)
+    xq, xs = O.quantize_mxfp8(x)
+    ref = O.iq3s_linear_f64(xq, xs, raw)
+    fields = prepare_iq3_s_fields(torch.from_numpy(raw).to(cuda_device))
+    out = launch_iq3_s_fp8_matmul(torch.from_numpy(xq).to(cuda_device), torch.from_numpy(xs).to(cuda_device), fields,
+                                  config=GEMM_F16)
+    assert O.relative_frobenius(to_np(out), ref) < ORACLE_FROB_TOL
