@@ -616,6 +616,11 @@ size_t mambo_iq3s_linear_workspace_bytes(int64_t m, int64_t n_rows, int64_t n_bl
                       st == MAMBO_OK ? info.sms : 148);
   const int sms = (st == MAMBO_OK && info.sms > 0) ? info.sms : 148;
   const int smem_optin = (st == MAMBO_OK && info.max_smem_optin > 0) ? info.max_smem_optin : kSmemOptinDefault;
+  if (c.kernel == MAMBO_KERNEL_AUTO) {  // resolved as mambo_iq3s_linear resolves it
+    MamboLinearConfig a;
+    default_config(m, n_rows, n_blocks, &a, smem_optin, sms);
+    c.kernel = a.kernel;
+  }
   // A GEMM call may fall back to the GEMV (unaligned activations, no packed
   // weight copy): room for both.
   MamboLinearConfig cv = c;

@@ -176,3 +176,13 @@ def test_f16_operands_exact_across_wide_scale_ranges(cuda_device):
     out = launch_iq3_s_fp8_matmul(torch.from_numpy(xq).to(cuda_device), torch.from_numpy(xs).to(cuda_device), fields,
                                   config=GEMM_F16)
     assert O.relative_frobenius(to_np(out), ref) < ORACLE_FROB_TOL
+
+
+def test_default_path_sizes_its_workspace_on_a_fresh_stream(cuda_device):
+    """The workspace query resolves the automatic kernel choice the way the call does."""
+    fields, xq, xs, ref = _case(cuda_device, 300, 256, 4096, seed=91)
+    stream = torch.cuda.Stream(cuda_device)
+    with torch.cuda.stream(stream):
+        out = launch_iq3_s_fp8_matmul(xq, xs, fields, stream=stream)
+    stream.synchronize()
+    assert O.relative_frobenius(to_np(out), ref) < ORACLE_FROB_TOL
