@@ -316,7 +316,7 @@ int launch_gemm(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t ldxs
   if (e != cudaSuccess) return cuda_fail(e, "iq3s_xs_atoms");
   GemmTmMaps maps;
   std::memset(&maps, 0, sizeof(maps));
-  if (!make_gemv_x_map(xq, ldxq, (int)m, (int)w->n_blocks, gemm_tm_tile_tokens(), &maps.x))
+  if (!make_gemm_x8_map(xq, ldxq, (int)m, w->n_blocks * 256, &maps.x))
     return fail(MAMBO_ECUDA, "could not encode the activation tensor map");
   GemmTmParams p{};
   p.m = (int)m;

@@ -14,8 +14,8 @@
 //  * warp 0, weight producer: one bulk copy of the unit's tile-major record
 //    (14080 bytes) into a ring of weight stages, refilled once decoded.
 //  * activation producer warp: after the previous kernel has finished
-//    (programmatic dependent launch), one 3D TMA copy of the unit's 128 x 256
-//    activation block into the UMMA B layout (rows past M read as zero) and one
+//    (programmatic dependent launch), two 2D TMA copies of the unit's 128 x 256
+//    activation block in 128-byte swizzled rows (rows past M read as zero) and one
 //    bulk copy of its scales, already in the tensor core's scale-factor atom
 //    layout (written by iq3s_xs_atoms_kernel), into a ring of 3 slots.
 //  * decoder warps (8): as in the GEMV, a thread owns a weight row (its TMEM
@@ -83,9 +83,10 @@ __device__ __forceinline__ void store_out_g(const GemmTmParams& p, int row, int 
 
 __global__ void __launch_bounds__(kThreadsG, 1)
     iq3s_gemm_tm_kernel(const __grid_constant__ GemmTmParams p, const __grid_constant__ GemmTmMaps maps) {
-  // B tile [16-byte K chunk][128 tokens][16 bytes]: K-direction core-matrix
-  // stride 128*16, token-group stride 128.
-  constexpr uint32_t kLbo = kTokG * 16u, kSbo = 128u;
+  // B tile: two [128 tokens][128 bytes] boxes in the 128-byte-swizzled
+  // K-major layout (8-row atoms 1024 bytes apart); group g (32 bytes of K)
+  // starts 32*(g%4) bytes into box g/4's rows.
+  constexpr uint32_t kBoxBytes = kTokG * 128u;
   constexpr uint32_t kIdesc = tc::idesc_mx_e4m3(kRowsG, kTokG, 0, 0);
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -189,7 +190,8 @@ __global__ void __launch_bounds__(kThreadsG, 1)
           if (it >= kXStagesG && !mbar_wait_bounded(kXempty + 8 * x, ph ^ 1, kSiteGemvEmpty)) return;
           const uint32_t full = kXfull + 8 * x, slot = smem_u32(x0 + (size_t)x * kXSlotG);
           mbar_arrive_expect_tx(full, kXSlotG);
-          tma_load_3d(slot, &maps.x, 0, tt * kTokG, kb * 16, full, keep);
+          tma_load_2d(slot, &maps.x, kb * 256, tt * kTokG, full, keep);
+          tma_load_2d(slot + kBoxBytes, &maps.x, kb * 256 + 128, tt * kTokG, full, keep);
           bulk_load_hint(slot + kBTileG, p.xs_atoms + ((size_t)tt * nq + 2 * kb) * 512, kSfBytesG, full, keep);
           if (++x == kXStagesG) {
             x = 0;
@@ -213,7 +215,7 @@ __global__ void __launch_bounds__(kThreadsG, 1)
         if (!ok) break;
         tc::fence_after_sync();
         const uint32_t xslot = smem_u32(x0 + (size_t)x * kXSlotG);
-        const uint64_t bdesc = tc::smem_desc(xslot, kLbo, kSbo);
+        const uint64_t bdesc = tc::smem_desc_sw128(xslot, 1024u);
         const uint32_t sfb = tmem + kTmSfb + 8u * (uint32_t)x, acol = tmem + kTmA + 64u * (uint32_t)r;
         if (tm::elect_one()) {
           // Groups 0-3 and 4-7 of the unit: 32 rows x 16 bytes each, 8-row core
@@ -232,7 +234,8 @@ __global__ void __launch_bounds__(kThreadsG, 1)
           tc::fence_after_sync();
           if (tm::elect_one()) {
             tc::mma_mx_e4m3_ts(tmem + kTmD + (uint32_t)(ds * kTokG), acol + (uint32_t)(g * 8),
-                               bdesc + (uint64_t)((2u * kLbo * (uint32_t)g) >> 4), kIdesc | ((uint32_t)(g & 3) << 4),
+                               bdesc + (uint64_t)((((uint32_t)g >> 2) * kBoxBytes + ((uint32_t)g & 3u) * 32u) >> 4),
+                               kIdesc | ((uint32_t)(g & 3) << 4),
                                tmem + kTmSfa, sfb + 4u * (uint32_t)(g >> 2), 0);
             tc::commit(kMdone + 8 * ds);
           }

@@ -573,6 +573,17 @@ bool make_gemv_x_map(const uint8_t* xq, int64_t ldxq, int m, int n_blocks, int b
   return encode(fn, map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, xq, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
+bool make_gemm_x8_map(const uint8_t* xq, int64_t ldxq, int m, int64_t k, CUtensorMap* map) {
+  EncodeTiledFn fn = get_encode_fn();
+  if (!fn || (uintptr_t)xq % 16 || ldxq % 16 || m < 1 || k % 128) return false;
+  // [m tokens][K bytes]: a box of 128 tokens x 128 bytes lands as eight
+  // 1024-byte atoms of the K-major 128-byte-swizzled UMMA layout.
+  cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)m};
+  cuuint64_t str[1] = {(cuuint64_t)ldxq};
+  cuuint32_t box[2] = {128, 128};
+  return encode(fn, map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, xq, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
 bool make_gemm_x16_map(const uint16_t* x16, int64_t ld, int m, int64_t k, CUtensorMap* map) {
   EncodeTiledFn fn = get_encode_fn();
   if (!fn || (uintptr_t)x16 % 16 || (ld * 2) % 16 || m < 1 || k % 128) return false;

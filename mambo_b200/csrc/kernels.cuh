@@ -181,8 +181,9 @@ struct GemmTmParams {
   int tok_tiles;
 };
 struct GemmTmMaps {
-  CUtensorMap x;  // activations [K/16 chunks][m tokens][16 bytes], box 16 x 128 x 16
+  CUtensorMap x;  // activations [m tokens][K bytes], box 128 bytes x 128 tokens, 128-byte swizzle
 };
+bool make_gemm_x8_map(const uint8_t* xq, int64_t ldxq, int m, int64_t k, CUtensorMap* map);
 cudaError_t launch_gemm_tm(const GemmTmParams& p, const GemmTmMaps& maps, int grid, cudaStream_t stream);
 uint32_t gemm_tm_smem_bytes(int wstages);
 int gemm_tm_max_wstages();
