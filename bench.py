@@ -320,6 +320,98 @@ def run_single(args) -> None:
     print(f"single N={n} K={k} M={m} config={cfg}: ok")
 
 
+TP70B = (  # name, N, K, split (Llama-3-70B)
+    ("qkv", 10240, 8192, "column"),
+    ("o", 8192, 8192, "row"),
+    ("gate", 28672, 8192, "column"),
+    ("up", 28672, 8192, "column"),
+    ("down", 8192, 28672, "row"),
+)
+
+
+def run_tp70b(args) -> None:
+    """Llama-3-70B linears tensor-parallel over the launched ranks (NCCL), M in {1, 64, 4096}.
+
+    Column split for QKV/gate/up (outputs all-gathered), row split for O/down (FP32 partials all-reduced).
+    Per M: CUDA-event time of one layer's 5 linears (max over ranks) and of its collectives alone; weights of
+    two layers per rank alternate between steps so that every step streams them from HBM.
+    """
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from mambo_b200.sharding import TensorParallelIQ3SLinear
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    layers = []
+    for li in range(2):
+        lin = {}
+        for pi, (name, n, k, split) in enumerate(TP70B):
+            gen = torch.Generator(device=dev).manual_seed(0x70B + 97 * li + pi)  # same weights on every rank
+            raw = torch.randint(0, 256, (n, k // 256, 110), dtype=torch.uint8, device=dev, generator=gen)
+            d = (torch.rand((n, k // 256), device=dev, generator=gen) * 9e-3 + 1e-3).half()
+            raw[..., :2] = d.view(torch.uint8).view(n, k // 256, 2)
+            lin[name] = TensorParallelIQ3SLinear(raw, split, out_dtype=torch.bfloat16)
+            del raw, d
+            torch.cuda.empty_cache()
+        layers.append(lin)
+    results = []
+    for m in (1, 64, 4096):
+        gen = torch.Generator(device=dev).manual_seed(20261017 + m)
+        xs = {k: torch.randn((m, k), device=dev, generator=gen).to(torch.bfloat16) for k in (8192, 28672)}
+
+        def layer(li, timed_coll=False):
+            coll = 0.0
+            for name, n, k, split in TP70B:
+                lin = layers[li][name]
+                lin(xs[k], time_collective=timed_coll)
+                coll += lin.times.collective_ms if timed_coll else 0.0
+            return coll
+
+        for w in range(args.warmup):
+            layer(w & 1)
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        steps = max(2, args.steps // 5)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for st in range(steps):
+            layer(st & 1)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / steps
+        coll = sum(layer(st & 1, timed_coll=True) for st in range(2)) / 2
+        if world > 1:
+            t = torch.tensor([ms, coll], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms, coll = float(t[0]), float(t[1])
+        w_bytes = sum(n * (k // 256) * 110 for _, n, k, _ in TP70B)
+        flops = sum(2 * m * n * k for _, n, k, _ in TP70B)
+        results.append({"m": m, "ms_per_layer": round(ms, 4), "collective_ms": round(coll, 4),
+                        "weight_gbs_total": round(w_bytes / (ms * 1e-3) / 1e9, 1),
+                        "tflops_total": round(flops / (ms * 1e-3) / 1e12, 1)})
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        peak, kind = load_peaks()
+        print(json.dumps({"workload": "tp70b (BASELINE config 5)", "n_gpus": world, "parallelism": f"tp{world}",
+                          "data": "synthetic", "weights_per_layer_bytes": sum(n * (k // 256) * 110
+                                                                               for _, n, k, _ in TP70B),
+                          "hbm_peak_gbs_per_gpu": peak, "peak_kind": kind,
+                          "note": "collective_ms: device time of the layer's NCCL all-gathers/all-reduces "
+                                  "measured alone in separate steps",
+                          "results": results}), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -331,10 +423,15 @@ def main() -> None:
     ap.add_argument("--single", metavar="N,K,M",
                     help="profiling mode: run four linears of one shape (random IQ3_S weights) and exit")
     ap.add_argument("--kernel", type=int, default=None, help="with --single: MAMBO_KERNEL_* to use")
+    ap.add_argument("--workload", choices=("decode", "tp70b"), default="decode",
+                    help="tp70b: Llama-3-70B linears tensor-parallel over the launched ranks (its own JSON line)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.single:
         run_single(args)
+        return
+    if args.workload == "tp70b" and args.impl == "mambo":
+        run_tp70b(args)
         return
 
     if args.impl == "reference":
