@@ -333,8 +333,9 @@ def run_tp70b(args) -> None:
     """Llama-3-70B linears tensor-parallel over the launched ranks (NCCL), M in {1, 64, 4096}.
 
     Column split for QKV/gate/up (outputs all-gathered), row split for O/down (FP32 partials all-reduced).
-    Per M: CUDA-event time of one layer's 5 linears (max over ranks) and of its collectives alone; weights of
-    two layers per rank alternate between steps so that every step streams them from HBM.
+    Per M: CUDA-event time of one layer's 5 linears (max over ranks) -- each rank's compute replayed from a
+    CUDA graph, the collectives issued eagerly in between -- and, eagerly, of its collectives alone; weights
+    of two layers per rank alternate between steps so that every step streams them from HBM.
     """
     import datetime
 
@@ -375,19 +376,45 @@ def run_tp70b(args) -> None:
                 coll += lin.times.collective_ms if timed_coll else 0.0
             return coll
 
-        for w in range(args.warmup):
-            layer(w & 1)
+        # Eager warm-up on the capture stream (allocates its workspace outside the capture).
+        stream = torch.cuda.Stream(dev)
+        with torch.cuda.stream(stream):
+            for w in range(args.warmup):
+                layer(w & 1)
+        torch.cuda.synchronize(dev)
+        # Per linear a CUDA graph of this rank's compute (quantization + linear); the NCCL
+        # collective runs eagerly between replays on the same stream.
+        graphs = {}
+        for li in range(2):
+            for name, n, k, split in TP70B:
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    y = layers[li][name].local(xs[k])
+                graphs[(li, name)] = (g, y)
+        torch.cuda.synchronize(dev)
+
+        def layer_graphed(li):
+            for name, n, k, split in TP70B:
+                g, y = graphs[(li, name)]
+                g.replay()
+                layers[li][name].combine(y)
+
+        with torch.cuda.stream(stream):
+            for w in range(args.warmup):
+                layer_graphed(w & 1)
         torch.cuda.synchronize(dev)
         if world > 1:
             dist.barrier()
         steps = max(2, args.steps // 5)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for st in range(steps):
-            layer(st & 1)
-        e1.record()
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for st in range(steps):
+                layer_graphed(st & 1)
+            e1.record(stream)
         torch.cuda.synchronize(dev)
         ms = e0.elapsed_time(e1) / steps
+        del graphs
         coll = sum(layer(st & 1, timed_coll=True) for st in range(2)) / 2
         if world > 1:
             t = torch.tensor([ms, coll], device=dev, dtype=torch.float64)
@@ -407,8 +434,9 @@ def run_tp70b(args) -> None:
                           "data": "synthetic", "weights_per_layer_bytes": sum(n * (k // 256) * 110
                                                                                for _, n, k, _ in TP70B),
                           "hbm_peak_gbs_per_gpu": peak, "peak_kind": kind,
-                          "note": "collective_ms: device time of the layer's NCCL all-gathers/all-reduces "
-                                  "measured alone in separate steps",
+                          "note": "ms_per_layer: per linear a CUDA-graph replay of the rank's compute "
+                                  "(quantize + linear) and the NCCL collective issued eagerly; collective_ms: "
+                                  "device time of the layer's all-gathers/all-reduces measured alone in eager steps",
                           "results": results}), flush=True)
 
 

@@ -126,16 +126,17 @@ class TensorParallelIQ3SLinear:
 
     def forward(self, x: torch.Tensor, *, time_collective: bool = False) -> torch.Tensor:
         """x: [M, K] (or [M, K/P] for a row split with sharded input) -> [M, N] (or [M, N/P])."""
+        return self.combine(self.local(x), time_collective=time_collective)
+
+    def local(self, x: torch.Tensor) -> torch.Tensor:
+        """This rank's compute: COLUMN -> out[:, n0:n1] in out_dtype; ROW -> the FP32 partial [M, N]."""
         if x.ndim != 2:
             raise ValueError("activation must be [M,K]")
         if self.mode == COLUMN:
             if x.shape[1] != self.k:
                 raise ValueError(f"column-split activation must be [M,{self.k}]")
             xq, xs = self._quantize(x)
-            y = self._linear(xq, xs, self.fields, self.out_dtype)
-            if not self.gather_output or self.world == 1:
-                return y
-            return self._timed(time_collective, lambda: self._gather_columns(y))
+            return self._linear(xq, xs, self.fields, self.out_dtype)
         # Row split: this rank's K slice (whole 256-weight blocks: MXFP8 groups stay intact).
         if self.input_is_sharded:
             if x.shape[1] != self.local_k:
@@ -145,20 +146,27 @@ class TensorParallelIQ3SLinear:
             if x.shape[1] != self.k:
                 raise ValueError(f"row-split activation must be [M,{self.k}]")
             xq, xs = self._quantize(x[:, self.k0:self.k0 + self.local_k])
-        partial = self._linear(xq, xs, self.fields, torch.float32)
+        return self._linear(xq, xs, self.fields, torch.float32)
+
+    def combine(self, y: torch.Tensor, *, time_collective: bool = False) -> torch.Tensor:
+        """The exchange step on local()'s result: all-gather (COLUMN, when asked) or all-reduce (ROW)."""
+        if self.mode == COLUMN:
+            if not self.gather_output or self.world == 1:
+                return y
+            return self._timed(time_collective, lambda: self._gather_columns(y))
         if self.world > 1:
-            self._timed(time_collective, lambda: dist.all_reduce(partial, op=dist.ReduceOp.SUM, group=self.group))
-        return partial if self.out_dtype == torch.float32 else partial.to(self.out_dtype)
+            self._timed(time_collective, lambda: dist.all_reduce(y, op=dist.ReduceOp.SUM, group=self.group))
+        return y if self.out_dtype == torch.float32 else y.to(self.out_dtype)
 
     __call__ = forward
 
     def _gather_columns(self, y: torch.Tensor) -> torch.Tensor:
         if dist.get_backend(self.group) == "nccl":
-            # One buffer: gather the [N/P, M] shards along dim 0, then transpose back.
-            yt = y.t().contiguous()
-            full = torch.empty((self.world * yt.shape[0], yt.shape[1]), dtype=y.dtype, device=y.device)
-            dist.all_gather_into_tensor(full, yt, group=self.group)
-            return full.t().contiguous()
+            # One buffer: the [M, N/P] shards land as [P, M, N/P]; one permuting copy makes [M, N].
+            m, nl = y.shape
+            parts = torch.empty((self.world, m, nl), dtype=y.dtype, device=y.device)
+            dist.all_gather_into_tensor(parts, y.contiguous(), group=self.group)
+            return parts.permute(1, 0, 2).reshape(m, self.world * nl)
         parts = [torch.empty_like(y) for _ in range(self.world)]
         dist.all_gather(parts, y.contiguous(), group=self.group)
         return torch.cat(parts, dim=1)
