@@ -168,6 +168,26 @@ MAMBO_API int mambo_iq3s_linear(const uint8_t* xq, int64_t ldxq, const uint8_t* 
                       const MamboIQ3SWeight* w, const uint32_t* fp8_table, void* out, int out_dtype, int64_t ldo,
                       const MamboLinearConfig* cfg, void* workspace, size_t workspace_bytes, mambo_stream_t stream);
 
+/*
+ * Quantization + linear in one call: x bf16 or f32 [M, K] (row stride ldx)
+ * -> MXFP8 (round to nearest even) -> the IQ3_S x MXFP8 linear -> out.
+ * Below 32 tokens, with bf16 rows 16-byte aligned, the tcgen05 GEMV quantizes
+ * the activations itself (one launch, no xq/xs round trip; the same
+ * arithmetic as mambo_quantize_mxfp8, bit-identical results); otherwise the
+ * quantizer runs into the workspace first. workspace:
+ * mambo_iq3s_linear_fused_workspace_bytes() bytes, zero-filled once.
+ * Replaces launch_quantize_fp8 + launch_iq3_s_fp8_matmul
+ * (src/python/mambo/kernels/quantize_fp8.py:67-84, iq3_s_fp8.py:364-399).
+ */
+MAMBO_API int mambo_iq3s_linear_fused(const void* x, int x_dtype, int64_t ldx, int64_t m, const MamboIQ3SWeight* w,
+                                      const uint32_t* fp8_table, void* out, int out_dtype, int64_t ldo,
+                                      const MamboLinearConfig* cfg, void* workspace, size_t workspace_bytes,
+                                      mambo_stream_t stream);
+
+/* Workspace bytes mambo_iq3s_linear_fused needs for this shape and configuration. */
+MAMBO_API size_t mambo_iq3s_linear_fused_workspace_bytes(int64_t m, int64_t n_rows, int64_t n_blocks,
+                                                         const MamboLinearConfig* cfg);
+
 /* Workspace bytes mambo_iq3s_linear needs for this shape and configuration. */
 MAMBO_API size_t mambo_iq3s_linear_workspace_bytes(int64_t m, int64_t n_rows, int64_t n_blocks, const MamboLinearConfig* cfg);
 

@@ -46,6 +46,8 @@ EXPORTED_SYMBOLS = (
     "mambo_iq3s_linear",
     "mambo_iq3s_linear_workspace_bytes",
     "mambo_iq3s_linear_noalloc",
+    "mambo_iq3s_linear_fused",
+    "mambo_iq3s_linear_fused_workspace_bytes",
     "mambo_num_configs",
     "mambo_config_at",
     "mambo_default_config",
@@ -142,6 +144,13 @@ def load() -> ctypes.CDLL:
                  ctypes.POINTER(MamboLinearConfig), vp],
                 i32,
             ),
+            "mambo_iq3s_linear_fused": (
+                [vp, i32, i64, i64, ctypes.POINTER(MamboIQ3SWeight), vp, vp, i32, i64,
+                 ctypes.POINTER(MamboLinearConfig), vp, ctypes.c_size_t, vp],
+                i32,
+            ),
+            "mambo_iq3s_linear_fused_workspace_bytes": (
+                [i64, i64, i64, ctypes.POINTER(MamboLinearConfig)], ctypes.c_size_t),
             "mambo_num_configs": ([i32], i32),
             "mambo_config_at": ([i32, i32, ctypes.POINTER(MamboLinearConfig)], i32),
             "mambo_default_config": ([i64, i64, i64, ctypes.POINTER(MamboLinearConfig)], i32),

@@ -384,7 +384,8 @@ int launch_gemm_f16_path(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int
 int launch_tc_chunk(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t ldxs, int64_t mc,
                     const MamboIQ3SWeight* w, const uint32_t* fp8_table, void* out, int out_dtype, int64_t ldo,
                     const MamboLinearConfig& c, const GemvPlan& P, const DeviceInfo& info, int* counters,
-                    float* partials, uint8_t* xcopy, uint8_t* xscopy, cudaStream_t stream) {
+                    float* partials, uint8_t* xcopy, uint8_t* xscopy, cudaStream_t stream,
+                    const uint16_t* x_bf16 = nullptr, int64_t ldx = 0) {
   GemvTmMaps maps;
   std::memset(&maps, 0, sizeof(maps));
   const uintptr_t fields[5] = {(uintptr_t)w->d, (uintptr_t)w->qs, (uintptr_t)w->qh, (uintptr_t)w->signs,
@@ -395,7 +396,11 @@ int launch_tc_chunk(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t 
                   "the tcgen05 GEMV needs N %% 8 == 0 and 16-byte aligned weight fields (use MAMBO_KERNEL_GEMV_SYNC)");
   const int64_t k = w->n_blocks * 256;
   const int box = 8 * P.nt;
-  if (!make_gemv_x_map(xq, ldxq, (int)mc, (int)w->n_blocks, box, &maps.x)) {
+  if (x_bf16) {
+    // Fused quantization: the kernel loads the bf16 rows itself.
+    if (!make_gemv_xb_map(x_bf16, ldx, (int)mc, k, box, &maps.xb))
+      return fail(MAMBO_EINVAL, "bf16 activations need 16-byte aligned rows");
+  } else if (!make_gemv_x_map(xq, ldxq, (int)mc, (int)w->n_blocks, box, &maps.x)) {
     if (!xcopy) return fail(MAMBO_EINVAL, "x_values rows must be 16-byte aligned");
     cudaError_t e = cudaMemcpy2DAsync(xcopy, (size_t)k, xq, (size_t)ldxq, (size_t)k, (size_t)mc,
                                       cudaMemcpyDeviceToDevice, stream);
@@ -403,7 +408,7 @@ int launch_tc_chunk(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t 
     if (!make_gemv_x_map(xcopy, k, (int)mc, (int)w->n_blocks, box, &maps.x))
       return fail(MAMBO_ECUDA, "activation tensor map could not be encoded");
   }
-  if (!make_gemv_xs_map(xs, ldxs, (int)mc, (int)w->n_blocks, box, &maps.xs)) {
+  if (!x_bf16 && !make_gemv_xs_map(xs, ldxs, (int)mc, (int)w->n_blocks, box, &maps.xs)) {
     if (!xscopy) return fail(MAMBO_EINVAL, "x_scales rows must be 16-byte aligned");
     const int64_t ld = xs_copy_stride(w->n_blocks);
     cudaError_t e = cudaMemcpy2DAsync(xscopy, (size_t)ld, xs, (size_t)ldxs, (size_t)(w->n_blocks * 8), (size_t)mc,
@@ -434,6 +439,8 @@ int launch_tc_chunk(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t 
   p.kparts = P.kparts;
   p.row_tiles = P.row_tiles;
   p.total_units = P.units;
+  p.x_bf16 = x_bf16;
+  p.ldx = ldx;
   cudaError_t e = launch_gemv_tm(p, P.nt, c.warps, maps, P.grid, stream);
   if (e != cudaSuccess) return cuda_fail(e, "iq3s_gemv_tm");
   return MAMBO_OK;
@@ -748,6 +755,80 @@ int mambo_iq3s_linear(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_
     }
   }
   return ok();
+}
+
+size_t mambo_iq3s_linear_fused_workspace_bytes(int64_t m, int64_t n_rows, int64_t n_blocks,
+                                               const MamboLinearConfig* cfg) {
+  const int64_t k = n_blocks * 256;
+  return align256(mambo_iq3s_linear_workspace_bytes(m, n_rows, n_blocks, cfg)) + align256((size_t)(m * k)) +
+         align256((size_t)(m * (k / 32)));
+}
+
+int mambo_iq3s_linear_fused(const void* x, int x_dtype, int64_t ldx, int64_t m, const MamboIQ3SWeight* w,
+                            const uint32_t* fp8_table, void* out, int out_dtype, int64_t ldo,
+                            const MamboLinearConfig* cfg, void* workspace, size_t workspace_bytes,
+                            mambo_stream_t stream) {
+  if (!x || !w || !fp8_table || !out) return fail(MAMBO_EINVAL, "null pointer");
+  if (!w->d || !w->qs || !w->qh || !w->signs || !w->scales) return fail(MAMBO_EINVAL, "null weight field");
+  if (w->n_rows < 1 || w->n_blocks < 1) return fail(MAMBO_EINVAL, "IQ3_S weight must have positive N and K");
+  if (w->n_rows > (1 << 30) || w->n_blocks > (1 << 20)) return fail(MAMBO_EINVAL, "weight too large");
+  if (x_dtype != MAMBO_F32 && x_dtype != MAMBO_BF16) return fail(MAMBO_EINVAL, "activation must be f32 or bf16");
+  const int64_t k = w->n_blocks * 256;
+  if (m < 1) return fail(MAMBO_EINVAL, "activation must be [M,K] with M >= 1");
+  if (ldx < k) return fail(MAMBO_EINVAL, "activation row stride is smaller than K");
+  if (out_dtype != MAMBO_F32 && out_dtype != MAMBO_BF16) return fail(MAMBO_EINVAL, "out must be f32 or bf16");
+  if (ldo < w->n_rows) return fail(MAMBO_EINVAL, "out row stride is smaller than N");
+  DeviceInfo info;
+  int st = require_sm100(&info);
+  if (st != MAMBO_OK) return st;
+  MamboLinearConfig c;
+  if (cfg) c = *cfg; else default_config(m, w->n_rows, w->n_blocks, &c, info.max_smem_optin, info.sms);
+  if (c.kernel == MAMBO_KERNEL_AUTO) {
+    MamboLinearConfig a;
+    default_config(m, w->n_rows, w->n_blocks, &a, info.max_smem_optin, info.sms);
+    c.kernel = a.kernel;
+    if (c.stages == 0) c.stages = a.stages;
+  }
+  const uintptr_t fields[6] = {(uintptr_t)w->d, (uintptr_t)w->qs, (uintptr_t)w->qh, (uintptr_t)w->signs,
+                               (uintptr_t)w->scales, (uintptr_t)w->packed};
+  bool aligned = w->n_rows % 8 == 0;
+  for (uintptr_t f : fields) aligned = aligned && f % 16 == 0;
+  // Decode-sized M on the tcgen05 GEMV: the kernel quantizes the bf16 rows itself.
+  if (x_dtype == MAMBO_BF16 && m < kGemmMinTokens && c.kernel == MAMBO_KERNEL_GEMV && c.loader == 0 && aligned &&
+      (uintptr_t)x % 16 == 0 && ldx % 8 == 0) {
+    st = validate_config(&c, m, w->n_blocks, info);
+    if (st != MAMBO_OK) return st;
+    // The bf16 box ring takes the room of one or two weight stages: the
+    // deepest pipeline that fits it under the same plan (fewer stages keep
+    // the cluster K split valid, so the summation order, and the result, is
+    // the two-step path's); without room at all, two steps.
+    const GemvPlan P = plan_gemv(m, w->n_rows, w->n_blocks, c, info.sms, info.max_smem_optin);
+    while (c.stages > 2 && (int)gemv_tm_smem_bytes(P.nt, c.stages, P.kparts, true) > info.max_smem_optin)
+      --c.stages;
+    if ((size_t)P.counter_slots * sizeof(int) > kCounterBytes)
+      return fail(MAMBO_EINVAL, "N=%lld needs more split-K counters than the workspace holds", (long long)w->n_rows);
+    if ((int)gemv_tm_smem_bytes(P.nt, c.stages, P.kparts, true) <= info.max_smem_optin) {
+      const size_t need = P.counters_bytes + P.partial_bytes;
+      if (!workspace || workspace_bytes < need)
+        return fail(MAMBO_EWORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+      if ((uintptr_t)workspace % 256) return fail(MAMBO_EINVAL, "workspace must be 256-byte aligned");
+      int* counters = (int*)workspace;
+      float* partials = (float*)((uint8_t*)workspace + P.counters_bytes);
+      st = launch_tc_chunk(nullptr, 0, nullptr, 0, m, w, fp8_table, out, out_dtype, ldo, c, P, info, counters,
+                           partials, nullptr, nullptr, (cudaStream_t)stream, (const uint16_t*)x, ldx);
+      return st == MAMBO_OK ? ok() : st;
+    }
+  }
+  // Otherwise: quantize into the workspace, then the linear.
+  const size_t lin = align256(mambo_iq3s_linear_workspace_bytes(m, w->n_rows, w->n_blocks, cfg));
+  const size_t need = mambo_iq3s_linear_fused_workspace_bytes(m, w->n_rows, w->n_blocks, cfg);
+  if (!workspace || workspace_bytes < need)
+    return fail(MAMBO_EWORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+  uint8_t* xq = (uint8_t*)workspace + lin;
+  uint8_t* xs = xq + align256((size_t)(m * k));
+  st = mambo_quantize_mxfp8(x, x_dtype, m, k, ldx, xq, k, xs, k / 32, MAMBO_ROUND_NEAREST_EVEN, stream);
+  if (st != MAMBO_OK) return st;
+  return mambo_iq3s_linear(xq, k, xs, k / 32, m, w, fp8_table, out, out_dtype, ldo, cfg, workspace, lin, stream);
 }
 
 }  // extern "C"

@@ -573,6 +573,17 @@ bool make_gemv_x_map(const uint8_t* xq, int64_t ldxq, int m, int n_blocks, int b
   return encode(fn, map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, xq, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
+bool make_gemv_xb_map(const uint16_t* x, int64_t ldx, int m, int64_t k, int box_tokens, CUtensorMap* map) {
+  EncodeTiledFn fn = get_encode_fn();
+  if (!fn || (uintptr_t)x % 16 || ldx % 8 || m < 1 || k % 256 || box_tokens > 256) return false;
+  // [m tokens][K bf16]: a box of box_tokens rows x 256 values (one K block,
+  // 512 bytes a row, unswizzled); rows past m are zero-filled.
+  cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)m};
+  cuuint64_t str[1] = {(cuuint64_t)(ldx * 2)};
+  cuuint32_t box[2] = {256, (cuuint32_t)box_tokens};
+  return encode(fn, map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, x, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
 bool make_gemm_x8_map(const uint8_t* xq, int64_t ldxq, int m, int64_t k, CUtensorMap* map) {
   EncodeTiledFn fn = get_encode_fn();
   if (!fn || (uintptr_t)xq % 16 || ldxq % 16 || m < 1 || k % 128) return false;

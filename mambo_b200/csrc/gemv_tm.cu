@@ -43,6 +43,7 @@
 #include "kernels.cuh"
 #include "tcgen05.cuh"
 #include "iq3s_tm.cuh"
+#include "mxfp8.cuh"
 
 namespace mambo {
 
@@ -63,6 +64,13 @@ __host__ __device__ constexpr int tm_box_tokens(int nt) { return 8 * nt; }    //
 // Activation tiles in flight (their own ring, filled ahead of the weights).
 constexpr int kMaxXStages = 8;
 __host__ __device__ constexpr int tm_xstages(int nt) { return nt == 1 ? 8 : nt == 2 ? 6 : 4; }
+// Fused quantization: a ring of bf16 activation boxes (one K block of the
+// token tile, [tokens][256 bf16]) that the activation warp quantizes into the
+// slots above. Its barriers follow the TMEM address slot in the barrier area.
+__host__ __device__ constexpr int tm_bstages(int nt) { return nt == 1 ? 4 : nt == 2 ? 3 : 2; }
+constexpr uint32_t kBfRowBytes = 512;
+constexpr int kBfBarIndex = 2 * kMaxStagesTm + 2 * kMaxXStages + 2 * kRing + 6;
+static_assert(kBfBarIndex + 4 <= (int)(kBarBytes / 8), "barrier area");
 __host__ __device__ constexpr int tm_nmma(int nt) { return nt == 4 ? 32 : 16; }  // MMA N
 // TMEM columns: the A ring at [0, 64*kRing), then D (8 groups x N columns),
 // double-buffered unless that would not fit in 512 columns (N = 32), then the
@@ -109,11 +117,12 @@ __host__ __device__ inline TmLayout tm_layout(int nt) {
 }
 
 // kparts > 1: rank 0 of each cluster also holds the other ranks' partials.
-__host__ __device__ inline uint32_t tm_smem_bytes(int nt, int stages, int kparts) {
+__host__ __device__ inline uint32_t tm_smem_bytes(int nt, int stages, int kparts, bool fused = false) {
   const TmLayout L = tm_layout(nt);
   const uint32_t cpart = kparts > 1 ? (uint32_t)(kparts - 1) * kRows * 8u * nt * 4u : 0u;
+  const uint32_t bf = fused ? 128u + (uint32_t)tm_bstages(nt) * tm_box_tokens(nt) * kBfRowBytes : 0u;
   return kTableBytes + 1024 + align_up_tm(stages * L.stage, 1024) + tm_xstages(nt) * L.xslot + kRing * L.aux +
-         kTableStageBytes + kBarBytes + cpart;
+         kTableStageBytes + kBarBytes + cpart + bf;
 }
 
 __device__ __forceinline__ int unit_begin_tm(int cta, int grid, int units) {
@@ -232,6 +241,7 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
   const uint32_t kXfull = bar0 + 16 * kMaxStagesTm, kXempty = kXfull + 8 * kMaxXStages;
   const uint32_t kAfull = kXempty + 8 * kMaxXStages, kEfree = kAfull + 8 * kRing;
   const uint32_t kMdone = kEfree + 8 * kRing, kEdone = kMdone + 16, kCred = kEdone + 8, kSfInit = kCred + 8;
+  const uint32_t kBfull = bar0 + 8 * kBfBarIndex;  // bf16 boxes landed (fused quantization)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // Work range: with kparts > 0 each row tile is split into kparts K ranges,
@@ -272,6 +282,7 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
     mbar_init(kEdone, kEpiWarps);
     mbar_init(kCred, p.kparts > 1 ? (p.kparts - 1) * kEpiWarps : 1);
     mbar_init(kSfInit, kEpiWarps);
+    for (int s = 0; s < tm_bstages(NT); ++s) mbar_init(kBfull + 8 * s, 1);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -357,10 +368,72 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
   if (warp == kXWarp) {
     const uint64_t keep = l2_policy_evict_last();  // every CTA reads them
     if (lane == 0) {
-      tma_prefetch_desc(&maps.x);
-      tma_prefetch_desc(&maps.xs);
+      if (p.x_bf16) {
+        tma_prefetch_desc(&maps.xb);
+      } else {
+        tma_prefetch_desc(&maps.x);
+        tma_prefetch_desc(&maps.xs);
+      }
     }
     pdl_wait();
+    if (p.x_bf16) {
+      // Fused quantization (the standalone quantizer's arithmetic): the bf16
+      // box of each K block arrives by TMA, BS units ahead. A lane quantizes
+      // one 32-value group of one token (4 tokens x 8 groups a pass), reading
+      // its four 16-byte chunks in an order rotated by token so that each
+      // quarter warp hits all banks, and writes the E4M3 bytes straight into
+      // the B tile [16-byte K chunk][token][16 bytes], the scale code into
+      // the token's scale row. Rows past M are left as they are: their D
+      // columns are never read.
+      constexpr int BS = tm_bstages(NT);
+      constexpr uint32_t kBoxBytes = BOX * kBfRowBytes;
+      const uint32_t cpart_bytes = p.kparts > 1 ? (uint32_t)(p.kparts - 1) * kRows * 8u * NT * 4u : 0u;
+      uint8_t* xb0 = reinterpret_cast<uint8_t*>(cpart) + cpart_bytes;
+      xb0 += (128u - (smem_u32(xb0) & 127u)) & 127u;
+      const int tl = lane & 3, g = lane >> 2;
+      int kb_issue = u0 % p.n_blocks;
+      auto issue_box = [&](int j) {  // lane 0
+        const uint32_t bar = kBfull + 8 * (j % BS);
+        mbar_arrive_expect_tx(bar, kBoxBytes);
+        tma_load_2d(smem_u32(xb0 + (size_t)(j % BS) * kBoxBytes), &maps.xb, kb_issue * 256, 0, bar, keep);
+        kb_issue = (kb_issue + 1 == p.n_blocks) ? 0 : kb_issue + 1;
+      };
+      if (lane == 0)
+        for (int j = 0; j < BS && j < n_units; ++j) issue_box(j);
+      int kb = u0 % p.n_blocks;
+      for (int j = 0; j < n_units; ++j, kb = (kb + 1 == p.n_blocks) ? 0 : kb + 1) {
+        const int x = j % AS;
+        bool ok = mbar_wait_bounded(kBfull + 8 * (j % BS), (uint32_t)(j / BS) & 1u, kSiteGemvFull);
+        if (j >= AS) ok = ok && mbar_wait_bounded(kXempty + 8 * x, ((j / AS) & 1) ^ 1, kSiteGemvEmpty);
+        if (!__all_sync(0xFFFFFFFFu, ok)) return;
+        const uint8_t* src = xb0 + (size_t)(j % BS) * kBoxBytes + g * 64;
+        uint8_t* sl = x0 + (size_t)x * L.xslot;
+        for (int t = tl; t < p.m; t += 4) {
+          uint4 c[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            c[i] = *reinterpret_cast<const uint4*>(src + t * kBfRowBytes + ((i + tl) & 3) * 16);
+          uint2 q[4];
+          const uint32_t code = mxfp8_group32_bf16_rne(c, q);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int ch = (i + tl) & 3;  // 8-value chunk of the group held in c[i]
+            *reinterpret_cast<uint2*>(sl + L.b + ((2 * g + (ch >> 1)) * BOX + t) * 16 + (ch & 1) * 8) = q[i];
+          }
+          sl[L.xs + t * 16 + (kb & 1) * 8 + g] = (uint8_t)code;
+        }
+        // The MMA reads the tile through the async proxy, and the next TMA
+        // load overwrites the bf16 box just read.
+        fence_proxy_async_shared();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(kXfull + 8 * x);
+          if (j + BS < n_units) issue_box(j + BS);
+        }
+        __syncwarp();
+      }
+      return;
+    }
     int kb = u0 % p.n_blocks;
     for (int j = 0; j < n_units; ++j, kb = (kb + 1 == p.n_blocks) ? 0 : kb + 1) {
       const int x = j % AS;
@@ -693,7 +766,9 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
 // --------------------------------------------------------------------------
 // Host side
 // --------------------------------------------------------------------------
-uint32_t gemv_tm_smem_bytes(int nt, int stages, int kparts) { return tm_smem_bytes(nt, stages, kparts); }
+uint32_t gemv_tm_smem_bytes(int nt, int stages, int kparts, bool fused) {
+  return tm_smem_bytes(nt, stages, kparts, fused);
+}
 int gemv_tm_max_stages() { return kMaxStagesTm; }
 
 template <int NT, int kDecWarps>
@@ -751,7 +826,7 @@ static int query_max_clusters(int nt, int dec_warps, int stages, int kparts) {
 
 template <int NT, int kDecWarps>
 static cudaError_t launch_gemv_tm_t(const GemvTmParams& p, const GemvTmMaps& maps, int grid, cudaStream_t stream) {
-  const uint32_t smem = tm_smem_bytes(NT, p.stages, p.kparts);
+  const uint32_t smem = tm_smem_bytes(NT, p.stages, p.kparts, p.x_bf16 != nullptr);
   const void* kern = tm_kernel<NT, kDecWarps>();
   cudaError_t e = ensure_smem_attribute(kern, smem);
   if (e != cudaSuccess) return e;

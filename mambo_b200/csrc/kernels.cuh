@@ -146,11 +146,16 @@ struct GemvTmParams {
   int kparts;    // > 0: row tile t is split into kparts K ranges, CTA t*kparts+k in a cluster of kparts; 0: stream-K
   int row_tiles;
   int total_units;
+  // Fused activation quantization: bf16 activations [m][ldx] (16-byte aligned
+  // rows) quantized to MXFP8 in the kernel instead of read as xq/xs; null: TMA.
+  const uint16_t* x_bf16;
+  int64_t ldx;
 };
 
 struct GemvTmMaps {
   CUtensorMap x;                         // activations [K/16 chunks][m tokens][16 bytes], box 16 x 8*NT x 16
   CUtensorMap xs;                        // activation scales [m tokens][K/32 groups], box 16 x 8*NT
+  CUtensorMap xb;                        // bf16 activations [m tokens][K], box 256 x 8*NT (fused quantization)
 };
 
 // Activation map for the tcgen05 GEMV; false when xq is not 16-byte aligned
@@ -160,7 +165,10 @@ bool make_gemv_x_map(const uint8_t* xq, int64_t ldxq, int m, int n_blocks, int b
 bool make_gemv_xs_map(const uint8_t* xs, int64_t ldxs, int m, int n_blocks, int box_tokens, CUtensorMap* map);
 cudaError_t launch_gemv_tm(const GemvTmParams& p, int nt, int dec_warps, const GemvTmMaps& maps, int grid,
                            cudaStream_t stream);
-uint32_t gemv_tm_smem_bytes(int nt, int stages, int kparts);
+uint32_t gemv_tm_smem_bytes(int nt, int stages, int kparts, bool fused = false);
+// bf16 activation map for the GEMV's fused quantization; false unless x is
+// 16-byte aligned with a row stride (elements) that is a multiple of 8.
+bool make_gemv_xb_map(const uint16_t* x, int64_t ldx, int m, int64_t k, int box_tokens, CUtensorMap* map);
 // Clusters of `kparts` CTAs of this configuration that can be resident at once (0 if none / on error).
 int gemv_tm_max_clusters(int nt, int dec_warps, int stages, int kparts);
 int gemv_tm_max_stages();

@@ -1,0 +1,95 @@
+// MXFP8 quantization arithmetic shared by the standalone quantizer and the
+// GEMV that quantizes its activations on the fly (bit-identical results):
+// per 32 values, the UE8M0 code of ceil(log2(amax / 448)) and E4M3 values
+// rounded to nearest even with saturation (quantize_fp8.py:23-39).
+#pragma once
+
+#include "common.cuh"
+
+namespace mambo {
+
+// Exact MXFP8 block exponent from the float bits of amax (amax >= 0).
+// Returns the UE8M0 scale code, 0xFF for a non-finite amax.
+__device__ __forceinline__ uint32_t mxfp8_scale_code(float amax) {
+  const uint32_t bits = __float_as_uint(amax);
+  const uint32_t biased = bits >> 23;  // sign is 0
+  if (bits == 0) return 127u;          // amax == 0 -> e = 0
+  if (biased == 0xFF) return 0xFFu;    // Inf / NaN
+  if (biased == 0) return 0u;          // subnormal amax -> e clamps to -127
+  // amax = 1.m * 2^(biased-127); 448 = 1.75 * 2^8.
+  int e = (int)biased - 127 - ((bits & 0x7FFFFFu) <= 0x600000u ? 8 : 7);
+  e = max(-127, min(127, e));
+  return (uint32_t)(e + 127);
+}
+
+// Two floats -> two E4M3 bytes (lo in bits 0..7), round-to-nearest-even, saturating.
+__device__ __forceinline__ uint32_t cvt_e4m3x2_rn(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// One 32-value group held by 4 consecutive lanes (8 values each; the quad
+// must be converged): returns the group's scale code and this lane's 8 E4M3
+// bytes (value i in byte i % 4 of word i / 4), round-to-nearest-even.
+__device__ __forceinline__ uint32_t mxfp8_quad_rne(const float (&v)[8], uint2& out) {
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  // fmaxf drops NaN; keep it visible so the group gets the NaN scale code.
+  bool any_nan = false;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) any_nan |= (v[i] != v[i]);
+  amax = any_nan ? __uint_as_float(0x7FC00000u) : amax;
+  float other = __shfl_xor_sync(0xFFFFFFFFu, amax, 1);
+  amax = (other != other) ? other : fmaxf(amax, other);
+  other = __shfl_xor_sync(0xFFFFFFFFu, amax, 2);
+  amax = (other != other) ? other : fmaxf(amax, other);
+  const uint32_t code = mxfp8_scale_code(amax);
+  // 2^-e with e = code - 127 (code 0xFF: scale by 2^-127, values become 0 / NaN / +-448).
+  const float inv = e8m0_to_float(code == 0xFFu ? 0u : 254u - code);
+  uint32_t packed[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const uint32_t lo = cvt_e4m3x2_rn(v[4 * h] * inv, v[4 * h + 1] * inv);
+    const uint32_t hi = cvt_e4m3x2_rn(v[4 * h + 2] * inv, v[4 * h + 3] * inv);
+    packed[h] = lo | (hi << 16);
+  }
+  out = make_uint2(packed[0], packed[1]);
+  return code;
+}
+
+// One 32-value group of bf16 held by one lane (c[i]: values 8i .. 8i+7, two
+// per word, the even one in the low half): returns the scale code and the
+// 32 E4M3 bytes (q[i]: those of c[i], as mxfp8_quad_rne packs them). The same
+// results as mxfp8_quad_rne on the widened values: the largest magnitude is
+// found on the 15 magnitude bits as unsigned integers, where every NaN pattern
+// sorts above Inf, and maps to the same code.
+__device__ __forceinline__ uint32_t mxfp8_group32_bf16_rne(const uint4 (&c)[4], uint2 (&q)[4]) {
+  uint32_t mx = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t w4[4] = {c[i].x, c[i].y, c[i].z, c[i].w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) asm("max.u16x2 %0, %0, %1;" : "+r"(mx) : "r"(w4[j] & 0x7FFF7FFFu));
+  }
+  const uint32_t mb = max(mx & 0xFFFFu, mx >> 16);
+  const uint32_t code = mxfp8_scale_code(__uint_as_float(mb << 16));
+  const float inv = e8m0_to_float(code == 0xFFu ? 0u : 254u - code);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t w4[4] = {c[i].x, c[i].y, c[i].z, c[i].w};
+    uint32_t packed[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t a = w4[2 * h], b = w4[2 * h + 1];
+      const uint32_t lo = cvt_e4m3x2_rn(__uint_as_float(a << 16) * inv, __uint_as_float(a & 0xFFFF0000u) * inv);
+      const uint32_t hi = cvt_e4m3x2_rn(__uint_as_float(b << 16) * inv, __uint_as_float(b & 0xFFFF0000u) * inv);
+      packed[h] = lo | (hi << 16);
+    }
+    q[i] = make_uint2(packed[0], packed[1]);
+  }
+  return code;
+}
+
+}  // namespace mambo

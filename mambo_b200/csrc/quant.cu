@@ -11,29 +11,9 @@
 // with two quad shuffles, and each lane writes its 8 E4M3 bytes as one 64-bit
 // store (a warp writes 256 contiguous bytes).
 #include "kernels.cuh"
+#include "mxfp8.cuh"
 
 namespace mambo {
-
-// Exact MXFP8 block exponent from the float bits of amax (amax >= 0).
-// Returns the UE8M0 scale code, 0xFF for a non-finite amax.
-__device__ __forceinline__ uint32_t mxfp8_scale_code(float amax) {
-  const uint32_t bits = __float_as_uint(amax);
-  const uint32_t biased = bits >> 23;  // sign is 0
-  if (bits == 0) return 127u;          // amax == 0 -> e = 0
-  if (biased == 0xFF) return 0xFFu;    // Inf / NaN
-  if (biased == 0) return 0u;          // subnormal amax -> e clamps to -127
-  // amax = 1.m * 2^(biased-127); 448 = 1.75 * 2^8.
-  int e = (int)biased - 127 - ((bits & 0x7FFFFFu) <= 0x600000u ? 8 : 7);
-  e = max(-127, min(127, e));
-  return (uint32_t)(e + 127);
-}
-
-// Two floats -> two E4M3 bytes (lo in bits 0..7), round-to-nearest-even, saturating.
-__device__ __forceinline__ uint32_t cvt_e4m3x2_rn(float lo, float hi) {
-  uint16_t r;
-  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
-  return r;
-}
 
 __device__ __forceinline__ float e4m3_to_float(uint32_t byte) {
   uint32_t h2;

@@ -254,13 +254,62 @@ def launch_iq3_s_fp8_matmul(x_values, x_scales, iq3_weight: IQ3SFields, *, strea
     return linear_into(x_values, x_scales, iq3_weight, out, config=config, stream=stream)
 
 
+def fused_linear_into(x: torch.Tensor, iq3_weight: IQ3SFields, out: torch.Tensor, config: dict | None = None,
+                      stream=None) -> torch.Tensor:
+    """Quantize (round to nearest even) and multiply in one C-ABI call into a preallocated out [M,N].
+
+    Below 32 tokens with bf16 rows the tcgen05 GEMV quantizes the activations
+    itself (one launch); otherwise the quantizer runs into the workspace first.
+    """
+    n_rows, blocks = _weight_dimensions(iq3_weight)
+    m = x.shape[0]
+    dev = x.device
+    cfg = _lib.MamboLinearConfig.from_dict(config if config is not None else select_config(m, n_rows, blocks * 256,
+                                                                                              dev))
+    w = weight_struct(iq3_weight)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        st = _runtime.stream_handle(stream, dev)
+        need = lib.mambo_iq3s_linear_fused_workspace_bytes(m, n_rows, blocks, cfg)
+        ws = _runtime.workspace(dev, st, need)
+        x_dtype = _lib.MAMBO_BF16 if x.dtype == torch.bfloat16 else _lib.MAMBO_F32
+        out_dtype = _lib.MAMBO_BF16 if out.dtype == torch.bfloat16 else _lib.MAMBO_F32
+        _lib.check(
+            lib.mambo_iq3s_linear_fused(
+                x.data_ptr(), x_dtype, x.stride(0), m, w, _get_iq3_table(dev).data_ptr(), out.data_ptr(), out_dtype,
+                out.stride(0), cfg, ws.data_ptr(), ws.numel(), st,
+            ),
+            "iq3_s_fp8_linear",
+        )
+    return out
+
+
 def iq3_s_fp8_linear(x, iq3_weight: IQ3SFields, *, stream=None, out_dtype: torch.dtype = torch.bfloat16,
                      rounding: str = "nearest_even", config: dict | None = None) -> torch.Tensor:
-    """bf16/f32 activations [M,K] -> MXFP8 -> IQ3_S linear -> out_dtype [M,N] (quantize + matmul)."""
+    """bf16/f32 activations [M,K] -> MXFP8 -> IQ3_S linear -> out_dtype [M,N] (quantize + matmul).
+
+    Round-to-nearest-even goes through the fused entry point (quantization inside
+    the decode GEMV below 32 tokens); the other rounding modes quantize first.
+    """
     from .quantize_fp8 import launch_quantize_fp8
 
-    xq, xs = launch_quantize_fp8(x, stream=stream, rounding=rounding)
-    return launch_iq3_s_fp8_matmul(xq, xs, iq3_weight, stream=stream, out_dtype=out_dtype, config=config)
+    if rounding != "nearest_even":
+        xq, xs = launch_quantize_fp8(x, stream=stream, rounding=rounding)
+        return launch_iq3_s_fp8_matmul(xq, xs, iq3_weight, stream=stream, out_dtype=out_dtype, config=config)
+    n_rows, k_blocks = _weight_dimensions(iq3_weight)
+    x = _runtime.as_cuda_tensor(x)
+    if x.ndim != 2 or x.dtype not in (torch.float32, torch.bfloat16) or x.shape[0] < 1 or x.shape[1] != k_blocks * 256:
+        raise ValueError("activation must be float32 or bfloat16 [M,K] with K = 256 * weight blocks")
+    if out_dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError("out_dtype must be torch.float32 or torch.bfloat16")
+    dev = x.device
+    if _sm_key(dev) not in BEST_CONFIGS:
+        raise RuntimeError(f"IQ3_S FP8 matmul has no tuned config for {_sm_key(dev)}")
+    _runtime.require_device(dev)
+    if x.stride(1) != 1:
+        x = x.contiguous()
+    out = torch.empty((x.shape[0], n_rows), dtype=out_dtype, device=dev)
+    return fused_linear_into(x, iq3_weight, out, config=config, stream=stream)
 
 
 # ----------------------------------------------------------------------------
