@@ -298,7 +298,7 @@ def run_single(args) -> None:
     """Four linear launches of one shape (for ncu captures of a single kernel)."""
     import torch
 
-    from mambo_b200.kernels.iq3_s_fp8 import linear_into, select_config
+    from mambo_b200.kernels.iq3_s_fp8 import fused_linear_into, linear_into, select_config
     from mambo_b200.kernels.quantize_fp8 import launch_quantize_fp8
     from mambo_b200.utils.iq3_s_weight import prepare_iq3_s_fields
 
@@ -309,13 +309,17 @@ def run_single(args) -> None:
     d = (torch.rand((n, k // 256), device=dev, generator=gen) * 9e-3 + 1e-3).half()
     raw[..., :2] = d.view(torch.uint8).view(n, k // 256, 2)
     fields = prepare_iq3_s_fields(raw)
-    xq, xs = launch_quantize_fp8(torch.randn((m, k), device=dev, generator=gen).to(torch.bfloat16))
+    x = torch.randn((m, k), device=dev, generator=gen).to(torch.bfloat16)
+    xq, xs = launch_quantize_fp8(x)
     out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
     cfg = dict(select_config(m, n, k, dev))
     if args.kernel is not None:
         cfg["kernel"] = args.kernel
     for _ in range(4):
-        linear_into(xq, xs, fields, out, config=cfg)
+        if args.prequantized:
+            linear_into(xq, xs, fields, out, config=cfg)
+        else:  # the bench's decode step: bf16 activations through the fused entry point
+            fused_linear_into(x, fields, out, config=cfg)
     torch.cuda.synchronize()
     print(f"single N={n} K={k} M={m} config={cfg}: ok")
 
@@ -451,6 +455,8 @@ def main() -> None:
     ap.add_argument("--single", metavar="N,K,M",
                     help="profiling mode: run four linears of one shape (random IQ3_S weights) and exit")
     ap.add_argument("--kernel", type=int, default=None, help="with --single: MAMBO_KERNEL_* to use")
+    ap.add_argument("--prequantized", action="store_true",
+                    help="with --single: MXFP8 activations quantized beforehand (mambo_iq3s_linear)")
     ap.add_argument("--workload", choices=("decode", "tp70b"), default="decode",
                     help="tp70b: Llama-3-70B linears tensor-parallel over the launched ranks (its own JSON line)")
     args = ap.parse_args()
@@ -549,13 +555,19 @@ def main() -> None:
     value = alg * world / (ms_per_step * 1e-3) / 1e9
 
     # ---- roofline of the GEMV kernel: per-launch CUDA-event durations ------
+    # Each linear is timed as LAUNCHES back-to-back launches inside one graph,
+    # the way the kernels run in the step: separately launched work (a stream
+    # launch, or a graph of one kernel) starts on a ~2 us grid on this GPU,
+    # which would round each launch up.
     per_launch = []
+    launches = 10
     for m in M_SWEEP:
         for p, n, k in PROJECTIONS:
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, stream=stream):
-                fused_linear_into(xs_dev[m][p], layers[m][p], out_buf[m][p], config=configs[m][p])
-            reps = 20
+                for _ in range(launches):
+                    fused_linear_into(xs_dev[m][p], layers[m][p], out_buf[m][p], config=configs[m][p])
+            reps = 10
             with torch.cuda.stream(stream):
                 for _ in range(3):
                     g.replay()
@@ -565,7 +577,7 @@ def main() -> None:
                     g.replay()
                 e1.record(stream)
             torch.cuda.synchronize(dev)
-            us = e0.elapsed_time(e1) * 1000 / reps
+            us = e0.elapsed_time(e1) * 1000 / (reps * launches)
             b = n * (k // 256) * 110 + m * k * 2 + m * n * 2
             per_launch.append({"m": m, "proj": p, "us": round(us, 3), "bytes": b, "gbs": round(b / us / 1e3, 1)})
             del g
@@ -661,6 +673,7 @@ def main() -> None:
                      "traffic": traffic, "peak_kind": peak_kind,
                      "kernel": "iq3s_gemv_tm_kernel with fused MXFP8 quantization (one launch per linear, "
                                "CUDA-graph replay)",
+                     "timing": "per linear: 10 back-to-back launches in one CUDA graph, 10 replays, mean",
                      "per_launch": per_launch},
         "e2e": {"value": alg * world / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
                 "h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": out_bytes,

@@ -59,7 +59,8 @@ using tm::kTableStageBytes;
 using tm::kRecordBytes;
 
 // Warps: weight producer, MMA, decoders, 4 epilogue, activation producer.
-__host__ __device__ constexpr int tm_threads(int dec_warps) { return (3 + dec_warps + kEpiWarps) * 32; }
+// Warps: weight producer, MMA, decoders, epilogue, two activation producers.
+__host__ __device__ constexpr int tm_threads(int dec_warps) { return (4 + dec_warps + kEpiWarps) * 32; }
 __host__ __device__ constexpr int tm_box_tokens(int nt) { return 8 * nt; }    // activation rows per B tile
 // Activation tiles in flight (their own ring, filled ahead of the weights).
 constexpr int kMaxXStages = 8;
@@ -67,7 +68,8 @@ __host__ __device__ constexpr int tm_xstages(int nt) { return nt == 1 ? 8 : nt =
 // Fused quantization: a ring of bf16 activation boxes (one K block of the
 // token tile, [tokens][256 bf16]) that the activation warp quantizes into the
 // slots above. Its barriers follow the TMEM address slot in the barrier area.
-__host__ __device__ constexpr int tm_bstages(int nt) { return nt == 1 ? 4 : nt == 2 ? 3 : 2; }
+// An even count: a warp refills the slot of each of its own units (every other one).
+__host__ __device__ constexpr int tm_bstages(int nt) { return nt == 1 ? 4 : 2; }
 constexpr uint32_t kBfRowBytes = 512;
 constexpr int kBfBarIndex = 2 * kMaxStagesTm + 2 * kMaxXStages + 2 * kRing + 6;
 static_assert(kBfBarIndex + 4 <= (int)(kBarBytes / 8), "barrier area");
@@ -211,7 +213,7 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
   // repeat rows 0-7 (stride 0) and their results are never read.
   constexpr uint32_t kLbo = BOX * 16u;
   constexpr uint32_t kSbo = NT == 1 ? 0u : 128u;
-  constexpr int kEpiWarp0 = 2 + kDecWarps, kXWarp = kEpiWarp0 + kEpiWarps;
+  constexpr int kEpiWarp0 = 2 + kDecWarps, kXWarp0 = kEpiWarp0 + kEpiWarps;
   constexpr int AS = tm_xstages(NT);
   static_assert(kDecWarps == 8 || kDecWarps == 16, "8 or 16 decoder warps");
 
@@ -361,13 +363,16 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
     return;
   }
 
-  // ------------------------------------------------------------------ activation producer
+  // ------------------------------------------------------------------ activation producers
   // Activation tiles (B operand and scale bytes of a K block) once the previous
   // kernel has finished (programmatic dependent launch), AS units ahead: slot
-  // j % AS is refilled when the MMAs of unit j - AS have completed.
-  if (warp == kXWarp) {
+  // j % AS is refilled when the MMAs of unit j - AS have completed. TMA
+  // copies need one warp; fused quantization takes both, every other unit.
+  if (warp >= kXWarp0) {
+    const int xw = warp - kXWarp0;
+    if (xw != 0 && !p.x_bf16) return;
     const uint64_t keep = l2_policy_evict_last();  // every CTA reads them
-    if (lane == 0) {
+    if (lane == 0 && xw == 0) {
       if (p.x_bf16) {
         tma_prefetch_desc(&maps.xb);
       } else {
@@ -383,25 +388,29 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
       // its four 16-byte chunks in an order rotated by token so that each
       // quarter warp hits all banks, and writes the E4M3 bytes straight into
       // the B tile [16-byte K chunk][token][16 bytes], the scale code into
-      // the token's scale row. Rows past M are left as they are: their D
-      // columns are never read.
+      // two 512-byte scale blocks ([token][16 bytes], groups 0-3 then 4-7 in
+      // bytes 0-3), which the MMA warp copies to TMEM. Rows past M are left
+      // as they are: their D columns are never read.
       constexpr int BS = tm_bstages(NT);
       constexpr uint32_t kBoxBytes = BOX * kBfRowBytes;
       const uint32_t cpart_bytes = p.kparts > 1 ? (uint32_t)(p.kparts - 1) * kRows * 8u * NT * 4u : 0u;
       uint8_t* xb0 = reinterpret_cast<uint8_t*>(cpart) + cpart_bytes;
       xb0 += (128u - (smem_u32(xb0) & 127u)) & 127u;
       const int tl = lane & 3, g = lane >> 2;
-      int kb_issue = u0 % p.n_blocks;
-      auto issue_box = [&](int j) {  // lane 0
+      auto kb_add = [&](int kbv, int d) {  // (kbv + d) mod n_blocks, d <= BS
+        kbv += d;
+        while (kbv >= p.n_blocks) kbv -= p.n_blocks;
+        return kbv;
+      };
+      auto issue_box = [&](int j, int kbj) {  // lane 0: unit j, K block kbj
         const uint32_t bar = kBfull + 8 * (j % BS);
         mbar_arrive_expect_tx(bar, kBoxBytes);
-        tma_load_2d(smem_u32(xb0 + (size_t)(j % BS) * kBoxBytes), &maps.xb, kb_issue * 256, 0, bar, keep);
-        kb_issue = (kb_issue + 1 == p.n_blocks) ? 0 : kb_issue + 1;
+        tma_load_2d(smem_u32(xb0 + (size_t)(j % BS) * kBoxBytes), &maps.xb, kbj * 256, 0, bar, keep);
       };
+      const int kb0 = kb_add(u0 % p.n_blocks, xw);  // K block of this warp's first unit
       if (lane == 0)
-        for (int j = 0; j < BS && j < n_units; ++j) issue_box(j);
-      int kb = u0 % p.n_blocks;
-      for (int j = 0; j < n_units; ++j, kb = (kb + 1 == p.n_blocks) ? 0 : kb + 1) {
+        for (int j = xw, kbj = kb0; j < BS && j < n_units; j += 2, kbj = kb_add(kbj, 2)) issue_box(j, kbj);
+      for (int j = xw, kb = kb0; j < n_units; j += 2, kb = kb_add(kb, 2)) {
         const int x = j % AS;
         bool ok = mbar_wait_bounded(kBfull + 8 * (j % BS), (uint32_t)(j / BS) & 1u, kSiteGemvFull);
         if (j >= AS) ok = ok && mbar_wait_bounded(kXempty + 8 * x, ((j / AS) & 1) ^ 1, kSiteGemvEmpty);
@@ -420,7 +429,7 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
             const int ch = (i + tl) & 3;  // 8-value chunk of the group held in c[i]
             *reinterpret_cast<uint2*>(sl + L.b + ((2 * g + (ch >> 1)) * BOX + t) * 16 + (ch & 1) * 8) = q[i];
           }
-          sl[L.xs + t * 16 + (kb & 1) * 8 + g] = (uint8_t)code;
+          sl[L.xs + (g >> 2) * 512 + t * 16 + (g & 3)] = (uint8_t)code;
         }
         // The MMA reads the tile through the async proxy, and the next TMA
         // load overwrites the bf16 box just read.
@@ -428,7 +437,7 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(kXfull + 8 * x);
-          if (j + BS < n_units) issue_box(j + BS);
+          if (j + BS < n_units) issue_box(j + BS, kb_add(kb, BS));
         }
         __syncwarp();
       }
@@ -474,8 +483,14 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
       tc::fence_after_sync();
       const uint64_t db0 = tc::smem_desc(smem_u32(x0 + (size_t)x * L.xslot + L.b), kLbo, kSbo);
       const uint32_t dcol = tmem + kTmemD + (uint32_t)(db * 8 * NM), acol = tmem + (uint32_t)(r * 64);
-      const uint32_t sfb = tmem + tm_sfb_col(NT) + 8u * r;  // written by the epilogue
+      // Written by the epilogue (activation tiles by TMA) or copied below (fused quantization).
+      const uint32_t sfb = tmem + tm_sfb_col(NT) + 8u * r;
       if (tm::elect_one()) {
+        if (p.x_bf16) {  // fused quantization: this unit's activation scales from shared memory
+          const uint32_t sfs = smem_u32(x0 + (size_t)x * L.xslot + L.xs);
+          tc::cp_32x128b_warpx4(sfb, tc::smem_desc(sfs, 128u, 128u));
+          tc::cp_32x128b_warpx4(sfb + 4u, tc::smem_desc(sfs + 512u, 128u, 128u));
+        }
 #pragma unroll
         for (int g = 0; g < 8; ++g)
           tc::mma_mx_e4m3_ts(dcol + (uint32_t)(g * NM), acol + (uint32_t)(g * 8), db0 + (uint64_t)((2u * kLbo * g) >> 4),
@@ -615,6 +630,7 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
     const uint32_t tsf = tmem + ((uint32_t)(32 * q) << 16) + tm_sfb_col(NT);
     // kbj: the K block of unit j (for the half of the scale row it uses).
     auto write_sf = [&](int j, int kbj) -> bool {
+      if (p.x_bf16) return true;  // the MMA warp copies them (fused quantization)
       const int xj = j % AS;
       bool ok = mbar_try_wait(kXfull + 8 * xj, (j / AS) & 1);
       if (!__all_sync(0xFFFFFFFFu, ok)) {
@@ -640,14 +656,22 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
     __syncwarp();
     int seg_begin = u0;
     int kb_next = kb_first, rt_next = u0 / p.n_blocks;  // K block and row tile of unit `it`
-    for (int it = 0, u = u0; sf_ok && u < u1; ++u, ++it, kb_ahead = kb_step(kb_ahead)) {
-      const int r = it % kRing, db = kDBuf == 2 ? (it & 1) : 0;
+    int r = 0;  // ring slot of unit `it` and its phase
+    uint32_t rph = 0;
+    auto next_slot = [&]() {
+      if (++r == kRing) {
+        r = 0;
+        rph ^= 1u;
+      }
+    };
+    for (int it = 0, u = u0; sf_ok && u < u1; ++u, ++it, kb_ahead = kb_step(kb_ahead), next_slot()) {
+      const int db = kDBuf == 2 ? (it & 1) : 0;
       const uint32_t mpar = kDBuf == 2 ? ((it >> 1) & 1) : (it & 1);
       bool ok = mbar_try_wait(kMdone + 8 * db, mpar);
-      bool ok2 = mbar_try_wait(kAfull + 8 * r, (it / kRing) & 1);
+      bool ok2 = mbar_try_wait(kAfull + 8 * r, rph);
       if (!__all_sync(0xFFFFFFFFu, ok && ok2)) {  // slow path, taken by the whole warp
         ok = mbar_wait_bounded(kMdone + 8 * db, mpar, kSiteGemvFull);
-        ok = ok && mbar_wait_bounded(kAfull + 8 * r, (it / kRing) & 1, kSiteGemvFull);
+        ok = ok && mbar_wait_bounded(kAfull + 8 * r, rph, kSiteGemvFull);
         if (!__all_sync(0xFFFFFFFFu, ok)) break;
       }
       tc::fence_after_sync();
@@ -660,7 +684,7 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
       const uint32_t tb0 = lop3_and_or(dsc.y << 1, 0x1E1E1E1Eu, 0x01010101u);
       const uint32_t tb1 = lop3_and_or(dsc.y >> 3, 0x1E1E1E1Eu, 0x01010101u);
       // Groups per batch of TMEM loads (one wait per batch), within the register budget.
-      constexpr int GB = kDecWarps == 8 ? (TOK <= 16 ? 4 : 2) : 2;
+      constexpr int GB = kDecWarps == 8 ? (TOK <= 8 ? 8 : TOK <= 16 ? 4 : 2) : 2;
 #pragma unroll
       for (int t0 = 0; t0 < TOK; t0 += 8) {
 #pragma unroll
@@ -712,8 +736,8 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
           __syncwarp();
         } else {
           if (__all_sync(0xFFFFFFFFu, mbar_wait_cluster_bounded(kCred, 0, kSiteGemvFull))) {
-            for (int r = 1; r < p.kparts; ++r) {
-              const float* src = cpart + ((r - 1) * kRows + rl) * TOK;
+            for (int rk = 1; rk < p.kparts; ++rk) {
+              const float* src = cpart + ((rk - 1) * kRows + rl) * TOK;
 #pragma unroll
               for (int t = 0; t < TOK; ++t) acc[t] += src[t];
             }
