@@ -62,32 +62,32 @@ __device__ __forceinline__ uint32_t mxfp8_quad_rne(const float (&v)[8], uint2& o
 // One 32-value group of bf16 held by one lane (c[i]: values 8i .. 8i+7, two
 // per word, the even one in the low half): returns the scale code and the
 // 32 E4M3 bytes (q[i]: those of c[i], as mxfp8_quad_rne packs them). The same
-// results as mxfp8_quad_rne on the widened values: the largest magnitude is
-// found on the 15 magnitude bits as unsigned integers, where every NaN pattern
-// sorts above Inf, and maps to the same code.
+// results as mxfp8_quad_rne on the widened values: the largest magnitude comes
+// from a bf16x2 maximum of absolute values that propagates NaN (the magnitude
+// is one of the inputs, exactly), and each product is one round-to-nearest
+// FP32 multiply, two per packed instruction.
 __device__ __forceinline__ uint32_t mxfp8_group32_bf16_rne(const uint4 (&c)[4], uint2 (&q)[4]) {
   uint32_t mx = 0;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const uint32_t w4[4] = {c[i].x, c[i].y, c[i].z, c[i].w};
 #pragma unroll
-    for (int j = 0; j < 4; ++j) asm("max.u16x2 %0, %0, %1;" : "+r"(mx) : "r"(w4[j] & 0x7FFF7FFFu));
+    for (int j = 0; j < 4; ++j) asm("max.NaN.xorsign.abs.bf16x2 %0, %0, %1;" : "+r"(mx) : "r"(w4[j]));
   }
-  const uint32_t mb = max(mx & 0xFFFFu, mx >> 16);
+  const uint32_t mb = max(mx & 0x7FFFu, (mx >> 16) & 0x7FFFu);  // the result's sign bits are not used
   const uint32_t code = mxfp8_scale_code(__uint_as_float(mb << 16));
   const float inv = e8m0_to_float(code == 0xFFu ? 0u : 254u - code);
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const uint32_t w4[4] = {c[i].x, c[i].y, c[i].z, c[i].w};
-    uint32_t packed[2];
+    uint32_t b[4];
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const uint32_t a = w4[2 * h], b = w4[2 * h + 1];
-      const uint32_t lo = cvt_e4m3x2_rn(__uint_as_float(a << 16) * inv, __uint_as_float(a & 0xFFFF0000u) * inv);
-      const uint32_t hi = cvt_e4m3x2_rn(__uint_as_float(b << 16) * inv, __uint_as_float(b & 0xFFFF0000u) * inv);
-      packed[h] = lo | (hi << 16);
+    for (int j = 0; j < 4; ++j) {
+      float lo, hi;
+      mul2(lo, hi, __uint_as_float(w4[j] << 16), __uint_as_float(w4[j] & 0xFFFF0000u), inv, inv);
+      b[j] = cvt_e4m3x2_rn(lo, hi);
     }
-    q[i] = make_uint2(packed[0], packed[1]);
+    q[i] = make_uint2(prmt(b[0], b[1], 0x5410u), prmt(b[2], b[3], 0x5410u));
   }
   return code;
 }
