@@ -188,6 +188,39 @@ MAMBO_API int mambo_iq3s_linear_fused(const void* x, int x_dtype, int64_t ldx, i
 MAMBO_API size_t mambo_iq3s_linear_fused_workspace_bytes(int64_t m, int64_t n_rows, int64_t n_blocks,
                                                          const MamboLinearConfig* cfg);
 
+/* One linear of a group: x [m, K] (row stride ldx, f32 or bf16) times w into
+ * out [m, N] (row stride ldo, f32 or bf16). */
+typedef struct MamboLinearItem {
+  const void* x;
+  int x_dtype;
+  int64_t ldx;
+  int64_t m;
+  const MamboIQ3SWeight* w;
+  void* out;
+  int out_dtype;
+  int64_t ldo;
+} MamboLinearItem;
+
+#define MAMBO_MAX_GROUP 32
+
+/*
+ * Several independent linears (no item's out overlaps another item's x or
+ * weights), each as mambo_iq3s_linear_fused computes it (MXFP8 activations,
+ * round to nearest even). With up to MAMBO_MAX_GROUP items, all with bf16
+ * activations in 16-byte aligned rows, M < 32 and w->packed set, this is ONE
+ * persistent GEMV launch over the units of every item (stream-K): the weights
+ * of the next linear stream in while the previous one finishes, and the
+ * per-launch set-up is paid once. Otherwise the items run one after another.
+ * workspace: mambo_iq3s_linear_group_workspace_bytes() bytes, zero-filled once.
+ * No reference counterpart (the reference launches one linear per call,
+ * iq3_s_fp8.py:364-399).
+ */
+MAMBO_API int mambo_iq3s_linear_group(const MamboLinearItem* items, int count, const uint32_t* fp8_table,
+                                      void* workspace, size_t workspace_bytes, mambo_stream_t stream);
+
+/* Workspace bytes mambo_iq3s_linear_group needs for these items. */
+MAMBO_API size_t mambo_iq3s_linear_group_workspace_bytes(const MamboLinearItem* items, int count);
+
 /* Workspace bytes mambo_iq3s_linear needs for this shape and configuration. */
 MAMBO_API size_t mambo_iq3s_linear_workspace_bytes(int64_t m, int64_t n_rows, int64_t n_blocks, const MamboLinearConfig* cfg);
 

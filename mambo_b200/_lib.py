@@ -48,6 +48,8 @@ EXPORTED_SYMBOLS = (
     "mambo_iq3s_linear_noalloc",
     "mambo_iq3s_linear_fused",
     "mambo_iq3s_linear_fused_workspace_bytes",
+    "mambo_iq3s_linear_group",
+    "mambo_iq3s_linear_group_workspace_bytes",
     "mambo_num_configs",
     "mambo_config_at",
     "mambo_default_config",
@@ -68,6 +70,24 @@ class MamboIQ3SWeight(ctypes.Structure):
         ("n_blocks", ctypes.c_int64),
         ("packed", ctypes.c_void_p),
     ]
+
+
+class MamboLinearItem(ctypes.Structure):
+    """One linear of mambo_iq3s_linear_group (x [m,K] times w into out [m,N])."""
+
+    _fields_ = [
+        ("x", ctypes.c_void_p),
+        ("x_dtype", ctypes.c_int),
+        ("ldx", ctypes.c_int64),
+        ("m", ctypes.c_int64),
+        ("w", ctypes.POINTER(MamboIQ3SWeight)),
+        ("out", ctypes.c_void_p),
+        ("out_dtype", ctypes.c_int),
+        ("ldo", ctypes.c_int64),
+    ]
+
+
+MAMBO_MAX_GROUP = 32
 
 
 class MamboLinearConfig(ctypes.Structure):
@@ -151,6 +171,9 @@ def load() -> ctypes.CDLL:
             ),
             "mambo_iq3s_linear_fused_workspace_bytes": (
                 [i64, i64, i64, ctypes.POINTER(MamboLinearConfig)], ctypes.c_size_t),
+            "mambo_iq3s_linear_group": (
+                [ctypes.POINTER(MamboLinearItem), i32, vp, vp, ctypes.c_size_t, vp], i32),
+            "mambo_iq3s_linear_group_workspace_bytes": ([ctypes.POINTER(MamboLinearItem), i32], ctypes.c_size_t),
             "mambo_num_configs": ([i32], i32),
             "mambo_config_at": ([i32, i32, ctypes.POINTER(MamboLinearConfig)], i32),
             "mambo_default_config": ([i64, i64, i64, ctypes.POINTER(MamboLinearConfig)], i32),

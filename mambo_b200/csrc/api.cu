@@ -834,6 +834,145 @@ int mambo_iq3s_linear_fused(const void* x, int x_dtype, int64_t ldx, int64_t m, 
 }  // extern "C"
 
 // --------------------------------------------------------------------------
+// Grouped linears: one persistent launch over independent linears.
+// --------------------------------------------------------------------------
+namespace {
+
+constexpr int kGroupDecWarps = 8;
+static_assert(MAMBO_MAX_GROUP == kGemvMaxItems, "group size limit of the C ABI and of the kernel");
+
+// Whether the items qualify for one grouped launch (bf16 activations with
+// 16-byte aligned rows, packed weights, M < 32, counters for every row tile).
+bool group_fusable(const MamboLinearItem* items, int count) {
+  if (count < 1 || count > kGemvMaxItems) return false;
+  int64_t tiles = 0, units = 0;
+  for (int i = 0; i < count; ++i) {
+    const MamboLinearItem& it = items[i];
+    const MamboIQ3SWeight* w = it.w;
+    if (it.x_dtype != MAMBO_BF16 || it.m < 1 || it.m >= kGemmMinTokens) return false;
+    if ((uintptr_t)it.x % 16 || it.ldx % 8) return false;
+    if (!w->packed || (uintptr_t)w->packed % 16 || w->n_rows % 8) return false;
+    const int64_t rt = (w->n_rows + 127) / 128;
+    tiles += rt;
+    units += rt * w->n_blocks;
+  }
+  return (size_t)tiles * 4 * sizeof(int) <= kCounterBytes && units < (int64_t)1 << 30;
+}
+
+int group_nt(const MamboLinearItem* items, int count) {
+  int64_t m = 1;
+  for (int i = 0; i < count; ++i) m = items[i].m > m ? items[i].m : m;
+  return gemv_nt_for(m);
+}
+
+size_t group_partial_bytes(int nt, int sms) { return align256((size_t)sms * 2 * 128 * 8 * nt * sizeof(float)); }
+
+}  // namespace
+
+extern "C" {
+
+size_t mambo_iq3s_linear_group_workspace_bytes(const MamboLinearItem* items, int count) {
+  if (!items || count < 1) return 0;
+  int st;
+  DeviceInfo info = device_info(&st);
+  const int sms = (st == MAMBO_OK && info.sms > 0) ? info.sms : 148;
+  size_t need = kCounterBytes + group_partial_bytes(group_nt(items, count), sms);
+  for (int i = 0; i < count; ++i) {  // the per-item path, when the group does not qualify
+    if (!items[i].w) continue;
+    const size_t b = mambo_iq3s_linear_fused_workspace_bytes(items[i].m, items[i].w->n_rows, items[i].w->n_blocks,
+                                                             nullptr);
+    need = b > need ? b : need;
+  }
+  return need;
+}
+
+int mambo_iq3s_linear_group(const MamboLinearItem* items, int count, const uint32_t* fp8_table, void* workspace,
+                            size_t workspace_bytes, mambo_stream_t stream) {
+  if (!items || !fp8_table) return fail(MAMBO_EINVAL, "null pointer");
+  if (count < 1) return fail(MAMBO_EINVAL, "a group needs at least one linear");
+  for (int i = 0; i < count; ++i) {
+    const MamboLinearItem& it = items[i];
+    const MamboIQ3SWeight* w = it.w;
+    if (!it.x || !w || !it.out) return fail(MAMBO_EINVAL, "item %d: null pointer", i);
+    if (!w->d || !w->qs || !w->qh || !w->signs || !w->scales) return fail(MAMBO_EINVAL, "item %d: null weight field", i);
+    if (w->n_rows < 1 || w->n_blocks < 1 || w->n_rows > (1 << 30) || w->n_blocks > (1 << 20))
+      return fail(MAMBO_EINVAL, "item %d: IQ3_S weight must have positive N and K", i);
+    if (it.x_dtype != MAMBO_F32 && it.x_dtype != MAMBO_BF16)
+      return fail(MAMBO_EINVAL, "item %d: activation must be f32 or bf16", i);
+    if (it.m < 1 || it.ldx < w->n_blocks * 256) return fail(MAMBO_EINVAL, "item %d: activation must be [M,K]", i);
+    if (it.out_dtype != MAMBO_F32 && it.out_dtype != MAMBO_BF16)
+      return fail(MAMBO_EINVAL, "item %d: out must be f32 or bf16", i);
+    if (it.ldo < w->n_rows) return fail(MAMBO_EINVAL, "item %d: out row stride is smaller than N", i);
+  }
+  if (!workspace || (uintptr_t)workspace % 256) return fail(MAMBO_EINVAL, "workspace must be 256-byte aligned");
+  DeviceInfo info;
+  int st = require_sm100(&info);
+  if (st != MAMBO_OK) return st;
+  if (!group_fusable(items, count)) {
+    // One call per item, in order, on the stream (they share the workspace).
+    for (int i = 0; i < count; ++i) {
+      const MamboLinearItem& it = items[i];
+      st = mambo_iq3s_linear_fused(it.x, it.x_dtype, it.ldx, it.m, it.w, fp8_table, it.out, it.out_dtype, it.ldo,
+                                   nullptr, workspace, workspace_bytes, stream);
+      if (st != MAMBO_OK) return st;
+    }
+    return ok();
+  }
+  const int nt = group_nt(items, count);
+  const size_t need = kCounterBytes + group_partial_bytes(nt, info.sms);
+  if (workspace_bytes < need)
+    return fail(MAMBO_EWORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+  GemvGroup g;
+  std::memset(&g, 0, sizeof(g));
+  g.count = count;
+  int units = 0, tiles = 0, box = 8 * nt;
+  for (int i = 0; i < count; ++i) {
+    const MamboLinearItem& it = items[i];
+    const MamboIQ3SWeight* w = it.w;
+    const int rt = (int)((w->n_rows + 127) / 128);
+    GemvItem& gi = g.items[i];
+    gi.packed = (const uint8_t*)w->packed;
+    gi.x = (const uint16_t*)it.x;
+    gi.out = it.out;
+    gi.ldx = it.ldx;
+    gi.ldo = it.ldo;
+    gi.n_rows = (int)w->n_rows;
+    gi.n_blocks = (int)w->n_blocks;
+    gi.m = (int)it.m;
+    gi.out_bf16 = it.out_dtype == MAMBO_BF16;
+    gi.unit0 = units;
+    gi.tile0 = tiles;
+    if (!make_gemv_xb_map(gi.x, it.ldx, gi.m, w->n_blocks * 256, box, &g.xb[i]))
+      return fail(MAMBO_EINVAL, "item %d: bf16 activations need 16-byte aligned rows", i);
+    units += rt * gi.n_blocks;
+    tiles += rt;
+  }
+  GemvTmParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.m = box;
+  p.n_rows = 0;
+  p.n_blocks = 1;  // per item in the group
+  p.packed = g.items[0].packed;
+  p.table = fp8_table;
+  p.counters = (int*)workspace;
+  p.partials = (float*)((uint8_t*)workspace + kCounterBytes);
+  p.stages = 8;
+  while (p.stages > 2 && (int)gemv_tm_smem_bytes(nt, p.stages, 0, true) > info.max_smem_optin) --p.stages;
+  if ((int)gemv_tm_smem_bytes(nt, p.stages, 0, true) > info.max_smem_optin)
+    return fail(MAMBO_EINVAL, "the grouped GEMV does not fit in shared memory");
+  p.prefetch = 0;
+  p.kparts = 0;
+  p.row_tiles = tiles;
+  p.total_units = units;
+  const int grid = units < info.sms ? units : info.sms;
+  cudaError_t e = launch_gemv_tm_group(p, g, nt, kGroupDecWarps, grid, (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "iq3s_gemv_tm_kernel (group)");
+  return ok();
+}
+
+}  // extern "C"
+
+// --------------------------------------------------------------------------
 // mambo_iq3s_linear_noalloc: the tcgen05 GEMV with library-held scratch, for
 // callers that cannot allocate device memory (see include/mambo_b200.h).
 // --------------------------------------------------------------------------

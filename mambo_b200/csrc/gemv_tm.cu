@@ -36,9 +36,11 @@
 //    they write the activation scales of the unit whose MMAs wait for that
 //    buffer into TMEM (tcgen05.st, all four quadrants), so the MMA warp only
 //    issues MMAs.
+#include <cstring>
 #include <map>
 #include <mutex>
 #include <tuple>
+#include <type_traits>
 
 #include "kernels.cuh"
 #include "tcgen05.cuh"
@@ -134,23 +136,40 @@ __device__ __forceinline__ int cta_of_unit_tm(int u, int grid, int units) {
   return (int)((((int64_t)u + 1) * grid - 1) / units);
 }
 
-__device__ __forceinline__ void store_out_tm(const GemvTmParams& p, int row, int tok, float v) {
-  if (row < p.n_rows && tok < p.m) {
-    if (p.out_bf16) {
-      reinterpret_cast<__nv_bfloat16*>(p.out)[(int64_t)tok * p.ldo + row] = __float2bfloat16_rn(v);
+// Where one linear's results go.
+struct OutView {
+  void* out;
+  int64_t ldo;
+  int out_bf16;
+  int n_rows;
+  int m;
+};
+
+__device__ __forceinline__ void store_out_tm(const OutView& o, int row, int tok, float v) {
+  if (row < o.n_rows && tok < o.m) {
+    if (o.out_bf16) {
+      reinterpret_cast<__nv_bfloat16*>(o.out)[(int64_t)tok * o.ldo + row] = __float2bfloat16_rn(v);
     } else {
-      reinterpret_cast<float*>(p.out)[(int64_t)tok * p.ldo + row] = v;
+      reinterpret_cast<float*>(o.out)[(int64_t)tok * o.ldo + row] = v;
     }
   }
+}
+
+// The item of a grouped launch that holds unit u, searching upwards from item l.
+__device__ __forceinline__ int group_item(const GemvGroup& g, int u, int l) {
+  while (l + 1 < g.count && g.items[l + 1].unit0 <= u) ++l;
+  return l;
 }
 
 // Sums the partials of one weight row (local row rl of tile rt) over the
 // contributing CTAs in CTA order and stores it; the partials of CTA `self`
 // come from `acc` (its registers) instead of memory. Loads for several
 // contributors are in flight together.
-template <int TOK>
-__device__ __forceinline__ void sum_partials(const GemvTmParams& p, int rt, int rl, int row, int self, int c_first,
-                                             int c_last, const float (&acc)[TOK]) {
+// tile: the row tile's number; tile_of(u): the row tile holding unit u.
+template <int TOK, class TileOf>
+__device__ __forceinline__ void sum_partials(const float* partials, int total_units, const OutView& o, int tile,
+                                             int rl, int row, int self, int c_first, int c_last, TileOf tile_of,
+                                             const float (&acc)[TOK]) {
   const int grid = gridDim.x;
 #pragma unroll
   for (int t0 = 0; t0 < TOK; t0 += 8) {
@@ -165,8 +184,8 @@ __device__ __forceinline__ void sum_partials(const GemvTmParams& p, int rt, int 
       for (int j = 0; j < kB; ++j) {
         const int c = c0 + j;
         if (c <= c_last && c != self) {
-          const int cs = (rt == unit_begin_tm(c, grid, p.total_units) / p.n_blocks) ? 0 : 1;
-          const float4* src = reinterpret_cast<const float4*>(p.partials + ((size_t)(c * 2 + cs) * 128 + rl) * TOK + t0);
+          const int cs = (tile == tile_of(unit_begin_tm(c, grid, total_units))) ? 0 : 1;
+          const float4* src = reinterpret_cast<const float4*>(partials + ((size_t)(c * 2 + cs) * 128 + rl) * TOK + t0);
           v[j][0] = __ldcg(src);
           v[j][1] = __ldcg(src + 1);
         } else {
@@ -190,15 +209,20 @@ __device__ __forceinline__ void sum_partials(const GemvTmParams& p, int rt, int 
       }
     }
 #pragma unroll
-    for (int t = 0; t < 8; ++t) store_out_tm(p, row, t0 + t, sum[t]);
+    for (int t = 0; t < 8; ++t) store_out_tm(o, row, t0 + t, sum[t]);
   }
 }
 
 }  // namespace
 
-template <int NT, int kDecWarps>
+// G: GemvNoGroup (one linear, described by p and maps) or GemvGroup (a grouped
+// launch: units of every item back to back, stream-K; weights packed,
+// activations bf16 quantized here).
+template <int NT, int kDecWarps, class G>
 __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
-    iq3s_gemv_tm_kernel(const __grid_constant__ GemvTmParams p, const __grid_constant__ GemvTmMaps maps) {
+    iq3s_gemv_tm_kernel(const __grid_constant__ GemvTmParams p, const __grid_constant__ GemvTmMaps maps,
+                        const __grid_constant__ G grp) {
+  constexpr bool kGroup = std::is_same<G, GemvGroup>::value;
   constexpr int TOK = 8 * NT;             // tokens the epilogue keeps
   constexpr int NM = tm_nmma(NT);         // MMA N
   constexpr int BOX = tm_box_tokens(NT);  // activation rows in a B tile
@@ -313,14 +337,25 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
       rows = (uint32_t)min(kRows, p.n_rows - n0);
       base = (size_t)(u % p.n_blocks) * p.n_rows + n0;
     };
+    // Tile-major record of unit u (units visited in ascending order through `hint`).
+    auto record = [&](int u, int& hint) -> const uint8_t* {
+      if constexpr (kGroup) {
+        hint = group_item(grp, u, hint);
+        return grp.items[hint].packed + (size_t)(u - grp.items[hint].unit0) * kRecordBytes;
+      } else {
+        return p.packed + (size_t)u * kRecordBytes;
+      }
+    };
+    int issue_hint = 0, prefetch_hint = 0;
     auto issue_weights = [&](int it, int s) {
       const uint32_t full = kWfull + 8 * s;
       const uint32_t st = smem_u32(st0 + (size_t)s * L.stage);
-      if (p.packed) {
+      if (kGroup || p.packed) {
         // Tile-major records have the stage's layout: one copy per unit.
+        const uint8_t* rec = record(u0 + it, issue_hint);
         if (lane == 0) {
           mbar_arrive_expect_tx(full, (uint32_t)kRecordBytes);
-          bulk_load_hint(st, p.packed + (size_t)(u0 + it) * kRecordBytes, kRecordBytes, full, policy);
+          bulk_load_hint(st, rec, kRecordBytes, full, policy);
         }
       } else {
         uint32_t rows;
@@ -333,8 +368,9 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
       __syncwarp();
     };
     auto prefetch = [&](int it) {
-      if (p.packed) {
-        if (lane == 0) bulk_prefetch_l2(p.packed + (size_t)(u0 + it) * kRecordBytes, kRecordBytes);
+      if (kGroup || p.packed) {
+        const uint8_t* rec = record(u0 + it, prefetch_hint);
+        if (lane == 0) bulk_prefetch_l2(rec, kRecordBytes);
       } else {
         uint32_t rows;
         size_t base;
@@ -370,9 +406,12 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
   // copies need one warp; fused quantization takes both, every other unit.
   if (warp >= kXWarp0) {
     const int xw = warp - kXWarp0;
-    if (xw != 0 && !p.x_bf16) return;
+    const bool fused = kGroup || p.x_bf16 != nullptr;
+    if (xw != 0 && !fused) return;
     const uint64_t keep = l2_policy_evict_last();  // every CTA reads them
-    if (lane == 0 && xw == 0) {
+    if constexpr (kGroup) {
+      if (xw == 0 && lane < grp.count) tma_prefetch_desc(&grp.xb[lane]);
+    } else if (lane == 0 && xw == 0) {
       if (p.x_bf16) {
         tma_prefetch_desc(&maps.xb);
       } else {
@@ -381,12 +420,13 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
       }
     }
     pdl_wait();
-    if (p.x_bf16) {
+    if (fused) {
       // Fused quantization (the standalone quantizer's arithmetic): the bf16
       // box of each K block arrives by TMA, BS units ahead. A lane quantizes
-      // one 32-value group of one token (4 tokens x 8 groups a pass), reading
-      // its four 16-byte chunks in an order rotated by token so that each
-      // quarter warp hits all banks, and writes the E4M3 bytes straight into
+      // one 32-value group of one token (4 tokens x 8 groups a pass; with 1-2
+      // tokens, four lanes a group), reading its four 16-byte chunks in an
+      // order rotated by token so that each quarter warp hits all banks, and
+      // writes the E4M3 bytes straight into
       // the B tile [16-byte K chunk][token][16 bytes], the scale code into
       // two 512-byte scale blocks ([token][16 bytes], groups 0-3 then 4-7 in
       // bytes 0-3), which the MMA warp copies to TMEM. Rows past M are left
@@ -397,39 +437,84 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
       uint8_t* xb0 = reinterpret_cast<uint8_t*>(cpart) + cpart_bytes;
       xb0 += (128u - (smem_u32(xb0) & 127u)) & 127u;
       const int tl = lane & 3, g = lane >> 2;
-      auto kb_add = [&](int kbv, int d) {  // (kbv + d) mod n_blocks, d <= BS
-        kbv += d;
-        while (kbv >= p.n_blocks) kbv -= p.n_blocks;
-        return kbv;
+      // Unit cursor: item, unit within the item, K block. It only moves to
+      // units of this CTA's range (which exist), by a few units at a time.
+      struct XCursor {
+        int j, l, v, kb, nb, units;
       };
-      auto issue_box = [&](int j, int kbj) {  // lane 0: unit j, K block kbj
+      auto cursor_at = [&](int j) {
+        XCursor c{j, 0, u0 + j, 0, p.n_blocks, 0x7FFFFFFF};
+        if constexpr (kGroup) {
+          c.l = group_item(grp, u0 + j, 0);
+          const GemvItem& gi = grp.items[c.l];
+          c.nb = gi.n_blocks;
+          c.units = ((gi.n_rows + kRows - 1) / kRows) * gi.n_blocks;
+          c.v = u0 + j - gi.unit0;
+        }
+        c.kb = c.v % c.nb;
+        return c;
+      };
+      auto move_to = [&](XCursor& c, int j) {
+        const int d = j - c.j;
+        c.j = j;
+        c.v += d;
+        c.kb += d;
+        while (c.kb >= c.nb) c.kb -= c.nb;
+        if constexpr (kGroup) {
+          while (c.v >= c.units && c.l + 1 < grp.count) {  // into the next item
+            c.v -= c.units;
+            const GemvItem& gi = grp.items[++c.l];
+            c.nb = gi.n_blocks;
+            c.units = ((gi.n_rows + kRows - 1) / kRows) * gi.n_blocks;
+            c.kb = c.v % c.nb;
+          }
+        }
+      };
+      XCursor ic = cursor_at(xw), qc = ic;  // next box to issue, unit being quantized
+      auto issue_box = [&](int j) {  // lane 0: the bf16 box of unit j
+        move_to(ic, j);
+        const CUtensorMap* map = &maps.xb;
+        if constexpr (kGroup) map = &grp.xb[ic.l];
         const uint32_t bar = kBfull + 8 * (j % BS);
         mbar_arrive_expect_tx(bar, kBoxBytes);
-        tma_load_2d(smem_u32(xb0 + (size_t)(j % BS) * kBoxBytes), &maps.xb, kbj * 256, 0, bar, keep);
+        tma_load_2d(smem_u32(xb0 + (size_t)(j % BS) * kBoxBytes), map, ic.kb * 256, 0, bar, keep);
       };
-      const int kb0 = kb_add(u0 % p.n_blocks, xw);  // K block of this warp's first unit
       if (lane == 0)
-        for (int j = xw, kbj = kb0; j < BS && j < n_units; j += 2, kbj = kb_add(kbj, 2)) issue_box(j, kbj);
-      for (int j = xw, kb = kb0; j < n_units; j += 2, kb = kb_add(kb, 2)) {
+        for (int j = xw; j < BS && j < n_units; j += 2) issue_box(j);
+      for (int j = xw; j < n_units; j += 2) {
         const int x = j % AS;
         bool ok = mbar_wait_bounded(kBfull + 8 * (j % BS), (uint32_t)(j / BS) & 1u, kSiteGemvFull);
         if (j >= AS) ok = ok && mbar_wait_bounded(kXempty + 8 * x, ((j / AS) & 1) ^ 1, kSiteGemvEmpty);
         if (!__all_sync(0xFFFFFFFFu, ok)) return;
-        const uint8_t* src = xb0 + (size_t)(j % BS) * kBoxBytes + g * 64;
+        const uint8_t* box = xb0 + (size_t)(j % BS) * kBoxBytes;
         uint8_t* sl = x0 + (size_t)x * L.xslot;
-        for (int t = tl; t < p.m; t += 4) {
-          uint4 c[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-            c[i] = *reinterpret_cast<const uint4*>(src + t * kBfRowBytes + ((i + tl) & 3) * 16);
-          uint2 q[4];
-          const uint32_t code = mxfp8_group32_bf16_rne(c, q);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int ch = (i + tl) & 3;  // 8-value chunk of the group held in c[i]
-            *reinterpret_cast<uint2*>(sl + L.b + ((2 * g + (ch >> 1)) * BOX + t) * 16 + (ch & 1) * 8) = q[i];
+        move_to(qc, j);
+        int mq = p.m;
+        if constexpr (kGroup) mq = grp.items[qc.l].m;
+        if (mq <= 2) {
+          // Few tokens: four lanes per group (one 16-byte chunk each), a token per pass.
+          for (int t = 0; t < mq; ++t) {
+            const uint4 c = *reinterpret_cast<const uint4*>(box + t * kBfRowBytes + lane * 16);
+            uint2 q;
+            const uint32_t code = mxfp8_quad_bf16_rne(c, q);
+            *reinterpret_cast<uint2*>(sl + L.b + ((2 * g + (tl >> 1)) * BOX + t) * 16 + (tl & 1) * 8) = q;
+            if (tl == 0) sl[L.xs + (g >> 2) * 512 + t * 16 + (g & 3)] = (uint8_t)code;
           }
-          sl[L.xs + (g >> 2) * 512 + t * 16 + (g & 3)] = (uint8_t)code;
+        } else {
+          for (int t = tl; t < mq; t += 4) {
+            uint4 c[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              c[i] = *reinterpret_cast<const uint4*>(box + t * kBfRowBytes + g * 64 + ((i + tl) & 3) * 16);
+            uint2 q[4];
+            const uint32_t code = mxfp8_group32_bf16_rne(c, q);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int ch = (i + tl) & 3;  // 8-value chunk of the group held in c[i]
+              *reinterpret_cast<uint2*>(sl + L.b + ((2 * g + (ch >> 1)) * BOX + t) * 16 + (ch & 1) * 8) = q[i];
+            }
+            sl[L.xs + (g >> 2) * 512 + t * 16 + (g & 3)] = (uint8_t)code;
+          }
         }
         // The MMA reads the tile through the async proxy, and the next TMA
         // load overwrites the bf16 box just read.
@@ -437,7 +522,7 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(kXfull + 8 * x);
-          if (j + BS < n_units) issue_box(j + BS, kb_add(kb, BS));
+          if (j + BS < n_units) issue_box(j + BS);
         }
         __syncwarp();
       }
@@ -486,7 +571,7 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
       // Written by the epilogue (activation tiles by TMA) or copied below (fused quantization).
       const uint32_t sfb = tmem + tm_sfb_col(NT) + 8u * r;
       if (tm::elect_one()) {
-        if (p.x_bf16) {  // fused quantization: this unit's activation scales from shared memory
+        if (kGroup || p.x_bf16) {  // fused quantization: this unit's activation scales from shared memory
           const uint32_t sfs = smem_u32(x0 + (size_t)x * L.xslot + L.xs);
           tc::cp_32x128b_warpx4(sfb, tc::smem_desc(sfs, 128u, 128u));
           tc::cp_32x128b_warpx4(sfb + 4u, tc::smem_desc(sfs + 512u, 128u, 128u));
@@ -529,7 +614,7 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
     // chunk-major ([16-byte chunk][row][16 bytes] for qs and signs, [4-byte
     // column][row][4 bytes] for qh), so the 8 rows of a load phase read
     // consecutive bytes; bulk-copied SoA fields land row-major.
-    const bool cm = p.packed != nullptr;
+    const bool cm = kGroup || p.packed != nullptr;
     uint32_t off_q0, off_q1, off_sg, off_qh;
     if constexpr (kParts == 2) {
       off_q0 = L.qs + (cm ? (2 * part) * 2048 + rl * 16 : rl * 64 + 32 * part);
@@ -630,7 +715,7 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
     const uint32_t tsf = tmem + ((uint32_t)(32 * q) << 16) + tm_sfb_col(NT);
     // kbj: the K block of unit j (for the half of the scale row it uses).
     auto write_sf = [&](int j, int kbj) -> bool {
-      if (p.x_bf16) return true;  // the MMA warp copies them (fused quantization)
+      if (kGroup || p.x_bf16) return true;  // the MMA warp copies them (fused quantization)
       const int xj = j % AS;
       bool ok = mbar_try_wait(kXfull + 8 * xj, (j / AS) & 1);
       if (!__all_sync(0xFFFFFFFFu, ok)) {
@@ -654,8 +739,38 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
     __syncwarp();
     if (lane == 0) mbar_arrive(kSfInit);
     __syncwarp();
+    // The linear of unit `it`: its output, K blocks, first unit and first row
+    // tile in the launch's numbering, row tiles (a grouped launch moves to the
+    // next item when they are done; a single linear has one).
+    OutView ov{p.out, p.ldo, p.out_bf16, p.n_rows, p.m};
+    int cur_nb = p.n_blocks, cur_unit0 = 0, cur_tile0 = 0, cur_tiles = 0, item = 0;
+    auto load_item = [&](int l) {
+      if constexpr (kGroup) {
+        const GemvItem& gi = grp.items[l];
+        ov = OutView{gi.out, gi.ldo, gi.out_bf16, gi.n_rows, gi.m};
+        cur_nb = gi.n_blocks;
+        cur_unit0 = gi.unit0;
+        cur_tile0 = gi.tile0;
+        cur_tiles = (gi.n_rows + kRows - 1) / kRows;
+      }
+    };
+    if constexpr (kGroup) {
+      item = group_item(grp, u0, 0);
+      load_item(item);
+    }
+    // Row tile (in the launch's numbering) holding unit u.
+    auto tile_of = [&](int u) -> int {
+      if constexpr (kGroup) {
+        const int l = group_item(grp, u, 0);
+        return grp.items[l].tile0 + (u - grp.items[l].unit0) / grp.items[l].n_blocks;
+      } else {
+        return u / p.n_blocks;
+      }
+    };
+    const int first_tile = tile_of(u0);
     int seg_begin = u0;
-    int kb_next = kb_first, rt_next = u0 / p.n_blocks;  // K block and row tile of unit `it`
+    // K block and row tile (within its linear) of unit `it`.
+    int kb_next = (u0 - cur_unit0) % cur_nb, rt_next = (u0 - cur_unit0) / cur_nb;
     int r = 0;  // ring slot of unit `it` and its phase
     uint32_t rph = 0;
     auto next_slot = [&]() {
@@ -701,7 +816,7 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
                                  dv, dneg);
 #pragma unroll
             for (int t = 0; t < 8; t += 2) {
-              if (t0 + t < p.m)  // tokens past M are padding (warp-uniform branch)
+              if (t0 + t < ov.m)  // tokens past M are padding (warp-uniform branch)
                 fma2(acc[t0 + t], acc[t0 + t + 1], c[j][t], c[j][t + 1], w, w);
             }
           }
@@ -716,12 +831,20 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
       __syncwarp();  // reconverge before the next waits
 
       const int kb = kb_next, rt = rt_next;
-      if (++kb_next == p.n_blocks) {
+      const OutView ou = ov;  // this unit's linear (the cursor may move to the next item below)
+      const int nbu = cur_nb, unit0u = cur_unit0, tile = cur_tile0 + rt;
+      if (++kb_next == cur_nb) {
         kb_next = 0;
         ++rt_next;
+        if constexpr (kGroup) {
+          if (rt_next == cur_tiles && u + 1 < u1) {
+            load_item(++item);
+            rt_next = 0;
+          }
+        }
       }
-      if (!(kb == p.n_blocks - 1 || u == u1 - 1)) continue;
-      const bool full_tile = (seg_begin % p.n_blocks == 0) && (kb == p.n_blocks - 1);
+      if (!(kb == nbu - 1 || u == u1 - 1)) continue;
+      const bool full_tile = (seg_begin == unit0u + rt * nbu) && (kb == nbu - 1);
       const int row = rt * kRows + rl;
       if (p.kparts > 1) {
         // Cluster K-split: ranks 1.. write their partials into rank 0's shared
@@ -742,22 +865,23 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
               for (int t = 0; t < TOK; ++t) acc[t] += src[t];
             }
 #pragma unroll
-            for (int t = 0; t < TOK; ++t) store_out_tm(p, row, t, acc[t]);
+            for (int t = 0; t < TOK; ++t) store_out_tm(ou, row, t, acc[t]);
           }
         }
       } else if (full_tile) {
 #pragma unroll
-        for (int t = 0; t < TOK; ++t) store_out_tm(p, row, t, acc[t]);
+        for (int t = 0; t < TOK; ++t) store_out_tm(ou, row, t, acc[t]);
       } else {
         // Stream-K: a row tile shared with other CTAs. The segment a CTA
         // finishes last is usually the last contribution: if every other
         // contributor has already published, sum at once; otherwise publish,
         // and the last to arrive sums (in CTA order either way).
         const int cta = blockIdx.x, grid = gridDim.x;
-        const int c_first = cta_of_unit_tm(rt * p.n_blocks, grid, p.total_units);
-        const int c_last = cta_of_unit_tm(rt * p.n_blocks + p.n_blocks - 1, grid, p.total_units);
-        const int slot_id = (rt == u0 / p.n_blocks) ? 0 : 1;
-        int* counter = p.counters + (size_t)rt * kEpiWarps + q;
+        const int tile_u0 = unit0u + rt * nbu;  // first unit of the row tile
+        const int c_first = cta_of_unit_tm(tile_u0, grid, p.total_units);
+        const int c_last = cta_of_unit_tm(tile_u0 + nbu - 1, grid, p.total_units);
+        const int slot_id = (tile == first_tile) ? 0 : 1;
+        int* counter = p.counters + (size_t)tile * kEpiWarps + q;
         int last = 0;
         if (u == u1 - 1) {
           if (lane == 0) last = ld_acquire_gpu(counter) == c_last - c_first;
@@ -774,7 +898,7 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
         }
         if (last) {
           if (lane == 0) *counter = 0;  // every contributor has arrived: leave it zeroed for the next launch
-          sum_partials<TOK>(p, rt, rl, row, cta, c_first, c_last, acc);
+          sum_partials<TOK>(p.partials, p.total_units, ou, tile, rl, row, cta, c_first, c_last, tile_of, acc);
         }
       }
 #pragma unroll
@@ -797,7 +921,11 @@ int gemv_tm_max_stages() { return kMaxStagesTm; }
 
 template <int NT, int kDecWarps>
 static const void* tm_kernel() {
-  return (const void*)iq3s_gemv_tm_kernel<NT, kDecWarps>;
+  return (const void*)iq3s_gemv_tm_kernel<NT, kDecWarps, GemvNoGroup>;
+}
+template <int NT, int kDecWarps>
+static const void* tm_kernel_group() {
+  return (const void*)iq3s_gemv_tm_kernel<NT, kDecWarps, GemvGroup>;
 }
 
 static int query_max_clusters(int nt, int dec_warps, int stages, int kparts);
@@ -854,8 +982,31 @@ static cudaError_t launch_gemv_tm_t(const GemvTmParams& p, const GemvTmMaps& map
   const void* kern = tm_kernel<NT, kDecWarps>();
   cudaError_t e = ensure_smem_attribute(kern, smem);
   if (e != cudaSuccess) return e;
+  const GemvNoGroup none{0};
   return launch_pdl_cluster(kern, dim3(grid), dim3(tm_threads(kDecWarps)), smem, stream, p.kparts > 1 ? p.kparts : 1,
-                            p, maps);
+                            p, maps, none);
+}
+
+// Grouped launches use 8 decoder warps and stream-K.
+template <int NT>
+static cudaError_t launch_gemv_tm_group_t(const GemvTmParams& p, const GemvGroup& g, int grid, cudaStream_t stream) {
+  const uint32_t smem = tm_smem_bytes(NT, p.stages, 0, true);
+  const void* kern = tm_kernel_group<NT, 8>();
+  cudaError_t e = ensure_smem_attribute(kern, smem);
+  if (e != cudaSuccess) return e;
+  GemvTmMaps maps;
+  std::memset(&maps, 0, sizeof(maps));
+  return launch_pdl_cluster(kern, dim3(grid), dim3(tm_threads(8)), smem, stream, 1, p, maps, g);
+}
+
+cudaError_t launch_gemv_tm_group(const GemvTmParams& p, const GemvGroup& g, int nt, int dec_warps, int grid,
+                                 cudaStream_t stream) {
+  if (dec_warps != 8 || p.kparts != 0) return cudaErrorInvalidValue;
+  switch (nt) {
+    case 1: return launch_gemv_tm_group_t<1>(p, g, grid, stream);
+    case 2: return launch_gemv_tm_group_t<2>(p, g, grid, stream);
+    default: return launch_gemv_tm_group_t<4>(p, g, grid, stream);
+  }
 }
 
 template <int NT>

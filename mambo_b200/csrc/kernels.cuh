@@ -158,6 +158,37 @@ struct GemvTmMaps {
   CUtensorMap xb;                        // bf16 activations [m tokens][K], box 256 x 8*NT (fused quantization)
 };
 
+// One linear of a grouped GEMV launch: independent linears (no output feeds
+// another's input) with bf16 activations quantized in the kernel and
+// tile-major packed weights. Units and row tiles are numbered across the
+// group in item order.
+struct GemvItem {
+  const uint8_t* packed;
+  const uint16_t* x;  // bf16 [m][ldx]
+  void* out;          // [m][ldo], f32 or bf16
+  int64_t ldx;
+  int64_t ldo;
+  int n_rows;
+  int n_blocks;
+  int m;
+  int out_bf16;
+  int unit0;  // first unit of this item in the launch's numbering
+  int tile0;  // first row tile of this item in the launch's numbering
+};
+constexpr int kGemvMaxItems = 32;
+struct GemvGroup {
+  CUtensorMap xb[kGemvMaxItems];  // bf16 activation map of each item (box 256 x 8*NT)
+  GemvItem items[kGemvMaxItems];
+  int count;
+};
+// The single-linear launch's stand-in for GemvGroup.
+struct GemvNoGroup {
+  int count;
+};
+// Grouped launch (stream-K over the concatenated units of every item).
+cudaError_t launch_gemv_tm_group(const GemvTmParams& p, const GemvGroup& g, int nt, int dec_warps, int grid,
+                                 cudaStream_t stream);
+
 // Activation map for the tcgen05 GEMV; false when xq is not 16-byte aligned
 // with a row stride that is a multiple of 16.
 bool make_gemv_x_map(const uint8_t* xq, int64_t ldxq, int m, int n_blocks, int box_tokens, CUtensorMap* map);

@@ -59,6 +59,36 @@ __device__ __forceinline__ uint32_t mxfp8_quad_rne(const float (&v)[8], uint2& o
   return code;
 }
 
+// Per half: the larger magnitude of a and b, NaN if either is NaN (sign bits unspecified).
+__device__ __forceinline__ uint32_t absmax_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.NaN.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// One 32-value group of bf16 held by 4 consecutive lanes (c: this lane's 8
+// values, the even one of each pair in the low half; the quad must be
+// converged): returns the group's scale code and this lane's 8 E4M3 bytes, as
+// mxfp8_quad_rne on the widened values.
+__device__ __forceinline__ uint32_t mxfp8_quad_bf16_rne(const uint4& c, uint2& q) {
+  uint32_t a = absmax_bf16x2(absmax_bf16x2(c.x, c.y), absmax_bf16x2(c.z, c.w));
+  a = absmax_bf16x2(a, __shfl_xor_sync(0xFFFFFFFFu, a, 1));
+  a = absmax_bf16x2(a, __shfl_xor_sync(0xFFFFFFFFu, a, 2));
+  const uint32_t mb = max(a & 0x7FFFu, (a >> 16) & 0x7FFFu);
+  const uint32_t code = mxfp8_scale_code(__uint_as_float(mb << 16));
+  const float inv = e8m0_to_float(code == 0xFFu ? 0u : 254u - code);
+  const uint32_t w4[4] = {c.x, c.y, c.z, c.w};
+  uint32_t b[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float lo, hi;
+    mul2(lo, hi, __uint_as_float(w4[j] << 16), __uint_as_float(w4[j] & 0xFFFF0000u), inv, inv);
+    b[j] = cvt_e4m3x2_rn(lo, hi);
+  }
+  q = make_uint2(prmt(b[0], b[1], 0x5410u), prmt(b[2], b[3], 0x5410u));
+  return code;
+}
+
 // One 32-value group of bf16 held by one lane (c[i]: values 8i .. 8i+7, two
 // per word, the even one in the low half): returns the scale code and the
 // 32 E4M3 bytes (q[i]: those of c[i], as mxfp8_quad_rne packs them). The same
@@ -67,13 +97,13 @@ __device__ __forceinline__ uint32_t mxfp8_quad_rne(const float (&v)[8], uint2& o
 // is one of the inputs, exactly), and each product is one round-to-nearest
 // FP32 multiply, two per packed instruction.
 __device__ __forceinline__ uint32_t mxfp8_group32_bf16_rne(const uint4 (&c)[4], uint2 (&q)[4]) {
-  uint32_t mx = 0;
+  uint32_t m4[4];  // a tree of maxima: a short dependency chain
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const uint32_t w4[4] = {c[i].x, c[i].y, c[i].z, c[i].w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) asm("max.NaN.xorsign.abs.bf16x2 %0, %0, %1;" : "+r"(mx) : "r"(w4[j]));
+    uint32_t a = absmax_bf16x2(c[i].x, c[i].y), b = absmax_bf16x2(c[i].z, c[i].w);
+    m4[i] = absmax_bf16x2(a, b);
   }
+  const uint32_t mx = absmax_bf16x2(absmax_bf16x2(m4[0], m4[1]), absmax_bf16x2(m4[2], m4[3]));
   const uint32_t mb = max(mx & 0x7FFFu, (mx >> 16) & 0x7FFFu);  // the result's sign bits are not used
   const uint32_t code = mxfp8_scale_code(__uint_as_float(mb << 16));
   const float inv = e8m0_to_float(code == 0xFFu ? 0u : 254u - code);

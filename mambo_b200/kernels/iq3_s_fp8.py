@@ -28,6 +28,7 @@ One IQ3_S block along K (256 weights, 110 bytes):
 
 from __future__ import annotations
 
+import ctypes
 import json
 import os
 import re
@@ -310,6 +311,72 @@ def iq3_s_fp8_linear(x, iq3_weight: IQ3SFields, *, stream=None, out_dtype: torch
         x = x.contiguous()
     out = torch.empty((x.shape[0], n_rows), dtype=out_dtype, device=dev)
     return fused_linear_into(x, iq3_weight, out, config=config, stream=stream)
+
+
+def group_linear_into(xs, iq3_weights, outs, stream=None) -> list:
+    """Independent linears ``outs[i] = linear(xs[i], iq3_weights[i])`` in one C-ABI call.
+
+    Each is what ``iq3_s_fp8_linear`` computes. With bf16 activations in
+    16-byte aligned rows, M < 32 and packed weights this is one persistent GEMV
+    launch for the whole group (up to ``MAMBO_MAX_GROUP`` linears); otherwise
+    the linears run one after another. No output may overlap another linear's
+    input. No validation beyond the C ABI's.
+    """
+    count = len(xs)
+    items = (_lib.MamboLinearItem * count)()
+    keep = []  # the weight structs must outlive the call
+    for i, (x, w, out) in enumerate(zip(xs, iq3_weights, outs)):
+        ws = weight_struct(w)
+        keep.append(ws)
+        items[i].x = x.data_ptr()
+        items[i].x_dtype = _lib.MAMBO_BF16 if x.dtype == torch.bfloat16 else _lib.MAMBO_F32
+        items[i].ldx = x.stride(0)
+        items[i].m = x.shape[0]
+        items[i].w = ctypes.pointer(ws)
+        items[i].out = out.data_ptr()
+        items[i].out_dtype = _lib.MAMBO_BF16 if out.dtype == torch.bfloat16 else _lib.MAMBO_F32
+        items[i].ldo = out.stride(0)
+    dev = xs[0].device
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        st = _runtime.stream_handle(stream, dev)
+        need = lib.mambo_iq3s_linear_group_workspace_bytes(items, count)
+        ws = _runtime.workspace(dev, st, need)
+        _lib.check(lib.mambo_iq3s_linear_group(items, count, _get_iq3_table(dev).data_ptr(), ws.data_ptr(),
+                                               ws.numel(), st), "iq3_s_fp8_linear_group")
+    return outs
+
+
+def iq3_s_fp8_linear_group(xs, iq3_weights, *, stream=None, out_dtype: torch.dtype = torch.bfloat16) -> list:
+    """Several independent ``iq3_s_fp8_linear`` calls as one (see ``group_linear_into``).
+
+    ``xs[i]``: float32 or bfloat16 [M_i, K_i]; ``iq3_weights[i]``: prepared
+    fields with K_i = 256 * blocks. Returns the list of out_dtype [M_i, N_i].
+    """
+    if len(xs) != len(iq3_weights) or not xs:
+        raise ValueError("xs and iq3_weights must be non-empty lists of the same length")
+    if len(xs) > _lib.MAMBO_MAX_GROUP:
+        raise ValueError(f"at most {_lib.MAMBO_MAX_GROUP} linears per group")
+    if out_dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError("out_dtype must be torch.float32 or torch.bfloat16")
+    xs = [_runtime.as_cuda_tensor(x) for x in xs]
+    dev = xs[0].device
+    outs, ready = [], []
+    for x, w in zip(xs, iq3_weights):
+        n_rows, k_blocks = _weight_dimensions(w)
+        if x.ndim != 2 or x.dtype not in (torch.float32, torch.bfloat16) or x.shape[0] < 1 \
+                or x.shape[1] != k_blocks * 256:
+            raise ValueError("activation must be float32 or bfloat16 [M,K] with K = 256 * weight blocks")
+        if x.device != dev:
+            raise ValueError("all activations must be on one device")
+        if x.stride(1) != 1:
+            x = x.contiguous()
+        ready.append(x)
+        outs.append(torch.empty((x.shape[0], n_rows), dtype=out_dtype, device=dev))
+    if _sm_key(dev) not in BEST_CONFIGS:
+        raise RuntimeError(f"IQ3_S FP8 matmul has no tuned config for {_sm_key(dev)}")
+    _runtime.require_device(dev)
+    return group_linear_into(ready, iq3_weights, outs, stream=stream)
 
 
 # ----------------------------------------------------------------------------
