@@ -60,13 +60,13 @@ def load_peaks() -> tuple[float, str]:
     return HBM_FALLBACK_GBS, "fallback"
 
 
-def read_profiled_traffic():
-    """DRAM bytes per GEMV launch from the committed ncu summary (a line 'dram_bytes_per_launch: N')."""
+def read_profiled_traffic(key: str = "dram_bytes_per_launch"):
+    """DRAM bytes per GEMV launch from the committed ncu summary (a line '<key>: N')."""
     path = ROOT / "profiles" / "iq3s_gemv_tm_decode_llama3_8b.md"
     if not path.is_file():
         return None
     for line in path.read_text().splitlines():
-        if line.strip().startswith("dram_bytes_per_launch:"):
+        if line.strip().startswith(key + ":"):
             try:
                 return float(line.split(":", 1)[1].split()[0])
             except (ValueError, IndexError):
@@ -324,6 +324,24 @@ def run_single(args) -> None:
     print(f"single N={n} K={k} M={m} config={cfg}: ok")
 
 
+def run_group_profile() -> None:
+    """Four grouped launches of the decode sweep (for ncu captures of the grouped kernel)."""
+    import torch
+
+    from mambo_b200.kernels.iq3_s_fp8 import group_linear_into
+
+    dev = torch.device("cuda", 0)
+    layers, inputs = build_workload(torch, dev)
+    order = [(m, p, n) for m in M_SWEEP for p, n, _ in PROJECTIONS]
+    xs = [inputs[m][p].to(dev) for m, p, _ in order]
+    ws = [layers[m][p] for m, p, _ in order]
+    outs = [torch.empty((m, n), dtype=torch.bfloat16, device=dev) for m, _, n in order]
+    for _ in range(4):
+        group_linear_into(xs, ws, outs)
+    torch.cuda.synchronize()
+    print(f"group profile: {len(order)} linears per launch: ok")
+
+
 TP70B = (  # name, N, K, split (Llama-3-70B)
     ("qkv", 10240, 8192, "column"),
     ("o", 8192, 8192, "row"),
@@ -459,10 +477,15 @@ def main() -> None:
                     help="with --single: MXFP8 activations quantized beforehand (mambo_iq3s_linear)")
     ap.add_argument("--workload", choices=("decode", "tp70b"), default="decode",
                     help="tp70b: Llama-3-70B linears tensor-parallel over the launched ranks (its own JSON line)")
+    ap.add_argument("--group-profile", action="store_true",
+                    help="profiling mode: four grouped launches of the decode sweep, then exit")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.single:
         run_single(args)
+        return
+    if args.group_profile:
+        run_group_profile()
         return
     if args.workload == "tp70b" and args.impl == "mambo":
         run_tp70b(args)
@@ -475,7 +498,7 @@ def main() -> None:
     import torch
     import torch.distributed as dist
 
-    from mambo_b200.kernels.iq3_s_fp8 import fused_linear_into, select_config
+    from mambo_b200.kernels.iq3_s_fp8 import fused_linear_into, group_linear_into, select_config
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -488,27 +511,38 @@ def main() -> None:
     layers, inputs = build_workload(torch, dev)
     stream = torch.cuda.Stream(dev)
 
-    # device buffers
-    xs_dev = {m: {p: inputs[m][p].to(dev) for p in inputs[m]} for m in M_SWEEP}
-    out_buf = {m: {p: torch.empty((m, n), dtype=torch.bfloat16, device=dev) for p, n, _ in PROJECTIONS}
-               for m in M_SWEEP}
-    configs = {m: {p: select_config(m, n, k, dev) for p, n, k in PROJECTIONS} for m in M_SWEEP}
+    # device buffers, in sweep order (M, projection)
+    order = [(m, p, n, k) for m in M_SWEEP for p, n, k in PROJECTIONS]
+    xs_dev = {(m, p): inputs[m][p].to(dev) for m, p, _, _ in order}
+    out_buf = {(m, p): torch.empty((m, n), dtype=torch.bfloat16, device=dev) for m, p, n, _ in order}
+    configs = {(m, p): select_config(m, n, k, dev) for m, p, n, k in order}
+    g_x = [xs_dev[(m, p)] for m, p, _, _ in order]
+    g_w = [layers[m][p] for m, p, _, _ in order]
+    g_o = [out_buf[(m, p)] for m, p, _, _ in order]
 
-    def step_ops(x_src):
+    def group_step():
+        # the whole sweep (20 independent linears) as one grouped GEMV launch
+        group_linear_into(g_x, g_w, g_o)
+
+    def per_linear_step():
         # one launch per linear: the decode GEMV quantizes its bf16 activations itself
-        for m in M_SWEEP:
-            for p, n, k in PROJECTIONS:
-                fused_linear_into(x_src[m][p], layers[m][p], out_buf[m][p], config=configs[m][p])
+        for m, p, _, _ in order:
+            fused_linear_into(xs_dev[(m, p)], layers[m][p], out_buf[(m, p)], config=configs[(m, p)])
 
-    # warm up eagerly (allocates the workspace), then capture one step
-    with torch.cuda.stream(stream):
-        for _ in range(2):
-            step_ops(xs_dev)
-    torch.cuda.synchronize(dev)
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
-        step_ops(xs_dev)
-    torch.cuda.synchronize(dev)
+    def capture(fn, copies: int = 1):
+        with torch.cuda.stream(stream):
+            for _ in range(2):
+                fn()  # eager warm-up (allocates the workspace)
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for _ in range(copies):
+                fn()
+        torch.cuda.synchronize(dev)
+        return g
+
+    graph = capture(group_step)
+    graph_sep = capture(per_linear_step)
 
     def barrier():
         if world > 1:
@@ -521,11 +555,24 @@ def main() -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    # ---- timed region: K graph replays of the step -------------------------
-    for _ in range(args.warmup):
-        graph.replay()
+    def time_replays(g, steps: int) -> float:
+        """ms per replay of g over `steps` replays, CUDA events on the launching stream."""
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        with torch.cuda.stream(stream):
+            for _ in range(steps):
+                g.replay()
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+        return t0.elapsed_time(t1) / steps
+
+    # ---- timed region: K graph replays of the step (one grouped launch) ----
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            graph.replay()
     torch.cuda.synchronize(dev)
     barrier()
+
     def keep_busy(seconds: float) -> None:
         # Back-to-back replays around the timed region so that the clock samples
         # (every 50 ms) see the GPU under the same load; not timed.
@@ -539,60 +586,56 @@ def main() -> None:
     with ClockSampler(local) as clocks:
         keep_busy(0.5)
         barrier()
-        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        t0.record(stream)
-        with torch.cuda.stream(stream):
-            for _ in range(args.steps):
-                graph.replay()
-        t1.record(stream)
-        torch.cuda.synchronize(dev)
+        step_ms = time_replays(graph, args.steps)
         keep_busy(0.5)
         barrier()
-    ms_per_step = max_over_ranks(t0.elapsed_time(t1) / args.steps)
+    ms_per_step = max_over_ranks(step_ms)
     clock = clocks.summary()
     w_bytes, in_bytes, out_bytes = step_bytes()
     alg = w_bytes + in_bytes + out_bytes
     value = alg * world / (ms_per_step * 1e-3) / 1e9
 
-    # ---- roofline of the GEMV kernel: per-launch CUDA-event durations ------
-    # Each linear is timed as LAUNCHES back-to-back launches inside one graph,
-    # the way the kernels run in the step: separately launched work (a stream
-    # launch, or a graph of one kernel) starts on a ~2 us grid on this GPU,
-    # which would round each launch up.
-    per_launch = []
+    # ---- the same sweep as 20 separate launches (one per linear) -----------
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            graph_sep.replay()
+    torch.cuda.synchronize(dev)
+    barrier()
+    sep_ms = max_over_ranks(time_replays(graph_sep, args.steps))
+
+    # ---- roofline: the grouped launch, and every linear launched alone ------
+    # Kernels are timed as back-to-back launches inside one graph, the way
+    # they run in the step: separately launched work (a stream launch, or a
+    # graph of one kernel) starts on a ~2 us grid on this GPU, which would
+    # round each launch up.
     launches = 10
-    for m in M_SWEEP:
-        for p, n, k in PROJECTIONS:
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=stream):
-                for _ in range(launches):
-                    fused_linear_into(xs_dev[m][p], layers[m][p], out_buf[m][p], config=configs[m][p])
-            reps = 10
-            with torch.cuda.stream(stream):
-                for _ in range(3):
-                    g.replay()
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record(stream)
-                for _ in range(reps):
-                    g.replay()
-                e1.record(stream)
-            torch.cuda.synchronize(dev)
-            us = e0.elapsed_time(e1) * 1000 / (reps * launches)
-            b = n * (k // 256) * 110 + m * k * 2 + m * n * 2
-            per_launch.append({"m": m, "proj": p, "us": round(us, 3), "bytes": b, "gbs": round(b / us / 1e3, 1)})
-            del g
+    g10 = capture(group_step, copies=launches)
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            g10.replay()
+    group_us = time_replays(g10, 5) * 1000 / launches
+    del g10
+    per_launch = []
+    for m, p, n, k in order:
+        g = capture(lambda: fused_linear_into(xs_dev[(m, p)], layers[m][p], out_buf[(m, p)], config=configs[(m, p)]),
+                    copies=launches)
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                g.replay()
+        us = time_replays(g, 10) * 1000 / launches
+        b = n * (k // 256) * 110 + m * k * 2 + m * n * 2
+        per_launch.append({"m": m, "proj": p, "us": round(us, 3), "bytes": b, "gbs": round(b / us / 1e3, 1)})
+        del g
     peak, peak_kind = load_peaks()
-    tot_b = sum(r["bytes"] for r in per_launch)
-    tot_us = sum(r["us"] for r in per_launch)
-    achieved = tot_b / tot_us / 1e3
-    traffic = read_profiled_traffic()
+    achieved = alg / group_us / 1e3
+    sep_achieved = sum(r["bytes"] for r in per_launch) / sum(r["us"] for r in per_launch) / 1e3
+    traffic = read_profiled_traffic("dram_bytes_per_group_launch")
 
     # ---- e2e: public API with pinned host buffers, H2D + D2H in the region --
-    from mambo_b200.kernels.iq3_s_fp8 import iq3_s_fp8_linear
-
     # One pinned buffer holds every input of a step and one holds every output:
-    # one H2D copy in, one D2H copy out per step (the linears run in between).
-    order = [(m, p, n, k) for m in M_SWEEP for p, n, k in PROJECTIONS]
+    # one H2D copy in, one D2H copy out per step, and in between one public
+    # call (group_linear_into) that writes each linear's output into its view
+    # of the device output buffer.
     host_in_all = torch.cat([inputs[m][p].reshape(-1) for m, p, _, _ in order]).pin_memory()
     host_out_all = torch.empty(sum(m * n for m, _, n, _ in order), dtype=torch.bfloat16).pin_memory()
     dev_in_all = torch.empty_like(host_in_all, device=dev)
@@ -603,34 +646,24 @@ def main() -> None:
         host_out[(m, p)] = host_out_all[off_o:off_o + m * n].view(m, n)
         off_i += m * k
         off_o += m * n
+    e2e_x = [dev_in[(m, p)] for m, p, _, _ in order]
+    e2e_o, off_o = [], 0
+    for m, _, n, _ in order:
+        e2e_o.append(dev_out_all[off_o:off_o + m * n].view(m, n))
+        off_o += m * n
 
     def e2e_step():
         dev_in_all.copy_(host_in_all, non_blocking=True)
-        ys = [iq3_s_fp8_linear(dev_in[(m, p)], layers[m][p], config=configs[m][p]) for m, p, _, _ in order]
-        torch.cat([y.reshape(-1) for y in ys], out=dev_out_all)
+        group_linear_into(e2e_x, g_w, e2e_o)
         host_out_all.copy_(dev_out_all, non_blocking=True)
 
-    with torch.cuda.stream(stream):
-        for _ in range(2):
-            e2e_step()
-    torch.cuda.synchronize(dev)
-    g_e2e = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g_e2e, stream=stream):
-        e2e_step()
+    g_e2e = capture(e2e_step)
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
             g_e2e.replay()
     torch.cuda.synchronize(dev)
     barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    with torch.cuda.stream(stream):
-        for _ in range(args.steps):
-            g_e2e.replay()
-    e1.record(stream)
-    torch.cuda.synchronize(dev)
-    barrier()
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    e2e_ms = max_over_ranks(time_replays(g_e2e, args.steps))
     # eager (no graph) for reference
     torch.cuda.synchronize(dev)
     t_e = time.perf_counter()
@@ -640,10 +673,13 @@ def main() -> None:
     torch.cuda.synchronize(dev)
     eager_ms = (time.perf_counter() - t_e) * 1000 / max(3, args.steps // 5)
     # correctness spot check of the e2e output against the device path
-    ok = all(torch.equal(host_out[(m, p)], out_buf[m][p].cpu()) for m, p, _, _ in order)
+    with torch.cuda.stream(stream):
+        graph.replay()
+    torch.cuda.synchronize(dev)
+    ok = all(torch.equal(host_out[(m, p)], out_buf[(m, p)].cpu()) for m, p, _, _ in order)
 
     if world > 1:
-        del graph, g_e2e
+        del graph, graph_sep, g_e2e
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
@@ -667,22 +703,31 @@ def main() -> None:
         "config": {"workload": "decode_gemv_sweep_llama3_8b (BASELINE config 2)", "m_sweep": list(M_SWEEP),
                    "projections": {p: [n, k] for p, n, k in PROJECTIONS},
                    "bytes_per_step": {"weights": w_bytes, "act_in_bf16": in_bytes, "out_bf16": out_bytes},
-                   "l2": "inputs larger than L2 (375 MB of weights per step)", "execution": "cuda graph replay",
+                   "l2": "inputs larger than L2 (375 MB of weights per step)",
+                   "execution": "cuda graph replay; the step's 20 independent linears in one grouped GEMV launch "
+                                "(mambo_iq3s_linear_group)",
                    "parallelism": f"replicas{world}"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": traffic, "peak_kind": peak_kind,
-                     "kernel": "iq3s_gemv_tm_kernel with fused MXFP8 quantization (one launch per linear, "
-                               "CUDA-graph replay)",
-                     "timing": "per linear: 10 back-to-back launches in one CUDA graph, 10 replays, mean",
-                     "per_launch": per_launch},
+                     "kernel": "iq3s_gemv_tm_kernel<1,8,GemvGroup>: the 20 linears of a step in one launch, "
+                               "MXFP8 quantization fused",
+                     "launch_us": group_us,
+                     "timing": "10 back-to-back launches in one CUDA graph, 5 replays, mean"},
+        # Every linear launched on its own (the reference's one-linear-per-call shape).
+        "per_linear": {"value": alg * world / (sep_ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": sep_ms,
+                       "gpu_launches_per_step": len(order), "kernel_achieved": sep_achieved,
+                       "kernel_frac": sep_achieved / peak,
+                       "timing": "per linear: 10 back-to-back launches in one CUDA graph, 10 replays, mean",
+                       "per_launch": per_launch},
         "e2e": {"value": alg * world / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
                 "h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": out_bytes,
                 "ms_per_step": e2e_ms,
-                "execution": "cuda graph per step: one H2D copy of all inputs, 20 public-API calls "
-                             "(iq3_s_fp8_linear), one D2H copy of all outputs",
+                "execution": "cuda graph per step: one H2D copy of all inputs, one public-API call "
+                             "(group_linear_into, 20 linears into views of one output buffer), one D2H copy of "
+                             "all outputs",
                 "eager_ms_per_step": eager_ms, "matches_device_path": ok},
-        # per linear: one IQ3_S GEMV with the MXFP8 quantization fused in
-        "gpu_launches": args.steps * len(M_SWEEP) * len(PROJECTIONS),
+        # one grouped GEMV launch per step
+        "gpu_launches": args.steps,
         "clocks": clock,
         "cpu_baseline": cpu,
         # BASELINE config 3 (prefill GEMM) at M=2048, for the TFLOP/s half of the metric
