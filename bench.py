@@ -342,6 +342,114 @@ def run_group_profile() -> None:
     print(f"group profile: {len(order)} linears per launch: ok")
 
 
+LLAMA3_8B_LAYERS = 32
+
+
+def run_llama3_8b(args) -> None:
+    """every linear of a 32-layer Llama-3-8B-shaped model (random IQ3_S
+    weights): one 4096-token prefill, then 128 decode steps at batch 8; linear time only.
+
+    A layer is QKV, O, gate, up, down. Decode keeps a model's dependency order:
+    per layer QKV, then O, then gate and up together (one grouped launch: they
+    read the same input), then down, each a launch in one CUDA graph per step.
+    Prefill runs each linear through the fused entry point (MXFP8 quantization,
+    then the FP16-operand GEMM). Activations are fixed random bf16 buffers of
+    each linear's shape (no attention or MLP math in between).
+    """
+    import torch
+
+    from mambo_b200.kernels.iq3_s_fp8 import fused_linear_into, group_linear_into
+    from mambo_b200.utils.iq3_s_weight import prepare_iq3_s_fields
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    prefill_m, decode_m, decode_steps = 4096, 8, 128
+    layers = []
+    for li in range(LLAMA3_8B_LAYERS):
+        projs = {}
+        for pi, (name, n, k) in enumerate(PROJECTIONS):
+            gen = torch.Generator(device=dev).manual_seed(0x1A3 + 7919 * li + pi)
+            raw = torch.randint(0, 256, (n, k // 256, 110), dtype=torch.uint8, device=dev, generator=gen)
+            d = (torch.rand((n, k // 256), device=dev, generator=gen) * 9e-3 + 1e-3).half()
+            raw[..., :2] = d.view(torch.uint8).view(n, k // 256, 2)
+            projs[name] = prepare_iq3_s_fields(raw)
+            del raw
+        layers.append(projs)
+    gen = torch.Generator(device=dev).manual_seed(20261017)
+    shapes = {name: (n, k) for name, n, k in PROJECTIONS}
+
+    def buffers(m):
+        x = {name: torch.randn((m, k), device=dev, generator=gen).to(torch.bfloat16) for name, (n, k) in shapes.items()}
+        y = {name: torch.empty((m, n), device=dev, dtype=torch.bfloat16) for name, (n, k) in shapes.items()}
+        return x, y
+
+    xp, yp = buffers(prefill_m)
+    xd, yd = buffers(decode_m)
+    stream = torch.cuda.Stream(dev)
+
+    def prefill():
+        for w in layers:
+            for name in shapes:
+                fused_linear_into(xp[name], w[name], yp[name])
+
+    def decode_step():
+        for w in layers:
+            fused_linear_into(xd["qkv"], w["qkv"], yd["qkv"])
+            fused_linear_into(xd["o"], w["o"], yd["o"])
+            group_linear_into([xd["gate"], xd["up"]], [w["gate"], w["up"]], [yd["gate"], yd["up"]])
+            fused_linear_into(xd["down"], w["down"], yd["down"])
+
+    def capture(fn):
+        with torch.cuda.stream(stream):
+            fn()
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            fn()
+        torch.cuda.synchronize(dev)
+        return g
+
+    g_prefill, g_decode = capture(prefill), capture(decode_step)
+
+    def timed(g, reps):
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                g.replay()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        with torch.cuda.stream(stream):
+            for _ in range(reps):
+                g.replay()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / reps
+
+    with ClockSampler(0) as clocks:
+        prefill_ms = timed(g_prefill, 3)
+        decode_ms = timed(g_decode, decode_steps)
+    w_bytes = layer_bytes() * LLAMA3_8B_LAYERS
+    flops = 2.0 * prefill_m * sum(n * k for _, n, k in PROJECTIONS) * LLAMA3_8B_LAYERS
+    dec_bytes = w_bytes + LLAMA3_8B_LAYERS * sum(decode_m * (k + n) * 2 for _, n, k in PROJECTIONS)
+    peak, peak_kind = load_peaks()
+    total_ms = prefill_ms + decode_steps * decode_ms
+    print(json.dumps({
+        "metric": "Llama-3-8B linear layers (32 layers): 4096-token prefill + 128 decode steps at batch 8, linear time",
+        "value": total_ms, "unit": "ms", "n_gpus": 1, "higher_is_better": False, "dtype": "e4m3",
+        "data": "synthetic (random IQ3_S weights, bf16 N(0,1) activations)",
+        "config": {"workload": "llama3_8b_linears (BASELINE config 4)", "layers": LLAMA3_8B_LAYERS,
+                   "prefill_tokens": prefill_m, "decode_batch": decode_m, "decode_steps": decode_steps,
+                   "weights_bytes": w_bytes,
+                   "decode_step": "per layer: QKV, O, grouped gate+up, down (4 launches), one CUDA graph per step",
+                   "prefill": "per linear: fused MXFP8 quantization + FP16-operand GEMM, one CUDA graph"},
+        "prefill": {"ms": prefill_ms, "tflops": flops / (prefill_ms * 1e-3) / 1e12},
+        "decode": {"ms_per_step": decode_ms, "gbs": dec_bytes / (decode_ms * 1e-3) / 1e9,
+                   "hbm_frac": dec_bytes / (decode_ms * 1e-3) / 1e9 / peak, "peak_gbs": peak, "peak_kind": peak_kind,
+                   "launches_per_step": 4 * LLAMA3_8B_LAYERS},
+        "clocks": clocks.summary(),
+    }), flush=True)
+
+
 TP70B = (  # name, N, K, split (Llama-3-70B)
     ("qkv", 10240, 8192, "column"),
     ("o", 8192, 8192, "row"),
@@ -475,8 +583,9 @@ def main() -> None:
     ap.add_argument("--kernel", type=int, default=None, help="with --single: MAMBO_KERNEL_* to use")
     ap.add_argument("--prequantized", action="store_true",
                     help="with --single: MXFP8 activations quantized beforehand (mambo_iq3s_linear)")
-    ap.add_argument("--workload", choices=("decode", "tp70b"), default="decode",
-                    help="tp70b: Llama-3-70B linears tensor-parallel over the launched ranks (its own JSON line)")
+    ap.add_argument("--workload", choices=("decode", "tp70b", "llama3_8b"), default="decode",
+                    help="tp70b: Llama-3-70B linears tensor-parallel over the launched ranks; llama3_8b: every "
+                         "linear of a 32-layer Llama-3-8B, prefill + 128 decode steps (each its own JSON line)")
     ap.add_argument("--group-profile", action="store_true",
                     help="profiling mode: four grouped launches of the decode sweep, then exit")
     args = ap.parse_args()
@@ -489,6 +598,9 @@ def main() -> None:
         return
     if args.workload == "tp70b" and args.impl == "mambo":
         run_tp70b(args)
+        return
+    if args.workload == "llama3_8b" and args.impl == "mambo":
+        run_llama3_8b(args)
         return
 
     if args.impl == "reference":
