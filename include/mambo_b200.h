@@ -91,13 +91,16 @@ typedef struct MamboLinearConfig {
  * GEMM_F16 = the large-M tcgen05 kernel with FP16 operands: the group scale
  * (1+2*nibble) folded exactly into the weight operand and one FP32 accumulator
  * per 256-wide K block; activations enter as FP16 relative to each token's
- * largest scale (exact unless a group's scale is more than 2^12 below it). */
+ * largest scale (exact unless a group's scale is more than 2^12 below it).
+ * MAMBO_KERNEL_GEMM_F16_PAIR: the same arithmetic on clusters of two CTAs
+ * whose tensor cores share each activation tile (256 weight rows per tile). */
 enum {
   MAMBO_KERNEL_AUTO = 0,
   MAMBO_KERNEL_GEMV = 1,
   MAMBO_KERNEL_GEMM = 2,
   MAMBO_KERNEL_GEMV_SYNC = 3,
-  MAMBO_KERNEL_GEMM_F16 = 4
+  MAMBO_KERNEL_GEMM_F16 = 4,
+  MAMBO_KERNEL_GEMM_F16_PAIR = 5
 };
 
 /* Library version string. */

@@ -32,6 +32,7 @@ MAMBO_KERNEL_GEMV = 1
 MAMBO_KERNEL_GEMM = 2
 MAMBO_KERNEL_GEMV_SYNC = 3
 MAMBO_KERNEL_GEMM_F16 = 4
+MAMBO_KERNEL_GEMM_F16_PAIR = 5
 
 # Every symbol include/mambo_b200.h declares.
 EXPORTED_SYMBOLS = (

@@ -159,13 +159,16 @@ int gemv_nt_for(int64_t m) { return m <= 8 ? 1 : (m <= 16 ? 2 : 4); }
 constexpr int kSmemOptinDefault = 232448;
 
 int kernel_of(const MamboLinearConfig& c) { return c.kernel == MAMBO_KERNEL_AUTO ? MAMBO_KERNEL_GEMV : c.kernel; }
+// The FP16-operand GEMM, on single CTAs or on CTA pairs.
+bool is_gemm_f16(int kind) { return kind == MAMBO_KERNEL_GEMM_F16 || kind == MAMBO_KERNEL_GEMM_F16_PAIR; }
+bool is_gemm(int kind) { return kind == MAMBO_KERNEL_GEMM || is_gemm_f16(kind); }
 
 // Shared memory of a configuration (for MAMBO_KERNEL_GEMV without the cluster
 // partials, which the plan sizes to what is left).
 uint32_t config_smem(const MamboLinearConfig& c, int nt, int64_t b) {
   if (kernel_of(c) == MAMBO_KERNEL_GEMV_SYNC) return gemv_smem_bytes_host(c.warps * 16, nt, c.stages, (int)b);
   if (kernel_of(c) == MAMBO_KERNEL_GEMM) return gemm_tm_smem_bytes(c.stages);
-  if (kernel_of(c) == MAMBO_KERNEL_GEMM_F16) return gemm_f16_smem_bytes(c.stages);
+  if (is_gemm_f16(kernel_of(c))) return gemm_f16_smem_bytes(c.stages);
   return gemv_tm_smem_bytes(nt, c.stages, 1);
 }
 
@@ -200,10 +203,9 @@ void default_config(int64_t m, int64_t n, int64_t b, MamboLinearConfig* cfg, int
 
 int validate_config(const MamboLinearConfig* cfg, int64_t m, int64_t b, const DeviceInfo& info) {
   const int kind = kernel_of(*cfg);
-  if (kind != MAMBO_KERNEL_GEMV && kind != MAMBO_KERNEL_GEMV_SYNC && kind != MAMBO_KERNEL_GEMM &&
-      kind != MAMBO_KERNEL_GEMM_F16)
+  if (kind != MAMBO_KERNEL_GEMV && kind != MAMBO_KERNEL_GEMV_SYNC && !is_gemm(kind))
     return fail(MAMBO_EINVAL, "unknown kernel kind %d", cfg->kernel);
-  if (kind == MAMBO_KERNEL_GEMM || kind == MAMBO_KERNEL_GEMM_F16) {
+  if (is_gemm(kind)) {
     const int smax = kind == MAMBO_KERNEL_GEMM ? gemm_tm_max_wstages() : gemm_f16_max_wstages();
     if (cfg->stages < 2 || cfg->stages > smax) return fail(MAMBO_EINVAL, "stages must be in [2, %d]", smax);
   } else if (kind == MAMBO_KERNEL_GEMV_SYNC) {
@@ -262,8 +264,10 @@ size_t gemm_workspace_bytes(int64_t m, int64_t b) {
 
 // The FP16 GEMM's workspace: the split-K counters (left zero for the GEMV),
 // the FP16 activations [m][K] and the per-token scales.
+// Counters, the FP16 activations [m][K], the tokens' scales (padded to whole
+// 128-token tiles: the epilogue reads them 16 at a time).
 size_t gemm_f16_workspace_bytes(int64_t m, int64_t b) {
-  return kCounterBytes + align256((size_t)m * (size_t)b * 256 * 2) + align256((size_t)m * 4);
+  return kCounterBytes + align256((size_t)m * (size_t)b * 256 * 2) + align256((size_t)((m + 127) / 128 * 128) * 4);
 }
 
 // The GEMM reads activations through a TMA map (16-byte aligned rows) and
@@ -356,9 +360,11 @@ int launch_gemm_f16_path(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int
   float* tok_scale = (float*)((uint8_t*)x16 + align256((size_t)m * k * 2));
   cudaError_t e = launch_x16(xq, ldxq, xs, ldxs, (int)m, k, x16, k, tok_scale, stream);
   if (e != cudaSuccess) return cuda_fail(e, "iq3s_x16");
+  const bool pair = c.kernel == MAMBO_KERNEL_GEMM_F16_PAIR;
   GemmF16Maps maps;
   std::memset(&maps, 0, sizeof(maps));
-  if (!make_gemm_x16_map(x16, k, (int)m, k, &maps.x16))
+  // A CTA of a pair loads 64 of the tile's 128 tokens.
+  if (!make_gemm_x16_map(x16, k, (int)m, k, pair ? 64 : 128, &maps.x16))
     return fail(MAMBO_ECUDA, "could not encode the FP16 activation tensor map");
   GemmF16Params p{};
   p.m = (int)m;
@@ -373,6 +379,15 @@ int launch_gemm_f16_path(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int
   p.wstages = c.stages;
   p.row_tiles = (int)((w->n_rows + 127) / 128);
   p.tok_tiles = (int)((m + 127) / 128);
+  if (pair) {
+    const int64_t tiles = (int64_t)((p.row_tiles + 1) / 2) * p.tok_tiles;
+    int clusters = gemm_f16_pair_max_clusters(c.stages);
+    if (clusters < 1) return fail(MAMBO_EINVAL, "no CTA pair of this configuration fits on the device");
+    if (tiles < clusters) clusters = (int)tiles;
+    e = launch_gemm_f16_pair(p, maps, clusters, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "iq3s_gemm_f16 (pairs)");
+    return ok();
+  }
   const int64_t tiles = (int64_t)p.row_tiles * p.tok_tiles;
   const int grid = (int)(tiles < info.sms ? tiles : info.sms);
   e = launch_gemm_f16(p, maps, grid, stream);
@@ -583,7 +598,7 @@ int mambo_default_config(int64_t m, int64_t n_rows, int64_t n_blocks, MamboLinea
 
 int mambo_num_configs(int kernel) {
   if (kernel == MAMBO_KERNEL_GEMV || kernel == MAMBO_KERNEL_AUTO) return kNumTcConfigs;
-  if (kernel == MAMBO_KERNEL_GEMM || kernel == MAMBO_KERNEL_GEMM_F16) return kNumGemmConfigs;
+  if (is_gemm(kernel)) return kNumGemmConfigs;
   if (kernel == MAMBO_KERNEL_GEMV_SYNC) return kNumSyncConfigs;
   return 0;
 }
@@ -597,7 +612,7 @@ int mambo_config_at(int kernel, int index, MamboLinearConfig* cfg) {
   cfg->kernel = kernel;
   cfg->ctas_per_sm = 1;
   cfg->split = index % 2;
-  if (kernel == MAMBO_KERNEL_GEMM || kernel == MAMBO_KERNEL_GEMM_F16) {
+  if (is_gemm(kernel)) {
     cfg->split = 0;
     cfg->warps = 8;
     cfg->stages = kGemmStages[index];
@@ -631,13 +646,13 @@ size_t mambo_iq3s_linear_workspace_bytes(int64_t m, int64_t n_rows, int64_t n_bl
   // A GEMM call may fall back to the GEMV (unaligned activations, no packed
   // weight copy): room for both.
   MamboLinearConfig cv = c;
-  if (kernel_of(c) == MAMBO_KERNEL_GEMM || kernel_of(c) == MAMBO_KERNEL_GEMM_F16)
+  if (is_gemm(kernel_of(c)))
     default_config(m < 32 ? m : 31, n_rows, n_blocks, &cv, smem_optin, sms);
   const int64_t m_chunk = m < 32 ? m : 32;
   GemvPlan P = plan_gemv(m_chunk, n_rows, n_blocks, cv, sms, smem_optin);
   const size_t gemv = P.counters_bytes + P.partial_bytes + P.xcopy_bytes + P.xscopy_bytes;
   const size_t gemm = kernel_of(c) == MAMBO_KERNEL_GEMM       ? gemm_workspace_bytes(m, n_blocks)
-                     : kernel_of(c) == MAMBO_KERNEL_GEMM_F16 ? gemm_f16_workspace_bytes(m, n_blocks)
+                     : is_gemm_f16(kernel_of(c))              ? gemm_f16_workspace_bytes(m, n_blocks)
                                                              : 0;
   return gemv > gemm ? gemv : gemm;
 }
@@ -667,17 +682,17 @@ int mambo_iq3s_linear(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_
     c.kernel = a.kernel;
     if (c.stages == 0) c.stages = a.stages;
   }
-  if (c.kernel == MAMBO_KERNEL_GEMM || c.kernel == MAMBO_KERNEL_GEMM_F16) {
+  if (is_gemm(c.kernel)) {
     if (gemm_usable(w, xq, ldxq, m)) {
       st = validate_config(&c, 32, w->n_blocks, info);
       if (st != MAMBO_OK) return st;
-      if (c.kernel == MAMBO_KERNEL_GEMM_F16)
+      if (is_gemm_f16(c.kernel))
         return launch_gemm_f16_path(xq, ldxq, xs, ldxs, m, w, fp8_table, out, out_dtype, ldo, c, info, workspace,
                                     workspace_bytes, (cudaStream_t)stream);
       return launch_gemm(xq, ldxq, xs, ldxs, m, w, fp8_table, out, out_dtype, ldo, c, info, workspace,
                          workspace_bytes, (cudaStream_t)stream);
     }
-    if (cfg && (cfg->kernel == MAMBO_KERNEL_GEMM || cfg->kernel == MAMBO_KERNEL_GEMM_F16))
+    if (cfg && is_gemm(cfg->kernel))
       return fail(MAMBO_EINVAL,
                   "the GEMM needs the tile-major packed weight copy (N %% 8 == 0) and 16-byte aligned activation rows");
     // Otherwise the GEMV in 32-token chunks.

@@ -199,6 +199,18 @@ __device__ __forceinline__ uint64_t l2_policy_evict_last() {
   return pol;
 }
 
+// As tma_load_2d for a CTA of a pair: the bytes land in this CTA's shared
+// memory at dst and complete on the barrier at cluster address bar, which may
+// be the other CTA's (no multicast).
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int32_t c0, int32_t c1,
+                                                 uint32_t bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar), "l"(policy)
+      : "memory");
+}
+
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int32_t c0, int32_t c1, uint32_t bar,
                                             uint64_t policy) {
   asm volatile(

@@ -37,9 +37,13 @@ constexpr int kRowsH = 128, kTokH = 128;
 constexpr int kDecWarpsH = 8, kEpiWarpsH = 8;
 constexpr int kARingH = 2;   // decoded A blocks in TMEM (128 columns each)
 constexpr int kDRingH = 2;   // D buffers (128 columns each)
-constexpr int kXStagesH = 3;  // FP16 activation half-blocks (128 tokens x 128 K)
+// FP16 activation half-blocks (the CTA's tokens x 128 K) in flight: 3 of 32 KB
+// for a single CTA (128 tokens), 6 of 16 KB for a CTA of a pair (64 tokens).
+constexpr int kXStagesMaxH = 6;
 constexpr int kMaxWStagesH = 6;
-constexpr uint32_t kXHalfBytes = kTokH * 128u * 2u;  // 32 KB
+constexpr uint32_t kXRingBytesH = 3u * kTokH * 128u * 2u;  // 96 KB either way
+__host__ __device__ constexpr int x_stages_h(bool pair) { return pair ? 6 : 3; }
+__host__ __device__ constexpr uint32_t x_half_bytes_h(bool pair) { return (pair ? 64u : 128u) * 256u; }
 // Rows' d of a block, in a ring of 4 with its own barriers (dfull, count 4:
 // the part-0 decoder warps). The decoders write slot it % 4 after the MMAs of
 // block it - 2 completed, which waited for the epilogue to release block
@@ -52,12 +56,14 @@ constexpr uint32_t kTmA = 0, kTmD = 128u * kARingH;
 constexpr uint32_t kTmColsH = 512;
 static_assert(kTmD + kDRingH * (uint32_t)kTokH <= kTmColsH, "TMEM plan exceeds 512 columns");
 constexpr int kThreadsH = (3 + kDecWarpsH + kEpiWarpsH) * 32;
+static_assert(2 * (kMaxWStagesH + kXStagesMaxH + kARingH + kDRingH) + 1 + kAuxRingH + 1 <= (int)(kBarBytesH / 8),
+              "barrier area");
 constexpr int kEpiWarp0H = 2 + kDecWarpsH, kXWarpH = kEpiWarp0H + kEpiWarpsH;
 
 __host__ __device__ constexpr uint32_t align_up_h(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
 __host__ __device__ inline uint32_t gemm_f16_smem(int wstages) {
-  return tm::kTableBytes + 1024 + align_up_h((uint32_t)wstages * tm::kRecordBytes, 1024) + kXStagesH * kXHalfBytes +
+  return tm::kTableBytes + 1024 + align_up_h((uint32_t)wstages * tm::kRecordBytes, 1024) + kXRingBytesH +
          kAuxRingH * kAuxH + tm::kTableStageBytes + kBarBytesH;
 }
 
@@ -87,35 +93,57 @@ __device__ __forceinline__ void store_out_h(const GemmF16Params& p, int row, int
 
 }  // namespace
 
+// kPair: tiles of 256 weight rows x 128 tokens on a cluster of two CTAs. Each
+// CTA decodes its 128 rows into its own TMEM and loads its 64 tokens of every
+// activation half-block; rank 0 issues M=256 MMAs over both (one activation
+// tile serves 256 weight rows: half the L2 traffic per FLOP) and its commits
+// arrive in both CTAs; rank 1's decoders and epilogue arrive on rank 0's
+// barriers. Otherwise 128 x 128 tiles on single CTAs.
+template <bool kPair>
 __global__ void __launch_bounds__(kThreadsH, 1)
     iq3s_gemm_f16_kernel(const __grid_constant__ GemmF16Params p, const __grid_constant__ GemmF16Maps maps) {
-  // B half-block (128 tokens x 128 K): two [128 tokens][128 bytes] boxes in
+  // B half-block (the CTA's tokens x 128 K): two [tokens][128 bytes] boxes in
   // the 128-byte-swizzled K-major layout (8-row atoms 1024 bytes apart); an
   // MMA's 16 K (32 bytes) start 32 bytes further into the row.
-  constexpr uint32_t kBoxBytes = kTokH * 128u;
-  constexpr uint32_t kIdesc = tc::idesc_f16_f32(kRowsH, kTokH);
+  constexpr int kTokLoad = kPair ? 64 : kTokH;
+  constexpr int kXS = x_stages_h(kPair);
+  constexpr uint32_t kXHalf = x_half_bytes_h(kPair);
+  constexpr uint32_t kBoxBytes = kTokLoad * 128u;
+  constexpr uint32_t kIdesc = tc::idesc_f16_f32(kPair ? 2 * kRowsH : kRowsH, kTokH);
+  constexpr uint16_t kBoth = 0x3;  // CTA mask of a pair
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* table = smem_raw;
   uint8_t* st0 = smem_raw + tm::kTableBytes + ((1024u - ((smem_u32(smem_raw) + tm::kTableBytes) & 1023u)) & 1023u);
   const int SW = p.wstages;
   uint8_t* x0 = st0 + align_up_h((uint32_t)SW * tm::kRecordBytes, 1024);
-  uint8_t* aux0 = x0 + (size_t)kXStagesH * kXHalfBytes;
+  uint8_t* aux0 = x0 + (size_t)kXRingBytesH;
   uint32_t* tstage = reinterpret_cast<uint32_t*>(aux0 + kAuxRingH * kAuxH);
   uint64_t* bars = reinterpret_cast<uint64_t*>(aux0 + kAuxRingH * kAuxH + tm::kTableStageBytes);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kMaxWStagesH + 2 * kXStagesH + 2 * kARingH +
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kMaxWStagesH + 2 * kXStagesMaxH + 2 * kARingH +
                                                     2 * kDRingH + 1 + kAuxRingH);
   const uint32_t bar0 = smem_u32(bars);
   // Barriers as in the FP8 GEMM, with activation slots per half block.
   const uint32_t kWfull = bar0, kWempty = bar0 + 8 * kMaxWStagesH;
-  const uint32_t kXfull = bar0 + 16 * kMaxWStagesH, kXempty = kXfull + 8 * kXStagesH;
-  const uint32_t kAfull = kXempty + 8 * kXStagesH, kAempty = kAfull + 8 * kARingH;
+  const uint32_t kXfull = bar0 + 16 * kMaxWStagesH, kXempty = kXfull + 8 * kXStagesMaxH;
+  const uint32_t kAfull = kXempty + 8 * kXStagesMaxH, kAempty = kAfull + 8 * kARingH;
   const uint32_t kMdone = kAempty + 8 * kARingH, kEfree = kMdone + 8 * kDRingH;
   const uint32_t kEdone = kEfree + 8 * kDRingH, kDfull = kEdone + 8;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nb = p.n_blocks, n_tiles = p.row_tiles * p.tok_tiles;
-  const int my_tiles = (int)blockIdx.x < n_tiles ? (n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  const uint32_t rank = kPair ? cluster_ctarank() : 0u;
+  // Tiles: (row group, token tile), a row group being one row tile (single
+  // CTAs) or two (pairs: rank r takes row tile 2*group + r).
+  const int nb = p.n_blocks;
+  const int groups = kPair ? (p.row_tiles + 1) / 2 : p.row_tiles;
+  const int n_tiles = groups * p.tok_tiles;
+  const int cl = kPair ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int ncl = kPair ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  const int my_tiles = cl < n_tiles ? (n_tiles - 1 - cl) / ncl + 1 : 0;
+  auto row_tile = [&](int t) { return ((cl + t * ncl) / p.tok_tiles) * (kPair ? 2 : 1) + (int)rank; };
+  auto tok_tile = [&](int t) { return (cl + t * ncl) % p.tok_tiles; };
+  // Rank 0's copy of a barrier (rank 1 arrives there).
+  auto lead = [&](uint32_t bar) { return kPair ? mapa_shared(bar, 0) : bar; };
 
   uint32_t tw[512 / (kDecWarpsH * 32)];
   if (warp >= 2 && warp < kEpiWarp0H) {
@@ -127,44 +155,59 @@ __global__ void __launch_bounds__(kThreadsH, 1)
       mbar_init(kWfull + 8 * s, 1);
       mbar_init(kWempty + 8 * s, kDecWarpsH);
     }
-    for (int x = 0; x < kXStagesH; ++x) {
+    for (int x = 0; x < kXS; ++x) {
       mbar_init(kXfull + 8 * x, 1);
       mbar_init(kXempty + 8 * x, 1);
     }
     for (int r = 0; r < kARingH; ++r) {
-      mbar_init(kAfull + 8 * r, kDecWarpsH);
+      mbar_init(kAfull + 8 * r, kPair ? 2 * kDecWarpsH : kDecWarpsH);
       mbar_init(kAempty + 8 * r, 1);
     }
     for (int d = 0; d < kDRingH; ++d) {
       mbar_init(kMdone + 8 * d, 1);
-      mbar_init(kEfree + 8 * d, kEpiWarpsH);
+      mbar_init(kEfree + 8 * d, kPair ? 2 * kEpiWarpsH : kEpiWarpsH);
     }
     mbar_init(kEdone, kEpiWarpsH);
     for (int a = 0; a < kAuxRingH; ++a) mbar_init(kDfull + 8 * a, 4);
     fence_barrier_init();
   }
   if (warp == 1) {
-    tc::alloc(smem_u32(tmem_slot), kTmColsH);
-    tc::relinquish();
+    if constexpr (kPair) {
+      tc::alloc_pair(smem_u32(tmem_slot), kTmColsH);
+      tc::relinquish_pair();
+    } else {
+      tc::alloc(smem_u32(tmem_slot), kTmColsH);
+      tc::relinquish();
+    }
   }
   tc::fence_before_sync();
   __syncthreads();
+  if constexpr (kPair) cluster_sync_all();  // both CTAs' barriers and TMEM ready before any remote use
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
 
-  // ------------------------------------------------------------------ weight producer
   if (warp == 0) {
+    // -------------------------------------------------------------- weight producer
     if (lane == 0) {
       int it = 0, s = 0;
       uint32_t ph = 0;
-      for (int t = 0; t < my_tiles; ++t) {
-        const int rt = ((int)blockIdx.x + t * (int)gridDim.x) / p.tok_tiles;
-        const uint8_t* rec = p.packed + (size_t)rt * nb * tm::kRecordBytes;
+      bool ok = true;
+      for (int t = 0; ok && t < my_tiles; ++t) {
+        const int rt = row_tile(t);
+        const bool have = rt < p.row_tiles;  // a pair's second row tile may not exist
+        const uint8_t* rec = p.packed + (size_t)(have ? rt : 0) * nb * tm::kRecordBytes;
         for (int kb = 0; kb < nb; ++kb, ++it) {
-          if (it >= SW && !mbar_wait_bounded(kWempty + 8 * s, ph ^ 1, kSiteGemvEmpty)) return;
-          mbar_arrive_expect_tx(kWfull + 8 * s, tm::kRecordBytes);
-          bulk_load(smem_u32(st0 + (size_t)s * tm::kRecordBytes), rec + (size_t)kb * tm::kRecordBytes,
-                    tm::kRecordBytes, kWfull + 8 * s);
+          if (it >= SW && !mbar_wait_bounded(kWempty + 8 * s, ph ^ 1, kSiteGemvEmpty)) {
+            ok = false;
+            break;
+          }
+          if (have) {
+            mbar_arrive_expect_tx(kWfull + 8 * s, tm::kRecordBytes);
+            bulk_load(smem_u32(st0 + (size_t)s * tm::kRecordBytes), rec + (size_t)kb * tm::kRecordBytes,
+                      tm::kRecordBytes, kWfull + 8 * s);
+          } else {
+            mbar_arrive(kWfull + 8 * s);  // nothing to load: the decoded rows are never stored
+          }
           if (++s == SW) {
             s = 0;
             ph ^= 1;
@@ -172,28 +215,37 @@ __global__ void __launch_bounds__(kThreadsH, 1)
         }
       }
     }
-    return;
-  }
-
-  // ------------------------------------------------------------------ activation producer
-  if (warp == kXWarpH) {
+    __syncwarp();
+  } else if (warp == kXWarpH) {
+    // -------------------------------------------------------------- activation producer
     if (lane == 0) {
       tma_prefetch_desc(&maps.x16);
       const uint64_t keep = l2_policy_evict_last();
       pdl_wait();
       int hj = 0, x = 0;
       uint32_t ph = 0;
-      for (int t = 0; t < my_tiles; ++t) {
-        const int tt = ((int)blockIdx.x + t * (int)gridDim.x) % p.tok_tiles;
-        for (int kb = 0; kb < nb; ++kb) {
+      bool ok = true;
+      for (int t = 0; ok && t < my_tiles; ++t) {
+        const int tok0 = tok_tile(t) * kTokH + (int)rank * kTokLoad;
+        for (int kb = 0; ok && kb < nb; ++kb) {
           for (int h = 0; h < 2; ++h, ++hj) {
-            if (hj >= kXStagesH && !mbar_wait_bounded(kXempty + 8 * x, ph ^ 1, kSiteGemvEmpty)) return;
+            if (hj >= kXS && !mbar_wait_bounded(kXempty + 8 * x, ph ^ 1, kSiteGemvEmpty)) {
+              ok = false;
+              break;
+            }
             const uint32_t full = kXfull + 8 * x;
-            mbar_arrive_expect_tx(full, kXHalfBytes);
-            const uint32_t dst = smem_u32(x0 + (size_t)x * kXHalfBytes);
-            tma_load_2d(dst, &maps.x16, kb * 256 + h * 128, tt * kTokH, full, keep);
-            tma_load_2d(dst + kBoxBytes, &maps.x16, kb * 256 + h * 128 + 64, tt * kTokH, full, keep);
-            if (++x == kXStagesH) {
+            const uint32_t dst = smem_u32(x0 + (size_t)x * kXHalf);
+            if constexpr (kPair) {
+              // Both halves complete on rank 0's barrier, which expects them.
+              if (rank == 0) mbar_arrive_expect_tx(full, 2 * kXHalf);
+              tma_load_2d_pair(dst, &maps.x16, kb * 256 + h * 128, tok0, lead(full), keep);
+              tma_load_2d_pair(dst + kBoxBytes, &maps.x16, kb * 256 + h * 128 + 64, tok0, lead(full), keep);
+            } else {
+              mbar_arrive_expect_tx(full, kXHalf);
+              tma_load_2d(dst, &maps.x16, kb * 256 + h * 128, tok0, full, keep);
+              tma_load_2d(dst + kBoxBytes, &maps.x16, kb * 256 + h * 128 + 64, tok0, full, keep);
+            }
+            if (++x == kXS) {
               x = 0;
               ph ^= 1;
             }
@@ -201,56 +253,72 @@ __global__ void __launch_bounds__(kThreadsH, 1)
         }
       }
     }
-    return;
-  }
-
-  // ------------------------------------------------------------------ MMA
-  if (warp == 1) {
+    __syncwarp();
+  } else if (warp == 1) {
+    // -------------------------------------------------------------- MMA (rank 0 of a pair)
     int it = 0, hj = 0;
-    bool ok = true;
+    bool ok = rank == 0;
     for (int t = 0; ok && t < my_tiles; ++t) {
       for (int kb = 0; ok && kb < nb; ++kb, ++it) {
         const int r = it % kARingH, db = it & 1;
-        ok = tm::warp_wait(kAfull + 8 * r, (it / kARingH) & 1, kSiteGemvFull);
-        // The D buffer is free once the epilogue has read block it - 2.
-        if (ok && it >= kDRingH) ok = tm::warp_wait(kEfree + 8 * db, ((it >> 1) & 1) ^ 1, kSiteGemvEmpty);
+        ok = kPair ? tm::warp_wait_cluster(kAfull + 8 * r, (it / kARingH) & 1, kSiteGemvFull)
+                   : tm::warp_wait(kAfull + 8 * r, (it / kARingH) & 1, kSiteGemvFull);
+        // The D buffer is free once the epilogue(s) have read block it - 2.
+        if (ok && it >= kDRingH)
+          ok = kPair ? tm::warp_wait_cluster(kEfree + 8 * db, ((it >> 1) & 1) ^ 1, kSiteGemvEmpty)
+                     : tm::warp_wait(kEfree + 8 * db, ((it >> 1) & 1) ^ 1, kSiteGemvEmpty);
         if (!ok) break;
         const uint32_t dcol = tmem + kTmD + (uint32_t)(db * kTokH), acol = tmem + kTmA + 128u * (uint32_t)r;
 #pragma unroll 1
         for (int h = 0; h < 2; ++h, ++hj) {
-          const int x = hj % kXStagesH;
-          if (!tm::warp_wait(kXfull + 8 * x, (hj / kXStagesH) & 1, kSiteGemvFull)) {
-            ok = false;
-            break;
-          }
+          const int x = hj % kXS;
+          ok = kPair ? tm::warp_wait_cluster(kXfull + 8 * x, (hj / kXS) & 1, kSiteGemvFull)
+                     : tm::warp_wait(kXfull + 8 * x, (hj / kXS) & 1, kSiteGemvFull);
+          if (!ok) break;
           tc::fence_after_sync();
-          const uint64_t bdesc = tc::smem_desc_sw128(smem_u32(x0 + (size_t)x * kXHalfBytes), 1024u);
+          const uint64_t bdesc = tc::smem_desc_sw128(smem_u32(x0 + (size_t)x * kXHalf), 1024u);
           if (tm::elect_one()) {
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-              tc::mma_f16_ts(dcol, acol + (uint32_t)((8 * h + j) * 8),
-                             bdesc + (uint64_t)(((j >> 2) * kBoxBytes + (j & 3) * 32u) >> 4), kIdesc, (h | j) != 0);
-            tc::commit(kXempty + 8 * x);
+            for (int j = 0; j < 8; ++j) {
+              const uint64_t bj = bdesc + (uint64_t)(((j >> 2) * kBoxBytes + (j & 3) * 32u) >> 4);
+              if constexpr (kPair) {
+                tc::mma_f16_ts_pair(dcol, acol + (uint32_t)((8 * h + j) * 8), bj, kIdesc, (h | j) != 0);
+              } else {
+                tc::mma_f16_ts(dcol, acol + (uint32_t)((8 * h + j) * 8), bj, kIdesc, (h | j) != 0);
+              }
+            }
+            if constexpr (kPair) {
+              tc::commit_pair(kXempty + 8 * x, kBoth);
+            } else {
+              tc::commit(kXempty + 8 * x);
+            }
           }
           __syncwarp();
         }
         if (!ok) break;
         if (tm::elect_one()) {
-          tc::commit(kAempty + 8 * r);
-          tc::commit(kMdone + 8 * db);
+          if constexpr (kPair) {
+            tc::commit_pair(kAempty + 8 * r, kBoth);
+            tc::commit_pair(kMdone + 8 * db, kBoth);
+          } else {
+            tc::commit(kAempty + 8 * r);
+            tc::commit(kMdone + 8 * db);
+          }
         }
         __syncwarp();
       }
     }
+    // Free the TMEM once this CTA's epilogue has read its last results.
     mbar_wait_bounded(kEdone, 0, kSiteGemvFull);
     __syncwarp();
     tc::fence_after_sync();
-    tc::dealloc(tmem, kTmColsH);
-    return;
-  }
-
-  // ------------------------------------------------------------------ decoders
-  if (warp < kEpiWarp0H) {
+    if constexpr (kPair) {
+      tc::dealloc_pair(tmem, kTmColsH);
+    } else {
+      tc::dealloc(tmem, kTmColsH);
+    }
+  } else if (warp < kEpiWarp0H) {
+    // -------------------------------------------------------------- decoders
     const int dw = warp - 2;
     const int q = warp & 3;
     const int part = dw >> 2;  // groups 4*part .. 4*part+3 of the block
@@ -266,12 +334,13 @@ __global__ void __launch_bounds__(kThreadsH, 1)
     const uint32_t off_qh = tm::kRecQh + (uint32_t)part * 512u + (uint32_t)rl * 4u;
     int it = 0, s = 0;
     uint32_t sph = 0;
-    for (int t = 0; t < my_tiles; ++t) {
+    bool ok = true;
+    for (int t = 0; ok && t < my_tiles; ++t) {
       for (int kb = 0; kb < nb; ++kb, ++it) {
         const int r = it % kARingH;
-        bool ok = tm::warp_wait(kWfull + 8 * s, sph, kSiteGemvFull);
+        ok = tm::warp_wait(kWfull + 8 * s, sph, kSiteGemvFull);
         if (ok && it >= kARingH) ok = tm::warp_wait(kAempty + 8 * r, ((it / kARingH) & 1) ^ 1, kSiteGemvEmpty);
-        if (!ok) return;
+        if (!ok) break;
         const uint8_t* st = st0 + (size_t)s * tm::kRecordBytes;
         const uint4 a = *reinterpret_cast<const uint4*>(st + off_q0);
         const uint4 c = *reinterpret_cast<const uint4*>(st + off_q1);
@@ -309,7 +378,11 @@ __global__ void __launch_bounds__(kThreadsH, 1)
         tc::fence_before_sync();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(kAfull + 8 * r);
+          if (kPair && rank != 0) {
+            mbar_arrive_cluster(lead(kAfull + 8 * r));
+          } else {
+            mbar_arrive(kAfull + 8 * r);
+          }
           mbar_arrive(kWempty + 8 * s);
         }
         __syncwarp();
@@ -319,11 +392,8 @@ __global__ void __launch_bounds__(kThreadsH, 1)
         }
       }
     }
-    return;
-  }
-
-  // ------------------------------------------------------------------ epilogue
-  {
+  } else {
+    // -------------------------------------------------------------- epilogue
     const int e = warp - kEpiWarp0H;
     const int q = warp & 3;
     const int h = e >> 2;  // tokens h*64 .. h*64+63 of the tile
@@ -337,8 +407,7 @@ __global__ void __launch_bounds__(kThreadsH, 1)
     int it = 0;
     bool ok = true;
     for (int t = 0; ok && t < my_tiles; ++t) {
-      const int ti = (int)blockIdx.x + t * (int)gridDim.x;
-      const int rt = ti / p.tok_tiles, tt = ti % p.tok_tiles;
+      const int rt = row_tile(t), tt = tok_tile(t);
       for (int kb = 0; kb < nb; ++kb, ++it) {
         const int db = it & 1;
         if (!tm::warp_wait(kDfull + 8 * (it % kAuxRingH), (it / kAuxRingH) & 1, kSiteGemvFull) ||
@@ -363,23 +432,98 @@ __global__ void __launch_bounds__(kThreadsH, 1)
         }
         tc::fence_before_sync();
         __syncwarp();
-        if (lane == 0) mbar_arrive(kEfree + 8 * db);
+        if (lane == 0) {
+          if (kPair && rank != 0) {
+            mbar_arrive_cluster(lead(kEfree + 8 * db));
+          } else {
+            mbar_arrive(kEfree + 8 * db);
+          }
+        }
         __syncwarp();
       }
       if (!ok) break;
+      // The tile's 64 tokens: their scales 8 at a time as float4 loads issued
+      // together (tok_scale is padded to whole tiles), then the stores.
       const int row = rt * kRowsH + rl, tok0 = tt * kTokH + h * 64;
+      const float4* ts = reinterpret_cast<const float4*>(p.tok_scale + tok0);
+      const bool odd = (lane & 1) != 0;
+      const bool pack4 = (p.ldo % 4 == 0) && ((uintptr_t)p.out % (p.out_bf16 ? 8u : 16u) == 0);
+      const bool pack2 = (p.ldo % 2 == 0) && ((uintptr_t)p.out % (p.out_bf16 ? 4u : 8u) == 0);
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const int tok = tok0 + i;
-        const float sc = tok < p.m ? __ldg(p.tok_scale + tok) : 0.f;
-        store_out_h(p, row, tok, acc[i] * sc);
-        acc[i] = 0.f;
+      for (int c = 0; c < 64; c += 8) {
+        const float4 s4a = __ldg(ts + c / 4), s4b = __ldg(ts + c / 4 + 1);
+        const float sc[8] = {s4a.x, s4a.y, s4a.z, s4a.w, s4b.x, s4b.y, s4b.z, s4b.w};
+        if (pack4) {
+          // Four rows per store: a 4 x 4 transpose within each quad of lanes
+          // (two exchange rounds) leaves lane L holding token i + (L & 3) for
+          // rows (L & ~3) .. (L & ~3) + 3 (N % 8 == 0: all four exist).
+          const int ql = lane & 3;
+          const bool hi2 = ql >= 2, qodd = (ql & 1) != 0;
+#pragma unroll
+          for (int i = 0; i < 8; i += 4) {
+            float v[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) v[j] = acc[c + i + j] * sc[i + j];
+            // Round 1 (lane ^ 2): lanes 0-1 keep tokens 0-1, lanes 2-3 tokens 2-3.
+            const float a0 = hi2 ? v[2] : v[0], a1 = hi2 ? v[3] : v[1];
+            const float r0 = __shfl_xor_sync(0xFFFFFFFFu, hi2 ? v[0] : v[2], 2);
+            const float r1 = __shfl_xor_sync(0xFFFFFFFFu, hi2 ? v[1] : v[3], 2);
+            // Round 2 (lane ^ 1): even lanes keep the first of their two tokens.
+            const float g0 = __shfl_xor_sync(0xFFFFFFFFu, qodd ? a0 : a1, 1);  // row L^1
+            const float g1 = __shfl_xor_sync(0xFFFFFFFFu, qodd ? r0 : r1, 1);  // row L^3
+            const float own = qodd ? a1 : a0, own2 = qodd ? r1 : r0;           // rows L, L^2
+            float o[4];
+#pragma unroll
+            for (int pos = 0; pos < 4; ++pos)
+              o[pos] = pos == ql ? own : pos == (ql ^ 2) ? own2 : pos == (ql ^ 1) ? g0 : g1;
+            const int tok = tok0 + c + i + ql, r0w = row - ql;
+            if (r0w < p.n_rows && tok < p.m) {
+              const int64_t at = (int64_t)tok * p.ldo + r0w;
+              if (p.out_bf16) {
+                const __nv_bfloat162 b01 = __floats2bfloat162_rn(o[0], o[1]), b23 = __floats2bfloat162_rn(o[2], o[3]);
+                *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(p.out) + at) =
+                    make_uint2(*reinterpret_cast<const uint32_t*>(&b01), *reinterpret_cast<const uint32_t*>(&b23));
+              } else {
+                *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + at) = make_float4(o[0], o[1], o[2], o[3]);
+              }
+            }
+          }
+        } else if (pack2) {
+          // Two rows per store: lanes L and L^1 trade one value, so that the
+          // even lane holds rows L, L+1 of token i and the odd lane rows L-1, L
+          // of token i+1 (N % 8 == 0: both rows exist when the first does).
+#pragma unroll
+          for (int i = 0; i < 8; i += 2) {
+            const float v0 = acc[c + i] * sc[i], v1 = acc[c + i + 1] * sc[i + 1];
+            const float got = __shfl_xor_sync(0xFFFFFFFFu, odd ? v0 : v1, 1);
+            const int tok = tok0 + c + i + (odd ? 1 : 0), r0 = row - (odd ? 1 : 0);
+            if (r0 < p.n_rows && tok < p.m) {
+              const int64_t at = (int64_t)tok * p.ldo + r0;
+              if (p.out_bf16) {
+                *reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<__nv_bfloat16*>(p.out) + at) =
+                    __floats2bfloat162_rn(odd ? got : v0, odd ? v1 : got);
+              } else {
+                *reinterpret_cast<float2*>(reinterpret_cast<float*>(p.out) + at) =
+                    make_float2(odd ? got : v0, odd ? v1 : got);
+              }
+            }
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) store_out_h(p, row, tok0 + c + i, acc[c + i] * sc[i]);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[c + i] = 0.f;
       }
     }
     tc::fence_before_sync();
     __syncwarp();
     if (lane == 0) mbar_arrive(kEdone);
+    __syncwarp();
   }
+  // Neither CTA of a pair leaves while the other may still use its shared
+  // memory or TMEM (remote arrivals, the pair MMAs).
+  if constexpr (kPair) cluster_sync_all();
 }
 
 // One CTA per token row: e_max over the row's UE8M0 scales, then every E4M3
@@ -441,10 +585,41 @@ cudaError_t launch_x16(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64
 
 cudaError_t launch_gemm_f16(const GemmF16Params& p, const GemmF16Maps& maps, int grid, cudaStream_t stream) {
   const uint32_t smem = gemm_f16_smem(p.wstages);
-  const void* kern = (const void*)iq3s_gemm_f16_kernel;
+  const void* kern = (const void*)iq3s_gemm_f16_kernel<false>;
   cudaError_t e = ensure_smem_attribute(kern, smem);
   if (e != cudaSuccess) return e;
   return launch_pdl(kern, dim3(grid), dim3(kThreadsH), smem, stream, p, maps);
+}
+
+int gemm_f16_pair_max_clusters(int wstages) {
+  const void* kern = (const void*)iq3s_gemm_f16_kernel<true>;
+  const uint32_t smem = gemm_f16_smem(wstages);
+  if (ensure_smem_attribute(kern, smem) != cudaSuccess) return 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2);
+  cfg.blockDim = dim3(kThreadsH);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+cudaError_t launch_gemm_f16_pair(const GemmF16Params& p, const GemmF16Maps& maps, int clusters, cudaStream_t stream) {
+  const uint32_t smem = gemm_f16_smem(p.wstages);
+  const void* kern = (const void*)iq3s_gemm_f16_kernel<true>;
+  cudaError_t e = ensure_smem_attribute(kern, smem);
+  if (e != cudaSuccess) return e;
+  return launch_pdl_cluster(kern, dim3(2 * clusters), dim3(kThreadsH), smem, stream, 2, p, maps);
 }
 
 }  // namespace mambo

@@ -595,14 +595,16 @@ bool make_gemm_x8_map(const uint8_t* xq, int64_t ldxq, int m, int64_t k, CUtenso
   return encode(fn, map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, xq, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-bool make_gemm_x16_map(const uint16_t* x16, int64_t ld, int m, int64_t k, CUtensorMap* map) {
+bool make_gemm_x16_map(const uint16_t* x16, int64_t ld, int m, int64_t k, int box_tokens, CUtensorMap* map) {
   EncodeTiledFn fn = get_encode_fn();
-  if (!fn || (uintptr_t)x16 % 16 || (ld * 2) % 16 || m < 1 || k % 128) return false;
-  // [m tokens][K halves]: a box of 128 tokens x 64 halves (128 bytes) lands as
-  // eight 1024-byte atoms of the K-major 128-byte-swizzled UMMA layout.
+  if (!fn || (uintptr_t)x16 % 16 || (ld * 2) % 16 || m < 1 || k % 128 || box_tokens % 8 || box_tokens > 256)
+    return false;
+  // [m tokens][K halves]: a box of box_tokens tokens x 64 halves (128 bytes)
+  // lands as 1024-byte atoms (8 tokens each) of the K-major 128-byte-swizzled
+  // UMMA layout.
   cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)m};
   cuuint64_t str[1] = {(cuuint64_t)(ld * 2)};
-  cuuint32_t box[2] = {64, 128};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_tokens};
   return encode(fn, map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, x16, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 

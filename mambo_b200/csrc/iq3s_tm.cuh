@@ -115,6 +115,12 @@ static __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, 
   if (__all_sync(0xFFFFFFFFu, mbar_try_wait(bar, parity))) return true;
   return __all_sync(0xFFFFFFFFu, mbar_wait_bounded(bar, parity, site));
 }
+// As warp_wait for a barrier that the other CTA of a cluster also arrives on
+// (acquire at cluster scope).
+static __device__ __forceinline__ bool warp_wait_cluster(uint32_t bar, uint32_t parity, int site) {
+  if (__all_sync(0xFFFFFFFFu, mbar_try_wait_cluster(bar, parity))) return true;
+  return __all_sync(0xFFFFFFFFu, mbar_wait_cluster_bounded(bar, parity, site));
+}
 
 }  // namespace tm
 }  // namespace mambo

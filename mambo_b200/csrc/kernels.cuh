@@ -253,7 +253,10 @@ int gemm_f16_max_wstages();
 // tok_scale[m] = 2^(e_max - 127). Exact while a group's exponent is within 12 of the token's largest.
 cudaError_t launch_x16(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t ldxs, int m, int64_t k,
                        uint16_t* x16, int64_t ld, float* tok_scale, cudaStream_t stream);
-bool make_gemm_x16_map(const uint16_t* x16, int64_t ld, int m, int64_t k, CUtensorMap* map);
+bool make_gemm_x16_map(const uint16_t* x16, int64_t ld, int m, int64_t k, int box_tokens, CUtensorMap* map);
+// CTA pairs of the FP16 GEMM that fit on the device at once, and their launch.
+int gemm_f16_pair_max_clusters(int wstages);
+cudaError_t launch_gemm_f16_pair(const GemmF16Params& p, const GemmF16Maps& maps, int clusters, cudaStream_t stream);
 
 // Activation scales [m][K/32] -> atoms [ceil(m/128)][K/128][32][16] (bytes: m_pad * K / 32).
 cudaError_t launch_xs_atoms(const uint8_t* xs, int64_t ldxs, int m, int n_blocks, uint8_t* atoms, cudaStream_t stream);

@@ -177,6 +177,43 @@ __device__ __forceinline__ void dealloc(uint32_t taddr, uint32_t ncols) {
   asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 
+// ---------------------------------------------------------------------------
+// CTA pairs (cta_group::2, a cluster of two CTAs): one MMA spans both CTAs'
+// tensor cores. A (M = 256) is rows 0-127 from CTA rank 0's TMEM and rows
+// 128-255 from rank 1's, at the same TMEM address; B (N) is columns 0..N/2-1
+// from rank 0's shared memory and N/2..N-1 from rank 1's, at the same
+// address; D rows land in the TMEM of the CTA that supplied them. Rank 0
+// issues the MMAs.
+// ---------------------------------------------------------------------------
+// Allocation, release and free: one warp of each CTA, the same warp in both,
+// the same dst address.
+__device__ __forceinline__ void alloc_pair(uint32_t dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// The pair MMA with FP16 operands (K = 16), A from TMEM; issued by one thread of rank 0.
+__device__ __forceinline__ void mma_f16_ts_pair(uint32_t tmem_d, uint32_t tmem_a, uint64_t desc_b, uint32_t idesc,
+                                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(desc_b), "r"(idesc), "r"(accumulate));
+}
+// Arrives on the barrier at address bar (a CTA-local offset) in every CTA of
+// cta_mask once the issuing thread's earlier pair MMAs have completed.
+__device__ __forceinline__ void commit_pair(uint32_t bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+      "h"(cta_mask)
+      : "memory");
+}
+
 __device__ __forceinline__ void fence_before_sync() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }

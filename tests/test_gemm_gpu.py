@@ -25,9 +25,10 @@ REL_FROB_TOL = 1e-3    # north star: vs fp32/f64 matmul of the dequantized opera
 ORACLE_FROB_TOL = 1e-4  # vs the float64 oracle on the same MXFP8 inputs (FP32 accumulation only)
 GEMM = {"kernel": _lib.MAMBO_KERNEL_GEMM, "warps": 8, "stages": 4}
 GEMM_F16 = {"kernel": _lib.MAMBO_KERNEL_GEMM_F16, "warps": 8, "stages": 4}
-# The per-group FP8 kernel (the reference's decomposition) and the FP16-operand kernel (group scale folded
-# into the weight operand, one accumulator per K block).
-KINDS = {"fp8_groups": GEMM, "f16": GEMM_F16}
+GEMM_F16_PAIR = {"kernel": _lib.MAMBO_KERNEL_GEMM_F16_PAIR, "warps": 8, "stages": 4}
+# The per-group FP8 kernel (the reference's decomposition), the FP16-operand kernel (group scale folded
+# into the weight operand, one accumulator per K block) and the same on CTA pairs (256-row tiles).
+KINDS = {"fp8_groups": GEMM, "f16": GEMM_F16, "f16_pair": GEMM_F16_PAIR}
 
 
 def to_np(t: torch.Tensor) -> np.ndarray:
