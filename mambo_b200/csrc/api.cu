@@ -379,9 +379,19 @@ int launch_gemm_f16_path(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int
   p.wstages = c.stages;
   p.row_tiles = (int)((w->n_rows + 127) / 128);
   p.tok_tiles = (int)((m + 127) / 128);
+  // bf16 output in 16-byte aligned rows: tiles leave through shared memory and
+  // a TMA store, with the weight stages it needs room for.
+  if (out_dtype == MAMBO_BF16 && make_gemm_out_map(out, ldo, (int)w->n_rows, (int)m, &maps.out)) {
+    int st = c.stages;
+    while (st > 2 && (int)gemm_f16_smem_bytes(st, true) > info.max_smem_optin) --st;
+    if ((int)gemm_f16_smem_bytes(st, true) <= info.max_smem_optin) {
+      p.out_tma = 1;
+      p.wstages = st;
+    }
+  }
   if (pair) {
     const int64_t tiles = (int64_t)((p.row_tiles + 1) / 2) * p.tok_tiles;
-    int clusters = gemm_f16_pair_max_clusters(c.stages);
+    int clusters = gemm_f16_pair_max_clusters(p.wstages, p.out_tma != 0);
     if (clusters < 1) return fail(MAMBO_EINVAL, "no CTA pair of this configuration fits on the device");
     if (tiles < clusters) clusters = (int)tiles;
     e = launch_gemm_f16_pair(p, maps, clusters, stream);

@@ -199,6 +199,19 @@ __device__ __forceinline__ uint64_t l2_policy_evict_last() {
   return pol;
 }
 
+// Tensor store of a 2-D box from shared memory (bulk-group completion), and
+// the waits on this thread's bulk groups: `read` until their shared memory
+// sources may be overwritten, plain until the writes are done.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, int32_t c0, int32_t c1, uint32_t src) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(src)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_group_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_group0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // As tma_load_2d for a CTA of a pair: the bytes land in this CTA's shared
 // memory at dst and complete on the barrier at cluster address bar, which may
 // be the other CTA's (no multicast).

@@ -56,15 +56,17 @@ constexpr uint32_t kTmA = 0, kTmD = 128u * kARingH;
 constexpr uint32_t kTmColsH = 512;
 static_assert(kTmD + kDRingH * (uint32_t)kTokH <= kTmColsH, "TMEM plan exceeds 512 columns");
 constexpr int kThreadsH = (3 + kDecWarpsH + kEpiWarpsH) * 32;
-static_assert(2 * (kMaxWStagesH + kXStagesMaxH + kARingH + kDRingH) + 1 + kAuxRingH + 1 <= (int)(kBarBytesH / 8),
+static_assert(2 * (kMaxWStagesH + kXStagesMaxH + kARingH + kDRingH) + 1 + kAuxRingH + 2 + 1 <= (int)(kBarBytesH / 8),
               "barrier area");
 constexpr int kEpiWarp0H = 2 + kDecWarpsH, kXWarpH = kEpiWarp0H + kEpiWarpsH;
 
 __host__ __device__ constexpr uint32_t align_up_h(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
-__host__ __device__ inline uint32_t gemm_f16_smem(int wstages) {
+// With out_stage: a 32 KB bf16 tile (128 tokens x 128 rows) for the TMA store, after the barriers.
+constexpr uint32_t kOutStageBytesH = kTokH * kRowsH * 2u;
+__host__ __device__ inline uint32_t gemm_f16_smem(int wstages, bool out_stage = false) {
   return tm::kTableBytes + 1024 + align_up_h((uint32_t)wstages * tm::kRecordBytes, 1024) + kXRingBytesH +
-         kAuxRingH * kAuxH + tm::kTableStageBytes + kBarBytesH;
+         kAuxRingH * kAuxH + tm::kTableStageBytes + kBarBytesH + (out_stage ? 128u + kOutStageBytesH : 0u);
 }
 
 // Two E4M3 values (bytes 0 and 1 of each half of v) -> two FP16 pairs.
@@ -121,7 +123,9 @@ __global__ void __launch_bounds__(kThreadsH, 1)
   uint32_t* tstage = reinterpret_cast<uint32_t*>(aux0 + kAuxRingH * kAuxH);
   uint64_t* bars = reinterpret_cast<uint64_t*>(aux0 + kAuxRingH * kAuxH + tm::kTableStageBytes);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kMaxWStagesH + 2 * kXStagesMaxH + 2 * kARingH +
-                                                    2 * kDRingH + 1 + kAuxRingH);
+                                                    2 * kDRingH + 1 + kAuxRingH + 2);
+  uint8_t* ostage = reinterpret_cast<uint8_t*>(bars) + kBarBytesH;  // bf16 output tile (out_tma)
+  ostage += (128u - (smem_u32(ostage) & 127u)) & 127u;
   const uint32_t bar0 = smem_u32(bars);
   // Barriers as in the FP8 GEMM, with activation slots per half block.
   const uint32_t kWfull = bar0, kWempty = bar0 + 8 * kMaxWStagesH;
@@ -129,6 +133,9 @@ __global__ void __launch_bounds__(kThreadsH, 1)
   const uint32_t kAfull = kXempty + 8 * kXStagesMaxH, kAempty = kAfull + 8 * kARingH;
   const uint32_t kMdone = kAempty + 8 * kARingH, kEfree = kMdone + 8 * kDRingH;
   const uint32_t kEdone = kEfree + 8 * kDRingH, kDfull = kEdone + 8;
+  // Output staging (out_tma): free for writing (the previous TMA store has
+  // read it), and written by all epilogue warps.
+  const uint32_t kOfree = kDfull + 8 * kAuxRingH, kOfull = kOfree + 8;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = kPair ? cluster_ctarank() : 0u;
@@ -169,6 +176,8 @@ __global__ void __launch_bounds__(kThreadsH, 1)
     }
     mbar_init(kEdone, kEpiWarpsH);
     for (int a = 0; a < kAuxRingH; ++a) mbar_init(kDfull + 8 * a, 4);
+    mbar_init(kOfree, 1);
+    mbar_init(kOfull, kEpiWarpsH);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -442,17 +451,59 @@ __global__ void __launch_bounds__(kThreadsH, 1)
         __syncwarp();
       }
       if (!ok) break;
-      // The tile's 64 tokens: their scales 8 at a time as float4 loads issued
-      // together (tok_scale is padded to whole tiles), then the stores.
+      // The tile's 64 tokens, 8 at a time: their scales as two float4 loads
+      // (tok_scale is padded to whole tiles), issued before the previous
+      // chunk's stores so that the load latency overlaps them.
       const int row = rt * kRowsH + rl, tok0 = tt * kTokH + h * 64;
       const float4* ts = reinterpret_cast<const float4*>(p.tok_scale + tok0);
+      if (p.out_tma) {
+        // bf16 tile into shared memory ([token][row], as the TMA box), then one
+        // TMA store: the epilogue moves on to the next tile at once. The
+        // previous tile's store must have read the staging tile first.
+        if (e == 0 && lane == 0) {
+          bulk_wait_group_read0();
+          mbar_arrive(kOfree);
+        }
+        if (!tm::warp_wait(kOfree, (uint32_t)t & 1u, kSiteGemvEmpty)) break;
+        __nv_bfloat16* stg = reinterpret_cast<__nv_bfloat16*>(ostage) + (size_t)(h * 64) * kRowsH + rl;
+        float4 n4a = __ldg(ts), n4b = __ldg(ts + 1);
+#pragma unroll
+        for (int c = 0; c < 64; c += 8) {
+          const float sc[8] = {n4a.x, n4a.y, n4a.z, n4a.w, n4b.x, n4b.y, n4b.z, n4b.w};
+          if (c + 8 < 64) {
+            n4a = __ldg(ts + (c + 8) / 4);
+            n4b = __ldg(ts + (c + 8) / 4 + 1);
+          }
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            stg[(size_t)(c + i) * kRowsH] = __float2bfloat16_rn(acc[c + i] * sc[i]);
+            acc[c + i] = 0.f;
+          }
+        }
+        fence_proxy_async_shared();  // the TMA store reads the tile through the async proxy
+        __syncwarp();
+        if (lane == 0) mbar_arrive(kOfull);
+        if (e == 0) {
+          if (!tm::warp_wait(kOfull, (uint32_t)t & 1u, kSiteGemvFull)) break;
+          if (lane == 0) {
+            tma_store_2d(&maps.out, rt * kRowsH, tt * kTokH, smem_u32(ostage));
+            bulk_commit_group();
+          }
+        }
+        __syncwarp();
+        continue;
+      }
       const bool odd = (lane & 1) != 0;
       const bool pack4 = (p.ldo % 4 == 0) && ((uintptr_t)p.out % (p.out_bf16 ? 8u : 16u) == 0);
       const bool pack2 = (p.ldo % 2 == 0) && ((uintptr_t)p.out % (p.out_bf16 ? 4u : 8u) == 0);
+      float4 n4a = __ldg(ts), n4b = __ldg(ts + 1);
 #pragma unroll
       for (int c = 0; c < 64; c += 8) {
-        const float4 s4a = __ldg(ts + c / 4), s4b = __ldg(ts + c / 4 + 1);
-        const float sc[8] = {s4a.x, s4a.y, s4a.z, s4a.w, s4b.x, s4b.y, s4b.z, s4b.w};
+        const float sc[8] = {n4a.x, n4a.y, n4a.z, n4a.w, n4b.x, n4b.y, n4b.z, n4b.w};
+        if (c + 8 < 64) {
+          n4a = __ldg(ts + (c + 8) / 4);
+          n4b = __ldg(ts + (c + 8) / 4 + 1);
+        }
         if (pack4) {
           // Four rows per store: a 4 x 4 transpose within each quad of lanes
           // (two exchange rounds) leaves lane L holding token i + (L & 3) for
@@ -516,6 +567,7 @@ __global__ void __launch_bounds__(kThreadsH, 1)
         for (int i = 0; i < 8; ++i) acc[c + i] = 0.f;
       }
     }
+    if (p.out_tma && e == 0 && lane == 0) bulk_wait_group0();  // the last tile's store is written
     tc::fence_before_sync();
     __syncwarp();
     if (lane == 0) mbar_arrive(kEdone);
@@ -574,7 +626,7 @@ __global__ void iq3s_x16_kernel(const uint8_t* __restrict__ xq, int64_t ldxq, co
 // --------------------------------------------------------------------------
 // Host side
 // --------------------------------------------------------------------------
-uint32_t gemm_f16_smem_bytes(int wstages) { return gemm_f16_smem(wstages); }
+uint32_t gemm_f16_smem_bytes(int wstages, bool out_stage) { return gemm_f16_smem(wstages, out_stage); }
 int gemm_f16_max_wstages() { return kMaxWStagesH; }
 
 cudaError_t launch_x16(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t ldxs, int m, int64_t k,
@@ -584,16 +636,16 @@ cudaError_t launch_x16(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64
 }
 
 cudaError_t launch_gemm_f16(const GemmF16Params& p, const GemmF16Maps& maps, int grid, cudaStream_t stream) {
-  const uint32_t smem = gemm_f16_smem(p.wstages);
+  const uint32_t smem = gemm_f16_smem(p.wstages, p.out_tma != 0);
   const void* kern = (const void*)iq3s_gemm_f16_kernel<false>;
   cudaError_t e = ensure_smem_attribute(kern, smem);
   if (e != cudaSuccess) return e;
   return launch_pdl(kern, dim3(grid), dim3(kThreadsH), smem, stream, p, maps);
 }
 
-int gemm_f16_pair_max_clusters(int wstages) {
+int gemm_f16_pair_max_clusters(int wstages, bool out_stage) {
   const void* kern = (const void*)iq3s_gemm_f16_kernel<true>;
-  const uint32_t smem = gemm_f16_smem(wstages);
+  const uint32_t smem = gemm_f16_smem(wstages, out_stage);
   if (ensure_smem_attribute(kern, smem) != cudaSuccess) return 0;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2);
@@ -615,7 +667,7 @@ int gemm_f16_pair_max_clusters(int wstages) {
 }
 
 cudaError_t launch_gemm_f16_pair(const GemmF16Params& p, const GemmF16Maps& maps, int clusters, cudaStream_t stream) {
-  const uint32_t smem = gemm_f16_smem(p.wstages);
+  const uint32_t smem = gemm_f16_smem(p.wstages, p.out_tma != 0);
   const void* kern = (const void*)iq3s_gemm_f16_kernel<true>;
   cudaError_t e = ensure_smem_attribute(kern, smem);
   if (e != cudaSuccess) return e;

@@ -584,6 +584,16 @@ bool make_gemv_xb_map(const uint16_t* x, int64_t ldx, int m, int64_t k, int box_
   return encode(fn, map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, x, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
+bool make_gemm_out_map(void* out, int64_t ldo, int n_rows, int m, CUtensorMap* map) {
+  EncodeTiledFn fn = get_encode_fn();
+  if (!fn || (uintptr_t)out % 16 || ldo % 8 || n_rows < 1 || m < 1) return false;
+  // [m tokens][n_rows bf16]: a 128-row x 128-token tile, rows contiguous (unswizzled).
+  cuuint64_t dims[2] = {(cuuint64_t)n_rows, (cuuint64_t)m};
+  cuuint64_t str[1] = {(cuuint64_t)(ldo * 2)};
+  cuuint32_t box[2] = {128, 128};
+  return encode(fn, map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, out, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
 bool make_gemm_x8_map(const uint8_t* xq, int64_t ldxq, int m, int64_t k, CUtensorMap* map) {
   EncodeTiledFn fn = get_encode_fn();
   if (!fn || (uintptr_t)xq % 16 || ldxq % 16 || m < 1 || k % 128) return false;

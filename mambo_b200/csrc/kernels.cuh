@@ -242,12 +242,16 @@ struct GemmF16Params {
   int wstages;
   int row_tiles;
   int tok_tiles;
+  int out_tma;  // 1: bf16 output tiles staged in shared memory and written by a TMA store
 };
 struct GemmF16Maps {
   CUtensorMap x16;  // FP16 activations [m tokens][K], box 64 halves x 128 tokens, 128-byte swizzle
+  CUtensorMap out;  // bf16 output [m][ldo] (with out_tma), box 128 rows x 128 tokens
 };
 cudaError_t launch_gemm_f16(const GemmF16Params& p, const GemmF16Maps& maps, int grid, cudaStream_t stream);
-uint32_t gemm_f16_smem_bytes(int wstages);
+uint32_t gemm_f16_smem_bytes(int wstages, bool out_stage = false);
+// bf16 output map for the FP16 GEMM's TMA stores; false unless out is 16-byte aligned with ldo % 8 == 0.
+bool make_gemm_out_map(void* out, int64_t ldo, int n_rows, int m, CUtensorMap* map);
 int gemm_f16_max_wstages();
 // MXFP8 activations -> FP16 x16[m][k] (row stride ld halves) = E4M3 * 2^(e_group - e_max(token)),
 // tok_scale[m] = 2^(e_max - 127). Exact while a group's exponent is within 12 of the token's largest.
@@ -255,7 +259,7 @@ cudaError_t launch_x16(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64
                        uint16_t* x16, int64_t ld, float* tok_scale, cudaStream_t stream);
 bool make_gemm_x16_map(const uint16_t* x16, int64_t ld, int m, int64_t k, int box_tokens, CUtensorMap* map);
 // CTA pairs of the FP16 GEMM that fit on the device at once, and their launch.
-int gemm_f16_pair_max_clusters(int wstages);
+int gemm_f16_pair_max_clusters(int wstages, bool out_stage);
 cudaError_t launch_gemm_f16_pair(const GemmF16Params& p, const GemmF16Maps& maps, int clusters, cudaStream_t stream);
 
 // Activation scales [m][K/32] -> atoms [ceil(m/128)][K/128][32][16] (bytes: m_pad * K / 32).

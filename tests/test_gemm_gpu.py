@@ -68,6 +68,16 @@ def test_gemm_bf16_output(cuda_device, kind):
     assert O.relative_frobenius(to_np(out.float()), ref) < 4e-3  # bf16 output rounding
 
 
+@pytest.mark.parametrize("m,n,k", [(32, 256, 512), (130, 384, 1024), (257, 136, 512), (300, 640, 1536), (2048, 1024, 1024)])
+@pytest.mark.parametrize("kind", sorted(KINDS))
+def test_gemm_bf16_output_is_the_rounded_f32_output(cuda_device, m, n, k, kind):
+    """bf16 tiles leave through shared memory and a TMA store (partial tiles clipped): bit for bit the f32 result rounded."""
+    fields, xq, xs, _ = _case(cuda_device, m, n, k, seed=500 + m + n)
+    f32 = launch_iq3_s_fp8_matmul(xq, xs, fields, config=KINDS[kind])
+    bf16 = launch_iq3_s_fp8_matmul(xq, xs, fields, out_dtype=torch.bfloat16, config=KINDS[kind])
+    assert torch.equal(bf16.view(torch.int16), f32.to(torch.bfloat16).view(torch.int16))
+
+
 def test_default_config_picks_the_gemm_at_large_m(cuda_device):
     lib = _lib.load()
     for m, kind in ((8, _lib.MAMBO_KERNEL_GEMV), (31, _lib.MAMBO_KERNEL_GEMV), (32, _lib.MAMBO_KERNEL_GEMM_F16),
