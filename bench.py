@@ -450,6 +450,7 @@ def run_llama3_8b(args) -> None:
     }), flush=True)
 
 
+TP70B_GROUPS = (("qkv",), ("o",), ("gate", "up"), ("down",))  # launches per layer, in a model's order
 TP70B = (  # name, N, K, split (Llama-3-70B)
     ("qkv", 10240, 8192, "column"),
     ("o", 8192, 8192, "row"),
@@ -472,7 +473,7 @@ def run_tp70b(args) -> None:
     import torch
     import torch.distributed as dist
 
-    from mambo_b200.sharding import TensorParallelIQ3SLinear
+    from mambo_b200.sharding import TensorParallelIQ3SLinear, local_group
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -512,22 +513,47 @@ def run_tp70b(args) -> None:
             for w in range(args.warmup):
                 layer(w & 1)
         torch.cuda.synchronize(dev)
-        # Per linear a CUDA graph of this rank's compute (quantization + linear); the NCCL
-        # collective runs eagerly between replays on the same stream.
+        # A layer in a model's order: QKV, O, gate and up together (one grouped
+        # launch: they read the same input), down. Per group a CUDA graph of this
+        # rank's compute; the NCCL collectives run eagerly between replays on the
+        # same stream. With one GPU (no collectives) the layer is one graph.
+        kdim = {name: k for name, n, k, split in TP70B}
+
+        def group_local(li, grp):
+            if len(grp) == 1:
+                return [layers[li][grp[0]].local(xs[kdim[grp[0]]])]
+            return local_group([layers[li][name] for name in grp], xs[kdim[grp[0]]])
+
+        with torch.cuda.stream(stream):
+            for li in range(2):
+                for grp in TP70B_GROUPS:
+                    group_local(li, grp)  # eager warm-up of the grouped path
+        torch.cuda.synchronize(dev)
         graphs = {}
         for li in range(2):
-            for name, n, k, split in TP70B:
+            if world == 1:
                 g = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(g, stream=stream):
-                    y = layers[li][name].local(xs[k])
-                graphs[(li, name)] = (g, y)
+                    for grp in TP70B_GROUPS:
+                        group_local(li, grp)
+                graphs[li] = g
+            else:
+                for grp in TP70B_GROUPS:
+                    g = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(g, stream=stream):
+                        ys = group_local(li, grp)
+                    graphs[(li, grp)] = (g, ys)
         torch.cuda.synchronize(dev)
 
         def layer_graphed(li):
-            for name, n, k, split in TP70B:
-                g, y = graphs[(li, name)]
+            if world == 1:
+                graphs[li].replay()
+                return
+            for grp in TP70B_GROUPS:
+                g, ys = graphs[(li, grp)]
                 g.replay()
-                layers[li][name].combine(y)
+                for name, y in zip(grp, ys):
+                    layers[li][name].combine(y)
 
         with torch.cuda.stream(stream):
             for w in range(args.warmup):
@@ -564,9 +590,10 @@ def run_tp70b(args) -> None:
                           "data": "synthetic", "weights_per_layer_bytes": sum(n * (k // 256) * 110
                                                                                for _, n, k, _ in TP70B),
                           "hbm_peak_gbs_per_gpu": peak, "peak_kind": kind,
-                          "note": "ms_per_layer: per linear a CUDA-graph replay of the rank's compute "
-                                  "(quantize + linear) and the NCCL collective issued eagerly; collective_ms: "
-                                  "device time of the layer's all-gathers/all-reduces measured alone in eager steps",
+                          "note": "ms_per_layer: QKV, O, grouped gate+up, down; per group a CUDA-graph replay of "
+                                  "the rank's compute (fused quantization + linear) and the NCCL collectives issued "
+                                  "eagerly (one graph per layer on one GPU); collective_ms: device time of the "
+                                  "layer's all-gathers/all-reduces measured alone in eager steps",
                           "results": results}), flush=True)
 
 

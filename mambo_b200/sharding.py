@@ -106,6 +106,9 @@ class TensorParallelIQ3SLinear:
         self.out_dtype = out_dtype
         self._quantize = quantize or _default_quantize
         self._linear = linear or _default_linear
+        # With the library's own kernels, quantization and linear are one call
+        # (one launch at decode sizes: the GEMV quantizes its bf16 rows itself).
+        self._fused = quantize is None and linear is None
         if raw_is_shard:
             local = raw
             full_n = raw.shape[0] * (self.world if mode == COLUMN else 1)
@@ -135,18 +138,23 @@ class TensorParallelIQ3SLinear:
         if self.mode == COLUMN:
             if x.shape[1] != self.k:
                 raise ValueError(f"column-split activation must be [M,{self.k}]")
-            xq, xs = self._quantize(x)
-            return self._linear(xq, xs, self.fields, self.out_dtype)
+            return self._quantized_linear(x, self.out_dtype)
         # Row split: this rank's K slice (whole 256-weight blocks: MXFP8 groups stay intact).
         if self.input_is_sharded:
             if x.shape[1] != self.local_k:
                 raise ValueError(f"sharded row-split activation must be [M,{self.local_k}]")
-            xq, xs = self._quantize(x)
-        else:
-            if x.shape[1] != self.k:
-                raise ValueError(f"row-split activation must be [M,{self.k}]")
-            xq, xs = self._quantize(x[:, self.k0:self.k0 + self.local_k])
-        return self._linear(xq, xs, self.fields, torch.float32)
+            return self._quantized_linear(x, torch.float32)
+        if x.shape[1] != self.k:
+            raise ValueError(f"row-split activation must be [M,{self.k}]")
+        return self._quantized_linear(x[:, self.k0:self.k0 + self.local_k], torch.float32)
+
+    def _quantized_linear(self, x: torch.Tensor, out_dtype: torch.dtype) -> torch.Tensor:
+        if self._fused and x.dtype in (torch.float32, torch.bfloat16):
+            from .kernels.iq3_s_fp8 import iq3_s_fp8_linear
+
+            return iq3_s_fp8_linear(x, self.fields, out_dtype=out_dtype)
+        xq, xs = self._quantize(x)
+        return self._linear(xq, xs, self.fields, out_dtype)
 
     def combine(self, y: torch.Tensor, *, time_collective: bool = False) -> torch.Tensor:
         """The exchange step on local()'s result: all-gather (COLUMN, when asked) or all-reduce (ROW)."""
@@ -183,3 +191,25 @@ class TensorParallelIQ3SLinear:
         e1.synchronize()
         self.times.collective_ms = e0.elapsed_time(e1)
         return out
+
+
+def local_group(linears, x: torch.Tensor) -> list:
+    """local() of several COLUMN shards that read the same activation (gate and
+    up, or separate Q, K, V weights) as one grouped launch on this rank.
+
+    Returns each shard's [M, N/P] output; pass each to its own combine().
+    Falls back to one local() per shard unless all use the library's kernels.
+    """
+    if not linears:
+        return []
+    if any(lin.mode != COLUMN or not lin._fused or lin.k != linears[0].k for lin in linears) \
+            or x.dtype not in (torch.float32, torch.bfloat16):
+        return [lin.local(x) for lin in linears]
+    if x.ndim != 2 or x.shape[1] != linears[0].k:
+        raise ValueError(f"column-split activation must be [M,{linears[0].k}]")
+    from .kernels.iq3_s_fp8 import group_linear_into
+
+    if x.stride(1) != 1:
+        x = x.contiguous()
+    outs = [torch.empty((x.shape[0], lin.local_n), dtype=lin.out_dtype, device=x.device) for lin in linears]
+    return group_linear_into([x] * len(linears), [lin.fields for lin in linears], outs)

@@ -145,3 +145,23 @@ def test_decode_sweep_as_one_group(cuda_device):
         one = iq3_s_fp8_linear(x, w, out_dtype=torch.float32)
         err = (torch.linalg.norm(y.double() - one.double()) / torch.linalg.norm(one.double())).item()
         assert err < 1e-5, err
+
+
+def test_tensor_parallel_local_group_matches_separate_shards(cuda_device):
+    """Column shards that read the same activation (gate and up) as one grouped launch on a rank."""
+    from mambo_b200.sharding import COLUMN, TensorParallelIQ3SLinear, local_group
+
+    gen = torch.Generator(device=cuda_device).manual_seed(81)
+    lins = []
+    for n in (1024, 1536):
+        raw = torch.randint(0, 256, (n, 8, 110), dtype=torch.uint8, device=cuda_device, generator=gen)
+        raw[..., :2] = (torch.rand((n, 8), device=cuda_device, generator=gen) * 9e-3 + 1e-3).half() \
+            .view(torch.uint8).view(n, 8, 2)
+        lins.append(TensorParallelIQ3SLinear(raw, COLUMN, out_dtype=torch.float32))
+    x = torch.randn((4, 2048), device=cuda_device, generator=gen).to(torch.bfloat16)
+    grouped = local_group(lins, x)
+    for lin, y in zip(lins, grouped):
+        one = lin.local(x)
+        assert y.shape == one.shape
+        err = (torch.linalg.norm(y.double() - one.double()) / torch.linalg.norm(one.double())).item()
+        assert err < 1e-5, err
