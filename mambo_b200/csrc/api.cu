@@ -864,6 +864,8 @@ int mambo_iq3s_linear_fused(const void* x, int x_dtype, int64_t ldx, int64_t m, 
 namespace {
 
 constexpr int kGroupDecWarps = 8;
+// Cost of a grouped launch's unit per token beyond two (thousandths of a one-token unit).
+constexpr int64_t kGroupCostPerToken = 40;
 static_assert(MAMBO_MAX_GROUP == kGemvMaxItems, "group size limit of the C ABI and of the kernel");
 
 // Whether the items qualify for one grouped launch (bf16 activations with
@@ -891,6 +893,40 @@ int group_nt(const MamboLinearItem* items, int count) {
 }
 
 size_t group_partial_bytes(int nt, int sms) { return align256((size_t)sms * 2 * 128 * 8 * nt * sizeof(float)); }
+
+// Estimated time of one (128-row tile, K block) unit of a grouped launch
+// item with m tokens, in thousandths of a one-token unit: the activation
+// warps' quantization of the unit's bf16 block grows with the token count.
+// Fitted on B200 with Llama-3-8B decode shapes: grouped launches of 1, 2, 4
+// and 8 tokens take 1.00, 1.12, 1.03 and 1.23 times as long per unit, and of
+// the linear costs tried, this one balances the mixed sweep best.
+int64_t group_unit_cost(int m) { return m <= 2 ? 1000 : 1000 + kGroupCostPerToken * (m - 2); }
+
+int64_t group_item_units(const GemvItem& gi) { return (int64_t)((gi.n_rows + 127) / 128) * gi.n_blocks; }
+
+// First unit of each CTA of a grouped launch (start[grid] = units): contiguous
+// ranges of about equal estimated time, at least one unit each (grid <= units).
+void split_group_units(const GemvGroup& g, int units, int grid, int* start) {
+  int64_t total = 0;
+  for (int i = 0; i < g.count; ++i) total += group_item_units(g.items[i]) * group_unit_cost(g.items[i].m);
+  start[0] = 0;
+  int item = 0;
+  int64_t before = 0;  // cost of the units of the items ahead of `item`
+  for (int c = 1; c < grid; ++c) {
+    const int64_t target = total * c / grid;
+    while (item + 1 < g.count &&
+           before + group_item_units(g.items[item]) * group_unit_cost(g.items[item].m) <= target) {
+      before += group_item_units(g.items[item]) * group_unit_cost(g.items[item].m);
+      ++item;
+    }
+    const int64_t cu = group_unit_cost(g.items[item].m);
+    // Rounded down, as a single linear's even split is: a group of one splits the same way.
+    const int64_t u = g.items[item].unit0 + (target - before) / cu;
+    const int64_t lo = start[c - 1] + 1, hi = units - (grid - c);
+    start[c] = (int)(u < lo ? lo : u > hi ? hi : u);
+  }
+  start[grid] = units;
+}
 
 }  // namespace
 
@@ -989,7 +1025,9 @@ int mambo_iq3s_linear_group(const MamboLinearItem* items, int count, const uint3
   p.kparts = 0;
   p.row_tiles = tiles;
   p.total_units = units;
-  const int grid = units < info.sms ? units : info.sms;
+  int grid = units < info.sms ? units : info.sms;
+  if (grid > kGemvMaxGrid) grid = kGemvMaxGrid;
+  split_group_units(g, units, grid, g.cta_start);
   cudaError_t e = launch_gemv_tm_group(p, g, nt, kGroupDecWarps, grid, (cudaStream_t)stream);
   if (e != cudaSuccess) return cuda_fail(e, "iq3s_gemv_tm_kernel (group)");
   return ok();

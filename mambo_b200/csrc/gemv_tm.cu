@@ -165,12 +165,12 @@ __device__ __forceinline__ int group_item(const GemvGroup& g, int u, int l) {
 // contributing CTAs in CTA order and stores it; the partials of CTA `self`
 // come from `acc` (its registers) instead of memory. Loads for several
 // contributors are in flight together.
-// tile: the row tile's number; tile_of(u): the row tile holding unit u.
-template <int TOK, class TileOf>
-__device__ __forceinline__ void sum_partials(const float* partials, int total_units, const OutView& o, int tile,
+// tile: the row tile's number; tile_of(u): the row tile holding unit u;
+// begin_of(c): the first unit of CTA c.
+template <int TOK, class TileOf, class BeginOf>
+__device__ __forceinline__ void sum_partials(const float* partials, BeginOf begin_of, const OutView& o, int tile,
                                              int rl, int row, int self, int c_first, int c_last, TileOf tile_of,
                                              const float (&acc)[TOK]) {
-  const int grid = gridDim.x;
 #pragma unroll
   for (int t0 = 0; t0 < TOK; t0 += 8) {
     float sum[8];
@@ -184,7 +184,7 @@ __device__ __forceinline__ void sum_partials(const float* partials, int total_un
       for (int j = 0; j < kB; ++j) {
         const int c = c0 + j;
         if (c <= c_last && c != self) {
-          const int cs = (tile == tile_of(unit_begin_tm(c, grid, total_units))) ? 0 : 1;
+          const int cs = (tile == tile_of(begin_of(c))) ? 0 : 1;
           const float4* src = reinterpret_cast<const float4*>(partials + ((size_t)(c * 2 + cs) * 128 + rl) * TOK + t0);
           v[j][0] = __ldcg(src);
           v[j][1] = __ldcg(src + 1);
@@ -272,14 +272,33 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // Work range: with kparts > 0 each row tile is split into kparts K ranges,
   // one per CTA of a cluster (rank = K part); otherwise a stream-K range.
+  // Stream-K ranges: a grouped launch takes them from the host's table,
+  // a single linear splits its units evenly.
+  auto unit_begin = [&](int c) -> int {
+    if constexpr (kGroup) return grp.cta_start[c];
+    else return unit_begin_tm(c, gridDim.x, p.total_units);
+  };
+  auto cta_of_unit = [&](int u) -> int {
+    if constexpr (kGroup) {
+      int lo = 0, hi = (int)gridDim.x - 1;  // last CTA whose range starts at or before u
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (grp.cta_start[mid] <= u) lo = mid;
+        else hi = mid - 1;
+      }
+      return lo;
+    } else {
+      return cta_of_unit_tm(u, gridDim.x, p.total_units);
+    }
+  };
   int u0, u1;
   if (p.kparts > 0) {
     const int t = blockIdx.x / p.kparts, k = blockIdx.x % p.kparts;
     u0 = t * p.n_blocks + (int)((int64_t)k * p.n_blocks / p.kparts);
     u1 = t * p.n_blocks + (int)((int64_t)(k + 1) * p.n_blocks / p.kparts);
   } else {
-    u0 = unit_begin_tm(blockIdx.x, gridDim.x, p.total_units);
-    u1 = unit_begin_tm(blockIdx.x + 1, gridDim.x, p.total_units);
+    u0 = unit_begin(blockIdx.x);
+    u1 = unit_begin(blockIdx.x + 1);
   }
   const int n_units = u1 - u0;
   const int S = p.stages;
@@ -876,10 +895,10 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
         // finishes last is usually the last contribution: if every other
         // contributor has already published, sum at once; otherwise publish,
         // and the last to arrive sums (in CTA order either way).
-        const int cta = blockIdx.x, grid = gridDim.x;
+        const int cta = blockIdx.x;
         const int tile_u0 = unit0u + rt * nbu;  // first unit of the row tile
-        const int c_first = cta_of_unit_tm(tile_u0, grid, p.total_units);
-        const int c_last = cta_of_unit_tm(tile_u0 + nbu - 1, grid, p.total_units);
+        const int c_first = cta_of_unit(tile_u0);
+        const int c_last = cta_of_unit(tile_u0 + nbu - 1);
         const int slot_id = (tile == first_tile) ? 0 : 1;
         int* counter = p.counters + (size_t)tile * kEpiWarps + q;
         int last = 0;
@@ -898,7 +917,7 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
         }
         if (last) {
           if (lane == 0) *counter = 0;  // every contributor has arrived: leave it zeroed for the next launch
-          sum_partials<TOK>(p.partials, p.total_units, ou, tile, rl, row, cta, c_first, c_last, tile_of, acc);
+          sum_partials<TOK>(p.partials, unit_begin, ou, tile, rl, row, cta, c_first, c_last, tile_of, acc);
         }
       }
 #pragma unroll

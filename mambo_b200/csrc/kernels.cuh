@@ -176,10 +176,15 @@ struct GemvItem {
   int tile0;  // first row tile of this item in the launch's numbering
 };
 constexpr int kGemvMaxItems = 32;
+constexpr int kGemvMaxGrid = 256;  // CTAs of a grouped launch (one per SM)
 struct GemvGroup {
   CUtensorMap xb[kGemvMaxItems];  // bf16 activation map of each item (box 256 x 8*NT)
   GemvItem items[kGemvMaxItems];
   int count;
+  // First unit of each CTA's stream-K range (cta_start[grid] = all units):
+  // ranges of about equal estimated time, not equal unit counts, since a
+  // unit's cost grows with its item's token count. Strictly increasing.
+  int cta_start[kGemvMaxGrid + 1];
 };
 // The single-linear launch's stand-in for GemvGroup.
 struct GemvNoGroup {
