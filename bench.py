@@ -290,7 +290,7 @@ def prefill_probe(torch, dev, m: int = 2048) -> dict:
     peak, kind = measure_fp8_peak(torch, dev)
     tf = tot_flop / tot_us / 1e6
     return {"m": m, "tflops": tf, "unit": "TFLOP/s", "peak_tflops": peak, "peak_kind": kind,
-            "frac": (tf / peak) if peak else None, "kernel": "iq3s_gemm_tm_kernel (+ iq3s_xs_atoms_kernel)",
+            "frac": (tf / peak) if peak else None, "kernel": "iq3s_gemm_f16_kernel (+ iq3s_x16_kernel: MXFP8 activations to FP16)",
             "l2": "flushed (256 MB write) before each timed launch", "per_shape": rows}
 
 
