@@ -864,8 +864,8 @@ int mambo_iq3s_linear_fused(const void* x, int x_dtype, int64_t ldx, int64_t m, 
 namespace {
 
 constexpr int kGroupDecWarps = 8;
-// Cost of a grouped launch's unit per token beyond two (thousandths of a one-token unit).
-constexpr int64_t kGroupCostPerToken = 40;
+// Cost of a grouped launch's unit per activation pass (thousandths of a one-token unit).
+constexpr int64_t kGroupCostPerPass = 200;
 static_assert(MAMBO_MAX_GROUP == kGemvMaxItems, "group size limit of the C ABI and of the kernel");
 
 // Whether the items qualify for one grouped launch (bf16 activations with
@@ -895,12 +895,12 @@ int group_nt(const MamboLinearItem* items, int count) {
 size_t group_partial_bytes(int nt, int sms) { return align256((size_t)sms * 2 * 128 * 8 * nt * sizeof(float)); }
 
 // Estimated time of one (128-row tile, K block) unit of a grouped launch
-// item with m tokens, in thousandths of a one-token unit: the activation
-// warps' quantization of the unit's bf16 block grows with the token count.
-// Fitted on B200 with Llama-3-8B decode shapes: grouped launches of 1, 2, 4
-// and 8 tokens take 1.00, 1.12, 1.03 and 1.23 times as long per unit, and of
-// the linear costs tried, this one balances the mixed sweep best.
-int64_t group_unit_cost(int m) { return m <= 2 ? 1000 : 1000 + kGroupCostPerToken * (m - 2); }
+// item with m tokens, in thousandths of a one-token unit. It grows with the
+// activation warps' passes over the unit's bf16 block (from two tokens a lane
+// quantizes one 32-value group of four tokens a pass). Measured on B200 with
+// Llama-3-8B decode shapes: grouped launches of 1, 2, 4 and 8 tokens take
+// 1.00, 1.03, 1.03 and 1.23 times as long per unit.
+int64_t group_unit_cost(int m) { return m <= 1 ? 1000 : 830 + kGroupCostPerPass * (int64_t)((m + 3) / 4); }
 
 int64_t group_item_units(const GemvItem& gi) { return (int64_t)((gi.n_rows + 127) / 128) * gi.n_blocks; }
 

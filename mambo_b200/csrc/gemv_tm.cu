@@ -442,8 +442,8 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
     if (fused) {
       // Fused quantization (the standalone quantizer's arithmetic): the bf16
       // box of each K block arrives by TMA, BS units ahead. A lane quantizes
-      // one 32-value group of one token (4 tokens x 8 groups a pass; with 1-2
-      // tokens, four lanes a group), reading its four 16-byte chunks in an
+      // one 32-value group of one token (4 tokens x 8 groups a pass; with one
+      // token, four lanes a group), reading its four 16-byte chunks in an
       // order rotated by token so that each quarter warp hits all banks, and
       // writes the E4M3 bytes straight into
       // the B tile [16-byte K chunk][token][16 bytes], the scale code into
@@ -510,8 +510,9 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
         move_to(qc, j);
         int mq = p.m;
         if constexpr (kGroup) mq = grp.items[qc.l].m;
-        if (mq <= 2) {
-          // Few tokens: four lanes per group (one 16-byte chunk each), a token per pass.
+        if (mq <= 1) {
+          // One token: four lanes per group (one 16-byte chunk each). From two tokens
+          // one lane per group takes fewer passes (two tokens: one pass, not two).
           for (int t = 0; t < mq; ++t) {
             const uint4 c = *reinterpret_cast<const uint4*>(box + t * kBfRowBytes + lane * 16);
             uint2 q;
