@@ -515,11 +515,11 @@ __global__ void __launch_bounds__(kThreadsH, 1)
             float v[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) v[j] = acc[c + i + j] * sc[i + j];
-            // Round 1 (lane ^ 2): lanes 0-1 keep tokens 0-1, lanes 2-3 tokens 2-3.
+            // Exchange step 1 (lane ^ 2): lanes 0-1 keep tokens 0-1, lanes 2-3 tokens 2-3.
             const float a0 = hi2 ? v[2] : v[0], a1 = hi2 ? v[3] : v[1];
             const float r0 = __shfl_xor_sync(0xFFFFFFFFu, hi2 ? v[0] : v[2], 2);
             const float r1 = __shfl_xor_sync(0xFFFFFFFFu, hi2 ? v[1] : v[3], 2);
-            // Round 2 (lane ^ 1): even lanes keep the first of their two tokens.
+            // Exchange step 2 (lane ^ 1): even lanes keep the first of their two tokens.
             const float g0 = __shfl_xor_sync(0xFFFFFFFFu, qodd ? a0 : a1, 1);  // row L^1
             const float g1 = __shfl_xor_sync(0xFFFFFFFFu, qodd ? r0 : r1, 1);  // row L^3
             const float own = qodd ? a1 : a0, own2 = qodd ? r1 : r0;           // rows L, L^2
