@@ -165,3 +165,25 @@ def test_tensor_parallel_local_group_matches_separate_shards(cuda_device):
         assert y.shape == one.shape
         err = (torch.linalg.norm(y.double() - one.double()) / torch.linalg.norm(one.double())).item()
         assert err < 1e-5, err
+
+
+def test_time_balanced_split_with_unequal_items(cuda_device):
+    """Items from 1 to 31 tokens: the launch cuts stream-K ranges by estimated time, so CTAs
+    get very different unit counts and some ranges lie inside one row tile. Every item must
+    still match its own launch, and repeated launches must agree bit for bit."""
+    shapes = [(1, 1024, 2048), (31, 512, 1024), (2, 2048, 1024), (17, 256, 3072),
+              (5, 1536, 512), (31, 768, 2048), (1, 136, 256), (9, 1024, 1024)]
+    raws, ws, xs = [], [], []
+    for i, (m, n, k) in enumerate(shapes):
+        raw, w = _weight(cuda_device, n, k, seed=900 + i)
+        raws.append(raw)
+        ws.append(w)
+        xs.append(_x(cuda_device, m, k, seed=950 + i))
+    a = iq3_s_fp8_linear_group(xs, ws, out_dtype=torch.float32)
+    b = iq3_s_fp8_linear_group(xs, ws, out_dtype=torch.float32)
+    for x, w, raw, ya, yb in zip(xs, ws, raws, a, b):
+        assert torch.equal(ya, yb)
+        one = iq3_s_fp8_linear(x, w, out_dtype=torch.float32)
+        assert O.relative_frobenius(ya.cpu().numpy(), one.cpu().numpy().astype(np.float64)) < 1e-5
+    for i in (1, 6):
+        assert O.relative_frobenius(a[i].cpu().numpy(), _oracle(xs[i], raws[i])) < ORACLE_FROB_TOL
