@@ -808,7 +808,7 @@ def main() -> None:
     # own H2D copy of the step's inputs and D2H read of its outputs, on a copy
     # stream that overlaps them with the neighbouring steps' linears (two
     # device buffer sets).
-    PIPE = 4
+    PIPE = 8
     copy_stream = torch.cuda.Stream(dev)
     sets = [(dev_in_all, dev_out_all, e2e_x, e2e_o)]
     di2, do2 = torch.empty_like(dev_in_all), torch.empty_like(dev_out_all)
@@ -913,7 +913,7 @@ def main() -> None:
                 "ms_per_step": e2e_ms,
                 "execution": "per step: one H2D copy of all the step's inputs, one public-API call "
                              "(group_linear_into, 20 linears into views of one output buffer), one D2H copy of "
-                             "all outputs; CUDA graphs of 4 such steps pipelined over a copy stream and two "
+                             f"all outputs; CUDA graphs of {PIPE} such steps pipelined over a copy stream and two "
                              "device buffer sets (copies overlap the neighbouring steps' linears)",
                 "serial_ms_per_step": e2e_serial_ms,
                 "serial_value": alg * world / (e2e_serial_ms * 1e-3) / 1e9,
