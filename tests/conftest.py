@@ -35,3 +35,29 @@ def cuda_device():
     if (major, minor) != (10, 0):
         pytest.fail(f"GPU tests need an sm_100 device, found sm{major}{minor}")
     return torch.device("cuda", 0)
+
+
+@pytest.fixture(scope="session")
+def write_gguf():
+    """Writes a GGUF v3 file with gguf-py's writer: ``write_gguf(path, {name: (array, type)})``.
+
+    ``type`` is a ``gguf.GGMLQuantizationType`` name ("IQ3_S", "F32", ...). A
+    quantized tensor is given as its packed bytes ``uint8 [rows, row_bytes]``.
+    """
+    def write(path, tensors):
+        from gguf import GGMLQuantizationType, GGUFWriter
+
+        writer = GGUFWriter(str(path), "llama")
+        for name, (array, type_name) in tensors.items():
+            qtype = GGMLQuantizationType[type_name]
+            if qtype in (GGMLQuantizationType.F32, GGMLQuantizationType.F16):
+                writer.add_tensor(name, array)
+            else:
+                writer.add_tensor(name, array, raw_dtype=qtype)
+        writer.write_header_to_file()
+        writer.write_kv_data_to_file()
+        writer.write_tensors_to_file()
+        writer.close()
+        return path
+
+    return write
