@@ -9,7 +9,7 @@
  * Each declaration cites the reference interface it replaces (paths relative
  * to the Menooker/Mambo tree). The reference launches cuTile kernels from
  * Python through CuPy; these functions are what its launch wrappers
- * (src/python/mambo/kernels/*.py) bind to in this build.
+ * (the modules in src/python/mambo/kernels) bind to in this build.
  */
 #ifndef MAMBO_B200_H
 #define MAMBO_B200_H
