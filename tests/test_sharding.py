@@ -97,3 +97,46 @@ def test_two_rank_linear_matches_unsharded(mode, input_sharded):
         xq, xs = O.quantize_mxfp8(x)
         ref = O.iq3s_linear_f64(xq, xs, raw)
         assert O.relative_frobenius(got.astype(np.float64), ref) < 1e-6
+
+
+def _rank_group_main(rank, world, port, path):
+    from mambo_b200.sharding import local_group
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=__import__("datetime").timedelta(seconds=60))
+    try:
+        fakes = dict(prepare=_oracle_prepare, quantize=_oracle_quantize, linear=_oracle_linear)
+        gate = TensorParallelIQ3SLinear(torch.from_numpy(O.make_synthetic_iq3s(128, 1024, 21)), COLUMN,
+                                        out_dtype=torch.float32, **fakes)
+        up = TensorParallelIQ3SLinear(torch.from_numpy(O.make_synthetic_iq3s(64, 1024, 22)), COLUMN,
+                                      out_dtype=torch.float32, **fakes)
+        down = TensorParallelIQ3SLinear(torch.from_numpy(O.make_synthetic_iq3s(64, 1024, 23)), ROW,
+                                        out_dtype=torch.float32, **fakes)
+        x = torch.from_numpy(np.random.default_rng(9).standard_normal((5, 1024)).astype(np.float32))
+        g, u = local_group([gate, up], x)
+        assert g.shape == (5, 64) and u.shape == (5, 32)
+        # A row shard in a group runs its own local(): the FP32 partial of its K slice.
+        (d,) = local_group([down], x)
+        assert torch.equal(d, down.local(x))
+        with pytest.raises(ValueError):
+            local_group([gate, up], x[:, :512])
+        if rank == 0:
+            np.savez(path, gate=gate.combine(g).numpy(), up=up.combine(u).numpy())
+        else:
+            gate.combine(g)
+            up.combine(u)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_local_group_matches_unsharded():
+    """Column shards that share an activation through local_group, then each shard's combine()."""
+    with tempfile.TemporaryDirectory() as tmp:
+        path = os.path.join(tmp, "y.npz")
+        mp.spawn(_rank_group_main, args=(2, _free_port(), path), nprocs=2, join=True)
+        got = dict(np.load(path))
+    x = np.random.default_rng(9).standard_normal((5, 1024)).astype(np.float32)
+    xq, xs = O.quantize_mxfp8(x)
+    for name, n, seed in (("gate", 128, 21), ("up", 64, 22)):
+        ref = O.iq3s_linear_f64(xq, xs, O.make_synthetic_iq3s(n, 1024, seed))
+        np.testing.assert_array_equal(got[name], ref.astype(np.float32))
