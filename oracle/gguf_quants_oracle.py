@@ -71,14 +71,18 @@ def q4_k_scales_mins(b: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
     return s, m
 
 
-def dequantize_q4_k(raw: np.ndarray) -> np.ndarray:
-    """Q4_K blocks (any shape whose bytes are whole 144-byte blocks) -> float32 [blocks * 256]."""
+def dequantize_q4_k(raw: np.ndarray, dtype=np.float32) -> np.ndarray:
+    """Q4_K blocks (any shape whose bytes are whole 144-byte blocks) -> ``dtype`` [blocks * 256].
+
+    float32 rounds each weight as gguf-py and ggml do; float64 is exact (fp16
+    scales times 6-bit and 4-bit integers).
+    """
     blk = _blocks(raw, Q4_K_BLOCK_BYTES)
-    d, dmin = _f16(blk, 0), _f16(blk, 2)
+    d, dmin = _f16(blk, 0).astype(dtype), _f16(blk, 2).astype(dtype)
     s, m = q4_k_scales_mins(blk[:, 4:16])
-    q = _nibbles(blk[:, 16:144], 32).reshape(-1, 8, 32).astype(np.float32)
-    scale = (d * s.astype(np.float32))[:, :, None]
-    offset = (dmin * m.astype(np.float32))[:, :, None]
+    q = _nibbles(blk[:, 16:144], 32).reshape(-1, 8, 32).astype(dtype)
+    scale = (d * s.astype(dtype))[:, :, None]
+    offset = (dmin * m.astype(dtype))[:, :, None]
     return (scale * q - offset).reshape(-1)
 
 
@@ -108,3 +112,33 @@ def dequantize_iq4_xs(raw: np.ndarray) -> np.ndarray:
     idx = _nibbles(blk[:, 8:136], 16).reshape(-1, 8, 32)
     v = iq4_nl_values()[idx].astype(np.float32)
     return (dl[:, :, None] * v).reshape(-1)
+
+
+def q4_k_linear_f64(x: np.ndarray, raw: np.ndarray) -> np.ndarray:
+    """Direct reference: float64 ``x [M, K] @ W.T`` with the exact (float64) weights of raw [N, K/256, 144]."""
+    n = raw.shape[0]
+    w = dequantize_q4_k(raw, np.float64).reshape(n, -1)
+    return np.asarray(x, dtype=np.float64) @ w.T
+
+
+def q4_k_linear_group_decomposed(x: np.ndarray, raw: np.ndarray) -> np.ndarray:
+    """The same product as the FP8 GEMV skeleton would form it, in float64.
+
+    Per 32-value group g of row r: P = sum x * code (the codes 0..15 are exact
+    E4M3 operands, so this is the tensor core's group partial), then
+    out += d*s_g * P - dmin*m_g * sum x (the epilogue, with the activation's
+    group sums from the quantizing warps).
+    """
+    x = np.asarray(x, dtype=np.float64)
+    m_tokens, k = x.shape
+    blk = _blocks(raw, Q4_K_BLOCK_BYTES)  # [N * K/256, 144]
+    n = raw.shape[0]
+    d, dmin = _f16(blk, 0).astype(np.float64), _f16(blk, 2).astype(np.float64)
+    s, mn = q4_k_scales_mins(blk[:, 4:16])
+    codes = _nibbles(blk[:, 16:144], 32).reshape(n, k // 32, 32).astype(np.float64)
+    scale = (d * s).reshape(n, k // 32)            # d * s_g per (row, group)
+    offset = (dmin * mn).reshape(n, k // 32)       # dmin * m_g per (row, group)
+    xg = x.reshape(m_tokens, k // 32, 32)
+    partial = np.einsum("tgj,rgj->trg", xg, codes)  # tensor-core group partials
+    xsum = xg.sum(axis=2)                            # [M, K/32] activation group sums
+    return np.einsum("trg,rg->tr", partial, scale) - xsum @ offset.T

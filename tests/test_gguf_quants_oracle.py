@@ -62,3 +62,21 @@ def test_partial_blocks_are_rejected():
         G.dequantize_q4_k(np.zeros(G.Q4_K_BLOCK_BYTES + 1, dtype=np.uint8))
     with pytest.raises(ValueError):
         G.dequantize_iq4_xs(np.zeros(G.IQ4_XS_BLOCK_BYTES - 1, dtype=np.uint8))
+
+
+def test_q4_k_group_decomposition_equals_the_direct_product():
+    """The planned Q4_K kernel arithmetic (exact E4M3 codes, per-group scale and the
+    min term through the activation's group sums) gives the dequantized product."""
+    from oracle import iq3s_oracle as O
+
+    rng = np.random.default_rng(0x4D)
+    raw = _blocks(rng, 64 * 4, G.Q4_K_BLOCK_BYTES, 2).reshape(64, 4, G.Q4_K_BLOCK_BYTES)
+    x = rng.standard_normal((6, 1024)).astype(np.float32)
+    xq, xs = O.quantize_mxfp8(x)
+    xe = O.decode_mxfp8(xq, xs)  # the MXFP8 activations the kernel multiplies
+    direct = G.q4_k_linear_f64(xe, raw)
+    split = G.q4_k_linear_group_decomposed(xe, raw)
+    assert O.relative_frobenius(split, direct) < 1e-12
+    # gguf-py's float32 weights round each value: the same product within float32 rounding.
+    w32 = G.dequantize_q4_k(raw).reshape(64, -1).astype(np.float64)
+    assert O.relative_frobenius(xe.astype(np.float64) @ w32.T, direct) < 1e-7
