@@ -142,3 +142,21 @@ def q4_k_linear_group_decomposed(x: np.ndarray, raw: np.ndarray) -> np.ndarray:
     partial = np.einsum("tgj,rgj->trg", xg, codes)  # tensor-core group partials
     xsum = xg.sum(axis=2)                            # [M, K/32] activation group sums
     return np.einsum("trg,rg->tr", partial, scale) - xsum @ offset.T
+
+
+def iq4_xs_linear_group_decomposed(x: np.ndarray, raw: np.ndarray) -> np.ndarray:
+    """IQ4_XS product as an FP16-operand kernel would form it, in float64.
+
+    The operand is the table value itself (an integer of magnitude <= 127, exact
+    in FP16, not always in E4M3); per 32-value group g of row r: P = sum x * value,
+    then out += d*(l_g - 32) * P in the epilogue.
+    """
+    x = np.asarray(x, dtype=np.float64)
+    m_tokens, k = x.shape
+    n = raw.shape[0]
+    blk = _blocks(raw, IQ4_XS_BLOCK_BYTES)
+    operand = iq4_nl_values().astype(np.float16)[_nibbles(blk[:, 8:136], 16)]  # FP16 operands
+    operand = operand.reshape(n, k // 32, 32).astype(np.float64)
+    scale = (_f16(blk, 0).astype(np.float64) * (iq4_xs_scales(blk) - 32)).reshape(n, k // 32)
+    partial = np.einsum("tgj,rgj->trg", x.reshape(m_tokens, k // 32, 32), operand)
+    return np.einsum("trg,rg->tr", partial, scale)

@@ -80,3 +80,15 @@ def test_q4_k_group_decomposition_equals_the_direct_product():
     # gguf-py's float32 weights round each value: the same product within float32 rounding.
     w32 = G.dequantize_q4_k(raw).reshape(64, -1).astype(np.float64)
     assert O.relative_frobenius(xe.astype(np.float64) @ w32.T, direct) < 1e-7
+
+
+def test_iq4_xs_fp16_operands_are_exact_and_the_decomposition_holds():
+    from oracle import iq3s_oracle as O
+
+    values = G.iq4_nl_values().astype(np.float64)
+    assert np.array_equal(values.astype(np.float16).astype(np.float64), values)
+    rng = np.random.default_rng(0x4E)
+    raw = _blocks(rng, 32 * 4, G.IQ4_XS_BLOCK_BYTES, 1).reshape(32, 4, G.IQ4_XS_BLOCK_BYTES)
+    x = rng.standard_normal((5, 1024))
+    direct = x @ G.dequantize_iq4_xs(raw).reshape(32, -1).astype(np.float64).T
+    assert O.relative_frobenius(G.iq4_xs_linear_group_decomposed(x, raw), direct) < 1e-12
