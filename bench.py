@@ -1,26 +1,39 @@
 """Benchmark of the IQ3_S x MXFP8 linear path on B200 (driver contract: one JSON line on rank 0).
 
-Workload ("decode GEMV sweep"): Llama-3-8B projection
-shapes -- QKV 4096->6144, O 4096->4096, gate 4096->14336, up 4096->14336,
-down 14336->4096 -- at M in {1, 2, 4, 8}. Each M uses its own layer of
-seeded random IQ3_S weights, so one step streams 4 x 93.7 MB = 375 MB of
-weights (larger than the 126 MB L2: no flush needed). A step runs, for each
-M, the layer's 5 linears through the fused path (bf16 activations ->
-MXFP8 quantization -> IQ3_S x MXFP8 GEMV -> bf16 output), captured once in
-a CUDA graph and replayed.
+Headline workload ("decode GEMV sweep"): Llama-3-8B
+projection shapes -- QKV 4096->6144, O 4096->4096, gate 4096->14336, up
+4096->14336, down 14336->4096 -- at M in {1, 2, 4, 8}. Each M uses its own
+layer of seeded random IQ3_S weights, so one step streams 4 x 93.7 MB =
+375 MB of weights (larger than the 126 MB L2: no flush needed). A step runs,
+for each M, the layer's 5 linears through the fused path (bf16 activations ->
+MXFP8 quantization -> IQ3_S x MXFP8 GEMV -> bf16 output), captured once in a
+CUDA graph and replayed.
 
 value  = algorithmic bytes per step (weights + bf16 activations in + bf16 out)
          / device time per step, GB/s, summed over ranks (weak scaling: every
-         rank runs the full workload on its own weights; the path does not
-         shard at this size, so N > 1 runs independent replicas).
+         rank runs the full sweep on its own weights).
 e2e    = the same step through the public API with pinned host buffers:
          host->device copy of the step's activations, the linears, and a
          device->host copy of the outputs, all inside the timed region.
 roofline = the GEMV kernel alone: algorithmic bytes per launch / mean CUDA-event
          duration of a launch, against MEASURED_PEAKS.json's HBM copy bandwidth.
 
-``--impl reference`` times the reference's CPU path (the C restatement of its
-IQ3_S decode + MXFP8 codec + float64 dot, oracle/iq3s_ref.c) on this host.
+Further blocks of the same JSON line:
+tp      = BASELINE config 5 at every N: one Llama-3-70B layer's linears
+          tensor-parallel over the launched ranks (column split QKV/gate/up,
+          row split O/down, NCCL all-reduce), M in {1, 64, 4096}, with the
+          sharded outputs checked against the unsharded linear on rank 0.
+prefill = BASELINE config 3 (N = 1): bf16 activations with 1 % outlier
+          columns -> quantization -> GEMM -> bf16 output, all inside the timed
+          region, M in {512, 2048, 8192}, TFLOP/s against an FP8 peak measured
+          in the same run.
+model   = BASELINE config 4 (N = 1): every linear of a 32-layer Llama-3-8B,
+          one 4096-token prefill + 128 decode steps at batch 8.
+cpu_baseline = the reference's CPU path on BASELINE config 1 (N = 1).
+
+``--impl reference`` times the reference's CPU path on BASELINE config 1 (the
+O projection shape at M = 16): gguf-py's IQ3_S dequantize, the reference test
+oracle's MXFP8 codec (restated in oracle/iq3s_oracle.py) and an fp32 matmul.
 """
 
 from __future__ import annotations
@@ -58,20 +71,6 @@ def load_peaks() -> tuple[float, str]:
         except (KeyError, ValueError):
             pass
     return HBM_FALLBACK_GBS, "fallback"
-
-
-def read_profiled_traffic(key: str = "dram_bytes_per_launch"):
-    """DRAM bytes per GEMV launch from the committed ncu summary (a line '<key>: N')."""
-    path = ROOT / "profiles" / "iq3s_gemv_tm_decode_llama3_8b.md"
-    if not path.is_file():
-        return None
-    for line in path.read_text().splitlines():
-        if line.strip().startswith(key + ":"):
-            try:
-                return float(line.split(":", 1)[1].split()[0])
-            except (ValueError, IndexError):
-                return None
-    return None
 
 
 def layer_bytes() -> int:
@@ -141,9 +140,87 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------
-# CPU baseline (the reference's CPU path, restated in C)
+# CPU baselines (the reference's CPU path)
 # ---------------------------------------------------------------------------
-def cpu_baseline(budget_s: float = 15.0) -> dict:
+CONFIG1 = (16, 4096, 4096)  # M, N, K (the O projection shape)
+
+
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def cpu_stock_step(raw, x) -> dict:
+    """One pass of the reference's CPU path on [M,K] activations and [N,K/256,110] IQ3_S blocks.
+
+    gguf-py's ``dequantize`` (the installed gguf package: the decoder the
+    reference's tests call, tests/python/utils/compute_reference_gguf.py:80-100),
+    the reference test oracle's MXFP8 codec ``encode_mxfp8_reference`` /
+    ``decode_mxfp8`` (tests/python/utils/fp8_reference.py:64-86, restated in
+    oracle/iq3s_oracle.py: nearest value, ties to the smaller magnitude), and
+    an fp32 torch.matmul of the decoded operands on all host threads
+    (compute_reference_gguf.py:111-121 multiplies them).
+    """
+    import numpy as np
+    import torch
+    from gguf import GGMLQuantizationType
+    from gguf.quants import dequantize
+
+    from oracle import iq3s_oracle as O
+
+    n = raw.shape[0]
+    t0 = time.perf_counter()
+    w = dequantize(raw.reshape(n, -1), GGMLQuantizationType.IQ3_S)
+    t1 = time.perf_counter()
+    q, sc = O.quantize_mxfp8(x, rounding="ties_down")
+    xd = O.decode_mxfp8(q, sc)
+    t2 = time.perf_counter()
+    y = torch.from_numpy(np.ascontiguousarray(xd)) @ torch.from_numpy(np.ascontiguousarray(w, dtype=np.float32)).T
+    t3 = time.perf_counter()
+    assert y.shape == (x.shape[0], n)
+    return {"dequant_s": t1 - t0, "quant_s": t2 - t1, "matmul_s": t3 - t2, "total_s": t3 - t0}
+
+
+def config1_inputs():
+    import numpy as np
+
+    from oracle import iq3s_oracle as O
+
+    m, n, k = CONFIG1
+    raw = O.make_synthetic_iq3s(n, k, seed=0x1A3)
+    x = np.random.default_rng(20261017).standard_normal((m, k)).astype(np.float32)
+    return raw, x
+
+
+def config1_bytes() -> int:
+    m, n, k = CONFIG1
+    return n * (k // 256) * 110 + m * k * 2 + m * n * 2
+
+
+def cpu_baseline_stock(reps: int = 2) -> dict:
+    import torch
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    raw, x = config1_inputs()
+    runs = [cpu_stock_step(raw, x) for _ in range(reps)]
+    best = min(runs, key=lambda r: r["total_s"])
+    m, n, k = CONFIG1
+    return {"value": config1_bytes() / best["total_s"] / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+            "cpu_model": cpu_model(),
+            "sample": f"BASELINE config 1 (M={m}, N={n}, K={k}) through the reference's CPU path: gguf-py "
+                      f"dequantize (single thread), the reference test oracle's MXFP8 codec (restated), fp32 "
+                      f"torch.matmul on {threads} threads; best of {reps}",
+            "seconds": {k2: round(v, 4) for k2, v in best.items()}}
+
+
+def cpu_baseline_c_port(budget_s: float = 15.0) -> dict:
+    """The same path restated in C (oracle/iq3s_ref.c: decode + MXFP8 + float64 dot, all host threads)."""
     import numpy as np
 
     from oracle import c_oracle
@@ -171,26 +248,42 @@ def cpu_baseline(budget_s: float = 15.0) -> dict:
                       f"float64 dot), {threads} host threads, {t:.2f} s"}
 
 
+def cpu_baseline() -> dict:
+    stock = cpu_baseline_stock()
+    stock["c_port"] = cpu_baseline_c_port()
+    return stock
+
+
 def run_reference(args) -> None:
+    """The reference arm: its CPU path on BASELINE config 1, one pass per step (rank 0 only)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    budget = max(0.5, 60.0 / max(1, args.steps + args.warmup))
-    res = None
+    import torch
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    raw, x = config1_inputs()
     for _ in range(args.warmup):
-        cpu_baseline(budget)
+        cpu_stock_step(raw, x)
     t0 = time.perf_counter()
-    vals = [cpu_baseline(budget) for _ in range(args.steps)]
+    runs = [cpu_stock_step(raw, x) for _ in range(args.steps)]
     wall = time.perf_counter() - t0
-    res = vals[-1]
-    value = statistics.mean(v["value"] for v in vals)
+    value = config1_bytes() * args.steps / wall / 1e9
+    m, n, k = CONFIG1
+    sample = (f"BASELINE config 1 (M={m}, N={n}, K={k}: the O projection of the decode sweep) per step: gguf-py "
+              f"dequantize, the reference test oracle's MXFP8 codec (restated), fp32 torch.matmul on {threads} "
+              f"threads")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": wall * 1000 / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
-        "data": "synthetic", "config": {"workload": "decode_gemv_sweep_llama3_8b (bounded CPU sample)",
-                                        "sample": res["sample"]},
-        "cpu_baseline": {**res, "value": value},
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": {"workload": "decode_gemv_sweep_llama3_8b (bounded CPU sample: BASELINE "
+                                                    "config 1)", "sample": sample},
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample,
+                         "cpu_model": cpu_model(),
+                         "seconds_per_step": {key: round(statistics.mean(r[key] for r in runs), 4)
+                                              for key in ("dequant_s", "quant_s", "matmul_s", "total_s")}},
         "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -247,51 +340,84 @@ def measure_fp8_peak(torch, dev) -> tuple[float | None, str]:
         return None, f"unavailable ({type(ex).__name__})"
 
 
-def prefill_probe(torch, dev, m: int = 2048) -> dict:
-    """The tcgen05 GEMM at M=2048 on the Llama-3-8B shapes (bf16 N(0,1) activations with
-    1% of K columns x50): device time per launch with L2 flushed before each, TFLOP/s against an FP8 peak."""
-    from mambo_b200.kernels.iq3_s_fp8 import linear_into, select_config
+PREFILL_SHAPES = (("qkv", 6144, 4096), ("o", 4096, 4096), ("gate_up", 14336, 4096), ("down", 4096, 14336))
+PREFILL_MS = (512, 2048, 8192)
+
+
+def prefill_block(torch, dev, ms=PREFILL_MS) -> dict:
+    """the Llama-3-8B shapes at prefill M, bf16 N(0,1) activations with 1 % of K columns x50.
+
+    Timed per launch with L2 flushed before each: the whole path from bf16
+    activations to the bf16 output through the public call (fused_linear_into:
+    activation quantization, then the tcgen05 GEMM), and the GEMM alone on
+    activations quantized beforehand.
+    """
+    from mambo_b200.kernels.iq3_s_fp8 import fused_linear_into, linear_into, select_config
     from mambo_b200.kernels.quantize_fp8 import launch_quantize_fp8
     from mambo_b200.utils.iq3_s_weight import prepare_iq3_s_fields
 
-    shapes = (("qkv", 6144, 4096), ("o", 4096, 4096), ("gate_up", 14336, 4096), ("down", 4096, 14336))
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
-    rows, tot_flop, tot_us = [], 0, 0.0
-    for i, (name, n, k) in enumerate(shapes):
+
+    def timed(fn, reps=5) -> float:
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize(dev)
+        us = []
+        for _ in range(reps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize(dev)
+            us.append(e0.elapsed_time(e1) * 1000)
+        return statistics.median(us)
+
+    weights = []
+    for i, (name, n, k) in enumerate(PREFILL_SHAPES):
         gen = torch.Generator(device=dev).manual_seed(0x51A + i)
         raw = torch.randint(0, 256, (n, k // 256, 110), dtype=torch.uint8, device=dev, generator=gen)
         d = (torch.rand((n, k // 256), device=dev, generator=gen) * 9e-3 + 1e-3).half()
         raw[..., :2] = d.view(torch.uint8).view(n, k // 256, 2)
-        fields = prepare_iq3_s_fields(raw)
+        weights.append(prepare_iq3_s_fields(raw))
         del raw, d
-        x = torch.randn((m, k), device=dev, generator=gen)
-        x[:, torch.randperm(k, device=dev, generator=gen)[: round(0.01 * k)]] *= 50.0
-        xq, xs = launch_quantize_fp8(x.to(torch.bfloat16))
-        out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
-        cfg = select_config(m, n, k, dev)
-        for _ in range(3):
-            linear_into(xq, xs, fields, out, config=cfg)
-        torch.cuda.synchronize(dev)
-        us = []
-        for _ in range(5):
-            flush.zero_()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            linear_into(xq, xs, fields, out, config=cfg)
-            e1.record()
-            torch.cuda.synchronize(dev)
-            us.append(e0.elapsed_time(e1) * 1000)
-        t = statistics.median(us)
-        flop = 2 * m * n * k
-        rows.append({"proj": name, "n": n, "k": k, "us": round(t, 1), "tflops": round(flop / t / 1e6, 1)})
-        tot_flop += flop
-        tot_us += t
-        del fields, x, xq, xs, out
+    per_m = []
+    for m in ms:
+        rows, flop_tot, us_tot, gemm_us_tot = [], 0, 0.0, 0.0
+        for i, (name, n, k) in enumerate(PREFILL_SHAPES):
+            gen = torch.Generator(device=dev).manual_seed(0x51A + 100 * i + m)
+            x = torch.randn((m, k), device=dev, generator=gen)
+            x[:, torch.randperm(k, device=dev, generator=gen)[: round(0.01 * k)]] *= 50.0
+            xb = x.to(torch.bfloat16)
+            del x
+            out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+            fields = weights[i]
+            us = timed(lambda: fused_linear_into(xb, fields, out))
+            xq, xs = launch_quantize_fp8(xb)
+            cfg = select_config(m, n, k, dev)
+            gemm_us = timed(lambda: linear_into(xq, xs, fields, out, config=cfg))
+            flop = 2 * m * n * k
+            rows.append({"proj": name, "n": n, "k": k, "us": round(us, 1), "tflops": round(flop / us / 1e6, 1),
+                         "gemm_us": round(gemm_us, 1), "gemm_tflops": round(flop / gemm_us / 1e6, 1)})
+            flop_tot += flop
+            us_tot += us
+            gemm_us_tot += gemm_us
+            del xb, xq, xs, out
+        per_m.append({"m": m, "tflops": flop_tot / us_tot / 1e6, "gemm_tflops": flop_tot / gemm_us_tot / 1e6,
+                      "per_shape": rows})
+    del weights, flush
+    torch.cuda.empty_cache()
     peak, kind = measure_fp8_peak(torch, dev)
-    tf = tot_flop / tot_us / 1e6
-    return {"m": m, "tflops": tf, "unit": "TFLOP/s", "peak_tflops": peak, "peak_kind": kind,
-            "frac": (tf / peak) if peak else None, "kernel": "iq3s_gemm_f16_kernel (+ iq3s_x16_kernel: MXFP8 activations to FP16)",
-            "l2": "flushed (256 MB write) before each timed launch", "per_shape": rows}
+    for r in per_m:
+        r["frac"] = r["tflops"] / peak if peak else None
+        r["gemm_frac"] = r["gemm_tflops"] / peak if peak else None
+    head = next(r for r in per_m if r["m"] == 2048) if 2048 in ms else per_m[0]
+    return {"m": head["m"], "tflops": head["tflops"], "unit": "TFLOP/s", "peak_tflops": peak, "peak_kind": kind,
+            "frac": head["frac"], "per_m": per_m,
+            "timed": "tflops: bf16 activations -> MXFP8 quantization -> GEMM -> bf16 output, one public call "
+                     "(fused_linear_into) per shape; gemm_tflops: the GEMM alone on prequantized activations",
+            "kernel": "iq3s_gemm_f16_kernel (FP16 operands, group scale folded exactly into the weights)",
+            "l2": "flushed (256 MB write) before each timed launch"}
 
 
 def run_single(args) -> None:
@@ -345,7 +471,7 @@ def run_group_profile() -> None:
 LLAMA3_8B_LAYERS = 32
 
 
-def run_llama3_8b(args) -> None:
+def model_block(torch, dev, warmup: int = 3) -> dict:
     """every linear of a 32-layer Llama-3-8B-shaped model (random IQ3_S
     weights): one 4096-token prefill, then 128 decode steps at batch 8; linear time only.
 
@@ -356,13 +482,9 @@ def run_llama3_8b(args) -> None:
     then the FP16-operand GEMM). Activations are fixed random bf16 buffers of
     each linear's shape (no attention or MLP math in between).
     """
-    import torch
-
     from mambo_b200.kernels.iq3_s_fp8 import fused_linear_into, group_linear_into
     from mambo_b200.utils.iq3_s_weight import prepare_iq3_s_fields
 
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
     prefill_m, decode_m, decode_steps = 4096, 8, 128
     layers = []
     for li in range(LLAMA3_8B_LAYERS):
@@ -413,7 +535,7 @@ def run_llama3_8b(args) -> None:
 
     def timed(g, reps):
         with torch.cuda.stream(stream):
-            for _ in range(args.warmup):
+            for _ in range(warmup):
                 g.replay()
         torch.cuda.synchronize(dev)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -425,32 +547,44 @@ def run_llama3_8b(args) -> None:
         torch.cuda.synchronize(dev)
         return e0.elapsed_time(e1) / reps
 
-    with ClockSampler(0) as clocks:
+    with ClockSampler(dev.index or 0) as clocks:
         prefill_ms = timed(g_prefill, 3)
         decode_ms = timed(g_decode, decode_steps)
+    del g_prefill, g_decode, layers
+    torch.cuda.empty_cache()
     w_bytes = layer_bytes() * LLAMA3_8B_LAYERS
     flops = 2.0 * prefill_m * sum(n * k for _, n, k in PROJECTIONS) * LLAMA3_8B_LAYERS
     dec_bytes = w_bytes + LLAMA3_8B_LAYERS * sum(decode_m * (k + n) * 2 for _, n, k in PROJECTIONS)
     peak, peak_kind = load_peaks()
     total_ms = prefill_ms + decode_steps * decode_ms
-    print(json.dumps({
-        "metric": "Llama-3-8B linear layers (32 layers): 4096-token prefill + 128 decode steps at batch 8, linear time",
-        "value": total_ms, "unit": "ms", "n_gpus": 1, "higher_is_better": False, "dtype": "e4m3",
-        "data": "synthetic (random IQ3_S weights, bf16 N(0,1) activations)",
-        "config": {"workload": "llama3_8b_linears (BASELINE config 4)", "layers": LLAMA3_8B_LAYERS,
-                   "prefill_tokens": prefill_m, "decode_batch": decode_m, "decode_steps": decode_steps,
-                   "weights_bytes": w_bytes,
-                   "decode_step": "per layer: QKV, O, grouped gate+up, down (4 launches), one CUDA graph per step",
-                   "prefill": "per linear: fused MXFP8 quantization + FP16-operand GEMM, one CUDA graph"},
+    return {
+        "workload": "llama3_8b_linears (BASELINE config 4)", "layers": LLAMA3_8B_LAYERS,
+        "prefill_tokens": prefill_m, "decode_batch": decode_m, "decode_steps": decode_steps,
+        "weights_bytes": w_bytes, "total_ms": total_ms,
+        "decode_step": "per layer: QKV, O, grouped gate+up, down (4 launches), one CUDA graph per step",
+        "prefill_exec": "per linear: fused MXFP8 quantization + FP16-operand GEMM, one CUDA graph",
         "prefill": {"ms": prefill_ms, "tflops": flops / (prefill_ms * 1e-3) / 1e12},
         "decode": {"ms_per_step": decode_ms, "gbs": dec_bytes / (decode_ms * 1e-3) / 1e9,
-                   "hbm_frac": dec_bytes / (decode_ms * 1e-3) / 1e9 / peak, "peak_gbs": peak, "peak_kind": peak_kind,
-                   "launches_per_step": 4 * LLAMA3_8B_LAYERS},
+                   "hbm_frac": dec_bytes / (decode_ms * 1e-3) / 1e9 / peak, "peak_gbs": peak,
+                   "peak_kind": peak_kind, "launches_per_step": 4 * LLAMA3_8B_LAYERS},
         "clocks": clocks.summary(),
-    }), flush=True)
+    }
 
 
-TP70B_GROUPS = (("qkv",), ("o",), ("gate", "up"), ("down",))  # launches per layer, in a model's order
+def run_llama3_8b(args) -> None:
+    """--workload llama3_8b: the model block alone, as its own JSON line."""
+    import torch
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    r = model_block(torch, dev, warmup=args.warmup)
+    print(json.dumps({
+        "metric": "Llama-3-8B linear layers (32 layers): 4096-token prefill + 128 decode steps at batch 8, linear time",
+        "value": r["total_ms"], "unit": "ms", "n_gpus": 1, "higher_is_better": False, "dtype": "e4m3",
+        "data": "synthetic (random IQ3_S weights, bf16 N(0,1) activations)", "config": {"workload": r["workload"]},
+        **r}), flush=True)
+
+
 TP70B = (  # name, N, K, split (Llama-3-70B)
     ("qkv", 10240, 8192, "column"),
     ("o", 8192, 8192, "row"),
@@ -458,22 +592,243 @@ TP70B = (  # name, N, K, split (Llama-3-70B)
     ("up", 28672, 8192, "column"),
     ("down", 8192, 28672, "row"),
 )
+TP70B_MS = (1, 64, 4096)
+TP_PARITY_TOL = 1e-5
+
+
+def _tp_raw(torch, dev, li: int, pi: int, n: int, k: int):
+    gen = torch.Generator(device=dev).manual_seed(0x70B + 97 * li + pi)  # the same weights on every rank
+    raw = torch.randint(0, 256, (n, k // 256, 110), dtype=torch.uint8, device=dev, generator=gen)
+    d = (torch.rand((n, k // 256), device=dev, generator=gen) * 9e-3 + 1e-3).half()
+    raw[..., :2] = d.view(torch.uint8).view(n, k // 256, 2)
+    return raw
+
+
+def tp_block(torch, world: int, rank: int, dev, steps: int, warmup: int) -> dict | None:
+    """one Llama-3-70B layer's linears tensor-parallel over the launched ranks.
+
+    Every rank (and the process group, when world > 1) takes part; rank 0 returns the results.
+    A layer, as a tensor-parallel transformer layer runs its linears: QKV
+    (column split, output kept sharded by heads), O (row split, input the
+    rank's K slice, FP32 partials all-reduced), gate and up (column split, one
+    grouped launch, outputs kept sharded), down (row split, all-reduced). Per
+    rank: two CUDA graphs of its compute (QKV + O, gate/up + down), each followed
+    by the NCCL all-reduce and the bf16 cast, issued eagerly. One GPU: the
+    unsharded layer (QKV, O, grouped gate+up, down) in one CUDA graph. Weights of
+    two layers alternate between steps, so every step streams them from HBM.
+
+    Parity (world > 1): for every projection of layer 0 and every M, the
+    gathered (column) or all-reduced (row) FP32 output against the unsharded
+    linear on rank 0, relative Frobenius error.
+    """
+    import torch.distributed as dist
+
+    from mambo_b200.kernels.iq3_s_fp8 import fused_linear_into, group_linear_into, iq3_s_fp8_linear
+    from mambo_b200.sharding import TensorParallelIQ3SLinear, gather_columns_group, local_group
+    from mambo_b200.utils.iq3_s_weight import prepare_iq3_s_fields
+
+    kdim = {name: k for name, n, k, split in TP70B}
+    layers, full = [], {}
+    for li in range(2):
+        lin = {}
+        for pi, (name, n, k, split) in enumerate(TP70B):
+            raw = _tp_raw(torch, dev, li, pi, n, k)
+            if world == 1:
+                lin[name] = prepare_iq3_s_fields(raw)
+            else:
+                lin[name] = TensorParallelIQ3SLinear(raw, split, gather_output=False,
+                                                     input_is_sharded=split == "row", out_dtype=torch.bfloat16)
+                if li == 0 and rank == 0:
+                    full[name] = prepare_iq3_s_fields(raw)
+            del raw
+            torch.cuda.empty_cache()
+        layers.append(lin)
+    stream = torch.cuda.Stream(dev)
+    results = []
+    for m in TP70B_MS:
+        gen = torch.Generator(device=dev).manual_seed(20261017 + m)  # the same activations on every rank
+        x_full = {k: torch.randn((m, k), device=dev, generator=gen).to(torch.bfloat16) for k in (8192, 28672)}
+        rec = {"m": m}
+        if world == 1:
+            outs = {name: torch.empty((m, n), dtype=torch.bfloat16, device=dev) for name, n, _, _ in TP70B}
+
+            def layer_1gpu(li, w=None):
+                w = w or layers[li]
+                fused_linear_into(x_full[kdim["qkv"]], w["qkv"], outs["qkv"])
+                fused_linear_into(x_full[kdim["o"]], w["o"], outs["o"])
+                group_linear_into([x_full[8192]] * 2, [w["gate"], w["up"]], [outs["gate"], outs["up"]])
+                fused_linear_into(x_full[kdim["down"]], w["down"], outs["down"])
+
+            with torch.cuda.stream(stream):
+                for li in range(2):
+                    layer_1gpu(li)  # eager warm-up (allocates the workspace outside the capture)
+            torch.cuda.synchronize(dev)
+            graphs = []
+            for li in range(2):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    layer_1gpu(li)
+                graphs.append(g)
+
+            def step(i):
+                graphs[i & 1].replay()
+        else:
+            l0 = layers[0]
+            # This rank's K slices of the row splits' inputs (attention output, MLP activation).
+            x_o = x_full[8192][:, l0["o"].k0:l0["o"].k0 + l0["o"].local_k].contiguous()
+            x_dn = x_full[28672][:, l0["down"].k0:l0["down"].k0 + l0["down"].local_k].contiguous()
+            # Parity: every projection's combined FP32 output against the unsharded linear.
+            errs = {}
+            for name, n, k, split in TP70B:
+                lin = l0[name]
+                if split == "column":
+                    y = lin(x_full[k], gather=True, out_dtype=torch.float32)
+                else:
+                    y = lin(x_full[k][:, lin.k0:lin.k0 + lin.local_k], out_dtype=torch.float32)
+                if rank == 0:
+                    ref = iq3_s_fp8_linear(x_full[k], full[name], out_dtype=torch.float32)
+                    errs[name] = (torch.linalg.norm((y - ref).double()) / torch.linalg.norm(ref.double())).item()
+            # The grouped gate/up gather (one collective) against the unsharded pair as well.
+            g, u = local_group([l0["gate"], l0["up"]], x_full[8192])
+            g32, u32 = gather_columns_group([l0["gate"], l0["up"]], [g.float(), u.float()])
+            if rank == 0:
+                for name, y in (("gate", g32), ("up", u32)):
+                    ref = iq3_s_fp8_linear(x_full[8192], full[name], out_dtype=torch.bfloat16).float()
+                    errs[f"{name}_grouped_bf16"] = (torch.linalg.norm((y - ref).double()) /
+                                                    torch.linalg.norm(ref.double())).item()
+                rec["parity_rel_frobenius"] = {k2: float(f"{v:.3g}") for k2, v in errs.items()}
+                # bf16 entries: both sides rounded to bf16 after FP32 sums in different orders
+                rec["parity_ok"] = all(v <= (TP_PARITY_TOL if "bf16" not in k2 else 1e-3) for k2, v in errs.items())
+
+            def compute_a(li):  # QKV (column, kept sharded) and O's local partial
+                w = layers[li]
+                w["qkv"].local(x_full[8192])
+                return w["o"].local(x_o)
+
+            def compute_b(li):  # gate + up (one grouped launch) and down's local partial
+                w = layers[li]
+                local_group([w["gate"], w["up"]], x_full[8192])
+                return w["down"].local(x_dn)
+
+            with torch.cuda.stream(stream):
+                for li in range(2):
+                    compute_a(li)
+                    compute_b(li)
+            torch.cuda.synchronize(dev)
+            graphs = []
+            for li in range(2):
+                ga, gb = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+                with torch.cuda.graph(ga, stream=stream):
+                    ya = compute_a(li)
+                with torch.cuda.graph(gb, stream=stream):
+                    yb = compute_b(li)
+                graphs.append((ga, ya, gb, yb))
+
+            def step(i):
+                ga, ya, gb, yb = graphs[i & 1]
+                w = layers[i & 1]
+                ga.replay()
+                w["o"].combine(ya)
+                gb.replay()
+                w["down"].combine(yb)
+        torch.cuda.synchronize(dev)
+        with torch.cuda.stream(stream):
+            for i in range(max(3, warmup)):
+                step(i)
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        n_steps = max(4, steps // 2)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for i in range(n_steps):
+                step(i)
+            e1.record(stream)
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / n_steps
+        coll = 0.0
+        if world > 1:
+            # The layer's two all-reduces alone (eager, device time), on this layer's partials.
+            ga, ya, gb, yb = graphs[0]
+            with torch.cuda.stream(stream):
+                for _ in range(2):
+                    dist.all_reduce(ya)
+                    dist.all_reduce(yb)
+                torch.cuda.synchronize(dev)
+                c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                c0.record(stream)
+                for _ in range(4):
+                    dist.all_reduce(ya)
+                    dist.all_reduce(yb)
+                c1.record(stream)
+            torch.cuda.synchronize(dev)
+            coll = c0.elapsed_time(c1) / 4
+            t = torch.tensor([ms, coll], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms, coll = float(t[0]), float(t[1])
+        del graphs
+        torch.cuda.synchronize(dev)
+        # The unsharded layer on rank 0 of this box (the N = 1 figure next to the sharded one).
+        if world > 1:
+            if rank == 0:
+                outs = {name: torch.empty((m, n), dtype=torch.bfloat16, device=dev) for name, n, _, _ in TP70B}
+
+                def layer_full():
+                    fused_linear_into(x_full[kdim["qkv"]], full["qkv"], outs["qkv"])
+                    fused_linear_into(x_full[kdim["o"]], full["o"], outs["o"])
+                    group_linear_into([x_full[8192]] * 2, [full["gate"], full["up"]], [outs["gate"], outs["up"]])
+                    fused_linear_into(x_full[kdim["down"]], full["down"], outs["down"])
+
+                with torch.cuda.stream(stream):
+                    layer_full()
+                torch.cuda.synchronize(dev)
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    layer_full()
+                with torch.cuda.stream(stream):
+                    for _ in range(3):
+                        g.replay()
+                    torch.cuda.synchronize(dev)
+                    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    f0.record(stream)
+                    for _ in range(n_steps):
+                        g.replay()
+                    f1.record(stream)
+                torch.cuda.synchronize(dev)
+                rec["ms_per_layer_1gpu"] = round(f0.elapsed_time(f1) / n_steps, 4)
+                rec["speedup_vs_1gpu"] = round(rec["ms_per_layer_1gpu"] / ms, 3)
+                del g
+            dist.barrier()
+        w_bytes = sum(n * (k // 256) * 110 for _, n, k, _ in TP70B)
+        flops = sum(2 * m * n * k for _, n, k, _ in TP70B)
+        rec.update({"ms_per_layer": round(ms, 4), "collective_ms": round(coll, 4),
+                    "weight_gbs_total": round(w_bytes / (ms * 1e-3) / 1e9, 1),
+                    "tflops_total": round(flops / (ms * 1e-3) / 1e12, 1)})
+        results.append(rec)
+    del layers, full
+    torch.cuda.empty_cache()
+    if rank != 0:
+        return None
+    peak, kind = load_peaks()
+    return {"workload": "tp70b (BASELINE config 5)", "n_gpus": world, "parallelism": f"tp{world}",
+            "scaling": "strong", "weights_per_layer_bytes": sum(n * (k // 256) * 110 for _, n, k, _ in TP70B),
+            "hbm_peak_gbs_per_gpu": peak, "peak_kind": kind, "parity_tol": TP_PARITY_TOL,
+            "layer": ("one GPU: QKV, O, grouped gate+up, down in one CUDA graph. N GPUs: per rank a CUDA graph "
+                      "of QKV (column shard) + O (row shard, local K slice), the NCCL all-reduce of O's FP32 "
+                      "partials + bf16 cast, a graph of gate+up (one grouped launch) + down (row shard), the "
+                      "all-reduce of down's partials + cast; column outputs stay sharded (the next row split "
+                      "consumes them)"),
+            "collective_ms": "device time of the layer's two all-reduces alone (eager), max over ranks",
+            "results": results}
 
 
 def run_tp70b(args) -> None:
-    """Llama-3-70B linears tensor-parallel over the launched ranks (NCCL), M in {1, 64, 4096}.
-
-    Column split for QKV/gate/up (outputs all-gathered), row split for O/down (FP32 partials all-reduced).
-    Per M: CUDA-event time of one layer's 5 linears (max over ranks) -- each rank's compute replayed from a
-    CUDA graph, the collectives issued eagerly in between -- and, eagerly, of its collectives alone; weights
-    of two layers per rank alternate between steps so that every step streams them from HBM.
-    """
+    """--workload tp70b: the TP block alone, as its own JSON line."""
     import datetime
 
     import torch
     import torch.distributed as dist
-
-    from mambo_b200.sharding import TensorParallelIQ3SLinear, local_group
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -482,119 +837,12 @@ def run_tp70b(args) -> None:
     dev = torch.device("cuda", local)
     if world > 1:
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
-    layers = []
-    for li in range(2):
-        lin = {}
-        for pi, (name, n, k, split) in enumerate(TP70B):
-            gen = torch.Generator(device=dev).manual_seed(0x70B + 97 * li + pi)  # same weights on every rank
-            raw = torch.randint(0, 256, (n, k // 256, 110), dtype=torch.uint8, device=dev, generator=gen)
-            d = (torch.rand((n, k // 256), device=dev, generator=gen) * 9e-3 + 1e-3).half()
-            raw[..., :2] = d.view(torch.uint8).view(n, k // 256, 2)
-            lin[name] = TensorParallelIQ3SLinear(raw, split, out_dtype=torch.bfloat16)
-            del raw, d
-            torch.cuda.empty_cache()
-        layers.append(lin)
-    results = []
-    for m in (1, 64, 4096):
-        gen = torch.Generator(device=dev).manual_seed(20261017 + m)
-        xs = {k: torch.randn((m, k), device=dev, generator=gen).to(torch.bfloat16) for k in (8192, 28672)}
-
-        def layer(li, timed_coll=False):
-            coll = 0.0
-            for name, n, k, split in TP70B:
-                lin = layers[li][name]
-                lin(xs[k], time_collective=timed_coll)
-                coll += lin.times.collective_ms if timed_coll else 0.0
-            return coll
-
-        # Eager warm-up on the capture stream (allocates its workspace outside the capture).
-        stream = torch.cuda.Stream(dev)
-        with torch.cuda.stream(stream):
-            for w in range(args.warmup):
-                layer(w & 1)
-        torch.cuda.synchronize(dev)
-        # A layer in a model's order: QKV, O, gate and up together (one grouped
-        # launch: they read the same input), down. Per group a CUDA graph of this
-        # rank's compute; the NCCL collectives run eagerly between replays on the
-        # same stream. With one GPU (no collectives) the layer is one graph.
-        kdim = {name: k for name, n, k, split in TP70B}
-
-        def group_local(li, grp):
-            if len(grp) == 1:
-                return [layers[li][grp[0]].local(xs[kdim[grp[0]]])]
-            return local_group([layers[li][name] for name in grp], xs[kdim[grp[0]]])
-
-        with torch.cuda.stream(stream):
-            for li in range(2):
-                for grp in TP70B_GROUPS:
-                    group_local(li, grp)  # eager warm-up of the grouped path
-        torch.cuda.synchronize(dev)
-        graphs = {}
-        for li in range(2):
-            if world == 1:
-                g = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(g, stream=stream):
-                    for grp in TP70B_GROUPS:
-                        group_local(li, grp)
-                graphs[li] = g
-            else:
-                for grp in TP70B_GROUPS:
-                    g = torch.cuda.CUDAGraph()
-                    with torch.cuda.graph(g, stream=stream):
-                        ys = group_local(li, grp)
-                    graphs[(li, grp)] = (g, ys)
-        torch.cuda.synchronize(dev)
-
-        def layer_graphed(li):
-            if world == 1:
-                graphs[li].replay()
-                return
-            for grp in TP70B_GROUPS:
-                g, ys = graphs[(li, grp)]
-                g.replay()
-                for name, y in zip(grp, ys):
-                    layers[li][name].combine(y)
-
-        with torch.cuda.stream(stream):
-            for w in range(args.warmup):
-                layer_graphed(w & 1)
-        torch.cuda.synchronize(dev)
-        if world > 1:
-            dist.barrier()
-        steps = max(2, args.steps // 5)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with torch.cuda.stream(stream):
-            e0.record(stream)
-            for st in range(steps):
-                layer_graphed(st & 1)
-            e1.record(stream)
-        torch.cuda.synchronize(dev)
-        ms = e0.elapsed_time(e1) / steps
-        del graphs
-        coll = sum(layer(st & 1, timed_coll=True) for st in range(2)) / 2
-        if world > 1:
-            t = torch.tensor([ms, coll], device=dev, dtype=torch.float64)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms, coll = float(t[0]), float(t[1])
-        w_bytes = sum(n * (k // 256) * 110 for _, n, k, _ in TP70B)
-        flops = sum(2 * m * n * k for _, n, k, _ in TP70B)
-        results.append({"m": m, "ms_per_layer": round(ms, 4), "collective_ms": round(coll, 4),
-                        "weight_gbs_total": round(w_bytes / (ms * 1e-3) / 1e9, 1),
-                        "tflops_total": round(flops / (ms * 1e-3) / 1e12, 1)})
+    r = tp_block(torch, world, rank, dev, args.steps, args.warmup)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
-        peak, kind = load_peaks()
-        print(json.dumps({"workload": "tp70b (BASELINE config 5)", "n_gpus": world, "parallelism": f"tp{world}",
-                          "data": "synthetic", "weights_per_layer_bytes": sum(n * (k // 256) * 110
-                                                                               for _, n, k, _ in TP70B),
-                          "hbm_peak_gbs_per_gpu": peak, "peak_kind": kind,
-                          "note": "ms_per_layer: QKV, O, grouped gate+up, down; per group a CUDA-graph replay of "
-                                  "the rank's compute (fused quantization + linear) and the NCCL collectives issued "
-                                  "eagerly (one graph per layer on one GPU); collective_ms: device time of the "
-                                  "layer's all-gathers/all-reduces measured alone in eager steps",
-                          "results": results}), flush=True)
+        print(json.dumps({"data": "synthetic", **r}), flush=True)
 
 
 def main() -> None:
@@ -604,7 +852,9 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("mambo", "reference"), default="mambo")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-prefill", action="store_true", help="skip the M=2048 prefill GEMM probe")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the prefill block (BASELINE config 3)")
+    ap.add_argument("--no-tp", action="store_true", help="skip the tensor-parallel block (BASELINE config 5)")
+    ap.add_argument("--no-model", action="store_true", help="skip the whole-model block (BASELINE config 4)")
     ap.add_argument("--single", metavar="N,K,M",
                     help="profiling mode: run four linears of one shape (random IQ3_S weights) and exit")
     ap.add_argument("--kernel", type=int, default=None, help="with --single: MAMBO_KERNEL_* to use")
@@ -768,7 +1018,6 @@ def main() -> None:
     peak, peak_kind = load_peaks()
     achieved = alg / group_us / 1e3
     sep_achieved = sum(r["bytes"] for r in per_launch) / sum(r["us"] for r in per_launch) / 1e3
-    traffic = read_profiled_traffic("dram_bytes_per_group_launch")
 
     # ---- e2e: public API with pinned host buffers, H2D + D2H in the region --
     # One pinned buffer holds every input of a step and one holds every output:
@@ -867,15 +1116,21 @@ def main() -> None:
     torch.cuda.synchronize(dev)
     ok = all(torch.equal(host_out[(m, p)], out_buf[(m, p)].cpu()) for m, p, _, _ in order)
 
+    del graph, graph_sep, g_e2e, g_pipe, layers
+    torch.cuda.synchronize(dev)
+    torch.cuda.empty_cache()
+    # BASELINE config 5 on every rank (tensor parallel over the launched GPUs).
+    tp = None if args.no_tp else tp_block(torch, world, rank, dev, args.steps, args.warmup)
     if world > 1:
-        del graph, graph_sep, g_e2e, g_pipe
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
         return
 
-    prefill = None if args.no_prefill else prefill_probe(torch, dev)
-    cpu = None if args.no_cpu_baseline else cpu_baseline()
+    # Single-GPU blocks (4 and 1) at N = 1 only.
+    prefill = None if (args.no_prefill or world > 1) else prefill_block(torch, dev)
+    model = None if (args.no_model or world > 1) else model_block(torch, dev)
+    cpu = None if (args.no_cpu_baseline or world > 1) else cpu_baseline()
     line = {
         "metric": METRIC,
         "value": value,
@@ -897,7 +1152,7 @@ def main() -> None:
                                 "(mambo_iq3s_linear_group)",
                    "parallelism": f"replicas{world}"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": traffic, "peak_kind": peak_kind,
+                     "traffic": None, "peak_kind": peak_kind,
                      "kernel": "iq3s_gemv_tm_kernel<1,8,GemvGroup>: the 20 linears of a step in one launch, "
                                "MXFP8 quantization fused",
                      "launch_us": group_us,
@@ -922,8 +1177,12 @@ def main() -> None:
         "gpu_launches": args.steps,
         "clocks": clock,
         "cpu_baseline": cpu,
-        # BASELINE config 3 (prefill GEMM) at M=2048, for the TFLOP/s half of the metric
+        # prefill from bf16 activations, TFLOP/s half of the metric
         "prefill": prefill,
+        # Llama-3-70B layer, tensor parallel over the N GPUs of this run
+        "tp": tp,
+        # every linear of a 32-layer Llama-3-8B
+        "model": model,
     }
     print(json.dumps(line), flush=True)
 

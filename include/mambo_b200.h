@@ -256,7 +256,8 @@ MAMBO_API size_t mambo_iq3s_linear_workspace_bytes(int64_t m, int64_t n_rows, in
  *
  * Set-up: the first call on each device looks up the array's device address
  * (cudaGetSymbolAddress, with that device current). Make that first call
- * before any stream capture.
+ * before any stream capture: a first call made while `stream` is capturing
+ * returns MAMBO_EINVAL and launches nothing.
  *
  * Zeroing: each call clears the split-K counters it uses, with
  * cudaMemsetAsync on `stream`, before launching its kernels.

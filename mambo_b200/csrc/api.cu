@@ -1049,6 +1049,9 @@ namespace {
 constexpr size_t kStaticCounterBytes = 64 * 1024;  // 4 counters per 128-row tile: N <= 524288
 constexpr int kStaticMaxCtas = 160;                // persistent grid cap (B200: 148 SMs)
 constexpr int64_t kStaticChunk = 8;                // tokens per launch (one 8-token tile)
+// Every chunk, the shorter last one included, is launched with the plan made
+// for a full chunk: that holds while all chunk sizes share one token tile.
+static_assert(kStaticChunk <= 8, "chunks of 1..kStaticChunk tokens must all use the 8-token tile (gemv_nt_for == 1)");
 constexpr size_t kStaticPartialBytes = (size_t)kStaticMaxCtas * 2 * 128 * 8 * sizeof(float);
 constexpr size_t kStaticXcopyOffset = kStaticCounterBytes + kStaticPartialBytes;
 constexpr int64_t kStaticMaxK = 98304;  // activation rows copied for alignment: kStaticChunk x K bytes
@@ -1057,8 +1060,10 @@ static_assert(kStaticXcopyOffset + kStaticChunk * kStaticMaxK + kStaticChunk * (
               "static scratch too small");
 
 // Device address of g_linear_scratch on the current device, looked up once per
-// device (with that device current) and cached.
-int static_scratch_address(uint8_t** out) {
+// device (with that device current) and cached. The look-up is not allowed
+// while `stream` is being captured into a CUDA graph: the first call on a
+// device must come before any capture.
+int static_scratch_address(uint8_t** out, cudaStream_t stream) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
@@ -1067,6 +1072,14 @@ int static_scratch_address(uint8_t** out) {
   static void* addr[64] = {nullptr};
   std::lock_guard<std::mutex> lock(mu);
   if (!addr[dev]) {
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    e = cudaStreamIsCapturing(stream, &cap);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamIsCapturing");
+    if (cap != cudaStreamCaptureStatusNone)
+      return fail(MAMBO_EINVAL,
+                  "the first mambo_iq3s_linear_noalloc call on device %d is inside a stream capture; make one call "
+                  "on this device before capturing",
+                  dev);
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_linear_scratch);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(static scratch)");
@@ -1119,7 +1132,7 @@ extern "C" int mambo_iq3s_linear_noalloc(const uint8_t* xq, int64_t ldxq, const 
     return fail(MAMBO_EINVAL, "grid of %d CTAs exceeds the static scratch", P.grid);
 
   uint8_t* scratch = nullptr;
-  st = static_scratch_address(&scratch);
+  st = static_scratch_address(&scratch, (cudaStream_t)stream);
   if (st != MAMBO_OK) return st;
   int* counters = (int*)scratch;
   float* partials = (float*)(scratch + kStaticCounterBytes);

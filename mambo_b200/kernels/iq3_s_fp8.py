@@ -1,4 +1,4 @@
-"""IQ3_S block decode and block-scaled FP8 projection on sm_100a (B200).
+"""IQ3_S block decode and IQ3_S x MXFP8 projection on sm_100a (B200).
 
 Mirror of src/python/mambo/kernels/iq3_s_fp8.py (Menooker/Mambo): the same
 constants, codebook helpers, launch wrappers, errors and benchmark-case
@@ -7,23 +7,24 @@ factory. The kernels are hand-written CUDA in libmambo_b200.so:
 * decode-sized M (< LARGE_TOKEN_THRESHOLD): a weight-streaming tcgen05 GEMV
   that bulk-copies tile-major IQ3_S records, decodes them into E4M3 bytes in
   tensor memory and splits K across all SMs (stream-K with a deterministic
-  fixup, or a thread-block-cluster K split);
-* prefill-sized M (>= LARGE_TOKEN_THRESHOLD): a tcgen05 GEMM over 128-row x
-  128-token tiles with the same decoder, one block-scaled MMA per 32-weight
-  group and the per-group FP32 rescale in the epilogue;
+  fixup, or a thread-block-cluster K split). Each 32-weight group is one
+  block-scaled FP8 MMA (the activation's UE8M0 scale applied by the tensor
+  core) and its FP32 partial is scaled by d*(1+2*nibble) in the epilogue --
+  the reference's arithmetic.
+* prefill-sized M (>= LARGE_TOKEN_THRESHOLD): by default a tcgen05 GEMM with
+  FP16 operands over 128-row x 128-token tiles. The group factor (1+2*nibble)
+  is folded into the FP16 weight operand and the activations enter as FP16
+  relative to each token's largest MXFP8 scale (both exact), so one FP32
+  accumulator covers a whole 256-wide K block and the epilogue applies d per
+  block. The reference's per-group decomposition (one block-scaled FP8 MMA
+  per group, FP32 rescale) is the non-default ``MAMBO_KERNEL_GEMM``.
 * the standalone decoder used by the bit-exactness tests.
 
-Arithmetic follows the reference exactly: every 32-weight group's E4M3 x E4M3
-product is accumulated in FP32 by the tensor core and scaled in FP32 by
-d*(1+2*nibble) and the activation's UE8M0 scale.
-
-One IQ3_S block along K (256 weights, 110 bytes):
-
-    byte  0..1   | d: FP16 base scale                 |  2 bytes
-    byte  2..65  | qs: 64 low 8-bit codebook indices  | 64 bytes
-    byte 66..73  | qh: 64 high index bits             |  8 bytes
-    byte 74..105 | signs: one bit per weight          | 32 bytes
-    byte 106..109| scales: 8 packed 4-bit values      |  4 bytes
+Layout of one GGUF IQ3_S block (256 consecutive weights of a row, 110 bytes):
+the FP16 base scale d first (2 bytes); then the low eight bits of the 64
+codebook indices (one byte each, 64 bytes); then their ninth bits packed
+eight to a byte (8 bytes); then one sign bit per weight (32 bytes); and last
+the eight 4-bit group scales (4 bytes).
 """
 
 from __future__ import annotations
@@ -101,23 +102,41 @@ def iq3_s_table() -> np.ndarray:
     return (grid[:, 0] | (grid[:, 1] << 8) | (grid[:, 2] << 16) | (grid[:, 3] << 24)).astype(np.uint32)
 
 
+def _e4m3_bits(value: int) -> int | None:
+    """Bit pattern of a positive integer in FP8 E4M3 (bias 7, 3 mantissa bits), None if it is not exact.
+
+    value = 2^p * (8 + m) / 8 with m < 8 gives exponent field p + 7 and mantissa m.
+    """
+    if value < 1:
+        return None
+    p = value.bit_length() - 1
+    if p > 8 or (p > 3 and value % (1 << (p - 3))):
+        return None
+    m = (value << 3 >> p) - 8
+    return ((p + 7) << 3) | m
+
+
 @lru_cache(maxsize=1)
 def iq3_s_fp8_table() -> np.ndarray:
-    """Pack positive magnitudes as E4M3 bits (iq3_s_fp8.py:77-94)."""
-    magnitudes = np.array([1, 3, 5, 7, 9, 11, 13, 15], dtype=np.uint8)
-    fp8_bits = np.array([0x38, 0x44, 0x4A, 0x4E, 0x51, 0x53, 0x55, 0x57], dtype=np.uint8)
-    lookup = np.zeros(256, dtype=np.uint8)
-    valid = np.zeros(256, dtype=np.bool_)
-    lookup[magnitudes] = fp8_bits
-    valid[magnitudes] = True
-    raw_table = iq3_s_table()
-    encoded = np.zeros_like(raw_table)
-    for shift in (0, 8, 16, 24):
-        magnitude = (raw_table >> shift) & 0xFF
-        if not np.all(valid[magnitude]):
+    """The codebook with each magnitude byte replaced by its E4M3 bit pattern (iq3_s_fp8.py:77-94).
+
+    The IQ3_S magnitudes are small odd integers, all exact in E4M3; the sign
+    bit (bit 7) stays clear and the kernels set it from the weight's sign bit.
+    """
+    encode = np.zeros(256, dtype=np.uint32)
+    exact = np.zeros(256, dtype=np.bool_)
+    for v in range(1, 256):
+        bits = _e4m3_bits(v)
+        if bits is not None:
+            encode[v], exact[v] = bits, True
+    table = iq3_s_table()
+    out = np.zeros(table.shape, dtype=np.uint32)
+    for byte in range(4):
+        mag = (table >> (8 * byte)) & 0xFF
+        if not exact[mag].all():
             raise ValueError("IQ3_S codebook contains a magnitude without an E4M3 encoding")
-        encoded |= lookup[magnitude].astype(np.uint32) << shift
-    return encoded
+        out |= encode[mag] << (8 * byte)
+    return out
 
 
 def _get_iq3_table(device: torch.device | None = None) -> torch.Tensor:

@@ -127,18 +127,23 @@ class TensorParallelIQ3SLinear:
         self.fields = (prepare or _default_prepare)(local)
         self.times = CollectiveTimes()
 
-    def forward(self, x: torch.Tensor, *, time_collective: bool = False) -> torch.Tensor:
-        """x: [M, K] (or [M, K/P] for a row split with sharded input) -> [M, N] (or [M, N/P])."""
-        return self.combine(self.local(x), time_collective=time_collective)
+    def forward(self, x: torch.Tensor, *, time_collective: bool = False, gather: bool | None = None,
+                out_dtype: torch.dtype | None = None) -> torch.Tensor:
+        """x: [M, K] (or [M, K/P] for a row split with sharded input) -> [M, N] (or [M, N/P]).
 
-    def local(self, x: torch.Tensor) -> torch.Tensor:
+        ``gather`` (COLUMN) and ``out_dtype`` override the instance's settings for this call.
+        """
+        return self.combine(self.local(x, out_dtype=out_dtype), time_collective=time_collective, gather=gather,
+                            out_dtype=out_dtype)
+
+    def local(self, x: torch.Tensor, *, out_dtype: torch.dtype | None = None) -> torch.Tensor:
         """This rank's compute: COLUMN -> out[:, n0:n1] in out_dtype; ROW -> the FP32 partial [M, N]."""
         if x.ndim != 2:
             raise ValueError("activation must be [M,K]")
         if self.mode == COLUMN:
             if x.shape[1] != self.k:
                 raise ValueError(f"column-split activation must be [M,{self.k}]")
-            return self._quantized_linear(x, self.out_dtype)
+            return self._quantized_linear(x, out_dtype or self.out_dtype)
         # Row split: this rank's K slice (whole 256-weight blocks: MXFP8 groups stay intact).
         if self.input_is_sharded:
             if x.shape[1] != self.local_k:
@@ -156,15 +161,17 @@ class TensorParallelIQ3SLinear:
         xq, xs = self._quantize(x)
         return self._linear(xq, xs, self.fields, out_dtype)
 
-    def combine(self, y: torch.Tensor, *, time_collective: bool = False) -> torch.Tensor:
+    def combine(self, y: torch.Tensor, *, time_collective: bool = False, gather: bool | None = None,
+                out_dtype: torch.dtype | None = None) -> torch.Tensor:
         """The exchange step on local()'s result: all-gather (COLUMN, when asked) or all-reduce (ROW)."""
         if self.mode == COLUMN:
-            if not self.gather_output or self.world == 1:
+            if not (self.gather_output if gather is None else gather) or self.world == 1:
                 return y
             return self._timed(time_collective, lambda: self._gather_columns(y))
         if self.world > 1:
             self._timed(time_collective, lambda: dist.all_reduce(y, op=dist.ReduceOp.SUM, group=self.group))
-        return y if self.out_dtype == torch.float32 else y.to(self.out_dtype)
+        dtype = out_dtype or self.out_dtype
+        return y if dtype == torch.float32 else y.to(dtype)
 
     __call__ = forward
 
@@ -213,3 +220,31 @@ def local_group(linears, x: torch.Tensor) -> list:
         x = x.contiguous()
     outs = [torch.empty((x.shape[0], lin.local_n), dtype=lin.out_dtype, device=x.device) for lin in linears]
     return group_linear_into([x] * len(linears), [lin.fields for lin in linears], outs)
+
+
+def gather_columns_group(linears, ys: list) -> list:
+    """combine(gather=True) of several COLUMN shards' outputs with ONE all-gather.
+
+    ``ys[i]``: linears[i]'s [M, N_i/P] output (same M and dtype for all).
+    Returns the [M, N_i] outputs, in order.
+    """
+    if not ys:
+        return []
+    lin0 = linears[0]
+    if lin0.world == 1:
+        return list(ys)
+    m, dtype = ys[0].shape[0], ys[0].dtype
+    widths = [y.shape[1] for y in ys]
+    send = torch.cat([y.reshape(-1) for y in ys])
+    parts = torch.empty((lin0.world, send.numel()), dtype=dtype, device=send.device)
+    if dist.get_backend(lin0.group) == "nccl":
+        dist.all_gather_into_tensor(parts, send, group=lin0.group)
+    else:
+        chunks = list(parts.unbind(0))
+        dist.all_gather(chunks, send, group=lin0.group)
+    outs, off = [], 0
+    for w in widths:
+        blk = parts[:, off:off + m * w].reshape(lin0.world, m, w)
+        outs.append(blk.permute(1, 0, 2).reshape(m, lin0.world * w))
+        off += m * w
+    return outs

@@ -1,19 +1,16 @@
-"""Prepare persistent IQ3_S SoA weight fields for the sm_100a kernels.
+"""IQ3_S weights split into per-field arrays for the sm_100a kernels.
 
-Mirror of src/python/mambo/utils/iq3_s_weight.py (Menooker/Mambo): same class,
-field names, dtypes, shapes and errors; the arrays are torch CUDA tensors and
-the AoS -> SoA split runs in libmambo_b200 (``mambo_iq3s_prepare``).
+Drop-in for src/python/mambo/utils/iq3_s_weight.py (Menooker/Mambo): the class,
+field names, dtypes, shapes and exception types are the reference's API; the
+arrays are torch CUDA tensors and the split itself is a kernel of
+libmambo_b200 (``mambo_iq3s_prepare``).
 
-One IQ3_S block along K (256 weights, 110 bytes):
-
-    byte  0..1   | d: FP16 base scale                 |  2 bytes
-    byte  2..65  | qs: 64 low 8-bit codebook indices  | 64 bytes
-    byte 66..73  | qh: 64 high index bits             |  8 bytes
-    byte 74..105 | signs: one bit per weight          | 32 bytes
-    byte 106..109| scales: 8 packed 4-bit values      |  4 bytes
-
-Each 9-bit (qs, qh) index selects four magnitudes from the codebook; each
-group of 32 weights uses scale d * (1 + 2 * scale_nibble).
+A GGUF IQ3_S tensor stores, for each row, one 110-byte record per 256 weights
+along K. The record starts with the FP16 scale d, followed by 64 bytes that
+give the low eight bits of the 64 nine-bit codebook indices (one index per
+four weights), 8 bytes of ninth index bits, 32 bytes of sign bits (one per
+weight) and 4 bytes holding eight 4-bit group scales. A weight of group g
+(32 weights) is sign * codebook magnitude * d * (1 + 2 * scale_g).
 """
 
 from __future__ import annotations
@@ -28,11 +25,12 @@ from .. import _lib, _runtime
 
 @dataclass(frozen=True)
 class IQ3SFields:
-    """Byte-preserving SoA, K-block first and N rows second (iq3_s_weight.py:10-22).
+    """The fields of every record, each in its own array indexed [K block, row, ...] (iq3_s_weight.py:10-22).
 
-    d: float16 [B,N]; qs: uint32 [B,N,16]; qh: uint16 [B,N,4];
-    signs: int32 [B,N,8]; scales: uint32 [B,N]. Total: 110 bytes/block.
-    Prepare once on the launch stream, then reuse for all projections.
+    The bytes are the GGUF ones, regrouped: d as float16 [B,N], the index low
+    bytes as uint32 [B,N,16], the ninth bits as uint16 [B,N,4], the sign bits
+    as int32 [B,N,8] and the group scales as uint32 [B,N] (B = K/256). Built
+    once by prepare_iq3_s_fields and then passed to every launch.
     """
 
     d: torch.Tensor
@@ -97,7 +95,7 @@ def pack_iq3_s_fields(fields: IQ3SFields, *, stream=None) -> IQ3SFields:
 
 
 def _weight_dimensions(iq3_weight: IQ3SFields) -> tuple[int, int]:
-    """Return N and the number of K blocks in the prepared fields (iq3_s_weight.py:57-62)."""
+    """(rows N, K blocks B) of prepared fields; TypeError for anything else (iq3_s_weight.py:57-62)."""
     if not isinstance(iq3_weight, IQ3SFields):
         raise TypeError("prepare IQ3_S weights with prepare_iq3_s_fields before launch")
     blocks, n_rows = iq3_weight.d.shape
@@ -109,7 +107,8 @@ def _weight_kernel_args(iq3_weight: IQ3SFields) -> tuple[torch.Tensor, ...]:
 
 
 def _large_weight_kernel_args(iq3_weight: IQ3SFields) -> tuple[torch.Tensor, ...]:
-    """Zero-copy views: qh as uint32 [B,N,2], signs as int32 [B,N*8] (iq3_s_weight.py:69-77)."""
+    """The fields with the ninth bits viewed as uint32 [B,N,2] and the signs flattened per K block
+    to int32 [B,N*8], without copying (iq3_s_weight.py:69-77)."""
     return (iq3_weight.d, iq3_weight.qs, iq3_weight.qh.view(torch.uint32),
             iq3_weight.signs.reshape(iq3_weight.signs.shape[0], -1), iq3_weight.scales)
 

@@ -1,9 +1,9 @@
 """Generate the golden vectors under tests/golden from the reference's own oracles.
 
-Run in a container where the reference tree is readable (default
-/root/reference, or MAMBO_REFERENCE_ROOT) and gguf-py is installed:
+Run where a checkout of the reference tree is readable and gguf-py is
+installed, with MAMBO_REFERENCE_ROOT naming the checkout's root directory:
 
-    python tests/golden/make_golden.py
+    MAMBO_REFERENCE_ROOT=<path to Menooker/Mambo> python tests/golden/make_golden.py
 
 Sources of truth (paths relative to the Menooker/Mambo tree):
 * IQ3_S decode: gguf-py 0.19.0 ``gguf.quants.dequantize`` -- the decoder the
@@ -31,11 +31,17 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-REF_ROOT = Path(os.environ.get("MAMBO_REFERENCE_ROOT", "/root/reference"))
+
+
+def _reference_root() -> Path:
+    root = os.environ.get("MAMBO_REFERENCE_ROOT")
+    if not root:
+        raise SystemExit("set MAMBO_REFERENCE_ROOT to the root of a Menooker/Mambo checkout")
+    return Path(root)
 
 
 def _load_fp8_reference():
-    path = REF_ROOT / "tests" / "python" / "utils" / "fp8_reference.py"
+    path = _reference_root() / "tests" / "python" / "utils" / "fp8_reference.py"
     spec = importlib.util.spec_from_file_location("mambo_ref_fp8_reference", path)
     mod = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(mod)

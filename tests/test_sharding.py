@@ -140,3 +140,46 @@ def test_two_rank_local_group_matches_unsharded():
     for name, n, seed in (("gate", 128, 21), ("up", 64, 22)):
         ref = O.iq3s_linear_f64(xq, xs, O.make_synthetic_iq3s(n, 1024, seed))
         np.testing.assert_array_equal(got[name], ref.astype(np.float32))
+
+
+def _rank_gather_group_main(rank, world, port, path):
+    from mambo_b200.sharding import gather_columns_group
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=__import__("datetime").timedelta(seconds=60))
+    try:
+        fakes = dict(prepare=_oracle_prepare, quantize=_oracle_quantize, linear=_oracle_linear)
+        # Column shards that keep their outputs sharded (gather_output=False), as in a layer whose
+        # next linear is a row split; a row split that takes its K slice as input.
+        gate = TensorParallelIQ3SLinear(torch.from_numpy(O.make_synthetic_iq3s(128, 1024, 31)), COLUMN,
+                                        gather_output=False, out_dtype=torch.float32, **fakes)
+        up = TensorParallelIQ3SLinear(torch.from_numpy(O.make_synthetic_iq3s(64, 1024, 32)), COLUMN,
+                                      gather_output=False, out_dtype=torch.float32, **fakes)
+        down = TensorParallelIQ3SLinear(torch.from_numpy(O.make_synthetic_iq3s(64, 1024, 33)), ROW,
+                                        input_is_sharded=True, out_dtype=torch.bfloat16, **fakes)
+        x = torch.from_numpy(np.random.default_rng(11).standard_normal((3, 1024)).astype(np.float32))
+        g, u = gate.local(x), up.local(x)
+        assert gate.combine(g).shape == (3, 64)  # kept sharded
+        full_g, full_u = gather_columns_group([gate, up], [g, u])
+        assert torch.equal(full_g, gate.combine(g, gather=True))
+        y = down(x[:, down.k0:down.k0 + down.local_k], out_dtype=torch.float32)
+        assert y.dtype == torch.float32
+        if rank == 0:
+            np.savez(path, gate=full_g.numpy(), up=full_u.numpy(), down=y.numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_grouped_gather_and_overrides():
+    """One all-gather for several column shards; per-call gather / output-dtype overrides."""
+    with tempfile.TemporaryDirectory() as tmp:
+        path = os.path.join(tmp, "y.npz")
+        mp.spawn(_rank_gather_group_main, args=(2, _free_port(), path), nprocs=2, join=True)
+        got = dict(np.load(path))
+    x = np.random.default_rng(11).standard_normal((3, 1024)).astype(np.float32)
+    xq, xs = O.quantize_mxfp8(x)
+    for name, n, seed in (("gate", 128, 31), ("up", 64, 32)):
+        ref = O.iq3s_linear_f64(xq, xs, O.make_synthetic_iq3s(n, 1024, seed))
+        np.testing.assert_array_equal(got[name], ref.astype(np.float32))
+    ref = O.iq3s_linear_f64(xq, xs, O.make_synthetic_iq3s(64, 1024, 33))
+    assert O.relative_frobenius(got["down"].astype(np.float64), ref) < 1e-6

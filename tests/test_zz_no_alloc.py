@@ -14,8 +14,8 @@ import numpy as np
 import pytest
 import torch
 
-from oracle import iq3s_oracle as O
 from mambo_b200 import _lib
+from oracle import iq3s_oracle as O
 from mambo_b200.kernels.iq3_s_fp8 import _get_iq3_table, launch_iq3_s_fp8_matmul
 from mambo_b200.utils.iq3_s_weight import prepare_iq3_s_fields, weight_struct
 
@@ -42,8 +42,10 @@ def test_noalloc_matches_workspace_entry_twice(cuda_device, m, n, k):
     fields = prepare_iq3_s_fields(torch.from_numpy(raw).to(cuda_device))
     xq, xs = torch.from_numpy(xq_np).to(cuda_device), torch.from_numpy(xs_np).to(cuda_device)
     table = _get_iq3_table(cuda_device)
+    oracle = O.iq3s_linear_f64(xq_np, xs_np, raw)
 
     expected = launch_iq3_s_fp8_matmul(xq, xs, fields).cpu().numpy().astype(np.float64)
+    assert O.relative_frobenius(expected, oracle) < FROB_TOL
     for call in range(2):
         out = torch.full((m, n), float("nan"), dtype=torch.float32, device=cuda_device)
         _lib.check(_noalloc(lib, xq, xs, fields, table, out), "mambo_iq3s_linear_noalloc")
@@ -51,7 +53,39 @@ def test_noalloc_matches_workspace_entry_twice(cuda_device, m, n, k):
         got = out.cpu().numpy().astype(np.float64)
         assert np.isfinite(got).all(), f"call {call}: unwritten outputs"
         assert O.relative_frobenius(got, expected) < FROB_TOL, f"call {call}"
+        assert O.relative_frobenius(got, oracle) < FROB_TOL, f"call {call} against the float64 oracle"
         np.testing.assert_allclose(got, expected, rtol=5e-4, atol=5e-4 * np.abs(expected).max())
+    assert _lib.device_status()[0] == _lib.MAMBO_OK
+
+
+def test_noalloc_unaligned_rows_bf16_output(cuda_device):
+    """Activation rows that are not 16-byte aligned go through the copies into the
+    static scratch; bf16 output rows are written chunk by chunk (8 + 5 tokens)."""
+    lib = _lib.load()
+    m, n, k = 13, 1032, 1024
+    raw = O.make_synthetic_iq3s(n, k, 777)
+    xq_np, xs_np = O.quantize_mxfp8(np.random.default_rng(5).standard_normal((m, k)).astype(np.float32))
+    fields = prepare_iq3_s_fields(torch.from_numpy(raw).to(cuda_device))
+    # Row strides k + 8 and k/32 + 3 bytes: rows 1.. start off a 16-byte boundary.
+    xq_big = torch.zeros((m, k + 8), dtype=torch.uint8, device=cuda_device)
+    xs_big = torch.zeros((m, k // 32 + 3), dtype=torch.uint8, device=cuda_device)
+    xq_big[:, :k] = torch.from_numpy(xq_np).to(cuda_device)
+    xs_big[:, : k // 32] = torch.from_numpy(xs_np).to(cuda_device)
+    xq, xs = xq_big[:, :k], xs_big[:, : k // 32]
+    assert xq.stride(0) % 16 and xs.stride(0) % 16
+    oracle = O.iq3s_linear_f64(xq_np, xs_np, raw)
+    table = _get_iq3_table(cuda_device)
+    for call in range(2):
+        out_big = torch.full((m, n + 8), float("nan"), dtype=torch.bfloat16, device=cuda_device)
+        out = out_big[:, :n]
+        _lib.check(_noalloc(lib, xq, xs, fields, table, out), "mambo_iq3s_linear_noalloc")
+        torch.cuda.synchronize(cuda_device)
+        got = out.float().cpu().numpy().astype(np.float64)
+        assert np.isfinite(got).all(), f"call {call}: unwritten outputs"
+        assert torch.isnan(out_big[:, n:]).all(), f"call {call}: wrote past the row"
+        # bf16 output: rounding of 2^-9 relative per element
+        assert O.relative_frobenius(got, oracle) < 4e-3, f"call {call}"
+        np.testing.assert_allclose(got, oracle, rtol=8e-3, atol=8e-3 * np.abs(oracle).max())
     assert _lib.device_status()[0] == _lib.MAMBO_OK
 
 
