@@ -147,7 +147,8 @@ const TcChoice kTcChoices[] = {
     {8, 3, 0}, {8, 4, 0}, {8, 4, 4}, {8, 6, 0}, {8, 6, 4}, {8, 8, 4},
     {16, 3, 0}, {16, 4, 0}, {16, 4, 4}, {16, 6, 0}, {16, 6, 4}, {16, 8, 4},
 };
-constexpr int kNumTcConfigs = 2 * (int)(sizeof(kTcChoices) / sizeof(kTcChoices[0]));
+// split 0 (stream-K), 1 (row tile per CTA) and 2 (cluster K split) for each choice.
+constexpr int kNumTcConfigs = 3 * (int)(sizeof(kTcChoices) / sizeof(kTcChoices[0]));
 // mma.sync GEMV (MAMBO_KERNEL_GEMV_SYNC): warps x stages x split.
 const int kSyncWarps[] = {4, 8, 12, 16};
 const int kSyncStages[] = {3, 4, 6, 8};
@@ -175,9 +176,26 @@ uint32_t config_smem(const MamboLinearConfig& c, int nt, int64_t b) {
 // Prefill-sized M (the reference's large-token path, LARGE_TOKEN_THRESHOLD):
 // the tcgen05 GEMM over 128 x 128 tiles.
 constexpr int64_t kGemmMinTokens = 32;
-// Weight stages of the GEMM configurations (the other fields are fixed).
+// Weight stages of the GEMM configurations, and the FP16 GEMM's K splits
+// (its search space is stages x splits; the other GEMMs search stages only).
 const int kGemmStages[] = {2, 3, 4};
 constexpr int kNumGemmConfigs = (int)(sizeof(kGemmStages) / sizeof(kGemmStages[0]));
+const int kGemmSplits[] = {1, 2, 3, 4, 6, 8};
+constexpr int kNumGemmF16Configs = kNumGemmConfigs * (int)(sizeof(kGemmSplits) / sizeof(kGemmSplits[0]));
+
+// Split-K counters live at the start of every workspace: 64 Ki ints, zero
+// between calls, a fixed region so that a call never finds another shape's
+// partials there. Shapes needing more are rejected.
+constexpr size_t kCounterBytes = 256 * 1024;
+// The first half holds the GEMVs' counters (4 per 128-row tile), the second
+// the FP16 GEMM's K-split counters (8 per output tile).
+constexpr size_t kGemvCounterBytes = 128 * 1024;
+constexpr size_t kGemmSplitCounterOffset = kGemvCounterBytes;
+constexpr size_t kGemmSplitCounterBytes = kCounterBytes - kGemmSplitCounterOffset;
+constexpr int kGemmMaxSplit = 8;
+
+int gemm_f16_default_split(int64_t m, int64_t n, int64_t b, int sms);
+int gemm_f16_clamp_split(int split, int64_t m, int64_t n, int64_t b);
 
 void default_config(int64_t m, int64_t n, int64_t b, MamboLinearConfig* cfg, int smem_optin, int sms) {
   std::memset(cfg, 0, sizeof(*cfg));
@@ -186,6 +204,7 @@ void default_config(int64_t m, int64_t n, int64_t b, MamboLinearConfig* cfg, int
     cfg->warps = 8;
     cfg->ctas_per_sm = 1;
     cfg->stages = 4;
+    cfg->split = gemm_f16_default_split(m, n, b, sms > 0 ? sms : 148);
     while (cfg->stages > 2 && (int)config_smem(*cfg, 4, b) > smem_optin) --cfg->stages;
     return;
   }
@@ -201,6 +220,17 @@ void default_config(int64_t m, int64_t n, int64_t b, MamboLinearConfig* cfg, int
   while (cfg->stages > 2 && (int)config_smem(*cfg, nt, b) > smem_optin) --cfg->stages;
 }
 
+// AUTO resolved for a shape: the kernel by M, and unset fields from the
+// tuned default (a GEMM also takes the default K split when split is 0).
+void resolve_auto(MamboLinearConfig* c, int64_t m, int64_t n, int64_t b, int smem_optin, int sms) {
+  if (c->kernel != MAMBO_KERNEL_AUTO) return;
+  MamboLinearConfig a;
+  default_config(m, n, b, &a, smem_optin, sms);
+  c->kernel = a.kernel;
+  if (c->stages == 0) c->stages = a.stages;
+  if (is_gemm(a.kernel) && c->split == 0) c->split = a.split;
+}
+
 int validate_config(const MamboLinearConfig* cfg, int64_t m, int64_t b, const DeviceInfo& info) {
   const int kind = kernel_of(*cfg);
   if (kind != MAMBO_KERNEL_GEMV && kind != MAMBO_KERNEL_GEMV_SYNC && !is_gemm(kind))
@@ -208,6 +238,9 @@ int validate_config(const MamboLinearConfig* cfg, int64_t m, int64_t b, const De
   if (is_gemm(kind)) {
     const int smax = kind == MAMBO_KERNEL_GEMM ? gemm_tm_max_wstages() : gemm_f16_max_wstages();
     if (cfg->stages < 2 || cfg->stages > smax) return fail(MAMBO_EINVAL, "stages must be in [2, %d]", smax);
+    const int smax_split = kind == MAMBO_KERNEL_GEMM_F16 ? kGemmMaxSplit : 1;
+    if (cfg->split < 0 || cfg->split > smax_split)
+      return fail(MAMBO_EINVAL, "split (K parts) must be in [0, %d] for this kernel", smax_split);
   } else if (kind == MAMBO_KERNEL_GEMV_SYNC) {
     if (cfg->warps != 4 && cfg->warps != 8 && cfg->warps != 12 && cfg->warps != 16)
       return fail(MAMBO_EINVAL, "warps must be 4, 8, 12 or 16");
@@ -227,10 +260,6 @@ int validate_config(const MamboLinearConfig* cfg, int64_t m, int64_t b, const De
   return MAMBO_OK;
 }
 
-// Split-K counters live at the start of every workspace: 64 Ki ints, zero
-// between calls, a fixed region so that a call never finds another shape's
-// partials there. Shapes needing more are rejected.
-constexpr size_t kCounterBytes = 256 * 1024;
 
 struct GemvPlan {
   int nt, rows, row_tiles, units, grid, counter_slots, kparts;
@@ -262,12 +291,47 @@ size_t gemm_workspace_bytes(int64_t m, int64_t b) {
   return kCounterBytes + align256((size_t)((m + tok - 1) / tok) * (size_t)b * 1024);
 }
 
-// The FP16 GEMM's workspace: the split-K counters (left zero for the GEMV),
-// the FP16 activations [m][K] and the per-token scales.
-// Counters, the FP16 activations [m][K], the tokens' scales (padded to whole
-// 128-token tiles: the epilogue reads them 16 at a time).
-size_t gemm_f16_workspace_bytes(int64_t m, int64_t b) {
-  return kCounterBytes + align256((size_t)m * (size_t)b * 256 * 2) + align256((size_t)((m + 127) / 128 * 128) * 4);
+// Output tiles of the FP16 GEMM, and the K split it can take: at most
+// kGemmMaxSplit parts, every part at least 4 K blocks, counters for every tile.
+int64_t gemm_f16_out_tiles(int64_t m, int64_t n) { return ((n + 127) / 128) * ((m + 127) / 128); }
+int gemm_f16_clamp_split(int split, int64_t m, int64_t n, int64_t b) {
+  int ks = split < 1 ? 1 : split > kGemmMaxSplit ? kGemmMaxSplit : split;
+  while (ks > 1 && b / ks < 4) --ks;
+  if (ks > 1 && (size_t)gemm_f16_out_tiles(m, n) * 8 * sizeof(int) > kGemmSplitCounterBytes) ks = 1;
+  return ks;
+}
+
+// The K split the FP16 GEMM takes by default: the one with the shortest
+// estimated makespan, counting in K blocks of one CTA: waves of work items
+// (items spread round-robin over the SMs) times an item's blocks, plus about
+// two blocks of pipeline fill per item and one and a half for publishing and
+// summing the FP32 partials of a split tile.
+int gemm_f16_default_split(int64_t m, int64_t n, int64_t b, int sms) {
+  const int64_t tiles = gemm_f16_out_tiles(m, n);
+  double best = 0.0;
+  int best_ks = 1;
+  for (int ks = 1; ks <= kGemmMaxSplit; ++ks) {
+    if (gemm_f16_clamp_split(ks, m, n, b) != ks) break;
+    const int64_t waves = (tiles * ks + sms - 1) / sms;
+    const double cost = (double)waves * ((double)b / ks + 2.0 + (ks > 1 ? 1.5 : 0.0));
+    if (ks == 1 || cost < best) {
+      best = cost;
+      best_ks = ks;
+    }
+  }
+  return best_ks;
+}
+
+// The FP16 GEMM's workspace: the counter region (the GEMVs' counters left
+// zero, the K-split counters), the FP16 activations [m][K], the tokens'
+// scales (padded to whole 128-token tiles: the epilogue reads them 16 at a
+// time) and, with a K split, the FP32 partials of every output tile.
+size_t gemm_f16_partial_bytes(int64_t m, int64_t n, int ks) {
+  return ks > 1 ? align256((size_t)gemm_f16_out_tiles(m, n) * ks * 128 * 128 * sizeof(float)) : 0;
+}
+size_t gemm_f16_workspace_bytes(int64_t m, int64_t n, int64_t b, int ks) {
+  return kCounterBytes + align256((size_t)m * (size_t)b * 256 * 2) + align256((size_t)((m + 127) / 128 * 128) * 4) +
+         gemm_f16_partial_bytes(m, n, ks);
 }
 
 // The GEMM reads activations through a TMA map (16-byte aligned rows) and
@@ -342,13 +406,27 @@ int launch_gemm(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t ldxs
   return ok();
 }
 
+// Where the FP16 GEMM's activation operand comes from: MXFP8 codes (xq, xs),
+// or bf16 / f32 rows quantized on the way (x, x_dtype, ldx).
+struct GemmF16Source {
+  const uint8_t* xq;
+  int64_t ldxq;
+  const uint8_t* xs;
+  int64_t ldxs;
+  const void* x;
+  int x_dtype;
+  int64_t ldx;
+};
+
 // The FP16-operand GEMM: activations to FP16 with per-token scales
-// (workspace), then one persistent launch over all tiles.
-int launch_gemm_f16_path(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t ldxs, int64_t m,
-                         const MamboIQ3SWeight* w, const uint32_t* fp8_table, void* out, int out_dtype, int64_t ldo,
-                         const MamboLinearConfig& c, const DeviceInfo& info, void* workspace, size_t workspace_bytes,
-                         cudaStream_t stream) {
-  const size_t need = gemm_f16_workspace_bytes(m, w->n_blocks);
+// (workspace; from bf16 / f32 rows the quantization is part of that pass),
+// then one persistent launch over all tiles.
+int launch_gemm_f16_path(const GemmF16Source& src, int64_t m, const MamboIQ3SWeight* w, const uint32_t* fp8_table,
+                         void* out, int out_dtype, int64_t ldo, const MamboLinearConfig& c, const DeviceInfo& info,
+                         void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  const bool pair = c.kernel == MAMBO_KERNEL_GEMM_F16_PAIR;
+  const int ks = pair ? 1 : gemm_f16_clamp_split(c.split, m, w->n_rows, w->n_blocks);
+  const size_t need = gemm_f16_workspace_bytes(m, w->n_rows, w->n_blocks, ks);
   if (!workspace || workspace_bytes < need)
     return fail(MAMBO_EWORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
   if ((uintptr_t)workspace % 256) return fail(MAMBO_EINVAL, "workspace must be 256-byte aligned");
@@ -358,9 +436,9 @@ int launch_gemm_f16_path(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int
   const int64_t k = w->n_blocks * 256;
   uint16_t* x16 = (uint16_t*)((uint8_t*)workspace + kCounterBytes);
   float* tok_scale = (float*)((uint8_t*)x16 + align256((size_t)m * k * 2));
-  cudaError_t e = launch_x16(xq, ldxq, xs, ldxs, (int)m, k, x16, k, tok_scale, stream);
-  if (e != cudaSuccess) return cuda_fail(e, "iq3s_x16");
-  const bool pair = c.kernel == MAMBO_KERNEL_GEMM_F16_PAIR;
+  cudaError_t e = src.x ? launch_x16_quant(src.x, src.x_dtype, src.ldx, (int)m, k, x16, k, tok_scale, stream)
+                        : launch_x16(src.xq, src.ldxq, src.xs, src.ldxs, (int)m, k, x16, k, tok_scale, stream);
+  if (e != cudaSuccess) return cuda_fail(e, src.x ? "iq3s_x16_quant" : "iq3s_x16");
   GemmF16Maps maps;
   std::memset(&maps, 0, sizeof(maps));
   // A CTA of a pair loads 64 of the tile's 128 tokens.
@@ -379,9 +457,16 @@ int launch_gemm_f16_path(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int
   p.wstages = c.stages;
   p.row_tiles = (int)((w->n_rows + 127) / 128);
   p.tok_tiles = (int)((m + 127) / 128);
+  p.ksplit = ks;
+  if (ks > 1) {
+    // Partials after the token scales; counters in the counter region's second half.
+    p.partials = (float*)((uint8_t*)tok_scale + align256((size_t)((m + 127) / 128 * 128) * 4));
+    p.split_counters = (int*)((uint8_t*)workspace + kGemmSplitCounterOffset);
+  }
   // bf16 output in 16-byte aligned rows: tiles leave through shared memory and
-  // a TMA store, with the weight stages it needs room for.
-  if (out_dtype == MAMBO_BF16 && make_gemm_out_map(out, ldo, (int)w->n_rows, (int)m, &maps.out)) {
+  // a TMA store, with the weight stages it needs room for (not with a K split:
+  // there each epilogue warp of a tile's last contributor stores its part).
+  if (ks == 1 && out_dtype == MAMBO_BF16 && make_gemm_out_map(out, ldo, (int)w->n_rows, (int)m, &maps.out)) {
     int st = c.stages;
     while (st > 2 && (int)gemm_f16_smem_bytes(st, true) > info.max_smem_optin) --st;
     if ((int)gemm_f16_smem_bytes(st, true) <= info.max_smem_optin) {
@@ -398,7 +483,7 @@ int launch_gemm_f16_path(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int
     if (e != cudaSuccess) return cuda_fail(e, "iq3s_gemm_f16 (pairs)");
     return ok();
   }
-  const int64_t tiles = (int64_t)p.row_tiles * p.tok_tiles;
+  const int64_t tiles = (int64_t)p.row_tiles * p.tok_tiles * ks;
   const int grid = (int)(tiles < info.sms ? tiles : info.sms);
   e = launch_gemm_f16(p, maps, grid, stream);
   if (e != cudaSuccess) return cuda_fail(e, "iq3s_gemm_f16");
@@ -608,6 +693,7 @@ int mambo_default_config(int64_t m, int64_t n_rows, int64_t n_blocks, MamboLinea
 
 int mambo_num_configs(int kernel) {
   if (kernel == MAMBO_KERNEL_GEMV || kernel == MAMBO_KERNEL_AUTO) return kNumTcConfigs;
+  if (kernel == MAMBO_KERNEL_GEMM_F16) return kNumGemmF16Configs;
   if (is_gemm(kernel)) return kNumGemmConfigs;
   if (kernel == MAMBO_KERNEL_GEMV_SYNC) return kNumSyncConfigs;
   return 0;
@@ -625,9 +711,15 @@ int mambo_config_at(int kernel, int index, MamboLinearConfig* cfg) {
   if (is_gemm(kernel)) {
     cfg->split = 0;
     cfg->warps = 8;
-    cfg->stages = kGemmStages[index];
+    if (kernel == MAMBO_KERNEL_GEMM_F16) {
+      cfg->stages = kGemmStages[index % kNumGemmConfigs];
+      cfg->split = kGemmSplits[index / kNumGemmConfigs];
+    } else {
+      cfg->stages = kGemmStages[index];
+    }
   } else if (kernel == MAMBO_KERNEL_GEMV) {
-    const TcChoice& t = kTcChoices[index / 2];
+    cfg->split = index % 3;
+    const TcChoice& t = kTcChoices[index / 3];
     cfg->warps = t.warps;
     cfg->stages = t.stages;
     cfg->prefetch = t.prefetch;
@@ -648,11 +740,7 @@ size_t mambo_iq3s_linear_workspace_bytes(int64_t m, int64_t n_rows, int64_t n_bl
                       st == MAMBO_OK ? info.sms : 148);
   const int sms = (st == MAMBO_OK && info.sms > 0) ? info.sms : 148;
   const int smem_optin = (st == MAMBO_OK && info.max_smem_optin > 0) ? info.max_smem_optin : kSmemOptinDefault;
-  if (c.kernel == MAMBO_KERNEL_AUTO) {  // resolved as mambo_iq3s_linear resolves it
-    MamboLinearConfig a;
-    default_config(m, n_rows, n_blocks, &a, smem_optin, sms);
-    c.kernel = a.kernel;
-  }
+  resolve_auto(&c, m, n_rows, n_blocks, smem_optin, sms);  // as mambo_iq3s_linear resolves it
   // A GEMM call may fall back to the GEMV (unaligned activations, no packed
   // weight copy): room for both.
   MamboLinearConfig cv = c;
@@ -662,7 +750,11 @@ size_t mambo_iq3s_linear_workspace_bytes(int64_t m, int64_t n_rows, int64_t n_bl
   GemvPlan P = plan_gemv(m_chunk, n_rows, n_blocks, cv, sms, smem_optin);
   const size_t gemv = P.counters_bytes + P.partial_bytes + P.xcopy_bytes + P.xscopy_bytes;
   const size_t gemm = kernel_of(c) == MAMBO_KERNEL_GEMM       ? gemm_workspace_bytes(m, n_blocks)
-                     : is_gemm_f16(kernel_of(c))              ? gemm_f16_workspace_bytes(m, n_blocks)
+                     : is_gemm_f16(kernel_of(c))
+                         ? gemm_f16_workspace_bytes(m, n_rows, n_blocks,
+                                                    c.kernel == MAMBO_KERNEL_GEMM_F16
+                                                        ? gemm_f16_clamp_split(c.split, m, n_rows, n_blocks)
+                                                        : 1)
                                                              : 0;
   return gemv > gemm ? gemv : gemm;
 }
@@ -686,19 +778,14 @@ int mambo_iq3s_linear(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_
   if (st != MAMBO_OK) return st;
   MamboLinearConfig c;
   if (cfg) c = *cfg; else default_config(m, w->n_rows, w->n_blocks, &c, info.max_smem_optin, info.sms);
-  if (c.kernel == MAMBO_KERNEL_AUTO) {
-    MamboLinearConfig a;
-    default_config(m, w->n_rows, w->n_blocks, &a, info.max_smem_optin, info.sms);
-    c.kernel = a.kernel;
-    if (c.stages == 0) c.stages = a.stages;
-  }
+  resolve_auto(&c, m, w->n_rows, w->n_blocks, info.max_smem_optin, info.sms);
   if (is_gemm(c.kernel)) {
     if (gemm_usable(w, xq, ldxq, m)) {
       st = validate_config(&c, 32, w->n_blocks, info);
       if (st != MAMBO_OK) return st;
       if (is_gemm_f16(c.kernel))
-        return launch_gemm_f16_path(xq, ldxq, xs, ldxs, m, w, fp8_table, out, out_dtype, ldo, c, info, workspace,
-                                    workspace_bytes, (cudaStream_t)stream);
+        return launch_gemm_f16_path(GemmF16Source{xq, ldxq, xs, ldxs, nullptr, 0, 0}, m, w, fp8_table, out,
+                                    out_dtype, ldo, c, info, workspace, workspace_bytes, (cudaStream_t)stream);
       return launch_gemm(xq, ldxq, xs, ldxs, m, w, fp8_table, out, out_dtype, ldo, c, info, workspace,
                          workspace_bytes, (cudaStream_t)stream);
     }
@@ -726,7 +813,7 @@ int mambo_iq3s_linear(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_
   for (int64_t m0 = 0; m0 < m; m0 += m_chunk_max) {
     const int64_t mc = (m - m0) < m_chunk_max ? (m - m0) : m_chunk_max;
     GemvPlan P = plan_gemv(mc, w->n_rows, w->n_blocks, c, info.sms, info.max_smem_optin);
-    if ((size_t)P.counter_slots * sizeof(int) > kCounterBytes)
+    if ((size_t)P.counter_slots * sizeof(int) > kGemvCounterBytes)
       return fail(MAMBO_EINVAL, "N=%lld needs more split-K counters than the workspace holds", (long long)w->n_rows);
     const size_t need = P.counters_bytes + P.partial_bytes + P.xcopy_bytes + P.xscopy_bytes;
     if (!workspace || workspace_bytes < need)
@@ -808,12 +895,7 @@ int mambo_iq3s_linear_fused(const void* x, int x_dtype, int64_t ldx, int64_t m, 
   if (st != MAMBO_OK) return st;
   MamboLinearConfig c;
   if (cfg) c = *cfg; else default_config(m, w->n_rows, w->n_blocks, &c, info.max_smem_optin, info.sms);
-  if (c.kernel == MAMBO_KERNEL_AUTO) {
-    MamboLinearConfig a;
-    default_config(m, w->n_rows, w->n_blocks, &a, info.max_smem_optin, info.sms);
-    c.kernel = a.kernel;
-    if (c.stages == 0) c.stages = a.stages;
-  }
+  resolve_auto(&c, m, w->n_rows, w->n_blocks, info.max_smem_optin, info.sms);
   const uintptr_t fields[6] = {(uintptr_t)w->d, (uintptr_t)w->qs, (uintptr_t)w->qh, (uintptr_t)w->signs,
                                (uintptr_t)w->scales, (uintptr_t)w->packed};
   bool aligned = w->n_rows % 8 == 0;
@@ -830,7 +912,7 @@ int mambo_iq3s_linear_fused(const void* x, int x_dtype, int64_t ldx, int64_t m, 
     const GemvPlan P = plan_gemv(m, w->n_rows, w->n_blocks, c, info.sms, info.max_smem_optin);
     while (c.stages > 2 && (int)gemv_tm_smem_bytes(P.nt, c.stages, P.kparts, true) > info.max_smem_optin)
       --c.stages;
-    if ((size_t)P.counter_slots * sizeof(int) > kCounterBytes)
+    if ((size_t)P.counter_slots * sizeof(int) > kGemvCounterBytes)
       return fail(MAMBO_EINVAL, "N=%lld needs more split-K counters than the workspace holds", (long long)w->n_rows);
     if ((int)gemv_tm_smem_bytes(P.nt, c.stages, P.kparts, true) <= info.max_smem_optin) {
       const size_t need = P.counters_bytes + P.partial_bytes;
@@ -843,6 +925,18 @@ int mambo_iq3s_linear_fused(const void* x, int x_dtype, int64_t ldx, int64_t m, 
                            partials, nullptr, nullptr, (cudaStream_t)stream, (const uint16_t*)x, ldx);
       return st == MAMBO_OK ? ok() : st;
     }
+  }
+  // Prefill-sized M on the FP16 GEMM: the quantization is part of the pass
+  // that writes the GEMM's FP16 activations (one launch instead of two, no
+  // MXFP8 round trip through memory); the same codes, the same results.
+  const int elt = x_dtype == MAMBO_BF16 ? 2 : 4;
+  if (m >= kGemmMinTokens && is_gemm_f16(c.kernel) && w->packed && aligned && (uintptr_t)x % 16 == 0 &&
+      (ldx * elt) % 16 == 0 && m <= (int64_t)1 << 30 && x16_quant_smem_bytes(k) <= (size_t)info.max_smem_optin) {
+    st = validate_config(&c, 32, w->n_blocks, info);
+    if (st != MAMBO_OK) return st;
+    st = launch_gemm_f16_path(GemmF16Source{nullptr, 0, nullptr, 0, x, x_dtype, ldx}, m, w, fp8_table, out,
+                              out_dtype, ldo, c, info, workspace, workspace_bytes, (cudaStream_t)stream);
+    return st == MAMBO_OK ? ok() : st;
   }
   // Otherwise: quantize into the workspace, then the linear.
   const size_t lin = align256(mambo_iq3s_linear_workspace_bytes(m, w->n_rows, w->n_blocks, cfg));
@@ -883,7 +977,7 @@ bool group_fusable(const MamboLinearItem* items, int count) {
     tiles += rt;
     units += rt * w->n_blocks;
   }
-  return (size_t)tiles * 4 * sizeof(int) <= kCounterBytes && units < (int64_t)1 << 30;
+  return (size_t)tiles * 4 * sizeof(int) <= kGemvCounterBytes && units < (int64_t)1 << 30;
 }
 
 int group_nt(const MamboLinearItem* items, int count) {

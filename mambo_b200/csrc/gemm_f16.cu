@@ -28,6 +28,7 @@
 #include "kernels.cuh"
 #include "tcgen05.cuh"
 #include "iq3s_tm.cuh"
+#include "mxfp8.cuh"
 
 namespace mambo {
 
@@ -139,16 +140,24 @@ __global__ void __launch_bounds__(kThreadsH, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = kPair ? cluster_ctarank() : 0u;
-  // Tiles: (row group, token tile), a row group being one row tile (single
-  // CTAs) or two (pairs: rank r takes row tile 2*group + r).
+  // Work items: (row group, token tile, K part), a row group being one row
+  // tile (single CTAs) or two (pairs: rank r takes row tile 2*group + r); the
+  // K parts of an output tile are consecutive items, so CTAs running at the
+  // same time share its weight and activation rows. Item t of this CTA covers
+  // K blocks [kb_begin(t), kb_end(t)).
   const int nb = p.n_blocks;
+  const int ks = kPair ? 1 : p.ksplit;
   const int groups = kPair ? (p.row_tiles + 1) / 2 : p.row_tiles;
-  const int n_tiles = groups * p.tok_tiles;
+  const int n_tiles = groups * p.tok_tiles * ks;
   const int cl = kPair ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
   const int ncl = kPair ? (int)(gridDim.x >> 1) : (int)gridDim.x;
   const int my_tiles = cl < n_tiles ? (n_tiles - 1 - cl) / ncl + 1 : 0;
-  auto row_tile = [&](int t) { return ((cl + t * ncl) / p.tok_tiles) * (kPair ? 2 : 1) + (int)rank; };
-  auto tok_tile = [&](int t) { return (cl + t * ncl) % p.tok_tiles; };
+  auto out_tile = [&](int t) { return ks == 1 ? cl + t * ncl : (cl + t * ncl) / ks; };
+  auto row_tile = [&](int t) { return (out_tile(t) / p.tok_tiles) * (kPair ? 2 : 1) + (int)rank; };
+  auto tok_tile = [&](int t) { return out_tile(t) % p.tok_tiles; };
+  auto kpart = [&](int t) { return ks == 1 ? 0 : (cl + t * ncl) % ks; };
+  auto kb_begin = [&](int t) { return ks == 1 ? 0 : kpart(t) * nb / ks; };  // nb * ks < 2^31
+  auto kb_end = [&](int t) { return ks == 1 ? nb : (kpart(t) + 1) * nb / ks; };
   // Rank 0's copy of a barrier (rank 1 arrives there).
   auto lead = [&](uint32_t bar) { return kPair ? mapa_shared(bar, 0) : bar; };
 
@@ -205,7 +214,7 @@ __global__ void __launch_bounds__(kThreadsH, 1)
         const int rt = row_tile(t);
         const bool have = rt < p.row_tiles;  // a pair's second row tile may not exist
         const uint8_t* rec = p.packed + (size_t)(have ? rt : 0) * nb * tm::kRecordBytes;
-        for (int kb = 0; kb < nb; ++kb, ++it) {
+        for (int kb = kb_begin(t), kbe = kb_end(t); kb < kbe; ++kb, ++it) {
           if (it >= SW && !mbar_wait_bounded(kWempty + 8 * s, ph ^ 1, kSiteGemvEmpty)) {
             ok = false;
             break;
@@ -236,7 +245,7 @@ __global__ void __launch_bounds__(kThreadsH, 1)
       bool ok = true;
       for (int t = 0; ok && t < my_tiles; ++t) {
         const int tok0 = tok_tile(t) * kTokH + (int)rank * kTokLoad;
-        for (int kb = 0; ok && kb < nb; ++kb) {
+        for (int kb = kb_begin(t), kbe = kb_end(t); ok && kb < kbe; ++kb) {
           for (int h = 0; h < 2; ++h, ++hj) {
             if (hj >= kXS && !mbar_wait_bounded(kXempty + 8 * x, ph ^ 1, kSiteGemvEmpty)) {
               ok = false;
@@ -268,7 +277,7 @@ __global__ void __launch_bounds__(kThreadsH, 1)
     int it = 0, hj = 0;
     bool ok = rank == 0;
     for (int t = 0; ok && t < my_tiles; ++t) {
-      for (int kb = 0; ok && kb < nb; ++kb, ++it) {
+      for (int kb = kb_begin(t), kbe = kb_end(t); ok && kb < kbe; ++kb, ++it) {
         const int r = it % kARingH, db = it & 1;
         ok = kPair ? tm::warp_wait_cluster(kAfull + 8 * r, (it / kARingH) & 1, kSiteGemvFull)
                    : tm::warp_wait(kAfull + 8 * r, (it / kARingH) & 1, kSiteGemvFull);
@@ -345,7 +354,7 @@ __global__ void __launch_bounds__(kThreadsH, 1)
     uint32_t sph = 0;
     bool ok = true;
     for (int t = 0; ok && t < my_tiles; ++t) {
-      for (int kb = 0; kb < nb; ++kb, ++it) {
+      for (int kb = kb_begin(t), kbe = kb_end(t); kb < kbe; ++kb, ++it) {
         const int r = it % kARingH;
         ok = tm::warp_wait(kWfull + 8 * s, sph, kSiteGemvFull);
         if (ok && it >= kARingH) ok = tm::warp_wait(kAempty + 8 * r, ((it / kARingH) & 1) ^ 1, kSiteGemvEmpty);
@@ -417,7 +426,7 @@ __global__ void __launch_bounds__(kThreadsH, 1)
     bool ok = true;
     for (int t = 0; ok && t < my_tiles; ++t) {
       const int rt = row_tile(t), tt = tok_tile(t);
-      for (int kb = 0; kb < nb; ++kb, ++it) {
+      for (int kb = kb_begin(t), kbe = kb_end(t); kb < kbe; ++kb, ++it) {
         const int db = it & 1;
         if (!tm::warp_wait(kDfull + 8 * (it % kAuxRingH), (it / kAuxRingH) & 1, kSiteGemvFull) ||
             !tm::warp_wait(kMdone + 8 * db, (it >> 1) & 1, kSiteGemvFull)) {
@@ -451,6 +460,50 @@ __global__ void __launch_bounds__(kThreadsH, 1)
         __syncwarp();
       }
       if (!ok) break;
+      if (ks > 1) {
+        // K split: publish this warp's partial (32 rows x 64 tokens, FP32,
+        // token quads major so that a warp's 16-byte stores are contiguous)
+        // and count in; the last contributor of the tile sums the partials
+        // in K-part order (its own from registers) and goes on to the store.
+        const int ot = out_tile(t), kp = kpart(t);
+        // Element (part j, token quad c/4 of this warp's half, row rl) of the tile's partials.
+        float4* part = reinterpret_cast<float4*>(p.partials) + (size_t)ot * ks * (kTokH / 4) * kRowsH +
+                       (h * 16) * kRowsH + rl;
+        constexpr int kPartStride = (kTokH / 4) * kRowsH;  // float4s per part
+#pragma unroll
+        for (int c = 0; c < 64; c += 4)
+          __stcg(part + kp * kPartStride + (c / 4) * kRowsH, make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]));
+        __threadfence();  // every lane's partial is visible GPU-wide before the count goes up
+        __syncwarp();
+        int* counter = p.split_counters + (size_t)ot * kEpiWarpsH + e;
+        int last = 0;
+        if (lane == 0) last = atomic_add_acq_rel_gpu(counter, 1) == ks - 1;
+        last = __shfl_sync(0xFFFFFFFFu, last, 0);
+        if (!last) {
+#pragma unroll
+          for (int i = 0; i < 64; ++i) acc[i] = 0.f;
+          continue;
+        }
+        if (lane == 0) *counter = 0;  // every part has arrived: zero again for the next launch
+        __threadfence();              // the other parts' partials are read after the count was seen
+        // Sum in part order (this warp's own part read back: it is in L2).
+#pragma unroll
+        for (int c = 0; c < 64; c += 4) {
+          float4 sum = __ldcg(part + (c / 4) * kRowsH);
+#pragma unroll 1
+          for (int j = 1; j < ks; ++j) {
+            const float4 v = __ldcg(part + j * kPartStride + (c / 4) * kRowsH);
+            sum.x += v.x;
+            sum.y += v.y;
+            sum.z += v.z;
+            sum.w += v.w;
+          }
+          acc[c] = sum.x;
+          acc[c + 1] = sum.y;
+          acc[c + 2] = sum.z;
+          acc[c + 3] = sum.w;
+        }
+      }
       // The tile's 64 tokens, 8 at a time: their scales as two float4 loads
       // (tok_scale is padded to whole tiles), issued before the previous
       // chunk's stores so that the load latency overlaps them.
@@ -578,18 +631,27 @@ __global__ void __launch_bounds__(kThreadsH, 1)
   if constexpr (kPair) cluster_sync_all();
 }
 
-// One CTA per token row: e_max over the row's UE8M0 scales, then every E4M3
-// value times 2^(e_g - e_max) rounded to FP16; tok_scale = 2^(e_max - 127).
-// A scale code 0xFF (NaN) makes its group NaN.
-__global__ void iq3s_x16_kernel(const uint8_t* __restrict__ xq, int64_t ldxq, const uint8_t* __restrict__ xs,
-                                int64_t ldxs, int64_t k, uint16_t* __restrict__ x16, int64_t ld,
-                                float* __restrict__ tok_scale) {
-  const int64_t t = blockIdx.x;
-  const int64_t groups = k / 32;
-  const uint8_t* srow = xs + t * ldxs;
+// Eight E4M3 values (bytes of raw, in order) -> eight FP16 values of E4M3 * f
+// (f = 2^(e_g - e_max), or NaN), each rounded to nearest once.
+__device__ __forceinline__ uint4 x16_from_e4m3x8(uint2 raw, float f) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t two = ((i < 2 ? raw.x : raw.y) >> (16 * (i & 1))) & 0xFFFFu;
+    const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)two, __NV_E4M3);
+    const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&hr));
+    const __half2 o = __floats2half2_rn(v.x * f, v.y * f);
+    w[i] = *reinterpret_cast<const uint32_t*>(&o);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// The largest scale code of a row (0xFF, a NaN group, counts as 0), reduced
+// over the CTA; every thread returns it. `codes` holds the row's k/32 codes.
+__device__ __forceinline__ int row_max_code(const uint8_t* codes, int64_t groups) {
   int emax = 0;
   for (int64_t g = threadIdx.x; g < groups; g += blockDim.x) {
-    const int e = srow[g];
+    const int e = codes[g];
     emax = max(emax, e == 0xFF ? 0 : e);
   }
   for (int o = 16; o > 0; o >>= 1) emax = max(emax, __shfl_xor_sync(0xFFFFFFFFu, emax, o));
@@ -602,7 +664,18 @@ __global__ void iq3s_x16_kernel(const uint8_t* __restrict__ xq, int64_t ldxq, co
     if (threadIdx.x == 0) wmax[0] = v;
   }
   __syncthreads();
-  emax = wmax[0];
+  return wmax[0];
+}
+
+// One CTA per token row: e_max over the row's UE8M0 scales, then every E4M3
+// value times 2^(e_g - e_max) rounded to FP16; tok_scale = 2^(e_max - 127).
+// A scale code 0xFF (NaN) makes its group NaN.
+__global__ void iq3s_x16_kernel(const uint8_t* __restrict__ xq, int64_t ldxq, const uint8_t* __restrict__ xs,
+                                int64_t ldxs, int64_t k, uint16_t* __restrict__ x16, int64_t ld,
+                                float* __restrict__ tok_scale) {
+  const int64_t t = blockIdx.x;
+  const uint8_t* srow = xs + t * ldxs;
+  const int emax = row_max_code(srow, k / 32);
   if (threadIdx.x == 0) tok_scale[t] = e8m0_to_float((uint32_t)emax);
   const uint8_t* qrow = xq + t * ldxq;
   uint16_t* orow = x16 + t * ld;
@@ -610,22 +683,10 @@ __global__ void iq3s_x16_kernel(const uint8_t* __restrict__ xq, int64_t ldxq, co
     const int e = srow[c / 4];
     const uint2 raw = *reinterpret_cast<const uint2*>(qrow + c * 8);
     const float f = e == 0xFF ? __uint_as_float(0x7FC00000u) : ldexpf(1.0f, e - emax);
-    uint32_t w[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint32_t two = ((i < 2 ? raw.x : raw.y) >> (16 * (i & 1))) & 0xFFFFu;
-      const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)two, __NV_E4M3);
-      const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&hr));
-      const __half2 o = __floats2half2_rn(v.x * f, v.y * f);
-      w[i] = *reinterpret_cast<const uint32_t*>(&o);
-    }
-    *reinterpret_cast<uint4*>(orow + c * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+    *reinterpret_cast<uint4*>(orow + c * 8) = x16_from_e4m3x8(raw, f);
   }
 }
 
-// --------------------------------------------------------------------------
-// Host side
-// --------------------------------------------------------------------------
 uint32_t gemm_f16_smem_bytes(int wstages, bool out_stage) { return gemm_f16_smem(wstages, out_stage); }
 int gemm_f16_max_wstages() { return kMaxWStagesH; }
 
@@ -633,6 +694,72 @@ cudaError_t launch_x16(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64
                        uint16_t* x16, int64_t ld, float* tok_scale, cudaStream_t stream) {
   iq3s_x16_kernel<<<(unsigned)m, 256, 0, stream>>>(xq, ldxq, xs, ldxs, k, x16, ld, tok_scale);
   return cudaGetLastError();
+}
+
+// Activation quantization fused into the FP16 conversion: bf16 (T = uint16_t)
+// or f32 rows -> the MXFP8 codes mambo_quantize_mxfp8 forms (round to nearest
+// even: quad of lanes per 32-value group, as quantize_mxfp8_kernel) -> the
+// FP16 operand and token scale iq3s_x16_kernel forms from those codes. One
+// CTA per token; the row's E4M3 bytes and scale codes wait in shared memory
+// (k + k/32 bytes) while the CTA finds the largest code. Rows 16-byte aligned;
+// k % 256 == 0, so every warp's lanes stay together through the quad shuffles.
+template <typename T>
+__global__ void __launch_bounds__(256) iq3s_x16_quant_kernel(const T* __restrict__ x, int64_t ldx, int64_t k,
+                                                             uint16_t* __restrict__ x16, int64_t ld,
+                                                             float* __restrict__ tok_scale) {
+  extern __shared__ __align__(16) uint8_t qsm[];
+  uint8_t* qrow = qsm;      // [k] E4M3 bytes
+  uint8_t* srow = qsm + k;  // [k/32] scale codes
+  const int64_t t = blockIdx.x;
+  const T* xrow = x + t * ldx;
+  pdl_wait();  // the activations may come from the previous kernel
+  for (int64_t c = threadIdx.x; c < k / 8; c += blockDim.x) {  // chunk of 8 values; group c/4
+    float v[8];
+    if constexpr (sizeof(T) == 2) {
+      const uint4 raw = __ldg(reinterpret_cast<const uint4*>(xrow + c * 8));
+      const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        v[2 * i] = __uint_as_float(w[i] << 16);
+        v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+      }
+    } else {
+      const float4 a = __ldg(reinterpret_cast<const float4*>(xrow + c * 8));
+      const float4 b = __ldg(reinterpret_cast<const float4*>(xrow + c * 8) + 1);
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+      v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    }
+    uint2 q;
+    const uint32_t code = mxfp8_quad_rne(v, q);
+    *reinterpret_cast<uint2*>(qrow + c * 8) = q;
+    if ((c & 3) == 0) srow[c / 4] = (uint8_t)code;
+  }
+  __syncthreads();
+  const int emax = row_max_code(srow, k / 32);
+  pdl_launch_dependents();
+  if (threadIdx.x == 0) tok_scale[t] = e8m0_to_float((uint32_t)emax);
+  uint16_t* orow = x16 + t * ld;
+  for (int64_t c = threadIdx.x; c < k / 8; c += blockDim.x) {
+    const int e = srow[c / 4];
+    const uint2 raw = *reinterpret_cast<const uint2*>(qrow + c * 8);
+    const float f = e == 0xFF ? __uint_as_float(0x7FC00000u) : ldexpf(1.0f, e - emax);
+    *reinterpret_cast<uint4*>(orow + c * 8) = x16_from_e4m3x8(raw, f);
+  }
+}
+
+size_t x16_quant_smem_bytes(int64_t k) { return (size_t)k + (size_t)(k / 32); }
+
+cudaError_t launch_x16_quant(const void* x, int x_dtype, int64_t ldx, int m, int64_t k, uint16_t* x16, int64_t ld,
+                             float* tok_scale, cudaStream_t stream) {
+  const size_t smem = x16_quant_smem_bytes(k);
+  const void* kern = x_dtype == MAMBO_BF16 ? (const void*)iq3s_x16_quant_kernel<uint16_t>
+                                           : (const void*)iq3s_x16_quant_kernel<float>;
+  cudaError_t e = ensure_smem_attribute(kern, smem);
+  if (e != cudaSuccess) return e;
+  if (x_dtype == MAMBO_BF16)
+    return launch_pdl(kern, dim3((unsigned)m), dim3(256), smem, stream, (const uint16_t*)x, ldx, k, x16, ld,
+                      tok_scale);
+  return launch_pdl(kern, dim3((unsigned)m), dim3(256), smem, stream, (const float*)x, ldx, k, x16, ld, tok_scale);
 }
 
 cudaError_t launch_gemm_f16(const GemmF16Params& p, const GemmF16Maps& maps, int grid, cudaStream_t stream) {

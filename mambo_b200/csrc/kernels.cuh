@@ -248,6 +248,14 @@ struct GemmF16Params {
   int row_tiles;
   int tok_tiles;
   int out_tma;  // 1: bf16 output tiles staged in shared memory and written by a TMA store
+  // K split (single CTAs only): each (row tile, token tile) is split into
+  // ksplit contiguous K ranges taken by different CTAs. Each epilogue warp
+  // publishes its FP32 partial [ksplit][32 token quads][128 rows][4] per tile
+  // and counts in on split_counters[tile * 8 + warp] (zero between launches);
+  // the last of the ksplit contributors sums them in K order and stores.
+  int ksplit;                  // 1 = no split
+  float* partials;             // [out tiles][ksplit][128 x 128] FP32
+  int* split_counters;         // [out tiles][8], zero on entry and left zero
 };
 struct GemmF16Maps {
   CUtensorMap x16;  // FP16 activations [m tokens][K], box 64 halves x 128 tokens, 128-byte swizzle
@@ -262,6 +270,11 @@ int gemm_f16_max_wstages();
 // tok_scale[m] = 2^(e_max - 127). Exact while a group's exponent is within 12 of the token's largest.
 cudaError_t launch_x16(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t ldxs, int m, int64_t k,
                        uint16_t* x16, int64_t ld, float* tok_scale, cudaStream_t stream);
+// bf16 / f32 activations [m][k] (row stride ldx elements, 16-byte aligned rows) -> MXFP8 codes
+// (round to nearest even, as mambo_quantize_mxfp8) -> the x16 / tok_scale launch_x16 forms, in one launch.
+cudaError_t launch_x16_quant(const void* x, int x_dtype, int64_t ldx, int m, int64_t k, uint16_t* x16, int64_t ld,
+                             float* tok_scale, cudaStream_t stream);
+size_t x16_quant_smem_bytes(int64_t k);
 bool make_gemm_x16_map(const uint16_t* x16, int64_t ld, int m, int64_t k, int box_tokens, CUtensorMap* map);
 // CTA pairs of the FP16 GEMM that fit on the device at once, and their launch.
 int gemm_f16_pair_max_clusters(int wstages, bool out_stage);

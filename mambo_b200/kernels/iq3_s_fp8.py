@@ -184,7 +184,18 @@ def _sm_key(device: torch.device) -> str:
 
 
 def _m_bucket(m: int) -> int:
-    return 8 if m <= 8 else (16 if m <= 16 else 32)
+    """Token counts that share a tuned configuration: up to 8, 16 and 31 (the GEMV's
+    token tiles), then powers of two from LARGE_TOKEN_THRESHOLD (the GEMM)."""
+    if m <= 8:
+        return 8
+    if m <= 16:
+        return 16
+    if m < LARGE_TOKEN_THRESHOLD:
+        return LARGE_TOKEN_THRESHOLD - 1
+    b = LARGE_TOKEN_THRESHOLD
+    while b < m:
+        b *= 2
+    return b
 
 
 def register_tuned_config(m: int, n: int, k: int, config: dict) -> None:
@@ -200,10 +211,31 @@ def load_tuned_configs(path: str | os.PathLike) -> int:
     return len(records)
 
 
-def select_config(m: int, n: int, k: int, device: torch.device) -> dict:
-    tuned = _TUNED.get((_m_bucket(m), n, k))
-    if tuned is not None:
-        return tuned
+# Configurations tuned on B200 by ``python -m mambo_b200.utils.kernel_benchmark`` for the
+# Llama-3 projection shapes; loaded the first time a configuration is selected.
+TUNED_CONFIGS_PATH = Path(__file__).resolve().parent / "tuned_sm100.json"
+_TUNED_LOADED = False
+
+
+def _load_packaged_tuned() -> None:
+    global _TUNED_LOADED
+    if _TUNED_LOADED:
+        return
+    _TUNED_LOADED = True
+    if TUNED_CONFIGS_PATH.is_file():
+        # Records registered explicitly before this point take precedence.
+        explicit = dict(_TUNED)
+        load_tuned_configs(TUNED_CONFIGS_PATH)
+        _TUNED.update(explicit)
+
+
+def select_config(m: int, n: int, k: int, device: torch.device, *, tuned: bool = True) -> dict:
+    """The configuration a launch uses: the autotuner's record for (M bucket, N, K) if any, else BEST_CONFIGS."""
+    if tuned and _sm_key(device) == "sm100":
+        _load_packaged_tuned()
+    rec = _TUNED.get((_m_bucket(m), n, k)) if tuned else None
+    if rec is not None:
+        return rec
     sm = _sm_key(device)
     if sm not in BEST_CONFIGS:
         raise RuntimeError(f"IQ3_S FP8 matmul has no tuned config for {sm}")
@@ -432,14 +464,23 @@ def make_benchmark_cases(iq3_weight, ms: tuple[int, ...] = (4, 128), seed: int =
         def run(config: dict) -> None:
             linear_into(x_values, x_scales, iq3_weight, out, config=config, stream=stream)
 
+        # The untuned default first (the tuner never ends up slower than it), then the
+        # kernel's space: below the threshold the tcgen05 GEMV (decoder warps x weight
+        # stages x L2 prefetch x split mode); from it the FP16 GEMM (weight stages x K
+        # split) and the same on CTA pairs (weight stages).
+        default = dict(select_config(m, n_rows, k, dev, tuned=False))
+        if m >= LARGE_TOKEN_THRESHOLD:
+            space = config_search_space(_lib.MAMBO_KERNEL_GEMM_F16) + \
+                config_search_space(_lib.MAMBO_KERNEL_GEMM_F16_PAIR)
+        else:
+            space = config_search_space(_lib.MAMBO_KERNEL_GEMV)
         return BenchmarkCase(
             name=f"M={m} N={n_rows} K={k}", stream=stream, kernel=run,
-            search_space=config_search_space(_lib.MAMBO_KERNEL_GEMM if m >= LARGE_TOKEN_THRESHOLD
-                                             else _lib.MAMBO_KERNEL_GEMV),
+            search_space=[default] + [c for c in space if c != default],
             grid_fn=lambda config: (config.get("ctas_per_sm", 1),),
             args_fn=lambda config: (config,),
             hints_fn=None,
-            summary_keys=("warps", "stages"),
+            summary_keys=("kernel", "stages", "split"),
             shape=(m, n_rows, k),
         )
 

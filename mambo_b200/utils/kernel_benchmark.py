@@ -16,6 +16,7 @@ from __future__ import annotations
 import argparse
 import importlib
 import json
+import tempfile
 from dataclasses import dataclass, field
 from pathlib import Path
 from time import perf_counter
@@ -152,29 +153,49 @@ _BENCHMARKS = {
 }
 
 
+def _merge_records(path: Path, records: list[dict]) -> None:
+    """Write ``records`` into the JSON list at ``path``, replacing entries of the same (m, n, k)."""
+    old = json.loads(path.read_text()) if path.is_file() else []
+    keep = {(r["m"], r["n"], r["k"]): r for r in old}
+    keep.update({(r["m"], r["n"], r["k"]): r for r in records})
+    path.write_text(json.dumps([keep[key] for key in sorted(keep)], indent=1) + "\n")
+
+
 def benchmark_main(argv: Sequence[str] | None = None) -> None:
-    parser = argparse.ArgumentParser(description="Autotune an sm_100a kernel on a GGUF weight (or a synthetic one)")
+    parser = argparse.ArgumentParser(description="Autotune an sm_100a kernel on a GGUF weight (or synthetic ones)")
     parser.add_argument("kernel", choices=sorted(_BENCHMARKS))
     parser.add_argument("--model", type=Path, help="GGUF model path")
     parser.add_argument("--weight-name", help="tensor name in the GGUF model")
-    parser.add_argument("--synthetic", metavar="N,K", help="seeded random IQ3_S weight of this shape instead")
+    parser.add_argument("--synthetic", metavar="N,K", nargs="+",
+                        help="seeded random IQ3_S weights of these shapes instead")
     parser.add_argument("--m", type=int, nargs="*", default=[4, 128], help="token counts to tune")
-    parser.add_argument("--save", type=Path, help="write the tuned configs as JSON")
+    parser.add_argument("--save", type=Path, help="write the tuned configs as JSON (merged into an existing file)")
     args = parser.parse_args(argv)
 
     expected_type, kernel_module, factory = _BENCHMARKS[args.kernel]
+    make_cases = getattr(importlib.import_module(kernel_module), factory)
     if args.synthetic:
-        n, k = (int(v) for v in args.synthetic.split(","))
-        rng = np.random.default_rng(0x1A3)
-        raw = rng.integers(0, 256, size=(n, k // 256, 110), dtype=np.uint8)
-        raw[..., :2] = rng.uniform(1e-3, 1e-2, size=(n, k // 256)).astype("<f2").view(np.uint8).reshape(n, -1, 2)
-        weight = torch.from_numpy(raw).cuda()
+        weights = []
+        for shape in args.synthetic:
+            n, k = (int(v) for v in shape.split(","))
+            rng = np.random.default_rng(0x1A3)
+            raw = rng.integers(0, 256, size=(n, k // 256, 110), dtype=np.uint8)
+            raw[..., :2] = rng.uniform(1e-3, 1e-2, size=(n, k // 256)).astype("<f2").view(np.uint8).reshape(n, -1, 2)
+            weights.append(torch.from_numpy(raw).cuda())
     else:
         if args.model is None or args.weight_name is None:
             parser.error("--model and --weight-name are required without --synthetic")
-        weight = load_gguf_weight(args.model, args.weight_name, expected_type)
-    make_cases = getattr(importlib.import_module(kernel_module), factory)
-    mini_benchmark(make_cases(weight, ms=tuple(args.m)), save_path=args.save)
+        weights = [load_gguf_weight(args.model, args.weight_name, expected_type)]
+    records = []
+    for weight in weights:
+        with tempfile.TemporaryDirectory() as tmp_dir:
+            tmp = Path(tmp_dir) / "tuned.json"
+            mini_benchmark(make_cases(weight, ms=tuple(args.m)), save_path=tmp)
+            records += json.loads(tmp.read_text())
+        del weight
+        torch.cuda.empty_cache()
+    if args.save is not None:
+        _merge_records(args.save, records)
 
 
 if __name__ == "__main__":

@@ -3,8 +3,9 @@
 The reference runs launch_quantize_fp8 then launch_iq3_s_fp8_matmul
 (src/python/mambo/kernels/quantize_fp8.py:67-84, iq3_s_fp8.py:364-399). Below
 32 tokens the tcgen05 GEMV here quantizes bf16 rows itself with the standalone
-quantizer's arithmetic, so its output must equal the two-step path bit for bit
-under the same configuration; elsewhere the entry point runs the two steps.
+quantizer's arithmetic; from 32 tokens the quantization is part of the pass
+that writes the FP16 GEMM's activation operand. Either way the output must
+equal the two-step path bit for bit under the same configuration.
 """
 
 from __future__ import annotations
@@ -135,15 +136,46 @@ def test_fused_nan_and_zero_rows(cuda_device):
     assert torch.isfinite(fused[[0, 3]]).all()
 
 
-@pytest.mark.parametrize("m", [32, 40])
-def test_fused_prefill_sizes_run_two_steps(cuda_device, m):
-    _, fields = _weight(cuda_device, 256, 1024, seed=51)
-    x = _activations(cuda_device, m, 1024, seed=52)
-    stream = torch.cuda.Stream(cuda_device)  # fresh stream: the workspace query covers the fallback
+@pytest.mark.parametrize("m", [32, 40, 130, 300])
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
+def test_fused_prefill_quantizes_in_the_fp16_pass(cuda_device, m, out_dtype):
+    """From 32 tokens: the quantizer is part of the pass that writes the GEMM's FP16 activations
+    (iq3s_x16_quant_kernel), then the GEMM -- two launches, the same bits as quantize + linear."""
+    raw, fields = _weight(cuda_device, 264, 1024, seed=51 + m)
+    x = _activations(cuda_device, m, 1024, seed=52 + m)
+    x[1, 7] = float("nan")  # a NaN group and an all-zero row go through as the standalone quantizer has them
+    x[2] = 0
+    stream = torch.cuda.Stream(cuda_device)  # fresh stream: the workspace query covers this path
     with torch.cuda.stream(stream):
-        fused = iq3_s_fp8_linear(x, fields, out_dtype=torch.float32, stream=stream)
+        fused = iq3_s_fp8_linear(x, fields, out_dtype=out_dtype, stream=stream)
     stream.synchronize()
-    assert _same_bits(fused, _two_step(x, fields, torch.float32, None))
+    assert _same_bits(fused, _two_step(x, fields, out_dtype, None))
+    kernels = _our_kernels(lambda: iq3_s_fp8_linear(x, fields, out_dtype=out_dtype))
+    if kernels:
+        assert len(kernels) == 2 and any("x16_quant" in k for k in kernels) \
+            and any("gemm_f16" in k for k in kernels), kernels
+    keep = [i for i in range(m) if i != 1]
+    xq, xs = O.quantize_mxfp8(x[keep].float().cpu().numpy())
+    ref = O.iq3s_linear_f64(xq, xs, raw)
+    tol = ORACLE_FROB_TOL if out_dtype == torch.float32 else 4e-3
+    assert O.relative_frobenius(fused[keep].float().cpu().numpy(), ref) < tol
+
+
+def test_fused_prefill_f32_and_strided_rows(cuda_device):
+    """f32 activations take the same fused pass; rows not 16-byte aligned fall back to two steps."""
+    _, fields = _weight(cuda_device, 256, 1024, seed=71)
+    x32 = _activations(cuda_device, 64, 1024, seed=72).float() * 1.0001  # not representable in bf16
+    assert _same_bits(iq3_s_fp8_linear(x32, fields, out_dtype=torch.float32),
+                      _two_step(x32, fields, torch.float32, None))
+    kernels = _our_kernels(lambda: iq3_s_fp8_linear(x32, fields))
+    assert not kernels or len(kernels) == 2, kernels
+    for pad in (8, 3):
+        big = _activations(cuda_device, 48, 1024 + pad, seed=73 + pad)
+        x = big[:, :1024]
+        fused = iq3_s_fp8_linear(x, fields, out_dtype=torch.float32)
+        assert _same_bits(fused, _two_step(x.contiguous(), fields, torch.float32, None)), pad
+        kernels = _our_kernels(lambda: iq3_s_fp8_linear(x, fields))
+        assert not kernels or len(kernels) == (2 if pad % 8 == 0 else 3), (pad, kernels)
 
 
 def test_fused_f32_activations(cuda_device):

@@ -197,3 +197,37 @@ def test_default_path_sizes_its_workspace_on_a_fresh_stream(cuda_device):
         out = launch_iq3_s_fp8_matmul(xq, xs, fields, stream=stream)
     stream.synchronize()
     assert O.relative_frobenius(to_np(out), ref) < ORACLE_FROB_TOL
+
+
+@pytest.mark.parametrize("m,n,k,outliers", [(32, 256, 2048, False), (130, 384, 4096, True), (257, 136, 3072, False),
+                                            (64, 1024, 7168, True)])
+@pytest.mark.parametrize("split", [2, 3, 8])
+def test_gemm_k_split_matches_oracle(cuda_device, m, n, k, outliers, split):
+    """The FP16 GEMM with each output tile's K blocks split over CTAs (partials summed in K order)."""
+    fields, xq, xs, ref = _case(cuda_device, m, n, k, seed=1300 + m + n + split, outliers=outliers)
+    cfg = dict(GEMM_F16, split=split)
+    out = launch_iq3_s_fp8_matmul(xq, xs, fields, config=cfg)
+    got = to_np(out).astype(np.float64)
+    assert O.relative_frobenius(got, ref) < ORACLE_FROB_TOL
+    np.testing.assert_allclose(got, ref, rtol=5e-4, atol=5e-4 * np.abs(ref).max())
+    # Deterministic (the sum order does not depend on which part arrives last), and the counters
+    # are left zero: a second call and a GEMV call after it give the same answers.
+    again = launch_iq3_s_fp8_matmul(xq, xs, fields, config=cfg)
+    assert torch.equal(out, again)
+    bf = launch_iq3_s_fp8_matmul(xq, xs, fields, config=cfg, out_dtype=torch.bfloat16)
+    assert O.relative_frobenius(to_np(bf.float()), ref) < 4e-3
+    x8 = xq[:8].contiguous(), xs[:8].contiguous()
+    small = launch_iq3_s_fp8_matmul(*x8, fields)
+    assert O.relative_frobenius(to_np(small), ref[:8]) < ORACLE_FROB_TOL
+
+
+def test_default_split_on_few_tiles_matches_oracle(cuda_device):
+    """Llama-3-70B O projection at 64 tokens: 64 output tiles, so the default config splits K."""
+    from mambo_b200.kernels.iq3_s_fp8 import select_config
+
+    fields, xq, xs, ref = _case(cuda_device, 64, 8192, 8192, seed=1401, outliers=True)
+    out = launch_iq3_s_fp8_matmul(xq, xs, fields)
+    assert O.relative_frobenius(to_np(out), ref) < ORACLE_FROB_TOL
+    assert select_config(64, 8192, 8192, cuda_device)["kernel"] in (_lib.MAMBO_KERNEL_AUTO,
+                                                                    _lib.MAMBO_KERNEL_GEMM_F16,
+                                                                    _lib.MAMBO_KERNEL_GEMM_F16_PAIR)

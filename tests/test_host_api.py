@@ -69,3 +69,43 @@ def test_install_as_mambo_aliases_modules():
     import mambo.kernels.iq3_s_fp8 as alias  # noqa: F401
 
     assert sys.modules["mambo.kernels.iq3_s_fp8"] is iq3_s_fp8
+
+
+def test_m_buckets_keep_gemv_and_gemm_apart():
+    b = iq3_s_fp8._m_bucket
+    assert [b(m) for m in (1, 8, 9, 16, 17, 31)] == [8, 8, 16, 16, 31, 31]
+    assert [b(m) for m in (32, 33, 64, 512, 513, 8192)] == [32, 64, 64, 512, 1024, 8192]
+
+
+def test_gemm_search_spaces():
+    from mambo_b200 import _lib
+
+    f16 = iq3_s_fp8.config_search_space(_lib.MAMBO_KERNEL_GEMM_F16)
+    assert {(c["stages"], c["split"]) for c in f16} == {(s, k) for s in (2, 3, 4) for k in (1, 2, 3, 4, 6, 8)}
+    pair = iq3_s_fp8.config_search_space(_lib.MAMBO_KERNEL_GEMM_F16_PAIR)
+    assert {c["stages"] for c in pair} == {2, 3, 4} and all(c["split"] == 0 for c in pair)
+    gemv = iq3_s_fp8.config_search_space(_lib.MAMBO_KERNEL_GEMV)
+    assert {c["split"] for c in gemv} == {0, 1, 2}
+
+
+def _default(m, n, k):
+    import ctypes
+
+    from mambo_b200 import _lib
+
+    c = _lib.MamboLinearConfig()
+    _lib.check(_lib.load().mambo_default_config(m, n, k // 256, ctypes.byref(c)))
+    return c.to_dict()
+
+
+def test_default_gemm_k_split_follows_the_tile_count():
+    """No GPU: the default for a 148-SM device. Few output tiles (Llama-3-70B O at 64 tokens:
+    64 tiles) split K; many tiles (8B gate at 2048 tokens) do not; decode stays on the GEMV."""
+    from mambo_b200 import _lib
+
+    o70 = _default(64, 8192, 8192)
+    assert o70["kernel"] == _lib.MAMBO_KERNEL_GEMM_F16 and o70["split"] == 2
+    down70 = _default(64, 8192, 28672)
+    assert down70["split"] == 2
+    assert _default(2048, 14336, 4096)["split"] == 1
+    assert _default(8, 4096, 4096)["kernel"] == _lib.MAMBO_KERNEL_GEMV
