@@ -224,6 +224,43 @@ MAMBO_API int mambo_iq3s_linear_group(const MamboLinearItem* items, int count, c
 /* Workspace bytes mambo_iq3s_linear_group needs for these items. */
 MAMBO_API size_t mambo_iq3s_linear_group_workspace_bytes(const MamboLinearItem* items, int count);
 
+/*
+ * The linear's output quantized to MXFP8 for the next linear, as
+ * mambo_quantize_mxfp8(out, round to nearest even) would give it: q E4M3
+ * [M, N] (row stride ldq), s UE8M0 [M, N/32] (row stride lds). N % 32 == 0.
+ */
+typedef struct MamboQuantOut {
+  uint8_t* q;
+  int64_t ldq;
+  uint8_t* s;
+  int64_t lds;
+} MamboQuantOut;
+
+/*
+ * mambo_iq3s_linear, mambo_iq3s_linear_fused and mambo_iq3s_linear_group that
+ * also write the output's MXFP8 quantization (qout; NULL, or an entry whose q
+ * is NULL, writes none). On the tcgen05 GEMV (M < 32, packed weights) the
+ * epilogue forms it where each output value is final -- a warp owns 32
+ * consecutive output features, one MXFP8 group per token -- so the next
+ * linear takes MXFP8 activations without a quantization pass; the codes are
+ * bit-identical to quantizing the stored output (bf16 or f32) separately.
+ * Elsewhere the quantizer runs on out after the linear. The workspace is that
+ * of the call without qout. qouts of the group: count entries.
+ * Replaces the launch_quantize_fp8 call on a linear's output that the next
+ * linear needs (src/python/mambo/kernels/quantize_fp8.py:42-52,67-84).
+ */
+MAMBO_API int mambo_iq3s_linear_q(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t ldxs, int64_t m,
+                                  const MamboIQ3SWeight* w, const uint32_t* fp8_table, void* out, int out_dtype,
+                                  int64_t ldo, const MamboQuantOut* qout, const MamboLinearConfig* cfg,
+                                  void* workspace, size_t workspace_bytes, mambo_stream_t stream);
+MAMBO_API int mambo_iq3s_linear_fused_q(const void* x, int x_dtype, int64_t ldx, int64_t m, const MamboIQ3SWeight* w,
+                                        const uint32_t* fp8_table, void* out, int out_dtype, int64_t ldo,
+                                        const MamboQuantOut* qout, const MamboLinearConfig* cfg, void* workspace,
+                                        size_t workspace_bytes, mambo_stream_t stream);
+MAMBO_API int mambo_iq3s_linear_group_q(const MamboLinearItem* items, const MamboQuantOut* qouts, int count,
+                                        const uint32_t* fp8_table, void* workspace, size_t workspace_bytes,
+                                        mambo_stream_t stream);
+
 /* Workspace bytes mambo_iq3s_linear needs for this shape and configuration. */
 MAMBO_API size_t mambo_iq3s_linear_workspace_bytes(int64_t m, int64_t n_rows, int64_t n_blocks, const MamboLinearConfig* cfg);
 

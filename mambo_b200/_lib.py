@@ -51,6 +51,9 @@ EXPORTED_SYMBOLS = (
     "mambo_iq3s_linear_fused_workspace_bytes",
     "mambo_iq3s_linear_group",
     "mambo_iq3s_linear_group_workspace_bytes",
+    "mambo_iq3s_linear_q",
+    "mambo_iq3s_linear_fused_q",
+    "mambo_iq3s_linear_group_q",
     "mambo_num_configs",
     "mambo_config_at",
     "mambo_default_config",
@@ -89,6 +92,17 @@ class MamboLinearItem(ctypes.Structure):
 
 
 MAMBO_MAX_GROUP = 32
+
+
+class MamboQuantOut(ctypes.Structure):
+    """A linear's output quantized to MXFP8 for the next linear: q [M,N] E4M3, s [M,N/32] UE8M0."""
+
+    _fields_ = [
+        ("q", ctypes.c_void_p),
+        ("ldq", ctypes.c_int64),
+        ("s", ctypes.c_void_p),
+        ("lds", ctypes.c_int64),
+    ]
 
 
 class MamboLinearConfig(ctypes.Structure):
@@ -175,6 +189,19 @@ def load() -> ctypes.CDLL:
             "mambo_iq3s_linear_group": (
                 [ctypes.POINTER(MamboLinearItem), i32, vp, vp, ctypes.c_size_t, vp], i32),
             "mambo_iq3s_linear_group_workspace_bytes": ([ctypes.POINTER(MamboLinearItem), i32], ctypes.c_size_t),
+            "mambo_iq3s_linear_q": (
+                [vp, i64, vp, i64, i64, ctypes.POINTER(MamboIQ3SWeight), vp, vp, i32, i64,
+                 ctypes.POINTER(MamboQuantOut), ctypes.POINTER(MamboLinearConfig), vp, ctypes.c_size_t, vp],
+                i32,
+            ),
+            "mambo_iq3s_linear_fused_q": (
+                [vp, i32, i64, i64, ctypes.POINTER(MamboIQ3SWeight), vp, vp, i32, i64,
+                 ctypes.POINTER(MamboQuantOut), ctypes.POINTER(MamboLinearConfig), vp, ctypes.c_size_t, vp],
+                i32,
+            ),
+            "mambo_iq3s_linear_group_q": (
+                [ctypes.POINTER(MamboLinearItem), ctypes.POINTER(MamboQuantOut), i32, vp, vp, ctypes.c_size_t, vp],
+                i32),
             "mambo_num_configs": ([i32], i32),
             "mambo_config_at": ([i32, i32, ctypes.POINTER(MamboLinearConfig)], i32),
             "mambo_default_config": ([i64, i64, i64, ctypes.POINTER(MamboLinearConfig)], i32),

@@ -301,25 +301,19 @@ int gemm_f16_clamp_split(int split, int64_t m, int64_t n, int64_t b) {
   return ks;
 }
 
-// The K split the FP16 GEMM takes by default: the one with the shortest
-// estimated makespan, counting in K blocks of one CTA: waves of work items
-// (items spread round-robin over the SMs) times an item's blocks, plus about
-// two blocks of pipeline fill per item and one and a half for publishing and
-// summing the FP32 partials of a split tile.
+// The K split the FP16 GEMM takes by default: only when the output tiles
+// leave SMs idle, the most parts (up to 4, at least 8 K blocks each) that
+// still run as one wave of work items. Measured on B200: splitting a launch
+// that already fills the SMs costs more in partials and per-item pipeline
+// fill than it gains in balance (Llama-3-8B down at 2048 tokens, 512 tiles:
+// 308 -> 349 us with two parts), while 64 tiles at 64 tokens gain (Llama-3-70B
+// O: 52 -> 41 us with two parts). The autotuner searches up to 8 parts.
 int gemm_f16_default_split(int64_t m, int64_t n, int64_t b, int sms) {
   const int64_t tiles = gemm_f16_out_tiles(m, n);
-  double best = 0.0;
-  int best_ks = 1;
-  for (int ks = 1; ks <= kGemmMaxSplit; ++ks) {
-    if (gemm_f16_clamp_split(ks, m, n, b) != ks) break;
-    const int64_t waves = (tiles * ks + sms - 1) / sms;
-    const double cost = (double)waves * ((double)b / ks + 2.0 + (ks > 1 ? 1.5 : 0.0));
-    if (ks == 1 || cost < best) {
-      best = cost;
-      best_ks = ks;
-    }
-  }
-  return best_ks;
+  int ks = 1;
+  for (int k = 2; k <= 4; ++k)
+    if (tiles * k <= sms && b / k >= 8 && gemm_f16_clamp_split(k, m, n, b) == k) ks = k;
+  return ks;
 }
 
 // The FP16 GEMM's workspace: the counter region (the GEMVs' counters left
@@ -495,7 +489,7 @@ int launch_tc_chunk(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t 
                     const MamboIQ3SWeight* w, const uint32_t* fp8_table, void* out, int out_dtype, int64_t ldo,
                     const MamboLinearConfig& c, const GemvPlan& P, const DeviceInfo& info, int* counters,
                     float* partials, uint8_t* xcopy, uint8_t* xscopy, cudaStream_t stream,
-                    const uint16_t* x_bf16 = nullptr, int64_t ldx = 0) {
+                    const uint16_t* x_bf16 = nullptr, int64_t ldx = 0, const MamboQuantOut* qo = nullptr) {
   GemvTmMaps maps;
   std::memset(&maps, 0, sizeof(maps));
   const uintptr_t fields[5] = {(uintptr_t)w->d, (uintptr_t)w->qs, (uintptr_t)w->qh, (uintptr_t)w->signs,
@@ -551,10 +545,41 @@ int launch_tc_chunk(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t 
   p.total_units = P.units;
   p.x_bf16 = x_bf16;
   p.ldx = ldx;
+  if (qo && qo->q) {  // quantized output for the next linear, written by the epilogue
+    p.q_out = qo->q;
+    p.ldq = qo->ldq;
+    p.s_out = qo->s;
+    p.lds = qo->lds;
+  }
   cudaError_t e = launch_gemv_tm(p, P.nt, c.warps, maps, P.grid, stream);
   if (e != cudaSuccess) return cuda_fail(e, "iq3s_gemv_tm");
   return MAMBO_OK;
 }
+
+bool want_qout(const MamboQuantOut* qo) { return qo != nullptr && qo->q != nullptr; }
+
+int check_qout(const MamboQuantOut* qo, int64_t n, int64_t m) {
+  if (!want_qout(qo)) return MAMBO_OK;
+  if (!qo->s) return fail(MAMBO_EINVAL, "quantized output: null scale pointer");
+  if (n % 32) return fail(MAMBO_EINVAL, "quantized output needs N %% 32 == 0 (N=%lld)", (long long)n);
+  if (qo->ldq < n || qo->lds < n / 32) return fail(MAMBO_EINVAL, "quantized output row stride is smaller than the row");
+  (void)m;
+  return MAMBO_OK;
+}
+
+// The quantized output chunk of tokens [m0, ...).
+MamboQuantOut qout_rows(const MamboQuantOut* qo, int64_t m0) {
+  MamboQuantOut r{};
+  if (want_qout(qo)) r = MamboQuantOut{qo->q + m0 * qo->ldq, qo->ldq, qo->s + m0 * qo->lds, qo->lds};
+  return r;
+}
+
+int linear_impl(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t ldxs, int64_t m, const MamboIQ3SWeight* w,
+                const uint32_t* fp8_table, void* out, int out_dtype, int64_t ldo, const MamboQuantOut* qo,
+                const MamboLinearConfig* cfg, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+int fused_impl(const void* x, int x_dtype, int64_t ldx, int64_t m, const MamboIQ3SWeight* w, const uint32_t* fp8_table,
+               void* out, int out_dtype, int64_t ldo, const MamboQuantOut* qo, const MamboLinearConfig* cfg,
+               void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
 }  // namespace
 
@@ -762,6 +787,34 @@ size_t mambo_iq3s_linear_workspace_bytes(int64_t m, int64_t n_rows, int64_t n_bl
 int mambo_iq3s_linear(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t ldxs, int64_t m,
                       const MamboIQ3SWeight* w, const uint32_t* fp8_table, void* out, int out_dtype, int64_t ldo,
                       const MamboLinearConfig* cfg, void* workspace, size_t workspace_bytes, mambo_stream_t stream) {
+  return linear_impl(xq, ldxq, xs, ldxs, m, w, fp8_table, out, out_dtype, ldo, nullptr, cfg, workspace,
+                     workspace_bytes, (cudaStream_t)stream);
+}
+
+int mambo_iq3s_linear_q(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t ldxs, int64_t m,
+                        const MamboIQ3SWeight* w, const uint32_t* fp8_table, void* out, int out_dtype, int64_t ldo,
+                        const MamboQuantOut* qout, const MamboLinearConfig* cfg, void* workspace,
+                        size_t workspace_bytes, mambo_stream_t stream) {
+  return linear_impl(xq, ldxq, xs, ldxs, m, w, fp8_table, out, out_dtype, ldo, qout, cfg, workspace, workspace_bytes,
+                     (cudaStream_t)stream);
+}
+
+}  // extern "C"
+
+namespace {
+
+// Runs the quantizer on a finished linear's output when the caller asked for
+// its MXFP8 quantization and the kernel did not form it in its epilogue.
+int quantize_output_after(int st, const MamboQuantOut* qo, const void* out, int out_dtype, int64_t m, int64_t n,
+                          int64_t ldo, cudaStream_t stream) {
+  if (st != MAMBO_OK || !want_qout(qo)) return st;
+  return mambo_quantize_mxfp8(out, out_dtype, m, n, ldo, qo->q, qo->ldq, qo->s, qo->lds, MAMBO_ROUND_NEAREST_EVEN,
+                              stream);
+}
+
+int linear_impl(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t ldxs, int64_t m, const MamboIQ3SWeight* w,
+                const uint32_t* fp8_table, void* out, int out_dtype, int64_t ldo, const MamboQuantOut* qo,
+                const MamboLinearConfig* cfg, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   if (!xq || !xs || !w || !fp8_table || !out) return fail(MAMBO_EINVAL, "null pointer");
   if (!w->d || !w->qs || !w->qh || !w->signs || !w->scales) return fail(MAMBO_EINVAL, "null weight field");
   if (w->n_rows < 1 || w->n_blocks < 1) return fail(MAMBO_EINVAL, "IQ3_S weight must have positive N and K");
@@ -773,6 +826,7 @@ int mambo_iq3s_linear(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_
   if (ldxs < k / 32) return fail(MAMBO_EINVAL, "x_scales row stride is smaller than K/32");
   if (out_dtype != MAMBO_F32 && out_dtype != MAMBO_BF16) return fail(MAMBO_EINVAL, "out must be f32 or bf16");
   if (ldo < w->n_rows) return fail(MAMBO_EINVAL, "out row stride is smaller than N");
+  if (check_qout(qo, w->n_rows, m) != MAMBO_OK) return g_last_code;
   DeviceInfo info;
   int st = require_sm100(&info);
   if (st != MAMBO_OK) return st;
@@ -784,10 +838,12 @@ int mambo_iq3s_linear(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_
       st = validate_config(&c, 32, w->n_blocks, info);
       if (st != MAMBO_OK) return st;
       if (is_gemm_f16(c.kernel))
-        return launch_gemm_f16_path(GemmF16Source{xq, ldxq, xs, ldxs, nullptr, 0, 0}, m, w, fp8_table, out,
-                                    out_dtype, ldo, c, info, workspace, workspace_bytes, (cudaStream_t)stream);
-      return launch_gemm(xq, ldxq, xs, ldxs, m, w, fp8_table, out, out_dtype, ldo, c, info, workspace,
-                         workspace_bytes, (cudaStream_t)stream);
+        st = launch_gemm_f16_path(GemmF16Source{xq, ldxq, xs, ldxs, nullptr, 0, 0}, m, w, fp8_table, out, out_dtype,
+                                  ldo, c, info, workspace, workspace_bytes, stream);
+      else
+        st = launch_gemm(xq, ldxq, xs, ldxs, m, w, fp8_table, out, out_dtype, ldo, c, info, workspace,
+                         workspace_bytes, stream);
+      return quantize_output_after(st, qo, out, out_dtype, m, w->n_rows, ldo, stream);
     }
     if (cfg && is_gemm(cfg->kernel))
       return fail(MAMBO_EINVAL,
@@ -826,9 +882,10 @@ int mambo_iq3s_linear(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_
     uint8_t* xscopy = xcopy + P.xcopy_bytes;
 
     if (tc) {
+      const MamboQuantOut qc = qout_rows(qo, m0);  // the epilogue quantizes this chunk's outputs
       st = launch_tc_chunk(xq + m0 * ldxq, ldxq, xs + m0 * ldxs, ldxs, mc, w, fp8_table,
                            (uint8_t*)out + m0 * ldo * esz, out_dtype, ldo, c, P, info, counters, partials, xcopy,
-                           xscopy, (cudaStream_t)stream);
+                           xscopy, stream, nullptr, 0, &qc);
       if (st != MAMBO_OK) return st;
       continue;
     }
@@ -862,12 +919,18 @@ int mambo_iq3s_linear(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_
       p.row_tiles = P.row_tiles;
       p.total_units = P.units;
       p.x_bulk = ((uintptr_t)p.xq % 16 == 0) && (ldxq % 16 == 0);
-      e = launch_gemv(p, P.nt, have_maps, maps, P.grid, (cudaStream_t)stream);
+      e = launch_gemv(p, P.nt, have_maps, maps, P.grid, stream);
       if (e != cudaSuccess) return cuda_fail(e, "iq3s_gemv_sync");
     }
   }
-  return ok();
+  // The legacy GEMV has no quantizing epilogue.
+  st = tc ? MAMBO_OK : quantize_output_after(MAMBO_OK, qo, out, out_dtype, m, w->n_rows, ldo, stream);
+  return st == MAMBO_OK ? ok() : st;
 }
+
+}  // namespace
+
+extern "C" {
 
 size_t mambo_iq3s_linear_fused_workspace_bytes(int64_t m, int64_t n_rows, int64_t n_blocks,
                                                const MamboLinearConfig* cfg) {
@@ -880,6 +943,25 @@ int mambo_iq3s_linear_fused(const void* x, int x_dtype, int64_t ldx, int64_t m, 
                             const uint32_t* fp8_table, void* out, int out_dtype, int64_t ldo,
                             const MamboLinearConfig* cfg, void* workspace, size_t workspace_bytes,
                             mambo_stream_t stream) {
+  return fused_impl(x, x_dtype, ldx, m, w, fp8_table, out, out_dtype, ldo, nullptr, cfg, workspace, workspace_bytes,
+                    (cudaStream_t)stream);
+}
+
+int mambo_iq3s_linear_fused_q(const void* x, int x_dtype, int64_t ldx, int64_t m, const MamboIQ3SWeight* w,
+                              const uint32_t* fp8_table, void* out, int out_dtype, int64_t ldo,
+                              const MamboQuantOut* qout, const MamboLinearConfig* cfg, void* workspace,
+                              size_t workspace_bytes, mambo_stream_t stream) {
+  return fused_impl(x, x_dtype, ldx, m, w, fp8_table, out, out_dtype, ldo, qout, cfg, workspace, workspace_bytes,
+                    (cudaStream_t)stream);
+}
+
+}  // extern "C"
+
+namespace {
+
+int fused_impl(const void* x, int x_dtype, int64_t ldx, int64_t m, const MamboIQ3SWeight* w, const uint32_t* fp8_table,
+               void* out, int out_dtype, int64_t ldo, const MamboQuantOut* qo, const MamboLinearConfig* cfg,
+               void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   if (!x || !w || !fp8_table || !out) return fail(MAMBO_EINVAL, "null pointer");
   if (!w->d || !w->qs || !w->qh || !w->signs || !w->scales) return fail(MAMBO_EINVAL, "null weight field");
   if (w->n_rows < 1 || w->n_blocks < 1) return fail(MAMBO_EINVAL, "IQ3_S weight must have positive N and K");
@@ -890,6 +972,7 @@ int mambo_iq3s_linear_fused(const void* x, int x_dtype, int64_t ldx, int64_t m, 
   if (ldx < k) return fail(MAMBO_EINVAL, "activation row stride is smaller than K");
   if (out_dtype != MAMBO_F32 && out_dtype != MAMBO_BF16) return fail(MAMBO_EINVAL, "out must be f32 or bf16");
   if (ldo < w->n_rows) return fail(MAMBO_EINVAL, "out row stride is smaller than N");
+  if (check_qout(qo, w->n_rows, m) != MAMBO_OK) return g_last_code;
   DeviceInfo info;
   int st = require_sm100(&info);
   if (st != MAMBO_OK) return st;
@@ -922,7 +1005,7 @@ int mambo_iq3s_linear_fused(const void* x, int x_dtype, int64_t ldx, int64_t m, 
       int* counters = (int*)workspace;
       float* partials = (float*)((uint8_t*)workspace + P.counters_bytes);
       st = launch_tc_chunk(nullptr, 0, nullptr, 0, m, w, fp8_table, out, out_dtype, ldo, c, P, info, counters,
-                           partials, nullptr, nullptr, (cudaStream_t)stream, (const uint16_t*)x, ldx);
+                           partials, nullptr, nullptr, stream, (const uint16_t*)x, ldx, qo);
       return st == MAMBO_OK ? ok() : st;
     }
   }
@@ -935,7 +1018,8 @@ int mambo_iq3s_linear_fused(const void* x, int x_dtype, int64_t ldx, int64_t m, 
     st = validate_config(&c, 32, w->n_blocks, info);
     if (st != MAMBO_OK) return st;
     st = launch_gemm_f16_path(GemmF16Source{nullptr, 0, nullptr, 0, x, x_dtype, ldx}, m, w, fp8_table, out,
-                              out_dtype, ldo, c, info, workspace, workspace_bytes, (cudaStream_t)stream);
+                              out_dtype, ldo, c, info, workspace, workspace_bytes, stream);
+    st = quantize_output_after(st, qo, out, out_dtype, m, w->n_rows, ldo, stream);
     return st == MAMBO_OK ? ok() : st;
   }
   // Otherwise: quantize into the workspace, then the linear.
@@ -947,8 +1031,13 @@ int mambo_iq3s_linear_fused(const void* x, int x_dtype, int64_t ldx, int64_t m, 
   uint8_t* xs = xq + align256((size_t)(m * k));
   st = mambo_quantize_mxfp8(x, x_dtype, m, k, ldx, xq, k, xs, k / 32, MAMBO_ROUND_NEAREST_EVEN, stream);
   if (st != MAMBO_OK) return st;
-  return mambo_iq3s_linear(xq, k, xs, k / 32, m, w, fp8_table, out, out_dtype, ldo, cfg, workspace, lin, stream);
+  return linear_impl(xq, k, xs, k / 32, m, w, fp8_table, out, out_dtype, ldo, qo, cfg, workspace, lin, stream);
 }
+
+}  // namespace
+
+extern "C" {
+
 
 }  // extern "C"
 
@@ -1043,6 +1132,12 @@ size_t mambo_iq3s_linear_group_workspace_bytes(const MamboLinearItem* items, int
 
 int mambo_iq3s_linear_group(const MamboLinearItem* items, int count, const uint32_t* fp8_table, void* workspace,
                             size_t workspace_bytes, mambo_stream_t stream) {
+  return mambo_iq3s_linear_group_q(items, nullptr, count, fp8_table, workspace, workspace_bytes, stream);
+}
+
+int mambo_iq3s_linear_group_q(const MamboLinearItem* items, const MamboQuantOut* qouts, int count,
+                              const uint32_t* fp8_table, void* workspace, size_t workspace_bytes,
+                              mambo_stream_t stream) {
   if (!items || !fp8_table) return fail(MAMBO_EINVAL, "null pointer");
   if (count < 1) return fail(MAMBO_EINVAL, "a group needs at least one linear");
   for (int i = 0; i < count; ++i) {
@@ -1058,6 +1153,7 @@ int mambo_iq3s_linear_group(const MamboLinearItem* items, int count, const uint3
     if (it.out_dtype != MAMBO_F32 && it.out_dtype != MAMBO_BF16)
       return fail(MAMBO_EINVAL, "item %d: out must be f32 or bf16", i);
     if (it.ldo < w->n_rows) return fail(MAMBO_EINVAL, "item %d: out row stride is smaller than N", i);
+    if (qouts && check_qout(&qouts[i], w->n_rows, it.m) != MAMBO_OK) return g_last_code;
   }
   if (!workspace || (uintptr_t)workspace % 256) return fail(MAMBO_EINVAL, "workspace must be 256-byte aligned");
   DeviceInfo info;
@@ -1067,8 +1163,8 @@ int mambo_iq3s_linear_group(const MamboLinearItem* items, int count, const uint3
     // One call per item, in order, on the stream (they share the workspace).
     for (int i = 0; i < count; ++i) {
       const MamboLinearItem& it = items[i];
-      st = mambo_iq3s_linear_fused(it.x, it.x_dtype, it.ldx, it.m, it.w, fp8_table, it.out, it.out_dtype, it.ldo,
-                                   nullptr, workspace, workspace_bytes, stream);
+      st = fused_impl(it.x, it.x_dtype, it.ldx, it.m, it.w, fp8_table, it.out, it.out_dtype, it.ldo,
+                      qouts ? &qouts[i] : nullptr, nullptr, workspace, workspace_bytes, (cudaStream_t)stream);
       if (st != MAMBO_OK) return st;
     }
     return ok();
@@ -1097,6 +1193,12 @@ int mambo_iq3s_linear_group(const MamboLinearItem* items, int count, const uint3
     gi.out_bf16 = it.out_dtype == MAMBO_BF16;
     gi.unit0 = units;
     gi.tile0 = tiles;
+    if (qouts && want_qout(&qouts[i])) {  // N % 32 == 0 was checked: the epilogue quantizes the output
+      gi.q_out = qouts[i].q;
+      gi.ldq = qouts[i].ldq;
+      gi.s_out = qouts[i].s;
+      gi.lds = qouts[i].lds;
+    }
     if (!make_gemv_xb_map(gi.x, it.ldx, gi.m, w->n_blocks * 256, box, &g.xb[i]))
       return fail(MAMBO_EINVAL, "item %d: bf16 activations need 16-byte aligned rows", i);
     units += rt * gi.n_blocks;

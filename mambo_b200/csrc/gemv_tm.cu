@@ -136,21 +136,46 @@ __device__ __forceinline__ int cta_of_unit_tm(int u, int grid, int units) {
   return (int)((((int64_t)u + 1) * grid - 1) / units);
 }
 
-// Where one linear's results go.
+// Where one linear's results go: out, and optionally its MXFP8 quantization
+// for the next linear (q: E4M3 bytes, s: UE8M0 codes; n_rows % 32 == 0).
 struct OutView {
   void* out;
   int64_t ldo;
   int out_bf16;
   int n_rows;
   int m;
+  uint8_t* q;
+  int64_t ldq;
+  uint8_t* s;
+  int64_t lds;
 };
 
+// Stores the final value v of (row, tok). Called by all 32 lanes of a warp
+// together, for 32 consecutive rows (a warp's lanes are consecutive TMEM rows
+// of a 128-row tile) and one token: with q set, those 32 outputs are one
+// MXFP8 group of the next linear's activation row `tok`, quantized here as
+// the standalone quantizer quantizes the stored values (largest magnitude by
+// one warp reduction; a NaN or infinity gives the scale code 0xFF; values
+// times 2^-e rounded to nearest even with saturation).
 __device__ __forceinline__ void store_out_tm(const OutView& o, int row, int tok, float v) {
-  if (row < o.n_rows && tok < o.m) {
+  const bool in = row < o.n_rows;
+  if (tok < o.m) {
     if (o.out_bf16) {
-      reinterpret_cast<__nv_bfloat16*>(o.out)[(int64_t)tok * o.ldo + row] = __float2bfloat16_rn(v);
-    } else {
+      const __nv_bfloat16 b = __float2bfloat16_rn(v);
+      if (in) reinterpret_cast<__nv_bfloat16*>(o.out)[(int64_t)tok * o.ldo + row] = b;
+      v = __bfloat162float(b);  // what a reader of out sees
+    } else if (in) {
       reinterpret_cast<float*>(o.out)[(int64_t)tok * o.ldo + row] = v;
+    }
+    if (o.q != nullptr) {  // warp-uniform
+      const uint32_t mag = in ? (__float_as_uint(v) & 0x7FFFFFFFu) : 0u;
+      const uint32_t amax = __reduce_max_sync(0xFFFFFFFFu, mag);  // NaN bits order above every number
+      const uint32_t code = mxfp8_scale_code(__uint_as_float(amax));
+      const float inv = e8m0_to_float(code == 0xFFu ? 0u : 254u - code);
+      if (in) {
+        o.q[(int64_t)tok * o.ldq + row] = (uint8_t)(cvt_e4m3x2_rn(v * inv, 0.f) & 0xFFu);
+        if ((row & 31) == 0) o.s[(int64_t)tok * o.lds + row / 32] = (uint8_t)code;
+      }
     }
   }
 }
@@ -762,12 +787,12 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
     // The linear of unit `it`: its output, K blocks, first unit and first row
     // tile in the launch's numbering, row tiles (a grouped launch moves to the
     // next item when they are done; a single linear has one).
-    OutView ov{p.out, p.ldo, p.out_bf16, p.n_rows, p.m};
+    OutView ov{p.out, p.ldo, p.out_bf16, p.n_rows, p.m, p.q_out, p.ldq, p.s_out, p.lds};
     int cur_nb = p.n_blocks, cur_unit0 = 0, cur_tile0 = 0, cur_tiles = 0, item = 0;
     auto load_item = [&](int l) {
       if constexpr (kGroup) {
         const GemvItem& gi = grp.items[l];
-        ov = OutView{gi.out, gi.ldo, gi.out_bf16, gi.n_rows, gi.m};
+        ov = OutView{gi.out, gi.ldo, gi.out_bf16, gi.n_rows, gi.m, gi.q_out, gi.ldq, gi.s_out, gi.lds};
         cur_nb = gi.n_blocks;
         cur_unit0 = gi.unit0;
         cur_tile0 = gi.tile0;

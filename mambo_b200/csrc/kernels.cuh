@@ -150,6 +150,13 @@ struct GemvTmParams {
   // rows) quantized to MXFP8 in the kernel instead of read as xq/xs; null: TMA.
   const uint16_t* x_bf16;
   int64_t ldx;
+  // Optional MXFP8 quantization of the output for the next linear (null q_out:
+  // none; needs n_rows % 32 == 0): q_out [m][ldq] E4M3 and s_out [m][lds] UE8M0
+  // of the values as stored in out, round to nearest even.
+  uint8_t* q_out;
+  int64_t ldq;
+  uint8_t* s_out;
+  int64_t lds;
 };
 
 struct GemvTmMaps {
@@ -174,6 +181,10 @@ struct GemvItem {
   int out_bf16;
   int unit0;  // first unit of this item in the launch's numbering
   int tile0;  // first row tile of this item in the launch's numbering
+  uint8_t* q_out;  // optional MXFP8 quantization of out (as GemvTmParams::q_out)
+  int64_t ldq;
+  uint8_t* s_out;
+  int64_t lds;
 };
 constexpr int kGemvMaxItems = 32;
 constexpr int kGemvMaxGrid = 256;  // CTAs of a grouped launch (one per SM)

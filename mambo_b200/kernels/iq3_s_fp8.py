@@ -250,8 +250,25 @@ def _sm_count(device: torch.device) -> int:
     return torch.cuda.get_device_properties(device).multi_processor_count
 
 
+def _quant_out_struct(qout) -> "_lib.MamboQuantOut | None":
+    """(q uint8 [M,N], s uint8 [M,N/32]) -> the C ABI's MamboQuantOut (None: no quantized output)."""
+    if qout is None:
+        return None
+    q, sc = qout
+    qo = _lib.MamboQuantOut()
+    qo.q, qo.ldq, qo.s, qo.lds = q.data_ptr(), q.stride(0), sc.data_ptr(), sc.stride(0)
+    return qo
+
+
+def _new_quant_out(m: int, n: int, dev) -> tuple[torch.Tensor, torch.Tensor]:
+    if n % IQ3_S_SCALE_VALUES:
+        raise ValueError("quantize_output needs N divisible by 32")
+    return (torch.empty((m, n), dtype=torch.uint8, device=dev),
+            torch.empty((m, n // IQ3_S_SCALE_VALUES), dtype=torch.uint8, device=dev))
+
+
 def linear_into(x_values: torch.Tensor, x_scales: torch.Tensor, iq3_weight: IQ3SFields, out: torch.Tensor,
-                config: dict | None = None, stream=None) -> torch.Tensor:
+                config: dict | None = None, stream=None, qout=None) -> torch.Tensor:
     """Launch the linear into a preallocated out [M,N] (f32 or bf16). No validation of x beyond the C ABI's."""
     n_rows, blocks = _weight_dimensions(iq3_weight)
     m = x_values.shape[0]
@@ -266,10 +283,10 @@ def linear_into(x_values: torch.Tensor, x_scales: torch.Tensor, iq3_weight: IQ3S
         ws = _runtime.workspace(dev, st, need)
         out_dtype = _lib.MAMBO_BF16 if out.dtype == torch.bfloat16 else _lib.MAMBO_F32
         _lib.check(
-            lib.mambo_iq3s_linear(
+            lib.mambo_iq3s_linear_q(
                 x_values.data_ptr(), x_values.stride(0), x_scales.data_ptr(), x_scales.stride(0), m, w,
-                _get_iq3_table(dev).data_ptr(), out.data_ptr(), out_dtype, out.stride(0), cfg,
-                ws.data_ptr(), ws.numel(), st,
+                _get_iq3_table(dev).data_ptr(), out.data_ptr(), out_dtype, out.stride(0), _quant_out_struct(qout),
+                cfg, ws.data_ptr(), ws.numel(), st,
             ),
             "launch_iq3_s_fp8_matmul",
         )
@@ -277,12 +294,16 @@ def linear_into(x_values: torch.Tensor, x_scales: torch.Tensor, iq3_weight: IQ3S
 
 
 def launch_iq3_s_fp8_matmul(x_values, x_scales, iq3_weight: IQ3SFields, *, stream=None,
-                            out_dtype: torch.dtype = torch.float32, config: dict | None = None) -> torch.Tensor:
+                            out_dtype: torch.dtype = torch.float32, config: dict | None = None,
+                            quantize_output: bool = False):
     """Multiply prepared SoA weights by prequantized MXFP8 activations (iq3_s_fp8.py:364-399).
 
     Returns float32 [M,N] by default (``out_dtype=torch.bfloat16`` for the bf16
     epilogue). Activation views with a non-unit column stride are copied to
-    contiguous memory first.
+    contiguous memory first. ``quantize_output``: also return the output's
+    MXFP8 quantization for the next linear, ``(out, (q, s))`` -- what
+    ``launch_quantize_fp8(out)`` gives, formed in the GEMV's epilogue below 32
+    tokens (N divisible by 32).
     """
     n_rows, k_blocks = _weight_dimensions(iq3_weight)
     k = k_blocks * 256
@@ -303,11 +324,14 @@ def launch_iq3_s_fp8_matmul(x_values, x_scales, iq3_weight: IQ3SFields, *, strea
     if x_scales.stride(1) != 1:
         x_scales = x_scales.contiguous()
     out = torch.empty((x_values.shape[0], n_rows), dtype=out_dtype, device=dev)
+    if quantize_output:
+        qout = _new_quant_out(x_values.shape[0], n_rows, dev)
+        return linear_into(x_values, x_scales, iq3_weight, out, config=config, stream=stream, qout=qout), qout
     return linear_into(x_values, x_scales, iq3_weight, out, config=config, stream=stream)
 
 
 def fused_linear_into(x: torch.Tensor, iq3_weight: IQ3SFields, out: torch.Tensor, config: dict | None = None,
-                      stream=None) -> torch.Tensor:
+                      stream=None, qout=None) -> torch.Tensor:
     """Quantize (round to nearest even) and multiply in one C-ABI call into a preallocated out [M,N].
 
     Below 32 tokens with bf16 rows the tcgen05 GEMV quantizes the activations
@@ -327,9 +351,9 @@ def fused_linear_into(x: torch.Tensor, iq3_weight: IQ3SFields, out: torch.Tensor
         x_dtype = _lib.MAMBO_BF16 if x.dtype == torch.bfloat16 else _lib.MAMBO_F32
         out_dtype = _lib.MAMBO_BF16 if out.dtype == torch.bfloat16 else _lib.MAMBO_F32
         _lib.check(
-            lib.mambo_iq3s_linear_fused(
+            lib.mambo_iq3s_linear_fused_q(
                 x.data_ptr(), x_dtype, x.stride(0), m, w, _get_iq3_table(dev).data_ptr(), out.data_ptr(), out_dtype,
-                out.stride(0), cfg, ws.data_ptr(), ws.numel(), st,
+                out.stride(0), _quant_out_struct(qout), cfg, ws.data_ptr(), ws.numel(), st,
             ),
             "iq3_s_fp8_linear",
         )
@@ -337,17 +361,21 @@ def fused_linear_into(x: torch.Tensor, iq3_weight: IQ3SFields, out: torch.Tensor
 
 
 def iq3_s_fp8_linear(x, iq3_weight: IQ3SFields, *, stream=None, out_dtype: torch.dtype = torch.bfloat16,
-                     rounding: str = "nearest_even", config: dict | None = None) -> torch.Tensor:
+                     rounding: str = "nearest_even", config: dict | None = None, quantize_output: bool = False):
     """bf16/f32 activations [M,K] -> MXFP8 -> IQ3_S linear -> out_dtype [M,N] (quantize + matmul).
 
     Round-to-nearest-even goes through the fused entry point (quantization inside
-    the decode GEMV below 32 tokens); the other rounding modes quantize first.
+    the decode GEMV below 32 tokens, inside the GEMM's FP16 pass from 32); the
+    other rounding modes quantize first. ``quantize_output``: return
+    ``(out, (q, s))`` with the output's MXFP8 quantization for the next linear
+    (see launch_iq3_s_fp8_matmul).
     """
     from .quantize_fp8 import launch_quantize_fp8
 
     if rounding != "nearest_even":
         xq, xs = launch_quantize_fp8(x, stream=stream, rounding=rounding)
-        return launch_iq3_s_fp8_matmul(xq, xs, iq3_weight, stream=stream, out_dtype=out_dtype, config=config)
+        return launch_iq3_s_fp8_matmul(xq, xs, iq3_weight, stream=stream, out_dtype=out_dtype, config=config,
+                                       quantize_output=quantize_output)
     n_rows, k_blocks = _weight_dimensions(iq3_weight)
     x = _runtime.as_cuda_tensor(x)
     if x.ndim != 2 or x.dtype not in (torch.float32, torch.bfloat16) or x.shape[0] < 1 or x.shape[1] != k_blocks * 256:
@@ -361,17 +389,22 @@ def iq3_s_fp8_linear(x, iq3_weight: IQ3SFields, *, stream=None, out_dtype: torch
     if x.stride(1) != 1:
         x = x.contiguous()
     out = torch.empty((x.shape[0], n_rows), dtype=out_dtype, device=dev)
+    if quantize_output:
+        qout = _new_quant_out(x.shape[0], n_rows, dev)
+        return fused_linear_into(x, iq3_weight, out, config=config, stream=stream, qout=qout), qout
     return fused_linear_into(x, iq3_weight, out, config=config, stream=stream)
 
 
-def group_linear_into(xs, iq3_weights, outs, stream=None) -> list:
+def group_linear_into(xs, iq3_weights, outs, stream=None, qouts=None) -> list:
     """Independent linears ``outs[i] = linear(xs[i], iq3_weights[i])`` in one C-ABI call.
 
     Each is what ``iq3_s_fp8_linear`` computes. With bf16 activations in
     16-byte aligned rows, M < 32 and packed weights this is one persistent GEMV
     launch for the whole group (up to ``MAMBO_MAX_GROUP`` linears); otherwise
     the linears run one after another. No output may overlap another linear's
-    input. No validation beyond the C ABI's.
+    input. No validation beyond the C ABI's. ``qouts``: per linear None or
+    ``(q, s)`` buffers for the output's MXFP8 quantization (formed in the
+    grouped launch's epilogue).
     """
     count = len(xs)
     items = (_lib.MamboLinearItem * count)()
@@ -393,8 +426,14 @@ def group_linear_into(xs, iq3_weights, outs, stream=None) -> list:
         st = _runtime.stream_handle(stream, dev)
         need = lib.mambo_iq3s_linear_group_workspace_bytes(items, count)
         ws = _runtime.workspace(dev, st, need)
-        _lib.check(lib.mambo_iq3s_linear_group(items, count, _get_iq3_table(dev).data_ptr(), ws.data_ptr(),
-                                               ws.numel(), st), "iq3_s_fp8_linear_group")
+        qarr = None
+        if qouts is not None:
+            qarr = (_lib.MamboQuantOut * count)()
+            for i, qo in enumerate(qouts):
+                if qo is not None:
+                    qarr[i] = _quant_out_struct(qo)
+        _lib.check(lib.mambo_iq3s_linear_group_q(items, qarr, count, _get_iq3_table(dev).data_ptr(), ws.data_ptr(),
+                                                 ws.numel(), st), "iq3_s_fp8_linear_group")
     return outs
 
 
@@ -443,8 +482,15 @@ def config_search_space(kernel: int = _lib.MAMBO_KERNEL_GEMV) -> list[dict]:
     return out
 
 
-def make_benchmark_cases(iq3_weight, ms: tuple[int, ...] = (4, 128), seed: int = 0) -> list:
-    """Prepare SoA weights and FP8 inputs once; benchmark only the matmul."""
+def make_benchmark_cases(iq3_weight, ms: tuple[int, ...] = (4, 128), seed: int = 0, *,
+                         bf16_input: bool = True) -> list:
+    """Prepare SoA weights and inputs once; benchmark the linear (iq3_s_fp8.py:402-465).
+
+    ``bf16_input``: time what a model calls, bf16 activations through the fused
+    entry point (below 32 tokens the GEMV quantizes them itself; from 32 the
+    quantizer is part of the GEMM's FP16 pass). False: the matmul alone on
+    prequantized MXFP8 activations, as the reference's cases do.
+    """
     from ..utils.kernel_benchmark import BenchmarkCase
     from .quantize_fp8 import launch_quantize_fp8
 
@@ -453,16 +499,26 @@ def make_benchmark_cases(iq3_weight, ms: tuple[int, ...] = (4, 128), seed: int =
     n_rows, k_blocks = _weight_dimensions(iq3_weight)
     k = k_blocks * IQ3_S_BLOCK_VALUES
     dev = iq3_weight.d.device
-    stream = torch.cuda.current_stream(dev)
+    # A stream of its own: candidates are timed as launches captured into a CUDA graph.
+    stream = torch.cuda.Stream(dev)
     gen = torch.Generator(device=dev).manual_seed(seed)
 
     def make_case(m: int) -> BenchmarkCase:
         x = torch.randn((m, k), generator=gen, device=dev, dtype=torch.float32)
-        x_values, x_scales = launch_quantize_fp8(x, stream=stream)
-        out = torch.empty((m, n_rows), dtype=torch.float32, device=dev)
+        stream.wait_stream(torch.cuda.current_stream(dev))
+        if bf16_input:
+            xb = x.to(torch.bfloat16)
+            stream.wait_stream(torch.cuda.current_stream(dev))
+            out = torch.empty((m, n_rows), dtype=torch.bfloat16, device=dev)
 
-        def run(config: dict) -> None:
-            linear_into(x_values, x_scales, iq3_weight, out, config=config, stream=stream)
+            def run(config: dict) -> None:
+                fused_linear_into(xb, iq3_weight, out, config=config, stream=stream)
+        else:
+            x_values, x_scales = launch_quantize_fp8(x, stream=stream)
+            out = torch.empty((m, n_rows), dtype=torch.float32, device=dev)
+
+            def run(config: dict) -> None:
+                linear_into(x_values, x_scales, iq3_weight, out, config=config, stream=stream)
 
         # The untuned default first (the tuner never ends up slower than it), then the
         # kernel's space: below the threshold the tcgen05 GEMV (decoder warps x weight

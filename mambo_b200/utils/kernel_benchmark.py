@@ -44,6 +44,11 @@ class BenchmarkCase:
 
 
 def _event_time_us(case: BenchmarkCase, config: Config, warmup: int, iters: int) -> float:
+    """Mean device time of one launch: `iters` launches captured into one CUDA graph, replayed and timed
+    with CUDA events on the case's stream (eager launches from Python cannot keep a microsecond-scale
+    decode kernel fed; a graph runs them back to back, as a serving step does). Falls back to eager
+    launches when the stream cannot be captured (e.g. the legacy default stream) or a per-launch reset
+    is needed."""
     args = case.args_fn(config)
 
     def launch() -> None:
@@ -53,14 +58,34 @@ def _event_time_us(case: BenchmarkCase, config: Config, warmup: int, iters: int)
 
     with torch.cuda.stream(case.stream):
         for _ in range(warmup):
-            launch()
-        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        start.record(case.stream)
-        for _ in range(iters):
-            launch()
-        stop.record(case.stream)
+            launch()  # eager: sizes the workspace outside any capture
+    case.stream.synchronize()
+    graph = None
+    if case.before_launch_fn is None and case.stream != torch.cuda.default_stream(case.stream.device):
+        try:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=case.stream):
+                for _ in range(iters):
+                    launch()
+        except RuntimeError:
+            graph = None
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(case.stream):
+        if graph is not None:
+            graph.replay()  # warm replay
+            start.record(case.stream)
+            reps = 3
+            for _ in range(reps):
+                graph.replay()
+            stop.record(case.stream)
+        else:
+            reps = 1
+            start.record(case.stream)
+            for _ in range(iters):
+                launch()
+            stop.record(case.stream)
     stop.synchronize()
-    return start.elapsed_time(stop) * 1000.0 / iters
+    return start.elapsed_time(stop) * 1000.0 / (iters * (reps if graph is not None else 1))
 
 
 def mini_benchmark(cases: Sequence[BenchmarkCase], *, warmup: int = 5, iters: int = 20, quiet: bool = False,
