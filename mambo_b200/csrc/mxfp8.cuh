@@ -29,23 +29,25 @@ __device__ __forceinline__ uint32_t cvt_e4m3x2_rn(float lo, float hi) {
   return r;
 }
 
+// The largest magnitude of a 32-value group held by 4 consecutive lanes (8
+// values each; the quad must be converged), the same in all four lanes. The
+// magnitudes' bit patterns are compared as unsigned integers: for numbers
+// that is their order, and every NaN orders above infinity, so a NaN anywhere
+// in the group reaches every lane (and gives the group the scale code 0xFF).
+__device__ __forceinline__ float quad_absmax(const float (&v)[8]) {
+  uint32_t m = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m = max(m, __float_as_uint(v[i]) & 0x7FFFFFFFu);
+  m = max(m, __shfl_xor_sync(0xFFFFFFFFu, m, 1));
+  m = max(m, __shfl_xor_sync(0xFFFFFFFFu, m, 2));
+  return __uint_as_float(m);
+}
+
 // One 32-value group held by 4 consecutive lanes (8 values each; the quad
 // must be converged): returns the group's scale code and this lane's 8 E4M3
 // bytes (value i in byte i % 4 of word i / 4), round-to-nearest-even.
 __device__ __forceinline__ uint32_t mxfp8_quad_rne(const float (&v)[8], uint2& out) {
-  float amax = 0.f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
-  // fmaxf drops NaN; keep it visible so the group gets the NaN scale code.
-  bool any_nan = false;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) any_nan |= (v[i] != v[i]);
-  amax = any_nan ? __uint_as_float(0x7FC00000u) : amax;
-  float other = __shfl_xor_sync(0xFFFFFFFFu, amax, 1);
-  amax = (other != other) ? other : fmaxf(amax, other);
-  other = __shfl_xor_sync(0xFFFFFFFFu, amax, 2);
-  amax = (other != other) ? other : fmaxf(amax, other);
-  const uint32_t code = mxfp8_scale_code(amax);
+  const uint32_t code = mxfp8_scale_code(quad_absmax(v));
   // 2^-e with e = code - 127 (code 0xFF: scale by 2^-127, values become 0 / NaN / +-448).
   const float inv = e8m0_to_float(code == 0xFFu ? 0u : 254u - code);
   uint32_t packed[2];

@@ -89,20 +89,7 @@ __global__ void __launch_bounds__(256) quantize_mxfp8_kernel(const QuantParams p
       for (int i = 0; i < 8; ++i) v[i] = 0.f;
     }
 
-    float amax = 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
-    // fmaxf drops NaN; keep it visible so the group gets the NaN scale code.
-    bool any_nan = false;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) any_nan |= (v[i] != v[i]);
-    amax = any_nan ? __uint_as_float(0x7FC00000u) : amax;
-    float other = __shfl_xor_sync(0xFFFFFFFFu, amax, 1);
-    amax = (other != other) ? other : fmaxf(amax, other);
-    other = __shfl_xor_sync(0xFFFFFFFFu, amax, 2);
-    amax = (other != other) ? other : fmaxf(amax, other);
-
-    const uint32_t code = mxfp8_scale_code(amax);
+    const uint32_t code = mxfp8_scale_code(quad_absmax(v));
     // 2^-e with e = code - 127 (code 0xFF: scale by 2^-127, values become 0 / NaN / +-448).
     const float inv = e8m0_to_float(code == 0xFFu ? 0u : 254u - code);
 

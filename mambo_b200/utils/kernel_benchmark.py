@@ -43,6 +43,11 @@ class BenchmarkCase:
     shape: tuple[int, int, int] | None = field(default=None)  # (M, N, K) the winner is recorded for
 
 
+# Launches captured per timed graph, at least: a case that rotates weight copies
+# (make_benchmark_cases) then takes each copy once per replay.
+MIN_GRAPH_LAUNCHES = 32
+
+
 def _event_time_us(case: BenchmarkCase, config: Config, warmup: int, iters: int) -> float:
     """Mean device time of one launch: `iters` launches captured into one CUDA graph, replayed and timed
     with CUDA events on the case's stream (eager launches from Python cannot keep a microsecond-scale
@@ -64,8 +69,9 @@ def _event_time_us(case: BenchmarkCase, config: Config, warmup: int, iters: int)
     if case.before_launch_fn is None and case.stream != torch.cuda.default_stream(case.stream.device):
         try:
             graph = torch.cuda.CUDAGraph()
+            glaunches = max(iters, MIN_GRAPH_LAUNCHES)
             with torch.cuda.graph(graph, stream=case.stream):
-                for _ in range(iters):
+                for _ in range(glaunches):
                     launch()
         except RuntimeError:
             graph = None
@@ -85,7 +91,7 @@ def _event_time_us(case: BenchmarkCase, config: Config, warmup: int, iters: int)
                 launch()
             stop.record(case.stream)
     stop.synchronize()
-    return start.elapsed_time(stop) * 1000.0 / (iters * (reps if graph is not None else 1))
+    return start.elapsed_time(stop) * 1000.0 / (glaunches * reps if graph is not None else iters)
 
 
 def mini_benchmark(cases: Sequence[BenchmarkCase], *, warmup: int = 5, iters: int = 20, quiet: bool = False,

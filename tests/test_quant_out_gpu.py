@@ -41,7 +41,11 @@ def _x(dev, m, k, seed):
 def _assert_codes_of(out: torch.Tensor, q: torch.Tensor, s: torch.Tensor) -> None:
     eq, es = launch_quantize_fp8(out)
     torch.cuda.synchronize()
-    assert torch.equal(q, eq), int((q != eq).sum())
+    bad = (q != eq).nonzero()[:8].tolist()
+    detail = [(t, n, int(q[t, n]), int(eq[t, n]), float(out[t, n]), int(s[t, n // 32]), int(es[t, n // 32]))
+              for t, n in bad]
+    assert torch.equal(q, eq), f"{int((q != eq).sum())} codes differ (token, feature, got, expected, value, " \
+                               f"scale got, scale expected): {detail}"
     assert torch.equal(s, es), int((s != es).sum())
 
 
@@ -156,3 +160,19 @@ def test_rejects_n_not_divisible_by_32(cuda_device):
     x = _x(cuda_device, 2, 512, seed=112)
     with pytest.raises(ValueError):
         iq3_s_fp8_linear(x, w, quantize_output=True)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_standalone_quantizer_flags_nan_and_inf_groups(cuda_device, dtype):
+    """The quantizer's rule for non-finite groups: a NaN or an infinity among a group's 32 values gives the
+    scale code 0xFF; the other groups of the row are unaffected."""
+    x = torch.randn((2, 128), device=cuda_device).to(dtype)
+    x[0, 3] = float("nan")
+    x[1, 70] = float("inf")
+    q, s = launch_quantize_fp8(x)
+    torch.cuda.synchronize()
+    ref_q, ref_s = O.quantize_mxfp8(torch.nan_to_num(x.float(), nan=0.0, posinf=0.0).cpu().numpy())
+    assert int(s[0, 0]) == 0xFF, s[0].tolist()
+    assert int(s[1, 2]) == 0xFF, s[1].tolist()
+    keep = [(0, 1), (0, 2), (0, 3), (1, 0), (1, 1), (1, 3)]
+    assert all(int(s[r, g]) == int(ref_s[r, g]) for r, g in keep)
