@@ -514,17 +514,12 @@ def model_block(torch, dev, warmup: int = 3) -> dict:
             for name in shapes:
                 fused_linear_into(xp[name], w[name], yp[name])
 
-    def decode_step(hints: bool = True):
-        # Each launch prefetches the first weight records of the launch after it (the next
-        # layer's QKV after down; the first layer's after the last) into L2 as it finishes.
-        for li, w in enumerate(layers):
-            nxt = layers[(li + 1) % len(layers)]
-            h = (lambda ws: (ws, decode_m)) if hints else (lambda ws: None)
-            fused_linear_into(xd["qkv"], w["qkv"], yd["qkv"], prefetch=h(w["o"]))
-            fused_linear_into(xd["o"], w["o"], yd["o"], prefetch=h([w["gate"], w["up"]]))
-            group_linear_into([xd["gate"], xd["up"]], [w["gate"], w["up"]], [yd["gate"], yd["up"]],
-                              prefetch=h(w["down"]))
-            fused_linear_into(xd["down"], w["down"], yd["down"], prefetch=h(nxt["qkv"]))
+    def decode_step():
+        for w in layers:
+            fused_linear_into(xd["qkv"], w["qkv"], yd["qkv"])
+            fused_linear_into(xd["o"], w["o"], yd["o"])
+            group_linear_into([xd["gate"], xd["up"]], [w["gate"], w["up"]], [yd["gate"], yd["up"]])
+            fused_linear_into(xd["down"], w["down"], yd["down"])
 
     def capture(fn):
         with torch.cuda.stream(stream):
@@ -537,7 +532,6 @@ def model_block(torch, dev, warmup: int = 3) -> dict:
         return g
 
     g_prefill, g_decode = capture(prefill), capture(decode_step)
-    g_decode_nohint = capture(lambda: decode_step(hints=False))
 
     def timed(g, reps):
         with torch.cuda.stream(stream):
@@ -556,8 +550,7 @@ def model_block(torch, dev, warmup: int = 3) -> dict:
     with ClockSampler(dev.index or 0) as clocks:
         prefill_ms = timed(g_prefill, 3)
         decode_ms = timed(g_decode, decode_steps)
-        decode_nohint_ms = timed(g_decode_nohint, decode_steps)
-    del g_prefill, g_decode, g_decode_nohint, layers
+    del g_prefill, g_decode, layers
     torch.cuda.empty_cache()
     w_bytes = layer_bytes() * LLAMA3_8B_LAYERS
     flops = 2.0 * prefill_m * sum(n * k for _, n, k in PROJECTIONS) * LLAMA3_8B_LAYERS
@@ -573,9 +566,7 @@ def model_block(torch, dev, warmup: int = 3) -> dict:
         "prefill": {"ms": prefill_ms, "tflops": flops / (prefill_ms * 1e-3) / 1e12},
         "decode": {"ms_per_step": decode_ms, "gbs": dec_bytes / (decode_ms * 1e-3) / 1e9,
                    "hbm_frac": dec_bytes / (decode_ms * 1e-3) / 1e9 / peak, "peak_gbs": peak,
-                   "peak_kind": peak_kind, "launches_per_step": 4 * LLAMA3_8B_LAYERS,
-                   "prefetch": "each launch prefetches the next launch's first weight records into L2",
-                   "no_prefetch_ms_per_step": decode_nohint_ms},
+                   "peak_kind": peak_kind, "launches_per_step": 4 * LLAMA3_8B_LAYERS},
         "clocks": clocks.summary(),
     }
 
@@ -922,13 +913,10 @@ def main() -> None:
         # the whole sweep (20 independent linears) as one grouped GEMV launch
         group_linear_into(g_x, g_w, g_o)
 
-    def per_linear_step(hints: bool = True):
-        # one launch per linear: the decode GEMV quantizes its bf16 activations itself; each
-        # launch prefetches the next linear's first weight records into L2 as it finishes
-        for i, (m, p, _, _) in enumerate(order):
-            nm, np_, _, _ = order[(i + 1) % len(order)]
-            fused_linear_into(xs_dev[(m, p)], layers[m][p], out_buf[(m, p)], config=configs[(m, p)],
-                              prefetch=(layers[nm][np_], nm) if hints else None)
+    def per_linear_step():
+        # one launch per linear: the decode GEMV quantizes its bf16 activations itself
+        for m, p, _, _ in order:
+            fused_linear_into(xs_dev[(m, p)], layers[m][p], out_buf[(m, p)], config=configs[(m, p)])
 
     def capture(fn, copies: int = 1):
         with torch.cuda.stream(stream):
@@ -944,7 +932,6 @@ def main() -> None:
 
     graph = capture(group_step)
     graph_sep = capture(per_linear_step)
-    graph_sep_nohint = capture(lambda: per_linear_step(hints=False))
 
     def barrier():
         if world > 1:
@@ -1004,12 +991,6 @@ def main() -> None:
     torch.cuda.synchronize(dev)
     barrier()
     sep_ms = max_over_ranks(time_replays(graph_sep, args.steps))
-    with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
-            graph_sep_nohint.replay()
-    torch.cuda.synchronize(dev)
-    barrier()
-    sep_nohint_ms = max_over_ranks(time_replays(graph_sep_nohint, args.steps))
 
     # ---- roofline: the grouped launch, and every linear launched alone ------
     # Kernels are timed as back-to-back launches inside one graph, the way
@@ -1135,7 +1116,7 @@ def main() -> None:
     torch.cuda.synchronize(dev)
     ok = all(torch.equal(host_out[(m, p)], out_buf[(m, p)].cpu()) for m, p, _, _ in order)
 
-    del graph, graph_sep, graph_sep_nohint, g_e2e, g_pipe, layers
+    del graph, graph_sep, g_e2e, g_pipe, layers
     torch.cuda.synchronize(dev)
     torch.cuda.empty_cache()
     # BASELINE config 5 on every rank (tensor parallel over the launched GPUs).
@@ -1178,11 +1159,6 @@ def main() -> None:
                      "timing": "10 back-to-back launches in one CUDA graph, 5 replays, mean"},
         # Every linear launched on its own (the reference's one-linear-per-call shape).
         "per_linear": {"value": alg * world / (sep_ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": sep_ms,
-                       "hbm_frac": alg / (sep_ms * 1e-3) / 1e9 / peak,
-                       "prefetch": "each launch prefetches the next linear's first weight records into L2 "
-                                   "(mambo_prefetch_next)",
-                       "no_prefetch": {"ms_per_step": sep_nohint_ms,
-                                       "value": alg * world / (sep_nohint_ms * 1e-3) / 1e9},
                        "gpu_launches_per_step": len(order), "kernel_achieved": sep_achieved,
                        "kernel_frac": sep_achieved / peak,
                        "timing": "per linear: 10 back-to-back launches in one CUDA graph, 10 replays, mean",

@@ -261,22 +261,6 @@ MAMBO_API int mambo_iq3s_linear_group_q(const MamboLinearItem* items, const Mamb
                                         const uint32_t* fp8_table, void* workspace, size_t workspace_bytes,
                                         mambo_stream_t stream);
 
-/*
- * Names the weights of the linear launch that will follow the next linear call
- * made from this thread: `count` weights (1, or up to 4 for a grouped launch,
- * in item order) and that launch's token count m. The next mambo_iq3s_linear*
- * call then has its tcgen05 GEMV prefetch, as it finishes, the first
- * tile-major records each CTA of that following launch will load, into L2, so
- * a chain of dependent linears (QKV -> O -> gate/up -> down in a decode step)
- * starts each launch from L2 instead of waiting on HBM latency. A hint only:
- * results never depend on it. It applies to exactly one call (any
- * mambo_iq3s_linear* entry point clears it on return, whether or not it used
- * it); count 0 clears it. Weights without a packed copy are ignored. No
- * counterpart in the reference (it launches one linear per call,
- * src/python/mambo/kernels/iq3_s_fp8.py:364-399).
- */
-MAMBO_API int mambo_prefetch_next(const MamboIQ3SWeight* const* weights, int count, int64_t m);
-
 /* Workspace bytes mambo_iq3s_linear needs for this shape and configuration. */
 MAMBO_API size_t mambo_iq3s_linear_workspace_bytes(int64_t m, int64_t n_rows, int64_t n_blocks, const MamboLinearConfig* cfg);
 

@@ -54,7 +54,6 @@ EXPORTED_SYMBOLS = (
     "mambo_iq3s_linear_q",
     "mambo_iq3s_linear_fused_q",
     "mambo_iq3s_linear_group_q",
-    "mambo_prefetch_next",
     "mambo_num_configs",
     "mambo_config_at",
     "mambo_default_config",
@@ -203,7 +202,6 @@ def load() -> ctypes.CDLL:
             "mambo_iq3s_linear_group_q": (
                 [ctypes.POINTER(MamboLinearItem), ctypes.POINTER(MamboQuantOut), i32, vp, vp, ctypes.c_size_t, vp],
                 i32),
-            "mambo_prefetch_next": ([ctypes.POINTER(ctypes.POINTER(MamboIQ3SWeight)), i32, i64], i32),
             "mambo_num_configs": ([i32], i32),
             "mambo_config_at": ([i32, i32, ctypes.POINTER(MamboLinearConfig)], i32),
             "mambo_default_config": ([i64, i64, i64, ctypes.POINTER(MamboLinearConfig)], i32),

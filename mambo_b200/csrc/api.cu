@@ -484,38 +484,6 @@ int launch_gemm_f16_path(const GemmF16Source& src, int64_t m, const MamboIQ3SWei
   return ok();
 }
 
-// The next launch's weights, named by mambo_prefetch_next on this thread and
-// applied to the next tcgen05 GEMV launch made from it (then cleared).
-struct PrefetchHint {
-  int count = 0;
-  const uint8_t* packed[kGemvMaxPrefetch] = {nullptr};
-  int units[kGemvMaxPrefetch] = {0};
-  int grid = 0;
-};
-thread_local PrefetchHint g_prefetch_hint;
-constexpr int kPrefetchRecords = 4;  // records per CTA of the next launch
-
-// A hint applies to the one linear call made right after it: every public
-// linear entry point clears it on return, used or not, so it never outlives
-// the weights it names.
-struct HintScope {
-  ~HintScope() { g_prefetch_hint = PrefetchHint{}; }
-};
-
-void apply_prefetch_hint(GemvTmParams* p) {
-  PrefetchHint& h = g_prefetch_hint;
-  if (h.count > 0) {
-    for (int i = 0; i < h.count; ++i) {
-      p->pf_packed[i] = h.packed[i];
-      p->pf_units[i] = h.units[i];
-    }
-    p->pf_count = h.count;
-    p->pf_grid = h.grid;
-    p->pf_records = kPrefetchRecords;
-  }
-  h = PrefetchHint{};
-}
-
 // Launches the tcgen05 GEMV for tokens [0, mc) of xq/xs (already offset to the chunk).
 int launch_tc_chunk(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t ldxs, int64_t mc,
                     const MamboIQ3SWeight* w, const uint32_t* fp8_table, void* out, int out_dtype, int64_t ldo,
@@ -577,7 +545,6 @@ int launch_tc_chunk(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t 
   p.total_units = P.units;
   p.x_bf16 = x_bf16;
   p.ldx = ldx;
-  apply_prefetch_hint(&p);
   if (qo && qo->q) {  // quantized output for the next linear, written by the epilogue
     p.q_out = qo->q;
     p.ldq = qo->ldq;
@@ -820,7 +787,6 @@ size_t mambo_iq3s_linear_workspace_bytes(int64_t m, int64_t n_rows, int64_t n_bl
 int mambo_iq3s_linear(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t ldxs, int64_t m,
                       const MamboIQ3SWeight* w, const uint32_t* fp8_table, void* out, int out_dtype, int64_t ldo,
                       const MamboLinearConfig* cfg, void* workspace, size_t workspace_bytes, mambo_stream_t stream) {
-  HintScope hint_scope;
   return linear_impl(xq, ldxq, xs, ldxs, m, w, fp8_table, out, out_dtype, ldo, nullptr, cfg, workspace,
                      workspace_bytes, (cudaStream_t)stream);
 }
@@ -829,7 +795,6 @@ int mambo_iq3s_linear_q(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int6
                         const MamboIQ3SWeight* w, const uint32_t* fp8_table, void* out, int out_dtype, int64_t ldo,
                         const MamboQuantOut* qout, const MamboLinearConfig* cfg, void* workspace,
                         size_t workspace_bytes, mambo_stream_t stream) {
-  HintScope hint_scope;
   return linear_impl(xq, ldxq, xs, ldxs, m, w, fp8_table, out, out_dtype, ldo, qout, cfg, workspace, workspace_bytes,
                      (cudaStream_t)stream);
 }
@@ -978,7 +943,6 @@ int mambo_iq3s_linear_fused(const void* x, int x_dtype, int64_t ldx, int64_t m, 
                             const uint32_t* fp8_table, void* out, int out_dtype, int64_t ldo,
                             const MamboLinearConfig* cfg, void* workspace, size_t workspace_bytes,
                             mambo_stream_t stream) {
-  HintScope hint_scope;
   return fused_impl(x, x_dtype, ldx, m, w, fp8_table, out, out_dtype, ldo, nullptr, cfg, workspace, workspace_bytes,
                     (cudaStream_t)stream);
 }
@@ -987,7 +951,6 @@ int mambo_iq3s_linear_fused_q(const void* x, int x_dtype, int64_t ldx, int64_t m
                               const uint32_t* fp8_table, void* out, int out_dtype, int64_t ldo,
                               const MamboQuantOut* qout, const MamboLinearConfig* cfg, void* workspace,
                               size_t workspace_bytes, mambo_stream_t stream) {
-  HintScope hint_scope;
   return fused_impl(x, x_dtype, ldx, m, w, fp8_table, out, out_dtype, ldo, qout, cfg, workspace, workspace_bytes,
                     (cudaStream_t)stream);
 }
@@ -1175,7 +1138,6 @@ int mambo_iq3s_linear_group(const MamboLinearItem* items, int count, const uint3
 int mambo_iq3s_linear_group_q(const MamboLinearItem* items, const MamboQuantOut* qouts, int count,
                               const uint32_t* fp8_table, void* workspace, size_t workspace_bytes,
                               mambo_stream_t stream) {
-  HintScope hint_scope;
   if (!items || !fp8_table) return fail(MAMBO_EINVAL, "null pointer");
   if (count < 1) return fail(MAMBO_EINVAL, "a group needs at least one linear");
   for (int i = 0; i < count; ++i) {
@@ -1259,44 +1221,11 @@ int mambo_iq3s_linear_group_q(const MamboLinearItem* items, const MamboQuantOut*
   p.kparts = 0;
   p.row_tiles = tiles;
   p.total_units = units;
-  apply_prefetch_hint(&p);
   int grid = units < info.sms ? units : info.sms;
   if (grid > kGemvMaxGrid) grid = kGemvMaxGrid;
   split_group_units(g, units, grid, g.cta_start);
   cudaError_t e = launch_gemv_tm_group(p, g, nt, kGroupDecWarps, grid, (cudaStream_t)stream);
   if (e != cudaSuccess) return cuda_fail(e, "iq3s_gemv_tm_kernel (group)");
-  return ok();
-}
-
-int mambo_prefetch_next(const MamboIQ3SWeight* const* weights, int count, int64_t m) {
-  g_prefetch_hint = PrefetchHint{};
-  if (count <= 0 || !weights) return ok();
-  if (count > kGemvMaxPrefetch) return fail(MAMBO_EINVAL, "at most %d weights per prefetch hint", kGemvMaxPrefetch);
-  if (m < 1) return fail(MAMBO_EINVAL, "the next launch's token count must be positive");
-  int st;
-  DeviceInfo info = device_info(&st);
-  if (st != MAMBO_OK) return st;
-  PrefetchHint h;
-  int64_t units = 0;
-  for (int i = 0; i < count; ++i) {
-    const MamboIQ3SWeight* w = weights[i];
-    if (!w || w->n_rows < 1 || w->n_blocks < 1) return fail(MAMBO_EINVAL, "prefetch hint %d: invalid weight", i);
-    if (!w->packed || (uintptr_t)w->packed % 16) return ok();  // nothing to prefetch from: no hint
-    h.packed[i] = (const uint8_t*)w->packed;
-    h.units[i] = (int)(((w->n_rows + 127) / 128) * w->n_blocks);
-    units += h.units[i];
-  }
-  h.count = count;
-  if (count == 1 && m < kGemmMinTokens) {
-    // One linear: the grid its tuned default runs on (cluster K split or stream-K).
-    MamboLinearConfig c;
-    default_config(m, weights[0]->n_rows, weights[0]->n_blocks, &c, info.max_smem_optin, info.sms);
-    h.grid = plan_gemv(m, weights[0]->n_rows, weights[0]->n_blocks, c, info.sms, info.max_smem_optin).grid;
-  } else {
-    // A grouped launch: one CTA per SM, its units split about evenly.
-    h.grid = (int)(units < info.sms ? units : info.sms);
-  }
-  g_prefetch_hint = h;
   return ok();
 }
 
@@ -1363,7 +1292,6 @@ extern "C" int mambo_iq3s_linear_noalloc(const uint8_t* xq, int64_t ldxq, const 
                                          const MamboIQ3SWeight* w, const uint32_t* fp8_table, void* out,
                                          int out_dtype, int64_t ldo, const MamboLinearConfig* cfg,
                                          mambo_stream_t stream) {
-  HintScope hint_scope;
   if (!xq || !xs || !w || !fp8_table || !out) return fail(MAMBO_EINVAL, "null pointer");
   if (!w->d || !w->qs || !w->qh || !w->signs || !w->scales) return fail(MAMBO_EINVAL, "null weight field");
   if (w->n_rows < 1 || w->n_blocks < 1) return fail(MAMBO_EINVAL, "IQ3_S weight must have positive N and K");

@@ -440,21 +440,6 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
       issue_weights(it, s);
       for (; pf < min(n_units, it + 1 + p.prefetch); ++pf) prefetch(pf);
     }
-    // Every copy of this CTA is issued: bring the next launch's first records
-    // into L2 while this launch drains, so its pipeline starts from L2.
-    if (p.pf_count > 0 && lane == 0) {
-      int total = 0;
-      for (int i = 0; i < p.pf_count && i < kGemvMaxPrefetch; ++i) total += p.pf_units[i];
-      for (int c = blockIdx.x; c < p.pf_grid; c += gridDim.x) {
-        const int first = (int)(((int64_t)c * total) / p.pf_grid);
-        const int last = min(total, first + p.pf_records);
-        int item = 0, base = 0;  // the item holding unit u, and its first unit
-        for (int u = first; u < last; ++u) {
-          while (item + 1 < p.pf_count && u >= base + p.pf_units[item]) base += p.pf_units[item++];
-          bulk_prefetch_l2(p.pf_packed[item] + (size_t)(u - base) * kRecordBytes, kRecordBytes);
-        }
-      }
-    }
     return;
   }
 

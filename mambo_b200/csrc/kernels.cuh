@@ -157,18 +157,7 @@ struct GemvTmParams {
   int64_t ldq;
   uint8_t* s_out;
   int64_t lds;
-  // L2 prefetch for the NEXT launch (a hint; no effect on results): the
-  // tile-major records of up to kGemvMaxPrefetch linears whose units that
-  // launch numbers back to back (pf_units each) over pf_grid CTAs. As its own
-  // last copies are issued, each CTA c prefetches the first pf_records records
-  // of the next launch's CTAs c, c + grid, ...: about units * j / pf_grid for CTA j.
-  const uint8_t* pf_packed[4];
-  int pf_units[4];
-  int pf_count;
-  int pf_grid;
-  int pf_records;
 };
-constexpr int kGemvMaxPrefetch = 4;
 
 struct GemvTmMaps {
   CUtensorMap x;                         // activations [K/16 chunks][m tokens][16 bytes], box 16 x 8*NT x 16

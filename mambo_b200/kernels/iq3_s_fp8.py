@@ -261,21 +261,6 @@ def _quant_out_struct(qout) -> "_lib.MamboQuantOut | None":
     return qo
 
 
-def prefetch_next(weights, m: int) -> None:
-    """Hint for the next linear call on this thread: the launch after it runs on ``weights``
-    (one IQ3SFields, or a list of up to 4 for a grouped launch) with ``m`` tokens, so the next
-    call's GEMV prefetches their first records into L2 as it finishes (mambo_prefetch_next).
-    Results never depend on it; it applies to one call only."""
-    if weights is None:
-        _lib.check(_lib.load().mambo_prefetch_next(None, 0, 1), "prefetch_next")
-        return
-    if isinstance(weights, IQ3SFields):
-        weights = [weights]
-    structs = [weight_struct(w) for w in weights]
-    arr = (ctypes.POINTER(_lib.MamboIQ3SWeight) * len(structs))(*[ctypes.pointer(w) for w in structs])
-    _lib.check(_lib.load().mambo_prefetch_next(arr, len(structs), int(m)), "prefetch_next")
-
-
 def _new_quant_out(m: int, n: int, dev) -> tuple[torch.Tensor, torch.Tensor]:
     if n % IQ3_S_SCALE_VALUES:
         raise ValueError("quantize_output needs N divisible by 32")
@@ -347,7 +332,7 @@ def launch_iq3_s_fp8_matmul(x_values, x_scales, iq3_weight: IQ3SFields, *, strea
 
 
 def fused_linear_into(x: torch.Tensor, iq3_weight: IQ3SFields, out: torch.Tensor, config: dict | None = None,
-                      stream=None, qout=None, prefetch=None) -> torch.Tensor:
+                      stream=None, qout=None) -> torch.Tensor:
     """Quantize (round to nearest even) and multiply in one C-ABI call into a preallocated out [M,N].
 
     Below 32 tokens with bf16 rows the tcgen05 GEMV quantizes the activations
@@ -364,8 +349,6 @@ def fused_linear_into(x: torch.Tensor, iq3_weight: IQ3SFields, out: torch.Tensor
         st = _runtime.stream_handle(stream, dev)
         need = lib.mambo_iq3s_linear_fused_workspace_bytes(m, n_rows, blocks, cfg)
         ws = _runtime.workspace(dev, st, need)
-        if prefetch is not None:  # (weights of the launch after this one, its token count)
-            prefetch_next(*prefetch)
         x_dtype = _lib.MAMBO_BF16 if x.dtype == torch.bfloat16 else _lib.MAMBO_F32
         out_dtype = _lib.MAMBO_BF16 if out.dtype == torch.bfloat16 else _lib.MAMBO_F32
         _lib.check(
@@ -413,7 +396,7 @@ def iq3_s_fp8_linear(x, iq3_weight: IQ3SFields, *, stream=None, out_dtype: torch
     return fused_linear_into(x, iq3_weight, out, config=config, stream=stream)
 
 
-def group_linear_into(xs, iq3_weights, outs, stream=None, qouts=None, prefetch=None) -> list:
+def group_linear_into(xs, iq3_weights, outs, stream=None, qouts=None) -> list:
     """Independent linears ``outs[i] = linear(xs[i], iq3_weights[i])`` in one C-ABI call.
 
     Each is what ``iq3_s_fp8_linear`` computes. With bf16 activations in
@@ -422,8 +405,7 @@ def group_linear_into(xs, iq3_weights, outs, stream=None, qouts=None, prefetch=N
     the linears run one after another. No output may overlap another linear's
     input. No validation beyond the C ABI's. ``qouts``: per linear None or
     ``(q, s)`` buffers for the output's MXFP8 quantization (formed in the
-    grouped launch's epilogue). ``prefetch``: ``(weights, m)`` of the launch
-    that will follow this one (see ``prefetch_next``).
+    grouped launch's epilogue).
     """
     count = len(xs)
     items = (_lib.MamboLinearItem * count)()
@@ -445,8 +427,6 @@ def group_linear_into(xs, iq3_weights, outs, stream=None, qouts=None, prefetch=N
         st = _runtime.stream_handle(stream, dev)
         need = lib.mambo_iq3s_linear_group_workspace_bytes(items, count)
         ws = _runtime.workspace(dev, st, need)
-        if prefetch is not None:  # (weights of the launch after this one, its token count)
-            prefetch_next(*prefetch)
         qarr = None
         if qouts is not None:
             qarr = (_lib.MamboQuantOut * count)()

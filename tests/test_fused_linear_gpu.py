@@ -200,34 +200,3 @@ def test_fused_decode_is_one_launch(cuda_device, proj):
         if not kernels:
             pytest.skip("profiler recorded no kernel activity")
         assert len(kernels) == 1 and "gemv_tm" in kernels[0], (m, kernels)
-
-
-def test_prefetch_hints_do_not_change_results(cuda_device):
-    """A chain of linears where each launch prefetches the next one's first weight records
-    (mambo_prefetch_next) gives the same bits as without the hints; a hint followed by a
-    prefill-sized call (no GEMV launch) is dropped, not carried to a later call."""
-    from mambo_b200.kernels.iq3_s_fp8 import fused_linear_into, group_linear_into, prefetch_next
-
-    _, w1 = _weight(cuda_device, 4096, 4096, seed=81)
-    _, w2 = _weight(cuda_device, 1024, 4096, seed=82)
-    _, w3 = _weight(cuda_device, 2048, 4096, seed=83)
-    x = _activations(cuda_device, 4, 4096, seed=84)
-
-    def chain(hints):
-        o1 = torch.empty((4, 4096), dtype=torch.bfloat16, device=cuda_device)
-        o2 = torch.empty((4, 1024), dtype=torch.bfloat16, device=cuda_device)
-        o3 = torch.empty((4, 2048), dtype=torch.bfloat16, device=cuda_device)
-        fused_linear_into(x, w1, o1, prefetch=([w2, w3], 4) if hints else None)
-        group_linear_into([x, x], [w2, w3], [o2, o3], prefetch=(w1, 4) if hints else None)
-        return o1, o2, o3
-
-    for a, b in zip(chain(True), chain(False)):
-        assert torch.equal(a, b)
-    with pytest.raises(ValueError):
-        prefetch_next([w1] * 5, 4)
-    prefetch_next(w1, 4)
-    big = _activations(cuda_device, 64, 4096, seed=85)
-    fused_linear_into(big, w2, torch.empty((64, 1024), dtype=torch.bfloat16, device=cuda_device))
-    o = torch.empty((4, 4096), dtype=torch.bfloat16, device=cuda_device)
-    fused_linear_into(x, w1, o)
-    assert torch.equal(o, chain(False)[0])
