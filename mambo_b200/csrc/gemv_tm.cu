@@ -136,47 +136,63 @@ __device__ __forceinline__ int cta_of_unit_tm(int u, int grid, int units) {
   return (int)((((int64_t)u + 1) * grid - 1) / units);
 }
 
-// Where one linear's results go: out, and optionally its MXFP8 quantization
-// for the next linear (q: E4M3 bytes, s: UE8M0 codes; n_rows % 32 == 0).
+// Where one linear's results go.
 struct OutView {
   void* out;
   int64_t ldo;
   int out_bf16;
   int n_rows;
   int m;
+};
+
+// Where the MXFP8 quantization of a linear's output goes, for the next linear
+// (q: E4M3 bytes, s: UE8M0 codes; null q: none; n_rows % 32 == 0). Only
+// kernels instantiated with kQ carry it.
+struct QuantView {
   uint8_t* q;
   int64_t ldq;
   uint8_t* s;
   int64_t lds;
 };
 
+// The MXFP8 quantization of 32 consecutive outputs (rows row - lane .. row -
+// lane + 31, one per lane) of token `tok`: one MXFP8 group of the next
+// linear's activation row, quantized as the standalone quantizer quantizes
+// the stored values (largest magnitude by one warp reduction over the bit
+// patterns, where a NaN orders above every number and gives the scale code
+// 0xFF; values times 2^-e rounded to nearest even with saturation). Called by
+// all 32 lanes together. Out of line: only launches asked for the quantized
+// output reach it, and the store path of the others keeps its size.
+__device__ __noinline__ void quantize_out_tm(uint8_t* q, int64_t ldq, uint8_t* sc, int64_t lds, int n_rows,
+                                            int out_bf16, int row, int tok, float v) {
+  const bool in = row < n_rows;  // the same for the whole warp (n_rows % 32 == 0)
+  if (out_bf16) v = __bfloat162float(__float2bfloat16_rn(v));  // what a reader of out sees
+  const uint32_t mag = in ? (__float_as_uint(v) & 0x7FFFFFFFu) : 0u;
+  const uint32_t amax = __reduce_max_sync(0xFFFFFFFFu, mag);
+  const uint32_t code = mxfp8_scale_code(__uint_as_float(amax));
+  const float inv = e8m0_to_float(code == 0xFFu ? 0u : 254u - code);
+  if (in) {
+    q[(int64_t)tok * ldq + row] = (uint8_t)(cvt_e4m3x2_rn(v * inv, 0.f) & 0xFFu);
+    if ((row & 31) == 0) sc[(int64_t)tok * lds + row / 32] = (uint8_t)code;
+  }
+}
+
 // Stores the final value v of (row, tok). Called by all 32 lanes of a warp
 // together, for 32 consecutive rows (a warp's lanes are consecutive TMEM rows
-// of a 128-row tile) and one token: with q set, those 32 outputs are one
-// MXFP8 group of the next linear's activation row `tok`, quantized here as
-// the standalone quantizer quantizes the stored values (largest magnitude by
-// one warp reduction; a NaN or infinity gives the scale code 0xFF; values
-// times 2^-e rounded to nearest even with saturation).
-__device__ __forceinline__ void store_out_tm(const OutView& o, int row, int tok, float v) {
-  const bool in = row < o.n_rows;
-  if (tok < o.m) {
+// of a 128-row tile) and one token; with kQ and qv.q set, also the MXFP8
+// quantization of those 32 outputs for the next linear.
+template <bool kQ>
+__device__ __forceinline__ void store_out_tm(const OutView& o, const QuantView& qv, int row, int tok, float v) {
+  if (row < o.n_rows && tok < o.m) {
     if (o.out_bf16) {
-      const __nv_bfloat16 b = __float2bfloat16_rn(v);
-      if (in) reinterpret_cast<__nv_bfloat16*>(o.out)[(int64_t)tok * o.ldo + row] = b;
-      v = __bfloat162float(b);  // what a reader of out sees
-    } else if (in) {
+      reinterpret_cast<__nv_bfloat16*>(o.out)[(int64_t)tok * o.ldo + row] = __float2bfloat16_rn(v);
+    } else {
       reinterpret_cast<float*>(o.out)[(int64_t)tok * o.ldo + row] = v;
     }
-    if (o.q != nullptr) {  // warp-uniform
-      const uint32_t mag = in ? (__float_as_uint(v) & 0x7FFFFFFFu) : 0u;
-      const uint32_t amax = __reduce_max_sync(0xFFFFFFFFu, mag);  // NaN bits order above every number
-      const uint32_t code = mxfp8_scale_code(__uint_as_float(amax));
-      const float inv = e8m0_to_float(code == 0xFFu ? 0u : 254u - code);
-      if (in) {
-        o.q[(int64_t)tok * o.ldq + row] = (uint8_t)(cvt_e4m3x2_rn(v * inv, 0.f) & 0xFFu);
-        if ((row & 31) == 0) o.s[(int64_t)tok * o.lds + row / 32] = (uint8_t)code;
-      }
-    }
+  }
+  if constexpr (kQ) {
+    if (qv.q != nullptr && tok < o.m)  // warp-uniform condition
+      quantize_out_tm(qv.q, qv.ldq, qv.s, qv.lds, o.n_rows, o.out_bf16, row, tok, v);
   }
 }
 
@@ -192,8 +208,9 @@ __device__ __forceinline__ int group_item(const GemvGroup& g, int u, int l) {
 // contributors are in flight together.
 // tile: the row tile's number; tile_of(u): the row tile holding unit u;
 // begin_of(c): the first unit of CTA c.
-template <int TOK, class TileOf, class BeginOf>
-__device__ __forceinline__ void sum_partials(const float* partials, BeginOf begin_of, const OutView& o, int tile,
+template <int TOK, bool kQ, class TileOf, class BeginOf>
+__device__ __forceinline__ void sum_partials(const float* partials, BeginOf begin_of, const OutView& o,
+                                             const QuantView& qv, int tile,
                                              int rl, int row, int self, int c_first, int c_last, TileOf tile_of,
                                              const float (&acc)[TOK]) {
 #pragma unroll
@@ -234,7 +251,7 @@ __device__ __forceinline__ void sum_partials(const float* partials, BeginOf begi
       }
     }
 #pragma unroll
-    for (int t = 0; t < 8; ++t) store_out_tm(o, row, t0 + t, sum[t]);
+    for (int t = 0; t < 8; ++t) store_out_tm<kQ>(o, qv, row, t0 + t, sum[t]);
   }
 }
 
@@ -243,7 +260,9 @@ __device__ __forceinline__ void sum_partials(const float* partials, BeginOf begi
 // G: GemvNoGroup (one linear, described by p and maps) or GemvGroup (a grouped
 // launch: units of every item back to back, stream-K; weights packed,
 // activations bf16 quantized here).
-template <int NT, int kDecWarps, class G>
+// kQ: the launch also writes its output's MXFP8 quantization (QuantView);
+// launches without it run a kernel that has none of that code.
+template <int NT, int kDecWarps, class G, bool kQ>
 __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
     iq3s_gemv_tm_kernel(const __grid_constant__ GemvTmParams p, const __grid_constant__ GemvTmMaps maps,
                         const __grid_constant__ G grp) {
@@ -787,12 +806,15 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
     // The linear of unit `it`: its output, K blocks, first unit and first row
     // tile in the launch's numbering, row tiles (a grouped launch moves to the
     // next item when they are done; a single linear has one).
-    OutView ov{p.out, p.ldo, p.out_bf16, p.n_rows, p.m, p.q_out, p.ldq, p.s_out, p.lds};
+    OutView ov{p.out, p.ldo, p.out_bf16, p.n_rows, p.m};
+    QuantView qv{};
+    if constexpr (kQ) qv = QuantView{p.q_out, p.ldq, p.s_out, p.lds};
     int cur_nb = p.n_blocks, cur_unit0 = 0, cur_tile0 = 0, cur_tiles = 0, item = 0;
     auto load_item = [&](int l) {
       if constexpr (kGroup) {
         const GemvItem& gi = grp.items[l];
-        ov = OutView{gi.out, gi.ldo, gi.out_bf16, gi.n_rows, gi.m, gi.q_out, gi.ldq, gi.s_out, gi.lds};
+        ov = OutView{gi.out, gi.ldo, gi.out_bf16, gi.n_rows, gi.m};
+        if constexpr (kQ) qv = QuantView{gi.q_out, gi.ldq, gi.s_out, gi.lds};
         cur_nb = gi.n_blocks;
         cur_unit0 = gi.unit0;
         cur_tile0 = gi.tile0;
@@ -877,6 +899,7 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
 
       const int kb = kb_next, rt = rt_next;
       const OutView ou = ov;  // this unit's linear (the cursor may move to the next item below)
+      const QuantView qu = qv;
       const int nbu = cur_nb, unit0u = cur_unit0, tile = cur_tile0 + rt;
       if (++kb_next == cur_nb) {
         kb_next = 0;
@@ -910,12 +933,12 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
               for (int t = 0; t < TOK; ++t) acc[t] += src[t];
             }
 #pragma unroll
-            for (int t = 0; t < TOK; ++t) store_out_tm(ou, row, t, acc[t]);
+            for (int t = 0; t < TOK; ++t) store_out_tm<kQ>(ou, qu, row, t, acc[t]);
           }
         }
       } else if (full_tile) {
 #pragma unroll
-        for (int t = 0; t < TOK; ++t) store_out_tm(ou, row, t, acc[t]);
+        for (int t = 0; t < TOK; ++t) store_out_tm<kQ>(ou, qu, row, t, acc[t]);
       } else {
         // Stream-K: a row tile shared with other CTAs. The segment a CTA
         // finishes last is usually the last contribution: if every other
@@ -943,7 +966,7 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
         }
         if (last) {
           if (lane == 0) *counter = 0;  // every contributor has arrived: leave it zeroed for the next launch
-          sum_partials<TOK>(p.partials, unit_begin, ou, tile, rl, row, cta, c_first, c_last, tile_of, acc);
+          sum_partials<TOK, kQ>(p.partials, unit_begin, ou, qu, tile, rl, row, cta, c_first, c_last, tile_of, acc);
         }
       }
 #pragma unroll
@@ -964,13 +987,13 @@ uint32_t gemv_tm_smem_bytes(int nt, int stages, int kparts, bool fused) {
 }
 int gemv_tm_max_stages() { return kMaxStagesTm; }
 
-template <int NT, int kDecWarps>
+template <int NT, int kDecWarps, bool kQ = false>
 static const void* tm_kernel() {
-  return (const void*)iq3s_gemv_tm_kernel<NT, kDecWarps, GemvNoGroup>;
+  return (const void*)iq3s_gemv_tm_kernel<NT, kDecWarps, GemvNoGroup, kQ>;
 }
-template <int NT, int kDecWarps>
+template <int NT, int kDecWarps, bool kQ = false>
 static const void* tm_kernel_group() {
-  return (const void*)iq3s_gemv_tm_kernel<NT, kDecWarps, GemvGroup>;
+  return (const void*)iq3s_gemv_tm_kernel<NT, kDecWarps, GemvGroup, kQ>;
 }
 
 static int query_max_clusters(int nt, int dec_warps, int stages, int kparts);
@@ -1024,7 +1047,7 @@ static int query_max_clusters(int nt, int dec_warps, int stages, int kparts) {
 template <int NT, int kDecWarps>
 static cudaError_t launch_gemv_tm_t(const GemvTmParams& p, const GemvTmMaps& maps, int grid, cudaStream_t stream) {
   const uint32_t smem = tm_smem_bytes(NT, p.stages, p.kparts, p.x_bf16 != nullptr);
-  const void* kern = tm_kernel<NT, kDecWarps>();
+  const void* kern = p.q_out != nullptr ? tm_kernel<NT, kDecWarps, true>() : tm_kernel<NT, kDecWarps, false>();
   cudaError_t e = ensure_smem_attribute(kern, smem);
   if (e != cudaSuccess) return e;
   const GemvNoGroup none{0};
@@ -1036,7 +1059,9 @@ static cudaError_t launch_gemv_tm_t(const GemvTmParams& p, const GemvTmMaps& map
 template <int NT>
 static cudaError_t launch_gemv_tm_group_t(const GemvTmParams& p, const GemvGroup& g, int grid, cudaStream_t stream) {
   const uint32_t smem = tm_smem_bytes(NT, p.stages, 0, true);
-  const void* kern = tm_kernel_group<NT, 8>();
+  bool quant = false;  // some item also writes its output's MXFP8 quantization
+  for (int i = 0; i < g.count; ++i) quant = quant || g.items[i].q_out != nullptr;
+  const void* kern = quant ? tm_kernel_group<NT, 8, true>() : tm_kernel_group<NT, 8, false>();
   cudaError_t e = ensure_smem_attribute(kern, smem);
   if (e != cudaSuccess) return e;
   GemvTmMaps maps;
