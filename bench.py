@@ -352,6 +352,7 @@ def prefill_block(torch, dev, ms=PREFILL_MS) -> dict:
     activation quantization, then the tcgen05 GEMM), and the GEMM alone on
     activations quantized beforehand.
     """
+    from mambo_b200 import _lib
     from mambo_b200.kernels.iq3_s_fp8 import fused_linear_into, linear_into, select_config
     from mambo_b200.kernels.quantize_fp8 import launch_quantize_fp8
     from mambo_b200.utils.iq3_s_weight import prepare_iq3_s_fields
@@ -383,7 +384,7 @@ def prefill_block(torch, dev, ms=PREFILL_MS) -> dict:
         del raw, d
     per_m = []
     for m in ms:
-        rows, flop_tot, us_tot, gemm_us_tot = [], 0, 0.0, 0.0
+        rows, flop_tot, us_tot, gemm_us_tot, fold_us_tot = [], 0, 0.0, 0.0, 0.0
         for i, (name, n, k) in enumerate(PREFILL_SHAPES):
             gen = torch.Generator(device=dev).manual_seed(0x51A + 100 * i + m)
             x = torch.randn((m, k), device=dev, generator=gen)
@@ -396,21 +397,28 @@ def prefill_block(torch, dev, ms=PREFILL_MS) -> dict:
             xq, xs = launch_quantize_fp8(xb)
             cfg = select_config(m, n, k, dev)
             gemm_us = timed(lambda: linear_into(xq, xs, fields, out, config=cfg))
+            # The folded variant (d folded, rounded, into the FP16 weights; 1e-3 bound), default stages/split.
+            fold_cfg = dict(cfg, kernel=_lib.MAMBO_KERNEL_GEMM_F16_FOLD) if cfg.get("kernel") != \
+                _lib.MAMBO_KERNEL_GEMM_F16_PAIR else {"kernel": _lib.MAMBO_KERNEL_GEMM_F16_FOLD, "stages": 4}
+            fold_us = timed(lambda: fused_linear_into(xb, fields, out, config=fold_cfg))
             flop = 2 * m * n * k
             rows.append({"proj": name, "n": n, "k": k, "us": round(us, 1), "tflops": round(flop / us / 1e6, 1),
-                         "gemm_us": round(gemm_us, 1), "gemm_tflops": round(flop / gemm_us / 1e6, 1)})
+                         "gemm_us": round(gemm_us, 1), "gemm_tflops": round(flop / gemm_us / 1e6, 1),
+                         "folded_us": round(fold_us, 1), "folded_tflops": round(flop / fold_us / 1e6, 1)})
             flop_tot += flop
             us_tot += us
             gemm_us_tot += gemm_us
+            fold_us_tot += fold_us
             del xb, xq, xs, out
         per_m.append({"m": m, "tflops": flop_tot / us_tot / 1e6, "gemm_tflops": flop_tot / gemm_us_tot / 1e6,
-                      "per_shape": rows})
+                      "folded_tflops": flop_tot / fold_us_tot / 1e6, "per_shape": rows})
     del weights, flush
     torch.cuda.empty_cache()
     peak, kind = measure_fp8_peak(torch, dev)
     for r in per_m:
         r["frac"] = r["tflops"] / peak if peak else None
         r["gemm_frac"] = r["gemm_tflops"] / peak if peak else None
+        r["folded_frac"] = r["folded_tflops"] / peak if peak else None
     head = next(r for r in per_m if r["m"] == 2048) if 2048 in ms else per_m[0]
     return {"m": head["m"], "tflops": head["tflops"], "unit": "TFLOP/s", "peak_tflops": peak, "peak_kind": kind,
             "frac": head["frac"], "per_m": per_m,

@@ -93,14 +93,20 @@ typedef struct MamboLinearConfig {
  * per 256-wide K block; activations enter as FP16 relative to each token's
  * largest scale (exact unless a group's scale is more than 2^12 below it).
  * MAMBO_KERNEL_GEMM_F16_PAIR: the same arithmetic on clusters of two CTAs
- * whose tensor cores share each activation tile (256 weight rows per tile). */
+ * whose tensor cores share each activation tile (256 weight rows per tile).
+ * MAMBO_KERNEL_GEMM_F16_FOLD: the FP16 GEMM with the block scale d folded too,
+ * rounded, into the weight operand (fp16(d * 2^-e * (1+2*nibble)) * grid, e a
+ * per-row exponent stored with the packed copy): one accumulator covers the
+ * whole K range, so no per-block epilogue; about 2^-12 relative rounding per
+ * weight, within the 1e-3 relative Frobenius bound of the linear. */
 enum {
   MAMBO_KERNEL_AUTO = 0,
   MAMBO_KERNEL_GEMV = 1,
   MAMBO_KERNEL_GEMM = 2,
   MAMBO_KERNEL_GEMV_SYNC = 3,
   MAMBO_KERNEL_GEMM_F16 = 4,
-  MAMBO_KERNEL_GEMM_F16_PAIR = 5
+  MAMBO_KERNEL_GEMM_F16_PAIR = 5,
+  MAMBO_KERNEL_GEMM_F16_FOLD = 6
 };
 
 /* Library version string. */
@@ -131,7 +137,10 @@ MAMBO_API int mambo_iq3s_prepare(const uint8_t* raw, int64_t n_rows, int64_t n_b
  * adjacent: qs [4][128][16 B] (16-byte chunk, row), signs [2][128][16 B],
  * qh [2][128][4 B], d [128] fp16, scales [128][4 B]; rows at or past N are zero. A run of work
  * units (consecutive K blocks of one tile, then the next tile) is one
- * contiguous range. mambo_iq3s_packed_bytes gives the size of the buffer and
+ * contiguous range. After the records, at byte tiles * B * RECORD_BYTES, one
+ * int8 per row of whole tiles: floor(log2(max_b |d_b|)) over the row's finite
+ * block scales (0 without one), used by MAMBO_KERNEL_GEMM_F16_FOLD.
+ * mambo_iq3s_packed_bytes gives the size of the buffer and
  * mambo_iq3s_pack fills it from prepared SoA fields (N % 8 == 0; 16-byte
  * aligned fields and buffer). The SoA fields stay valid and unchanged.
  */

@@ -161,7 +161,11 @@ constexpr int kSmemOptinDefault = 232448;
 
 int kernel_of(const MamboLinearConfig& c) { return c.kernel == MAMBO_KERNEL_AUTO ? MAMBO_KERNEL_GEMV : c.kernel; }
 // The FP16-operand GEMM, on single CTAs or on CTA pairs.
-bool is_gemm_f16(int kind) { return kind == MAMBO_KERNEL_GEMM_F16 || kind == MAMBO_KERNEL_GEMM_F16_PAIR; }
+bool is_gemm_f16(int kind) {
+  return kind == MAMBO_KERNEL_GEMM_F16 || kind == MAMBO_KERNEL_GEMM_F16_PAIR || kind == MAMBO_KERNEL_GEMM_F16_FOLD;
+}
+// FP16 GEMM kinds that run on single CTAs and take a K split.
+bool is_gemm_f16_single(int kind) { return kind == MAMBO_KERNEL_GEMM_F16 || kind == MAMBO_KERNEL_GEMM_F16_FOLD; }
 bool is_gemm(int kind) { return kind == MAMBO_KERNEL_GEMM || is_gemm_f16(kind); }
 
 // Shared memory of a configuration (for MAMBO_KERNEL_GEMV without the cluster
@@ -238,7 +242,7 @@ int validate_config(const MamboLinearConfig* cfg, int64_t m, int64_t b, const De
   if (is_gemm(kind)) {
     const int smax = kind == MAMBO_KERNEL_GEMM ? gemm_tm_max_wstages() : gemm_f16_max_wstages();
     if (cfg->stages < 2 || cfg->stages > smax) return fail(MAMBO_EINVAL, "stages must be in [2, %d]", smax);
-    const int smax_split = kind == MAMBO_KERNEL_GEMM_F16 ? kGemmMaxSplit : 1;
+    const int smax_split = is_gemm_f16_single(kind) ? kGemmMaxSplit : 1;
     if (cfg->split < 0 || cfg->split > smax_split)
       return fail(MAMBO_EINVAL, "split (K parts) must be in [0, %d] for this kernel", smax_split);
   } else if (kind == MAMBO_KERNEL_GEMV_SYNC) {
@@ -419,6 +423,7 @@ int launch_gemm_f16_path(const GemmF16Source& src, int64_t m, const MamboIQ3SWei
                          void* out, int out_dtype, int64_t ldo, const MamboLinearConfig& c, const DeviceInfo& info,
                          void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   const bool pair = c.kernel == MAMBO_KERNEL_GEMM_F16_PAIR;
+  const bool fold = c.kernel == MAMBO_KERNEL_GEMM_F16_FOLD;
   const int ks = pair ? 1 : gemm_f16_clamp_split(c.split, m, w->n_rows, w->n_blocks);
   const size_t need = gemm_f16_workspace_bytes(m, w->n_rows, w->n_blocks, ks);
   if (!workspace || workspace_bytes < need)
@@ -452,6 +457,8 @@ int launch_gemm_f16_path(const GemmF16Source& src, int64_t m, const MamboIQ3SWei
   p.row_tiles = (int)((w->n_rows + 127) / 128);
   p.tok_tiles = (int)((m + 127) / 128);
   p.ksplit = ks;
+  if (fold)  // the row exponents after the packed records
+    p.row_exp = (const int8_t*)w->packed + (size_t)p.row_tiles * (size_t)w->n_blocks * MAMBO_IQ3S_RECORD_BYTES;
   if (ks > 1) {
     // Partials after the token scales; counters in the counter region's second half.
     p.partials = (float*)((uint8_t*)tok_scale + align256((size_t)((m + 127) / 128 * 128) * 4));
@@ -479,8 +486,8 @@ int launch_gemm_f16_path(const GemmF16Source& src, int64_t m, const MamboIQ3SWei
   }
   const int64_t tiles = (int64_t)p.row_tiles * p.tok_tiles * ks;
   const int grid = (int)(tiles < info.sms ? tiles : info.sms);
-  e = launch_gemm_f16(p, maps, grid, stream);
-  if (e != cudaSuccess) return cuda_fail(e, "iq3s_gemm_f16");
+  e = launch_gemm_f16(p, maps, grid, stream, fold);
+  if (e != cudaSuccess) return cuda_fail(e, fold ? "iq3s_gemm_f16 (folded)" : "iq3s_gemm_f16");
   return ok();
 }
 
@@ -651,8 +658,9 @@ int mambo_iq3s_prepare(const uint8_t* raw, int64_t n_rows, int64_t n_blocks, int
 
 size_t mambo_iq3s_packed_bytes(int64_t n_rows, int64_t n_blocks) {
   if (n_rows < 1 || n_blocks < 1) return 0;
-  return (size_t)((n_rows + MAMBO_IQ3S_TILE_ROWS - 1) / MAMBO_IQ3S_TILE_ROWS) * (size_t)n_blocks *
-         MAMBO_IQ3S_RECORD_BYTES;
+  const size_t tiles = (size_t)((n_rows + MAMBO_IQ3S_TILE_ROWS - 1) / MAMBO_IQ3S_TILE_ROWS);
+  // The records, then one row exponent per row of whole tiles (16-byte padded).
+  return tiles * (size_t)n_blocks * MAMBO_IQ3S_RECORD_BYTES + (tiles * MAMBO_IQ3S_TILE_ROWS + 15) / 16 * 16;
 }
 
 int mambo_iq3s_pack(const MamboIQ3SWeight* w, void* packed, mambo_stream_t stream) {
@@ -671,6 +679,10 @@ int mambo_iq3s_pack(const MamboIQ3SWeight* w, void* packed, mambo_stream_t strea
                      (const uint8_t*)w->scales, w->n_rows, w->n_blocks, (uint8_t*)packed};
   cudaError_t e = launch_iq3s_pack(p, info.sms, (cudaStream_t)stream);
   if (e != cudaSuccess) return cuda_fail(e, "iq3s_pack");
+  const size_t records = (size_t)((w->n_rows + 127) / 128) * (size_t)w->n_blocks * MAMBO_IQ3S_RECORD_BYTES;
+  e = launch_iq3s_row_exp((const uint8_t*)w->d, w->n_rows, w->n_blocks, (int8_t*)packed + records,
+                          (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "iq3s_row_exp");
   return ok();
 }
 
@@ -718,7 +730,7 @@ int mambo_default_config(int64_t m, int64_t n_rows, int64_t n_blocks, MamboLinea
 
 int mambo_num_configs(int kernel) {
   if (kernel == MAMBO_KERNEL_GEMV || kernel == MAMBO_KERNEL_AUTO) return kNumTcConfigs;
-  if (kernel == MAMBO_KERNEL_GEMM_F16) return kNumGemmF16Configs;
+  if (is_gemm_f16_single(kernel)) return kNumGemmF16Configs;
   if (is_gemm(kernel)) return kNumGemmConfigs;
   if (kernel == MAMBO_KERNEL_GEMV_SYNC) return kNumSyncConfigs;
   return 0;
@@ -736,7 +748,7 @@ int mambo_config_at(int kernel, int index, MamboLinearConfig* cfg) {
   if (is_gemm(kernel)) {
     cfg->split = 0;
     cfg->warps = 8;
-    if (kernel == MAMBO_KERNEL_GEMM_F16) {
+    if (is_gemm_f16_single(kernel)) {
       cfg->stages = kGemmStages[index % kNumGemmConfigs];
       cfg->split = kGemmSplits[index / kNumGemmConfigs];
     } else {
@@ -777,7 +789,7 @@ size_t mambo_iq3s_linear_workspace_bytes(int64_t m, int64_t n_rows, int64_t n_bl
   const size_t gemm = kernel_of(c) == MAMBO_KERNEL_GEMM       ? gemm_workspace_bytes(m, n_blocks)
                      : is_gemm_f16(kernel_of(c))
                          ? gemm_f16_workspace_bytes(m, n_rows, n_blocks,
-                                                    c.kernel == MAMBO_KERNEL_GEMM_F16
+                                                    is_gemm_f16_single(c.kernel)
                                                         ? gemm_f16_clamp_split(c.split, m, n_rows, n_blocks)
                                                         : 1)
                                                              : 0;

@@ -102,9 +102,15 @@ __device__ __forceinline__ void store_out_h(const GemmF16Params& p, int row, int
 // tile serves 256 weight rows: half the L2 traffic per FLOP) and its commits
 // arrive in both CTAs; rank 1's decoders and epilogue arrive on rank 0's
 // barriers. Otherwise 128 x 128 tiles on single CTAs.
-template <bool kPair>
+// kFold (single CTAs only): the block scale d folded, rounded, into the FP16
+// weight operand with each row's exponent taken out (GemmF16Params::row_exp),
+// so one accumulator covers the tile's whole K range: the epilogue runs once
+// per tile instead of once per K block, and the MMAs never wait for it inside
+// a tile. Each weight carries one FP16 rounding (about 2^-12 relative).
+template <bool kPair, bool kFold = false>
 __global__ void __launch_bounds__(kThreadsH, 1)
     iq3s_gemm_f16_kernel(const __grid_constant__ GemmF16Params p, const __grid_constant__ GemmF16Maps maps) {
+  static_assert(!(kPair && kFold), "the folded GEMM runs on single CTAs");
   // B half-block (the CTA's tokens x 128 K): two [tokens][128 bytes] boxes in
   // the 128-byte-swizzled K-major layout (8-row atoms 1024 bytes apart); an
   // MMA's 16 K (32 bytes) start 32 bytes further into the row.
@@ -277,12 +283,19 @@ __global__ void __launch_bounds__(kThreadsH, 1)
     int it = 0, hj = 0;
     bool ok = rank == 0;
     for (int t = 0; ok && t < my_tiles; ++t) {
-      for (int kb = kb_begin(t), kbe = kb_end(t); ok && kb < kbe; ++kb, ++it) {
-        const int r = it % kARingH, db = it & 1;
+      // Folded: D buffer t % 2 holds tile t for its whole K range; it is free
+      // once the epilogue has read tile t - 2.
+      if constexpr (kFold) {
+        if (t >= kDRingH) ok = tm::warp_wait(kEfree + 8 * (t & 1), ((t >> 1) & 1) ^ 1, kSiteGemvEmpty);
+        if (!ok) break;
+      }
+      const int kb0 = kb_begin(t), kbe = kb_end(t);
+      for (int kb = kb0; ok && kb < kbe; ++kb, ++it) {
+        const int r = it % kARingH, db = kFold ? (t & 1) : (it & 1);
         ok = kPair ? tm::warp_wait_cluster(kAfull + 8 * r, (it / kARingH) & 1, kSiteGemvFull)
                    : tm::warp_wait(kAfull + 8 * r, (it / kARingH) & 1, kSiteGemvFull);
         // The D buffer is free once the epilogue(s) have read block it - 2.
-        if (ok && it >= kDRingH)
+        if (!kFold && ok && it >= kDRingH)
           ok = kPair ? tm::warp_wait_cluster(kEfree + 8 * db, ((it >> 1) & 1) ^ 1, kSiteGemvEmpty)
                      : tm::warp_wait(kEfree + 8 * db, ((it >> 1) & 1) ^ 1, kSiteGemvEmpty);
         if (!ok) break;
@@ -302,7 +315,9 @@ __global__ void __launch_bounds__(kThreadsH, 1)
               if constexpr (kPair) {
                 tc::mma_f16_ts_pair(dcol, acol + (uint32_t)((8 * h + j) * 8), bj, kIdesc, (h | j) != 0);
               } else {
-                tc::mma_f16_ts(dcol, acol + (uint32_t)((8 * h + j) * 8), bj, kIdesc, (h | j) != 0);
+                // Folded: accumulate over the tile's K blocks (a fresh sum at its first MMA).
+                tc::mma_f16_ts(dcol, acol + (uint32_t)((8 * h + j) * 8), bj, kIdesc,
+                               kFold ? (kb != kb0 || (h | j) != 0) : (h | j) != 0);
               }
             }
             if constexpr (kPair) {
@@ -320,7 +335,7 @@ __global__ void __launch_bounds__(kThreadsH, 1)
             tc::commit_pair(kMdone + 8 * db, kBoth);
           } else {
             tc::commit(kAempty + 8 * r);
-            tc::commit(kMdone + 8 * db);
+            if (!kFold || kb == kbe - 1) tc::commit(kMdone + 8 * db);  // folded: once the tile is summed
           }
         }
         __syncwarp();
@@ -354,6 +369,9 @@ __global__ void __launch_bounds__(kThreadsH, 1)
     uint32_t sph = 0;
     bool ok = true;
     for (int t = 0; ok && t < my_tiles; ++t) {
+      // Folded: 2^-e of this row (rows past N read the tail's zero entries).
+      float fold = 1.f;
+      if constexpr (kFold) fold = ldexpf(1.f, -(int)__ldg(p.row_exp + (size_t)row_tile(t) * kRowsH + rl));
       for (int kb = kb_begin(t), kbe = kb_end(t); kb < kbe; ++kb, ++it) {
         const int r = it % kARingH;
         ok = tm::warp_wait(kWfull + 8 * s, sph, kSiteGemvFull);
@@ -367,7 +385,10 @@ __global__ void __launch_bounds__(kThreadsH, 1)
         const uint32_t scw = *reinterpret_cast<const uint32_t*>(st + tm::kRecScales + rl * 4);
         const uint32_t qw[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
         const uint32_t sw[4] = {gs.x, gs.y, gs.z, gs.w};
-        if (part == 0) {
+        float dfold = 0.f;  // folded: this block's d * 2^-e (exact)
+        if constexpr (kFold) {
+          dfold = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(st + tm::kRecD + rl * 2))) * fold;
+        } else if (part == 0) {
           // The row's d for the epilogue.
           reinterpret_cast<uint32_t*>(aux0 + (size_t)(it % kAuxRingH) * kAuxH)[rl] =
               *reinterpret_cast<const uint16_t*>(st + tm::kRecD + rl * 2);
@@ -378,9 +399,11 @@ __global__ void __launch_bounds__(kThreadsH, 1)
         for (int g = 0; g < 4; ++g) {
           uint32_t e[8];
           tm::decode_group_packed(table, qw[2 * g], qw[2 * g + 1], hw, 2u * (uint32_t)g, sw[g], l4, e);
-          // (1 + 2*nibble) of group 4*part + g as an FP16 pair (an odd integer <= 31: exact).
+          // (1 + 2*nibble) of group 4*part + g as an FP16 pair (an odd integer <= 31: exact);
+          // folded, times d * 2^-e, rounded to FP16.
           const uint32_t mult = 1u + 2u * ((scw >> (4 * (4 * part + g))) & 0xFu);
-          const uint32_t mh = (uint32_t)__half_as_ushort(__uint2half_rn(mult));
+          const uint32_t mh = kFold ? (uint32_t)__half_as_ushort(__float2half_rn(dfold * (float)mult))
+                                    : (uint32_t)__half_as_ushort(__uint2half_rn(mult));
           const uint32_t m2 = mh | (mh << 16);
           uint32_t v[16];
 #pragma unroll
@@ -426,7 +449,32 @@ __global__ void __launch_bounds__(kThreadsH, 1)
     bool ok = true;
     for (int t = 0; ok && t < my_tiles; ++t) {
       const int rt = row_tile(t), tt = tok_tile(t);
-      for (int kb = kb_begin(t), kbe = kb_end(t); kb < kbe; ++kb, ++it) {
+      if constexpr (kFold) {
+        // The tile's sum over its whole K range, in D buffer t % 2, times 2^e of the row.
+        const int db = t & 1;
+        if (!tm::warp_wait(kMdone + 8 * db, (t >> 1) & 1, kSiteGemvFull)) {
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
+        const float rs = ldexpf(1.f, (int)__ldg(p.row_exp + (size_t)rt * kRowsH + rl));
+        const uint32_t tq = tq0 + (uint32_t)(db * kTokH);
+#pragma unroll
+        for (int c0 = 0; c0 < 64; c0 += 16) {
+          const uint32_t off[2] = {(uint32_t)c0, (uint32_t)c0 + 8u};
+          float cv[2][8];
+          tc::ld_x8_multi<2>(tq, off, cv);
+#pragma unroll
+          for (int j = 0; j < 2; ++j)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[c0 + 8 * j + i] = cv[j][i] * rs;
+        }
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(kEfree + 8 * db);
+        __syncwarp();
+      }
+      for (int kb = kb_begin(t), kbe = kb_end(t); !kFold && kb < kbe; ++kb, ++it) {
         const int db = it & 1;
         if (!tm::warp_wait(kDfull + 8 * (it % kAuxRingH), (it / kAuxRingH) & 1, kSiteGemvFull) ||
             !tm::warp_wait(kMdone + 8 * db, (it >> 1) & 1, kSiteGemvFull)) {
@@ -762,9 +810,10 @@ cudaError_t launch_x16_quant(const void* x, int x_dtype, int64_t ldx, int m, int
   return launch_pdl(kern, dim3((unsigned)m), dim3(256), smem, stream, (const float*)x, ldx, k, x16, ld, tok_scale);
 }
 
-cudaError_t launch_gemm_f16(const GemmF16Params& p, const GemmF16Maps& maps, int grid, cudaStream_t stream) {
+cudaError_t launch_gemm_f16(const GemmF16Params& p, const GemmF16Maps& maps, int grid, cudaStream_t stream,
+                            bool fold) {
   const uint32_t smem = gemm_f16_smem(p.wstages, p.out_tma != 0);
-  const void* kern = (const void*)iq3s_gemm_f16_kernel<false>;
+  const void* kern = fold ? (const void*)iq3s_gemm_f16_kernel<false, true> : (const void*)iq3s_gemm_f16_kernel<false>;
   cudaError_t e = ensure_smem_attribute(kern, smem);
   if (e != cudaSuccess) return e;
   return launch_pdl(kern, dim3(grid), dim3(kThreadsH), smem, stream, p, maps);

@@ -267,12 +267,21 @@ struct GemmF16Params {
   int ksplit;                  // 1 = no split
   float* partials;             // [out tiles][ksplit][128 x 128] FP32
   int* split_counters;         // [out tiles][8], zero on entry and left zero
+  // Folded kernel (MAMBO_KERNEL_GEMM_F16_FOLD): per-row exponents e (rows of
+  // whole tiles); the weight operand is fp16(d * 2^-e * (1+2*nibble)) * grid,
+  // one accumulator covers the whole K range, out = D * 2^e * tok_scale.
+  const int8_t* row_exp;
 };
+// Per-row exponents for the folded FP16 GEMM (the tail of the packed buffer):
+// row_exp[r] = floor(log2(max_b |d_b|)) over row r's finite block scales.
+cudaError_t launch_iq3s_row_exp(const uint8_t* d, int64_t n_rows, int64_t n_blocks, int8_t* row_exp,
+                                cudaStream_t stream);
 struct GemmF16Maps {
   CUtensorMap x16;  // FP16 activations [m tokens][K], box 64 halves x 128 tokens, 128-byte swizzle
   CUtensorMap out;  // bf16 output [m][ldo] (with out_tma), box 128 rows x 128 tokens
 };
-cudaError_t launch_gemm_f16(const GemmF16Params& p, const GemmF16Maps& maps, int grid, cudaStream_t stream);
+cudaError_t launch_gemm_f16(const GemmF16Params& p, const GemmF16Maps& maps, int grid, cudaStream_t stream,
+                            bool fold = false);
 uint32_t gemm_f16_smem_bytes(int wstages, bool out_stage = false);
 // bf16 output map for the FP16 GEMM's TMA stores; false unless out is 16-byte aligned with ldo % 8 == 0.
 bool make_gemm_out_map(void* out, int64_t ldo, int n_rows, int m, CUtensorMap* map);

@@ -1,5 +1,7 @@
 // IQ3_S weight preparation (AoS GGUF blocks -> SoA fields) and the standalone
 // decoder used by the bit-exactness tests.
+#include <cuda_fp16.h>
+
 #include "kernels.cuh"
 
 namespace mambo {
@@ -107,6 +109,38 @@ __global__ void iq3s_pack_kernel(const PackWeightParams p) {
     }
     reinterpret_cast<uint4*>(p.packed)[i] = v;
   }
+}
+
+// The exponent of each row's largest block scale, floor(log2(max_b |d_b|))
+// over the finite d of the row (0 for a row without a finite non-zero d;
+// rows past N, up to whole 128-row tiles, also 0): the folded FP16 GEMM
+// scales each row's weights by 2^-e so that they stay in FP16's normal range.
+// One thread per row.
+__global__ void iq3s_row_exp_kernel(const uint16_t* __restrict__ d, int64_t n_rows, int64_t n_blocks, int64_t rows_pad,
+                                    int8_t* __restrict__ row_exp) {
+  for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < rows_pad;
+       r += (int64_t)gridDim.x * blockDim.x) {
+    uint32_t mag = 0;  // largest finite |d| as fp16 bits (ordered like the values)
+    if (r < n_rows)
+      for (int64_t b = 0; b < n_blocks; ++b) {
+        const uint32_t m = __ldg(d + b * n_rows + r) & 0x7FFFu;
+        if (m < 0x7C00u) mag = max(mag, m);  // skip Inf and NaN
+      }
+    int e = 0;
+    if (mag != 0) {
+      const float v = __half2float(__ushort_as_half((unsigned short)mag));
+      e = (int)((__float_as_uint(v) >> 23) & 0xFFu) - 127;
+    }
+    row_exp[r] = (int8_t)e;
+  }
+}
+
+cudaError_t launch_iq3s_row_exp(const uint8_t* d, int64_t n_rows, int64_t n_blocks, int8_t* row_exp,
+                                cudaStream_t stream) {
+  const int64_t rows_pad = (n_rows + 127) / 128 * 128;
+  iq3s_row_exp_kernel<<<(unsigned)((rows_pad + 255) / 256), 256, 0, stream>>>(
+      reinterpret_cast<const uint16_t*>(d), n_rows, n_blocks, rows_pad, row_exp);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_iq3s_pack(const PackWeightParams& p, int num_sms, cudaStream_t stream) {

@@ -231,3 +231,61 @@ def test_default_split_on_few_tiles_matches_oracle(cuda_device):
     assert select_config(64, 8192, 8192, cuda_device)["kernel"] in (_lib.MAMBO_KERNEL_AUTO,
                                                                     _lib.MAMBO_KERNEL_GEMM_F16,
                                                                     _lib.MAMBO_KERNEL_GEMM_F16_PAIR)
+
+
+GEMM_F16_FOLD = {"kernel": _lib.MAMBO_KERNEL_GEMM_F16_FOLD, "warps": 8, "stages": 4}
+FOLD_FROB_TOL = 1e-3  # north star bound; each folded weight carries one or two FP16 roundings (~4e-4 RMS)
+
+
+@pytest.mark.parametrize("m,n,k,outliers", [(32, 256, 512, False), (130, 384, 1024, True), (257, 136, 512, False),
+                                            (64, 640, 1536, True), (300, 256, 2048, True)])
+@pytest.mark.parametrize("stages,split", [(2, 1), (3, 1), (4, 1), (4, 3)])
+def test_folded_gemm_within_north_star_bound(cuda_device, m, n, k, outliers, stages, split):
+    fields, xq, xs, ref = _case(cuda_device, m, n, k, seed=1700 + m + n + stages + split, outliers=outliers)
+    cfg = dict(GEMM_F16_FOLD, stages=stages, split=split)
+    out = launch_iq3_s_fp8_matmul(xq, xs, fields, config=cfg)
+    got = to_np(out).astype(np.float64)
+    err = O.relative_frobenius(got, ref)
+    assert err < FOLD_FROB_TOL, err
+    np.testing.assert_allclose(got, ref, rtol=4e-3, atol=2e-3 * np.abs(ref).max())
+    assert torch.equal(out, launch_iq3_s_fp8_matmul(xq, xs, fields, config=cfg))  # deterministic
+
+
+def test_folded_gemm_wide_scale_ranges(cuda_device):
+    """Block scales spread over 2^10 within a row, and a zero block: the per-row exponent keeps every
+    folded weight in FP16's normal range."""
+    raw = O.make_synthetic_iq3s(256, 4096, 1801)
+    rng = np.random.default_rng(1802)
+    d = (np.exp2(rng.integers(-16, -6, size=(256, 16))) * rng.uniform(1, 2, size=(256, 16))).astype("<f2")
+    d[5, 3] = 0
+    raw[..., :2] = d.view(np.uint8).reshape(256, 16, 2)
+    xq, xs = O.quantize_mxfp8(rng.standard_normal((96, 4096)).astype(np.float32))
+    ref = O.iq3s_linear_f64(xq, xs, raw)
+    fields = prepare_iq3_s_fields(torch.from_numpy(raw).to(cuda_device))
+    out = launch_iq3_s_fp8_matmul(torch.from_numpy(xq).to(cuda_device), torch.from_numpy(xs).to(cuda_device),
+                                  fields, config=GEMM_F16_FOLD)
+    assert O.relative_frobenius(to_np(out), ref) < FOLD_FROB_TOL
+
+
+@pytest.mark.parametrize("proj", sorted(LLAMA3_8B))
+def test_folded_full_size_prefill(cuda_device, proj):
+    """Llama-3-8B shapes at M = 2048 with 1 % outlier columns (x50) against a float64 GPU reference."""
+    n, k = LLAMA3_8B[proj]
+    m = 2048
+    gen = torch.Generator(device=cuda_device).manual_seed(1901 + n)
+    raw = torch.randint(0, 256, (n, k // 256, 110), dtype=torch.uint8, device=cuda_device, generator=gen)
+    d = (torch.rand((n, k // 256), device=cuda_device, generator=gen) * 9e-3 + 1e-3).half()
+    raw[..., :2] = d.view(torch.uint8).view(n, k // 256, 2)
+    fields = prepare_iq3_s_fields(raw)
+    x = torch.randn((m, k), device=cuda_device, generator=gen)
+    x[:, torch.randperm(k, device=cuda_device, generator=gen)[: round(0.01 * k)]] *= 50.0
+    xq, xs = launch_quantize_fp8(x.to(torch.bfloat16))
+    out = launch_iq3_s_fp8_matmul(xq, xs, fields, config=GEMM_F16_FOLD)
+    bits, scales = launch_dequant_iq3_s(fields)
+    lut = torch.from_numpy(O.decode_e4m3(np.arange(256, dtype=np.uint8))).to(cuda_device)
+    w = (lut[bits.long()] * scales.repeat_interleave(32, dim=1)).double()
+    del bits, scales
+    xe = lut[xq.long()].double() * torch.exp2(xs.double() - 127).repeat_interleave(32, dim=1)
+    ref = xe @ w.t()
+    err = (torch.linalg.norm(out.double() - ref) / torch.linalg.norm(ref)).item()
+    assert err < FOLD_FROB_TOL, err

@@ -301,7 +301,15 @@ def test_packed_layout_and_results_match_soa(cuda_device, m, n, k):
     packed = prepare_iq3_s_fields(torch.from_numpy(raw).to(cuda_device))
     assert soa.packed is None and packed.packed is not None
     blocks, tiles = k // 256, (n + 127) // 128
-    rec = to_np(packed.packed).reshape(tiles, blocks, 14080)
+    buf = to_np(packed.packed)
+    rec = buf[: tiles * blocks * 14080].reshape(tiles, blocks, 14080)
+    # Tail: per row of whole tiles, floor(log2(max |d|)) over the row's finite block scales (0 past N).
+    d = np.abs(raw[:, :, 0:2].copy().view("<f2")[..., 0].astype(np.float64))
+    d[~np.isfinite(d)] = 0
+    dmax = d.max(axis=1)
+    expect_exp = np.zeros(tiles * 128, dtype=np.int8)
+    expect_exp[:n] = np.where(dmax > 0, np.floor(np.log2(np.where(dmax > 0, dmax, 1))), 0).astype(np.int8)
+    np.testing.assert_array_equal(buf[tiles * blocks * 14080:][: tiles * 128].view(np.int8), expect_exp)
     pad = np.zeros((tiles * 128, blocks, 110), dtype=np.uint8)
     pad[:n] = raw
     for t in range(tiles):
