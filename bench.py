@@ -428,6 +428,84 @@ def prefill_block(torch, dev, ms=PREFILL_MS) -> dict:
             "l2": "flushed (256 MB write) before each timed launch"}
 
 
+def synthetic_q4k(torch, dev, n: int, k: int, seed: int):
+    """Random Q4_K blocks uint8 [N, K/256, 144] on the device: uniform bytes, fp16 d and dmin in +-[1e-4, 1e-2)."""
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    raw = torch.randint(0, 256, (n, k // 256, 144), dtype=torch.uint8, device=dev, generator=gen)
+    for f in range(2):
+        sign = torch.randint(0, 2, (n, k // 256), device=dev, generator=gen) * 2 - 1
+        v = ((torch.rand((n, k // 256), device=dev, generator=gen) * 9.9e-3 + 1e-4) * sign).half()
+        raw[..., 2 * f:2 * f + 2] = v.view(torch.uint8).view(n, k // 256, 2)
+    return raw
+
+
+def q4k_block(torch, dev) -> dict:
+    """Q4_K x MXFP8 decode linears (GGUF type Q4_K, 144 bytes per 256 weights) on the tcgen05 GEMV.
+
+    The Llama-3-8B projections of the decode sweep at M in {1, 2, 4, 8}, random
+    Q4_K weights (fp16 d and dmin in +-[1e-4, 1e-2)), bf16 N(0,1) activations.
+    Per linear, 10 back-to-back launches in one CUDA graph: the GEMV alone on
+    activations quantized beforehand (with their group sums), and the public
+    call from bf16 activations (the quantizer with sums, then the GEMV).
+    Weights per step exceed the L2 (the sweep's 20 weights are 487 MB).
+    """
+    from mambo_b200.kernels.q4_k_fp8 import launch_q4_k_fp8_matmul, launch_quantize_fp8_sums, \
+        prepare_q4_k_fields, q4_k_fp8_linear
+
+    stream = torch.cuda.Stream(dev)
+    launches = 10
+
+    def graph_us(fn, replays=10) -> float:
+        with torch.cuda.stream(stream):
+            fn()
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for _ in range(launches):
+                fn()
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                g.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(replays):
+                g.replay()
+            e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) * 1000 / (replays * launches)
+
+    rows, w_tot, b_tot, fb_tot, us_tot, fused_us_tot = [], 0, 0, 0, 0.0, 0.0
+    for pi, (name, n, k) in enumerate(PROJECTIONS):
+        gen = torch.Generator(device=dev).manual_seed(0x4B80 + pi)
+        w = prepare_q4_k_fields(synthetic_q4k(torch, dev, n, k, seed=0x4B00 + pi))
+        for m in M_SWEEP:
+            x = torch.randn((m, k), device=dev, generator=gen).to(torch.bfloat16)
+            xq, xs, xsum = launch_quantize_fp8_sums(x)
+            out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+            us = graph_us(lambda: launch_q4_k_fp8_matmul(xq, xs, xsum, w, out=out, stream=stream))
+            fused_us = graph_us(lambda: q4_k_fp8_linear(x, w, out=out, stream=stream))
+            wb = n * (k // 256) * 144
+            b = wb + m * k + m * (k // 32) * 5 + m * n * 2  # weights, E4M3 codes, scales + sums, bf16 out
+            rows.append({"m": m, "proj": name, "us": round(us, 2), "gbs": round(b / us / 1e3, 1),
+                         "fused_us": round(fused_us, 2)})
+            w_tot += wb
+            b_tot += b
+            fb_tot += wb + m * k * 2 + m * n * 2  # from bf16 activations to the bf16 output
+            us_tot += us
+            fused_us_tot += fused_us
+        del w
+    torch.cuda.empty_cache()
+    peak, kind = load_peaks()
+    achieved = b_tot / us_tot / 1e3
+    return {"value": achieved, "unit": "GB/s", "frac": achieved / peak, "peak": peak, "peak_kind": kind,
+            "weights_bytes_per_sweep": w_tot, "bytes_per_sweep": b_tot, "gemv_us_per_sweep": us_tot,
+            "fused_us_per_sweep": fused_us_tot,
+            "fused_gbs": fb_tot / fused_us_tot / 1e3,
+            "kernel": "iq3s_gemv_tm_kernel<NT,8,GemvNoGroup,false,true> (Q4_K decoders, stream-K)",
+            "timing": "per linear: 10 back-to-back launches in one CUDA graph, 10 replays, mean",
+            "per_launch": rows}
+
+
 def run_single(args) -> None:
     """Four linear launches of one shape (for ncu captures of a single kernel)."""
     import torch
@@ -438,6 +516,18 @@ def run_single(args) -> None:
 
     n, k, m = (int(v) for v in args.single.split(","))
     dev = torch.device("cuda", 0)
+    if args.q4k:
+        # Four Q4_K launches (prequantized activations with their group sums), then the IQ3_S ones below.
+        from mambo_b200.kernels.q4_k_fp8 import launch_q4_k_fp8_matmul, launch_quantize_fp8_sums, \
+            prepare_q4_k_fields
+        w4 = prepare_q4_k_fields(synthetic_q4k(torch, dev, n, k, seed=2))
+        xq4, xs4, xsum4 = launch_quantize_fp8_sums(torch.randn((m, k), device=dev).to(torch.bfloat16))
+        out4 = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+        for _ in range(4):
+            launch_q4_k_fp8_matmul(xq4, xs4, xsum4, w4, out=out4)
+        torch.cuda.synchronize()
+        del w4
+        args.prequantized = True
     gen = torch.Generator(device=dev).manual_seed(1)
     raw = torch.randint(0, 256, (n, k // 256, 110), dtype=torch.uint8, device=dev, generator=gen)
     d = (torch.rand((n, k // 256), device=dev, generator=gen) * 9e-3 + 1e-3).half()
@@ -863,9 +953,12 @@ def main() -> None:
     ap.add_argument("--no-prefill", action="store_true", help="skip the prefill block (BASELINE config 3)")
     ap.add_argument("--no-tp", action="store_true", help="skip the tensor-parallel block (BASELINE config 5)")
     ap.add_argument("--no-model", action="store_true", help="skip the whole-model block (BASELINE config 4)")
+    ap.add_argument("--no-q4k", action="store_true", help="skip the Q4_K decode block")
     ap.add_argument("--single", metavar="N,K,M",
                     help="profiling mode: run four linears of one shape (random IQ3_S weights) and exit")
     ap.add_argument("--kernel", type=int, default=None, help="with --single: MAMBO_KERNEL_* to use")
+    ap.add_argument("--q4k", action="store_true",
+                    help="with --single: four Q4_K launches of the shape first, then the IQ3_S ones prequantized")
     ap.add_argument("--prequantized", action="store_true",
                     help="with --single: MXFP8 activations quantized beforehand (mambo_iq3s_linear)")
     ap.add_argument("--workload", choices=("decode", "tp70b", "llama3_8b"), default="decode",
@@ -1138,6 +1231,7 @@ def main() -> None:
     # Single-GPU blocks (4 and 1) at N = 1 only.
     prefill = None if (args.no_prefill or world > 1) else prefill_block(torch, dev)
     model = None if (args.no_model or world > 1) else model_block(torch, dev)
+    q4k = None if (args.no_q4k or world > 1) else q4k_block(torch, dev)
     cpu = None if (args.no_cpu_baseline or world > 1) else cpu_baseline()
     line = {
         "metric": METRIC,
@@ -1191,6 +1285,8 @@ def main() -> None:
         "tp": tp,
         # every linear of a 32-layer Llama-3-8B
         "model": model,
+        # the decode sweep's linears with Q4_K weights (the next GGUF type)
+        "q4k": q4k,
     }
     print(json.dumps(line), flush=True)
 

@@ -316,6 +316,64 @@ MAMBO_API int mambo_iq3s_linear_noalloc(const uint8_t* xq, int64_t ldxq, const u
                               const MamboIQ3SWeight* w, const uint32_t* fp8_table, void* out, int out_dtype,
                               int64_t ldo, const MamboLinearConfig* cfg, mambo_stream_t stream);
 
+/*
+ * Q4_K x MXFP8 linear (GGUF type Q4_K; no counterpart kernel in the reference,
+ * which lists the type in its tensor-type table,
+ * src/python/mambo/utils/gguf_manifest.py:30-42, and decodes it only through
+ * gguf-py). A Q4_K block holds 256 weights in 144 bytes: fp16 d, fp16 dmin, 12
+ * bytes of eight 6-bit scales s_g and mins m_g, 128 bytes of 4-bit codes q;
+ * weight = d*s_g*q - dmin*m_g. The codes 0..15 are exact E4M3 operands of the
+ * tensor cores; per 32-weight group g the FP32 epilogue adds d*s_g times the
+ * group's partial product and subtracts dmin*m_g times the token's sum of the
+ * group's (quantized) activations.
+ *
+ * Packed layout: one record of MAMBO_Q4K_RECORD_BYTES per (128-row tile t,
+ * K block b) at ((t * B) + b) * MAMBO_Q4K_RECORD_BYTES: codes [8 chunks][128
+ * rows][16 B] (chunk c = code bytes 16c..16c+15 of the row's block), then
+ * [128 rows][4 B] d and dmin, then [128 rows][12 B] scales and mins; rows at or
+ * past N are zero. mambo_q4k_pack fills it from raw blocks [N, B, 144] with any
+ * byte strides (any alignment); the packed buffer must be 16-byte aligned.
+ */
+#define MAMBO_Q4K_BLOCK_BYTES 144
+#define MAMBO_Q4K_RECORD_BYTES 18432
+MAMBO_API size_t mambo_q4k_packed_bytes(int64_t n_rows, int64_t n_blocks);
+MAMBO_API int mambo_q4k_pack(const uint8_t* raw, int64_t n_rows, int64_t n_blocks, int64_t stride_row,
+                             int64_t stride_block, int64_t stride_byte, void* packed, mambo_stream_t stream);
+
+/*
+ * mambo_quantize_mxfp8 that also writes, per 32-value group, the sum of its
+ * quantized values E4M3(q) * 2^e as FP32 (sums [M, K/32], row stride ld_sums):
+ * exact, since 32 E4M3 values sum to at most 23 significant bits. A group with
+ * scale code 0xFF (NaN or infinity among its values) gets a NaN sum.
+ */
+MAMBO_API int mambo_quantize_mxfp8_sums(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, uint8_t* q,
+                                        int64_t ldq, uint8_t* s, int64_t lds, float* sums, int64_t ld_sums,
+                                        int rounding, mambo_stream_t stream);
+
+/*
+ * out[M, N] = decode_mxfp8(xq, xs) @ dequant_q4k(w).T with FP32 accumulation.
+ * xq, xs as for mambo_iq3s_linear; xsum: the group sums of the same quantized
+ * activations (mambo_quantize_mxfp8_sums), 16-byte aligned, row stride ldsum a
+ * multiple of 4. packed: the mambo_q4k_pack buffer of an [N, K] weight (B =
+ * K/256 blocks per row). cfg: NULL, or MAMBO_KERNEL_GEMV / AUTO with warps 0
+ * or 8, split 0 (stream-K); stages and prefetch are tunable. The tcgen05 GEMV
+ * runs in chunks of 32 tokens. workspace: mambo_q4k_linear_workspace_bytes()
+ * bytes, zero-filled once (the kernels leave it zeroed again).
+ */
+MAMBO_API size_t mambo_q4k_linear_workspace_bytes(int64_t m, int64_t n_rows, int64_t n_blocks,
+                                                  const MamboLinearConfig* cfg);
+MAMBO_API int mambo_q4k_linear(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t ldxs, const float* xsum,
+                               int64_t ldsum, int64_t m, const void* packed, int64_t n_rows, int64_t n_blocks,
+                               void* out, int out_dtype, int64_t ldo, const MamboLinearConfig* cfg, void* workspace,
+                               size_t workspace_bytes, mambo_stream_t stream);
+/* Quantization (round to nearest even, with group sums) into the workspace, then mambo_q4k_linear. */
+MAMBO_API size_t mambo_q4k_linear_fused_workspace_bytes(int64_t m, int64_t n_rows, int64_t n_blocks,
+                                                        const MamboLinearConfig* cfg);
+MAMBO_API int mambo_q4k_linear_fused(const void* x, int x_dtype, int64_t ldx, int64_t m, const void* packed,
+                                     int64_t n_rows, int64_t n_blocks, void* out, int out_dtype, int64_t ldo,
+                                     const MamboLinearConfig* cfg, void* workspace, size_t workspace_bytes,
+                                     mambo_stream_t stream);
+
 /* Number of tunable configurations of a kernel kind, and the i-th one (for the autotuner).
  * Replaces the search spaces of make_benchmark_cases (src/python/mambo/kernels/iq3_s_fp8.py:402-465). */
 MAMBO_API int mambo_num_configs(int kernel);

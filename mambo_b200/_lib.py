@@ -61,6 +61,13 @@ EXPORTED_SYMBOLS = (
     "mambo_device_status",
     "mambo_set_wait_limit_ns",
     "mambo_selftest_wait_timeout",
+    "mambo_q4k_packed_bytes",
+    "mambo_q4k_pack",
+    "mambo_quantize_mxfp8_sums",
+    "mambo_q4k_linear_workspace_bytes",
+    "mambo_q4k_linear",
+    "mambo_q4k_linear_fused_workspace_bytes",
+    "mambo_q4k_linear_fused",
 )
 
 
@@ -209,6 +216,23 @@ def load() -> ctypes.CDLL:
             "mambo_device_status": ([i32, ctypes.POINTER(i32), ctypes.POINTER(i32), ctypes.POINTER(i32)], i32),
             "mambo_set_wait_limit_ns": ([u64], i32),
             "mambo_selftest_wait_timeout": ([u64, vp], i32),
+            "mambo_q4k_packed_bytes": ([i64, i64], ctypes.c_size_t),
+            "mambo_q4k_pack": ([vp, i64, i64, i64, i64, i64, vp, vp], i32),
+            "mambo_quantize_mxfp8_sums": ([vp, i32, i64, i64, i64, vp, i64, vp, i64, vp, i64, i32, vp], i32),
+            "mambo_q4k_linear_workspace_bytes": ([i64, i64, i64, ctypes.POINTER(MamboLinearConfig)],
+                                                 ctypes.c_size_t),
+            "mambo_q4k_linear": (
+                [vp, i64, vp, i64, vp, i64, i64, vp, i64, i64, vp, i32, i64, ctypes.POINTER(MamboLinearConfig), vp,
+                 ctypes.c_size_t, vp],
+                i32,
+            ),
+            "mambo_q4k_linear_fused_workspace_bytes": ([i64, i64, i64, ctypes.POINTER(MamboLinearConfig)],
+                                                       ctypes.c_size_t),
+            "mambo_q4k_linear_fused": (
+                [vp, i32, i64, i64, vp, i64, i64, vp, i32, i64, ctypes.POINTER(MamboLinearConfig), vp,
+                 ctypes.c_size_t, vp],
+                i32,
+            ),
         }
         for name, (args, res) in sigs.items():
             fn = getattr(lib, name)

@@ -278,12 +278,15 @@ int64_t xs_copy_stride(int64_t n_blocks) { return (n_blocks * 8 + 15) / 16 * 16;
 // tile its own cluster on the SMs (at most 8, the portable cluster size, and
 // one K block each), within shared memory, and with every cluster resident at
 // once.
-int cluster_kparts(int row_tiles, int64_t b, const MamboLinearConfig& cfg, int nt, int sms, int smem_optin) {
+// q4k: the Q4_K variant of the kernel (its own shared-memory size).
+int cluster_kparts(int row_tiles, int64_t b, const MamboLinearConfig& cfg, int nt, int sms, int smem_optin,
+                   bool q4k = false) {
   int kp = row_tiles > 0 ? sms / row_tiles : 1;
   kp = kp < 1 ? 1 : kp > 8 ? 8 : kp;
   if (kp > b) kp = (int)b;
-  while (kp > 1 && (int)gemv_tm_smem_bytes(nt, cfg.stages, kp) > smem_optin) --kp;
-  while (kp > 1 && gemv_tm_max_clusters(nt, cfg.warps, cfg.stages, kp) < row_tiles) --kp;
+  auto smem = [&](int k) { return q4k ? q4k_gemv_smem_bytes(nt, cfg.stages, k) : gemv_tm_smem_bytes(nt, cfg.stages, k); };
+  while (kp > 1 && (int)smem(kp) > smem_optin) --kp;
+  while (kp > 1 && gemv_tm_max_clusters(nt, cfg.warps, cfg.stages, kp, q4k) < row_tiles) --kp;
   return kp;
 }
 
@@ -339,7 +342,8 @@ bool gemm_usable(const MamboIQ3SWeight* w, const uint8_t* xq, int64_t ldxq, int6
          m <= (int64_t)1 << 30;
 }
 
-GemvPlan plan_gemv(int64_t m_chunk, int64_t n, int64_t b, const MamboLinearConfig& cfg, int sms, int smem_optin) {
+GemvPlan plan_gemv(int64_t m_chunk, int64_t n, int64_t b, const MamboLinearConfig& cfg, int sms, int smem_optin,
+                   bool q4k = false) {
   GemvPlan P{};
   const bool tc = kernel_of(cfg) == MAMBO_KERNEL_GEMV;
   P.nt = gemv_nt_for(m_chunk);
@@ -350,7 +354,7 @@ GemvPlan plan_gemv(int64_t m_chunk, int64_t n, int64_t b, const MamboLinearConfi
   P.counters_bytes = kCounterBytes;
   if (tc && cfg.split != 0) {
     // Whole row tiles (split 1) or row tiles split over the CTAs of a cluster (split 2).
-    P.kparts = cfg.split == 2 ? cluster_kparts(P.row_tiles, b, cfg, P.nt, sms, smem_optin) : 1;
+    P.kparts = cfg.split == 2 ? cluster_kparts(P.row_tiles, b, cfg, P.nt, sms, smem_optin, q4k) : 1;
     P.grid = P.row_tiles * P.kparts;
   } else {
     int ctas = sms * (!tc && cfg.ctas_per_sm > 0 ? cfg.ctas_per_sm : 1);
@@ -491,6 +495,31 @@ int launch_gemm_f16_path(const GemmF16Source& src, int64_t m, const MamboIQ3SWei
   return ok();
 }
 
+// The GEMV's activation tensor maps (MXFP8 codes and scales of tokens [0, mc));
+// rows that are not 16-byte aligned are copied to xcopy / xscopy first.
+int gemv_activation_maps(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t ldxs, int64_t mc, int64_t b,
+                         int box, uint8_t* xcopy, uint8_t* xscopy, GemvTmMaps* maps, cudaStream_t stream) {
+  const int64_t k = b * 256;
+  if (!make_gemv_x_map(xq, ldxq, (int)mc, (int)b, box, &maps->x)) {
+    if (!xcopy) return fail(MAMBO_EINVAL, "x_values rows must be 16-byte aligned");
+    cudaError_t e = cudaMemcpy2DAsync(xcopy, (size_t)k, xq, (size_t)ldxq, (size_t)k, (size_t)mc,
+                                      cudaMemcpyDeviceToDevice, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "copy of unaligned x_values");
+    if (!make_gemv_x_map(xcopy, k, (int)mc, (int)b, box, &maps->x))
+      return fail(MAMBO_ECUDA, "activation tensor map could not be encoded");
+  }
+  if (!make_gemv_xs_map(xs, ldxs, (int)mc, (int)b, box, &maps->xs)) {
+    if (!xscopy) return fail(MAMBO_EINVAL, "x_scales rows must be 16-byte aligned");
+    const int64_t ld = xs_copy_stride(b);
+    cudaError_t e = cudaMemcpy2DAsync(xscopy, (size_t)ld, xs, (size_t)ldxs, (size_t)(b * 8), (size_t)mc,
+                                      cudaMemcpyDeviceToDevice, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "copy of unaligned x_scales");
+    if (!make_gemv_xs_map(xscopy, ld, (int)mc, (int)b, box, &maps->xs))
+      return fail(MAMBO_ECUDA, "activation-scale tensor map could not be encoded");
+  }
+  return MAMBO_OK;
+}
+
 // Launches the tcgen05 GEMV for tokens [0, mc) of xq/xs (already offset to the chunk).
 int launch_tc_chunk(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t ldxs, int64_t mc,
                     const MamboIQ3SWeight* w, const uint32_t* fp8_table, void* out, int out_dtype, int64_t ldo,
@@ -505,28 +534,14 @@ int launch_tc_chunk(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t 
     if (f % 16 != 0 || w->n_rows % 8 != 0)
       return fail(MAMBO_EINVAL,
                   "the tcgen05 GEMV needs N %% 8 == 0 and 16-byte aligned weight fields (use MAMBO_KERNEL_GEMV_SYNC)");
-  const int64_t k = w->n_blocks * 256;
   const int box = 8 * P.nt;
   if (x_bf16) {
     // Fused quantization: the kernel loads the bf16 rows itself.
-    if (!make_gemv_xb_map(x_bf16, ldx, (int)mc, k, box, &maps.xb))
+    if (!make_gemv_xb_map(x_bf16, ldx, (int)mc, w->n_blocks * 256, box, &maps.xb))
       return fail(MAMBO_EINVAL, "bf16 activations need 16-byte aligned rows");
-  } else if (!make_gemv_x_map(xq, ldxq, (int)mc, (int)w->n_blocks, box, &maps.x)) {
-    if (!xcopy) return fail(MAMBO_EINVAL, "x_values rows must be 16-byte aligned");
-    cudaError_t e = cudaMemcpy2DAsync(xcopy, (size_t)k, xq, (size_t)ldxq, (size_t)k, (size_t)mc,
-                                      cudaMemcpyDeviceToDevice, stream);
-    if (e != cudaSuccess) return cuda_fail(e, "copy of unaligned x_values");
-    if (!make_gemv_x_map(xcopy, k, (int)mc, (int)w->n_blocks, box, &maps.x))
-      return fail(MAMBO_ECUDA, "activation tensor map could not be encoded");
-  }
-  if (!x_bf16 && !make_gemv_xs_map(xs, ldxs, (int)mc, (int)w->n_blocks, box, &maps.xs)) {
-    if (!xscopy) return fail(MAMBO_EINVAL, "x_scales rows must be 16-byte aligned");
-    const int64_t ld = xs_copy_stride(w->n_blocks);
-    cudaError_t e = cudaMemcpy2DAsync(xscopy, (size_t)ld, xs, (size_t)ldxs, (size_t)(w->n_blocks * 8), (size_t)mc,
-                                      cudaMemcpyDeviceToDevice, stream);
-    if (e != cudaSuccess) return cuda_fail(e, "copy of unaligned x_scales");
-    if (!make_gemv_xs_map(xscopy, ld, (int)mc, (int)w->n_blocks, box, &maps.xs))
-      return fail(MAMBO_ECUDA, "activation-scale tensor map could not be encoded");
+  } else {
+    const int st = gemv_activation_maps(xq, ldxq, xs, ldxs, mc, w->n_blocks, box, xcopy, xscopy, &maps, stream);
+    if (st != MAMBO_OK) return st;
   }
   GemvTmParams p{};
   p.m = (int)mc;
@@ -1361,3 +1376,208 @@ extern "C" int mambo_iq3s_linear_noalloc(const uint8_t* xq, int64_t ldxq, const 
   }
   return ok();
 }
+
+// ---------------------------------------------------------------------------
+// Q4_K x MXFP8 linear on the tcgen05 GEMV (GGUF type Q4_K; the reference lists
+// the type in src/python/mambo/utils/gguf_manifest.py:30-42 and has no kernel
+// for it). Stream-K over (128-row tile, K block) units, 32-token chunks.
+namespace {
+
+// The Q4_K GEMV configuration: tcgen05 GEMV, 8 decoder warps. Default as for
+// IQ3_S: the cluster K-split while every row tile gets its own CTAs,
+// stream-K beyond that; the deepest weight ring up to 8 stages that fits.
+int q4k_config(const MamboLinearConfig* cfg, int64_t mc, int64_t n, const DeviceInfo& info, MamboLinearConfig* c) {
+  MamboLinearConfig d{};
+  d.kernel = MAMBO_KERNEL_GEMV;
+  d.warps = 8;
+  d.ctas_per_sm = 1;
+  d.split = (n + 127) / 128 <= info.sms ? 2 : 0;
+  d.prefetch = 4;
+  d.stages = 8;
+  while (d.stages > 2 && (int)q4k_gemv_smem_bytes(gemv_nt_for(mc), d.stages, 0) > info.max_smem_optin) --d.stages;
+  if (cfg && cfg->kernel != MAMBO_KERNEL_AUTO) {
+    if (cfg->kernel != MAMBO_KERNEL_GEMV)
+      return fail(MAMBO_EINVAL, "Q4_K runs on the tcgen05 GEMV (MAMBO_KERNEL_GEMV) only");
+    if (cfg->warps != 0 && cfg->warps != 8) return fail(MAMBO_EINVAL, "Q4_K decodes with 8 decoder warps");
+    if (cfg->loader != 0) return fail(MAMBO_EINVAL, "Q4_K streams the packed records (loader 0)");
+    if (cfg->split < 0 || cfg->split > 2)
+      return fail(MAMBO_EINVAL, "split must be 0 (stream-K), 1 (row tile per CTA) or 2 (cluster K-split)");
+    if (cfg->stages != 0) d.stages = cfg->stages;
+    d.split = cfg->split;
+    d.prefetch = cfg->prefetch;
+  }
+  if (d.stages < 2 || d.stages > gemv_tm_max_stages())
+    return fail(MAMBO_EINVAL, "stages must be in [2, %d]", gemv_tm_max_stages());
+  if (d.prefetch < 0 || d.prefetch > 64) return fail(MAMBO_EINVAL, "prefetch must be in [0, 64]");
+  const uint32_t smem = q4k_gemv_smem_bytes(gemv_nt_for(mc), d.stages, d.split == 2 ? 2 : 0);
+  if ((int)smem > info.max_smem_optin)
+    return fail(MAMBO_EINVAL, "configuration needs %u bytes of shared memory (device allows %d)", smem,
+                info.max_smem_optin);
+  *c = d;
+  return MAMBO_OK;
+}
+
+size_t q4k_gemv_workspace(const GemvPlan& P) {
+  return P.counters_bytes + P.partial_bytes + P.xcopy_bytes + P.xscopy_bytes;
+}
+
+size_t q4k_plan_bytes(int64_t m, int64_t n_rows, int64_t n_blocks, const MamboLinearConfig* cfg) {
+  int st;
+  DeviceInfo info = device_info(&st);
+  if (st != MAMBO_OK || info.sms <= 0) {
+    info.sms = 148;
+    info.max_smem_optin = kSmemOptinDefault;
+  }
+  MamboLinearConfig c;
+  const int64_t mc = m < 32 ? m : 32;
+  if (q4k_config(cfg, mc, n_rows, info, &c) != MAMBO_OK) return 0;
+  return q4k_gemv_workspace(plan_gemv(mc, n_rows, n_blocks, c, info.sms, info.max_smem_optin, true));
+}
+
+int q4k_linear_impl(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t ldxs, const float* xsum,
+                    int64_t ldsum, int64_t m, const void* packed, int64_t n_rows, int64_t n_blocks, void* out,
+                    int out_dtype, int64_t ldo, const MamboLinearConfig* cfg, void* workspace, size_t workspace_bytes,
+                    cudaStream_t stream) {
+  if (!xq || !xs || !xsum || !packed || !out) return fail(MAMBO_EINVAL, "null pointer");
+  if (n_rows < 1 || n_blocks < 1) return fail(MAMBO_EINVAL, "Q4_K weight must have positive N and K");
+  if (n_rows > (int64_t)1 << 24 || n_blocks > 4096) return fail(MAMBO_EINVAL, "Q4_K weight too large");
+  const int64_t k = n_blocks * 256;
+  if (m < 1) return fail(MAMBO_EINVAL, "x_values must be uint8 [M,K] with M >= 1");
+  if (ldxq < k || ldxs < k / 32 || ldsum < k / 32) return fail(MAMBO_EINVAL, "activation row stride smaller than the row");
+  if ((uintptr_t)xsum % 16 || ldsum % 4)
+    return fail(MAMBO_EINVAL, "x_sums must be 16-byte aligned with a row stride that is a multiple of 4");
+  if ((uintptr_t)packed % 16) return fail(MAMBO_EINVAL, "the packed weight buffer must be 16-byte aligned");
+  if (out_dtype != MAMBO_F32 && out_dtype != MAMBO_BF16) return fail(MAMBO_EINVAL, "out must be f32 or bf16");
+  if (ldo < n_rows) return fail(MAMBO_EINVAL, "out row stride is smaller than N");
+  DeviceInfo info;
+  int st = require_sm100(&info);
+  if (st != MAMBO_OK) return st;
+  const int64_t m_chunk_max = 32;
+  const size_t esz = out_dtype == MAMBO_BF16 ? 2 : 4;
+  for (int64_t m0 = 0; m0 < m; m0 += m_chunk_max) {
+    const int64_t mc = (m - m0) < m_chunk_max ? (m - m0) : m_chunk_max;
+    MamboLinearConfig c;
+    st = q4k_config(cfg, mc, n_rows, info, &c);
+    if (st != MAMBO_OK) return st;
+    const GemvPlan P = plan_gemv(mc, n_rows, n_blocks, c, info.sms, info.max_smem_optin, true);
+    if ((size_t)P.counter_slots * sizeof(int) > kGemvCounterBytes)
+      return fail(MAMBO_EINVAL, "N=%lld needs more split-K counters than the workspace holds", (long long)n_rows);
+    const size_t need = q4k_gemv_workspace(P);
+    if (!workspace || workspace_bytes < need)
+      return fail(MAMBO_EWORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+    if ((uintptr_t)workspace % 256) return fail(MAMBO_EINVAL, "workspace must be 256-byte aligned");
+    uint8_t* xcopy = (uint8_t*)workspace + P.counters_bytes + P.partial_bytes;
+    GemvTmMaps maps;
+    std::memset(&maps, 0, sizeof(maps));
+    st = gemv_activation_maps(xq + m0 * ldxq, ldxq, xs + m0 * ldxs, ldxs, mc, n_blocks, 8 * P.nt, xcopy,
+                              xcopy + P.xcopy_bytes, &maps, stream);
+    if (st != MAMBO_OK) return st;
+    GemvTmParams p{};
+    p.m = (int)mc;
+    p.n_rows = (int)n_rows;
+    p.n_blocks = (int)n_blocks;
+    p.packed = (const uint8_t*)packed;
+    p.out = (uint8_t*)out + m0 * ldo * esz;
+    p.out_bf16 = out_dtype == MAMBO_BF16;
+    p.ldo = ldo;
+    p.partials = (float*)((uint8_t*)workspace + P.counters_bytes);
+    p.counters = (int*)workspace;
+    p.stages = c.stages;
+    p.prefetch = c.prefetch;
+    p.kparts = P.kparts;
+    p.row_tiles = P.row_tiles;
+    p.total_units = P.units;
+    p.xsum = xsum + m0 * ldsum;
+    p.ldsum = ldsum;
+    cudaError_t e = launch_gemv_tm(p, P.nt, 8, maps, P.grid, stream, true);
+    if (e != cudaSuccess) return cuda_fail(e, "q4k_gemv_tm");
+  }
+  return ok();
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t mambo_q4k_packed_bytes(int64_t n_rows, int64_t n_blocks) {
+  if (n_rows < 1 || n_blocks < 1) return 0;
+  return (size_t)((n_rows + 127) / 128) * (size_t)n_blocks * kQ4kRecordBytes;
+}
+
+int mambo_q4k_pack(const uint8_t* raw, int64_t n_rows, int64_t n_blocks, int64_t stride_row, int64_t stride_block,
+                   int64_t stride_byte, void* packed, mambo_stream_t stream) {
+  if (!raw || !packed) return fail(MAMBO_EINVAL, "null pointer");
+  if (n_rows < 1 || n_blocks < 1) return fail(MAMBO_EINVAL, "Q4_K weight must have positive N and K");
+  if ((uintptr_t)packed % 16) return fail(MAMBO_EINVAL, "the packed buffer must be 16-byte aligned");
+  DeviceInfo info;
+  int st = require_sm100(&info);
+  if (st != MAMBO_OK) return st;
+  Q4kPackParams p{raw, n_rows, n_blocks, stride_row, stride_block, stride_byte, (uint8_t*)packed};
+  cudaError_t e = launch_q4k_pack(p, info.sms, (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "q4k_pack");
+  return ok();
+}
+
+int mambo_quantize_mxfp8_sums(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, uint8_t* q, int64_t ldq,
+                              uint8_t* s, int64_t lds, float* sums, int64_t ld_sums, int rounding,
+                              mambo_stream_t stream) {
+  if (!x || !q || !s || !sums) return fail(MAMBO_EINVAL, "null pointer");
+  if (x_dtype != MAMBO_F32 && x_dtype != MAMBO_BF16) return fail(MAMBO_EINVAL, "activation must be f32 or bf16");
+  if (m < 1 || k < 32 || k % 32) return fail(MAMBO_EINVAL, "activation must be [M,K] with K divisible by 32");
+  if (ldx < k || ldq < k || lds < k / 32 || ld_sums < k / 32)
+    return fail(MAMBO_EINVAL, "row stride smaller than the row");
+  if (rounding != MAMBO_ROUND_NEAREST_EVEN && rounding != MAMBO_ROUND_TIES_DOWN)
+    return fail(MAMBO_EINVAL, "unknown rounding mode %d", rounding);
+  DeviceInfo info;
+  int st = require_sm100(&info);
+  if (st != MAMBO_OK) return st;
+  QuantParams p{x, m, k, ldx, q, ldq, s, lds, sums, ld_sums};
+  cudaError_t e = launch_quantize_mxfp8(p, x_dtype, rounding, info.sms, (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "quantize_mxfp8 (sums)");
+  return ok();
+}
+
+size_t mambo_q4k_linear_workspace_bytes(int64_t m, int64_t n_rows, int64_t n_blocks, const MamboLinearConfig* cfg) {
+  if (m < 1 || n_rows < 1 || n_blocks < 1) return 0;
+  return q4k_plan_bytes(m, n_rows, n_blocks, cfg);
+}
+
+int mambo_q4k_linear(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t ldxs, const float* xsum,
+                     int64_t ldsum, int64_t m, const void* packed, int64_t n_rows, int64_t n_blocks, void* out,
+                     int out_dtype, int64_t ldo, const MamboLinearConfig* cfg, void* workspace,
+                     size_t workspace_bytes, mambo_stream_t stream) {
+  return q4k_linear_impl(xq, ldxq, xs, ldxs, xsum, ldsum, m, packed, n_rows, n_blocks, out, out_dtype, ldo, cfg,
+                         workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+size_t mambo_q4k_linear_fused_workspace_bytes(int64_t m, int64_t n_rows, int64_t n_blocks,
+                                              const MamboLinearConfig* cfg) {
+  if (m < 1 || n_rows < 1 || n_blocks < 1) return 0;
+  const int64_t k = n_blocks * 256;
+  return align256(q4k_plan_bytes(m, n_rows, n_blocks, cfg)) + align256((size_t)(m * k)) +
+         align256((size_t)(m * xs_copy_stride(n_blocks))) + align256((size_t)(m * (k / 32)) * sizeof(float));
+}
+
+int mambo_q4k_linear_fused(const void* x, int x_dtype, int64_t ldx, int64_t m, const void* packed, int64_t n_rows,
+                           int64_t n_blocks, void* out, int out_dtype, int64_t ldo, const MamboLinearConfig* cfg,
+                           void* workspace, size_t workspace_bytes, mambo_stream_t stream) {
+  if (!x || !packed || !out) return fail(MAMBO_EINVAL, "null pointer");
+  if (m < 1 || n_rows < 1 || n_blocks < 1) return fail(MAMBO_EINVAL, "shapes must be positive");
+  const size_t need = mambo_q4k_linear_fused_workspace_bytes(m, n_rows, n_blocks, cfg);
+  if (!workspace || workspace_bytes < need)
+    return fail(MAMBO_EWORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+  if ((uintptr_t)workspace % 256) return fail(MAMBO_EINVAL, "workspace must be 256-byte aligned");
+  const int64_t k = n_blocks * 256, lds = xs_copy_stride(n_blocks);
+  const size_t gemv_bytes = align256(q4k_plan_bytes(m, n_rows, n_blocks, cfg));
+  uint8_t* xq = (uint8_t*)workspace + gemv_bytes;
+  uint8_t* xs = xq + align256((size_t)(m * k));
+  float* xsum = (float*)(xs + align256((size_t)(m * lds)));
+  int st = mambo_quantize_mxfp8_sums(x, x_dtype, m, k, ldx, xq, k, xs, lds, xsum, k / 32, MAMBO_ROUND_NEAREST_EVEN,
+                                     stream);
+  if (st != MAMBO_OK) return st;
+  return q4k_linear_impl(xq, k, xs, lds, xsum, k / 32, m, packed, n_rows, n_blocks, out, out_dtype, ldo, cfg,
+                         workspace, gemv_bytes, (cudaStream_t)stream);
+}
+
+}  // extern "C"
+static_assert(MAMBO_Q4K_RECORD_BYTES == kQ4kRecordBytes, "Q4_K record size of the C ABI and of the kernel");

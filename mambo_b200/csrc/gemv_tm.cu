@@ -104,29 +104,31 @@ struct TmLayout {
   uint32_t w, aux;  // one of kRing epilogue buffers: rows' (d, scale word)
 };
 
-__host__ __device__ inline TmLayout tm_layout(int nt) {
+// q4k: Q4_K records (kQ4kRecordBytes; no codebook, 16 bytes of epilogue data per row).
+__host__ __device__ inline TmLayout tm_layout(int nt, bool q4k = false) {
   TmLayout L{};
   L.qs = 0;
   L.signs = kRows * 64;         // 8192
   L.qh = L.signs + kRows * 32;  // 12288
   L.d = L.qh + kRows * 8;       // 13312
   L.scales = L.d + kRows * 2;   // 13568
-  L.stage = L.scales + kRows * 4;  // 14080 = kRecordBytes
+  L.stage = q4k ? kQ4kRecordBytes : L.scales + kRows * 4;  // 14080 = kRecordBytes
   L.b = 0;
   L.xs = 256u * tm_box_tokens(nt);  // activation scale bytes: [tokens][16] (two K blocks' groups)
   L.xslot = align_up_tm(L.xs + 16u * tm_box_tokens(nt), 1024);
   L.w = 0;
-  L.aux = kRows * 8;
+  L.aux = kRows * (q4k ? 16 : 8);
   return L;
 }
 
 // kparts > 1: rank 0 of each cluster also holds the other ranks' partials.
-__host__ __device__ inline uint32_t tm_smem_bytes(int nt, int stages, int kparts, bool fused = false) {
-  const TmLayout L = tm_layout(nt);
+__host__ __device__ inline uint32_t tm_smem_bytes(int nt, int stages, int kparts, bool fused = false,
+                                                  bool q4k = false) {
+  const TmLayout L = tm_layout(nt, q4k);
   const uint32_t cpart = kparts > 1 ? (uint32_t)(kparts - 1) * kRows * 8u * nt * 4u : 0u;
   const uint32_t bf = fused ? 128u + (uint32_t)tm_bstages(nt) * tm_box_tokens(nt) * kBfRowBytes : 0u;
-  return kTableBytes + 1024 + align_up_tm(stages * L.stage, 1024) + tm_xstages(nt) * L.xslot + kRing * L.aux +
-         kTableStageBytes + kBarBytes + cpart + bf;
+  return (q4k ? 0u : kTableBytes) + 1024 + align_up_tm(stages * L.stage, 1024) + tm_xstages(nt) * L.xslot +
+         kRing * L.aux + kTableStageBytes + kBarBytes + cpart + bf;
 }
 
 __device__ __forceinline__ int unit_begin_tm(int cta, int grid, int units) {
@@ -196,6 +198,24 @@ __device__ __forceinline__ void store_out_tm(const OutView& o, const QuantView& 
   }
 }
 
+// Q4_K code word -> E4M3: byte j of w holds code lo_j (low nibble, one
+// 32-value group) and hi_j (high nibble, the next group). lo gets
+// E4M3(lo_0..lo_3), hi gets E4M3(hi_0..hi_3). The codes 0..15 are exact in
+// E4M3: two 8-entry byte lookups (prmt) for 0-7 and 8-15, and a prmt in
+// sign-replicate mode (selector bit 3 = code bit 3, source bytes 0x80) for the
+// byte mask that picks between them.
+__device__ __forceinline__ void q4k_e4m3(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  constexpr uint32_t kLut0 = 0x44403800u, kLut1 = 0x4E4C4A48u;  // E4M3 of 0..7
+  constexpr uint32_t kLut2 = 0x53525150u, kLut3 = 0x57565554u;  // E4M3 of 8..15
+  const uint32_t sel = w & 0x77777777u, selh = sel >> 16, wh = w >> 16;
+  const uint32_t a0 = prmt(kLut0, kLut1, sel), b0 = prmt(kLut2, kLut3, sel), m0 = prmt(0x80808080u, 0x80808080u, w);
+  const uint32_t a1 = prmt(kLut0, kLut1, selh), b1 = prmt(kLut2, kLut3, selh), m1 = prmt(0x80808080u, 0x80808080u, wh);
+  const uint32_t r0 = (a0 & ~m0) | (b0 & m0);  // [lo0, hi0, lo1, hi1]
+  const uint32_t r1 = (a1 & ~m1) | (b1 & m1);  // [lo2, hi2, lo3, hi3]
+  lo = prmt(r0, r1, 0x6420u);
+  hi = prmt(r0, r1, 0x7531u);
+}
+
 // The item of a grouped launch that holds unit u, searching upwards from item l.
 __device__ __forceinline__ int group_item(const GemvGroup& g, int u, int l) {
   while (l + 1 < g.count && g.items[l + 1].unit0 <= u) ++l;
@@ -262,7 +282,10 @@ __device__ __forceinline__ void sum_partials(const float* partials, BeginOf begi
 // activations bf16 quantized here).
 // kQ: the launch also writes its output's MXFP8 quantization (QuantView);
 // launches without it run a kernel that has none of that code.
-template <int NT, int kDecWarps, class G, bool kQ>
+// kQ4K: Q4_K weights (q4k records; prequantized activations with their group
+// sums, p.xsum): the decoders turn 4-bit codes into E4M3 and the epilogue
+// applies d*s_g and subtracts dmin*m_g times the activation group sum.
+template <int NT, int kDecWarps, class G, bool kQ, bool kQ4K = false>
 __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
     iq3s_gemv_tm_kernel(const __grid_constant__ GemvTmParams p, const __grid_constant__ GemvTmMaps maps,
                         const __grid_constant__ G grp) {
@@ -286,13 +309,16 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
   static_assert(kDecWarps == 8 || kDecWarps == 16, "8 or 16 decoder warps");
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  const TmLayout L = tm_layout(NT);
+  const TmLayout L = tm_layout(NT, kQ4K);
+  constexpr uint32_t kTableRegion = kQ4K ? 0u : (uint32_t)kTableBytes;  // no codebook for Q4_K
+  constexpr uint32_t kRecBytes = kQ4K ? kQ4kRecordBytes : (uint32_t)kRecordBytes;
+  static_assert(!(kQ4K && (kQ || std::is_same<G, GemvGroup>::value)), "Q4_K runs single linears only");
   // The codebook sits at the start of dynamic shared memory (a link-time
   // constant address); the stages follow, aligned to 1024 bytes at run time.
   // (Offsets from smem_raw keep the pointers in the shared address space, so
   // every access below compiles to a shared-memory instruction.)
   uint8_t* table = smem_raw;
-  uint8_t* st0 = smem_raw + kTableBytes + ((1024u - ((smem_u32(smem_raw) + kTableBytes) & 1023u)) & 1023u);
+  uint8_t* st0 = smem_raw + kTableRegion + ((1024u - ((smem_u32(smem_raw) + kTableRegion) & 1023u)) & 1023u);
   uint8_t* x0 = st0 + align_up_tm((uint32_t)p.stages * L.stage, 1024);  // activation slots
   uint8_t* aux0 = x0 + (size_t)AS * L.xslot;
   uint32_t* tstage = reinterpret_cast<uint32_t*>(aux0 + kRing * L.aux);
@@ -350,7 +376,7 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
   // Decoder threads fetch the 2 KB codebook now, so that its global-memory
   // latency overlaps the barrier and TMEM set-up below.
   uint32_t tw[512 / (kDecWarps * 32)];
-  if (warp >= 2 && warp < kEpiWarp0) {
+  if (!kQ4K && warp >= 2 && warp < kEpiWarp0) {
 #pragma unroll
     for (int j = 0; j < 512 / (kDecWarps * 32); ++j) tw[j] = __ldg(p.table + (threadIdx.x - 64) + j * kDecWarps * 32);
   }
@@ -404,9 +430,9 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
     auto record = [&](int u, int& hint) -> const uint8_t* {
       if constexpr (kGroup) {
         hint = group_item(grp, u, hint);
-        return grp.items[hint].packed + (size_t)(u - grp.items[hint].unit0) * kRecordBytes;
+        return grp.items[hint].packed + (size_t)(u - grp.items[hint].unit0) * kRecBytes;
       } else {
-        return p.packed + (size_t)u * kRecordBytes;
+        return p.packed + (size_t)u * kRecBytes;
       }
     };
     int issue_hint = 0, prefetch_hint = 0;
@@ -417,8 +443,8 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
         // Tile-major records have the stage's layout: one copy per unit.
         const uint8_t* rec = record(u0 + it, issue_hint);
         if (lane == 0) {
-          mbar_arrive_expect_tx(full, (uint32_t)kRecordBytes);
-          bulk_load_hint(st, rec, kRecordBytes, full, policy);
+          mbar_arrive_expect_tx(full, kRecBytes);
+          bulk_load_hint(st, rec, kRecBytes, full, policy);
         }
       } else {
         uint32_t rows;
@@ -433,7 +459,7 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
     auto prefetch = [&](int it) {
       if (kGroup || p.packed) {
         const uint8_t* rec = record(u0 + it, prefetch_hint);
-        if (lane == 0) bulk_prefetch_l2(rec, kRecordBytes);
+        if (lane == 0) bulk_prefetch_l2(rec, kRecBytes);
       } else {
         uint32_t rows;
         size_t base;
@@ -665,6 +691,66 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
     const int rl = 32 * q + lane;  // weight row within the tile = TMEM lane
     const int nthreads = kDecWarps * 32;
     const int tid = threadIdx.x - 64;
+    if constexpr (kQ4K) {
+      // Q4_K: this thread's half of the block is code bytes 64*part .. 64*part+63
+      // (chunks 4*part .. 4*part+3): byte groups 2*part and 2*part+1, each holding
+      // two 32-value groups (low and high nibbles) = local groups 0..3.
+      static_assert(kParts == 2, "Q4_K decodes with 8 decoder warps");
+      (void)tw;
+      const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(part * 32);
+      if (part == 0)
+        tc::st_x4(tmem + ((uint32_t)(32 * q) << 16) + tm_sfa_col(NT), 0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu,
+                  0x7F7F7F7Fu);
+      int s = 0, r = 0;
+      uint32_t sph = 0, rph = 0;
+      for (int it = 0; it < n_units; ++it) {
+        const bool ok1 = mbar_try_wait(kWfull + 8 * s, sph);
+        const bool ok2 = it < kRing || mbar_try_wait(kEfree + 8 * r, rph ^ 1);
+        if (!__all_sync(0xFFFFFFFFu, ok1 && ok2)) {
+          bool ok = mbar_wait_bounded(kWfull + 8 * s, sph, kSiteGemvFull);
+          if (it >= kRing) ok = ok && mbar_wait_bounded(kEfree + 8 * r, rph ^ 1, kSiteGemvEmpty);
+          if (!__all_sync(0xFFFFFFFFu, ok)) return;
+        }
+        const uint8_t* st = st0 + (size_t)s * L.stage;
+        uint4 ch[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) ch[i] = *reinterpret_cast<const uint4*>(st + (4 * part + i) * 2048 + rl * 16);
+        if (part == 0) {
+          // The row's d, dmin and 12 scale bytes for the epilogue.
+          const uint8_t* sc = st + kQ4kRecSc + rl * 12;
+          reinterpret_cast<uint4*>(aux0 + (size_t)r * L.aux + L.w)[rl] =
+              make_uint4(*reinterpret_cast<const uint32_t*>(st + kQ4kRecDm + rl * 4),
+                         *reinterpret_cast<const uint32_t*>(sc), *reinterpret_cast<const uint32_t*>(sc + 4),
+                         *reinterpret_cast<const uint32_t*>(sc + 8));
+        }
+        uint32_t v[32];  // local group g: columns 8g..8g+7, weights 4c..4c+3 in column c
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int g = 2 * (i >> 1), h = i & 1;  // byte group i/2: groups g (low) and g+1 (high)
+          const uint32_t w4[4] = {ch[i].x, ch[i].y, ch[i].z, ch[i].w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) q4k_e4m3(w4[k], v[g * 8 + 4 * h + k], v[(g + 1) * 8 + 4 * h + k]);
+        }
+        tc::st_cols<32>(tq + (uint32_t)(r * 64), v);
+        tc::wait_st();
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(kAfull + 8 * r);
+          mbar_arrive(kEmpty + 8 * s);
+        }
+        __syncwarp();
+        if (++s == S) {
+          s = 0;
+          sph ^= 1;
+        }
+        if (++r == kRing) {
+          r = 0;
+          rph ^= 1;
+        }
+      }
+      return;
+    } else {
     // Codebook: stage the 2 KB read at kernel entry, then expand to the
     // lane-private copy, four lanes' copies (16 contiguous bytes) per store.
     tm::build_table(table, tstage, tw, tid, nthreads);
@@ -758,6 +844,7 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
       }
     }
     return;
+    }  // the IQ3_S decoders
   }
 
   // ------------------------------------------------------------------ epilogue
@@ -838,6 +925,40 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
     int seg_begin = u0;
     // K block and row tile (within its linear) of unit `it`.
     int kb_next = (u0 - cur_unit0) % cur_nb, rt_next = (u0 - cur_unit0) / cur_nb;
+    // Q4_K: the activations' group sums of a unit, spread over the warp (lane
+    // l holds kSF of them: token l / (8 / kSF), groups (l % (8 / kSF)) * kSF
+    // on) and read with shuffles. The next unit's are loaded while this one
+    // is processed, so their latency stays off the epilogue's path.
+    constexpr int kSF = TOK / 4, kSLanes = 8 / kSF;
+    float sum_cur[kSF], sum_next[kSF];
+    auto load_sums = [&](int kb, float (&dst)[kSF]) {
+      if constexpr (kQ4K) {
+        const int t = lane / kSLanes;
+        if (t < p.m) {
+          const float* src = p.xsum + (size_t)t * p.ldsum + (size_t)kb * 8 + (lane % kSLanes) * kSF;
+          if constexpr (kSF == 2) {
+            const float2 v = __ldg(reinterpret_cast<const float2*>(src));
+            dst[0] = v.x;
+            dst[1] = v.y;
+          } else {
+#pragma unroll
+            for (int j = 0; j < kSF; j += 4) {
+              const float4 v = __ldg(reinterpret_cast<const float4*>(src + j));
+              dst[j] = v.x;
+              dst[j + 1] = v.y;
+              dst[j + 2] = v.z;
+              dst[j + 3] = v.w;
+            }
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < kSF; ++j) dst[j] = 0.f;
+        }
+      }
+    };
+    if constexpr (kQ4K) {
+      if (u0 < u1) load_sums(kb_next, sum_next);
+    }
     int r = 0;  // ring slot of unit `it` and its phase
     uint32_t rph = 0;
     auto next_slot = [&]() {
@@ -859,32 +980,72 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
       tc::fence_after_sync();
       const uint32_t tq = tq0 + (uint32_t)(db * 8 * NM);
       const uint8_t* aux = aux0 + (size_t)r * L.aux;
-      const uint2 dsc = reinterpret_cast<const uint2*>(aux + L.w)[rl];
-      const float dv = __half2float(__ushort_as_half((unsigned short)dsc.x));
-      const float dneg = -8388608.0f * dv;
-      // 2*nibble+1 of group g is byte g/2 of tb[g&1]; float(2^23 + t)*d - 2^23*d = t*d exactly.
-      const uint32_t tb0 = lop3_and_or(dsc.y << 1, 0x1E1E1E1Eu, 0x01010101u);
-      const uint32_t tb1 = lop3_and_or(dsc.y >> 3, 0x1E1E1E1Eu, 0x01010101u);
-      // Groups per batch of TMEM loads (one wait per batch), within the register budget.
-      constexpr int GB = kDecWarps == 8 ? (TOK <= 8 ? 8 : TOK <= 16 ? 4 : 2) : 2;
+      if constexpr (kQ4K) {
+        // Q4_K: out += P_g * d*s_g - dmin*m_g * (the token's sum of group g's activations).
 #pragma unroll
-      for (int t0 = 0; t0 < TOK; t0 += 8) {
+        for (int j = 0; j < kSF; ++j) sum_cur[j] = sum_next[j];
+        if (u + 1 < u1) load_sums(kb_step(kb_next), sum_next);
+        const uint4 a4 = reinterpret_cast<const uint4*>(aux + L.w)[rl];
+        const float dv = __half2float(__ushort_as_half((unsigned short)(a4.x & 0xFFFFu)));
+        const float dmv = __half2float(__ushort_as_half((unsigned short)(a4.x >> 16)));
+        const uint32_t b[3] = {a4.y, a4.z, a4.w};  // the 12 scale bytes
+        auto byte = [&](int i) -> uint32_t { return (b[i >> 2] >> (8 * (i & 3))) & 0xFFu; };
+        float wg[8], og[8];
 #pragma unroll
-        for (int g0 = 0; g0 < 8; g0 += GB) {
-          uint32_t off[GB];
+        for (int g = 0; g < 8; ++g) {
+          const uint32_t sg = g < 4 ? byte(g) & 63u : (byte(g + 4) & 15u) | ((byte(g - 4) >> 6) << 4);
+          const uint32_t mg = g < 4 ? byte(g + 4) & 63u : (byte(g + 4) >> 4) | ((byte(g) >> 6) << 4);
+          wg[g] = dv * (float)sg;
+          og[g] = dmv * (float)mg;
+        }
 #pragma unroll
-          for (int j = 0; j < GB; ++j) off[j] = (uint32_t)((g0 + j) * NM + t0);
-          float c[GB][8];
-          tc::ld_x8_multi<GB>(tq, off, c);
+        for (int t0 = 0; t0 < TOK; t0 += 8) {
+          uint32_t off[8];
 #pragma unroll
-          for (int j = 0; j < GB; ++j) {
-            const int g = g0 + j;
-            const float w = fmaf(__uint_as_float(prmt((g & 1) ? tb1 : tb0, 0x4B000000u, 0x7650u | (uint32_t)(g >> 1))),
-                                 dv, dneg);
+          for (int j = 0; j < 8; ++j) off[j] = (uint32_t)(j * NM + t0);
+          float c[8][8];
+          tc::ld_x8_multi<8>(tq, off, c);
 #pragma unroll
-            for (int t = 0; t < 8; t += 2) {
-              if (t0 + t < ov.m)  // tokens past M are padding (warp-uniform branch)
-                fma2(acc[t0 + t], acc[t0 + t + 1], c[j][t], c[j][t + 1], w, w);
+          for (int t = 0; t < 8; ++t) {
+            if (t0 + t < ov.m) {  // tokens past M are padding (warp-uniform branch)
+              float a = acc[t0 + t];
+#pragma unroll
+              for (int g = 0; g < 8; ++g) {
+                const float sv = __shfl_sync(0xFFFFFFFFu, sum_cur[g % kSF], (t0 + t) * kSLanes + g / kSF);
+                a = fmaf(-og[g], sv, fmaf(c[g][t], wg[g], a));
+              }
+              acc[t0 + t] = a;
+            }
+          }
+        }
+      } else {
+        const uint2 dsc = reinterpret_cast<const uint2*>(aux + L.w)[rl];
+        const float dv = __half2float(__ushort_as_half((unsigned short)dsc.x));
+        const float dneg = -8388608.0f * dv;
+        // 2*nibble+1 of group g is byte g/2 of tb[g&1]; float(2^23 + t)*d - 2^23*d = t*d exactly.
+        const uint32_t tb0 = lop3_and_or(dsc.y << 1, 0x1E1E1E1Eu, 0x01010101u);
+        const uint32_t tb1 = lop3_and_or(dsc.y >> 3, 0x1E1E1E1Eu, 0x01010101u);
+        // Groups per batch of TMEM loads (one wait per batch), within the register budget.
+        constexpr int GB = kDecWarps == 8 ? (TOK <= 8 ? 8 : TOK <= 16 ? 4 : 2) : 2;
+  #pragma unroll
+        for (int t0 = 0; t0 < TOK; t0 += 8) {
+  #pragma unroll
+          for (int g0 = 0; g0 < 8; g0 += GB) {
+            uint32_t off[GB];
+  #pragma unroll
+            for (int j = 0; j < GB; ++j) off[j] = (uint32_t)((g0 + j) * NM + t0);
+            float c[GB][8];
+            tc::ld_x8_multi<GB>(tq, off, c);
+  #pragma unroll
+            for (int j = 0; j < GB; ++j) {
+              const int g = g0 + j;
+              const float w = fmaf(__uint_as_float(prmt((g & 1) ? tb1 : tb0, 0x4B000000u, 0x7650u | (uint32_t)(g >> 1))),
+                                   dv, dneg);
+  #pragma unroll
+              for (int t = 0; t < 8; t += 2) {
+                if (t0 + t < ov.m)  // tokens past M are padding (warp-uniform branch)
+                  fma2(acc[t0 + t], acc[t0 + t + 1], c[j][t], c[j][t + 1], w, w);
+              }
             }
           }
         }
@@ -987,43 +1148,45 @@ uint32_t gemv_tm_smem_bytes(int nt, int stages, int kparts, bool fused) {
 }
 int gemv_tm_max_stages() { return kMaxStagesTm; }
 
-template <int NT, int kDecWarps, bool kQ = false>
+template <int NT, int kDecWarps, bool kQ = false, bool kQ4K = false>
 static const void* tm_kernel() {
-  return (const void*)iq3s_gemv_tm_kernel<NT, kDecWarps, GemvNoGroup, kQ>;
+  return (const void*)iq3s_gemv_tm_kernel<NT, kDecWarps, GemvNoGroup, kQ, kQ4K>;
 }
 template <int NT, int kDecWarps, bool kQ = false>
 static const void* tm_kernel_group() {
   return (const void*)iq3s_gemv_tm_kernel<NT, kDecWarps, GemvGroup, kQ>;
 }
 
-static int query_max_clusters(int nt, int dec_warps, int stages, int kparts);
+static int query_max_clusters(int nt, int dec_warps, int stages, int kparts, bool q4k);
 
-static const void* tm_kernel_for(int nt, int dec_warps) {
+static const void* tm_kernel_for(int nt, int dec_warps, bool q4k = false) {
+  if (q4k) return nt == 1 ? tm_kernel<1, 8, false, true>() : nt == 2 ? tm_kernel<2, 8, false, true>()
+                                                                    : tm_kernel<4, 8, false, true>();
   if (dec_warps == 16) return nt == 1 ? tm_kernel<1, 16>() : nt == 2 ? tm_kernel<2, 16>() : tm_kernel<4, 16>();
   return nt == 1 ? tm_kernel<1, 8>() : nt == 2 ? tm_kernel<2, 8>() : tm_kernel<4, 8>();
 }
 
-int gemv_tm_max_clusters(int nt, int dec_warps, int stages, int kparts) {
+int gemv_tm_max_clusters(int nt, int dec_warps, int stages, int kparts, bool q4k) {
   // Cached per (device, configuration): the query runs once.
   static std::mutex mu;
-  static std::map<std::tuple<int, int, int, int, int>, int> cache;
+  static std::map<std::tuple<int, int, int, int, int, bool>, int> cache;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 0;
-  const auto key = std::make_tuple(dev, nt, dec_warps, stages, kparts);
+  const auto key = std::make_tuple(dev, nt, dec_warps, stages, kparts, q4k);
   {
     std::lock_guard<std::mutex> lock(mu);
     auto it = cache.find(key);
     if (it != cache.end()) return it->second;
   }
-  const int n = query_max_clusters(nt, dec_warps, stages, kparts);
+  const int n = query_max_clusters(nt, dec_warps, stages, kparts, q4k);
   std::lock_guard<std::mutex> lock(mu);
   cache[key] = n;
   return n;
 }
 
-static int query_max_clusters(int nt, int dec_warps, int stages, int kparts) {
-  const void* kern = tm_kernel_for(nt, dec_warps);
-  const uint32_t smem = tm_smem_bytes(nt, stages, kparts);
+static int query_max_clusters(int nt, int dec_warps, int stages, int kparts, bool q4k) {
+  const void* kern = tm_kernel_for(nt, dec_warps, q4k);
+  const uint32_t smem = tm_smem_bytes(nt, stages, kparts, false, q4k);
   if (ensure_smem_attribute(kern, smem) != cudaSuccess) return 0;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(kparts * 16);
@@ -1045,9 +1208,11 @@ static int query_max_clusters(int nt, int dec_warps, int stages, int kparts) {
 }
 
 template <int NT, int kDecWarps>
-static cudaError_t launch_gemv_tm_t(const GemvTmParams& p, const GemvTmMaps& maps, int grid, cudaStream_t stream) {
-  const uint32_t smem = tm_smem_bytes(NT, p.stages, p.kparts, p.x_bf16 != nullptr);
-  const void* kern = p.q_out != nullptr ? tm_kernel<NT, kDecWarps, true>() : tm_kernel<NT, kDecWarps, false>();
+static cudaError_t launch_gemv_tm_t(const GemvTmParams& p, const GemvTmMaps& maps, int grid, cudaStream_t stream,
+                                    bool q4k = false) {
+  const uint32_t smem = tm_smem_bytes(NT, p.stages, p.kparts, p.x_bf16 != nullptr, q4k);
+  const void* kern = q4k ? tm_kernel<NT, 8, false, true>()
+                     : p.q_out != nullptr ? tm_kernel<NT, kDecWarps, true>() : tm_kernel<NT, kDecWarps, false>();
   cudaError_t e = ensure_smem_attribute(kern, smem);
   if (e != cudaSuccess) return e;
   const GemvNoGroup none{0};
@@ -1081,18 +1246,23 @@ cudaError_t launch_gemv_tm_group(const GemvTmParams& p, const GemvGroup& g, int 
 
 template <int NT>
 static cudaError_t launch_gemv_tm_n(const GemvTmParams& p, int dec_warps, const GemvTmMaps& maps, int grid,
-                                    cudaStream_t stream) {
+                                    cudaStream_t stream, bool q4k) {
+  if (q4k) return launch_gemv_tm_t<NT, 8>(p, maps, grid, stream, true);
   if (dec_warps == 16) return launch_gemv_tm_t<NT, 16>(p, maps, grid, stream);
   return launch_gemv_tm_t<NT, 8>(p, maps, grid, stream);
 }
 
 cudaError_t launch_gemv_tm(const GemvTmParams& p, int nt, int dec_warps, const GemvTmMaps& maps, int grid,
-                           cudaStream_t stream) {
+                           cudaStream_t stream, bool q4k) {
+  if (q4k && (dec_warps != 8 || p.x_bf16 != nullptr || p.q_out != nullptr || !p.packed || !p.xsum))
+    return cudaErrorInvalidValue;
   switch (nt) {
-    case 1: return launch_gemv_tm_n<1>(p, dec_warps, maps, grid, stream);
-    case 2: return launch_gemv_tm_n<2>(p, dec_warps, maps, grid, stream);
-    default: return launch_gemv_tm_n<4>(p, dec_warps, maps, grid, stream);
+    case 1: return launch_gemv_tm_n<1>(p, dec_warps, maps, grid, stream, q4k);
+    case 2: return launch_gemv_tm_n<2>(p, dec_warps, maps, grid, stream, q4k);
+    default: return launch_gemv_tm_n<4>(p, dec_warps, maps, grid, stream, q4k);
   }
 }
+
+uint32_t q4k_gemv_smem_bytes(int nt, int stages, int kparts) { return tm_smem_bytes(nt, stages, kparts, false, true); }
 
 }  // namespace mambo

@@ -51,6 +51,10 @@ struct QuantParams {
   int64_t ldq;
   uint8_t* s;
   int64_t lds;
+  // Optional: per 32-value group, the sum of its quantized values E4M3 * 2^e in
+  // FP32 ([m][k/32], row stride ld_sums), summed in a fixed order.
+  float* sums;
+  int64_t ld_sums;
 };
 cudaError_t launch_quantize_mxfp8(const QuantParams& p, int x_dtype, int rounding, int num_sms, cudaStream_t stream);
 
@@ -85,6 +89,21 @@ struct PackWeightParams {
   uint8_t* packed;
 };
 cudaError_t launch_iq3s_pack(const PackWeightParams& p, int num_sms, cudaStream_t stream);
+
+// Q4_K (GGUF, 144 bytes per 256 values: fp16 d, fp16 dmin, 12 bytes of 6-bit
+// scales and mins, 128 bytes of 4-bit codes) in tile-major records of
+// kQ4kRecordBytes per (128-row tile, K block): the codes chunk-major
+// [8 chunks][128 rows][16 bytes] (chunk c = code bytes 16c..16c+15), then
+// [128 rows][4 bytes] d and dmin, then [128 rows][12 bytes] scales and mins;
+// rows at or past N are zero.
+constexpr uint32_t kQ4kRecordBytes = 18432;
+constexpr uint32_t kQ4kRecDm = 16384, kQ4kRecSc = 16896;
+struct Q4kPackParams {
+  const uint8_t* raw;  // [N][B][144] with any byte strides
+  int64_t n_rows, n_blocks, stride_row, stride_block, stride_byte;
+  uint8_t* packed;
+};
+cudaError_t launch_q4k_pack(const Q4kPackParams& p, int num_sms, cudaStream_t stream);
 
 struct GemvParams {
   const uint8_t* xq;
@@ -157,6 +176,9 @@ struct GemvTmParams {
   int64_t ldq;
   uint8_t* s_out;
   int64_t lds;
+  // Q4_K launches: the activations' group sums [m][K/32] (row stride ldsum, 16-byte aligned rows).
+  const float* xsum;
+  int64_t ldsum;
 };
 
 struct GemvTmMaps {
@@ -211,13 +233,15 @@ bool make_gemv_x_map(const uint8_t* xq, int64_t ldxq, int m, int n_blocks, int b
 // Scale map for the tcgen05 GEMV; false unless xs is 16-byte aligned with a row stride that is a multiple of 16.
 bool make_gemv_xs_map(const uint8_t* xs, int64_t ldxs, int m, int n_blocks, int box_tokens, CUtensorMap* map);
 cudaError_t launch_gemv_tm(const GemvTmParams& p, int nt, int dec_warps, const GemvTmMaps& maps, int grid,
-                           cudaStream_t stream);
+                           cudaStream_t stream, bool q4k = false);
+// Shared memory of the Q4_K GEMV (no codebook, 18,432-byte records).
+uint32_t q4k_gemv_smem_bytes(int nt, int stages, int kparts);
 uint32_t gemv_tm_smem_bytes(int nt, int stages, int kparts, bool fused = false);
 // bf16 activation map for the GEMV's fused quantization; false unless x is
 // 16-byte aligned with a row stride (elements) that is a multiple of 8.
 bool make_gemv_xb_map(const uint16_t* x, int64_t ldx, int m, int64_t k, int box_tokens, CUtensorMap* map);
 // Clusters of `kparts` CTAs of this configuration that can be resident at once (0 if none / on error).
-int gemv_tm_max_clusters(int nt, int dec_warps, int stages, int kparts);
+int gemv_tm_max_clusters(int nt, int dec_warps, int stages, int kparts, bool q4k = false);
 int gemv_tm_max_stages();
 
 // tcgen05 GEMM for prefill-sized M (128 weight rows x 128 tokens per tile).

@@ -111,6 +111,50 @@ __global__ void iq3s_pack_kernel(const PackWeightParams p) {
   }
 }
 
+// One thread per 16-byte chunk of the Q4_K packed buffer (record layout in kernels.cuh).
+__global__ void q4k_pack_kernel(const Q4kPackParams p) {
+  constexpr int kChunks = (int)(kQ4kRecordBytes / 16);
+  const int64_t tiles = (p.n_rows + 127) / 128;
+  const int64_t total = tiles * p.n_blocks * kChunks;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t rec = i / kChunks;
+    const int off = (int)(i - rec * kChunks) * 16;
+    const int64_t t = rec / p.n_blocks, b = rec - t * p.n_blocks;
+    uint8_t out[16];
+    // Source byte of block (row, b) at in-block offset o.
+    auto src = [&](int64_t row, int o) -> uint8_t {
+      return row < p.n_rows ? __ldg(p.raw + row * p.stride_row + b * p.stride_block + (int64_t)o * p.stride_byte) : 0;
+    };
+    if (off < (int)kQ4kRecDm) {  // codes: 16 bytes of one row
+      const int c = off / 2048, r = (off % 2048) / 16;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) out[j] = src(t * 128 + r, 16 + 16 * c + j);
+    } else if (off < (int)kQ4kRecSc) {  // d, dmin: 4 rows x 4 bytes
+      const int r0 = (off - (int)kQ4kRecDm) / 4;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) out[j] = src(t * 128 + r0 + j / 4, j % 4);
+    } else {  // scales and mins: 12 bytes per row, rows back to back
+      const int o0 = off - (int)kQ4kRecSc;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) out[j] = src(t * 128 + (o0 + j) / 12, 4 + (o0 + j) % 12);
+    }
+    uint4 v;
+    v.x = out[0] | (out[1] << 8) | (out[2] << 16) | ((uint32_t)out[3] << 24);
+    v.y = out[4] | (out[5] << 8) | (out[6] << 16) | ((uint32_t)out[7] << 24);
+    v.z = out[8] | (out[9] << 8) | (out[10] << 16) | ((uint32_t)out[11] << 24);
+    v.w = out[12] | (out[13] << 8) | (out[14] << 16) | ((uint32_t)out[15] << 24);
+    reinterpret_cast<uint4*>(p.packed)[i] = v;
+  }
+}
+
+cudaError_t launch_q4k_pack(const Q4kPackParams& p, int num_sms, cudaStream_t stream) {
+  const int64_t chunks = (p.n_rows + 127) / 128 * p.n_blocks * (kQ4kRecordBytes / 16);
+  int64_t blocks = (chunks + 255) / 256;
+  if (blocks > (int64_t)num_sms * 16) blocks = (int64_t)num_sms * 16;
+  q4k_pack_kernel<<<(int)blocks, 256, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
 // The exponent of each row's largest block scale, floor(log2(max_b |d_b|))
 // over the finite d of the row (0 for a row without a finite non-zero d;
 // rows past N, up to whole 128-row tiles, also 0): the folded FP16 GEMM

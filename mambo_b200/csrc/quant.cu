@@ -110,6 +110,28 @@ __global__ void __launch_bounds__(256) quantize_mxfp8_kernel(const QuantParams p
       packed[h] = lo | (hi << 16);
     }
 
+    if (p.sums != nullptr) {
+      // The group's quantized values summed: E4M3 values are multiples of 2^-9
+      // below 2^9, so a sum of 32 of them needs at most 23 bits and is exact in
+      // FP32 in any order; times 2^e (exact). A NaN scale code gives NaN.
+      float sum = 0.f;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          uint32_t h2;
+          const uint16_t two = (uint16_t)(packed[h] >> (16 * j));
+          asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(two));
+          sum += __half2float(__ushort_as_half((unsigned short)(h2 & 0xFFFFu)));
+          sum += __half2float(__ushort_as_half((unsigned short)(h2 >> 16)));
+        }
+      }
+      sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 1);
+      sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 2);
+      if (active && quad_lane == 0)
+        p.sums[row * p.ld_sums + cg] = code == 0xFFu ? __uint_as_float(0x7FC00000u) : sum * e8m0_to_float(code);
+    }
+
     if (active) {
       uint8_t* dst = p.q + row * p.ldq + cg * 32 + quad_lane * 8;
       if constexpr (kVec) {

@@ -114,6 +114,19 @@ def dequantize_iq4_xs(raw: np.ndarray) -> np.ndarray:
     return (dl[:, :, None] * v).reshape(-1)
 
 
+def make_synthetic_q4_k(n_rows: int, k: int, seed: int, d_low: float = 1e-4, d_high: float = 1e-2) -> np.ndarray:
+    """uint8 [N, K/256, 144]: uniform random scale, min and code bytes with finite fp16 d and dmin of
+    either sign, |d|, |dmin| in [d_low, d_high) (test input, not a property of the format)."""
+    if k % BLOCK_VALUES:
+        raise ValueError("Q4_K K must be divisible by 256")
+    rng = np.random.default_rng(seed)
+    raw = rng.integers(0, 256, size=(n_rows, k // BLOCK_VALUES, Q4_K_BLOCK_BYTES), dtype=np.uint8)
+    for f in range(2):
+        v = rng.uniform(d_low, d_high, size=raw.shape[:2]) * rng.choice([-1.0, 1.0], size=raw.shape[:2])
+        raw[..., 2 * f:2 * f + 2] = v.astype("<f2").view(np.uint8).reshape(*raw.shape[:2], 2)
+    return raw
+
+
 def q4_k_linear_f64(x: np.ndarray, raw: np.ndarray) -> np.ndarray:
     """Direct reference: float64 ``x [M, K] @ W.T`` with the exact (float64) weights of raw [N, K/256, 144]."""
     n = raw.shape[0]
