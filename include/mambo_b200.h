@@ -322,16 +322,20 @@ MAMBO_API int mambo_iq3s_linear_noalloc(const uint8_t* xq, int64_t ldxq, const u
  * src/python/mambo/utils/gguf_manifest.py:30-42, and decodes it only through
  * gguf-py). A Q4_K block holds 256 weights in 144 bytes: fp16 d, fp16 dmin, 12
  * bytes of eight 6-bit scales s_g and mins m_g, 128 bytes of 4-bit codes q;
- * weight = d*s_g*q - dmin*m_g. The codes 0..15 are exact E4M3 operands of the
- * tensor cores; per 32-weight group g the FP32 epilogue adds d*s_g times the
- * group's partial product and subtracts dmin*m_g times the token's sum of the
+ * weight = d*s_g*q - dmin*m_g = (d*s_g/2)*(2q - 15) + (7.5*d*s_g - dmin*m_g).
+ * The odd integers 2q - 15 (-15..15) are exact E4M3 operands of the tensor
+ * cores; per 32-weight group g the FP32 epilogue adds d*s_g/2 times the
+ * group's partial product and the constant term times the token's sum of the
  * group's (quantized) activations.
  *
  * Packed layout: one record of MAMBO_Q4K_RECORD_BYTES per (128-row tile t,
  * K block b) at ((t * B) + b) * MAMBO_Q4K_RECORD_BYTES: codes [8 chunks][128
- * rows][16 B] (chunk c = code bytes 16c..16c+15 of the row's block), then
- * [128 rows][4 B] d and dmin, then [128 rows][12 B] scales and mins; rows at or
- * past N are zero. mambo_q4k_pack fills it from raw blocks [N, B, 144] with any
+ * rows][16 B], then [128 rows][4 B] d and dmin, then [128 rows][12 B] scales
+ * and mins; rows at or past N are zero. Chunk c holds code bytes 16c..16c+15
+ * of the row's block as four 32-bit words: the word of bytes b0..b3 carries
+ * their low nibbles in bits 0-15 and their high nibbles in bits 16-31 (value j
+ * of a half in bits 4j..4j+3), each re-coded as (q >= 8 ? q : 7 - q), the sign
+ * and magnitude index of 2q - 15. mambo_q4k_pack fills it from raw blocks [N, B, 144] with any
  * byte strides (any alignment); the packed buffer must be 16-byte aligned.
  */
 #define MAMBO_Q4K_BLOCK_BYTES 144

@@ -540,7 +540,8 @@ int launch_tc_chunk(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t 
     if (!make_gemv_xb_map(x_bf16, ldx, (int)mc, w->n_blocks * 256, box, &maps.xb))
       return fail(MAMBO_EINVAL, "bf16 activations need 16-byte aligned rows");
   } else {
-    const int st = gemv_activation_maps(xq, ldxq, xs, ldxs, mc, w->n_blocks, box, xcopy, xscopy, &maps, stream);
+    // TMA boxes of the chunk's own rows (mc <= box).
+    const int st = gemv_activation_maps(xq, ldxq, xs, ldxs, mc, w->n_blocks, (int)mc, xcopy, xscopy, &maps, stream);
     if (st != MAMBO_OK) return st;
   }
   GemvTmParams p{};
@@ -567,6 +568,7 @@ int launch_tc_chunk(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t 
   p.total_units = P.units;
   p.x_bf16 = x_bf16;
   p.ldx = ldx;
+  p.box_rows = x_bf16 ? 0 : (int)mc;
   if (qo && qo->q) {  // quantized output for the next linear, written by the epilogue
     p.q_out = qo->q;
     p.ldq = qo->ldq;
@@ -1383,18 +1385,20 @@ extern "C" int mambo_iq3s_linear_noalloc(const uint8_t* xq, int64_t ldxq, const 
 // for it). Stream-K over (128-row tile, K block) units, 32-token chunks.
 namespace {
 
-// The Q4_K GEMV configuration: tcgen05 GEMV, 8 decoder warps. Default as for
-// IQ3_S: the cluster K-split while every row tile gets its own CTAs,
-// stream-K beyond that; the deepest weight ring up to 8 stages that fits.
-int q4k_config(const MamboLinearConfig* cfg, int64_t mc, int64_t n, const DeviceInfo& info, MamboLinearConfig* c) {
+// The Q4_K GEMV configuration: tcgen05 GEMV, 8 decoder warps. Default (from
+// B200 measurements of the Llama-3-8B decode shapes with weights rotated past
+// the L2): 4 weight stages, no L2 prefetch; the cluster K-split for long K
+// (32 blocks or more) when every row tile gets at least two CTAs, stream-K
+// otherwise.
+int q4k_config(const MamboLinearConfig* cfg, int64_t mc, int64_t n, int64_t b, const DeviceInfo& info,
+               MamboLinearConfig* c) {
   MamboLinearConfig d{};
   d.kernel = MAMBO_KERNEL_GEMV;
   d.warps = 8;
   d.ctas_per_sm = 1;
-  d.split = (n + 127) / 128 <= info.sms ? 2 : 0;
-  d.prefetch = 4;
-  d.stages = 8;
-  while (d.stages > 2 && (int)q4k_gemv_smem_bytes(gemv_nt_for(mc), d.stages, 0) > info.max_smem_optin) --d.stages;
+  d.split = (b >= 32 && (n + 127) / 128 * 2 <= info.sms) ? 2 : 0;
+  d.prefetch = 0;
+  d.stages = 4;
   if (cfg && cfg->kernel != MAMBO_KERNEL_AUTO) {
     if (cfg->kernel != MAMBO_KERNEL_GEMV)
       return fail(MAMBO_EINVAL, "Q4_K runs on the tcgen05 GEMV (MAMBO_KERNEL_GEMV) only");
@@ -1430,7 +1434,7 @@ size_t q4k_plan_bytes(int64_t m, int64_t n_rows, int64_t n_blocks, const MamboLi
   }
   MamboLinearConfig c;
   const int64_t mc = m < 32 ? m : 32;
-  if (q4k_config(cfg, mc, n_rows, info, &c) != MAMBO_OK) return 0;
+  if (q4k_config(cfg, mc, n_rows, n_blocks, info, &c) != MAMBO_OK) return 0;
   return q4k_gemv_workspace(plan_gemv(mc, n_rows, n_blocks, c, info.sms, info.max_smem_optin, true));
 }
 
@@ -1457,7 +1461,7 @@ int q4k_linear_impl(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t 
   for (int64_t m0 = 0; m0 < m; m0 += m_chunk_max) {
     const int64_t mc = (m - m0) < m_chunk_max ? (m - m0) : m_chunk_max;
     MamboLinearConfig c;
-    st = q4k_config(cfg, mc, n_rows, info, &c);
+    st = q4k_config(cfg, mc, n_rows, n_blocks, info, &c);
     if (st != MAMBO_OK) return st;
     const GemvPlan P = plan_gemv(mc, n_rows, n_blocks, c, info.sms, info.max_smem_optin, true);
     if ((size_t)P.counter_slots * sizeof(int) > kGemvCounterBytes)
@@ -1469,7 +1473,7 @@ int q4k_linear_impl(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t 
     uint8_t* xcopy = (uint8_t*)workspace + P.counters_bytes + P.partial_bytes;
     GemvTmMaps maps;
     std::memset(&maps, 0, sizeof(maps));
-    st = gemv_activation_maps(xq + m0 * ldxq, ldxq, xs + m0 * ldxs, ldxs, mc, n_blocks, 8 * P.nt, xcopy,
+    st = gemv_activation_maps(xq + m0 * ldxq, ldxq, xs + m0 * ldxs, ldxs, mc, n_blocks, (int)mc, xcopy,
                               xcopy + P.xcopy_bytes, &maps, stream);
     if (st != MAMBO_OK) return st;
     GemvTmParams p{};
@@ -1489,6 +1493,7 @@ int q4k_linear_impl(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t 
     p.total_units = P.units;
     p.xsum = xsum + m0 * ldsum;
     p.ldsum = ldsum;
+    p.box_rows = (int)mc;
     cudaError_t e = launch_gemv_tm(p, P.nt, 8, maps, P.grid, stream, true);
     if (e != cudaSuccess) return cuda_fail(e, "q4k_gemv_tm");
   }

@@ -121,6 +121,13 @@ __host__ __device__ inline TmLayout tm_layout(int nt, bool q4k = false) {
   return L;
 }
 
+// The region after the epilogue ring: the IQ3_S decoders' codebook staging,
+// or for Q4_K the epilogue warps' copies of a unit's activation group sums
+// (4 warps x 8*nt tokens x 8 floats).
+__host__ __device__ constexpr uint32_t tm_stage_region(int nt, bool q4k) {
+  return q4k && 1024u * (uint32_t)nt > kTableStageBytes ? 1024u * (uint32_t)nt : kTableStageBytes;
+}
+
 // kparts > 1: rank 0 of each cluster also holds the other ranks' partials.
 __host__ __device__ inline uint32_t tm_smem_bytes(int nt, int stages, int kparts, bool fused = false,
                                                   bool q4k = false) {
@@ -128,7 +135,7 @@ __host__ __device__ inline uint32_t tm_smem_bytes(int nt, int stages, int kparts
   const uint32_t cpart = kparts > 1 ? (uint32_t)(kparts - 1) * kRows * 8u * nt * 4u : 0u;
   const uint32_t bf = fused ? 128u + (uint32_t)tm_bstages(nt) * tm_box_tokens(nt) * kBfRowBytes : 0u;
   return (q4k ? 0u : kTableBytes) + 1024 + align_up_tm(stages * L.stage, 1024) + tm_xstages(nt) * L.xslot +
-         kRing * L.aux + kTableStageBytes + kBarBytes + cpart + bf;
+         kRing * L.aux + tm_stage_region(nt, q4k) + kBarBytes + cpart + bf;
 }
 
 __device__ __forceinline__ int unit_begin_tm(int cta, int grid, int units) {
@@ -198,22 +205,19 @@ __device__ __forceinline__ void store_out_tm(const OutView& o, const QuantView& 
   }
 }
 
-// Q4_K code word -> E4M3: byte j of w holds code lo_j (low nibble, one
-// 32-value group) and hi_j (high nibble, the next group). lo gets
-// E4M3(lo_0..lo_3), hi gets E4M3(hi_0..hi_3). The codes 0..15 are exact in
-// E4M3: two 8-entry byte lookups (prmt) for 0-7 and 8-15, and a prmt in
-// sign-replicate mode (selector bit 3 = code bit 3, source bytes 0x80) for the
-// byte mask that picks between them.
+// Q4_K: eight stored codes of one 32-bit word (bits 0-15: four values of one
+// group, bits 16-31: four of the next; each (v > 0) << 3 | (|v| - 1) / 2 for
+// the odd integer v = 2q - 15) -> the E4M3 bytes of v, four per output word.
+// The magnitude comes from an 8-byte table (prmt on the low three bits); a
+// selector nibble with bit 3 set picks the replicated sign of a 0x01 byte
+// (0x00), a clear one the byte itself (0x01), which times 128 is the sign bit.
 __device__ __forceinline__ void q4k_e4m3(uint32_t w, uint32_t& lo, uint32_t& hi) {
-  constexpr uint32_t kLut0 = 0x44403800u, kLut1 = 0x4E4C4A48u;  // E4M3 of 0..7
-  constexpr uint32_t kLut2 = 0x53525150u, kLut3 = 0x57565554u;  // E4M3 of 8..15
-  const uint32_t sel = w & 0x77777777u, selh = sel >> 16, wh = w >> 16;
-  const uint32_t a0 = prmt(kLut0, kLut1, sel), b0 = prmt(kLut2, kLut3, sel), m0 = prmt(0x80808080u, 0x80808080u, w);
-  const uint32_t a1 = prmt(kLut0, kLut1, selh), b1 = prmt(kLut2, kLut3, selh), m1 = prmt(0x80808080u, 0x80808080u, wh);
-  const uint32_t r0 = (a0 & ~m0) | (b0 & m0);  // [lo0, hi0, lo1, hi1]
-  const uint32_t r1 = (a1 & ~m1) | (b1 & m1);  // [lo2, hi2, lo3, hi3]
-  lo = prmt(r0, r1, 0x6420u);
-  hi = prmt(r0, r1, 0x7531u);
+  constexpr uint32_t kOdd0 = 0x4E4A4438u, kOdd1 = 0x57555351u;  // E4M3 of 1, 3, 5, ..., 15
+  const uint32_t sel = w & 0x77777777u, wh = w >> 16;
+  const uint32_t a0 = prmt(kOdd0, kOdd1, sel), a1 = prmt(kOdd0, kOdd1, sel >> 16);
+  const uint32_t n0 = prmt(0x01010101u, 0x01010101u, w), n1 = prmt(0x01010101u, 0x01010101u, wh);
+  lo = n0 * 128u + a0;
+  hi = n1 * 128u + a1;
 }
 
 // The item of a grouped launch that holds unit u, searching upwards from item l.
@@ -283,8 +287,9 @@ __device__ __forceinline__ void sum_partials(const float* partials, BeginOf begi
 // kQ: the launch also writes its output's MXFP8 quantization (QuantView);
 // launches without it run a kernel that has none of that code.
 // kQ4K: Q4_K weights (q4k records; prequantized activations with their group
-// sums, p.xsum): the decoders turn 4-bit codes into E4M3 and the epilogue
-// applies d*s_g and subtracts dmin*m_g times the activation group sum.
+// sums, p.xsum): the decoders turn the stored codes into E4M3 operands 2q - 15
+// and the epilogue applies d*s_g/2 and the group's constant term
+// (7.5*d*s_g - dmin*m_g) times the activation group sum.
 template <int NT, int kDecWarps, class G, bool kQ, bool kQ4K = false>
 __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
     iq3s_gemv_tm_kernel(const __grid_constant__ GemvTmParams p, const __grid_constant__ GemvTmMaps maps,
@@ -298,11 +303,17 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
   constexpr uint32_t kCols = tm_tmem_cols(NT);
   constexpr int kParts = kDecWarps / 4;  // decoder threads per weight row
   constexpr int kGroups = 8 / kParts;    // 32-weight groups per decoder thread and unit
-  constexpr uint32_t kBytesX = BOX * 256u + BOX * 16u;
-  // B tile [16-byte K chunk][BOX tokens][16 bytes]: K-direction core-matrix
-  // stride BOX*16, token-group stride 128. With 8 tokens the MMA's rows 8-15
-  // repeat rows 0-7 (stride 0) and their results are never read.
-  constexpr uint32_t kLbo = BOX * 16u;
+  // B tile [16-byte K chunk][R tokens][16 bytes]: K-direction core-matrix
+  // stride R*16, token-group stride 128. R = BOX when the kernel quantizes the
+  // activations itself; with TMA loads R = the box rows (the launch's tokens),
+  // so that no box holds out-of-bounds rows (TMA zero-fills them one 16-byte
+  // line at a time, which made a one-token launch slower than an eight-token
+  // one). A core matrix's rows past R read the next chunk's rows: they feed
+  // only D columns of tokens past M, which are never read. With 8 tokens the
+  // MMA's rows 8-15 repeat rows 0-7 (stride 0) and their results are never read.
+  const uint32_t xrows = (!kGroup && p.x_bf16 == nullptr && p.box_rows > 0) ? (uint32_t)p.box_rows : (uint32_t)BOX;
+  const uint32_t kBytesX = xrows * 256u + xrows * 16u;
+  const uint32_t kLbo = xrows * 16u;
   constexpr uint32_t kSbo = NT == 1 ? 0u : 128u;
   constexpr int kEpiWarp0 = 2 + kDecWarps, kXWarp0 = kEpiWarp0 + kEpiWarps;
   constexpr int AS = tm_xstages(NT);
@@ -322,8 +333,9 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
   uint8_t* x0 = st0 + align_up_tm((uint32_t)p.stages * L.stage, 1024);  // activation slots
   uint8_t* aux0 = x0 + (size_t)AS * L.xslot;
   uint32_t* tstage = reinterpret_cast<uint32_t*>(aux0 + kRing * L.aux);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(aux0 + kRing * L.aux + kTableStageBytes);
-  float* cpart = reinterpret_cast<float*>(aux0 + kRing * L.aux + kTableStageBytes + kBarBytes);  // cluster partials
+  constexpr uint32_t kStageRegion = tm_stage_region(NT, kQ4K);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(aux0 + kRing * L.aux + kStageRegion);
+  float* cpart = reinterpret_cast<float*>(aux0 + kRing * L.aux + kStageRegion + kBarBytes);  // cluster partials
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kMaxStagesTm + 2 * kMaxXStages + 2 * kRing + 5);
   const uint32_t bar0 = smem_u32(bars);
   // Barriers: per weight stage wfull (landed) and empty (decoded); per
@@ -981,10 +993,20 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
       const uint32_t tq = tq0 + (uint32_t)(db * 8 * NM);
       const uint8_t* aux = aux0 + (size_t)r * L.aux;
       if constexpr (kQ4K) {
-        // Q4_K: out += P_g * d*s_g - dmin*m_g * (the token's sum of group g's activations).
+        // Q4_K: out += P_g * d*s_g/2 - (dmin*m_g - 7.5*d*s_g) * (the token's sum of group g's activations),
+        // P_g the group's product with the odd integers 2q - 15.
 #pragma unroll
         for (int j = 0; j < kSF; ++j) sum_cur[j] = sum_next[j];
         if (u + 1 < u1) load_sums(kb_step(kb_next), sum_next);
+        // This unit's sums into the warp's copy [TOK][8] (lane l holds entries l*kSF..), read back as
+        // broadcasts.
+        float* scr = reinterpret_cast<float*>(tstage) + (warp - kEpiWarp0) * TOK * 8;
+        __syncwarp();  // every lane has read the previous unit's copy
+#pragma unroll
+        for (int j = 0; j < kSF; j += 2)
+          *reinterpret_cast<float2*>(scr + lane * kSF + j) = make_float2(sum_cur[j], sum_cur[j + 1]);
+        __syncwarp();
+        const float4* scr4 = reinterpret_cast<const float4*>(scr);
         const uint4 a4 = reinterpret_cast<const uint4*>(aux + L.w)[rl];
         const float dv = __half2float(__ushort_as_half((unsigned short)(a4.x & 0xFFFFu)));
         const float dmv = __half2float(__ushort_as_half((unsigned short)(a4.x >> 16)));
@@ -995,26 +1017,55 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
         for (int g = 0; g < 8; ++g) {
           const uint32_t sg = g < 4 ? byte(g) & 63u : (byte(g + 4) & 15u) | ((byte(g - 4) >> 6) << 4);
           const uint32_t mg = g < 4 ? byte(g + 4) & 63u : (byte(g + 4) >> 4) | ((byte(g) >> 6) << 4);
-          wg[g] = dv * (float)sg;
-          og[g] = dmv * (float)mg;
+          // The MMA summed v = 2q - 15: d*s*q - dmin*m = (d*s/2)*v + (7.5*d*s - dmin*m).
+          wg[g] = 0.5f * dv * (float)sg;
+          og[g] = dmv * (float)mg - 7.5f * dv * (float)sg;
         }
+        // One token's group sums from the warp's copy.
+        auto sums_of = [&](int t, float (&sv)[8]) {
+          const float4 lo = scr4[2 * t], hi = scr4[2 * t + 1];
+          sv[0] = lo.x; sv[1] = lo.y; sv[2] = lo.z; sv[3] = lo.w;
+          sv[4] = hi.x; sv[5] = hi.y; sv[6] = hi.z; sv[7] = hi.w;
+        };
 #pragma unroll
         for (int t0 = 0; t0 < TOK; t0 += 8) {
+          if (t0 >= ov.m) break;  // warp-uniform
           uint32_t off[8];
 #pragma unroll
           for (int j = 0; j < 8; ++j) off[j] = (uint32_t)(j * NM + t0);
           float c[8][8];
           tc::ld_x8_multi<8>(tq, off, c);
+          if (t0 + 8 <= ov.m) {
+            // Eight tokens: two token pairs' sums at a time, the scale and the constant term in separate
+            // paired accumulators (independent FMA chains).
 #pragma unroll
-          for (int t = 0; t < 8; ++t) {
-            if (t0 + t < ov.m) {  // tokens past M are padding (warp-uniform branch)
-              float a = acc[t0 + t];
+            for (int t = 0; t < 8; t += 2) {
+              float sa[8], sb[8];
+              sums_of(t0 + t, sa);
+              sums_of(t0 + t + 1, sb);
+              float pa = 0.f, pb = 0.f, qa = 0.f, qb = 0.f;
 #pragma unroll
               for (int g = 0; g < 8; ++g) {
-                const float sv = __shfl_sync(0xFFFFFFFFu, sum_cur[g % kSF], (t0 + t) * kSLanes + g / kSF);
-                a = fmaf(-og[g], sv, fmaf(c[g][t], wg[g], a));
+                fma2(pa, pb, c[g][t], c[g][t + 1], wg[g], wg[g]);
+                fma2(qa, qb, sa[g], sb[g], og[g], og[g]);
               }
-              acc[t0 + t] = a;
+              acc[t0 + t] += pa - qa;
+              acc[t0 + t + 1] += pb - qb;
+            }
+          } else {
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+              if (t0 + t < ov.m) {  // tokens past M are padding (warp-uniform branch)
+                float sv[8];
+                sums_of(t0 + t, sv);
+                float pa = 0.f, qa = 0.f;
+#pragma unroll
+                for (int g = 0; g < 8; ++g) {
+                  pa = fmaf(c[g][t], wg[g], pa);
+                  qa = fmaf(sv[g], og[g], qa);
+                }
+                acc[t0 + t] += pa - qa;
+              }
             }
           }
         }

@@ -91,11 +91,14 @@ struct PackWeightParams {
 cudaError_t launch_iq3s_pack(const PackWeightParams& p, int num_sms, cudaStream_t stream);
 
 // Q4_K (GGUF, 144 bytes per 256 values: fp16 d, fp16 dmin, 12 bytes of 6-bit
-// scales and mins, 128 bytes of 4-bit codes) in tile-major records of
+// scales and mins, 128 bytes of 4-bit codes q) in tile-major records of
 // kQ4kRecordBytes per (128-row tile, K block): the codes chunk-major
-// [8 chunks][128 rows][16 bytes] (chunk c = code bytes 16c..16c+15), then
-// [128 rows][4 bytes] d and dmin, then [128 rows][12 bytes] scales and mins;
-// rows at or past N are zero.
+// [8 chunks][128 rows][16 bytes], then [128 rows][4 bytes] d and dmin, then
+// [128 rows][12 bytes] scales and mins; rows at or past N are zero. Chunk c
+// holds code bytes 16c..16c+15 as four 32-bit words; the word of bytes
+// b0..b3 carries their low nibbles (group 2(c/2)) in bits 0-15 and their high
+// nibbles (group 2(c/2)+1) in bits 16-31, value j of a half in bits 4j..4j+3,
+// each re-coded as the odd integer v = 2q - 15: (v > 0) << 3 | (|v| - 1) / 2.
 constexpr uint32_t kQ4kRecordBytes = 18432;
 constexpr uint32_t kQ4kRecDm = 16384, kQ4kRecSc = 16896;
 struct Q4kPackParams {
@@ -165,6 +168,9 @@ struct GemvTmParams {
   int kparts;    // > 0: row tile t is split into kparts K ranges, CTA t*kparts+k in a cluster of kparts; 0: stream-K
   int row_tiles;
   int total_units;
+  // Tokens per activation TMA box (the maps' box rows; 1..8*NT, 0 = 8*NT):
+  // boxes of the launch's own rows only, no out-of-bounds rows to fill.
+  int box_rows;
   // Fused activation quantization: bf16 activations [m][ldx] (16-byte aligned
   // rows) quantized to MXFP8 in the kernel instead of read as xq/xs; null: TMA.
   const uint16_t* x_bf16;

@@ -111,6 +111,10 @@ __global__ void iq3s_pack_kernel(const PackWeightParams p) {
   }
 }
 
+// The stored 4-bit code of Q4_K value q (0..15): the odd integer v = 2q - 15
+// as (v > 0) << 3 | (|v| - 1) / 2, which is q for q >= 8 and 7 - q below.
+__device__ __forceinline__ uint32_t q4k_stored_code(uint32_t q) { return q >= 8u ? q : 7u - q; }
+
 // One thread per 16-byte chunk of the Q4_K packed buffer (record layout in kernels.cuh).
 __global__ void q4k_pack_kernel(const Q4kPackParams p) {
   constexpr int kChunks = (int)(kQ4kRecordBytes / 16);
@@ -125,10 +129,21 @@ __global__ void q4k_pack_kernel(const Q4kPackParams p) {
     auto src = [&](int64_t row, int o) -> uint8_t {
       return row < p.n_rows ? __ldg(p.raw + row * p.stride_row + b * p.stride_block + (int64_t)o * p.stride_byte) : 0;
     };
-    if (off < (int)kQ4kRecDm) {  // codes: 16 bytes of one row
+    if (off < (int)kQ4kRecDm) {  // codes: 16 bytes of one row, re-coded and regrouped per 32-bit word
       const int c = off / 2048, r = (off % 2048) / 16;
 #pragma unroll
-      for (int j = 0; j < 16; ++j) out[j] = src(t * 128 + r, 16 + 16 * c + j);
+      for (int w = 0; w < 4; ++w) {
+        uint32_t lo = 0, hi = 0;  // the four low nibbles (group 2c'), the four high ones (group 2c'+1)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t byte = src(t * 128 + r, 16 + 16 * c + 4 * w + j);
+          lo |= q4k_stored_code(byte & 15u) << (4 * j);
+          hi |= q4k_stored_code(byte >> 4) << (4 * j);
+        }
+        const uint32_t word = lo | (hi << 16);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) out[4 * w + j] = (uint8_t)(word >> (8 * j));
+      }
     } else if (off < (int)kQ4kRecSc) {  // d, dmin: 4 rows x 4 bytes
       const int r0 = (off - (int)kQ4kRecDm) / 4;
 #pragma unroll

@@ -8,11 +8,12 @@ device, activations quantized to MXFP8, one linear launch.
 
 Block layout (144 bytes per 256 weights): fp16 d, fp16 dmin, 12 bytes of eight
 6-bit scales s_g and mins m_g, 128 bytes of 4-bit codes q; weight =
-d*s_g*q - dmin*m_g for the 32-weight group g. The codes 0..15 are exact E4M3
-operands, so the tensor cores form each group's partial product P_g of the
-codes and the MXFP8 activations exactly as for IQ3_S; the FP32 epilogue adds
-d*s_g*P_g and subtracts dmin*m_g times the token's sum of the group's
-quantized activations, which the quantizer writes beside its codes.
+d*s_g*q - dmin*m_g = (d*s_g/2)*(2q - 15) + (7.5*d*s_g - dmin*m_g) for the
+32-weight group g. The odd integers 2q - 15 are exact E4M3 operands (the
+packed copy stores them in sign/magnitude form), so the tensor cores form each
+group's partial product P_g with the MXFP8 activations as for IQ3_S; the FP32
+epilogue adds (d*s_g/2)*P_g and the constant term times the token's sum of the
+group's quantized activations, which the quantizer writes beside its codes.
 """
 
 from __future__ import annotations

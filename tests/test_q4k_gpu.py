@@ -35,8 +35,20 @@ def _x(dev, m, k, seed):
     return torch.from_numpy(x).to(dev).to(torch.bfloat16)
 
 
+def _stored_codes(codes: np.ndarray) -> np.ndarray:
+    """Code bytes [..., 128] -> the packed words' bytes: per 4 bytes, their low nibbles in the word's
+    low half and their high nibbles in its high half, each q stored as 2q - 15 in sign/magnitude form
+    ((v > 0) << 3 | (|v| - 1) / 2, i.e. q for q >= 8 and 7 - q below)."""
+    c = codes.astype(np.uint32).reshape(*codes.shape[:-1], 32, 4)
+    lo, hi = c & 15, c >> 4
+    lo, hi = np.where(lo >= 8, lo, 7 - lo), np.where(hi >= 8, hi, 7 - hi)
+    shift = np.arange(4, dtype=np.uint32) * 4
+    word = (lo << shift).sum(axis=-1) | ((hi << shift).sum(axis=-1) << 16)
+    return word.astype("<u4").view(np.uint8).reshape(codes.shape)
+
+
 def _packed_layout(raw: np.ndarray) -> np.ndarray:
-    """The documented record layout, restated in NumPy: per (128-row tile, K block) the codes
+    """The documented record layout, restated in NumPy: per (128-row tile, K block) the stored codes
     [8 chunks][128 rows][16 B], then [128 rows] d|dmin (4 B), then [128 rows] 12 scale bytes."""
     n, b, _ = raw.shape
     tiles = (n + 127) // 128
@@ -47,7 +59,7 @@ def _packed_layout(raw: np.ndarray) -> np.ndarray:
         rows = pad[t * 128:(t + 1) * 128]
         for kb in range(b):
             blk = rows[:, kb]
-            codes = blk[:, 16:144].reshape(128, 8, 16).transpose(1, 0, 2).reshape(-1)
+            codes = _stored_codes(blk[:, 16:144]).reshape(128, 8, 16).transpose(1, 0, 2).reshape(-1)
             out += [codes, blk[:, 0:4].reshape(-1), blk[:, 4:16].reshape(-1)]
     return np.concatenate(out)
 
