@@ -400,6 +400,42 @@ MAMBO_API int mambo_set_wait_limit_ns(unsigned long long ns);
  * after limit_ns; afterwards mambo_device_status reports MAMBO_ETIMEOUT. */
 MAMBO_API int mambo_selftest_wait_timeout(unsigned long long limit_ns, mambo_stream_t stream);
 
+/*
+ * Tensor-parallel row split with its all-reduce in the same launch (no
+ * counterpart in the reference, which runs every linear on one GPU). Each of
+ * `world` ranks (one process per GPU, up to 8) holds a K slice of the weight;
+ * the GEMV that multiplies it writes each row tile's partial straight into
+ * every rank's exchange buffer over NVLink (plain peer stores, no multicast),
+ * raises a flag there, waits (bounded, MAMBO_ETIMEOUT) for every rank's
+ * partial of the same rows and sums them in rank order: every rank gets the
+ * identical [m, N] result, with no separate collective launch. This replaces
+ * the GEMV + NCCL all-reduce pair of a row split (the O and down projections
+ * of a tensor-parallel layer) at decode sizes.
+ *
+ * mambo_ar_comm_create allocates this rank's exchange buffer on the current
+ * device (slots for up to max_rows output rows, a multiple of 128, and 32
+ * tokens; about 256 * world * max_rows bytes) and writes its CUDA IPC handle
+ * (MAMBO_AR_HANDLE_BYTES bytes) to ipc_handle. The caller exchanges the
+ * handles between the ranks (e.g. an all-gather over its process group) and
+ * passes all of them, in rank order, to mambo_ar_comm_connect. Every rank
+ * must then make the same sequence of mambo_iq3s_linear_fused_ar calls on a
+ * communicator (same M, N and configuration): each call's epoch pairs it with
+ * the peers' matching call. Calls on one communicator must not overlap on the
+ * GPU (issue them on one stream).
+ */
+typedef struct MamboArComm MamboArComm;
+#define MAMBO_AR_HANDLE_BYTES 64
+MAMBO_API int mambo_ar_comm_create(int world, int rank, int64_t max_rows, MamboArComm** comm, void* ipc_handle);
+MAMBO_API int mambo_ar_comm_connect(MamboArComm* comm, const void* ipc_handles);
+MAMBO_API int mambo_ar_comm_destroy(MamboArComm* comm);
+/* This rank's slice: x [m, K/world] (bf16, 16-byte aligned rows, m < 32) times
+ * its weight shard w [N, K/world] -> out [m, N] (f32 or bf16), the sum over
+ * all ranks. workspace: mambo_iq3s_linear_fused_workspace_bytes() bytes. */
+MAMBO_API int mambo_iq3s_linear_fused_ar(const void* x, int x_dtype, int64_t ldx, int64_t m, const MamboIQ3SWeight* w,
+                                         const uint32_t* fp8_table, void* out, int out_dtype, int64_t ldo,
+                                         MamboArComm* comm, const MamboLinearConfig* cfg, void* workspace,
+                                         size_t workspace_bytes, mambo_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

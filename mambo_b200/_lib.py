@@ -68,7 +68,13 @@ EXPORTED_SYMBOLS = (
     "mambo_q4k_linear",
     "mambo_q4k_linear_fused_workspace_bytes",
     "mambo_q4k_linear_fused",
+    "mambo_ar_comm_create",
+    "mambo_ar_comm_connect",
+    "mambo_ar_comm_destroy",
+    "mambo_iq3s_linear_fused_ar",
 )
+
+MAMBO_AR_HANDLE_BYTES = 64
 
 
 class MamboIQ3SWeight(ctypes.Structure):
@@ -231,6 +237,14 @@ def load() -> ctypes.CDLL:
             "mambo_q4k_linear_fused": (
                 [vp, i32, i64, i64, vp, i64, i64, vp, i32, i64, ctypes.POINTER(MamboLinearConfig), vp,
                  ctypes.c_size_t, vp],
+                i32,
+            ),
+            "mambo_ar_comm_create": ([i32, i32, i64, ctypes.POINTER(vp), vp], i32),
+            "mambo_ar_comm_connect": ([vp, vp], i32),
+            "mambo_ar_comm_destroy": ([vp], i32),
+            "mambo_iq3s_linear_fused_ar": (
+                [vp, i32, i64, i64, ctypes.POINTER(MamboIQ3SWeight), vp, vp, i32, i64, vp,
+                 ctypes.POINTER(MamboLinearConfig), vp, ctypes.c_size_t, vp],
                 i32,
             ),
         }

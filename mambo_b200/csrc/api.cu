@@ -4,6 +4,7 @@
 #include <cstring>
 #include <map>
 #include <mutex>
+#include <new>
 #include <string>
 
 #include "kernels.cuh"
@@ -1586,3 +1587,181 @@ int mambo_q4k_linear_fused(const void* x, int x_dtype, int64_t ldx, int64_t m, c
 
 }  // extern "C"
 static_assert(MAMBO_Q4K_RECORD_BYTES == kQ4kRecordBytes, "Q4_K record size of the C ABI and of the kernel");
+
+// --------------------------------------------------------------------------
+// Row split with the all-reduce fused into the GEMV (mambo_iq3s_linear_fused_ar)
+// --------------------------------------------------------------------------
+static_assert(MAMBO_AR_HANDLE_BYTES == sizeof(cudaIpcMemHandle_t), "IPC handle size of the C ABI and of CUDA");
+
+struct MamboArComm {
+  int world, rank, device, max_rows;
+  uint8_t* local;  // this rank's exchange buffer (cudaMalloc, exported by IPC)
+  size_t bytes;
+  GemvAr ar;       // every rank's buffer as mapped here
+  bool connected;
+};
+
+namespace {
+
+size_t ar_buffer_bytes(int world, int max_rows) {
+  return gemv_ar_slot_bytes(world, max_rows) + gemv_ar_flag_bytes(world, max_rows) + 256;
+}
+
+}  // namespace
+
+extern "C" {
+
+int mambo_ar_comm_create(int world, int rank, int64_t max_rows, MamboArComm** comm, void* ipc_handle) {
+  if (!comm || !ipc_handle) return fail(MAMBO_EINVAL, "null pointer");
+  *comm = nullptr;
+  if (world < 1 || world > kGemvArMaxRanks) return fail(MAMBO_EINVAL, "world must be 1..%d", kGemvArMaxRanks);
+  if (rank < 0 || rank >= world) return fail(MAMBO_EINVAL, "rank must be in [0, world)");
+  if (max_rows < 128 || max_rows % 128 || max_rows > (1 << 20))
+    return fail(MAMBO_EINVAL, "max_rows must be a positive multiple of 128 up to 2^20");
+  DeviceInfo info;
+  int st = require_sm100(&info);
+  if (st != MAMBO_OK) return st;
+  MamboArComm* c = new (std::nothrow) MamboArComm{};
+  if (!c) return fail(MAMBO_EINVAL, "out of host memory");
+  c->world = world;
+  c->rank = rank;
+  c->max_rows = (int)max_rows;
+  cudaGetDevice(&c->device);
+  c->bytes = ar_buffer_bytes(world, (int)max_rows);
+  cudaError_t e = cudaMalloc((void**)&c->local, c->bytes);
+  if (e != cudaSuccess) {
+    delete c;
+    return cuda_fail(e, "cudaMalloc(exchange buffer)");
+  }
+  // Flags and epoch start at zero; every launch then tags its flags with epoch + 1.
+  e = cudaMemset(c->local, 0, c->bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle((cudaIpcMemHandle_t*)ipc_handle, c->local);
+  if (e != cudaSuccess) {
+    cudaFree(c->local);
+    delete c;
+    return cuda_fail(e, "exchange buffer set-up");
+  }
+  c->ar.world = world;
+  c->ar.rank = rank;
+  c->ar.max_rows = (int)max_rows;
+  c->ar.flags_offset = (uint32_t)gemv_ar_slot_bytes(world, (int)max_rows);
+  c->ar.ctl_offset = c->ar.flags_offset + (uint32_t)gemv_ar_flag_bytes(world, (int)max_rows);
+  c->ar.base[rank] = c->local;
+  *comm = c;
+  return ok();
+}
+
+int mambo_ar_comm_connect(MamboArComm* c, const void* ipc_handles) {
+  if (!c || !ipc_handles) return fail(MAMBO_EINVAL, "null pointer");
+  if (c->connected) return fail(MAMBO_EINVAL, "communicator already connected");
+  int dev = -1;
+  cudaGetDevice(&dev);
+  if (dev != c->device) return fail(MAMBO_EINVAL, "connect on the device the communicator was created on");
+  const cudaIpcMemHandle_t* h = (const cudaIpcMemHandle_t*)ipc_handles;
+  for (int j = 0; j < c->world; ++j) {
+    if (j == c->rank) continue;
+    void* p = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&p, h[j], cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      for (int i = 0; i < j; ++i)
+        if (i != c->rank && c->ar.base[i]) cudaIpcCloseMemHandle(c->ar.base[i]);
+      return cuda_fail(e, "cudaIpcOpenMemHandle(peer exchange buffer)");
+    }
+    c->ar.base[j] = (uint8_t*)p;
+  }
+  c->connected = true;
+  return ok();
+}
+
+int mambo_ar_comm_destroy(MamboArComm* c) {
+  if (!c) return ok();
+  if (c->connected)
+    for (int j = 0; j < c->world; ++j)
+      if (j != c->rank && c->ar.base[j]) cudaIpcCloseMemHandle(c->ar.base[j]);
+  if (c->local) cudaFree(c->local);
+  delete c;
+  return ok();
+}
+
+int mambo_iq3s_linear_fused_ar(const void* x, int x_dtype, int64_t ldx, int64_t m, const MamboIQ3SWeight* w,
+                               const uint32_t* fp8_table, void* out, int out_dtype, int64_t ldo, MamboArComm* comm,
+                               const MamboLinearConfig* cfg, void* workspace, size_t workspace_bytes,
+                               mambo_stream_t stream) {
+  if (!x || !w || !fp8_table || !out || !comm) return fail(MAMBO_EINVAL, "null pointer");
+  if (!comm->connected) return fail(MAMBO_EINVAL, "communicator not connected");
+  if (!w->d || !w->qs || !w->qh || !w->signs || !w->scales || !w->packed)
+    return fail(MAMBO_EINVAL, "the fused all-reduce needs the packed weight copy");
+  if (x_dtype != MAMBO_BF16) return fail(MAMBO_EINVAL, "the fused all-reduce takes bf16 activations");
+  if (m < 1 || m >= kGemmMinTokens) return fail(MAMBO_EINVAL, "the fused all-reduce takes 1 to %d tokens",
+                                                 kGemmMinTokens - 1);
+  if (w->n_rows < 1 || w->n_blocks < 1 || w->n_rows % 8) return fail(MAMBO_EINVAL, "weight must be [N, K] with N % 8 == 0");
+  const int64_t k = w->n_blocks * 256;
+  if (ldx < k || ldx % 8 || (uintptr_t)x % 16) return fail(MAMBO_EINVAL, "bf16 activations need 16-byte aligned rows of K");
+  if (out_dtype != MAMBO_F32 && out_dtype != MAMBO_BF16) return fail(MAMBO_EINVAL, "out must be f32 or bf16");
+  if (ldo < w->n_rows) return fail(MAMBO_EINVAL, "out row stride is smaller than N");
+  if ((w->n_rows + 127) / 128 * 128 > comm->max_rows)
+    return fail(MAMBO_EINVAL, "N=%lld exceeds the communicator's %d rows", (long long)w->n_rows, comm->max_rows);
+  const uintptr_t fields[6] = {(uintptr_t)w->d, (uintptr_t)w->qs, (uintptr_t)w->qh, (uintptr_t)w->signs,
+                               (uintptr_t)w->scales, (uintptr_t)w->packed};
+  for (uintptr_t f : fields)
+    if (f % 16) return fail(MAMBO_EINVAL, "weight fields must be 16-byte aligned");
+  DeviceInfo info;
+  int st = require_sm100(&info);
+  if (st != MAMBO_OK) return st;
+  int dev = -1;
+  cudaGetDevice(&dev);
+  if (dev != comm->device) return fail(MAMBO_EINVAL, "call on the device the communicator was created on");
+  MamboLinearConfig c;
+  if (cfg) c = *cfg; else default_config(m, w->n_rows, w->n_blocks, &c, info.max_smem_optin, info.sms);
+  resolve_auto(&c, m, w->n_rows, w->n_blocks, info.max_smem_optin, info.sms);
+  // Every row's sum over this rank's K slice forms in one CTA (whole row
+  // tiles, or a cluster K split summed in its rank 0): the exchange runs there.
+  c.kernel = MAMBO_KERNEL_GEMV;
+  c.loader = 0;
+  c.warps = 8;
+  if (c.split != 1) c.split = 2;
+  st = validate_config(&c, m, w->n_blocks, info);
+  if (st != MAMBO_OK) return st;
+  const GemvPlan P = plan_gemv(m, w->n_rows, w->n_blocks, c, info.sms, info.max_smem_optin);
+  if (P.kparts < 1) return fail(MAMBO_EINVAL, "no whole-tile plan for this shape");
+  while (c.stages > 2 && (int)gemv_tm_smem_bytes(P.nt, c.stages, P.kparts, true) > info.max_smem_optin) --c.stages;
+  if ((int)gemv_tm_smem_bytes(P.nt, c.stages, P.kparts, true) > info.max_smem_optin)
+    return fail(MAMBO_EINVAL, "the fused all-reduce GEMV does not fit in shared memory");
+  const size_t need = P.counters_bytes + P.partial_bytes;
+  if (!workspace || workspace_bytes < need)
+    return fail(MAMBO_EWORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+  if ((uintptr_t)workspace % 256) return fail(MAMBO_EINVAL, "workspace must be 256-byte aligned");
+  GemvTmMaps maps;
+  std::memset(&maps, 0, sizeof(maps));
+  if (!make_gemv_xb_map((const uint16_t*)x, ldx, (int)m, (int)k, 8 * P.nt, &maps.xb))
+    return fail(MAMBO_EINVAL, "bf16 activations need 16-byte aligned rows");
+  GemvTmParams p{};
+  p.m = (int)m;
+  p.n_rows = (int)w->n_rows;
+  p.n_blocks = (int)w->n_blocks;
+  p.d = (const uint8_t*)w->d;
+  p.qs = (const uint8_t*)w->qs;
+  p.qh = (const uint8_t*)w->qh;
+  p.signs = (const uint8_t*)w->signs;
+  p.scales = (const uint8_t*)w->scales;
+  p.packed = (const uint8_t*)w->packed;
+  p.table = fp8_table;
+  p.out = out;
+  p.out_bf16 = out_dtype == MAMBO_BF16;
+  p.ldo = ldo;
+  p.counters = (int*)workspace;
+  p.partials = (float*)((uint8_t*)workspace + P.counters_bytes);
+  p.stages = c.stages;
+  p.prefetch = c.prefetch;
+  p.kparts = P.kparts;
+  p.row_tiles = P.row_tiles;
+  p.total_units = P.units;
+  p.x_bf16 = (const uint16_t*)x;
+  p.ldx = ldx;
+  cudaError_t e = launch_gemv_tm_ar(p, comm->ar, P.nt, maps, P.grid, (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "iq3s_gemv_tm_kernel (fused all-reduce)");
+  return ok();
+}
+
+}  // extern "C"

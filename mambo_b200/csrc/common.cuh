@@ -30,6 +30,7 @@ enum WaitSite : int {
   kSiteGemvFull = 1,
   kSiteGemvEmpty = 2,
   kSiteSelfTest = 9,
+  kSiteArPeer = 10,  // a peer rank's partial never arrived (fused all-reduce)
 };
 
 __device__ __forceinline__ void record_timeout(int site) {
@@ -285,6 +286,17 @@ __device__ __forceinline__ int ld_acquire_gpu(const int* addr) {
   asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
   return v;
 }
+
+// System-scope accesses for data shared with peer GPUs over NVLink.
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* addr) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys_u32(uint32_t* addr, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 
 // Release/acquire counter increment at GPU scope (orders this warp's earlier
 // stores, made visible to the lane by __syncwarp, before the increment).

@@ -205,6 +205,72 @@ __device__ __forceinline__ void store_out_tm(const OutView& o, const QuantView& 
   }
 }
 
+// Fused all-reduce of a row-split linear, for one warp's 32 rows (lane = row)
+// and TOK tokens, called where the rows' final sums over this rank's K slice
+// are formed. This rank's partial goes into every rank's slot for this rank
+// (plain stores, over NVLink for peers; a system-scope fence; then one release
+// flag per rank carrying the launch epoch + 1). Once every rank's flag for the
+// 32-row group carries this epoch, the partials are summed in rank order, so
+// every rank forms the identical result. The slots alternate between two
+// buffers by epoch parity: a rank one launch ahead writes the other buffer,
+// and none gets two launches ahead (it needs this rank's next partials).
+// False when a rank's partial did not arrive within the wait limit (recorded
+// as a timeout at kSiteArPeer).
+template <int TOK>
+__device__ bool ar_exchange(const GemvAr& ar, uint32_t epoch, int row, int lane, float (&acc)[TOK]) {
+  const uint32_t par = epoch & 1u, tag = epoch + 1u;
+  const int groups = ar.max_rows / 32, g32 = row >> 5;
+  const size_t slot = (size_t)ar.max_rows * TOK;  // floats of one source rank's partial
+  const size_t row_off = (size_t)row * TOK;
+  for (int j = 0; j < ar.world; ++j) {
+    float* dst = reinterpret_cast<float*>(ar.base[j]) + ((size_t)par * ar.world + ar.rank) * slot + row_off;
+#pragma unroll
+    for (int t = 0; t < TOK; t += 4)
+      *reinterpret_cast<float4*>(dst + t) = make_float4(acc[t], acc[t + 1], acc[t + 2], acc[t + 3]);
+  }
+  fence_acq_rel_sys();
+  __syncwarp();
+  if (lane < ar.world) {  // lane j raises this rank's flag in rank j's buffer
+    uint32_t* f = reinterpret_cast<uint32_t*>(ar.base[lane] + ar.flags_offset) +
+                  ((size_t)par * ar.world + ar.rank) * groups + g32;
+    st_release_sys_u32(f, tag);
+  }
+  const uint32_t* mine =
+      reinterpret_cast<const uint32_t*>(ar.base[ar.rank] + ar.flags_offset) + (size_t)par * ar.world * groups + g32;
+  bool ok = true;
+  if (lane < ar.world) {  // lane j waits for rank j's partial of these rows
+    const unsigned long long limit = g_wait_limit_ns, t0 = globaltimer_ns();
+    for (uint32_t i = 0; ld_acquire_sys_u32(mine + (size_t)lane * groups) != tag; ++i) {
+      __nanosleep(32);
+      if ((i & 15u) == 15u && (*(volatile int*)&g_device_status.code != 0 || globaltimer_ns() - t0 > limit)) {
+        record_timeout(kSiteArPeer);
+        ok = false;
+        break;
+      }
+    }
+  }
+  if (!__all_sync(0xFFFFFFFFu, ok)) return false;
+  // Each lane acquires every flag itself (all set by now) before it reads the partials.
+  for (int j = 0; j < ar.world; ++j) (void)ld_acquire_sys_u32(mine + (size_t)j * groups);
+  const float* src = reinterpret_cast<const float*>(ar.base[ar.rank]) + (size_t)par * ar.world * slot + row_off;
+  float sum[TOK];
+#pragma unroll
+  for (int t = 0; t < TOK; ++t) sum[t] = 0.f;
+  for (int j = 0; j < ar.world; ++j) {
+#pragma unroll
+    for (int t = 0; t < TOK; t += 4) {
+      const float4 v = __ldcv(reinterpret_cast<const float4*>(src + (size_t)j * slot + t));
+      sum[t] += v.x;
+      sum[t + 1] += v.y;
+      sum[t + 2] += v.z;
+      sum[t + 3] += v.w;
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < TOK; ++t) acc[t] = sum[t];
+  return true;
+}
+
 // Q4_K: eight stored codes of one 32-bit word (bits 0-15: four values of one
 // group, bits 16-31: four of the next; each (v > 0) << 3 | (|v| - 1) / 2 for
 // the odd integer v = 2q - 15) -> the E4M3 bytes of v, four per output word.
@@ -295,6 +361,7 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
     iq3s_gemv_tm_kernel(const __grid_constant__ GemvTmParams p, const __grid_constant__ GemvTmMaps maps,
                         const __grid_constant__ G grp) {
   constexpr bool kGroup = std::is_same<G, GemvGroup>::value;
+  constexpr bool kAR = std::is_same<G, GemvAr>::value;  // row split with its all-reduce fused
   constexpr int TOK = 8 * NT;             // tokens the epilogue keeps
   constexpr int NM = tm_nmma(NT);         // MMA N
   constexpr int BOX = tm_box_tokens(NT);  // activation rows in a B tile
@@ -869,6 +936,8 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
     for (int t = 0; t < TOK; ++t) acc[t] = 0.f;
     pdl_wait();  // the workspace and output may still be in use by the previous kernel
     pdl_launch_dependents();
+    uint32_t ar_epoch = 0;  // this launch's exchange epoch (the previous launch has completed)
+    if constexpr (kAR) ar_epoch = *reinterpret_cast<volatile const uint32_t*>(grp.base[grp.rank] + grp.ctl_offset);
     // Unit j's activation scales (UE8M0, one per token and 32-wide group) go
     // to TMEM scale-factor slot j % kRing of this warp's quadrant, token t in
     // lane t: groups 0-3 in bytes 0-3 of column +0, groups 4-7 in column +4
@@ -1144,13 +1213,21 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
 #pragma unroll
               for (int t = 0; t < TOK; ++t) acc[t] += src[t];
             }
+            bool keep = true;
+            if constexpr (kAR) keep = ar_exchange<TOK>(grp, ar_epoch, row, lane, acc);
+            if (keep) {
 #pragma unroll
-            for (int t = 0; t < TOK; ++t) store_out_tm<kQ>(ou, qu, row, t, acc[t]);
+              for (int t = 0; t < TOK; ++t) store_out_tm<kQ>(ou, qu, row, t, acc[t]);
+            }
           }
         }
       } else if (full_tile) {
+        bool keep = true;
+        if constexpr (kAR) keep = ar_exchange<TOK>(grp, ar_epoch, row, lane, acc);
+        if (keep) {
 #pragma unroll
-        for (int t = 0; t < TOK; ++t) store_out_tm<kQ>(ou, qu, row, t, acc[t]);
+          for (int t = 0; t < TOK; ++t) store_out_tm<kQ>(ou, qu, row, t, acc[t]);
+        }
       } else {
         // Stream-K: a row tile shared with other CTAs. The segment a CTA
         // finishes last is usually the last contribution: if every other
@@ -1184,6 +1261,19 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
 #pragma unroll
       for (int t = 0; t < TOK; ++t) acc[t] = 0.f;
       seg_begin = u + 1;
+    }
+    if constexpr (kAR) {
+      // The last CTA to finish advances the epoch for the next launch (which
+      // reads it only after this grid has completed).
+      if (warp == kEpiWarp0 && lane == 0) {
+        uint32_t* ctl = reinterpret_cast<uint32_t*>(grp.base[grp.rank] + grp.ctl_offset);
+        __threadfence();
+        if (atomicAdd(ctl + 1, 1u) == gridDim.x - 1) {
+          ctl[1] = 0;
+          ctl[0] = ar_epoch + 1u;
+          __threadfence();
+        }
+      }
     }
     tc::fence_before_sync();
     __syncwarp();
@@ -1315,5 +1405,30 @@ cudaError_t launch_gemv_tm(const GemvTmParams& p, int nt, int dec_warps, const G
 }
 
 uint32_t q4k_gemv_smem_bytes(int nt, int stages, int kparts) { return tm_smem_bytes(nt, stages, kparts, false, true); }
+
+// Row-split linear with its all-reduce fused: 8 decoder warps, bf16 rows
+// quantized in the kernel, whole row tiles or cluster K splits (kparts >= 1:
+// every row's final sum is formed in one CTA, where the exchange runs).
+template <int NT>
+static cudaError_t launch_gemv_tm_ar_t(const GemvTmParams& p, const GemvAr& ar, const GemvTmMaps& maps, int grid,
+                                       cudaStream_t stream) {
+  const uint32_t smem = tm_smem_bytes(NT, p.stages, p.kparts, true);
+  const void* kern = (const void*)iq3s_gemv_tm_kernel<NT, 8, GemvAr, false>;
+  cudaError_t e = ensure_smem_attribute(kern, smem);
+  if (e != cudaSuccess) return e;
+  return launch_pdl_cluster(kern, dim3(grid), dim3(tm_threads(8)), smem, stream, p.kparts > 1 ? p.kparts : 1, p,
+                            maps, ar);
+}
+
+cudaError_t launch_gemv_tm_ar(const GemvTmParams& p, const GemvAr& ar, int nt, const GemvTmMaps& maps, int grid,
+                              cudaStream_t stream) {
+  if (p.kparts < 1 || p.x_bf16 == nullptr || p.q_out != nullptr || ar.world < 1 || ar.world > kGemvArMaxRanks)
+    return cudaErrorInvalidValue;
+  switch (nt) {
+    case 1: return launch_gemv_tm_ar_t<1>(p, ar, maps, grid, stream);
+    case 2: return launch_gemv_tm_ar_t<2>(p, ar, maps, grid, stream);
+    default: return launch_gemv_tm_ar_t<4>(p, ar, maps, grid, stream);
+  }
+}
 
 }  // namespace mambo

@@ -361,6 +361,36 @@ def fused_linear_into(x: torch.Tensor, iq3_weight: IQ3SFields, out: torch.Tensor
     return out
 
 
+def fused_linear_ar_into(x: torch.Tensor, iq3_weight: IQ3SFields, out: torch.Tensor, comm, config: dict | None = None,
+                         stream=None) -> torch.Tensor:
+    """A row-split linear and its all-reduce in one launch (mambo_iq3s_linear_fused_ar).
+
+    ``x``: this rank's bf16 K slice [M, K/world] (M < 32); ``iq3_weight``: its
+    shard [N, K/world]; ``comm``: a :class:`mambo_b200.sharding.FusedAllReduce`.
+    ``out`` [M, N] receives the sum over all ranks (identical on every rank).
+    """
+    n_rows, blocks = _weight_dimensions(iq3_weight)
+    m = x.shape[0]
+    dev = x.device
+    cfg = _lib.MamboLinearConfig.from_dict(config if config is not None else select_config(m, n_rows, blocks * 256,
+                                                                                              dev))
+    w = weight_struct(iq3_weight)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        st = _runtime.stream_handle(stream, dev)
+        need = lib.mambo_iq3s_linear_fused_workspace_bytes(m, n_rows, blocks, cfg)
+        ws = _runtime.workspace(dev, st, need)
+        out_dtype = _lib.MAMBO_BF16 if out.dtype == torch.bfloat16 else _lib.MAMBO_F32
+        _lib.check(
+            lib.mambo_iq3s_linear_fused_ar(
+                x.data_ptr(), _lib.MAMBO_BF16, x.stride(0), m, w, _get_iq3_table(dev).data_ptr(), out.data_ptr(),
+                out_dtype, out.stride(0), comm.handle, cfg, ws.data_ptr(), ws.numel(), st,
+            ),
+            "fused all-reduce linear",
+        )
+    return out
+
+
 def iq3_s_fp8_linear(x, iq3_weight: IQ3SFields, *, stream=None, out_dtype: torch.dtype = torch.bfloat16,
                      rounding: str = "nearest_even", config: dict | None = None, quantize_output: bool = False):
     """bf16/f32 activations [M,K] -> MXFP8 -> IQ3_S linear -> out_dtype [M,N] (quantize + matmul).

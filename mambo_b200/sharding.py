@@ -17,6 +17,11 @@ K into whole 256-weight blocks; ``K % (256 * world) == 0`` and
 The collectives go through ``torch.distributed`` (NCCL on GPUs, gloo in the
 CPU tests). The per-rank compute is the single-GPU path of this package;
 ``linear``/``quantize`` can be replaced (the CPU tests plug in a restatement).
+
+At decode sizes (M < 32) a row split can instead run its all-reduce inside the
+GEMV launch (:class:`FusedAllReduce`, ``TensorParallelIQ3SLinear.fused``):
+each row tile's partial goes straight into every rank's exchange buffer over
+NVLink and every rank sums all partials in rank order, with no NCCL call.
 """
 
 from __future__ import annotations
@@ -29,6 +34,51 @@ import torch.distributed as dist
 
 COLUMN = "column"
 ROW = "row"
+
+
+class FusedAllReduce:
+    """This rank's side of the fused row-split all-reduce.
+
+    Allocates an exchange buffer on the current GPU for outputs of up to
+    ``max_rows`` rows (the C ABI's mambo_ar_comm_create), all-gathers the
+    buffers' CUDA IPC handles over ``group`` and maps every peer's buffer
+    (mambo_ar_comm_connect). Every rank must then issue the same sequence of
+    fused linears on it (same shapes), on one stream per rank. ``close()``
+    releases the mappings and the buffer.
+    """
+
+    def __init__(self, max_rows: int, group=None):
+        import ctypes
+
+        from . import _lib
+
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.max_rows = (max_rows + 127) // 128 * 128
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        lib = _lib.load()
+        handle = ctypes.create_string_buffer(_lib.MAMBO_AR_HANDLE_BYTES)
+        comm = ctypes.c_void_p()
+        _lib.check(lib.mambo_ar_comm_create(self.world, self.rank, self.max_rows, ctypes.byref(comm), handle),
+                   "mambo_ar_comm_create")
+        self.handle = comm
+        handles = [bytes(handle.raw)]
+        if self.world > 1:
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(handle.raw), group=group)
+        try:
+            _lib.check(lib.mambo_ar_comm_connect(comm, b"".join(handles)), "mambo_ar_comm_connect")
+        except Exception:
+            lib.mambo_ar_comm_destroy(comm)
+            self.handle = None
+            raise
+
+    def close(self) -> None:
+        if self.handle is not None:
+            from . import _lib
+
+            _lib.load().mambo_ar_comm_destroy(self.handle)
+            self.handle = None
 
 
 def shard_range(total: int, rank: int, world: int, unit: int) -> tuple[int, int]:
@@ -174,6 +224,30 @@ class TensorParallelIQ3SLinear:
         return y if dtype == torch.float32 else y.to(dtype)
 
     __call__ = forward
+
+    def fused(self, x: torch.Tensor, comm: FusedAllReduce, *, out_dtype: torch.dtype | None = None,
+              out: torch.Tensor | None = None) -> torch.Tensor:
+        """Row split at decode sizes: this rank's GEMV and the sum over ranks in one launch.
+
+        ``x``: [M, K] (or [M, K/P] with ``input_is_sharded``), bf16, M < 32.
+        Returns the full [M, N] output, identical on every rank.
+        """
+        from .kernels.iq3_s_fp8 import fused_linear_ar_into
+
+        if self.mode != ROW:
+            raise ValueError("the fused all-reduce applies to a row split")
+        if x.ndim != 2 or x.dtype != torch.bfloat16:
+            raise ValueError("activation must be bf16 [M,K]")
+        if not self.input_is_sharded:
+            if x.shape[1] != self.k:
+                raise ValueError(f"row-split activation must be [M,{self.k}]")
+            x = x[:, self.k0:self.k0 + self.local_k]
+        elif x.shape[1] != self.local_k:
+            raise ValueError(f"sharded row-split activation must be [M,{self.local_k}]")
+        dtype = out_dtype or self.out_dtype
+        if out is None:
+            out = torch.empty((x.shape[0], self.n), dtype=dtype, device=x.device)
+        return fused_linear_ar_into(x, self.fields, out, comm)
 
     def _gather_columns(self, y: torch.Tensor) -> torch.Tensor:
         if dist.get_backend(self.group) == "nccl":
