@@ -722,7 +722,7 @@ def tp_block(torch, world: int, rank: int, dev, steps: int, warmup: int) -> dict
     import torch.distributed as dist
 
     from mambo_b200.kernels.iq3_s_fp8 import fused_linear_into, group_linear_into, iq3_s_fp8_linear
-    from mambo_b200.sharding import TensorParallelIQ3SLinear, gather_columns_group, local_group
+    from mambo_b200.sharding import FusedAllReduce, TensorParallelIQ3SLinear, gather_columns_group, local_group
     from mambo_b200.utils.iq3_s_weight import prepare_iq3_s_fields
 
     kdim = {name: k for name, n, k, split in TP70B}
@@ -743,6 +743,7 @@ def tp_block(torch, world: int, rank: int, dev, steps: int, warmup: int) -> dict
         layers.append(lin)
     stream = torch.cuda.Stream(dev)
     results = []
+    fused_comm = None  # the fused row-split all-reduce's exchange buffers (world > 1, decode sizes)
     for m in TP70B_MS:
         gen = torch.Generator(device=dev).manual_seed(20261017 + m)  # the same activations on every rank
         x_full = {k: torch.randn((m, k), device=dev, generator=gen).to(torch.bfloat16) for k in (8192, 28672)}
@@ -867,6 +868,59 @@ def tp_block(torch, world: int, rank: int, dev, steps: int, warmup: int) -> dict
             ms, coll = float(t[0]), float(t[1])
         del graphs
         torch.cuda.synchronize(dev)
+        if world > 1 and m < 32:
+            # Decode sizes: the row splits' all-reduces fused into their GEMVs (peer stores over NVLink, no
+            # NCCL call), so the rank's whole layer is one CUDA graph.
+            if fused_comm is None:
+                fused_comm = FusedAllReduce(8192)
+            l0 = layers[0]
+            f_errs = {}
+            for name, x_in in (("o", x_o), ("down", x_dn)):
+                y32 = l0[name].fused(x_in, fused_comm, out_dtype=torch.float32)
+                torch.cuda.synchronize(dev)
+                if rank == 0:
+                    ref = iq3_s_fp8_linear(x_full[kdim[name]], full[name], out_dtype=torch.float32)
+                    f_errs[name] = (torch.linalg.norm((y32 - ref).double()) / torch.linalg.norm(ref.double())).item()
+            y_o = torch.empty((m, 8192), dtype=torch.bfloat16, device=dev)
+            y_dn = torch.empty((m, 8192), dtype=torch.bfloat16, device=dev)
+
+            def layer_fused(li):
+                w = layers[li]
+                w["qkv"].local(x_full[8192])
+                w["o"].fused(x_o, fused_comm, out=y_o)
+                local_group([w["gate"], w["up"]], x_full[8192])
+                w["down"].fused(x_dn, fused_comm, out=y_dn)
+
+            with torch.cuda.stream(stream):
+                for li in range(2):
+                    layer_fused(li)
+            torch.cuda.synchronize(dev)
+            fgraphs = []
+            for li in range(2):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    layer_fused(li)
+                fgraphs.append(g)
+            with torch.cuda.stream(stream):
+                for i in range(max(3, warmup)):
+                    fgraphs[i & 1].replay()
+            torch.cuda.synchronize(dev)
+            dist.barrier()
+            with torch.cuda.stream(stream):
+                e0.record(stream)
+                for i in range(n_steps):
+                    fgraphs[i & 1].replay()
+                e1.record(stream)
+            torch.cuda.synchronize(dev)
+            t = torch.tensor([e0.elapsed_time(e1) / n_steps], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            rec["ms_per_layer_fused_allreduce"] = round(float(t[0]), 4)
+            if rank == 0:
+                rec["parity_fused_allreduce_rel_frobenius"] = {k2: float(f"{v:.3g}") for k2, v in f_errs.items()}
+                rec["parity_ok"] = rec.get("parity_ok", True) and all(v <= TP_PARITY_TOL for v in f_errs.values())
+            del fgraphs
+            torch.cuda.synchronize(dev)
+            dist.barrier()
         # The unsharded layer on rank 0 of this box (the N = 1 figure next to the sharded one).
         if world > 1:
             if rank == 0:
@@ -896,6 +950,9 @@ def tp_block(torch, world: int, rank: int, dev, steps: int, warmup: int) -> dict
                 torch.cuda.synchronize(dev)
                 rec["ms_per_layer_1gpu"] = round(f0.elapsed_time(f1) / n_steps, 4)
                 rec["speedup_vs_1gpu"] = round(rec["ms_per_layer_1gpu"] / ms, 3)
+                if "ms_per_layer_fused_allreduce" in rec:
+                    rec["speedup_fused_allreduce_vs_1gpu"] = round(
+                        rec["ms_per_layer_1gpu"] / rec["ms_per_layer_fused_allreduce"], 3)
                 del g
             dist.barrier()
         w_bytes = sum(n * (k // 256) * 110 for _, n, k, _ in TP70B)
@@ -904,6 +961,10 @@ def tp_block(torch, world: int, rank: int, dev, steps: int, warmup: int) -> dict
                     "weight_gbs_total": round(w_bytes / (ms * 1e-3) / 1e9, 1),
                     "tflops_total": round(flops / (ms * 1e-3) / 1e12, 1)})
         results.append(rec)
+    if fused_comm is not None:
+        torch.cuda.synchronize(dev)
+        dist.barrier()  # every rank is done writing into the peers' buffers
+        fused_comm.close()
     del layers, full
     torch.cuda.empty_cache()
     if rank != 0:
@@ -918,6 +979,10 @@ def tp_block(torch, world: int, rank: int, dev, steps: int, warmup: int) -> dict
                       "all-reduce of down's partials + cast; column outputs stay sharded (the next row split "
                       "consumes them)"),
             "collective_ms": "device time of the layer's two all-reduces alone (eager), max over ranks",
+            "fused_allreduce": ("M < 32, N GPUs: O and down each one launch of mambo_iq3s_linear_fused_ar (the GEMV "
+                                "writes each row tile's FP32 partial into every rank's exchange buffer over NVLink "
+                                "and sums all ranks' partials in rank order), the rank's whole layer one CUDA graph "
+                                "with no NCCL call; parity of O and down against the unsharded linear"),
             "results": results}
 
 

@@ -405,16 +405,17 @@ MAMBO_API int mambo_selftest_wait_timeout(unsigned long long limit_ns, mambo_str
  * counterpart in the reference, which runs every linear on one GPU). Each of
  * `world` ranks (one process per GPU, up to 8) holds a K slice of the weight;
  * the GEMV that multiplies it writes each row tile's partial straight into
- * every rank's exchange buffer over NVLink (plain peer stores, no multicast),
- * raises a flag there, waits (bounded, MAMBO_ETIMEOUT) for every rank's
- * partial of the same rows and sums them in rank order: every rank gets the
- * identical [m, N] result, with no separate collective launch. This replaces
+ * every rank's exchange buffer over NVLink (plain peer stores, no multicast;
+ * each value shares an 8-byte word with the call's tag, so no fence or flag is
+ * needed), waits (bounded, MAMBO_ETIMEOUT) for every rank's partial of the
+ * same rows and sums them in rank order: every rank gets the identical [m, N]
+ * result, with no separate collective launch. This replaces
  * the GEMV + NCCL all-reduce pair of a row split (the O and down projections
  * of a tensor-parallel layer) at decode sizes.
  *
  * mambo_ar_comm_create allocates this rank's exchange buffer on the current
- * device (slots for up to max_rows output rows, a multiple of 128, and 32
- * tokens; about 256 * world * max_rows bytes) and writes its CUDA IPC handle
+ * device (slots for up to max_rows output rows, a multiple of 128 up to 2^18,
+ * and 32 tokens: 512 * world * max_rows bytes) and writes its CUDA IPC handle
  * (MAMBO_AR_HANDLE_BYTES bytes) to ipc_handle. The caller exchanges the
  * handles between the ranks (e.g. an all-gather over its process group) and
  * passes all of them, in rank order, to mambo_ar_comm_connect. Every rank

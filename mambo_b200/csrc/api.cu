@@ -1603,9 +1603,7 @@ struct MamboArComm {
 
 namespace {
 
-size_t ar_buffer_bytes(int world, int max_rows) {
-  return gemv_ar_slot_bytes(world, max_rows) + gemv_ar_flag_bytes(world, max_rows) + 256;
-}
+size_t ar_buffer_bytes(int world, int max_rows) { return gemv_ar_slot_bytes(world, max_rows) + 256; }
 
 }  // namespace
 
@@ -1616,8 +1614,8 @@ int mambo_ar_comm_create(int world, int rank, int64_t max_rows, MamboArComm** co
   *comm = nullptr;
   if (world < 1 || world > kGemvArMaxRanks) return fail(MAMBO_EINVAL, "world must be 1..%d", kGemvArMaxRanks);
   if (rank < 0 || rank >= world) return fail(MAMBO_EINVAL, "rank must be in [0, world)");
-  if (max_rows < 128 || max_rows % 128 || max_rows > (1 << 20))
-    return fail(MAMBO_EINVAL, "max_rows must be a positive multiple of 128 up to 2^20");
+  if (max_rows < 128 || max_rows % 128 || max_rows > (1 << 18))
+    return fail(MAMBO_EINVAL, "max_rows must be a positive multiple of 128 up to 2^18");
   DeviceInfo info;
   int st = require_sm100(&info);
   if (st != MAMBO_OK) return st;
@@ -1633,7 +1631,7 @@ int mambo_ar_comm_create(int world, int rank, int64_t max_rows, MamboArComm** co
     delete c;
     return cuda_fail(e, "cudaMalloc(exchange buffer)");
   }
-  // Flags and epoch start at zero; every launch then tags its flags with epoch + 1.
+  // Tags and epoch start at zero; every launch then tags its words with epoch + 1.
   e = cudaMemset(c->local, 0, c->bytes);
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e == cudaSuccess) e = cudaIpcGetMemHandle((cudaIpcMemHandle_t*)ipc_handle, c->local);
@@ -1645,8 +1643,7 @@ int mambo_ar_comm_create(int world, int rank, int64_t max_rows, MamboArComm** co
   c->ar.world = world;
   c->ar.rank = rank;
   c->ar.max_rows = (int)max_rows;
-  c->ar.flags_offset = (uint32_t)gemv_ar_slot_bytes(world, (int)max_rows);
-  c->ar.ctl_offset = c->ar.flags_offset + (uint32_t)gemv_ar_flag_bytes(world, (int)max_rows);
+  c->ar.ctl_offset = (uint32_t)gemv_ar_slot_bytes(world, (int)max_rows);
   c->ar.base[rank] = c->local;
   *comm = c;
   return ok();

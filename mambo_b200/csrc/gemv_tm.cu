@@ -207,68 +207,62 @@ __device__ __forceinline__ void store_out_tm(const OutView& o, const QuantView& 
 
 // Fused all-reduce of a row-split linear, for one warp's 32 rows (lane = row)
 // and TOK tokens, called where the rows' final sums over this rank's K slice
-// are formed. This rank's partial goes into every rank's slot for this rank
-// (plain stores, over NVLink for peers; a system-scope fence; then one release
-// flag per rank carrying the launch epoch + 1). Once every rank's flag for the
-// 32-row group carries this epoch, the partials are summed in rank order, so
-// every rank forms the identical result. The slots alternate between two
-// buffers by epoch parity: a rank one launch ahead writes the other buffer,
-// and none gets two launches ahead (it needs this rank's next partials).
-// False when a rank's partial did not arrive within the wait limit (recorded
-// as a timeout at kSiteArPeer).
+// are formed. Each value travels with the launch's tag (epoch + 1) in one
+// 8-byte word, which a single aligned store writes and a single load reads
+// whole: a reader that sees the tag sees the value, with no fence or flag
+// (the low-latency scheme of NCCL's LL protocol). This rank's partial goes into
+// every rank's slot for this rank (plain stores, over NVLink for peers); then
+// each lane polls its row of every rank's slot here until the tags carry this
+// launch's, and sums the partials in rank order, so every rank forms the
+// identical result. The slots alternate between two buffers by epoch parity: a
+// rank one launch ahead writes the other buffer, and none gets two launches
+// ahead (it needs this rank's next partials). False when a rank's partial did
+// not arrive within the wait limit (recorded as a timeout at kSiteArPeer).
 template <int TOK>
 __device__ bool ar_exchange(const GemvAr& ar, uint32_t epoch, int row, int lane, float (&acc)[TOK]) {
+  static_assert(TOK % 2 == 0, "values go in pairs");
   const uint32_t par = epoch & 1u, tag = epoch + 1u;
-  const int groups = ar.max_rows / 32, g32 = row >> 5;
-  const size_t slot = (size_t)ar.max_rows * TOK;  // floats of one source rank's partial
+  const size_t slot = (size_t)ar.max_rows * TOK;  // 8-byte words of one source rank's partial
   const size_t row_off = (size_t)row * TOK;
   for (int j = 0; j < ar.world; ++j) {
-    float* dst = reinterpret_cast<float*>(ar.base[j]) + ((size_t)par * ar.world + ar.rank) * slot + row_off;
+    uint2* dst = reinterpret_cast<uint2*>(ar.base[j]) + ((size_t)par * ar.world + ar.rank) * slot + row_off;
 #pragma unroll
-    for (int t = 0; t < TOK; t += 4)
-      *reinterpret_cast<float4*>(dst + t) = make_float4(acc[t], acc[t + 1], acc[t + 2], acc[t + 3]);
+    for (int t = 0; t < TOK; t += 2)
+      asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(dst + t), "r"(__float_as_uint(acc[t])),
+                   "r"(tag), "r"(__float_as_uint(acc[t + 1])), "r"(tag)
+                   : "memory");
   }
-  fence_acq_rel_sys();
-  __syncwarp();
-  if (lane < ar.world) {  // lane j raises this rank's flag in rank j's buffer
-    uint32_t* f = reinterpret_cast<uint32_t*>(ar.base[lane] + ar.flags_offset) +
-                  ((size_t)par * ar.world + ar.rank) * groups + g32;
-    st_release_sys_u32(f, tag);
-  }
-  const uint32_t* mine =
-      reinterpret_cast<const uint32_t*>(ar.base[ar.rank] + ar.flags_offset) + (size_t)par * ar.world * groups + g32;
-  bool ok = true;
-  if (lane < ar.world) {  // lane j waits for rank j's partial of these rows
-    const unsigned long long limit = g_wait_limit_ns, t0 = globaltimer_ns();
-    for (uint32_t i = 0; ld_acquire_sys_u32(mine + (size_t)lane * groups) != tag; ++i) {
-      __nanosleep(32);
-      if ((i & 15u) == 15u && (*(volatile int*)&g_device_status.code != 0 || globaltimer_ns() - t0 > limit)) {
-        record_timeout(kSiteArPeer);
-        ok = false;
-        break;
-      }
-    }
-  }
-  if (!__all_sync(0xFFFFFFFFu, ok)) return false;
-  // Each lane acquires every flag itself (all set by now) before it reads the partials.
-  for (int j = 0; j < ar.world; ++j) (void)ld_acquire_sys_u32(mine + (size_t)j * groups);
-  const float* src = reinterpret_cast<const float*>(ar.base[ar.rank]) + (size_t)par * ar.world * slot + row_off;
+  const uint2* src = reinterpret_cast<const uint2*>(ar.base[ar.rank]) + (size_t)par * ar.world * slot + row_off;
   float sum[TOK];
 #pragma unroll
   for (int t = 0; t < TOK; ++t) sum[t] = 0.f;
+  bool ok = true;
+  const unsigned long long limit = g_wait_limit_ns;
+  unsigned long long t0 = 0;
   for (int j = 0; j < ar.world; ++j) {
 #pragma unroll
-    for (int t = 0; t < TOK; t += 4) {
-      const float4 v = __ldcv(reinterpret_cast<const float4*>(src + (size_t)j * slot + t));
-      sum[t] += v.x;
-      sum[t + 1] += v.y;
-      sum[t + 2] += v.z;
-      sum[t + 3] += v.w;
+    for (int t = 0; t < TOK; t += 2) {
+      uint32_t a, ta, b, tb;
+      for (uint32_t i = 0;; ++i) {
+        asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(a), "=r"(ta), "=r"(b), "=r"(tb)
+                     : "l"(src + (size_t)j * slot + t)
+                     : "memory");
+        if ((ta == tag && tb == tag) || !ok) break;
+        if (i == 0) t0 = globaltimer_ns();
+        __nanosleep(20);
+        if ((i & 15u) == 15u && (*(volatile int*)&g_device_status.code != 0 || globaltimer_ns() - t0 > limit)) {
+          record_timeout(kSiteArPeer);
+          ok = false;
+        }
+      }
+      sum[t] += __uint_as_float(a);
+      sum[t + 1] += __uint_as_float(b);
     }
   }
 #pragma unroll
   for (int t = 0; t < TOK; ++t) acc[t] = sum[t];
-  return true;
+  return __all_sync(0xFFFFFFFFu, ok);
 }
 
 // Q4_K: eight stored codes of one 32-bit word (bits 0-15: four values of one

@@ -232,23 +232,18 @@ struct GemvNoGroup {
 // Row-split tensor-parallel linear with its all-reduce in the same launch (the
 // third policy type of the GEMV, in place of GemvGroup / GemvNoGroup). Every
 // rank's exchange buffer, mapped into this process (base[rank] is this rank's
-// own): [2 launch parities][world source ranks][max_rows][tokens] FP32
-// partials, then at flags_offset [2][world][max_rows / 32] uint32 flags (one
-// per source rank and 32-row group: the launch epoch + 1 once that rank's
-// partial has landed), then at ctl_offset {epoch, CTAs done}.
+// own): [2 launch parities][world source ranks][max_rows][tokens] 8-byte words
+// {FP32 partial, launch tag}, then at ctl_offset {epoch, CTAs done}.
 constexpr int kGemvArMaxRanks = 8;
 struct GemvAr {
   uint8_t* base[kGemvArMaxRanks];
   int world, rank;
   int max_rows;  // rows of a source rank's partial slot (a multiple of 128)
-  uint32_t flags_offset, ctl_offset;
+  uint32_t ctl_offset;
 };
-// Byte sizes of one rank's exchange buffer: slots (up to 32 tokens), flags, control words.
+// Byte size of one rank's exchange slots (up to 32 tokens).
 __host__ __device__ inline size_t gemv_ar_slot_bytes(int world, int max_rows) {
-  return (size_t)2 * world * max_rows * 32 * sizeof(float);
-}
-__host__ __device__ inline size_t gemv_ar_flag_bytes(int world, int max_rows) {
-  return ((size_t)2 * world * (max_rows / 32) * sizeof(uint32_t) + 255) / 256 * 256;
+  return (size_t)2 * world * max_rows * 32 * 8;
 }
 cudaError_t launch_gemv_tm_ar(const GemvTmParams& p, const GemvAr& ar, int nt, const GemvTmMaps& maps, int grid,
                               cudaStream_t stream);
