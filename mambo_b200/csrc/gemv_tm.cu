@@ -556,6 +556,10 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
       }
       if (!__all_sync(0xFFFFFFFFu, ok)) return;
       issue_weights(it, s);
+      // L2 prefetch of the units after the ones already requested. (The window
+      // once began at the unit just issued: with no prefetch distance every
+      // unit was requested twice, and the copy engine spent its time on both.)
+      pf = max(pf, it + 1);
       for (; pf < min(n_units, it + 1 + p.prefetch); ++pf) prefetch(pf);
     }
     return;
