@@ -98,7 +98,11 @@ typedef struct MamboLinearConfig {
  * rounded, into the weight operand (fp16(d * 2^-e * (1+2*nibble)) * grid, e a
  * per-row exponent stored with the packed copy): one accumulator covers the
  * whole K range, so no per-block epilogue; about 2^-12 relative rounding per
- * weight, within the 1e-3 relative Frobenius bound of the linear. */
+ * weight, within the 1e-3 relative Frobenius bound of the linear.
+ * MAMBO_KERNEL_GEMM_F16_WIDE: the folded arithmetic on CTA pairs with tiles of
+ * 256 weight rows x 256 tokens: each decoded weight block feeds twice the
+ * tensor work of a 128-token tile (the GEMM_F16 kernels are paced by their
+ * weight decoders), and each activation tile serves 256 weight rows. */
 enum {
   MAMBO_KERNEL_AUTO = 0,
   MAMBO_KERNEL_GEMV = 1,
@@ -106,7 +110,8 @@ enum {
   MAMBO_KERNEL_GEMV_SYNC = 3,
   MAMBO_KERNEL_GEMM_F16 = 4,
   MAMBO_KERNEL_GEMM_F16_PAIR = 5,
-  MAMBO_KERNEL_GEMM_F16_FOLD = 6
+  MAMBO_KERNEL_GEMM_F16_FOLD = 6,
+  MAMBO_KERNEL_GEMM_F16_WIDE = 7
 };
 
 /* Library version string. */

@@ -34,6 +34,7 @@ MAMBO_KERNEL_GEMV_SYNC = 3
 MAMBO_KERNEL_GEMM_F16 = 4
 MAMBO_KERNEL_GEMM_F16_PAIR = 5
 MAMBO_KERNEL_GEMM_F16_FOLD = 6
+MAMBO_KERNEL_GEMM_F16_WIDE = 7
 
 # Every symbol include/mambo_b200.h declares.
 EXPORTED_SYMBOLS = (

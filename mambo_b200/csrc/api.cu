@@ -163,7 +163,8 @@ constexpr int kSmemOptinDefault = 232448;
 int kernel_of(const MamboLinearConfig& c) { return c.kernel == MAMBO_KERNEL_AUTO ? MAMBO_KERNEL_GEMV : c.kernel; }
 // The FP16-operand GEMM, on single CTAs or on CTA pairs.
 bool is_gemm_f16(int kind) {
-  return kind == MAMBO_KERNEL_GEMM_F16 || kind == MAMBO_KERNEL_GEMM_F16_PAIR || kind == MAMBO_KERNEL_GEMM_F16_FOLD;
+  return kind == MAMBO_KERNEL_GEMM_F16 || kind == MAMBO_KERNEL_GEMM_F16_PAIR || kind == MAMBO_KERNEL_GEMM_F16_FOLD ||
+         kind == MAMBO_KERNEL_GEMM_F16_WIDE;
 }
 // FP16 GEMM kinds that run on single CTAs and take a K split.
 bool is_gemm_f16_single(int kind) { return kind == MAMBO_KERNEL_GEMM_F16 || kind == MAMBO_KERNEL_GEMM_F16_FOLD; }
@@ -326,13 +327,15 @@ int gemm_f16_default_split(int64_t m, int64_t n, int64_t b, int sms) {
 
 // The FP16 GEMM's workspace: the counter region (the GEMVs' counters left
 // zero, the K-split counters), the FP16 activations [m][K], the tokens'
-// scales (padded to whole 128-token tiles: the epilogue reads them 16 at a
-// time) and, with a K split, the FP32 partials of every output tile.
+// scales (padded to whole 256-token tiles: the epilogue reads them 16 at a
+// time, the wide GEMM's tiles are 256 tokens) and, with a K split, the FP32
+// partials of every output tile.
+size_t gemm_f16_tok_scale_bytes(int64_t m) { return align256((size_t)((m + 255) / 256 * 256) * 4); }
 size_t gemm_f16_partial_bytes(int64_t m, int64_t n, int ks) {
   return ks > 1 ? align256((size_t)gemm_f16_out_tiles(m, n) * ks * 128 * 128 * sizeof(float)) : 0;
 }
 size_t gemm_f16_workspace_bytes(int64_t m, int64_t n, int64_t b, int ks) {
-  return kCounterBytes + align256((size_t)m * (size_t)b * 256 * 2) + align256((size_t)((m + 127) / 128 * 128) * 4) +
+  return kCounterBytes + align256((size_t)m * (size_t)b * 256 * 2) + gemm_f16_tok_scale_bytes(m) +
          gemm_f16_partial_bytes(m, n, ks);
 }
 
@@ -427,8 +430,9 @@ struct GemmF16Source {
 int launch_gemm_f16_path(const GemmF16Source& src, int64_t m, const MamboIQ3SWeight* w, const uint32_t* fp8_table,
                          void* out, int out_dtype, int64_t ldo, const MamboLinearConfig& c, const DeviceInfo& info,
                          void* workspace, size_t workspace_bytes, cudaStream_t stream) {
-  const bool pair = c.kernel == MAMBO_KERNEL_GEMM_F16_PAIR;
-  const bool fold = c.kernel == MAMBO_KERNEL_GEMM_F16_FOLD;
+  const bool wide = c.kernel == MAMBO_KERNEL_GEMM_F16_WIDE;
+  const bool pair = c.kernel == MAMBO_KERNEL_GEMM_F16_PAIR || wide;
+  const bool fold = c.kernel == MAMBO_KERNEL_GEMM_F16_FOLD || wide;
   const int ks = pair ? 1 : gemm_f16_clamp_split(c.split, m, w->n_rows, w->n_blocks);
   const size_t need = gemm_f16_workspace_bytes(m, w->n_rows, w->n_blocks, ks);
   if (!workspace || workspace_bytes < need)
@@ -445,8 +449,8 @@ int launch_gemm_f16_path(const GemmF16Source& src, int64_t m, const MamboIQ3SWei
   if (e != cudaSuccess) return cuda_fail(e, src.x ? "iq3s_x16_quant" : "iq3s_x16");
   GemmF16Maps maps;
   std::memset(&maps, 0, sizeof(maps));
-  // A CTA of a pair loads 64 of the tile's 128 tokens.
-  if (!make_gemm_x16_map(x16, k, (int)m, k, pair ? 64 : 128, &maps.x16))
+  // A CTA of a pair loads 64 of the tile's 128 tokens (wide: 128 of 256).
+  if (!make_gemm_x16_map(x16, k, (int)m, k, pair && !wide ? 64 : 128, &maps.x16))
     return fail(MAMBO_ECUDA, "could not encode the FP16 activation tensor map");
   GemmF16Params p{};
   p.m = (int)m;
@@ -460,13 +464,13 @@ int launch_gemm_f16_path(const GemmF16Source& src, int64_t m, const MamboIQ3SWei
   p.ldo = ldo;
   p.wstages = c.stages;
   p.row_tiles = (int)((w->n_rows + 127) / 128);
-  p.tok_tiles = (int)((m + 127) / 128);
+  p.tok_tiles = (int)(wide ? (m + 255) / 256 : (m + 127) / 128);
   p.ksplit = ks;
   if (fold)  // the row exponents after the packed records
     p.row_exp = (const int8_t*)w->packed + (size_t)p.row_tiles * (size_t)w->n_blocks * MAMBO_IQ3S_RECORD_BYTES;
   if (ks > 1) {
     // Partials after the token scales; counters in the counter region's second half.
-    p.partials = (float*)((uint8_t*)tok_scale + align256((size_t)((m + 127) / 128 * 128) * 4));
+    p.partials = (float*)((uint8_t*)tok_scale + gemm_f16_tok_scale_bytes(m));
     p.split_counters = (int*)((uint8_t*)workspace + kGemmSplitCounterOffset);
   }
   // bf16 output in 16-byte aligned rows: tiles leave through shared memory and
@@ -485,8 +489,8 @@ int launch_gemm_f16_path(const GemmF16Source& src, int64_t m, const MamboIQ3SWei
     int clusters = gemm_f16_pair_max_clusters(p.wstages, p.out_tma != 0);
     if (clusters < 1) return fail(MAMBO_EINVAL, "no CTA pair of this configuration fits on the device");
     if (tiles < clusters) clusters = (int)tiles;
-    e = launch_gemm_f16_pair(p, maps, clusters, stream);
-    if (e != cudaSuccess) return cuda_fail(e, "iq3s_gemm_f16 (pairs)");
+    e = launch_gemm_f16_pair(p, maps, clusters, stream, wide);
+    if (e != cudaSuccess) return cuda_fail(e, wide ? "iq3s_gemm_f16 (wide pairs)" : "iq3s_gemm_f16 (pairs)");
     return ok();
   }
   const int64_t tiles = (int64_t)p.row_tiles * p.tok_tiles * ks;

@@ -102,23 +102,32 @@ __device__ __forceinline__ void store_out_h(const GemmF16Params& p, int row, int
 // tile serves 256 weight rows: half the L2 traffic per FLOP) and its commits
 // arrive in both CTAs; rank 1's decoders and epilogue arrive on rank 0's
 // barriers. Otherwise 128 x 128 tiles on single CTAs.
-// kFold (single CTAs only): the block scale d folded, rounded, into the FP16
-// weight operand with each row's exponent taken out (GemmF16Params::row_exp),
-// so one accumulator covers the tile's whole K range: the epilogue runs once
-// per tile instead of once per K block, and the MMAs never wait for it inside
-// a tile. Each weight carries one FP16 rounding (about 2^-12 relative).
+// kFold: the block scale d folded, rounded, into the FP16 weight operand with
+// each row's exponent taken out (GemmF16Params::row_exp), so one accumulator
+// covers the tile's whole K range: the epilogue runs once per tile instead of
+// once per K block, and the MMAs never wait for it inside a tile. Each weight
+// carries one FP16 rounding (about 2^-12 relative).
+// kPair and kFold together (the wide GEMM): tiles of 256 weight rows x 256
+// tokens on a CTA pair, each CTA loading 128 tokens of every activation
+// half-block and holding its rows' 128 x 256 accumulator (all of TMEM beside
+// the A ring, so one accumulator per tile). Each decoded weight block feeds
+// twice the tensor work of a 128-token tile, and each activation tile serves
+// 256 weight rows.
 template <bool kPair, bool kFold = false>
 __global__ void __launch_bounds__(kThreadsH, 1)
     iq3s_gemm_f16_kernel(const __grid_constant__ GemmF16Params p, const __grid_constant__ GemmF16Maps maps) {
-  static_assert(!(kPair && kFold), "the folded GEMM runs on single CTAs");
+  constexpr bool kWide = kPair && kFold;
+  constexpr int kTokT = kWide ? 2 * kTokH : kTokH;  // tokens of a tile
+  constexpr int kPasses = kWide ? 2 : 1;            // epilogue passes of 128 tokens per tile
   // B half-block (the CTA's tokens x 128 K): two [tokens][128 bytes] boxes in
   // the 128-byte-swizzled K-major layout (8-row atoms 1024 bytes apart); an
   // MMA's 16 K (32 bytes) start 32 bytes further into the row.
-  constexpr int kTokLoad = kPair ? 64 : kTokH;
-  constexpr int kXS = x_stages_h(kPair);
-  constexpr uint32_t kXHalf = x_half_bytes_h(kPair);
+  constexpr int kTokLoad = kPair && !kWide ? 64 : kTokH;
+  constexpr int kXS = x_stages_h(kPair && !kWide);
+  constexpr uint32_t kXHalf = x_half_bytes_h(kPair && !kWide);
   constexpr uint32_t kBoxBytes = kTokLoad * 128u;
-  constexpr uint32_t kIdesc = tc::idesc_f16_f32(kPair ? 2 * kRowsH : kRowsH, kTokH);
+  constexpr uint32_t kIdesc = tc::idesc_f16_f32(kPair ? 2 * kRowsH : kRowsH, kTokT);
+  static_assert(!kWide || kTmD + (uint32_t)kTokT <= kTmColsH, "wide GEMM: one 256-column accumulator beside the A ring");
   constexpr uint16_t kBoth = 0x3;  // CTA mask of a pair
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -250,7 +259,7 @@ __global__ void __launch_bounds__(kThreadsH, 1)
       uint32_t ph = 0;
       bool ok = true;
       for (int t = 0; ok && t < my_tiles; ++t) {
-        const int tok0 = tok_tile(t) * kTokH + (int)rank * kTokLoad;
+        const int tok0 = tok_tile(t) * kTokT + (int)rank * kTokLoad;
         for (int kb = kb_begin(t), kbe = kb_end(t); ok && kb < kbe; ++kb) {
           for (int h = 0; h < 2; ++h, ++hj) {
             if (hj >= kXS && !mbar_wait_bounded(kXempty + 8 * x, ph ^ 1, kSiteGemvEmpty)) {
@@ -285,13 +294,17 @@ __global__ void __launch_bounds__(kThreadsH, 1)
     for (int t = 0; ok && t < my_tiles; ++t) {
       // Folded: D buffer t % 2 holds tile t for its whole K range; it is free
       // once the epilogue has read tile t - 2.
-      if constexpr (kFold) {
+      // Wide: the one accumulator is free once both CTAs' epilogues have read tile t - 1.
+      if constexpr (kWide) {
+        if (t >= 1) ok = tm::warp_wait_cluster(kEfree, (uint32_t)(t - 1) & 1u, kSiteGemvEmpty);
+        if (!ok) break;
+      } else if constexpr (kFold) {
         if (t >= kDRingH) ok = tm::warp_wait(kEfree + 8 * (t & 1), ((t >> 1) & 1) ^ 1, kSiteGemvEmpty);
         if (!ok) break;
       }
       const int kb0 = kb_begin(t), kbe = kb_end(t);
       for (int kb = kb0; ok && kb < kbe; ++kb, ++it) {
-        const int r = it % kARingH, db = kFold ? (t & 1) : (it & 1);
+        const int r = it % kARingH, db = kWide ? 0 : kFold ? (t & 1) : (it & 1);
         ok = kPair ? tm::warp_wait_cluster(kAfull + 8 * r, (it / kARingH) & 1, kSiteGemvFull)
                    : tm::warp_wait(kAfull + 8 * r, (it / kARingH) & 1, kSiteGemvFull);
         // The D buffer is free once the epilogue(s) have read block it - 2.
@@ -313,7 +326,8 @@ __global__ void __launch_bounds__(kThreadsH, 1)
             for (int j = 0; j < 8; ++j) {
               const uint64_t bj = bdesc + (uint64_t)(((j >> 2) * kBoxBytes + (j & 3) * 32u) >> 4);
               if constexpr (kPair) {
-                tc::mma_f16_ts_pair(dcol, acol + (uint32_t)((8 * h + j) * 8), bj, kIdesc, (h | j) != 0);
+                tc::mma_f16_ts_pair(dcol, acol + (uint32_t)((8 * h + j) * 8), bj, kIdesc,
+                                    kFold ? (kb != kb0 || (h | j) != 0) : (h | j) != 0);
               } else {
                 // Folded: accumulate over the tile's K blocks (a fresh sum at its first MMA).
                 tc::mma_f16_ts(dcol, acol + (uint32_t)((8 * h + j) * 8), bj, kIdesc,
@@ -332,7 +346,7 @@ __global__ void __launch_bounds__(kThreadsH, 1)
         if (tm::elect_one()) {
           if constexpr (kPair) {
             tc::commit_pair(kAempty + 8 * r, kBoth);
-            tc::commit_pair(kMdone + 8 * db, kBoth);
+            if (!kFold || kb == kbe - 1) tc::commit_pair(kMdone + 8 * db, kBoth);  // wide: once the tile is summed
           } else {
             tc::commit(kAempty + 8 * r);
             if (!kFold || kb == kbe - 1) tc::commit(kMdone + 8 * db);  // folded: once the tile is summed
@@ -433,6 +447,103 @@ __global__ void __launch_bounds__(kThreadsH, 1)
         }
       }
     }
+  } else if constexpr (kWide) {
+    // -------------------------------------------------------------- epilogue (wide tiles)
+    // Each CTA's 128 rows x 256 tokens leave in two passes of 128 tokens; the
+    // two warps of a lane quadrant take 64 tokens each a pass. The one
+    // accumulator is released (to both CTAs' MMA issuer) after the second
+    // pass's reads.
+    const int e = warp - kEpiWarp0H;
+    const int q = warp & 3;
+    const int h = e >> 2;
+    const int rl = 32 * q + lane;
+    const uint32_t tq0 = tmem + ((uint32_t)(32 * q) << 16) + kTmD + (uint32_t)(h * 64);
+    pdl_wait();  // tok_scale and the output may belong to the previous kernel
+    pdl_launch_dependents();
+    bool ok = true;
+    for (int t = 0; ok && t < my_tiles; ++t) {
+      const int rt = row_tile(t), tt = tok_tile(t);
+      if (!tm::warp_wait(kMdone, (uint32_t)t & 1u, kSiteGemvFull)) break;
+      tc::fence_after_sync();
+      const float rs = ldexpf(1.f, (int)__ldg(p.row_exp + (size_t)rt * kRowsH + rl));
+      const int row = rt * kRowsH + rl;
+      for (int pass = 0; pass < 2; ++pass) {
+        float acc[64];
+#pragma unroll
+        for (int c0 = 0; c0 < 64; c0 += 16) {
+          const uint32_t off[2] = {(uint32_t)c0, (uint32_t)c0 + 8u};
+          float cv[2][8];
+          tc::ld_x8_multi<2>(tq0 + (uint32_t)(pass * kTokH), off, cv);
+#pragma unroll
+          for (int j = 0; j < 2; ++j)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[c0 + 8 * j + i] = cv[j][i] * rs;
+        }
+        if (pass == 1) {
+          tc::fence_before_sync();
+          __syncwarp();
+          if (lane == 0) {
+            if (rank != 0) {
+              mbar_arrive_cluster(lead(kEfree));
+            } else {
+              mbar_arrive(kEfree);
+            }
+          }
+          __syncwarp();
+        }
+        const int tok0 = tt * kTokT + pass * kTokH + h * 64;
+        const float4* ts = reinterpret_cast<const float4*>(p.tok_scale + tok0);
+        if (p.out_tma) {
+          // As the single-CTA epilogue: bf16 tile of 128 tokens in shared memory, one TMA store.
+          const uint32_t ph = (uint32_t)(2 * t + pass) & 1u;
+          if (e == 0 && lane == 0) {
+            bulk_wait_group_read0();
+            mbar_arrive(kOfree);
+          }
+          if (!tm::warp_wait(kOfree, ph, kSiteGemvEmpty)) {
+            ok = false;
+            break;
+          }
+          __nv_bfloat16* stg = reinterpret_cast<__nv_bfloat16*>(ostage) + (size_t)(h * 64) * kRowsH + rl;
+#pragma unroll
+          for (int c = 0; c < 64; c += 4) {
+            const float4 sc = __ldg(ts + c / 4);
+            stg[(size_t)(c + 0) * kRowsH] = __float2bfloat16_rn(acc[c + 0] * sc.x);
+            stg[(size_t)(c + 1) * kRowsH] = __float2bfloat16_rn(acc[c + 1] * sc.y);
+            stg[(size_t)(c + 2) * kRowsH] = __float2bfloat16_rn(acc[c + 2] * sc.z);
+            stg[(size_t)(c + 3) * kRowsH] = __float2bfloat16_rn(acc[c + 3] * sc.w);
+          }
+          fence_proxy_async_shared();  // the TMA store reads the tile through the async proxy
+          __syncwarp();
+          if (lane == 0) mbar_arrive(kOfull);
+          if (e == 0) {
+            if (!tm::warp_wait(kOfull, ph, kSiteGemvFull)) {
+              ok = false;
+              break;
+            }
+            if (lane == 0) {
+              tma_store_2d(&maps.out, rt * kRowsH, tt * kTokT + pass * kTokH, smem_u32(ostage));
+              bulk_commit_group();
+            }
+          }
+          __syncwarp();
+        } else {
+#pragma unroll
+          for (int c = 0; c < 64; c += 4) {
+            const float4 sc = __ldg(ts + c / 4);
+            store_out_h(p, row, tok0 + c + 0, acc[c + 0] * sc.x);
+            store_out_h(p, row, tok0 + c + 1, acc[c + 1] * sc.y);
+            store_out_h(p, row, tok0 + c + 2, acc[c + 2] * sc.z);
+            store_out_h(p, row, tok0 + c + 3, acc[c + 3] * sc.w);
+          }
+        }
+      }
+    }
+    if (p.out_tma && e == 0 && lane == 0) bulk_wait_group0();  // the last tile's store is written
+    tc::fence_before_sync();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(kEdone);
+    __syncwarp();
   } else {
     // -------------------------------------------------------------- epilogue
     const int e = warp - kEpiWarp0H;
@@ -842,9 +953,10 @@ int gemm_f16_pair_max_clusters(int wstages, bool out_stage) {
   return n;
 }
 
-cudaError_t launch_gemm_f16_pair(const GemmF16Params& p, const GemmF16Maps& maps, int clusters, cudaStream_t stream) {
+cudaError_t launch_gemm_f16_pair(const GemmF16Params& p, const GemmF16Maps& maps, int clusters, cudaStream_t stream,
+                                 bool wide) {
   const uint32_t smem = gemm_f16_smem(p.wstages, p.out_tma != 0);
-  const void* kern = (const void*)iq3s_gemm_f16_kernel<true>;
+  const void* kern = wide ? (const void*)iq3s_gemm_f16_kernel<true, true> : (const void*)iq3s_gemm_f16_kernel<true>;
   cudaError_t e = ensure_smem_attribute(kern, smem);
   if (e != cudaSuccess) return e;
   return launch_pdl_cluster(kern, dim3(2 * clusters), dim3(kThreadsH), smem, stream, 2, p, maps);

@@ -346,7 +346,9 @@ size_t x16_quant_smem_bytes(int64_t k);
 bool make_gemm_x16_map(const uint16_t* x16, int64_t ld, int m, int64_t k, int box_tokens, CUtensorMap* map);
 // CTA pairs of the FP16 GEMM that fit on the device at once, and their launch.
 int gemm_f16_pair_max_clusters(int wstages, bool out_stage);
-cudaError_t launch_gemm_f16_pair(const GemmF16Params& p, const GemmF16Maps& maps, int clusters, cudaStream_t stream);
+// wide: the 256 x 256-token tiles of MAMBO_KERNEL_GEMM_F16_WIDE (block scale folded).
+cudaError_t launch_gemm_f16_pair(const GemmF16Params& p, const GemmF16Maps& maps, int clusters, cudaStream_t stream,
+                                 bool wide = false);
 
 // Activation scales [m][K/32] -> atoms [ceil(m/128)][K/128][32][16] (bytes: m_pad * K / 32).
 cudaError_t launch_xs_atoms(const uint8_t* xs, int64_t ldxs, int m, int n_blocks, uint8_t* atoms, cudaStream_t stream);

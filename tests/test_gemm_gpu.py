@@ -289,3 +289,58 @@ def test_folded_full_size_prefill(cuda_device, proj):
     ref = xe @ w.t()
     err = (torch.linalg.norm(out.double() - ref) / torch.linalg.norm(ref)).item()
     assert err < FOLD_FROB_TOL, err
+
+
+GEMM_F16_WIDE = {"kernel": _lib.MAMBO_KERNEL_GEMM_F16_WIDE, "warps": 8, "stages": 4}
+
+
+@pytest.mark.parametrize("m,n,k,outliers", [(32, 256, 512, False), (130, 384, 1024, True), (257, 136, 512, False),
+                                            (300, 256, 2048, True), (513, 520, 1024, True), (64, 1032, 768, False)])
+@pytest.mark.parametrize("stages", [2, 3, 4])
+def test_wide_gemm_within_north_star_bound(cuda_device, m, n, k, outliers, stages):
+    """256 x 256-token tiles on CTA pairs (block scale folded): ragged M and N, a lone last row tile of a
+    pair, token tiles past M; within the folded bound, deterministic, and equal to the single-CTA folded
+    kernel to FP32 rounding."""
+    fields, xq, xs, ref = _case(cuda_device, m, n, k, seed=2100 + m + n + stages, outliers=outliers)
+    cfg = dict(GEMM_F16_WIDE, stages=stages)
+    out = launch_iq3_s_fp8_matmul(xq, xs, fields, config=cfg)
+    got = to_np(out).astype(np.float64)
+    err = O.relative_frobenius(got, ref)
+    assert err < FOLD_FROB_TOL, err
+    np.testing.assert_allclose(got, ref, rtol=4e-3, atol=2e-3 * np.abs(ref).max())
+    assert torch.equal(out, launch_iq3_s_fp8_matmul(xq, xs, fields, config=cfg))  # deterministic
+    fold = launch_iq3_s_fp8_matmul(xq, xs, fields, config=dict(GEMM_F16_FOLD, stages=stages))
+    assert O.relative_frobenius(got, to_np(fold).astype(np.float64)) < 1e-5
+
+
+@pytest.mark.parametrize("m,n,k", [(600, 1024, 1024), (2048, 512, 2048)])
+def test_wide_gemm_bf16_output_is_the_rounded_f32_output(cuda_device, m, n, k):
+    """bf16 output leaves through the staging tile and TMA stores, two per 256-token tile."""
+    fields, xq, xs, _ = _case(cuda_device, m, n, k, seed=2200 + m)
+    f32 = launch_iq3_s_fp8_matmul(xq, xs, fields, config=GEMM_F16_WIDE)
+    b16 = launch_iq3_s_fp8_matmul(xq, xs, fields, config=GEMM_F16_WIDE, out_dtype=torch.bfloat16)
+    assert torch.equal(b16, f32.to(torch.bfloat16))
+
+
+@pytest.mark.parametrize("proj", sorted(LLAMA3_8B))
+def test_wide_full_size_prefill(cuda_device, proj):
+    """Llama-3-8B shapes at M = 2048 with 1 % outlier columns (x50) against a float64 GPU reference."""
+    n, k = LLAMA3_8B[proj]
+    m = 2048
+    gen = torch.Generator(device=cuda_device).manual_seed(2301 + n)
+    raw = torch.randint(0, 256, (n, k // 256, 110), dtype=torch.uint8, device=cuda_device, generator=gen)
+    d = (torch.rand((n, k // 256), device=cuda_device, generator=gen) * 9e-3 + 1e-3).half()
+    raw[..., :2] = d.view(torch.uint8).view(n, k // 256, 2)
+    fields = prepare_iq3_s_fields(raw)
+    x = torch.randn((m, k), device=cuda_device, generator=gen)
+    x[:, torch.randperm(k, device=cuda_device, generator=gen)[: round(0.01 * k)]] *= 50.0
+    xq, xs = launch_quantize_fp8(x.to(torch.bfloat16))
+    out = launch_iq3_s_fp8_matmul(xq, xs, fields, config=GEMM_F16_WIDE)
+    bits, scales = launch_dequant_iq3_s(fields)
+    lut = torch.from_numpy(O.decode_e4m3(np.arange(256, dtype=np.uint8))).to(cuda_device)
+    w = (lut[bits.long()] * scales.repeat_interleave(32, dim=1)).double()
+    del bits, scales
+    xe = lut[xq.long()].double() * torch.exp2(xs.double() - 127).repeat_interleave(32, dim=1)
+    ref = xe @ w.t()
+    err = (torch.linalg.norm(out.double() - ref) / torch.linalg.norm(ref)).item()
+    assert err < FOLD_FROB_TOL, err
