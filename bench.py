@@ -384,7 +384,7 @@ def prefill_block(torch, dev, ms=PREFILL_MS) -> dict:
         del raw, d
     per_m = []
     for m in ms:
-        rows, flop_tot, us_tot, gemm_us_tot, fold_us_tot = [], 0, 0.0, 0.0, 0.0
+        rows, flop_tot, us_tot, gemm_us_tot, fold_us_tot, wide_us_tot = [], 0, 0.0, 0.0, 0.0, 0.0
         for i, (name, n, k) in enumerate(PREFILL_SHAPES):
             gen = torch.Generator(device=dev).manual_seed(0x51A + 100 * i + m)
             x = torch.randn((m, k), device=dev, generator=gen)
@@ -401,17 +401,23 @@ def prefill_block(torch, dev, ms=PREFILL_MS) -> dict:
             fold_cfg = dict(cfg, kernel=_lib.MAMBO_KERNEL_GEMM_F16_FOLD) if cfg.get("kernel") != \
                 _lib.MAMBO_KERNEL_GEMM_F16_PAIR else {"kernel": _lib.MAMBO_KERNEL_GEMM_F16_FOLD, "stages": 4}
             fold_us = timed(lambda: fused_linear_into(xb, fields, out, config=fold_cfg))
+            # The wide variant (CTA pairs, 256 x 256-token tiles, d folded as above).
+            wide_cfg = {"kernel": _lib.MAMBO_KERNEL_GEMM_F16_WIDE, "warps": 8, "stages": 4}
+            wide_us = timed(lambda: fused_linear_into(xb, fields, out, config=wide_cfg))
             flop = 2 * m * n * k
             rows.append({"proj": name, "n": n, "k": k, "us": round(us, 1), "tflops": round(flop / us / 1e6, 1),
                          "gemm_us": round(gemm_us, 1), "gemm_tflops": round(flop / gemm_us / 1e6, 1),
-                         "folded_us": round(fold_us, 1), "folded_tflops": round(flop / fold_us / 1e6, 1)})
+                         "folded_us": round(fold_us, 1), "folded_tflops": round(flop / fold_us / 1e6, 1),
+                         "wide_us": round(wide_us, 1), "wide_tflops": round(flop / wide_us / 1e6, 1)})
             flop_tot += flop
             us_tot += us
             gemm_us_tot += gemm_us
             fold_us_tot += fold_us
+            wide_us_tot += wide_us
             del xb, xq, xs, out
         per_m.append({"m": m, "tflops": flop_tot / us_tot / 1e6, "gemm_tflops": flop_tot / gemm_us_tot / 1e6,
-                      "folded_tflops": flop_tot / fold_us_tot / 1e6, "per_shape": rows})
+                      "folded_tflops": flop_tot / fold_us_tot / 1e6, "wide_tflops": flop_tot / wide_us_tot / 1e6,
+                      "per_shape": rows})
     del weights, flush
     torch.cuda.empty_cache()
     peak, kind = measure_fp8_peak(torch, dev)
@@ -419,11 +425,15 @@ def prefill_block(torch, dev, ms=PREFILL_MS) -> dict:
         r["frac"] = r["tflops"] / peak if peak else None
         r["gemm_frac"] = r["gemm_tflops"] / peak if peak else None
         r["folded_frac"] = r["folded_tflops"] / peak if peak else None
+        r["wide_frac"] = r["wide_tflops"] / peak if peak else None
     head = next(r for r in per_m if r["m"] == 2048) if 2048 in ms else per_m[0]
     return {"m": head["m"], "tflops": head["tflops"], "unit": "TFLOP/s", "peak_tflops": peak, "peak_kind": kind,
             "frac": head["frac"], "per_m": per_m,
             "timed": "tflops: bf16 activations -> MXFP8 quantization -> GEMM -> bf16 output, one public call "
-                     "(fused_linear_into) per shape; gemm_tflops: the GEMM alone on prequantized activations",
+                     "(fused_linear_into) per shape; gemm_tflops: the GEMM alone on prequantized activations; "
+                     "folded_tflops / wide_tflops: the same call with MAMBO_KERNEL_GEMM_F16_FOLD / _WIDE (block "
+                     "scale folded into the FP16 weights, within the 1e-3 bound; wide: CTA pairs, 256 x 256-token "
+                     "tiles)",
             "kernel": "iq3s_gemm_f16_kernel (FP16 operands, group scale folded exactly into the weights)",
             "l2": "flushed (256 MB write) before each timed launch"}
 
