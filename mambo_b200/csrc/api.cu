@@ -1111,6 +1111,24 @@ int group_nt(const MamboLinearItem* items, int count) {
 
 size_t group_partial_bytes(int nt, int sms) { return align256((size_t)sms * 2 * 128 * 8 * nt * sizeof(float)); }
 
+// A grouped launch quantizes its activations in a pre-pass (launch_group_xtiles)
+// when an item has two or more tokens: the GEMV's activation warps would
+// otherwise quantize every K block once per row tile, and from two tokens that
+// work paces the pipeline (grouped launches of 8 tokens took 1.23 times as long
+// per unit as those of one). One-token groups keep the quantization in the GEMV.
+bool group_prequantize(const MamboLinearItem* items, int count) {
+  for (int i = 0; i < count; ++i)
+    if (items[i].m >= 2) return true;
+  return false;
+}
+// The pre-pass's activation tiles: one per item and K block.
+size_t group_xtiles_bytes(const MamboLinearItem* items, int count) {
+  if (!group_prequantize(items, count)) return 0;
+  size_t tiles = 0;
+  for (int i = 0; i < count; ++i) tiles += (size_t)items[i].w->n_blocks;
+  return align256(tiles * gemv_xtile_bytes(group_nt(items, count)));
+}
+
 // Estimated time of one (128-row tile, K block) unit of a grouped launch
 // item with m tokens, in thousandths of a one-token unit. It grows with the
 // activation warps' passes over the unit's bf16 block (from two tokens a lane
@@ -1123,20 +1141,22 @@ int64_t group_item_units(const GemvItem& gi) { return (int64_t)((gi.n_rows + 127
 
 // First unit of each CTA of a grouped launch (start[grid] = units): contiguous
 // ranges of about equal estimated time, at least one unit each (grid <= units).
-void split_group_units(const GemvGroup& g, int units, int grid, int* start) {
+// uniform: every unit costs the same (the activations were quantized beforehand).
+void split_group_units(const GemvGroup& g, int units, int grid, int* start, bool uniform) {
+  auto cost = [uniform](int m) -> int64_t { return uniform ? 1000 : group_unit_cost(m); };
   int64_t total = 0;
-  for (int i = 0; i < g.count; ++i) total += group_item_units(g.items[i]) * group_unit_cost(g.items[i].m);
+  for (int i = 0; i < g.count; ++i) total += group_item_units(g.items[i]) * cost(g.items[i].m);
   start[0] = 0;
   int item = 0;
   int64_t before = 0;  // cost of the units of the items ahead of `item`
   for (int c = 1; c < grid; ++c) {
     const int64_t target = total * c / grid;
     while (item + 1 < g.count &&
-           before + group_item_units(g.items[item]) * group_unit_cost(g.items[item].m) <= target) {
-      before += group_item_units(g.items[item]) * group_unit_cost(g.items[item].m);
+           before + group_item_units(g.items[item]) * cost(g.items[item].m) <= target) {
+      before += group_item_units(g.items[item]) * cost(g.items[item].m);
       ++item;
     }
-    const int64_t cu = group_unit_cost(g.items[item].m);
+    const int64_t cu = cost(g.items[item].m);
     // Rounded down, as a single linear's even split is: a group of one splits the same way.
     const int64_t u = g.items[item].unit0 + (target - before) / cu;
     const int64_t lo = start[c - 1] + 1, hi = units - (grid - c);
@@ -1155,6 +1175,9 @@ size_t mambo_iq3s_linear_group_workspace_bytes(const MamboLinearItem* items, int
   DeviceInfo info = device_info(&st);
   const int sms = (st == MAMBO_OK && info.sms > 0) ? info.sms : 148;
   size_t need = kCounterBytes + group_partial_bytes(group_nt(items, count), sms);
+  bool have_w = true;
+  for (int i = 0; i < count; ++i) have_w = have_w && items[i].w != nullptr;
+  if (have_w && group_fusable(items, count)) need += group_xtiles_bytes(items, count);
   for (int i = 0; i < count; ++i) {  // the per-item path, when the group does not qualify
     if (!items[i].w) continue;
     const size_t b = mambo_iq3s_linear_fused_workspace_bytes(items[i].m, items[i].w->n_rows, items[i].w->n_blocks,
@@ -1204,13 +1227,14 @@ int mambo_iq3s_linear_group_q(const MamboLinearItem* items, const MamboQuantOut*
     return ok();
   }
   const int nt = group_nt(items, count);
-  const size_t need = kCounterBytes + group_partial_bytes(nt, info.sms);
+  const bool pre = group_prequantize(items, count);
+  const size_t need = kCounterBytes + group_partial_bytes(nt, info.sms) + group_xtiles_bytes(items, count);
   if (workspace_bytes < need)
     return fail(MAMBO_EWORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
   GemvGroup g;
   std::memset(&g, 0, sizeof(g));
   g.count = count;
-  int units = 0, tiles = 0, box = 8 * nt;
+  int units = 0, tiles = 0, box = 8 * nt, xtiles = 0;
   for (int i = 0; i < count; ++i) {
     const MamboLinearItem& it = items[i];
     const MamboIQ3SWeight* w = it.w;
@@ -1227,6 +1251,8 @@ int mambo_iq3s_linear_group_q(const MamboLinearItem* items, const MamboQuantOut*
     gi.out_bf16 = it.out_dtype == MAMBO_BF16;
     gi.unit0 = units;
     gi.tile0 = tiles;
+    gi.xt0 = xtiles;
+    xtiles += gi.n_blocks;
     if (qouts && want_qout(&qouts[i])) {  // N % 32 == 0 was checked: the epilogue quantizes the output
       gi.q_out = qouts[i].q;
       gi.ldq = qouts[i].ldq;
@@ -1257,7 +1283,31 @@ int mambo_iq3s_linear_group_q(const MamboLinearItem* items, const MamboQuantOut*
   p.total_units = units;
   int grid = units < info.sms ? units : info.sms;
   if (grid > kGemvMaxGrid) grid = kGemvMaxGrid;
-  split_group_units(g, units, grid, g.cta_start);
+  split_group_units(g, units, grid, g.cta_start, pre);
+  if (pre) {
+    // The pre-pass writes every item's activation tiles after the partials;
+    // the GEMV (launched with programmatic serialization) starts its weight
+    // stream while the pre-pass runs and reads the tiles after it.
+    uint8_t* xt = (uint8_t*)workspace + kCounterBytes + group_partial_bytes(nt, info.sms);
+    GroupXtilesParams xp;
+    std::memset(&xp, 0, sizeof(xp));
+    xp.count = count;
+    xp.total_tiles = xtiles;
+    xp.box = box;
+    xp.tiles = xt;
+    for (int i = 0; i < count; ++i)
+      xp.items[i] = GroupXtilesParams::Item{g.items[i].x, g.items[i].ldx, g.items[i].m, g.items[i].n_blocks,
+                                            g.items[i].xt0};
+    cudaError_t e = launch_group_xtiles(xp, (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(e, "group_xtiles_kernel");
+    GemvGroupPre gp;
+    std::memset(&gp, 0, sizeof(gp));
+    static_cast<GemvGroup&>(gp) = g;
+    gp.xtiles = xt;
+    e = launch_gemv_tm_group_pre(p, gp, nt, grid, (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(e, "iq3s_gemv_tm_kernel (group, quantized beforehand)");
+    return ok();
+  }
   cudaError_t e = launch_gemv_tm_group(p, g, nt, kGroupDecWarps, grid, (cudaStream_t)stream);
   if (e != cudaSuccess) return cuda_fail(e, "iq3s_gemv_tm_kernel (group)");
   return ok();

@@ -354,7 +354,8 @@ template <int NT, int kDecWarps, class G, bool kQ, bool kQ4K = false>
 __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
     iq3s_gemv_tm_kernel(const __grid_constant__ GemvTmParams p, const __grid_constant__ GemvTmMaps maps,
                         const __grid_constant__ G grp) {
-  constexpr bool kGroup = std::is_same<G, GemvGroup>::value;
+  constexpr bool kPre = std::is_same<G, GemvGroupPre>::value;  // a group with its activation tiles made beforehand
+  constexpr bool kGroup = std::is_same<G, GemvGroup>::value || kPre;
   constexpr bool kAR = std::is_same<G, GemvAr>::value;  // row split with its all-reduce fused
   constexpr int TOK = 8 * NT;             // tokens the epilogue keeps
   constexpr int NM = tm_nmma(NT);         // MMA N
@@ -384,7 +385,7 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
   const TmLayout L = tm_layout(NT, kQ4K);
   constexpr uint32_t kTableRegion = kQ4K ? 0u : (uint32_t)kTableBytes;  // no codebook for Q4_K
   constexpr uint32_t kRecBytes = kQ4K ? kQ4kRecordBytes : (uint32_t)kRecordBytes;
-  static_assert(!(kQ4K && (kQ || std::is_same<G, GemvGroup>::value)), "Q4_K runs single linears only");
+  static_assert(!(kQ4K && (kQ || kGroup)), "Q4_K runs single linears only");
   // The codebook sits at the start of dynamic shared memory (a link-time
   // constant address); the stages follow, aligned to 1024 bytes at run time.
   // (Offsets from smem_raw keep the pointers in the shared address space, so
@@ -572,6 +573,42 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
   // copies need one warp; fused quantization takes both, every other unit.
   if (warp >= kXWarp0) {
     const int xw = warp - kXWarp0;
+    if constexpr (kPre) {
+      // Tiles quantized by the pre-pass: three bulk copies per unit (the B
+      // tile and the rows of both scale blocks) complete the slot's barrier;
+      // the two warps take alternate units, following their item with a
+      // forward cursor.
+      pdl_wait();
+      int l = group_item(grp, u0 + xw, 0);
+      int v = u0 + xw - grp.items[l].unit0, nb = grp.items[l].n_blocks;
+      int units = ((grp.items[l].n_rows + kRows - 1) / kRows) * nb;
+      int kb = v % nb;
+      for (int j = xw; j < n_units; j += 2) {
+        const int x = j % AS;
+        if (j >= AS && !__all_sync(0xFFFFFFFFu, mbar_wait_bounded(kXempty + 8 * x, ((j / AS) & 1) ^ 1, kSiteGemvEmpty)))
+          return;
+        if (lane == 0) {
+          const uint8_t* src = grp.xtiles + (size_t)(grp.items[l].xt0 + kb) * gemv_xtile_bytes(NT);
+          const uint32_t dst = smem_u32(x0 + (size_t)x * L.xslot), full = kXfull + 8 * x;
+          mbar_arrive_expect_tx(full, gemv_xtile_bytes(NT));
+          bulk_load(dst + L.b, src, 256u * BOX, full);
+          bulk_load(dst + L.xs, src + 256u * BOX, 16u * BOX, full);
+          bulk_load(dst + L.xs + 512u, src + 272u * BOX, 16u * BOX, full);
+        }
+        __syncwarp();
+        v += 2;
+        kb += 2;
+        while (kb >= nb) kb -= nb;
+        while (v >= units && l + 1 < grp.count) {  // into the next item
+          v -= units;
+          ++l;
+          nb = grp.items[l].n_blocks;
+          units = ((grp.items[l].n_rows + kRows - 1) / kRows) * nb;
+          kb = v % nb;
+        }
+      }
+      return;
+    }
     const bool fused = kGroup || p.x_bf16 != nullptr;
     if (xw != 0 && !fused) return;
     const uint64_t keep = l2_policy_evict_last();  // every CTA reads them
@@ -1295,6 +1332,10 @@ template <int NT, int kDecWarps, bool kQ = false>
 static const void* tm_kernel_group() {
   return (const void*)iq3s_gemv_tm_kernel<NT, kDecWarps, GemvGroup, kQ>;
 }
+template <int NT, bool kQ = false>
+static const void* tm_kernel_group_pre() {
+  return (const void*)iq3s_gemv_tm_kernel<NT, 8, GemvGroupPre, kQ>;
+}
 
 static int query_max_clusters(int nt, int dec_warps, int stages, int kparts, bool q4k);
 
@@ -1371,6 +1412,30 @@ static cudaError_t launch_gemv_tm_group_t(const GemvTmParams& p, const GemvGroup
   GemvTmMaps maps;
   std::memset(&maps, 0, sizeof(maps));
   return launch_pdl_cluster(kern, dim3(grid), dim3(tm_threads(8)), smem, stream, 1, p, maps, g);
+}
+
+template <int NT>
+static cudaError_t launch_gemv_tm_group_pre_t(const GemvTmParams& p, const GemvGroupPre& g, int grid,
+                                              cudaStream_t stream) {
+  const uint32_t smem = tm_smem_bytes(NT, p.stages, 0, true);
+  bool quant = false;  // some item also writes its output's MXFP8 quantization
+  for (int i = 0; i < g.count; ++i) quant = quant || g.items[i].q_out != nullptr;
+  const void* kern = quant ? tm_kernel_group_pre<NT, true>() : tm_kernel_group_pre<NT, false>();
+  cudaError_t e = ensure_smem_attribute(kern, smem);
+  if (e != cudaSuccess) return e;
+  GemvTmMaps maps;
+  std::memset(&maps, 0, sizeof(maps));
+  return launch_pdl_cluster(kern, dim3(grid), dim3(tm_threads(8)), smem, stream, 1, p, maps, g);
+}
+
+cudaError_t launch_gemv_tm_group_pre(const GemvTmParams& p, const GemvGroupPre& g, int nt, int grid,
+                                     cudaStream_t stream) {
+  if (p.kparts != 0) return cudaErrorInvalidValue;
+  switch (nt) {
+    case 1: return launch_gemv_tm_group_pre_t<1>(p, g, grid, stream);
+    case 2: return launch_gemv_tm_group_pre_t<2>(p, g, grid, stream);
+    default: return launch_gemv_tm_group_pre_t<4>(p, g, grid, stream);
+  }
 }
 
 cudaError_t launch_gemv_tm_group(const GemvTmParams& p, const GemvGroup& g, int nt, int dec_warps, int grid,

@@ -209,6 +209,7 @@ struct GemvItem {
   int out_bf16;
   int unit0;  // first unit of this item in the launch's numbering
   int tile0;  // first row tile of this item in the launch's numbering
+  int xt0;    // GemvGroupPre: first activation tile of this item (one per K block)
   uint8_t* q_out;  // optional MXFP8 quantization of out (as GemvTmParams::q_out)
   int64_t ldq;
   uint8_t* s_out;
@@ -225,6 +226,36 @@ struct GemvGroup {
   // unit's cost grows with its item's token count. Strictly increasing.
   int cta_start[kGemvMaxGrid + 1];
 };
+// A grouped launch whose activations a pre-pass quantized (launch_group_xtiles):
+// per item and K block one tile at xtiles + (items[l].xt0 + kb) * gemv_xtile_bytes(NT),
+// laid out as the GEMV's activation slot needs it; the GEMV's activation warps
+// only copy tiles (three bulk copies per unit) instead of quantizing every
+// K block once per row tile.
+struct GemvGroupPre : GemvGroup {
+  const uint8_t* xtiles;
+};
+// Bytes of one activation tile: the B tile [16 K chunks][8*NT tokens][16 bytes]
+// (E4M3), then the rows of the two scale blocks ([8*NT tokens][16 bytes] each,
+// groups 0-3 / 4-7 of the K block in bytes 0-3).
+__host__ __device__ constexpr uint32_t gemv_xtile_bytes(int nt) { return 288u * 8u * (uint32_t)nt; }
+// The pre-pass: bf16 rows of every item -> its activation tiles, the standalone
+// quantizer's arithmetic (round to nearest even). Rows past an item's M are
+// left as they are (their products are never read).
+struct GroupXtilesParams {
+  struct Item {
+    const uint16_t* x;
+    int64_t ldx;
+    int m;
+    int n_blocks;
+    int xt0;
+  } items[kGemvMaxItems];
+  int count;
+  int total_tiles;
+  int box;  // token rows of a tile (8*NT)
+  uint8_t* tiles;
+};
+cudaError_t launch_group_xtiles(const GroupXtilesParams& p, cudaStream_t stream);
+
 // The single-linear launch's stand-in for GemvGroup.
 struct GemvNoGroup {
   int count;
@@ -250,6 +281,8 @@ cudaError_t launch_gemv_tm_ar(const GemvTmParams& p, const GemvAr& ar, int nt, c
 // Grouped launch (stream-K over the concatenated units of every item).
 cudaError_t launch_gemv_tm_group(const GemvTmParams& p, const GemvGroup& g, int nt, int dec_warps, int grid,
                                  cudaStream_t stream);
+cudaError_t launch_gemv_tm_group_pre(const GemvTmParams& p, const GemvGroupPre& g, int nt, int grid,
+                                     cudaStream_t stream);
 
 // Activation map for the tcgen05 GEMV; false when xq is not 16-byte aligned
 // with a row stride that is a multiple of 16.

@@ -173,4 +173,34 @@ cudaError_t launch_quantize_mxfp8(const QuantParams& p, int x_dtype, int roundin
              : launch_quant_t<float, false>(p, rounding, (int)blocks, stream);
 }
 
+// Activation tiles of a grouped GEMV launch (GemvGroupPre): one CTA per
+// (item, K block), one warp per token. Lane 4g + j takes values 8j .. 8j+7 of
+// 32-value group g, so a quad holds a group, as quantize_mxfp8_kernel's lanes
+// do, and writes its 8 E4M3 bytes where the GEMV's B tile keeps them (K chunk
+// 2g + j/2 of 16 values, token row t); lane 4g writes the scale code into row t
+// of scale block g/4, byte g%4.
+__global__ void __launch_bounds__(256) group_xtiles_kernel(const __grid_constant__ GroupXtilesParams p) {
+  pdl_wait();  // the activations may come from the previous kernel
+  pdl_launch_dependents();
+  const int tile = blockIdx.x;
+  int l = 0;
+  while (l + 1 < p.count && p.items[l + 1].xt0 <= tile) ++l;
+  const GroupXtilesParams::Item& it = p.items[l];
+  const int kb = tile - it.xt0;
+  uint8_t* dst = p.tiles + (size_t)tile * (size_t)(288 * p.box);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, j = lane & 3;
+  for (int t = warp; t < it.m; t += 8) {
+    const uint4 c = __ldg(reinterpret_cast<const uint4*>(it.x + (size_t)t * it.ldx + (size_t)kb * 256 + g * 32 + j * 8));
+    uint2 q;
+    const uint32_t code = mxfp8_quad_bf16_rne(c, q);
+    *reinterpret_cast<uint2*>(dst + ((2 * g + (j >> 1)) * p.box + t) * 16 + (j & 1) * 8) = q;
+    if (j == 0) dst[256 * p.box + (g >> 2) * 16 * p.box + t * 16 + (g & 3)] = (uint8_t)code;
+  }
+}
+
+cudaError_t launch_group_xtiles(const GroupXtilesParams& p, cudaStream_t stream) {
+  if (p.total_tiles < 1) return cudaSuccess;
+  return launch_pdl((const void*)group_xtiles_kernel, dim3((unsigned)p.total_tiles), dim3(256), 0, stream, p);
+}
+
 }  // namespace mambo
