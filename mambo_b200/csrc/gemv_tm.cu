@@ -1191,15 +1191,36 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
             for (int j = 0; j < GB; ++j) off[j] = (uint32_t)((g0 + j) * NM + t0);
             float c[GB][8];
             tc::ld_x8_multi<GB>(tq, off, c);
+            if constexpr (kGroup) {
+              // Grouped launches (items of 1 to 8 tokens): the group factors first, then one
+              // warp-uniform branch per token pair. (Single linears keep the loop below; the
+              // same order would cost them 2-3 % in code layout, measured.)
+              float wv[GB];
   #pragma unroll
-            for (int j = 0; j < GB; ++j) {
-              const int g = g0 + j;
-              const float w = fmaf(__uint_as_float(prmt((g & 1) ? tb1 : tb0, 0x4B000000u, 0x7650u | (uint32_t)(g >> 1))),
-                                   dv, dneg);
+              for (int j = 0; j < GB; ++j) {
+                const int g = g0 + j;
+                wv[j] = fmaf(__uint_as_float(prmt((g & 1) ? tb1 : tb0, 0x4B000000u, 0x7650u | (uint32_t)(g >> 1))),
+                             dv, dneg);
+              }
   #pragma unroll
               for (int t = 0; t < 8; t += 2) {
-                if (t0 + t < ov.m)  // tokens past M are padding (warp-uniform branch)
-                  fma2(acc[t0 + t], acc[t0 + t + 1], c[j][t], c[j][t + 1], w, w);
+                if (t0 + t < ov.m) {
+  #pragma unroll
+                  for (int j = 0; j < GB; ++j)
+                    fma2(acc[t0 + t], acc[t0 + t + 1], c[j][t], c[j][t + 1], wv[j], wv[j]);
+                }
+              }
+            } else {
+  #pragma unroll
+              for (int j = 0; j < GB; ++j) {
+                const int g = g0 + j;
+                const float w = fmaf(__uint_as_float(prmt((g & 1) ? tb1 : tb0, 0x4B000000u, 0x7650u | (uint32_t)(g >> 1))),
+                                     dv, dneg);
+  #pragma unroll
+                for (int t = 0; t < 8; t += 2) {
+                  if (t0 + t < ov.m)  // tokens past M are padding (warp-uniform branch)
+                    fma2(acc[t0 + t], acc[t0 + t + 1], c[j][t], c[j][t + 1], w, w);
+                }
               }
             }
           }
