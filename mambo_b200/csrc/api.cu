@@ -161,6 +161,13 @@ int gemv_nt_for(int64_t m) { return m <= 8 ? 1 : (m <= 16 ? 2 : 4); }
 constexpr int kSmemOptinDefault = 232448;
 
 int kernel_of(const MamboLinearConfig& c) { return c.kernel == MAMBO_KERNEL_AUTO ? MAMBO_KERNEL_GEMV : c.kernel; }
+// All five SoA fields are present.
+bool has_soa(const MamboIQ3SWeight* w) { return w->d && w->qs && w->qh && w->signs && w->scales; }
+// A weight the linears can use: d and scales, and either the packed copy (the
+// tcgen05 kernels read only it) or the remaining SoA fields.
+bool weight_fields_ok(const MamboIQ3SWeight* w) {
+  return w->d && w->scales && (w->packed || (w->qs && w->qh && w->signs));
+}
 // The FP16-operand GEMM, on single CTAs or on CTA pairs.
 bool is_gemm_f16(int kind) {
   return kind == MAMBO_KERNEL_GEMM_F16 || kind == MAMBO_KERNEL_GEMM_F16_PAIR || kind == MAMBO_KERNEL_GEMM_F16_FOLD ||
@@ -711,6 +718,7 @@ int mambo_iq3s_pack(const MamboIQ3SWeight* w, void* packed, mambo_stream_t strea
 int mambo_iq3s_decode(const MamboIQ3SWeight* w, const uint32_t* fp8_table, uint8_t* values, float* scales,
                       mambo_stream_t stream) {
   if (!w || !fp8_table || !values || !scales) return fail(MAMBO_EINVAL, "null pointer");
+  if (!has_soa(w)) return fail(MAMBO_EINVAL, "the decoder reads the SoA weight fields, which this weight does not carry");
   if (w->n_rows < 1 || w->n_blocks < 1) return fail(MAMBO_EINVAL, "IQ3_S weight must have positive N and K");
   if ((uintptr_t)values % 8) return fail(MAMBO_EINVAL, "values must be 8-byte aligned");
   DeviceInfo info;
@@ -850,7 +858,7 @@ int linear_impl(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t ldxs
                 const uint32_t* fp8_table, void* out, int out_dtype, int64_t ldo, const MamboQuantOut* qo,
                 const MamboLinearConfig* cfg, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   if (!xq || !xs || !w || !fp8_table || !out) return fail(MAMBO_EINVAL, "null pointer");
-  if (!w->d || !w->qs || !w->qh || !w->signs || !w->scales) return fail(MAMBO_EINVAL, "null weight field");
+  if (!weight_fields_ok(w)) return fail(MAMBO_EINVAL, "null weight field");
   if (w->n_rows < 1 || w->n_blocks < 1) return fail(MAMBO_EINVAL, "IQ3_S weight must have positive N and K");
   if (w->n_rows > (1 << 30) || w->n_blocks > (1 << 20)) return fail(MAMBO_EINVAL, "weight too large");
   const int64_t k = w->n_blocks * 256;
@@ -923,6 +931,8 @@ int linear_impl(const uint8_t* xq, int64_t ldxq, const uint8_t* xs, int64_t ldxs
       if (st != MAMBO_OK) return st;
       continue;
     }
+    if (!has_soa(w))
+      return fail(MAMBO_EINVAL, "MAMBO_KERNEL_GEMV_SYNC reads the SoA weight fields, which this weight does not carry");
     GemvParams mp{};
     mp.n_rows = (int)w->n_rows;
     mp.n_blocks = (int)w->n_blocks;
@@ -997,7 +1007,7 @@ int fused_impl(const void* x, int x_dtype, int64_t ldx, int64_t m, const MamboIQ
                void* out, int out_dtype, int64_t ldo, const MamboQuantOut* qo, const MamboLinearConfig* cfg,
                void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   if (!x || !w || !fp8_table || !out) return fail(MAMBO_EINVAL, "null pointer");
-  if (!w->d || !w->qs || !w->qh || !w->signs || !w->scales) return fail(MAMBO_EINVAL, "null weight field");
+  if (!weight_fields_ok(w)) return fail(MAMBO_EINVAL, "null weight field");
   if (w->n_rows < 1 || w->n_blocks < 1) return fail(MAMBO_EINVAL, "IQ3_S weight must have positive N and K");
   if (w->n_rows > (1 << 30) || w->n_blocks > (1 << 20)) return fail(MAMBO_EINVAL, "weight too large");
   if (x_dtype != MAMBO_F32 && x_dtype != MAMBO_BF16) return fail(MAMBO_EINVAL, "activation must be f32 or bf16");
@@ -1201,7 +1211,7 @@ int mambo_iq3s_linear_group_q(const MamboLinearItem* items, const MamboQuantOut*
     const MamboLinearItem& it = items[i];
     const MamboIQ3SWeight* w = it.w;
     if (!it.x || !w || !it.out) return fail(MAMBO_EINVAL, "item %d: null pointer", i);
-    if (!w->d || !w->qs || !w->qh || !w->signs || !w->scales) return fail(MAMBO_EINVAL, "item %d: null weight field", i);
+    if (!weight_fields_ok(w)) return fail(MAMBO_EINVAL, "item %d: null weight field", i);
     if (w->n_rows < 1 || w->n_blocks < 1 || w->n_rows > (1 << 30) || w->n_blocks > (1 << 20))
       return fail(MAMBO_EINVAL, "item %d: IQ3_S weight must have positive N and K", i);
     if (it.x_dtype != MAMBO_F32 && it.x_dtype != MAMBO_BF16)
@@ -1377,7 +1387,7 @@ extern "C" int mambo_iq3s_linear_noalloc(const uint8_t* xq, int64_t ldxq, const 
                                          int out_dtype, int64_t ldo, const MamboLinearConfig* cfg,
                                          mambo_stream_t stream) {
   if (!xq || !xs || !w || !fp8_table || !out) return fail(MAMBO_EINVAL, "null pointer");
-  if (!w->d || !w->qs || !w->qh || !w->signs || !w->scales) return fail(MAMBO_EINVAL, "null weight field");
+  if (!weight_fields_ok(w)) return fail(MAMBO_EINVAL, "null weight field");
   if (w->n_rows < 1 || w->n_blocks < 1) return fail(MAMBO_EINVAL, "IQ3_S weight must have positive N and K");
   const int64_t k = w->n_blocks * 256;
   if (m < 1) return fail(MAMBO_EINVAL, "x_values must be uint8 [M,K] with M >= 1");
@@ -1741,8 +1751,7 @@ int mambo_iq3s_linear_fused_ar(const void* x, int x_dtype, int64_t ldx, int64_t 
                                mambo_stream_t stream) {
   if (!x || !w || !fp8_table || !out || !comm) return fail(MAMBO_EINVAL, "null pointer");
   if (!comm->connected) return fail(MAMBO_EINVAL, "communicator not connected");
-  if (!w->d || !w->qs || !w->qh || !w->signs || !w->scales || !w->packed)
-    return fail(MAMBO_EINVAL, "the fused all-reduce needs the packed weight copy");
+  if (!weight_fields_ok(w) || !w->packed) return fail(MAMBO_EINVAL, "the fused all-reduce needs the packed weight copy");
   if (x_dtype != MAMBO_BF16) return fail(MAMBO_EINVAL, "the fused all-reduce takes bf16 activations");
   if (m < 1 || m >= kGemmMinTokens) return fail(MAMBO_EINVAL, "the fused all-reduce takes 1 to %d tokens",
                                                  kGemmMinTokens - 1);

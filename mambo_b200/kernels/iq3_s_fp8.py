@@ -164,6 +164,8 @@ def launch_dequant_iq3_s(iq3_weight: IQ3SFields, *, tile_n: int = 1, stream=None
     """Return [N,K] E4M3 bit patterns and [N,K/32] original F32 scales (iq3_s_fp8.py:341-351)."""
     _power_of_two(tile_n, "tile_n")
     n_rows, blocks = _weight_dimensions(iq3_weight)
+    if iq3_weight.qs.numel() == 0:
+        raise ValueError("the decoder reads the SoA fields, which a weight prepared with soa=False does not keep")
     w = weight_struct(iq3_weight)
     dev = iq3_weight.d.device
     _runtime.require_device(dev)

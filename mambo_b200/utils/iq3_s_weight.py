@@ -43,13 +43,18 @@ class IQ3SFields:
     packed: torch.Tensor | None = None
 
 
-def prepare_iq3_s_fields(iq3_weight, *, stream=None, packed: bool = True) -> IQ3SFields:
+def prepare_iq3_s_fields(iq3_weight, *, stream=None, packed: bool = True, soa: bool = True) -> IQ3SFields:
     """Split GGUF uint8 [N,B,110] blocks into aligned SoA fields once (iq3_s_weight.py:25-54).
 
     Accepts any strides and address alignment of the source view. The copy is
     outside kernel timing. With ``packed`` (and N % 8 == 0) it also builds the
     tile-major copy the tcgen05 GEMV streams with one copy per work unit; that
-    doubles the weight memory.
+    doubles the weight memory. ``soa=False`` (needs ``packed`` and N % 8 == 0)
+    keeps only the packed copy plus the small d and scales fields: qs, qh and
+    signs become empty [B,N,0] tensors (104 of the 110 bytes per block freed).
+    Every linear runs on such a weight; the standalone decoder
+    (launch_dequant_iq3_s) and the legacy MAMBO_KERNEL_GEMV_SYNC kernel need
+    the SoA fields and raise.
     """
     raw = _runtime.as_cuda_tensor(iq3_weight)
     if raw.ndim != 3 or raw.dtype != torch.uint8 or raw.shape[2] != 110:
@@ -57,6 +62,8 @@ def prepare_iq3_s_fields(iq3_weight, *, stream=None, packed: bool = True) -> IQ3
     n, blocks, _ = raw.shape
     if n < 1 or blocks < 1:
         raise ValueError("IQ3_S weight must have positive N and K")
+    if not soa and (not packed or n % 8):
+        raise ValueError("soa=False keeps only the packed copy: it needs packed=True and N % 8 == 0")
     dev = raw.device
     _runtime.require_device(dev)
     mk = lambda *shape: torch.empty(shape, dtype=torch.uint8, device=dev)  # noqa: E731
@@ -79,7 +86,18 @@ def prepare_iq3_s_fields(iq3_weight, *, stream=None, packed: bool = True) -> IQ3
     )
     if packed and n % 8 == 0:
         fields = pack_iq3_s_fields(fields, stream=stream)
+    if not soa:
+        # The packed copy holds every byte; keep d and scales (dimensions, C-ABI checks) and free the rest.
+        fields = dataclasses.replace(
+            fields, qs=torch.empty((blocks, n, 0), dtype=torch.uint32, device=dev),
+            qh=torch.empty((blocks, n, 0), dtype=torch.uint16, device=dev),
+            signs=torch.empty((blocks, n, 0), dtype=torch.int32, device=dev))
     return fields
+
+
+def has_soa_fields(iq3_weight: IQ3SFields) -> bool:
+    """False for weights prepared with soa=False (only the packed copy carries qs, qh and signs)."""
+    return iq3_weight.qs.numel() > 0
 
 
 def pack_iq3_s_fields(fields: IQ3SFields, *, stream=None) -> IQ3SFields:
@@ -123,15 +141,19 @@ def weight_struct(iq3_weight: IQ3SFields) -> _lib.MamboIQ3SWeight:
         "signs": ((b, n, 8), torch.int32),
         "scales": ((b, n), torch.uint32),
     }
+    packed = getattr(iq3_weight, "packed", None)
+    dropped = packed is not None and iq3_weight.qs.numel() == 0  # prepared with soa=False
     for name, (shape, dtype) in expect.items():
         t = getattr(iq3_weight, name)
+        if dropped and name in ("qs", "qh", "signs"):
+            shape = shape[:2] + (0,)
         if tuple(t.shape) != shape or t.dtype != dtype or not t.is_contiguous() or not t.is_cuda:
             raise ValueError(f"IQ3SFields.{name} must be a contiguous CUDA {dtype} tensor of shape {shape}")
     w = _lib.MamboIQ3SWeight()
-    w.d, w.qs, w.qh = iq3_weight.d.data_ptr(), iq3_weight.qs.data_ptr(), iq3_weight.qh.data_ptr()
-    w.signs, w.scales = iq3_weight.signs.data_ptr(), iq3_weight.scales.data_ptr()
+    w.d, w.scales = iq3_weight.d.data_ptr(), iq3_weight.scales.data_ptr()
+    if not dropped:
+        w.qs, w.qh, w.signs = iq3_weight.qs.data_ptr(), iq3_weight.qh.data_ptr(), iq3_weight.signs.data_ptr()
     w.n_rows, w.n_blocks = n, b
-    packed = getattr(iq3_weight, "packed", None)
     w.packed = packed.data_ptr() if packed is not None else None
     return w
 
