@@ -64,6 +64,9 @@ typedef struct MamboIQ3SWeight {
   const void* packed; /* optional tile-major copy made by mambo_iq3s_pack (NULL = none): the
                          tcgen05 GEMV then fetches a work unit with one copy instead of five */
 } MamboIQ3SWeight;
+/* With `packed` set, qs, qh and signs may be NULL (the packed copy holds their bytes; d and
+ * scales stay required): every linear entry point runs on such a weight, while
+ * mambo_iq3s_decode, mambo_iq3s_pack and MAMBO_KERNEL_GEMV_SYNC return MAMBO_EINVAL. */
 
 /* Rows per tile of the packed layout and bytes per (tile, K block) record. */
 #define MAMBO_IQ3S_TILE_ROWS 128
