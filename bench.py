@@ -460,7 +460,7 @@ def q4k_block(torch, dev) -> dict:
     Weights per step exceed the L2 (the sweep's 20 weights are 487 MB).
     """
     from mambo_b200.kernels.q4_k_fp8 import launch_q4_k_fp8_matmul, launch_quantize_fp8_sums, \
-        prepare_q4_k_fields, q4_k_fp8_linear
+        prepare_q4_k_fields, q4_k_fp8_linear, q4_k_linear_group_into
 
     stream = torch.cuda.Stream(dev)
     launches = 10
@@ -505,12 +505,30 @@ def q4k_block(torch, dev) -> dict:
             fused_us_tot += fused_us
         del w
     torch.cuda.empty_cache()
+    # The same sweep as one grouped call: 20 distinct weights (487 MB), bf16 activations; the
+    # quantization pre-pass (codes and group sums of all 20 inputs) and one grouped GEMV launch.
+    gws, gxs, gouts, g_bytes = [], [], [], 0
+    for mi, m in enumerate(M_SWEEP):
+        for pi, (name, n, k) in enumerate(PROJECTIONS):
+            gws.append(prepare_q4_k_fields(synthetic_q4k(torch, dev, n, k, seed=0x4C00 + 16 * mi + pi)))
+            gen = torch.Generator(device=dev).manual_seed(0x4C80 + 16 * mi + pi)
+            gxs.append(torch.randn((m, k), device=dev, generator=gen).to(torch.bfloat16))
+            gouts.append(torch.empty((m, n), dtype=torch.bfloat16, device=dev))
+            g_bytes += n * (k // 256) * 144 + m * k * 2 + m * n * 2
+    group_us = graph_us(lambda: q4_k_linear_group_into(gxs, gws, gouts, stream=stream))
+    del gws, gxs, gouts
+    torch.cuda.empty_cache()
     peak, kind = load_peaks()
     achieved = b_tot / us_tot / 1e3
     return {"value": achieved, "unit": "GB/s", "frac": achieved / peak, "peak": peak, "peak_kind": kind,
             "weights_bytes_per_sweep": w_tot, "bytes_per_sweep": b_tot, "gemv_us_per_sweep": us_tot,
             "fused_us_per_sweep": fused_us_tot,
             "fused_gbs": fb_tot / fused_us_tot / 1e3,
+            "grouped": {"us_per_sweep": group_us, "gbs": g_bytes / group_us / 1e3,
+                        "frac": g_bytes / group_us / 1e3 / peak,
+                        "execution": "the 20 linears of the sweep (distinct weights) in one call from bf16 "
+                                     "activations: group_xtiles_kernel with group sums, then "
+                                     "iq3s_gemv_tm_kernel<1,8,GemvGroupPre,false,true>; 10 calls per CUDA graph"},
             "kernel": "iq3s_gemv_tm_kernel<NT,8,GemvNoGroup,false,true> (Q4_K decoders, stream-K)",
             "timing": "per linear: 10 back-to-back launches in one CUDA graph, 10 replays, mean",
             "per_launch": rows}

@@ -386,6 +386,31 @@ MAMBO_API int mambo_q4k_linear_fused(const void* x, int x_dtype, int64_t ldx, in
                                      const MamboLinearConfig* cfg, void* workspace, size_t workspace_bytes,
                                      mambo_stream_t stream);
 
+/*
+ * Several independent Q4_K linears in one call (no counterpart in the reference, whose linears
+ * run one per call): out_i[M_i, N_i] = linear(x_i, packed_i) as mambo_q4k_linear_fused computes
+ * it. When every item has bf16 activations in 16-byte aligned rows, 1 <= M < 32 and N % 8 == 0,
+ * a pre-pass quantizes all items' activations once (MXFP8 codes and group sums) and one
+ * persistent GEMV launch streams all items' packed records; otherwise the items run one after
+ * another through mambo_q4k_linear_fused. workspace: mambo_q4k_linear_group_workspace_bytes(),
+ * zero-filled once. No output may overlap another item's input.
+ */
+typedef struct MamboQ4KItem {
+  const void* x;      /* activations [m, K], bf16 or f32 (x_dtype), row stride ldx */
+  int x_dtype;
+  int64_t ldx;
+  int64_t m;
+  const void* packed; /* mambo_q4k_pack buffer of the [n_rows, K] weight, K = 256 * n_blocks */
+  int64_t n_rows;
+  int64_t n_blocks;
+  void* out;          /* [m, n_rows], out_dtype, row stride ldo */
+  int out_dtype;
+  int64_t ldo;
+} MamboQ4KItem;
+MAMBO_API size_t mambo_q4k_linear_group_workspace_bytes(const MamboQ4KItem* items, int count);
+MAMBO_API int mambo_q4k_linear_group(const MamboQ4KItem* items, int count, void* workspace, size_t workspace_bytes,
+                                     mambo_stream_t stream);
+
 /* Number of tunable configurations of a kernel kind, and the i-th one (for the autotuner).
  * Replaces the search spaces of make_benchmark_cases (src/python/mambo/kernels/iq3_s_fp8.py:402-465). */
 MAMBO_API int mambo_num_configs(int kernel);

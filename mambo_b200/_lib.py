@@ -69,6 +69,8 @@ EXPORTED_SYMBOLS = (
     "mambo_q4k_linear",
     "mambo_q4k_linear_fused_workspace_bytes",
     "mambo_q4k_linear_fused",
+    "mambo_q4k_linear_group_workspace_bytes",
+    "mambo_q4k_linear_group",
     "mambo_ar_comm_create",
     "mambo_ar_comm_connect",
     "mambo_ar_comm_destroy",
@@ -107,6 +109,23 @@ class MamboLinearItem(ctypes.Structure):
 
 
 MAMBO_MAX_GROUP = 32
+
+
+class MamboQ4KItem(ctypes.Structure):
+    """One Q4_K linear of mambo_q4k_linear_group (x [m,K] times the packed weight into out [m,N])."""
+
+    _fields_ = [
+        ("x", ctypes.c_void_p),
+        ("x_dtype", ctypes.c_int),
+        ("ldx", ctypes.c_int64),
+        ("m", ctypes.c_int64),
+        ("packed", ctypes.c_void_p),
+        ("n_rows", ctypes.c_int64),
+        ("n_blocks", ctypes.c_int64),
+        ("out", ctypes.c_void_p),
+        ("out_dtype", ctypes.c_int),
+        ("ldo", ctypes.c_int64),
+    ]
 
 
 class MamboQuantOut(ctypes.Structure):
@@ -240,6 +259,8 @@ def load() -> ctypes.CDLL:
                  ctypes.c_size_t, vp],
                 i32,
             ),
+            "mambo_q4k_linear_group_workspace_bytes": ([ctypes.POINTER(MamboQ4KItem), i32], ctypes.c_size_t),
+            "mambo_q4k_linear_group": ([ctypes.POINTER(MamboQ4KItem), i32, vp, ctypes.c_size_t, vp], i32),
             "mambo_ar_comm_create": ([i32, i32, i64, ctypes.POINTER(vp), vp], i32),
             "mambo_ar_comm_connect": ([vp, vp], i32),
             "mambo_ar_comm_destroy": ([vp], i32),

@@ -1652,6 +1652,164 @@ int mambo_q4k_linear_fused(const void* x, int x_dtype, int64_t ldx, int64_t m, c
 }  // extern "C"
 static_assert(MAMBO_Q4K_RECORD_BYTES == kQ4kRecordBytes, "Q4_K record size of the C ABI and of the kernel");
 
+// ---- Grouped Q4_K linears (a quantization pre-pass with group sums, then one grouped GEMV launch)
+
+namespace {
+
+bool q4k_group_fusable(const MamboQ4KItem* items, int count) {
+  if (count < 1 || count > kGemvMaxItems) return false;
+  int64_t tiles = 0, units = 0;
+  for (int i = 0; i < count; ++i) {
+    const MamboQ4KItem& it = items[i];
+    if (it.x_dtype != MAMBO_BF16 || it.m < 1 || it.m >= kGemmMinTokens) return false;
+    if ((uintptr_t)it.x % 16 || it.ldx % 8 || (uintptr_t)it.packed % 16 || it.n_rows % 8) return false;
+    const int64_t rt = (it.n_rows + 127) / 128;
+    tiles += rt;
+    units += rt * it.n_blocks;
+  }
+  return (size_t)tiles * 4 * sizeof(int) <= kGemvCounterBytes && units < (int64_t)1 << 30;
+}
+
+int q4k_group_nt(const MamboQ4KItem* items, int count) {
+  int64_t m = 1;
+  for (int i = 0; i < count; ++i) m = items[i].m > m ? items[i].m : m;
+  return gemv_nt_for(m);
+}
+
+// Workspace of the grouped launch: counters, stream-K partials, the pre-pass's activation tiles
+// (one per item and K block), then each item's group sums [m][K/32] (256-byte aligned per item).
+size_t q4k_group_bytes(const MamboQ4KItem* items, int count, int sms, size_t* tiles_off, size_t* sums_off) {
+  const int nt = q4k_group_nt(items, count);
+  size_t tiles = 0, sums = 0;
+  for (int i = 0; i < count; ++i) {
+    tiles += (size_t)items[i].n_blocks;
+    sums += align256((size_t)items[i].m * (size_t)items[i].n_blocks * 8 * sizeof(float));
+  }
+  const size_t t0 = kCounterBytes + group_partial_bytes(nt, sms);
+  const size_t s0 = t0 + align256(tiles * gemv_xtile_bytes(nt));
+  if (tiles_off) *tiles_off = t0;
+  if (sums_off) *sums_off = s0;
+  return s0 + sums;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t mambo_q4k_linear_group_workspace_bytes(const MamboQ4KItem* items, int count) {
+  if (!items || count < 1) return 0;
+  int st;
+  DeviceInfo info = device_info(&st);
+  const int sms = (st == MAMBO_OK && info.sms > 0) ? info.sms : 148;
+  size_t need = 0;
+  for (int i = 0; i < count; ++i) {
+    if (items[i].m < 1 || items[i].n_rows < 1 || items[i].n_blocks < 1) return 0;
+    const size_t b = mambo_q4k_linear_fused_workspace_bytes(items[i].m, items[i].n_rows, items[i].n_blocks, nullptr);
+    need = b > need ? b : need;  // the per-item path, when the group does not qualify
+  }
+  if (q4k_group_fusable(items, count)) {
+    const size_t g = q4k_group_bytes(items, count, sms, nullptr, nullptr);
+    need = g > need ? g : need;
+  }
+  return need;
+}
+
+int mambo_q4k_linear_group(const MamboQ4KItem* items, int count, void* workspace, size_t workspace_bytes,
+                           mambo_stream_t stream) {
+  if (!items) return fail(MAMBO_EINVAL, "null pointer");
+  if (count < 1) return fail(MAMBO_EINVAL, "a group needs at least one linear");
+  for (int i = 0; i < count; ++i) {
+    const MamboQ4KItem& it = items[i];
+    if (!it.x || !it.packed || !it.out) return fail(MAMBO_EINVAL, "item %d: null pointer", i);
+    if (it.m < 1 || it.n_rows < 1 || it.n_blocks < 1) return fail(MAMBO_EINVAL, "item %d: shapes must be positive", i);
+    if (it.n_rows > (int64_t)1 << 24 || it.n_blocks > 4096) return fail(MAMBO_EINVAL, "item %d: weight too large", i);
+    if (it.x_dtype != MAMBO_F32 && it.x_dtype != MAMBO_BF16)
+      return fail(MAMBO_EINVAL, "item %d: activation must be f32 or bf16", i);
+    if (it.ldx < it.n_blocks * 256) return fail(MAMBO_EINVAL, "item %d: activation must be [M,K]", i);
+    if (it.out_dtype != MAMBO_F32 && it.out_dtype != MAMBO_BF16)
+      return fail(MAMBO_EINVAL, "item %d: out must be f32 or bf16", i);
+    if (it.ldo < it.n_rows) return fail(MAMBO_EINVAL, "item %d: out row stride is smaller than N", i);
+  }
+  if (!workspace || (uintptr_t)workspace % 256) return fail(MAMBO_EINVAL, "workspace must be 256-byte aligned");
+  DeviceInfo info;
+  int st = require_sm100(&info);
+  if (st != MAMBO_OK) return st;
+  if (!q4k_group_fusable(items, count)) {
+    for (int i = 0; i < count; ++i) {
+      const MamboQ4KItem& it = items[i];
+      st = mambo_q4k_linear_fused(it.x, it.x_dtype, it.ldx, it.m, it.packed, it.n_rows, it.n_blocks, it.out,
+                                  it.out_dtype, it.ldo, nullptr, workspace, workspace_bytes, stream);
+      if (st != MAMBO_OK) return st;
+    }
+    return ok();
+  }
+  const int nt = q4k_group_nt(items, count);
+  size_t tiles_off = 0, sums_off = 0;
+  const size_t need = q4k_group_bytes(items, count, info.sms, &tiles_off, &sums_off);
+  if (workspace_bytes < need)
+    return fail(MAMBO_EWORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+  GemvGroupPre g;
+  std::memset(&g, 0, sizeof(g));
+  g.count = count;
+  GroupXtilesParams xp;
+  std::memset(&xp, 0, sizeof(xp));
+  int units = 0, tiles = 0, xtiles = 0;
+  const int box = 8 * nt;
+  float* sums = (float*)((uint8_t*)workspace + sums_off);
+  for (int i = 0; i < count; ++i) {
+    const MamboQ4KItem& it = items[i];
+    const int rt = (int)((it.n_rows + 127) / 128);
+    GemvItem& gi = g.items[i];
+    gi.packed = (const uint8_t*)it.packed;
+    gi.x = (const uint16_t*)it.x;
+    gi.out = it.out;
+    gi.ldx = it.ldx;
+    gi.ldo = it.ldo;
+    gi.n_rows = (int)it.n_rows;
+    gi.n_blocks = (int)it.n_blocks;
+    gi.m = (int)it.m;
+    gi.out_bf16 = it.out_dtype == MAMBO_BF16;
+    gi.unit0 = units;
+    gi.tile0 = tiles;
+    gi.xt0 = xtiles;
+    gi.xsum = sums;
+    gi.ldsum = it.n_blocks * 8;
+    xp.items[i] = GroupXtilesParams::Item{gi.x, gi.ldx, gi.m, gi.n_blocks, gi.xt0, sums, gi.ldsum};
+    sums += align256((size_t)it.m * (size_t)it.n_blocks * 8 * sizeof(float)) / sizeof(float);
+    xtiles += gi.n_blocks;
+    units += rt * gi.n_blocks;
+    tiles += rt;
+  }
+  GemvTmParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.m = box;
+  p.n_blocks = 1;  // per item in the group
+  p.packed = g.items[0].packed;
+  p.counters = (int*)workspace;
+  p.partials = (float*)((uint8_t*)workspace + kCounterBytes);
+  p.stages = 8;
+  while (p.stages > 2 && (int)gemv_tm_smem_bytes(nt, p.stages, 0, true, true) > info.max_smem_optin) --p.stages;
+  if ((int)gemv_tm_smem_bytes(nt, p.stages, 0, true, true) > info.max_smem_optin)
+    return fail(MAMBO_EINVAL, "the grouped Q4_K GEMV does not fit in shared memory");
+  p.row_tiles = tiles;
+  p.total_units = units;
+  int grid = units < info.sms ? units : info.sms;
+  if (grid > kGemvMaxGrid) grid = kGemvMaxGrid;
+  split_group_units(g, units, grid, g.cta_start, true);
+  xp.count = count;
+  xp.total_tiles = xtiles;
+  xp.box = box;
+  xp.tiles = (uint8_t*)workspace + tiles_off;
+  cudaError_t e = launch_group_xtiles(xp, (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "group_xtiles_kernel (Q4_K)");
+  g.xtiles = xp.tiles;
+  e = launch_gemv_tm_group_pre(p, g, nt, grid, (cudaStream_t)stream, true);
+  if (e != cudaSuccess) return cuda_fail(e, "iq3s_gemv_tm_kernel (Q4_K group)");
+  return ok();
+}
+
+}  // extern "C"
+
 // --------------------------------------------------------------------------
 // Row split with the all-reduce fused into the GEMV (mambo_iq3s_linear_fused_ar)
 // --------------------------------------------------------------------------

@@ -385,7 +385,7 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
   const TmLayout L = tm_layout(NT, kQ4K);
   constexpr uint32_t kTableRegion = kQ4K ? 0u : (uint32_t)kTableBytes;  // no codebook for Q4_K
   constexpr uint32_t kRecBytes = kQ4K ? kQ4kRecordBytes : (uint32_t)kRecordBytes;
-  static_assert(!(kQ4K && (kQ || kGroup)), "Q4_K runs single linears only");
+  static_assert(!(kQ4K && (kQ || (kGroup && !kPre))), "Q4_K runs single linears or pre-quantized groups");
   // The codebook sits at the start of dynamic shared memory (a link-time
   // constant address); the stages follow, aligned to 1024 bytes at run time.
   // (Offsets from smem_raw keep the pointers in the shared address space, so
@@ -1072,8 +1072,32 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
         }
       }
     };
+    // Grouped Q4_K launches: the sums of unit uu come from its item (forward cursor).
+    int sum_item = 0;
+    auto load_sums_of = [&](int uu, int kb_single, float (&dst)[kSF]) {
+      if constexpr (kQ4K && kGroup) {
+        sum_item = group_item(grp, uu, sum_item);
+        const GemvItem& gi = grp.items[sum_item];
+        const int kb = (uu - gi.unit0) % gi.n_blocks;
+        const int t = lane / kSLanes;
+        if (t < gi.m) {
+          const float* src = gi.xsum + (size_t)t * gi.ldsum + (size_t)kb * 8 + (lane % kSLanes) * kSF;
+#pragma unroll
+          for (int j = 0; j < kSF; j += 2) {
+            const float2 v = __ldg(reinterpret_cast<const float2*>(src + j));
+            dst[j] = v.x;
+            dst[j + 1] = v.y;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < kSF; ++j) dst[j] = 0.f;
+        }
+      } else {
+        load_sums(kb_single, dst);
+      }
+    };
     if constexpr (kQ4K) {
-      if (u0 < u1) load_sums(kb_next, sum_next);
+      if (u0 < u1) load_sums_of(u0, kb_next, sum_next);
     }
     int r = 0;  // ring slot of unit `it` and its phase
     uint32_t rph = 0;
@@ -1101,7 +1125,7 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
         // P_g the group's product with the odd integers 2q - 15.
 #pragma unroll
         for (int j = 0; j < kSF; ++j) sum_cur[j] = sum_next[j];
-        if (u + 1 < u1) load_sums(kb_step(kb_next), sum_next);
+        if (u + 1 < u1) load_sums_of(u + 1, kb_step(kb_next), sum_next);
         // This unit's sums into the warp's copy [TOK][8] (lane l holds entries l*kSF..), read back as
         // broadcasts.
         float* scr = reinterpret_cast<float*>(tstage) + (warp - kEpiWarp0) * TOK * 8;
@@ -1340,8 +1364,8 @@ __global__ void __launch_bounds__(tm_threads(kDecWarps), 1)
 // --------------------------------------------------------------------------
 // Host side
 // --------------------------------------------------------------------------
-uint32_t gemv_tm_smem_bytes(int nt, int stages, int kparts, bool fused) {
-  return tm_smem_bytes(nt, stages, kparts, fused);
+uint32_t gemv_tm_smem_bytes(int nt, int stages, int kparts, bool fused, bool q4k) {
+  return tm_smem_bytes(nt, stages, kparts, fused, q4k);
 }
 int gemv_tm_max_stages() { return kMaxStagesTm; }
 
@@ -1353,9 +1377,9 @@ template <int NT, int kDecWarps, bool kQ = false>
 static const void* tm_kernel_group() {
   return (const void*)iq3s_gemv_tm_kernel<NT, kDecWarps, GemvGroup, kQ>;
 }
-template <int NT, bool kQ = false>
+template <int NT, bool kQ = false, bool kQ4K = false>
 static const void* tm_kernel_group_pre() {
-  return (const void*)iq3s_gemv_tm_kernel<NT, 8, GemvGroupPre, kQ>;
+  return (const void*)iq3s_gemv_tm_kernel<NT, 8, GemvGroupPre, kQ, kQ4K>;
 }
 
 static int query_max_clusters(int nt, int dec_warps, int stages, int kparts, bool q4k);
@@ -1437,11 +1461,13 @@ static cudaError_t launch_gemv_tm_group_t(const GemvTmParams& p, const GemvGroup
 
 template <int NT>
 static cudaError_t launch_gemv_tm_group_pre_t(const GemvTmParams& p, const GemvGroupPre& g, int grid,
-                                              cudaStream_t stream) {
-  const uint32_t smem = tm_smem_bytes(NT, p.stages, 0, true);
+                                              cudaStream_t stream, bool q4k) {
+  const uint32_t smem = tm_smem_bytes(NT, p.stages, 0, true, q4k);
   bool quant = false;  // some item also writes its output's MXFP8 quantization
   for (int i = 0; i < g.count; ++i) quant = quant || g.items[i].q_out != nullptr;
-  const void* kern = quant ? tm_kernel_group_pre<NT, true>() : tm_kernel_group_pre<NT, false>();
+  if (q4k && quant) return cudaErrorInvalidValue;
+  const void* kern = q4k ? tm_kernel_group_pre<NT, false, true>()
+                         : quant ? tm_kernel_group_pre<NT, true>() : tm_kernel_group_pre<NT, false>();
   cudaError_t e = ensure_smem_attribute(kern, smem);
   if (e != cudaSuccess) return e;
   GemvTmMaps maps;
@@ -1450,12 +1476,12 @@ static cudaError_t launch_gemv_tm_group_pre_t(const GemvTmParams& p, const GemvG
 }
 
 cudaError_t launch_gemv_tm_group_pre(const GemvTmParams& p, const GemvGroupPre& g, int nt, int grid,
-                                     cudaStream_t stream) {
+                                     cudaStream_t stream, bool q4k) {
   if (p.kparts != 0) return cudaErrorInvalidValue;
   switch (nt) {
-    case 1: return launch_gemv_tm_group_pre_t<1>(p, g, grid, stream);
-    case 2: return launch_gemv_tm_group_pre_t<2>(p, g, grid, stream);
-    default: return launch_gemv_tm_group_pre_t<4>(p, g, grid, stream);
+    case 1: return launch_gemv_tm_group_pre_t<1>(p, g, grid, stream, q4k);
+    case 2: return launch_gemv_tm_group_pre_t<2>(p, g, grid, stream, q4k);
+    default: return launch_gemv_tm_group_pre_t<4>(p, g, grid, stream, q4k);
   }
 }
 

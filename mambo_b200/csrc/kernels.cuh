@@ -210,6 +210,8 @@ struct GemvItem {
   int unit0;  // first unit of this item in the launch's numbering
   int tile0;  // first row tile of this item in the launch's numbering
   int xt0;    // GemvGroupPre: first activation tile of this item (one per K block)
+  const float* xsum;  // Q4_K groups: the activations' group sums [m][ldsum] (made by the pre-pass)
+  int64_t ldsum;
   uint8_t* q_out;  // optional MXFP8 quantization of out (as GemvTmParams::q_out)
   int64_t ldq;
   uint8_t* s_out;
@@ -248,6 +250,8 @@ struct GroupXtilesParams {
     int m;
     int n_blocks;
     int xt0;
+    float* sums;  // optional (Q4_K): each 32-value group's sum of quantized values [m][ld_sums]
+    int64_t ld_sums;
   } items[kGemvMaxItems];
   int count;
   int total_tiles;
@@ -282,7 +286,7 @@ cudaError_t launch_gemv_tm_ar(const GemvTmParams& p, const GemvAr& ar, int nt, c
 cudaError_t launch_gemv_tm_group(const GemvTmParams& p, const GemvGroup& g, int nt, int dec_warps, int grid,
                                  cudaStream_t stream);
 cudaError_t launch_gemv_tm_group_pre(const GemvTmParams& p, const GemvGroupPre& g, int nt, int grid,
-                                     cudaStream_t stream);
+                                     cudaStream_t stream, bool q4k = false);
 
 // Activation map for the tcgen05 GEMV; false when xq is not 16-byte aligned
 // with a row stride that is a multiple of 16.
@@ -293,7 +297,7 @@ cudaError_t launch_gemv_tm(const GemvTmParams& p, int nt, int dec_warps, const G
                            cudaStream_t stream, bool q4k = false);
 // Shared memory of the Q4_K GEMV (no codebook, 18,432-byte records).
 uint32_t q4k_gemv_smem_bytes(int nt, int stages, int kparts);
-uint32_t gemv_tm_smem_bytes(int nt, int stages, int kparts, bool fused = false);
+uint32_t gemv_tm_smem_bytes(int nt, int stages, int kparts, bool fused = false, bool q4k = false);
 // bf16 activation map for the GEMV's fused quantization; false unless x is
 // 16-byte aligned with a row stride (elements) that is a multiple of 8.
 bool make_gemv_xb_map(const uint16_t* x, int64_t ldx, int m, int64_t k, int box_tokens, CUtensorMap* map);

@@ -195,6 +195,28 @@ __global__ void __launch_bounds__(256) group_xtiles_kernel(const __grid_constant
     const uint32_t code = mxfp8_quad_bf16_rne(c, q);
     *reinterpret_cast<uint2*>(dst + ((2 * g + (j >> 1)) * p.box + t) * 16 + (j & 1) * 8) = q;
     if (j == 0) dst[256 * p.box + (g >> 2) * 16 * p.box + t * 16 + (g & 3)] = (uint8_t)code;
+    if (it.sums != nullptr) {
+      // The group's quantized values summed (exact in FP32 in any order: 32 E4M3 values need at
+      // most 23 bits), times 2^e; a NaN scale code gives NaN (as quantize_mxfp8_kernel's sums).
+      float sum = 0.f;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t w = h ? q.y : q.x;
+#pragma unroll
+        for (int b = 0; b < 2; ++b) {
+          uint32_t h2;
+          const uint16_t two = (uint16_t)(w >> (16 * b));
+          asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(two));
+          sum += __half2float(__ushort_as_half((unsigned short)(h2 & 0xFFFFu)));
+          sum += __half2float(__ushort_as_half((unsigned short)(h2 >> 16)));
+        }
+      }
+      sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 1);
+      sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 2);
+      if (j == 0)
+        it.sums[(size_t)t * it.ld_sums + (size_t)kb * 8 + g] =
+            code == 0xFFu ? __uint_as_float(0x7FC00000u) : sum * e8m0_to_float(code);
+    }
   }
 }
 

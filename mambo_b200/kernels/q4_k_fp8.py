@@ -153,3 +153,49 @@ def q4_k_fp8_linear(x, weight: Q4KFields, *, stream=None, out_dtype: torch.dtype
             _lib.MAMBO_BF16 if out.dtype == torch.bfloat16 else _lib.MAMBO_F32, out.stride(0), cfg, ws.data_ptr(),
             ws.numel(), st), "q4_k_fp8_linear")
     return out
+
+
+def q4_k_linear_group_into(xs, weights, outs, *, stream=None) -> list:
+    """Independent Q4_K linears ``outs[i] = q4_k_fp8_linear(xs[i], weights[i])`` in one C-ABI call.
+
+    With bf16 activations in 16-byte aligned rows, 1 <= M < 32 and N % 8 == 0
+    for every item, this is a quantization pre-pass (codes and group sums of all
+    items at once) and one persistent GEMV launch over all items' weights;
+    otherwise the items run one after another. No output may overlap another
+    item's input.
+    """
+    count = len(xs)
+    if count < 1 or len(weights) != count or len(outs) != count:
+        raise ValueError("xs, weights and outs must be non-empty lists of the same length")
+    if count > _lib.MAMBO_MAX_GROUP:
+        raise ValueError(f"at most {_lib.MAMBO_MAX_GROUP} linears per group")
+    items = (_lib.MamboQ4KItem * count)()
+    for i, (x, w, out) in enumerate(zip(xs, weights, outs)):
+        n_rows, n_blocks = w["n_rows"], w["n_blocks"]
+        if x.ndim != 2 or x.dtype not in (torch.float32, torch.bfloat16) or x.shape[1] != n_blocks * Q4_K_BLOCK_VALUES \
+                or x.stride(1) != 1:
+            raise ValueError(f"xs[{i}] must be float32 or bfloat16 [M,K] with unit column stride")
+        if tuple(out.shape) != (x.shape[0], n_rows) or out.dtype not in (torch.float32, torch.bfloat16) \
+                or out.stride(1) != 1:
+            raise ValueError(f"outs[{i}] must be float32 or bfloat16 [M,N] with unit column stride")
+        items[i].x, items[i].ldx, items[i].m = x.data_ptr(), x.stride(0), x.shape[0]
+        items[i].x_dtype = _lib.MAMBO_BF16 if x.dtype == torch.bfloat16 else _lib.MAMBO_F32
+        items[i].packed, items[i].n_rows, items[i].n_blocks = w["packed"].data_ptr(), n_rows, n_blocks
+        items[i].out, items[i].ldo = out.data_ptr(), out.stride(0)
+        items[i].out_dtype = _lib.MAMBO_BF16 if out.dtype == torch.bfloat16 else _lib.MAMBO_F32
+    dev = xs[0].device
+    _runtime.require_device(dev)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        st = _runtime.stream_handle(stream, dev)
+        ws = _runtime.workspace(dev, st, lib.mambo_q4k_linear_group_workspace_bytes(items, count))
+        _lib.check(lib.mambo_q4k_linear_group(items, count, ws.data_ptr(), ws.numel(), st), "q4_k_linear_group")
+    return outs
+
+
+def q4_k_fp8_linear_group(xs, weights, *, stream=None, out_dtype: torch.dtype = torch.bfloat16) -> list:
+    """Several independent ``q4_k_fp8_linear`` calls as one (see ``q4_k_linear_group_into``)."""
+    if out_dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError("out_dtype must be torch.float32 or torch.bfloat16")
+    outs = [torch.empty((x.shape[0], w["n_rows"]), dtype=out_dtype, device=x.device) for x, w in zip(xs, weights)]
+    return q4_k_linear_group_into(xs, weights, outs, stream=stream)

@@ -217,3 +217,25 @@ def test_rejects_bad_inputs(cuda_device):
         launch_q4_k_fp8_matmul(xq, xs, misaligned, w)
     with pytest.raises(ValueError):
         prepare_q4_k_fields(torch.zeros((4, 145), dtype=torch.uint8, device=cuda_device))
+
+
+def test_grouped_q4k_linears_match_each_linear_and_the_oracle(cuda_device):
+    """Independent Q4_K linears of 1 to 31 tokens in one call: a quantization pre-pass (codes and group
+    sums) and one grouped GEMV launch. Each output equals the single fused call to FP32 rounding (the
+    stream-K split differs) and the oracle's float64 product of the same MXFP8 operands."""
+    from mambo_b200.kernels.q4_k_fp8 import q4_k_fp8_linear, q4_k_fp8_linear_group
+
+    shapes = [(1, 256, 512), (8, 1024, 2048), (3, 384, 1024), (17, 512, 768), (5, 2048, 1024), (31, 128, 256)]
+    raws, ws, xs = [], [], []
+    for i, (m, n, k) in enumerate(shapes):
+        raw = G.make_synthetic_q4_k(n, k, seed=700 + i)
+        raws.append(raw)
+        ws.append(prepare_q4_k_fields(torch.from_numpy(raw).to(cuda_device)))
+        xs.append(_x(cuda_device, m, k, seed=800 + i))
+    for _ in range(2):  # the second call reuses the workspace's tiles and sums
+        outs = q4_k_fp8_linear_group(xs, ws, out_dtype=torch.float32)
+        for x, w, raw, out in zip(xs, ws, raws, outs):
+            one = q4_k_fp8_linear(x, w, out_dtype=torch.float32)
+            assert O.relative_frobenius(out.cpu().numpy(), one.cpu().numpy().astype(np.float64)) < 1e-5
+            xq, xs_ = launch_quantize_fp8(x)
+            assert O.relative_frobenius(out.cpu().numpy(), _oracle(xq, xs_, raw)) < ORACLE_FROB_TOL
