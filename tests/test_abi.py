@@ -62,3 +62,27 @@ def test_workspace_size_is_positive_and_monotone():
     small = lib.mambo_iq3s_linear_workspace_bytes(8, 4096, 16, None)
     big = lib.mambo_iq3s_linear_workspace_bytes(8, 28672, 112, None)
     assert 0 < small <= big
+
+
+def test_grouped_entry_points_check_arguments_without_gpu():
+    """The grouped IQ3_S and Q4_K calls reject bad groups before any device work."""
+    lib = _lib.load()
+    items = (_lib.MamboQ4KItem * 2)()
+    for i, (m, n, b) in enumerate(((1, 4096, 16), (8, 14336, 16))):
+        items[i].m, items[i].n_rows, items[i].n_blocks = m, n, b
+        items[i].x_dtype, items[i].ldx = _lib.MAMBO_BF16, b * 256
+        items[i].out_dtype, items[i].ldo = _lib.MAMBO_BF16, n
+    assert lib.mambo_q4k_linear_group(None, 1, None, 0, None) == _lib.MAMBO_EINVAL
+    assert lib.mambo_q4k_linear_group(items, 0, None, 0, None) == _lib.MAMBO_EINVAL
+    assert lib.mambo_q4k_linear_group(items, 2, None, 0, None) == _lib.MAMBO_EINVAL
+    assert "item 0: null pointer" in _lib.last_error()
+    # Workspace: zero for an empty group, and a group needs at least what its largest item does.
+    assert lib.mambo_q4k_linear_group_workspace_bytes(None, 0) == 0
+    one = lib.mambo_q4k_linear_group_workspace_bytes(items, 1)
+    two = lib.mambo_q4k_linear_group_workspace_bytes(items, 2)
+    assert 0 < one <= two
+    assert two >= lib.mambo_q4k_linear_fused_workspace_bytes(8, 14336, 16, None)
+    linears = (_lib.MamboLinearItem * 1)()
+    assert lib.mambo_iq3s_linear_group(None, 1, None, None, 0, None) == _lib.MAMBO_EINVAL
+    assert lib.mambo_iq3s_linear_group(linears, 1, None, None, 0, None) == _lib.MAMBO_EINVAL
+    assert "null" in _lib.last_error()
